@@ -1,0 +1,226 @@
+"""ctypes bindings for the CPU checkers (TEST INFRASTRUCTURE ONLY).
+
+Two libraries share one set of wrappers:
+
+* ``liboracle.so``  -- the C restatement in oracle/dsv4_oracle.c (prefix
+  ``dsv4o_``), always buildable from this repository;
+* ``_ref/libdsv4ref.so`` -- the reference's own src/core + src/model C, compiled
+  from its sources by ``make -C oracle ref`` (prefix ``dsv4_``). It exists only
+  where the reference was present at build time (and travels as a built file).
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg import
+this module. The product never does.
+"""
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libdsv4ref.so")
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+_u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_i = C.c_int
+_f = C.c_float
+_d = C.c_double
+_vp = C.c_void_p
+
+
+def build_oracle():
+    """Compile liboracle.so if missing (gcc is present on every box)."""
+    if not os.path.exists(ORACLE_SO):
+        subprocess.run(["make", "-C", HERE, "liboracle.so"], check=True,
+                       stdout=subprocess.DEVNULL)
+    return ORACLE_SO
+
+
+class HcW(C.Structure):
+    """Layout of the reference's DSV4HcW (include/dsv4/dsv4.h:266-270)."""
+    _fields_ = [("fn", _vp), ("base", _vp), ("scale", _vp)]
+
+
+class _Lib:
+    def __init__(self, path, prefix):
+        self.path, self.p = path, prefix
+        self.lib = C.CDLL(path)
+
+    def fn(self, name, argtypes, restype=None):
+        f = getattr(self.lib, self.p + name)
+        f.argtypes, f.restype = argtypes, restype
+        return f
+
+
+def _c(a, dt):
+    return np.ascontiguousarray(a, dtype=dt)
+
+
+class Checker:
+    """Numpy-level wrappers over one checker library.
+
+    ``kind`` is "port" (the restatement) or "reference" (the reference's own
+    C). Functions the reference lacks (f32 GEMV, sigmoid routing) raise
+    AttributeError on the reference checker.
+    """
+
+    def __init__(self, kind="port"):
+        self.kind = kind
+        if kind == "port":
+            self._l = _Lib(build_oracle(), "dsv4o_")
+            self._pre = {"fp8": "gemv_fp8", "fp4": "gemv_fp4", "bf16": "gemv_bf16"}
+        else:
+            self._l = _Lib(REF_SO, "dsv4_")
+            self._pre = {"fp8": "matmul_fp8", "fp4": "matmul_fp4", "bf16": "matmul_bf16"}
+
+    # ---- formats -------------------------------------------------------
+    def e4m3(self, b):
+        f = self._l.fn("e4m3", [C.c_uint8], _f)
+        return np.array([f(int(v)) for v in np.ravel(b)], np.float32)
+
+    # ---- GEMV ----------------------------------------------------------
+    def gemv_fp8(self, x, W, S, out, inn, blk_r=128, blk_c=128):
+        x = _c(x, np.float32); nt = x.size // inn
+        y = np.empty(nt * out, np.float32)
+        if nt == 1:
+            self._l.fn(self._pre["fp8"], [_f32p, _f32p, _u8p, _u8p, _i, _i, _i, _i])(
+                y, x, _c(W, np.uint8), _c(S, np.uint8), inn, out, blk_r, blk_c)
+        else:
+            self._l.fn(self._pre["fp8"] + "_n", [_f32p, _f32p, _u8p, _u8p, _i, _i, _i, _i, _i])(
+                y, x, _c(W, np.uint8), _c(S, np.uint8), inn, out, blk_r, blk_c, nt)
+        return y.reshape(nt, out) if nt > 1 else y
+
+    def gemv_fp4(self, x, W, S, out, inn, blk_r=1, blk_c=32):
+        x = _c(x, np.float32); nt = x.size // inn
+        y = np.empty(nt * out, np.float32)
+        if nt == 1:
+            self._l.fn(self._pre["fp4"], [_f32p, _f32p, _u8p, _u8p, _i, _i, _i, _i])(
+                y, x, _c(W, np.uint8), _c(S, np.uint8), inn, out, blk_r, blk_c)
+        else:
+            self._l.fn(self._pre["fp4"] + "_n", [_f32p, _f32p, _u8p, _u8p, _i, _i, _i, _i, _i])(
+                y, x, _c(W, np.uint8), _c(S, np.uint8), inn, out, blk_r, blk_c, nt)
+        return y.reshape(nt, out) if nt > 1 else y
+
+    def gemv_bf16(self, x, W, out, inn):
+        x = _c(x, np.float32); nt = x.size // inn
+        y = np.empty(nt * out, np.float32)
+        if nt == 1:
+            self._l.fn(self._pre["bf16"], [_f32p, _f32p, _u16p, _i, _i])(
+                y, x, _c(W, np.uint16), inn, out)
+        else:
+            self._l.fn(self._pre["bf16"] + "_n", [_f32p, _f32p, _u16p, _i, _i, _i])(
+                y, x, _c(W, np.uint16), inn, out, nt)
+        return y.reshape(nt, out) if nt > 1 else y
+
+    def gemv_f32(self, x, W, out, inn):
+        y = np.empty(out, np.float32)
+        self._l.fn("gemv_f32", [_f32p, _f32p, _f32p, _i, _i])(
+            y, _c(x, np.float32), _c(W, np.float32), inn, out)
+        return y
+
+    # ---- elementwise ----------------------------------------------------
+    def rmsnorm(self, x, w, eps):
+        x = _c(x, np.float32); y = np.empty_like(x)
+        self._l.fn("rmsnorm", [_f32p, _f32p, _f32p, _i, _f])(y, x, _c(w, np.float32), x.size, eps)
+        return y
+
+    def swiglu(self, g, u, limit):
+        g = _c(g, np.float32); y = np.empty_like(g)
+        self._l.fn("swiglu", [_f32p, _f32p, _f32p, _i, _f])(y, g, _c(u, np.float32), g.size, limit)
+        return y
+
+    def route(self, logits, topk, route_scale, bias=None, tid2eid=None,
+              token_id=0, score_func=1):
+        scores = _c(logits, np.float32).copy()
+        n = scores.size
+        orig = np.empty(n, np.float32)
+        idx = np.empty(topk, np.int32); w = np.empty(topk, np.float32)
+        bias_p = None if bias is None else _c(bias, np.float32)
+        tid_p = None if tid2eid is None else _c(tid2eid, np.int64)
+        args = [idx.ctypes.data, w.ctypes.data, scores.ctypes.data, orig.ctypes.data,
+                None if bias_p is None else bias_p.ctypes.data,
+                None if tid_p is None else tid_p.ctypes.data,
+                token_id, n, topk, route_scale]
+        at = [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f]
+        if self.kind == "port":
+            self._l.fn("route", at + [_i])(*args, score_func)
+        else:
+            if score_func != 1:
+                raise AttributeError("the reference C implements sqrtsoftplus only")
+            self._l.fn("route", at)(*args)
+        return idx, w
+
+    # ---- indexer / attention -------------------------------------------
+    def indexer_score(self, q, kv, weights, n_heads, head_dim):
+        kv = _c(kv, np.float32); n_pos = kv.size // head_dim
+        out = np.empty(n_pos, np.float32)
+        self._l.fn("indexer_score", [_f32p, _f32p, _f32p, _f32p, _i, _i, _i])(
+            out, _c(q, np.float32), kv, _c(weights, np.float32), n_heads, head_dim, n_pos)
+        return out
+
+    def topk(self, scores, k):
+        scores = _c(scores, np.float32)
+        idx = np.full(max(k, 1), -1, np.int32)
+        n = self._l.fn("topk", [_i32p, _f32p, _i, _i], _i)(idx, scores, scores.size, k)
+        return idx[:n]
+
+    def sparse_attn(self, q, kv, sink, idxs, scale):
+        q = _c(q, np.float32); h, d = q.shape
+        idxs = _c(idxs, np.int32)
+        o = np.empty((h, d), np.float32)
+        scratch = np.empty(h * max(idxs.size, 1), np.float32)
+        self._l.fn("sparse_attn", [_f32p, _f32p, _f32p, _f32p, _i32p, _i, _i, _i, _f, _f32p])(
+            o, q, _c(kv, np.float32), _c(sink, np.float32), idxs, h, d, idxs.size, scale, scratch)
+        return o
+
+    def window_idxs(self, pos, win):
+        idx = np.empty(win, np.int32)
+        n = self._l.fn("window_idxs", [_i32p, _i, _i], _i)(idx, pos, win)
+        return idx, n
+
+    # ---- rope / hc / compressor ------------------------------------------
+    def rope_table(self, dim, seqlen, orig, base, factor, bf, bs):
+        cs = np.empty(seqlen * (dim // 2), np.float32); sn = np.empty_like(cs)
+        self._l.fn("rope_table", [_f32p, _f32p, _i, _i, _i, _d, _d, _d, _d])(
+            cs, sn, dim, seqlen, orig, base, factor, bf, bs)
+        return cs, sn
+
+    def rope_apply(self, v, rd, cs, sn, pos, inverse):
+        v = _c(v, np.float32).copy()
+        self._l.fn("rope_apply", [_f32p, _i, _i, _f32p, _f32p, _i, _i, _i])(
+            v, v.size, rd, cs, sn, pos, rd // 2, inverse)
+        return v
+
+    def hc_pre(self, x, fn, base, scale, hc, hidden, iters, norm_eps, hc_eps):
+        y = np.empty(hidden, np.float32); post = np.empty(hc, np.float32)
+        comb = np.empty(hc * hc, np.float32); mixes = np.empty((2 + hc) * hc, np.float32)
+        x, fn, base, scale = (_c(a, np.float32) for a in (x, fn, base, scale))
+        if self.kind == "port":
+            self._l.fn("hc_pre", [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
+                                  _i, _i, _i, _f, _f])(
+                y, post, comb, mixes, x, fn, base, scale, hc, hidden, iters, norm_eps, hc_eps)
+        else:
+            w = HcW(fn.ctypes.data, base.ctypes.data, scale.ctypes.data)
+            self._l.fn("hc_pre", [_f32p, _f32p, _f32p, _f32p, _f32p, C.POINTER(HcW),
+                                  _i, _i, _i, _f, _f])(
+                y, post, comb, mixes, x, C.byref(w), hc, hidden, iters, norm_eps, hc_eps)
+        return y, post, comb
+
+    def hc_post(self, x, residual, post, comb, hc, hidden):
+        y = np.empty(hc * hidden, np.float32)
+        self._l.fn("hc_post", [_f32p, _f32p, _f32p, _f32p, _f32p, _i, _i])(
+            y, _c(x, np.float32), _c(residual, np.float32), _c(post, np.float32),
+            _c(comb, np.float32), hc, hidden)
+        return y
+
+    def compress_step(self, kv_in, score_in, ape, kv_state, score_state, pos,
+                      ratio, head_dim):
+        out = np.zeros(head_dim, np.float32)
+        r = self._l.fn("compress_step", [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
+                                         _i, _i, _i], _i)(
+            out, _c(kv_in, np.float32), _c(score_in, np.float32), _c(ape, np.float32),
+            kv_state, score_state, pos, ratio, head_dim)
+        return r, out

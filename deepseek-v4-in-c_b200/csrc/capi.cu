@@ -1,0 +1,277 @@
+// capi.cu - the reference-compatible C ABI (include/dsv4_b200.h, layer 1) and
+// the device GEMV entry (layer 2).
+//
+// Mirrors include/dsv4/dsv4_cuda.h of the reference: same symbols, same 0/-1
+// contract, abort() on misuse (src/cuda/dsv4_cuda.cu:387-434). Differences by
+// design: weights of every format can be resident, residency resolves row
+// slices of a resident matrix, and host<->device traffic goes through pinned
+// staging on one non-blocking stream with a single synchronisation per call.
+#include <stdlib.h>
+#include <string.h>
+
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+#include "../../include/dsv4_b200.h"
+
+namespace dsv4b {
+
+struct Resident {
+    const void *key;        // host m->w
+    const void *skey;       // host m->s
+    uint8_t *dw, *ds;       // device copies
+    int wdt, rows, cols, blk_r, blk_c, sc;
+    size_t wbytes, sbytes, rowbytes;
+};
+
+struct State {
+    int ready = 0, dev = 0;
+    cudaStream_t st = nullptr;
+    std::vector<Resident> res;
+    float *dx = nullptr, *dy = nullptr, *hx = nullptr, *hy = nullptr;
+    size_t xcap = 0, ycap = 0, hxcap = 0, hycap = 0;
+};
+State g;
+
+cudaStream_t stream_of(void *s) { return s ? (cudaStream_t)s : g.st; }
+
+static int scale_rows(int rows, int blk_r) { return (rows + blk_r - 1) / blk_r; }
+
+// Exact residency, then containment: a matrix whose host rows are whole
+// row-blocks inside a resident matrix of the same format and width is that
+// matrix's slice (the grouped wo_a call, dsv4_layer.c:321-334). `row0` is the
+// first row of the slice within the resident matrix.
+static const Resident *find(const DSV4QMat *m, int *row0)
+{
+    if (!m || !m->w) return nullptr;
+    for (const Resident &r : g.res)
+        if (r.key == m->w && r.rows == m->rows && r.cols == m->cols && r.wdt == m->wdt) {
+            *row0 = 0;
+            return &r;
+        }
+    for (const Resident &r : g.res) {
+        if (r.wdt != m->wdt || r.cols != m->cols) continue;
+        const uint8_t *base = (const uint8_t *)r.key, *p = (const uint8_t *)m->w;
+        if (p < base || p >= base + r.wbytes) continue;
+        const size_t off = (size_t)(p - base);
+        if (off % r.rowbytes) continue;
+        const int o0 = (int)(off / r.rowbytes);
+        if (o0 + m->rows > r.rows) continue;
+        if (r.wdt >= DSV4_WFP8) {
+            if (o0 % r.blk_r || m->blk_r != r.blk_r || m->blk_c != r.blk_c) continue;
+            const uint8_t *sp = (const uint8_t *)r.skey + (size_t)(o0 / r.blk_r) * r.sc;
+            if ((const uint8_t *)m->s != sp) continue;
+        }
+        *row0 = o0;
+        return &r;
+    }
+    return nullptr;
+}
+
+static int stage(size_t xn, size_t yn)
+{
+    if (xn > g.xcap) {
+        if (g.dx) cudaFree(g.dx);
+        g.dx = nullptr; g.xcap = 0;
+        DSV4B_CUDA_OK(cudaMalloc(&g.dx, xn * sizeof(float)));
+        g.xcap = xn;
+    }
+    if (yn > g.ycap) {
+        if (g.dy) cudaFree(g.dy);
+        g.dy = nullptr; g.ycap = 0;
+        DSV4B_CUDA_OK(cudaMalloc(&g.dy, yn * sizeof(float)));
+        g.ycap = yn;
+    }
+    if (xn > g.hxcap) {
+        if (g.hx) cudaFreeHost(g.hx);
+        g.hx = nullptr; g.hxcap = 0;
+        DSV4B_CUDA_OK(cudaHostAlloc(&g.hx, xn * sizeof(float), cudaHostAllocDefault));
+        g.hxcap = xn;
+    }
+    if (yn > g.hycap) {
+        if (g.hy) cudaFreeHost(g.hy);
+        g.hy = nullptr; g.hycap = 0;
+        DSV4B_CUDA_OK(cudaHostAlloc(&g.hy, yn * sizeof(float), cudaHostAllocDefault));
+        g.hycap = yn;
+    }
+    return 0;
+}
+
+// Host-buffer GEMV through pinned staging: one H2D, the kernel, one D2H, one
+// stream synchronisation.
+static int host_gemv(float *y, const float *x, const Resident &r, int row0, int rows, int nt)
+{
+    const size_t xn = (size_t)nt * r.cols, yn = (size_t)nt * rows;
+    if (stage(xn, yn) != 0) return -1;
+    memcpy(g.hx, x, xn * sizeof(float));
+    DSV4B_CUDA_OK(cudaMemcpyAsync(g.dx, g.hx, xn * sizeof(float), cudaMemcpyHostToDevice, g.st));
+    const uint8_t *dw = r.dw + (size_t)row0 * r.rowbytes;
+    const uint8_t *ds = r.ds ? r.ds + (size_t)(row0 / r.blk_r) * r.sc : nullptr;
+    if (gemv(r.wdt, g.dy, rows, g.dx, r.cols, dw, ds, rows, r.cols, r.blk_r, r.blk_c, nt, g.st) != 0)
+        return -1;
+    DSV4B_CUDA_OK(cudaMemcpyAsync(g.hy, g.dy, yn * sizeof(float), cudaMemcpyDeviceToHost, g.st));
+    DSV4B_CUDA_OK(cudaStreamSynchronize(g.st));
+    memcpy(y, g.hy, yn * sizeof(float));
+    return 0;
+}
+
+}  // namespace dsv4b
+
+using namespace dsv4b;
+
+extern "C" int dsv4_cuda_available(void)
+{
+    int n = 0;
+    return (cudaGetDeviceCount(&n) == cudaSuccess && n > 0) ? 1 : 0;
+}
+
+extern "C" int dsv4_cuda_set_blocking_sync(void)
+{
+    DSV4B_CUDA_OK(cudaSetDeviceFlags(cudaDeviceScheduleBlockingSync));
+    return 0;
+}
+
+extern "C" int dsv4_cuda_init(void)
+{
+    if (g.ready) return 0;
+    int n = 0;
+    DSV4B_CUDA_OK(cudaGetDeviceCount(&n));
+    if (n < 1) { fprintf(stderr, "dsv4_b200: no device\n"); return -1; }
+    const char *e = getenv("DSV4_DEVICE");
+    g.dev = e ? atoi(e) : 0;
+    if (g.dev < 0 || g.dev >= n) { fprintf(stderr, "dsv4_b200: DSV4_DEVICE=%d of %d\n", g.dev, n); return -1; }
+    DSV4B_CUDA_OK(cudaSetDevice(g.dev));
+    cudaDeviceProp p;
+    DSV4B_CUDA_OK(cudaGetDeviceProperties(&p, g.dev));
+    if (p.major != 10) {
+        fprintf(stderr, "dsv4_b200: built for sm_100a, device is sm_%d%d\n", p.major, p.minor);
+        return -1;
+    }
+    DSV4B_CUDA_OK(cudaStreamCreateWithFlags(&g.st, cudaStreamNonBlocking));
+    size_t fr = 0, tot = 0;
+    DSV4B_CUDA_OK(cudaMemGetInfo(&fr, &tot));
+    printf("cuda: %s, sm_%d%d, %d SMs, %.2f GB free of %.2f GB\n", p.name, p.major, p.minor,
+           p.multiProcessorCount, fr / 1073741824.0, tot / 1073741824.0);
+    g.ready = 1;
+    return 0;
+}
+
+extern "C" size_t dsv4_cuda_free_vram(void)
+{
+    size_t fr = 0, tot = 0;
+    if (!g.ready || cudaMemGetInfo(&fr, &tot) != cudaSuccess) return 0;
+    return fr;
+}
+
+extern "C" int dsv4_cuda_has(const DSV4QMat *m)
+{
+    int row0;
+    return (g.ready && find(m, &row0)) ? 1 : 0;
+}
+
+extern "C" int dsv4_cuda_upload(const DSV4QMat *m)
+{
+    if (!g.ready || !m || !m->w || m->rows <= 0 || m->cols <= 0) return -1;
+    if (m->wdt < DSV4_WF32 || m->wdt > DSV4_WFP4) return -1;
+    const bool scaled = m->wdt >= DSV4_WFP8;
+    if (scaled && (!m->s || m->blk_r <= 0 || m->blk_c <= 0)) return -1;
+    if (m->wdt == DSV4_WFP4 && (m->cols & 1)) return -1;
+    int row0;
+    const Resident *have = find(m, &row0);
+    if (have && row0 == 0 && have->key == m->w) return 0;
+
+    Resident r = {};
+    r.key = m->w; r.skey = m->s; r.wdt = m->wdt;
+    r.rows = m->rows; r.cols = m->cols;
+    r.blk_r = scaled ? m->blk_r : 1; r.blk_c = scaled ? m->blk_c : 1;
+    r.sc = scaled ? (m->cols + m->blk_c - 1) / m->blk_c : 0;
+    r.rowbytes = row_bytes(m->wdt, m->cols);
+    r.wbytes = r.rowbytes * (size_t)m->rows;
+    r.sbytes = scaled ? (size_t)scale_rows(m->rows, m->blk_r) * r.sc : 0;
+    // Headroom, as the reference keeps (dsv4_cuda.cu:317-320).
+    if (r.wbytes + r.sbytes + (256u << 20) > dsv4_cuda_free_vram()) return -1;
+    if (cudaMalloc(&r.dw, r.wbytes) != cudaSuccess) return -1;
+    if (r.sbytes && cudaMalloc(&r.ds, r.sbytes) != cudaSuccess) { cudaFree(r.dw); return -1; }
+    if (cudaMemcpy(r.dw, m->w, r.wbytes, cudaMemcpyHostToDevice) != cudaSuccess ||
+        (r.sbytes && cudaMemcpy(r.ds, m->s, r.sbytes, cudaMemcpyHostToDevice) != cudaSuccess)) {
+        cudaFree(r.dw);
+        if (r.ds) cudaFree(r.ds);
+        return -1;
+    }
+    g.res.push_back(r);
+    return 0;
+}
+
+extern "C" int dsv4_cuda_resident_ptrs(const DSV4QMat *m, const void **dw, const void **ds)
+{
+    int row0;
+    const Resident *r = g.ready ? find(m, &row0) : nullptr;
+    if (!r) return -1;
+    if (dw) *dw = r->dw + (size_t)row0 * r->rowbytes;
+    if (ds) *ds = r->ds ? r->ds + (size_t)(row0 / r->blk_r) * r->sc : nullptr;
+    return 0;
+}
+
+extern "C" void dsv4_cuda_mmq(float *y, const float *x, const DSV4QMat *m)
+{
+    int row0 = 0;
+    const Resident *r = g.ready ? find(m, &row0) : nullptr;
+    if (!r || host_gemv(y, x, *r, row0, m->rows, 1) != 0) {
+        fprintf(stderr, "dsv4_b200: mmq called for a matrix that is not resident\n");
+        abort();
+    }
+}
+
+extern "C" void dsv4_cuda_mmq_n(float *y, const float *x, const DSV4QMat *m, int nt)
+{
+    if (nt <= 1) { dsv4_cuda_mmq(y, x, m); return; }
+    int row0 = 0;
+    const Resident *r = g.ready ? find(m, &row0) : nullptr;
+    if (!r || nt > DSV4_MAX_BATCH || host_gemv(y, x, *r, row0, m->rows, nt) != 0) {
+        fprintf(stderr, "dsv4_b200: mmq_n called for a matrix that is not resident, "
+                        "or a batch that will not stage\n");
+        abort();
+    }
+}
+
+extern "C" void dsv4_cuda_shutdown(void)
+{
+    if (!g.ready) return;
+    cudaStreamSynchronize(g.st);
+    for (Resident &r : g.res) {
+        cudaFree(r.dw);
+        if (r.ds) cudaFree(r.ds);
+    }
+    g.res.clear();
+    if (g.dx) cudaFree(g.dx);
+    if (g.dy) cudaFree(g.dy);
+    if (g.hx) cudaFreeHost(g.hx);
+    if (g.hy) cudaFreeHost(g.hy);
+    g.dx = g.dy = g.hx = g.hy = nullptr;
+    g.xcap = g.ycap = g.hxcap = g.hycap = 0;
+    cudaStreamDestroy(g.st);
+    g.st = nullptr;
+    g.ready = 0;
+}
+
+extern "C" int dsv4_cuda_dump_e4m3(float *host256)
+{
+    if (!g.ready && dsv4_cuda_init() != 0) return -1;
+    float *d = nullptr;
+    DSV4B_CUDA_OK(cudaMalloc(&d, 256 * sizeof(float)));
+    int rc = dump_e4m3(d, g.st);
+    if (rc == 0 && cudaMemcpyAsync(host256, d, 256 * sizeof(float), cudaMemcpyDeviceToHost, g.st) != cudaSuccess) rc = -1;
+    if (cudaStreamSynchronize(g.st) != cudaSuccess) rc = -1;
+    cudaFree(d);
+    return rc;
+}
+
+extern "C" int dsv4b_gemv(int wdt, float *y, const float *x, const void *W, const void *S,
+                          int rows, int cols, int blk_r, int blk_c, int nt, void *stream)
+{
+    if (wdt < DSV4_WF32 || wdt > DSV4_WFP4 || !y || !x || !W) return -1;
+    if (wdt >= DSV4_WFP8 && (!S || blk_r <= 0 || blk_c <= 0)) return -1;
+    return gemv(wdt, y, rows, x, cols, W, (const uint8_t *)S, rows, cols, blk_r, blk_c, nt,
+                stream_of(stream));
+}

@@ -1,0 +1,171 @@
+"""ctypes binding of libdsv4_b200.so (include/dsv4_b200.h).
+
+The product's Python face: the same C ABI the reference's C host links
+against, reachable from numpy (host buffers, layer 1) and from torch CUDA
+tensors (device pointers, layer 2). There is no CPU fallback: loading fails
+loudly when the library is missing, and every call that the C ABI rejects
+raises.
+"""
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libdsv4_b200.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "dsv4_b200.h")
+
+WF32, WBF16, WFP8, WFP4 = 0, 1, 2, 3
+
+
+class QMat(C.Structure):
+    """The reference's DSV4QMat (include/dsv4/dsv4.h:208-214)."""
+    _fields_ = [("w", C.c_void_p), ("s", C.c_void_p), ("wdt", C.c_int),
+                ("rows", C.c_int), ("cols", C.c_int),
+                ("blk_r", C.c_int), ("blk_c", C.c_int)]
+
+
+def build():
+    """Compile the library in-tree (nvcc cross-compiles without a GPU)."""
+    subprocess.run(["make", "-C", HERE, "-j8"], check=True)
+    return LIB_PATH
+
+
+_lib = None
+
+
+def lib():
+    """Load libdsv4_b200.so once; raise if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError("libdsv4_b200.so is not built (run `make -C %s`)" % HERE)
+        _lib = C.CDLL(LIB_PATH)
+        _declare(_lib)
+    return _lib
+
+
+def _declare(L):
+    vp, i, f, sz = C.c_void_p, C.c_int, C.c_float, C.c_size_t
+    qp = C.POINTER(QMat)
+    sig = {
+        "dsv4_cuda_available": ([], i),
+        "dsv4_cuda_init": ([], i),
+        "dsv4_cuda_set_blocking_sync": ([], i),
+        "dsv4_cuda_upload": ([qp], i),
+        "dsv4_cuda_has": ([qp], i),
+        "dsv4_cuda_mmq": ([vp, vp, qp], None),
+        "dsv4_cuda_mmq_n": ([vp, vp, qp, i], None),
+        "dsv4_cuda_free_vram": ([], sz),
+        "dsv4_cuda_shutdown": ([], None),
+        "dsv4_cuda_dump_e4m3": ([vp], i),
+        "dsv4_cuda_resident_ptrs": ([qp, C.POINTER(vp), C.POINTER(vp)], i),
+        "dsv4b_gemv": ([i, vp, vp, vp, vp, i, i, i, i, i, vp], i),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(L, name)
+        fn.argtypes, fn.restype = args, res
+
+
+def header_functions():
+    """Names of every function include/dsv4_b200.h declares."""
+    import re
+    txt = open(HEADER).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(dsv4b?_\w+)\s*\(", txt)))
+
+
+def check(rc, what):
+    if rc != 0:
+        raise RuntimeError("%s failed (rc=%d)" % (what, rc))
+
+
+def ptr(a):
+    """Address of a numpy array or torch tensor."""
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    return a.data_ptr()
+
+
+def stream_ptr(s=None):
+    return None if s is None else s.cuda_stream
+
+
+# ----------------------------------------------------------- host-side API
+
+class Matrix:
+    """A host matrix in one of the checkpoint formats, kept alive while it is
+    resident (the backend keys residency on the host pointer, as the
+    reference's does)."""
+
+    def __init__(self, wdt, W, S=None, rows=None, cols=None, blk=None):
+        self.W = np.ascontiguousarray(W)
+        self.S = None if S is None else np.ascontiguousarray(S, dtype=np.uint8)
+        if rows is None:
+            rows = self.W.shape[0]
+        if cols is None:
+            cols = {WF32: self.W.shape[1], WBF16: self.W.shape[1],
+                    WFP8: self.W.shape[1], WFP4: self.W.shape[1] * 2}[wdt]
+        if blk is None:
+            blk = {WFP8: (128, 128), WFP4: (1, 32)}.get(wdt, (0, 0))
+        self.q = QMat(self.W.ctypes.data, None if self.S is None else self.S.ctypes.data,
+                      wdt, rows, cols, blk[0], blk[1])
+
+    def slice_rows(self, r0, nrows):
+        """A DSV4QMat of rows [r0, r0+nrows), sharing this matrix's bytes --
+        the way the reference layer slices wo_a per group."""
+        m = Matrix.__new__(Matrix)
+        m.W, m.S = self.W, self.S
+        q = self.q
+        rb = {WF32: 4 * q.cols, WBF16: 2 * q.cols, WFP8: q.cols, WFP4: q.cols // 2}[q.wdt]
+        s = None
+        if self.S is not None:
+            sc = -(-q.cols // q.blk_c)
+            s = self.S.ctypes.data + (r0 // q.blk_r) * sc
+        m.q = QMat(self.W.ctypes.data + r0 * rb, s, q.wdt, nrows, q.cols, q.blk_r, q.blk_c)
+        return m
+
+    def upload(self):
+        return lib().dsv4_cuda_upload(C.byref(self.q))
+
+    def has(self):
+        return lib().dsv4_cuda_has(C.byref(self.q))
+
+    def mmq(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        nt = x.size // self.q.cols
+        y = np.empty(nt * self.q.rows, np.float32)
+        if nt == 1:
+            lib().dsv4_cuda_mmq(y.ctypes.data, x.ctypes.data, C.byref(self.q))
+        else:
+            lib().dsv4_cuda_mmq_n(y.ctypes.data, x.ctypes.data, C.byref(self.q), nt)
+        return y.reshape(nt, self.q.rows) if nt > 1 else y
+
+    def device_ptrs(self):
+        dw, ds = C.c_void_p(), C.c_void_p()
+        check(lib().dsv4_cuda_resident_ptrs(C.byref(self.q), C.byref(dw), C.byref(ds)),
+              "dsv4_cuda_resident_ptrs")
+        return dw.value, ds.value
+
+
+def init():
+    L = lib()
+    if not L.dsv4_cuda_available():
+        raise RuntimeError("no CUDA device: the B200 backend has no CPU fallback")
+    check(L.dsv4_cuda_init(), "dsv4_cuda_init")
+    return L
+
+
+def dump_e4m3():
+    out = np.empty(256, np.float32)
+    check(lib().dsv4_cuda_dump_e4m3(out.ctypes.data), "dsv4_cuda_dump_e4m3")
+    return out
+
+
+# ---------------------------------------------------------- device-side API
+
+def gemv(wdt, y, x, W, S, rows, cols, blk_r=0, blk_c=0, nt=1, stream=None):
+    check(lib().dsv4b_gemv(wdt, ptr(y), ptr(x), W if isinstance(W, int) else ptr(W),
+                           None if S is None else (S if isinstance(S, int) else ptr(S)),
+                           rows, cols, blk_r, blk_c, nt, stream_ptr(stream)), "dsv4b_gemv")

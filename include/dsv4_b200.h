@@ -1,0 +1,105 @@
+/* dsv4_b200.h - C ABI of the B200 (sm_100a) decode backend for deepseek-v4-in-c.
+ *
+ * Two layers, both plain C (pointers and sizes, no CUDA or torch types):
+ *
+ * 1. THE DROP-IN. Every symbol the reference host calls through
+ *    include/dsv4/dsv4_cuda.h, with the same names, arguments, 0/-1 returns and
+ *    abort-on-misuse, so libdsv4_b200.so links in place of the reference's
+ *    build/dsv4_cuda.o (reference Makefile:148-160). Widened where the
+ *    reference stops short: uploads accept FP8, FP4, BF16 and F32 (it accepts
+ *    FP8 only, dsv4_cuda.cu:310), and a matrix whose rows lie inside a
+ *    resident matrix -- the grouped wo_a slices of dsv4_layer.c:321-334 -- runs
+ *    on the device instead of silently falling back to the CPU.
+ *    Host-buffer twins of the reference's CPU kernels on the hot path
+ *    (router, expert FFN, indexer, top-k, sparse attention) follow, each with
+ *    the argument meaning of the function it replaces.
+ *
+ * 2. THE DEVICE API (dsv4b_*). The same kernels on device pointers, enqueued
+ *    on a caller stream (a cudaStream_t passed as void*; NULL = the backend's
+ *    own stream), never synchronising, so a whole decode step can be captured
+ *    in a CUDA graph.
+ *
+ * Weight formats are the checkpoint's (reference src/core/dsv4_quant.h):
+ * wdt 0 = F32, 1 = BF16, 2 = FP8 e4m3 + E8M0 blocks (128x128), 3 = FP4 e2m1
+ * packed two per byte (even element in the low nibble) + E8M0 1x32 blocks.
+ */
+#ifndef DSV4_B200_H
+#define DSV4_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifndef DSV4_H
+/* Layout-identical to the reference's DSV4QMat (include/dsv4/dsv4.h:208-214)
+ * and storage tags (:92), so a pointer to the reference's struct can be passed
+ * straight through. When the reference's dsv4.h is included first, its own
+ * definitions are used. */
+typedef struct {
+    const void *w;
+    const void *s;
+    int wdt;
+    int rows, cols;
+    int blk_r, blk_c;
+} DSV4QMat;
+enum { DSV4_WF32 = 0, DSV4_WBF16 = 1, DSV4_WFP8 = 2, DSV4_WFP4 = 3 };
+#define DSV4_MAX_BATCH 64
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ===================================================== 1. the drop-in ===== */
+
+/* include/dsv4/dsv4_cuda.h:65 -- 1 when a CUDA device is present. */
+int dsv4_cuda_available(void);
+
+/* include/dsv4/dsv4_cuda.h:70 -- bring up device 0 (or $DSV4_DEVICE); prints
+ * the device and free HBM. 0 on success, -1 on failure. */
+int dsv4_cuda_init(void);
+
+/* src/cuda/dsv4_cuda.cu:264 -- choose blocking sync; call before init. */
+int dsv4_cuda_set_blocking_sync(void);
+
+/* include/dsv4/dsv4_cuda.h:80 -- copy one matrix to HBM, keyed by its host
+ * weight pointer. 0 on success (or already resident), -1 = keep it on the CPU
+ * (recoverable: no device, would not fit, unsupported format). */
+int dsv4_cuda_upload(const DSV4QMat *m);
+
+/* include/dsv4/dsv4_cuda.h:83 -- 1 when m runs on the device: uploaded
+ * itself, or a whole-row-block slice of an uploaded matrix. */
+int dsv4_cuda_has(const DSV4QMat *m);
+
+/* include/dsv4/dsv4_cuda.h:88 -- y[rows] = m * x[cols], host buffers,
+ * synchronous. abort() if !dsv4_cuda_has(m), as the reference does. */
+void dsv4_cuda_mmq(float *y, const float *x, const DSV4QMat *m);
+
+/* include/dsv4/dsv4_cuda.h:94 -- x [nt][cols] -> y [nt][rows], one pass over
+ * the weights per 8 tokens; nt <= DSV4_MAX_BATCH (abort otherwise). Each
+ * token's result is bit-identical to a dsv4_cuda_mmq call. */
+void dsv4_cuda_mmq_n(float *y, const float *x, const DSV4QMat *m, int nt);
+
+/* include/dsv4/dsv4_cuda.h:97 -- bytes of HBM still free. */
+size_t dsv4_cuda_free_vram(void);
+
+/* include/dsv4/dsv4_cuda.h:99 -- release every device buffer. */
+void dsv4_cuda_shutdown(void);
+
+/* src/cuda/dsv4_cuda.cu:460 -- the device e4m3 decoder on all 256 codes. */
+int dsv4_cuda_dump_e4m3(float *host256);
+
+/* Device copies of a resident matrix (the slice's own rows for a slice), so
+ * a caller can reach the same weights through the device API. 0 or -1. */
+int dsv4_cuda_resident_ptrs(const DSV4QMat *m, const void **dw, const void **ds);
+
+/* ===================================================== 2. device API ====== */
+
+/* y[t*rows + o] = sum_c W[o][c] * x[t*cols + c] for t < nt; any nt >= 1.
+ * W/S are device pointers in the storage format `wdt`. 0 or -1. */
+int dsv4b_gemv(int wdt, float *y, const float *x, const void *W, const void *S,
+               int rows, int cols, int blk_r, int blk_c, int nt, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DSV4_B200_H */

@@ -149,6 +149,7 @@ extern "C" int dsv4_cuda_init(void)
         return -1;
     }
     DSV4B_CUDA_OK(cudaStreamCreateWithFlags(&g.st, cudaStreamNonBlocking));
+    if (workspace_init() != 0) { fprintf(stderr, "dsv4_b200: workspace allocation failed\n"); return -1; }
     size_t fr = 0, tot = 0;
     DSV4B_CUDA_OK(cudaMemGetInfo(&fr, &tot));
     printf("cuda: %s, sm_%d%d, %d SMs, %.2f GB free of %.2f GB\n", p.name, p.major, p.minor,
@@ -203,6 +204,22 @@ extern "C" int dsv4_cuda_upload(const DSV4QMat *m)
     return 0;
 }
 
+extern "C" int dsv4_cuda_evict(const DSV4QMat *m)
+{
+    if (!g.ready || !m) return -1;
+    for (size_t i = 0; i < g.res.size(); i++) {
+        Resident &r = g.res[i];
+        if (r.key == m->w && r.rows == m->rows && r.cols == m->cols && r.wdt == m->wdt) {
+            cudaStreamSynchronize(g.st);
+            cudaFree(r.dw);
+            if (r.ds) cudaFree(r.ds);
+            g.res.erase(g.res.begin() + (long)i);
+            return 0;
+        }
+    }
+    return -1;
+}
+
 extern "C" int dsv4_cuda_resident_ptrs(const DSV4QMat *m, const void **dw, const void **ds)
 {
     int row0;
@@ -250,6 +267,7 @@ extern "C" void dsv4_cuda_shutdown(void)
     if (g.hy) cudaFreeHost(g.hy);
     g.dx = g.dy = g.hx = g.hy = nullptr;
     g.xcap = g.ycap = g.hxcap = g.hycap = 0;
+    workspace_free();
     cudaStreamDestroy(g.st);
     g.st = nullptr;
     g.ready = 0;

@@ -1,69 +1,31 @@
-// gemv.cu - block-scaled GEMV / skinny GEMM against HBM-resident weights.
+// gemv.cu - GEMV / skinny GEMM against HBM-resident weights: the register
+// kernel (batched tokens, and shapes the TMA pipeline does not take), the
+// generic any-shape kernel, and the dispatch.
 //
 // Replaces the reference's k_mmq_fp8 / k_mmq_fp8_n (src/cuda/dsv4_cuda.cu:93-230)
 // and widens it to the four storage formats dsv4_mmq dispatches on
 // (src/core/dsv4_matmul.c:516-591): FP8 128x128, FP4 1x32, BF16 and F32.
-//
-// Batch-1 decode is HBM-bound (one multiply-add per weight byte for FP8), so
-// the kernel is a weight stream: every lane issues 16-byte non-allocating loads,
-// several rows x several units deep, decodes in registers with the hardware
-// e4m3/e2m1 converters and multiplies with packed f32x2 FMAs. x is read through
-// L1 (it is shared by every row) and each x chunk is reused by R rows.
-//
-// ARITHMETIC (fixed, independent of R, NT and the grid):
-//   a 16-byte unit of one row holds EPU elements (4 f32, 8 bf16, 16 fp8,
-//   32 fp4) that never straddle a scale block. Its dot product is two float
-//   chains (even / odd elements, fma in element order), summed, multiplied by
-//   the block scale (exact: a power of two), and added into a per-lane DOUBLE.
-//   Lanes take units lane, lane+32, ...; the 32 lane totals are folded by a
-//   fixed xor butterfly in double and rounded to float once.
-// The reduction of one (row, token) therefore never depends on how many rows or
-// tokens share the launch, which makes mmq_n bit-identical to nt separate mmq
-// calls -- the property the reference's GPU gate checks
-// (tests/unit/test_cuda.c:194-257). Against the reference CPU's double tree it
-// agrees to ~1e-7 relative.
-#include "common.cuh"
+// Batch-1 calls go to the TMA pipeline in gemv_tma.cu; every kernel sums in
+// the order fixed by gemv_core.cuh, so a token's result never depends on the
+// kernel, the grid or the batch it ran in.
+#include "gemv_core.cuh"
 #include "internal.h"
 
 namespace dsv4b {
 
-template <int FMT> struct Fmt;
-template <> struct Fmt<DSV4B_WF32> { static constexpr int EPU = 4; static constexpr bool SC = false; };
-template <> struct Fmt<DSV4B_WBF16> { static constexpr int EPU = 8; static constexpr bool SC = false; };
-template <> struct Fmt<DSV4B_WFP8> { static constexpr int EPU = 16; static constexpr bool SC = true; };
-template <> struct Fmt<DSV4B_WFP4> { static constexpr int EPU = 32; static constexpr bool SC = true; };
-
-// Decode elements [4k, 4k+4) of a unit into two float pairs.
-template <int FMT>
-__device__ __forceinline__ void decode4(const uint4 &u, int k, float2 &a, float2 &b)
-{
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-    if constexpr (FMT == DSV4B_WF32) {
-        a = make_float2(__uint_as_float(w[0]), __uint_as_float(w[1]));
-        b = make_float2(__uint_as_float(w[2]), __uint_as_float(w[3]));
-    } else if constexpr (FMT == DSV4B_WBF16) {
-        a = bf16x2(w[2 * k]);
-        b = bf16x2(w[2 * k + 1]);
-    } else if constexpr (FMT == DSV4B_WFP8) {
-        a = e4m3x2((uint16_t)(w[k] & 0xFFFFu));
-        b = e4m3x2((uint16_t)(w[k] >> 16));
-    } else {
-        const uint32_t h = w[k >> 1] >> ((k & 1) * 16);
-        a = e2m1x2((uint8_t)(h & 0xFFu));
-        b = e2m1x2((uint8_t)((h >> 8) & 0xFFu));
-    }
-}
-
-template <int FMT, int NT, int R, int U>
+// One warp: R rows x NT tokens. Half-warp h takes segments j = h, h+2, ...;
+// lane (l & 15) takes unit 16j + (l & 15). Segment sums fold into lane 0's
+// double totals in segment order (seg 2m from half 0, then 2m+1 from half 1).
+template <int FMT, int NT, int R, int UP>
 __global__ void __launch_bounds__(64)
-k_gemv(GemvArgs g)
+k_gemv_reg(GemvArgs g)
 {
     constexpr int EPU = Fmt<FMT>::EPU;
-    const int lane = threadIdx.x & 31;
+    const int lane = threadIdx.x & 31, half = lane >> 4, li = lane & 15;
     const int warp = (int)((blockIdx.x * (unsigned)blockDim.x + threadIdx.x) >> 5);
     const int row0 = warp * R;
     if (row0 >= g.rows) return;
-    const int upr = g.rowbytes >> 4;
+    const int upr = g.rowbytes >> 4, nseg = (upr + 15) >> 4;
 
     const uint8_t *wr[R];
     int srow[R];
@@ -71,77 +33,64 @@ k_gemv(GemvArgs g)
     for (int r = 0; r < R; r++) {
         const int o = min(row0 + r, g.rows - 1);
         wr[r] = g.W + (size_t)o * g.rowbytes;
-        srow[r] = (o / g.blk_r) * g.sc;
+        srow[r] = Fmt<FMT>::SC ? ((FMT == DSV4B_WFP4) ? o * g.sc : (o / g.blk_r) * g.sc) : 0;
     }
-
-    double acc[R][NT];
+    double tot[R][NT];
 #pragma unroll
     for (int r = 0; r < R; r++)
 #pragma unroll
-        for (int t = 0; t < NT; t++) acc[r][t] = 0.0;
+        for (int t = 0; t < NT; t++) tot[r][t] = 0.0;
 
-    for (int u0 = lane; u0 < upr; u0 += 32 * U) {
-        uint4 wv[U][R];
+    for (int m0 = 0; m0 < nseg; m0 += 2 * UP) {
+        uint4 wv[UP][R];
 #pragma unroll
-        for (int j = 0; j < U; j++) {
-            const int u = u0 + 32 * j;
+        for (int j = 0; j < UP; j++) {
+            const int seg = m0 + 2 * j + half, u = seg * 16 + li;
 #pragma unroll
             for (int r = 0; r < R; r++)
-                if (u < upr) wv[j][r] = ld_stream16(wr[r] + (size_t)u * 16);
+                if (seg < nseg && u < upr) wv[j][r] = ld_stream16(wr[r] + (size_t)u * 16);
         }
 #pragma unroll
-        for (int j = 0; j < U; j++) {
-            const int u = u0 + 32 * j;
-            if (u < upr) {
-                const int col0 = u * EPU;
-                float2 c[R][NT];
+        for (int j = 0; j < UP; j++) {
+            const int seg = m0 + 2 * j + half, u = seg * 16 + li;
+            const bool ok = (seg < nseg && u < upr);
+            float q[R][NT];
 #pragma unroll
-                for (int r = 0; r < R; r++)
-#pragma unroll
-                    for (int t = 0; t < NT; t++) c[r][t] = make_float2(0.f, 0.f);
-#pragma unroll
-                for (int k = 0; k < EPU / 4; k++) {
-                    float4 xv[NT];
-#pragma unroll
-                    for (int t = 0; t < NT; t++)
-                        xv[t] = ld_f4(g.x + (size_t)t * g.xstride + col0 + 4 * k);
-#pragma unroll
-                    for (int r = 0; r < R; r++) {
-                        float2 wa, wb;
-                        decode4<FMT>(wv[j][r], k, wa, wb);
-#pragma unroll
-                        for (int t = 0; t < NT; t++) {
-                            c[r][t] = fma2(wa, make_float2(xv[t].x, xv[t].y), c[r][t]);
-                            c[r][t] = fma2(wb, make_float2(xv[t].z, xv[t].w), c[r][t]);
-                        }
-                    }
+            for (int r = 0; r < R; r++) {
+                float s = 1.0f;
+                if constexpr (Fmt<FMT>::SC) {
+                    if (ok) s = e8m0(__ldg(g.S + srow[r] + (u * EPU) / g.blk_c));
                 }
 #pragma unroll
-                for (int r = 0; r < R; r++) {
-                    double s = 1.0;
-                    if constexpr (Fmt<FMT>::SC) s = (double)e8m0(g.S[srow[r] + col0 / g.blk_c]);
-#pragma unroll
-                    for (int t = 0; t < NT; t++) {
-                        const float p = __fadd_rn(c[r][t].x, c[r][t].y);
-                        acc[r][t] = __fma_rn((double)p, s, acc[r][t]);
-                    }
-                }
+                for (int t = 0; t < NT; t++)
+                    q[r][t] = ok ? __fmul_rn(unit_dot<FMT>(wv[j][r], g.x + (size_t)t * g.xstride + (size_t)u * EPU), s)
+                                 : 0.0f;
             }
+            const int sev = m0 + 2 * j;
+#pragma unroll
+            for (int r = 0; r < R; r++)
+#pragma unroll
+                for (int t = 0; t < NT; t++) {
+                    const float v = seg_sum16(q[r][t]);
+                    const float vodd = __shfl_sync(0xffffffffu, v, 16);
+                    if (lane == 0) {
+                        if (sev < nseg) tot[r][t] = __dadd_rn(tot[r][t], (double)v);
+                        if (sev + 1 < nseg) tot[r][t] = __dadd_rn(tot[r][t], (double)vodd);
+                    }
+                }
         }
     }
+    if (lane == 0)
 #pragma unroll
-    for (int r = 0; r < R; r++)
+        for (int r = 0; r < R; r++)
 #pragma unroll
-        for (int t = 0; t < NT; t++) {
-            const double v = warp_sum_d(acc[r][t]);
-            if (lane == 0 && row0 + r < g.rows)
-                g.y[(size_t)t * g.ystride + row0 + r] = (float)v;
-        }
+            for (int t = 0; t < NT; t++)
+                if (row0 + r < g.rows) g.y[(size_t)t * g.ystride + row0 + r] = (float)tot[r][t];
 }
 
 // Any shape: one warp per (row, token), scalar loads, exact products summed in
 // double. Only reached by shapes whose rows are not 16-byte multiples (the
-// reference's hand-sized test matrices); every model matrix takes k_gemv.
+// reference's hand-sized test matrices); every model matrix takes the others.
 __global__ void k_gemv_generic(GemvArgs g, int fmt, int nt)
 {
     const int lane = threadIdx.x & 31;
@@ -168,12 +117,12 @@ __global__ void k_gemv_generic(GemvArgs g, int fmt, int nt)
 template <int FMT, int NT>
 static void launch_nt(const GemvArgs &g, cudaStream_t st)
 {
-    constexpr int R = (NT <= 2) ? 4 : (NT <= 4 ? 2 : 1);
-    constexpr int U = (NT <= 4) ? 4 : 2;
+    constexpr int R = (NT <= 2) ? 2 : 1;
+    constexpr int UP = (NT <= 2) ? 2 : 1;
     const int warps = (g.rows + R - 1) / R;
     const int threads = 64;
     const int blocks = (warps * 32 + threads - 1) / threads;
-    k_gemv<FMT, NT, R, U><<<blocks, threads, 0, st>>>(g);
+    k_gemv_reg<FMT, NT, R, UP><<<blocks, threads, 0, st>>>(g);
 }
 
 template <int FMT>
@@ -214,6 +163,23 @@ bool gemv_vectorizable(int fmt, const void *W, int cols, int blk_c, const float 
     return true;
 }
 
+int gemv_reg(const GemvArgs &g0, int fmt, int nt, cudaStream_t st)
+{
+    GemvArgs g = g0;
+    for (int t0 = 0; t0 < nt; t0 += 8) {
+        const int n = (nt - t0 < 8) ? nt - t0 : 8;
+        g.x = g0.x + (size_t)t0 * g0.xstride;
+        g.y = g0.y + (size_t)t0 * g0.ystride;
+        switch (fmt) {
+        case DSV4B_WF32: launch_fmt<DSV4B_WF32>(g, n, st); break;
+        case DSV4B_WBF16: launch_fmt<DSV4B_WBF16>(g, n, st); break;
+        case DSV4B_WFP8: launch_fmt<DSV4B_WFP8>(g, n, st); break;
+        default: launch_fmt<DSV4B_WFP4>(g, n, st); break;
+        }
+    }
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
+}
+
 int gemv(int fmt, float *y, long ystride, const float *x, long xstride,
          const void *W, const uint8_t *S, int rows, int cols, int blk_r,
          int blk_c, int nt, cudaStream_t st)
@@ -227,24 +193,18 @@ int gemv(int fmt, float *y, long ystride, const float *x, long xstride,
     g.sc = fmt >= DSV4B_WFP8 ? (cols + g.blk_c - 1) / g.blk_c : 0;
     g.rowbytes = (int)row_bytes(fmt, cols);
     g.xstride = xstride; g.ystride = ystride;
+    g.x = x; g.y = y;
     if (!gemv_vectorizable(fmt, W, cols, blk_c, x, xstride)) {
-        g.x = x; g.y = y;
         const long warps = (long)rows * nt;
         k_gemv_generic<<<(unsigned)((warps * 32 + 127) / 128), 128, 0, st>>>(g, fmt, nt);
         return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
     }
-    for (int t0 = 0; t0 < nt; t0 += 8) {
-        const int n = (nt - t0 < 8) ? nt - t0 : 8;
-        g.x = x + (size_t)t0 * xstride;
-        g.y = y + (size_t)t0 * ystride;
-        switch (fmt) {
-        case DSV4B_WF32: launch_fmt<DSV4B_WF32>(g, n, st); break;
-        case DSV4B_WBF16: launch_fmt<DSV4B_WBF16>(g, n, st); break;
-        case DSV4B_WFP8: launch_fmt<DSV4B_WFP8>(g, n, st); break;
-        default: launch_fmt<DSV4B_WFP4>(g, n, st); break;
-        }
+    if (nt == 1 && gemv_tma_ok(fmt, g)) {
+        TmaGroup grp = {};
+        grp.W = g.W; grp.S = g.S; grp.x = x; grp.y = y; grp.rows = rows; grp.sel = -1;
+        return gemv_tma(fmt, &grp, 1, cols, g.blk_r, g.blk_c, nullptr, st);
     }
-    return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
+    return gemv_reg(g, fmt, nt, st);
 }
 
 // Device decoder dump for the all-codes gate (reference dsv4_cuda.cu:454-469).

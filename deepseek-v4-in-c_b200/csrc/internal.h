@@ -17,6 +17,19 @@ struct GemvArgs {
     long xstride, ystride;
 };
 
+// One matrix of a grouped TMA GEMV launch. With sel >= 0 the weights are
+// W + sel_idx[sel] * wstride (and S likewise): a routed expert picked on the
+// device, read without a host round trip.
+struct TmaGroup {
+    const uint8_t *W, *S;
+    long wstride, sstride;
+    const float *x;
+    float *y;
+    int rows, sel;
+};
+
+constexpr int kTmaMaxGroups = 16;
+
 size_t row_bytes(int fmt, int cols);
 bool gemv_vectorizable(int fmt, const void *W, int cols, int blk_c,
                        const float *x, long xstride);
@@ -24,6 +37,25 @@ bool gemv_vectorizable(int fmt, const void *W, int cols, int blk_c,
 int gemv(int fmt, float *y, long ystride, const float *x, long xstride,
          const void *W, const uint8_t *S, int rows, int cols, int blk_r,
          int blk_c, int nt, cudaStream_t st);
+int gemv_reg(const GemvArgs &g, int fmt, int nt, cudaStream_t st);
+bool gemv_tma_ok(int fmt, const GemvArgs &g);
+// Batch-1 GEMV of up to kTmaMaxGroups matrices sharing format and width.
+int gemv_tma(int fmt, const TmaGroup *grp, int ngroups, int cols, int blk_r,
+             int blk_c, const int *sel_idx, cudaStream_t st);
 int dump_e4m3(float *dev_out, cudaStream_t st);
+
+// Per-device scratch of the split-tile protocol (segment partial sums and
+// arrival counters), allocated once at init. Counters return to zero at the
+// end of every launch.
+struct Workspace {
+    float *segbuf;
+    int *cnt;
+    int *err;
+    int slots;
+    int nsm;
+};
+Workspace &workspace();
+int workspace_init();
+void workspace_free();
 
 }  // namespace dsv4b

@@ -60,6 +60,7 @@ def _declare(L):
         "dsv4_cuda_free_vram": ([], sz),
         "dsv4_cuda_shutdown": ([], None),
         "dsv4_cuda_dump_e4m3": ([vp], i),
+        "dsv4_cuda_evict": ([qp], i),
         "dsv4_cuda_resident_ptrs": ([qp, C.POINTER(vp), C.POINTER(vp)], i),
         "dsv4b_gemv": ([i, vp, vp, vp, vp, i, i, i, i, i, vp], i),
     }
@@ -127,7 +128,23 @@ class Matrix:
         return m
 
     def upload(self):
-        return lib().dsv4_cuda_upload(C.byref(self.q))
+        rc = lib().dsv4_cuda_upload(C.byref(self.q))
+        self._owned = (rc == 0)
+        return rc
+
+    def evict(self):
+        if getattr(self, "_owned", False):
+            self._owned = False
+            return lib().dsv4_cuda_evict(C.byref(self.q))
+        return -1
+
+    def __del__(self):
+        # Residency is keyed on the host address (as in the reference); once
+        # this buffer is freed the address may be reused by another matrix.
+        try:
+            self.evict()
+        except Exception:
+            pass
 
     def has(self):
         return lib().dsv4_cuda_has(C.byref(self.q))

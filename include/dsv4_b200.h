@@ -88,6 +88,11 @@ void dsv4_cuda_shutdown(void);
 /* src/cuda/dsv4_cuda.cu:460 -- the device e4m3 decoder on all 256 codes. */
 int dsv4_cuda_dump_e4m3(float *host256);
 
+/* Release the device copy of an uploaded matrix (exact match only), so its
+ * host buffer may be freed and its address reused. No reference counterpart:
+ * the reference never releases a single matrix before shutdown. 0 or -1. */
+int dsv4_cuda_evict(const DSV4QMat *m);
+
 /* Device copies of a resident matrix (the slice's own rows for a slice), so
  * a caller can reach the same weights through the device API. 0 or -1. */
 int dsv4_cuda_resident_ptrs(const DSV4QMat *m, const void **dw, const void **ds);

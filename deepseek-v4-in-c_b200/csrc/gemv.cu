@@ -8,32 +8,37 @@
 // Batch-1 calls go to the TMA pipeline in gemv_tma.cu; every kernel sums in
 // the order fixed by gemv_core.cuh, so a token's result never depends on the
 // kernel, the grid or the batch it ran in.
+#include <stdlib.h>
+
 #include "gemv_core.cuh"
 #include "internal.h"
 
 namespace dsv4b {
 
 // One warp: R rows x NT tokens. Half-warp h takes segments j = h, h+2, ...;
-// lane (l & 15) takes unit 16j + (l & 15). Segment sums fold into lane 0's
-// double totals in segment order (seg 2m from half 0, then 2m+1 from half 1).
+// lane li = l & 15 takes the NSTEP steps of gemv_core.cuh in that segment.
+// Segment sums fold into lane 0's double totals in segment order (seg 2m from
+// half 0, then 2m+1 from half 1). x is read once per (segment, token) and
+// reused by the R rows.
 template <int FMT, int NT, int R, int UP>
 __global__ void __launch_bounds__(64)
 k_gemv_reg(GemvArgs g)
 {
-    constexpr int EPU = Fmt<FMT>::EPU;
+    using F = Fmt<FMT>;
+    constexpr int NS = F::NSTEP, SB = F::SB;
     const int lane = threadIdx.x & 31, half = lane >> 4, li = lane & 15;
     const int warp = (int)((blockIdx.x * (unsigned)blockDim.x + threadIdx.x) >> 5);
     const int row0 = warp * R;
     if (row0 >= g.rows) return;
-    const int upr = g.rowbytes >> 4, nseg = (upr + 15) >> 4;
+    const int rb = g.rowbytes, nseg = (rb + 255) >> 8;
 
     const uint8_t *wr[R];
     int srow[R];
 #pragma unroll
     for (int r = 0; r < R; r++) {
         const int o = min(row0 + r, g.rows - 1);
-        wr[r] = g.W + (size_t)o * g.rowbytes;
-        srow[r] = Fmt<FMT>::SC ? ((FMT == DSV4B_WFP4) ? o * g.sc : (o / g.blk_r) * g.sc) : 0;
+        wr[r] = g.W + (size_t)o * rb;
+        srow[r] = F::SC ? (o >> g.lbr) * g.sc : 0;
     }
     double tot[R][NT];
 #pragma unroll
@@ -42,29 +47,50 @@ k_gemv_reg(GemvArgs g)
         for (int t = 0; t < NT; t++) tot[r][t] = 0.0;
 
     for (int m0 = 0; m0 < nseg; m0 += 2 * UP) {
-        uint4 wv[UP][R];
+        uint4 wv[UP][R][NS];
 #pragma unroll
         for (int j = 0; j < UP; j++) {
-            const int seg = m0 + 2 * j + half, u = seg * 16 + li;
+            const int seg = m0 + 2 * j + half;
 #pragma unroll
-            for (int r = 0; r < R; r++)
-                if (seg < nseg && u < upr) wv[j][r] = ld_stream16(wr[r] + (size_t)u * 16);
+            for (int k = 0; k < NS; k++) {
+                const int off = seg * 256 + SB * (16 * k + li);
+#pragma unroll
+                for (int r = 0; r < R; r++)
+                    wv[j][r][k] = (seg < nseg && off < rb) ? ldg_step<FMT>(wr[r] + off) : make_uint4(0u, 0u, 0u, 0u);
+            }
         }
 #pragma unroll
         for (int j = 0; j < UP; j++) {
-            const int seg = m0 + 2 * j + half, u = seg * 16 + li;
-            const bool ok = (seg < nseg && u < upr);
+            const int seg = m0 + 2 * j + half;
             float q[R][NT];
 #pragma unroll
-            for (int r = 0; r < R; r++) {
-                float s = 1.0f;
-                if constexpr (Fmt<FMT>::SC) {
-                    if (ok) s = e8m0(__ldg(g.S + srow[r] + (u * EPU) / g.blk_c));
-                }
+            for (int r = 0; r < R; r++)
 #pragma unroll
-                for (int t = 0; t < NT; t++)
-                    q[r][t] = ok ? __fmul_rn(unit_dot<FMT>(wv[j][r], g.x + (size_t)t * g.xstride + (size_t)u * EPU), s)
-                                 : 0.0f;
+                for (int t = 0; t < NT; t++) q[r][t] = 0.0f;
+            if (seg < nseg) {
+                const int e0 = seg * 256 * 4 / SB;
+                int nvalid = 0;
+#pragma unroll
+                for (int k = 0; k < NS; k++) nvalid += (seg * 256 + SB * (16 * k + li) < rb) ? 1 : 0;
+                const StepMasks m = step_masks<FMT>(e0, li, nvalid, g.lbc);
+                float s[R][NS];
+#pragma unroll
+                for (int r = 0; r < R; r++)
+#pragma unroll
+                    for (int k = 0; k < NS; k++)
+                        s[r][k] = (F::SC && k < nvalid) ? e8m0(__ldg(g.S + srow[r] + ((e0 + 4 * (16 * k + li)) >> g.lbc)))
+                                                        : 1.0f;
+#pragma unroll
+                for (int t = 0; t < NT; t++) {
+                    float4 xv[NS];
+#pragma unroll
+                    for (int k = 0; k < NS; k++)
+                        xv[k] = (k < nvalid) ? __ldg(reinterpret_cast<const float4 *>(
+                                                   g.x + (size_t)t * g.xstride + e0 + 4 * (16 * k + li)))
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int r = 0; r < R; r++) q[r][t] = lane_q<FMT>(wv[j][r], xv, s[r], m);
+                }
             }
             const int sev = m0 + 2 * j;
 #pragma unroll
@@ -114,15 +140,39 @@ __global__ void k_gemv_generic(GemvArgs g, int fmt, int nt)
     if (lane == 0) g.y[(size_t)t * g.ystride + o] = (float)acc;
 }
 
-template <int FMT, int NT>
-static void launch_nt(const GemvArgs &g, cudaStream_t st)
+template <int FMT, int NT, int R, int UP>
+static void launch_ru(const GemvArgs &g, cudaStream_t st)
 {
-    constexpr int R = (NT <= 2) ? 2 : 1;
-    constexpr int UP = (NT <= 2) ? 2 : 1;
     const int warps = (g.rows + R - 1) / R;
     const int threads = 64;
     const int blocks = (warps * 32 + threads - 1) / threads;
     k_gemv_reg<FMT, NT, R, UP><<<blocks, threads, 0, st>>>(g);
+}
+
+template <int FMT, int NT>
+static void launch_nt(const GemvArgs &g, cudaStream_t st)
+{
+    if constexpr (NT == 1) {
+        // rows per warp x segment pairs in flight, chosen by measurement
+        static const int ru = [] {
+            const char *e = getenv("DSV4B_GEMV_RU");
+            return e ? atoi(e) : 22;
+        }();
+        switch (ru) {
+        case 11: launch_ru<FMT, 1, 1, 1>(g, st); return;
+        case 12: launch_ru<FMT, 1, 1, 2>(g, st); return;
+        case 14: launch_ru<FMT, 1, 1, 4>(g, st); return;
+        case 18: launch_ru<FMT, 1, 1, 8>(g, st); return;
+        case 22: launch_ru<FMT, 1, 2, 2>(g, st); return;
+        case 24: launch_ru<FMT, 1, 2, 4>(g, st); return;
+        case 42: launch_ru<FMT, 1, 4, 2>(g, st); return;
+        default: launch_ru<FMT, 1, 2, 2>(g, st); return;
+        }
+    } else {
+        constexpr int R = (NT <= 2) ? 2 : 1;
+        constexpr int UP = (NT <= 2) ? 2 : 1;
+        launch_ru<FMT, NT, R, UP>(g, st);
+    }
 }
 
 template <int FMT>
@@ -144,6 +194,13 @@ static int epu_of(int fmt)
 {
     return fmt == DSV4B_WF32 ? 4 : fmt == DSV4B_WBF16 ? 8 : fmt == DSV4B_WFP8 ? 16 : 32;
 }
+static int log2_exact(int v)
+{
+    if (v <= 0 || (v & (v - 1))) return -1;
+    int l = 0;
+    while ((1 << l) < v) l++;
+    return l;
+}
 
 size_t row_bytes(int fmt, int cols)
 {
@@ -155,11 +212,13 @@ size_t row_bytes(int fmt, int cols)
     }
 }
 
-bool gemv_vectorizable(int fmt, const void *W, int cols, int blk_c, const float *x, long xstride)
+bool gemv_vectorizable(int fmt, const void *W, int cols, int blk_r, int blk_c, const float *x, long xstride)
 {
     const size_t rb = row_bytes(fmt, cols);
     if (rb % 16 || ((uintptr_t)W & 15) || ((uintptr_t)x & 15) || (xstride & 3)) return false;
-    if (fmt >= DSV4B_WFP8 && (blk_c <= 0 || blk_c % epu_of(fmt))) return false;
+    // scale blocks: powers of two, and a step's 4 elements inside one block
+    if (fmt >= DSV4B_WFP8 && (log2_exact(blk_c) < 2 || log2_exact(blk_r) < 0)) return false;
+    (void)epu_of;
     return true;
 }
 
@@ -194,12 +253,21 @@ int gemv(int fmt, float *y, long ystride, const float *x, long xstride,
     g.rowbytes = (int)row_bytes(fmt, cols);
     g.xstride = xstride; g.ystride = ystride;
     g.x = x; g.y = y;
-    if (!gemv_vectorizable(fmt, W, cols, blk_c, x, xstride)) {
+    g.lbr = fmt >= DSV4B_WFP8 ? log2_exact(g.blk_r) : 0;
+    g.lbc = fmt >= DSV4B_WFP8 ? log2_exact(g.blk_c) : 30;
+    if (!gemv_vectorizable(fmt, W, cols, g.blk_r, blk_c, x, xstride)) {
         const long warps = (long)rows * nt;
         k_gemv_generic<<<(unsigned)((warps * 32 + 127) / 128), 128, 0, st>>>(g, fmt, nt);
         return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
     }
-    if (nt == 1 && gemv_tma_ok(fmt, g)) {
+    // Batch-1 path: the register kernel measured faster than the TMA stream
+    // on every model shape (both are bound by CUDA-core dequantisation, not
+    // HBM); DSV4B_GEMV_PATH=tma selects the stream.
+    static const int use_tma = [] {
+        const char *e = getenv("DSV4B_GEMV_PATH");
+        return (e && e[0] == 't') ? 1 : 0;
+    }();
+    if (nt == 1 && use_tma && gemv_tma_ok(fmt, g)) {
         TmaGroup grp = {};
         grp.W = g.W; grp.S = g.S; grp.x = x; grp.y = y; grp.rows = rows; grp.sel = -1;
         return gemv_tma(fmt, &grp, 1, cols, g.blk_r, g.blk_c, nullptr, st);

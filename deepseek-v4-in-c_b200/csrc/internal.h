@@ -14,6 +14,7 @@ struct GemvArgs {
     const uint8_t *W;
     const uint8_t *S;
     int rows, cols, blk_r, blk_c, sc, rowbytes;
+    int lbr, lbc;           // log2 of the (power-of-two) block sizes
     long xstride, ystride;
 };
 
@@ -31,7 +32,7 @@ struct TmaGroup {
 constexpr int kTmaMaxGroups = 16;
 
 size_t row_bytes(int fmt, int cols);
-bool gemv_vectorizable(int fmt, const void *W, int cols, int blk_c,
+bool gemv_vectorizable(int fmt, const void *W, int cols, int blk_r, int blk_c,
                        const float *x, long xstride);
 // y[t*ystride + o] = sum_c W[o][c] * x[t*xstride + c], t < nt, o < rows.
 int gemv(int fmt, float *y, long ystride, const float *x, long xstride,

@@ -153,3 +153,37 @@ def test_device_api_with_torch_tensors(dev, port):
 def test_misuse_is_refused(dev):
     bad = B.Matrix(B.WFP8, np.zeros((128, 128), np.uint8), None)   # no scales
     assert bad.upload() == -1 and bad.has() == 0
+
+
+@pytest.mark.parametrize("fmt,rows,cols", [(B.WFP8, 300, 4000), (B.WBF16, 130, 2000),
+                                           (B.WF32, 70, 1000), (B.WFP4, 260, 4096),
+                                           (B.WFP8, 16, 16384), (B.WBF16, 1000, 4096)])
+def test_single_and_batched_bit_identical_all_formats(dev, port, fmt, rows, cols):
+    """Batch-1 calls take the TMA stream, batched calls the register kernel;
+    both sum in the same fixed order, so every token must match bitwise.
+    Shapes include partial chunks and partial 256-byte segments."""
+    rng = np.random.default_rng(rows + cols)
+    if fmt == B.WFP8:
+        W, S = Q.random_fp8(rng, rows, cols)
+    elif fmt == B.WFP4:
+        W, S = Q.random_fp4(rng, rows, cols)
+    elif fmt == B.WBF16:
+        W, S = Q.bf16_encode(rng.standard_normal((rows, cols)).astype(np.float32) * 0.05), None
+    else:
+        W, S = (rng.standard_normal((rows, cols)) * 0.05).astype(np.float32), None
+    m = B.Matrix(fmt, W, S, cols=cols)
+    assert m.upload() == 0
+    xn = rng.standard_normal((3, cols)).astype(np.float32)
+    yn = m.mmq(xn)
+    for t in range(3):
+        y1 = m.mmq(xn[t])
+        assert y1.tobytes() == yn[t].tobytes(), "token %d" % t
+        if fmt == B.WFP8:
+            ref = port.gemv_fp8(xn[t], W, S, rows, cols)
+        elif fmt == B.WFP4:
+            ref = port.gemv_fp4(xn[t], W, S, rows, cols)
+        elif fmt == B.WBF16:
+            ref = port.gemv_bf16(xn[t], W, rows, cols)
+        else:
+            ref = port.gemv_f32(xn[t], W, rows, cols)
+        assert vrel(y1, ref) < TOL

@@ -13,6 +13,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "moe.h"
 #include "../../include/dsv4_b200.h"
 
 namespace dsv4b {
@@ -292,4 +293,141 @@ extern "C" int dsv4b_gemv(int wdt, float *y, const float *x, const void *W, cons
     if (wdt >= DSV4_WFP8 && (!S || blk_r <= 0 || blk_c <= 0)) return -1;
     return gemv(wdt, y, rows, x, cols, W, (const uint8_t *)S, rows, cols, blk_r, blk_c, nt,
                 stream_of(stream));
+}
+
+// ------------------------------------------------------------------- MoE ---
+
+namespace dsv4b {
+
+static bool devmat(const DSV4QMat *m, DevMat &d)
+{
+    int row0 = 0;
+    const Resident *r = find(m, &row0);
+    if (!r) return false;
+    d.w = r->dw + (size_t)row0 * r->rowbytes;
+    d.s = r->ds ? r->ds + (size_t)(row0 / r->blk_r) * r->sc : nullptr;
+    d.wdt = r->wdt;
+    d.rows = m->rows;
+    d.cols = m->cols;
+    d.blk_r = r->blk_r;
+    d.blk_c = r->blk_c;
+    return true;
+}
+
+}  // namespace dsv4b
+
+struct dsv4b_moe {
+    dsv4b::MoeLayer L;
+    dsv4b::MoeScratch S;
+    void *tables;       // 6 x n_experts device pointers
+    float *scratch;
+    float *bias;
+    int *fixed;
+    float *dx, *dout;
+};
+
+extern "C" dsv4b_moe *dsv4_cuda_moe_prepare(const DSV4QMat *gate, const float *bias,
+                                            const DSV4QMat *experts, int n_experts,
+                                            const DSV4QMat *shared, int topk, float route_scale,
+                                            int score_func, float swiglu_limit)
+{
+    using namespace dsv4b;
+    if (!g.ready || !gate || !experts || n_experts < 1 || n_experts > kMoeMaxExperts || topk < 1 ||
+        topk > kMoeMaxTopk || topk > n_experts || (score_func != 1 && score_func != 2))
+        return nullptr;
+    dsv4b_moe *m = (dsv4b_moe *)calloc(1, sizeof *m);
+    if (!m) return nullptr;
+    MoeLayer &L = m->L;
+    bool ok = devmat(gate, L.gate);
+    L.n_experts = n_experts;
+    L.topk = topk;
+    L.hidden = gate->cols;
+    L.inter = experts[0].rows;
+    L.efmt = experts[0].wdt;
+    L.eblk_r = experts[0].blk_r;
+    L.eblk_c = experts[0].blk_c;
+    L.route_scale = route_scale;
+    L.score_func = score_func;
+    L.swiglu_limit = swiglu_limit;
+    std::vector<const uint8_t *> tab((size_t)6 * n_experts, nullptr);
+    for (int e = 0; ok && e < n_experts; e++) {
+        const DSV4QMat *x3 = experts + 3 * e;
+        for (int j = 0; j < 3 && ok; j++) {
+            DevMat d;
+            ok = devmat(&x3[j], d) && x3[j].wdt == L.efmt;
+            if (!ok) break;
+            const int want_rows = (j == 2) ? L.hidden : L.inter, want_cols = (j == 2) ? L.inter : L.hidden;
+            ok = (d.rows == want_rows && d.cols == want_cols);
+            tab[(size_t)(2 * j) * n_experts + e] = d.w;
+            tab[(size_t)(2 * j + 1) * n_experts + e] = d.s;
+        }
+    }
+    if (ok && shared) {
+        L.has_shared = 1;
+        for (int j = 0; j < 3 && ok; j++) ok = devmat(&shared[j], L.sh[j]);
+        L.inter_shared = ok ? shared[0].rows : 0;
+    }
+    const size_t nf = moe_scratch_floats(L.hidden, L.inter, L.inter_shared, n_experts, topk);
+    if (ok) ok = cudaMalloc(&m->tables, tab.size() * sizeof(void *)) == cudaSuccess &&
+                 cudaMemcpy(m->tables, tab.data(), tab.size() * sizeof(void *), cudaMemcpyHostToDevice) == cudaSuccess;
+    if (ok) ok = cudaMalloc(&m->scratch, (nf + kMoeMaxTopk) * sizeof(float)) == cudaSuccess;
+    if (ok) ok = cudaMalloc(&m->fixed, kMoeMaxTopk * sizeof(int)) == cudaSuccess;
+    if (ok) ok = cudaMalloc(&m->dx, (size_t)L.hidden * sizeof(float)) == cudaSuccess &&
+                 cudaMalloc(&m->dout, (size_t)L.hidden * sizeof(float)) == cudaSuccess;
+    if (ok && bias)
+        ok = cudaMalloc(&m->bias, n_experts * sizeof(float)) == cudaSuccess &&
+             cudaMemcpy(m->bias, bias, n_experts * sizeof(float), cudaMemcpyHostToDevice) == cudaSuccess;
+    if (!ok) {
+        dsv4_cuda_moe_free(m);
+        return nullptr;
+    }
+    const uint8_t *const *t = (const uint8_t *const *)m->tables;
+    L.w1tab = t; L.s1tab = t + n_experts;
+    L.w3tab = t + 2 * n_experts; L.s3tab = t + 3 * n_experts;
+    L.w2tab = t + 4 * n_experts; L.s2tab = t + 5 * n_experts;
+    L.bias = m->bias;
+    moe_scratch_carve(m->S, m->scratch, L.hidden, L.inter, L.inter_shared, n_experts, topk);
+    return m;
+}
+
+extern "C" void dsv4_cuda_moe_free(dsv4b_moe *m)
+{
+    if (!m) return;
+    if (g.st) cudaStreamSynchronize(g.st);
+    cudaFree(m->tables);
+    cudaFree(m->scratch);
+    cudaFree(m->fixed);
+    cudaFree(m->bias);
+    cudaFree(m->dx);
+    cudaFree(m->dout);
+    free(m);
+}
+
+extern "C" int dsv4b_moe_forward(dsv4b_moe *m, float *out, const float *x, void *stream)
+{
+    if (!m) return -1;
+    m->L.fixed = nullptr;
+    return dsv4b::moe_forward(m->L, m->S, out, x, nullptr, stream_of(stream));
+}
+
+extern "C" int dsv4_cuda_moe(dsv4b_moe *m, float *out, const float *x, const int *fixed_experts,
+                             int *idx_out, float *w_out)
+{
+    if (!m || !out || !x) return -1;
+    const int H = m->L.hidden, K = m->L.topk;
+    DSV4B_CUDA_OK(cudaMemcpyAsync(m->dx, x, (size_t)H * sizeof(float), cudaMemcpyHostToDevice, g.st));
+    m->L.fixed = nullptr;
+    if (fixed_experts) {
+        for (int k = 0; k < K; k++)
+            if (fixed_experts[k] < 0 || fixed_experts[k] >= m->L.n_experts) return -1;
+        DSV4B_CUDA_OK(cudaMemcpyAsync(m->fixed, fixed_experts, K * sizeof(int), cudaMemcpyHostToDevice, g.st));
+        m->L.fixed = m->fixed;
+    }
+    if (dsv4b::moe_forward(m->L, m->S, m->dout, m->dx, nullptr, g.st) != 0) return -1;
+    DSV4B_CUDA_OK(cudaMemcpyAsync(out, m->dout, (size_t)H * sizeof(float), cudaMemcpyDeviceToHost, g.st));
+    if (idx_out) DSV4B_CUDA_OK(cudaMemcpyAsync(idx_out, m->S.sel, K * sizeof(int), cudaMemcpyDeviceToHost, g.st));
+    if (w_out) DSV4B_CUDA_OK(cudaMemcpyAsync(w_out, m->S.wts, K * sizeof(float), cudaMemcpyDeviceToHost, g.st));
+    DSV4B_CUDA_OK(cudaStreamSynchronize(g.st));
+    m->L.fixed = nullptr;
+    return 0;
 }

@@ -32,12 +32,18 @@ k_gemv_reg(GemvArgs g)
     if (row0 >= g.rows) return;
     const int rb = g.rowbytes, nseg = (rb + 255) >> 8;
 
+    const uint8_t *W = g.W, *Sg = g.S;
+    if (g.wtab) {
+        const int e = g.sel[g.slot];
+        W = g.wtab[e];
+        Sg = g.stab ? g.stab[e] : nullptr;
+    }
     const uint8_t *wr[R];
     int srow[R];
 #pragma unroll
     for (int r = 0; r < R; r++) {
         const int o = min(row0 + r, g.rows - 1);
-        wr[r] = g.W + (size_t)o * rb;
+        wr[r] = W + (size_t)o * rb;
         srow[r] = F::SC ? (o >> g.lbr) * g.sc : 0;
     }
     double tot[R][NT];
@@ -78,7 +84,7 @@ k_gemv_reg(GemvArgs g)
                 for (int r = 0; r < R; r++)
 #pragma unroll
                     for (int k = 0; k < NS; k++)
-                        s[r][k] = (F::SC && k < nvalid) ? e8m0(__ldg(g.S + srow[r] + ((e0 + 4 * (16 * k + li)) >> g.lbc)))
+                        s[r][k] = (F::SC && k < nvalid) ? e8m0(__ldg(Sg + srow[r] + ((e0 + 4 * (16 * k + li)) >> g.lbc)))
                                                         : 1.0f;
 #pragma unroll
                 for (int t = 0; t < NT; t++) {
@@ -239,13 +245,33 @@ int gemv_reg(const GemvArgs &g0, int fmt, int nt, cudaStream_t st)
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 
+int gemv_sel(int fmt, float *y, const float *x, const uint8_t *const *wtab,
+             const uint8_t *const *stab, const int *sel, int slot, int rows,
+             int cols, int blk_r, int blk_c, cudaStream_t st)
+{
+    GemvArgs g = {};
+    g.rows = rows; g.cols = cols;
+    g.blk_r = blk_r > 0 ? blk_r : 1; g.blk_c = blk_c > 0 ? blk_c : 1;
+    g.sc = fmt >= DSV4B_WFP8 ? (cols + g.blk_c - 1) / g.blk_c : 0;
+    g.rowbytes = (int)row_bytes(fmt, cols);
+    g.xstride = cols; g.ystride = rows;
+    g.x = x; g.y = y;
+    g.lbr = fmt >= DSV4B_WFP8 ? log2_exact(g.blk_r) : 0;
+    g.lbc = fmt >= DSV4B_WFP8 ? log2_exact(g.blk_c) : 30;
+    g.wtab = wtab; g.stab = stab; g.sel = sel; g.slot = slot;
+    // the table's matrices are uploaded (256-byte aligned); the shape decides
+    if (g.rowbytes % 16 || ((uintptr_t)x & 15)) return -1;
+    if (fmt >= DSV4B_WFP8 && (g.lbc < 2 || g.lbr < 0)) return -1;
+    return gemv_reg(g, fmt, 1, st);
+}
+
 int gemv(int fmt, float *y, long ystride, const float *x, long xstride,
          const void *W, const uint8_t *S, int rows, int cols, int blk_r,
          int blk_c, int nt, cudaStream_t st)
 {
     if (rows <= 0 || cols <= 0 || nt <= 0) return 0;
     if (fmt == DSV4B_WFP4 && (cols & 1)) return -1;
-    GemvArgs g;
+    GemvArgs g = {};
     g.W = (const uint8_t *)W; g.S = S;
     g.rows = rows; g.cols = cols;
     g.blk_r = blk_r > 0 ? blk_r : 1; g.blk_c = blk_c > 0 ? blk_c : 1;

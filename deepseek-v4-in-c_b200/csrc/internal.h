@@ -16,6 +16,12 @@ struct GemvArgs {
     int rows, cols, blk_r, blk_c, sc, rowbytes;
     int lbr, lbc;           // log2 of the (power-of-two) block sizes
     long xstride, ystride;
+    // Device-side matrix selection (routed experts): when wtab != nullptr the
+    // weights are wtab[sel[slot]] and the scales stab[sel[slot]].
+    const uint8_t *const *wtab;
+    const uint8_t *const *stab;
+    const int *sel;
+    int slot;
 };
 
 // One matrix of a grouped TMA GEMV launch. With sel >= 0 the weights are
@@ -39,6 +45,10 @@ int gemv(int fmt, float *y, long ystride, const float *x, long xstride,
          const void *W, const uint8_t *S, int rows, int cols, int blk_r,
          int blk_c, int nt, cudaStream_t st);
 int gemv_reg(const GemvArgs &g, int fmt, int nt, cudaStream_t st);
+// Batch-1 GEMV whose weights are picked on the device: W = wtab[sel[slot]].
+int gemv_sel(int fmt, float *y, const float *x, const uint8_t *const *wtab,
+             const uint8_t *const *stab, const int *sel, int slot, int rows,
+             int cols, int blk_r, int blk_c, cudaStream_t st);
 bool gemv_tma_ok(int fmt, const GemvArgs &g);
 // Batch-1 GEMV of up to kTmaMaxGroups matrices sharing format and width.
 int gemv_tma(int fmt, const TmaGroup *grp, int ngroups, int cols, int blk_r,

@@ -1,0 +1,173 @@
+// moe.cu - the routed-expert FFN for one token, on the device.
+//
+// Restates moe() (src/model/dsv4_layer.c:369-484): router GEMV, scoring and
+// top-k (src/core/dsv4_ops.c:102-141), each selected expert's w1/w3 GEMV,
+// SwiGLU (dsv4_ops.c:60-78), w2 GEMV into a per-k accumulator, the weighted
+// sum strictly in k order, then the shared expert added unweighted. The
+// experts are picked on the device (sel[] written by the router kernel and
+// read by the GEMVs through a device pointer table), so a decode step never
+// waits on the host between routing and the expert matmuls.
+#include <stdlib.h>
+#include <string.h>
+
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+#include "moe.h"
+
+namespace dsv4b {
+
+// Router scoring and selection (dsv4_ops.c:102-141, with sigmoid from
+// tools/dsv4_ref.py:64-93). One block. fixed != nullptr means hash routing:
+// the experts are given (tid2eid row), the weights still come from scores.
+__global__ void k_route(const float *logits, const float *bias, const int *fixed,
+                        const int64_t *tid2eid, const int *token, int n, int topk,
+                        float route_scale, int score_func, int *sel_out, float *w_out)
+{
+    __shared__ float orig[kMoeMaxExperts], sc[kMoeMaxExperts];
+    __shared__ unsigned char taken[kMoeMaxExperts];
+    __shared__ int chosen[kMoeMaxTopk];
+    __shared__ float wv[32];
+    __shared__ int wi[32];
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    for (int e = tid; e < n; e += nthr) {
+        const float l = logits[e];
+        float o;
+        if (score_func == 2) o = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-l)));
+        else o = sqrtf((l > 20.0f) ? l : log1pf(expf(l)));
+        orig[e] = o;
+        sc[e] = bias ? __fadd_rn(o, bias[e]) : o;
+        taken[e] = 0;
+    }
+    __syncthreads();
+    if (fixed || tid2eid) {
+        if (tid < topk) chosen[tid] = fixed ? fixed[tid] : (int)tid2eid[(long)token[0] * topk + tid];
+    } else {
+        // topk rounds of block argmax: value descending, ties to the lower
+        // index -- the order of the reference's repeated-argmax selection.
+        for (int k = 0; k < topk; k++) {
+            float bv = 0.0f;
+            int bi = -1;
+            for (int e = tid; e < n; e += nthr)
+                if (!taken[e] && (bi < 0 || sc[e] > bv || (sc[e] == bv && e < bi))) { bv = sc[e]; bi = e; }
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+            }
+            if ((tid & 31) == 0) { wv[tid >> 5] = bv; wi[tid >> 5] = bi; }
+            __syncthreads();
+            if (tid == 0) {
+                float v = 0.0f;
+                int b = -1;
+                for (int w = 0; w < (nthr + 31) / 32; w++)
+                    if (wi[w] >= 0 && (b < 0 || wv[w] > v || (wv[w] == v && wi[w] < b))) { v = wv[w]; b = wi[w]; }
+                chosen[k] = b;
+                taken[b] = 1;
+            }
+            __syncthreads();
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float wts[kMoeMaxTopk];
+        double sum = 0.0;
+        for (int k = 0; k < topk; k++) { wts[k] = orig[chosen[k]]; sum += (double)wts[k]; }
+        const float inv = (sum != 0.0) ? (float)(1.0 / sum) : 0.0f;
+        for (int k = 0; k < topk; k++) {
+            w_out[k] = __fmul_rn(__fmul_rn(wts[k], inv), route_scale);
+            sel_out[k] = chosen[k];
+        }
+    }
+}
+
+// SwiGLU with the reference's asymmetric clamp (dsv4_ops.c:60-78): up is
+// clamped to +-limit, gate from above only; limit <= 0 disables both.
+__device__ __forceinline__ float swiglu1(float g, float u, float limit)
+{
+    if (limit > 0.0f) {
+        u = fmaxf(fminf(u, limit), -limit);
+        g = fminf(g, limit);
+    }
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
+__global__ void k_swiglu(float *h, const float *g, const float *u, int n, float limit)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) h[i] = swiglu1(g[i], u[i], limit);
+}
+
+// out[i] = sum_k w[k] * acc[k][i] in k order, each product and sum rounded
+// separately (dsv4_layer.c:471-475), then + shared[i] (:479-483).
+__global__ void k_combine(float *out, const float *acc, const float *w, int topk, int hidden,
+                          const float *shared)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= hidden) return;
+    float o = 0.0f;
+    for (int k = 0; k < topk; k++) o = __fadd_rn(o, __fmul_rn(w[k], acc[(size_t)k * hidden + i]));
+    if (shared) o = __fadd_rn(o, shared[i]);
+    out[i] = o;
+}
+
+int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float *x,
+                const int *token, cudaStream_t st)
+{
+    const int H = L.hidden, I = L.inter, K = L.topk;
+    if (K < 1 || K > kMoeMaxTopk || L.n_experts > kMoeMaxExperts) return -1;
+    // router
+    if (gemv(L.gate.wdt, S.logits, L.n_experts, x, H, L.gate.w, L.gate.s, L.n_experts, H,
+             L.gate.blk_r, L.gate.blk_c, 1, st))
+        return -1;
+    k_route<<<1, 256, 0, st>>>(S.logits, L.bias, L.fixed, L.tid2eid, token, L.n_experts, K,
+                               L.route_scale, L.score_func, S.sel, S.wts);
+    // gate / up of the selected experts
+    for (int k = 0; k < K; k++) {
+        if (gemv_sel(L.efmt, S.g + (size_t)k * I, x, L.w1tab, L.s1tab, S.sel, k, I, H, L.eblk_r, L.eblk_c, st))
+            return -1;
+        if (gemv_sel(L.efmt, S.u + (size_t)k * I, x, L.w3tab, L.s3tab, S.sel, k, I, H, L.eblk_r, L.eblk_c, st))
+            return -1;
+    }
+    const int Is = L.has_shared ? L.inter_shared : 0;
+    float *gs = S.g + (size_t)K * I, *us = S.u + (size_t)K * I, *hs = S.h + (size_t)K * I;
+    if (Is) {
+        if (gemv(L.sh[0].wdt, gs, Is, x, H, L.sh[0].w, L.sh[0].s, Is, H, L.sh[0].blk_r, L.sh[0].blk_c, 1, st)) return -1;
+        if (gemv(L.sh[1].wdt, us, Is, x, H, L.sh[1].w, L.sh[1].s, Is, H, L.sh[1].blk_r, L.sh[1].blk_c, 1, st)) return -1;
+    }
+    const int n = K * I + Is;
+    k_swiglu<<<(n + 255) / 256, 256, 0, st>>>(S.h, S.g, S.u, n, L.swiglu_limit);
+    // down
+    for (int k = 0; k < K; k++)
+        if (gemv_sel(L.efmt, S.acc + (size_t)k * H, S.h + (size_t)k * I, L.w2tab, L.s2tab, S.sel, k, H, I,
+                     L.eblk_r, L.eblk_c, st))
+            return -1;
+    float *accs = S.acc + (size_t)K * H;
+    if (Is && gemv(L.sh[2].wdt, accs, H, hs, Is, L.sh[2].w, L.sh[2].s, H, Is, L.sh[2].blk_r, L.sh[2].blk_c, 1, st))
+        return -1;
+    k_combine<<<(H + 255) / 256, 256, 0, st>>>(out, S.acc, S.wts, K, H, Is ? accs : nullptr);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
+}
+
+size_t moe_scratch_floats(int hidden, int inter, int inter_shared, int n_experts, int topk)
+{
+    const size_t im = (size_t)topk * inter + inter_shared;
+    return (size_t)n_experts + 3 * im + (size_t)(topk + 1) * hidden + 2 * kMoeMaxTopk;
+}
+
+void moe_scratch_carve(MoeScratch &S, float *base, int hidden, int inter, int inter_shared, int n_experts,
+                       int topk)
+{
+    const size_t im = (size_t)topk * inter + inter_shared;
+    float *p = base;
+    S.logits = p; p += n_experts;
+    S.g = p; p += im;
+    S.u = p; p += im;
+    S.h = p; p += im;
+    S.acc = p; p += (size_t)(topk + 1) * hidden;
+    S.wts = p; p += kMoeMaxTopk;
+    S.sel = reinterpret_cast<int *>(p);
+}
+
+}  // namespace dsv4b

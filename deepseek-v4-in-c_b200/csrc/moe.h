@@ -1,0 +1,46 @@
+// moe.h - device-side MoE layer description shared by moe.cu, the model and
+// the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dsv4b {
+
+constexpr int kMoeMaxExperts = 1024;
+constexpr int kMoeMaxTopk = 16;
+
+// A device-resident matrix in one of the checkpoint formats.
+struct DevMat {
+    const uint8_t *w, *s;
+    int wdt, rows, cols, blk_r, blk_c;
+};
+
+struct MoeLayer {
+    DevMat gate;                    // router [n_experts][hidden]
+    const float *bias;              // [n_experts] or nullptr (selection only)
+    const int64_t *tid2eid;         // [vocab][topk] or nullptr: hash routing
+    const int *fixed;               // [topk] experts given by the caller, or nullptr
+    // routed experts: device pointer tables indexed by expert id
+    const uint8_t *const *w1tab, *const *s1tab;
+    const uint8_t *const *w3tab, *const *s3tab;
+    const uint8_t *const *w2tab, *const *s2tab;
+    int efmt, eblk_r, eblk_c;
+    DevMat sh[3];                   // shared expert w1, w3, w2
+    int has_shared;
+    int n_experts, topk, hidden, inter, inter_shared, score_func;
+    float route_scale, swiglu_limit;
+};
+
+struct MoeScratch {
+    float *logits, *g, *u, *h, *acc, *wts;
+    int *sel;
+};
+
+int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float *x,
+                const int *token, cudaStream_t st);
+size_t moe_scratch_floats(int hidden, int inter, int inter_shared, int n_experts, int topk);
+void moe_scratch_carve(MoeScratch &S, float *base, int hidden, int inter, int inter_shared,
+                       int n_experts, int topk);
+
+}  // namespace dsv4b

@@ -63,6 +63,10 @@ def _declare(L):
         "dsv4_cuda_evict": ([qp], i),
         "dsv4_cuda_resident_ptrs": ([qp, C.POINTER(vp), C.POINTER(vp)], i),
         "dsv4b_gemv": ([i, vp, vp, vp, vp, i, i, i, i, i, vp], i),
+        "dsv4_cuda_moe_prepare": ([qp, vp, qp, i, qp, i, f, i, f], vp),
+        "dsv4_cuda_moe": ([vp, vp, vp, vp, vp, vp], i),
+        "dsv4_cuda_moe_free": ([vp], None),
+        "dsv4b_moe_forward": ([vp, vp, vp, vp], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -186,3 +190,47 @@ def gemv(wdt, y, x, W, S, rows, cols, blk_r=0, blk_c=0, nt=1, stream=None):
     check(lib().dsv4b_gemv(wdt, ptr(y), ptr(x), W if isinstance(W, int) else ptr(W),
                            None if S is None else (S if isinstance(S, int) else ptr(S)),
                            rows, cols, blk_r, blk_c, nt, stream_ptr(stream)), "dsv4b_gemv")
+
+
+class MoE:
+    """One layer's MoE bound to resident matrices (dsv4_cuda_moe_prepare)."""
+
+    def __init__(self, gate, experts, shared=None, bias=None, topk=6, route_scale=1.0,
+                 score_func=2, swiglu_limit=10.0):
+        self.gate, self.experts, self.shared = gate, experts, shared
+        n = len(experts)
+        self._qs = (QMat * (3 * n))(*[m.q for trio in experts for m in trio])
+        self._sh = None if shared is None else (QMat * 3)(*[m.q for m in shared])
+        self.bias = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        self.topk, self.hidden = topk, gate.q.cols
+        self.h = lib().dsv4_cuda_moe_prepare(C.byref(gate.q),
+                                             None if self.bias is None else self.bias.ctypes.data,
+                                             self._qs, n, self._sh, topk, route_scale, score_func,
+                                             swiglu_limit)
+        if not self.h:
+            raise RuntimeError("dsv4_cuda_moe_prepare failed (matrix not resident or bad shapes)")
+
+    def __call__(self, x, fixed=None):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty(self.hidden, np.float32)
+        idx = np.empty(self.topk, np.int32)
+        w = np.empty(self.topk, np.float32)
+        fx = None if fixed is None else np.ascontiguousarray(fixed, np.int32)
+        check(lib().dsv4_cuda_moe(self.h, out.ctypes.data, x.ctypes.data,
+                                  None if fx is None else fx.ctypes.data, idx.ctypes.data,
+                                  w.ctypes.data), "dsv4_cuda_moe")
+        return out, idx, w
+
+    def forward_dev(self, out, x, stream=None):
+        check(lib().dsv4b_moe_forward(self.h, ptr(out), ptr(x), stream_ptr(stream)), "dsv4b_moe_forward")
+
+    def close(self):
+        if self.h:
+            lib().dsv4_cuda_moe_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

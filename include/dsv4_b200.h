@@ -97,12 +97,40 @@ int dsv4_cuda_evict(const DSV4QMat *m);
  * a caller can reach the same weights through the device API. 0 or -1. */
 int dsv4_cuda_resident_ptrs(const DSV4QMat *m, const void **dw, const void **ds);
 
+/* ---- MoE for one token: src/model/dsv4_layer.c:369-484 (moe) with the
+ * router of src/core/dsv4_ops.c:102-141 (dsv4_route). ---- */
+typedef struct dsv4b_moe dsv4b_moe;
+
+/* Bind one layer's MoE to resident matrices. gate: router [n_experts][hidden]
+ * (F32 / BF16 / FP8); bias: [n_experts] host floats or NULL (selection only,
+ * as in the reference); experts: n_experts x {w1, w3, w2} descriptors, every
+ * one uploaded (FP4 1x32 in the checkpoint); shared: {w1, w3, w2} or NULL,
+ * added unweighted. score_func 1 = sqrt(softplus) (the reference's), 2 =
+ * sigmoid. Returns NULL when a matrix is not resident or shapes disagree. */
+dsv4b_moe *dsv4_cuda_moe_prepare(const DSV4QMat *gate, const float *bias,
+                                 const DSV4QMat *experts, int n_experts,
+                                 const DSV4QMat *shared, int topk,
+                                 float route_scale, int score_func,
+                                 float swiglu_limit);
+
+/* out[hidden] = moe(x[hidden]) with host buffers, synchronous. fixed_experts
+ * (topk ids) replaces top-k selection on hash-routed layers -- the caller's
+ * tid2eid row, as dsv4_route takes it; NULL = score top-k. idx_out / w_out
+ * (topk each, may be NULL) receive the routing decision. 0 or -1. */
+int dsv4_cuda_moe(dsv4b_moe *m, float *out, const float *x,
+                  const int *fixed_experts, int *idx_out, float *w_out);
+
+void dsv4_cuda_moe_free(dsv4b_moe *m);
+
 /* ===================================================== 2. device API ====== */
 
 /* y[t*rows + o] = sum_c W[o][c] * x[t*cols + c] for t < nt; any nt >= 1.
  * W/S are device pointers in the storage format `wdt`. 0 or -1. */
 int dsv4b_gemv(int wdt, float *y, const float *x, const void *W, const void *S,
                int rows, int cols, int blk_r, int blk_c, int nt, void *stream);
+
+/* The prepared MoE on device buffers x[hidden] -> out[hidden], stream-ordered. */
+int dsv4b_moe_forward(dsv4b_moe *m, float *out, const float *x, void *stream);
 
 #ifdef __cplusplus
 }

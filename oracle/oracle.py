@@ -224,3 +224,33 @@ class Checker:
             out, _c(kv_in, np.float32), _c(score_in, np.float32), _c(ape, np.float32),
             kv_state, score_state, pos, ratio, head_dim)
         return r, out
+
+
+class Mat(C.Structure):
+    """dsv4o_mat: a DSV4QMat flattened (oracle/dsv4_oracle.h)."""
+    _fields_ = [("w", _vp), ("s", _vp), ("wdt", _i), ("rows", _i), ("cols", _i),
+                ("blk_r", _i), ("blk_c", _i)]
+
+
+def mat(wdt, W, S, rows, cols, blk=(0, 0)):
+    return Mat(W.ctypes.data, None if S is None else S.ctypes.data, wdt, rows, cols, blk[0], blk[1])
+
+
+def moe(chk, x, gate, experts, shared, bias, topk, route_scale, score_func, swiglu_limit,
+        hidden, inter, inter_shared, fixed=None):
+    """dsv4o_moe with dsv4o_mat descriptors (the port only). experts: list of
+    (w1, w3, w2) Mat triples; shared: triple or None; fixed: hash-routing row."""
+    n = len(experts)
+    arr = (Mat * (3 * n))(*[m for t in experts for m in t])
+    sh = None if shared is None else (Mat * 3)(*shared)
+    out = np.empty(hidden, np.float32)
+    idx = np.empty(topk, np.int32); w = np.empty(topk, np.float32)
+    x = _c(x, np.float32)
+    b = None if bias is None else _c(bias, np.float32)
+    tid = None if fixed is None else np.ascontiguousarray(np.asarray(fixed, np.int64).reshape(1, -1))
+    f = chk._l.fn("moe", [_f32p, _f32p, C.POINTER(Mat), _vp, _vp, _i, C.POINTER(Mat), C.POINTER(Mat),
+                          _i, _i, _f, _i, _i, _i, _i, _f, _i32p, _f32p])
+    f(out, x, C.byref(gate), None if b is None else b.ctypes.data,
+      None if tid is None else tid.ctypes.data, 0, arr, sh, n, topk, route_scale, score_func,
+      hidden, inter, inter_shared, swiglu_limit, idx, w)
+    return out, idx, w

@@ -66,6 +66,8 @@ struct Workspace {
     int nsm;
 };
 Workspace &workspace();
+// The backend's own stream (NULL stream arguments of the device API).
+cudaStream_t stream_of(void *s);
 int workspace_init();
 void workspace_free();
 

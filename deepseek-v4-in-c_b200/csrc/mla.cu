@@ -1,0 +1,402 @@
+// mla.cu - sparse MLA decode: lightning-indexer scoring, exact top-k, and
+// attention over the selected latent KV rows, for a batch of sequences.
+//
+// Restates src/core/dsv4_indexer.c:64-106 and src/core/dsv4_attn.c:60-108.
+//
+// INDEXER (k_indexer_score). The selected set must equal the reference's, so
+// the score is computed with the reference's own arithmetic: per head a
+// SEQUENTIAL double fma chain over the head dimension, the ReLU, then heads
+// folded in order as total += dot * w (product and sum rounded separately),
+// and out = (float)total * scale. Same inputs, same operations, same order:
+// the float scores are bit-identical, so the selection is too.
+//
+// TOP-K (k_topk). One CTA per sequence: radix select of the k-th key over the
+// scores held in shared memory, then a bitonic sort of the chosen (value,
+// index) pairs -- descending by value, ties to the lower index, exactly the
+// sequence dsv4_topk's repeated argmax produces.
+//
+// ATTENTION (k_attn_chunk + k_attn_combine). Flash-decoding split over chunks
+// of 64 selected positions: a chunk computes scores for all heads, its own
+// max, exp-sums and weighted value sums; the combine rescales chunks in chunk
+// order and adds the sink to the denominator only (dsv4_attn.c:84-92).
+// Within one chunk this is the reference's softmax exactly; across chunks it
+// agrees to float rounding.
+#include <stdlib.h>
+
+#include "common.cuh"
+#include "internal.h"
+#include "mla.h"
+
+namespace dsv4b {
+
+__device__ __forceinline__ float load_elem(const void *base, size_t i, int dt)
+{
+    if (dt == DSV4B_DT_F32) return reinterpret_cast<const float *>(base)[i];
+    if (dt == DSV4B_DT_BF16) return __uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(base)[i] << 16);
+    return e4m3x2((uint16_t)reinterpret_cast<const uint8_t *>(base)[i]).x;
+}
+
+// ---------------------------------------------------------------- indexer
+// grid (ceil(n_pos / 32), batch), 256 threads. Thread t: position t & 31 of
+// the tile, heads (t >> 5) * 8 .. +8. q and the key tile live in shared
+// memory as double (keys transposed so a warp reads 32 consecutive doubles).
+constexpr int IX_TP = 32;
+
+__global__ void __launch_bounds__(256)
+k_indexer_score(float *out, const float *q, const void *keys, int key_dt, long key_stride,
+                long seq_key_stride, const float *w, int n_heads, int head_dim, int n_pos,
+                float scale, long seq_q_stride, long seq_out_stride)
+{
+    extern __shared__ double ixs[];
+    double *qs = ixs;                               // [n_heads][head_dim]
+    double *kt = qs + n_heads * head_dim;           // [head_dim][IX_TP]
+    double *dots = kt + head_dim * IX_TP;           // [IX_TP][n_heads]
+    const int b = blockIdx.y, t0 = blockIdx.x * IX_TP;
+    q += (size_t)b * seq_q_stride;
+    w += (size_t)b * n_heads;
+    const char *kb = reinterpret_cast<const char *>(keys);
+    const int esz = key_dt == DSV4B_DT_F32 ? 4 : key_dt == DSV4B_DT_BF16 ? 2 : 1;
+    kb += (size_t)b * seq_key_stride * esz;
+    for (int i = threadIdx.x; i < n_heads * head_dim; i += blockDim.x) qs[i] = (double)q[i];
+    for (int i = threadIdx.x; i < head_dim * IX_TP; i += blockDim.x) {
+        const int p = i / head_dim, c = i % head_dim;
+        kt[c * IX_TP + p] = (t0 + p < n_pos) ? (double)load_elem(kb, (size_t)(t0 + p) * key_stride + c, key_dt) : 0.0;
+    }
+    __syncthreads();
+    const int p = threadIdx.x & 31, hg = threadIdx.x >> 5;
+    for (int h0 = hg * 8; h0 < n_heads; h0 += 64) {
+        double acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[j] = 0.0;
+        for (int c = 0; c < head_dim; c++) {
+            const double kv = kt[c * IX_TP + p];
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                if (h0 + j < n_heads) acc[j] = __fma_rn(qs[(h0 + j) * head_dim + c], kv, acc[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (h0 + j < n_heads) dots[p * n_heads + h0 + j] = acc[j];
+    }
+    __syncthreads();
+    if (threadIdx.x < IX_TP && t0 + threadIdx.x < n_pos) {
+        double total = 0.0;
+        for (int h = 0; h < n_heads; h++) {
+            const double d = dots[threadIdx.x * n_heads + h];
+            if (d > 0.0) total = __dadd_rn(total, __dmul_rn(d, (double)w[h]));
+        }
+        out[(size_t)b * seq_out_stride + t0 + threadIdx.x] = __fmul_rn((float)total, scale);
+    }
+}
+
+// ------------------------------------------------------------------- top-k
+// Orderable key: larger value -> larger key (IEEE total order on non-NaN).
+__device__ __forceinline__ uint32_t fkey(float v)
+{
+    const uint32_t u = __float_as_uint(v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// One CTA (1024 threads) per sequence. scores [n] -> idx [min(k, n)] in
+// descending order, ties to the lower index. n <= kTopkMaxN, k <= kTopkMaxK.
+__global__ void __launch_bounds__(1024)
+k_topk(int *idx_out, const float *scores, int n, int k, long seq_in_stride, long seq_out_stride)
+{
+    extern __shared__ uint32_t tks[];
+    uint32_t *key = tks;                                   // [n]
+    unsigned long long *sel = reinterpret_cast<unsigned long long *>(key + ((n + 1) & ~1)); // [kpow2]
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t s_prefix, s_want, s_gt, s_eqtaken;
+    const int b = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
+    scores += (size_t)b * seq_in_stride;
+    idx_out += (size_t)b * seq_out_stride;
+    if (k > n) k = n;
+    if (k <= 0) return;
+    for (int i = tid; i < n; i += nt) key[i] = fkey(scores[i]);
+    if (tid == 0) { s_prefix = 0; s_want = (uint32_t)k; }
+    __syncthreads();
+    // radix select, 8 bits at a time from the top: find the k-th largest key
+    uint32_t mask = 0;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = tid; i < 256; i += nt) hist[i] = 0;
+        __syncthreads();
+        const uint32_t pre = s_prefix;
+        for (int i = tid; i < n; i += nt)
+            if ((key[i] & mask) == pre) atomicAdd(&hist[(key[i] >> shift) & 255u], 1u);
+        __syncthreads();
+        if (tid == 0) {
+            uint32_t want = s_want, acc = 0;
+            int bin = 255;
+            for (; bin > 0; bin--) {
+                if (acc + hist[bin] >= want) break;
+                acc += hist[bin];
+            }
+            s_want = want - acc;
+            s_prefix = pre | ((uint32_t)bin << shift);
+        }
+        mask |= 255u << shift;
+        __syncthreads();
+    }
+    const uint32_t kth = s_prefix;            // key of the k-th largest
+    const uint32_t need_eq = s_want;          // how many == kth are taken (lowest indices)
+    // count > kth, collect them; then the first need_eq indices with == kth
+    if (tid == 0) { s_gt = 0; s_eqtaken = 0; }
+    __syncthreads();
+    int kp = 1;
+    while (kp < k) kp <<= 1;
+    for (int i = tid; i < kp; i += nt) sel[i] = 0ull;   // padding sorts last
+    __syncthreads();
+    for (int i = tid; i < n; i += nt)
+        if (key[i] > kth) {
+            const uint32_t slot = atomicAdd(&s_gt, 1u);
+            sel[slot] = ((unsigned long long)key[i] << 32) | (uint32_t)(~(uint32_t)i);
+        }
+    __syncthreads();
+    // ties at the threshold: lowest indices first -- a block-wide ordered scan
+    const uint32_t base = s_gt;
+    for (int c0 = 0; c0 < n && s_eqtaken < need_eq; c0 += nt) {
+        const int i = c0 + tid;
+        const int is_eq = (i < n && key[i] == kth) ? 1 : 0;
+        // exclusive prefix of is_eq within this pass
+        __shared__ int wsum[32];
+        int v = is_eq;
+        for (int o = 1; o < 32; o <<= 1) {
+            const int u = __shfl_up_sync(0xffffffffu, v, o);
+            if ((tid & 31) >= o) v += u;
+        }
+        if ((tid & 31) == 31) wsum[tid >> 5] = v;
+        __syncthreads();
+        if (tid < 32) {
+            int s = (tid < (nt >> 5)) ? wsum[tid] : 0;
+            for (int o = 1; o < 32; o <<= 1) {
+                const int u = __shfl_up_sync(0xffffffffu, s, o);
+                if (tid >= o) s += u;
+            }
+            wsum[tid] = s;
+        }
+        __syncthreads();
+        const int incl = v + ((tid >> 5) ? wsum[(tid >> 5) - 1] : 0);
+        const uint32_t rank = s_eqtaken + (uint32_t)(incl - is_eq);
+        if (is_eq && rank < need_eq)
+            sel[base + rank] = ((unsigned long long)kth << 32) | (uint32_t)(~(uint32_t)i);
+        __syncthreads();
+        if (tid == nt - 1) s_eqtaken += (uint32_t)incl;
+        __syncthreads();
+    }
+    // bitonic sort, descending by (key, ~index): larger value first, and for
+    // equal values the larger ~index, i.e. the lower index, first
+    for (int size = 2; size <= kp; size <<= 1)
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = tid; i < kp; i += nt) {
+                const int j = i ^ stride;
+                if (j > i) {
+                    const unsigned long long a = sel[i], c = sel[j];
+                    const bool desc = ((i & size) == 0);
+                    if (desc ? (a < c) : (a > c)) { sel[i] = c; sel[j] = a; }
+                }
+            }
+            __syncthreads();
+        }
+    for (int i = tid; i < k; i += nt) idx_out[i] = (int)(~(uint32_t)(sel[i] & 0xffffffffull));
+}
+
+// --------------------------------------------------------------- attention
+constexpr int AT_CH = 64;      // selected positions per chunk
+constexpr int AT_HG = 16;      // heads per q tile in shared memory
+
+// Per (sequence, chunk, head) partials: chunk max pm, exp-sum pden (double)
+// and the unnormalised value sum po[d].
+struct AttnPart {
+    float *po;
+    float *pm;
+    double *pden;
+};
+
+size_t attn_smem_bytes(int d) { return ((size_t)AT_CH * (d + 1) + (size_t)AT_HG * d) * 4 + (size_t)64 * AT_CH * 4; }
+
+// grid (nchunk, batch), 256 threads.
+__global__ void __launch_bounds__(256)
+k_attn_chunk(AttnPart part, const float *q, const void *kv, int kv_dt, long seq_kv_rows,
+             const int *idxs, long seq_idx_stride, int n_heads, int d, int topk, float scale,
+             long seq_q_stride)
+{
+    extern __shared__ float ats[];
+    const int dp = d + 1;                                   // padded row: conflict-free
+    float *kvs = ats;                                       // [AT_CH][dp]
+    float *qs = kvs + AT_CH * dp;                           // [AT_HG][d]
+    float *sc = qs + AT_HG * d;                             // [n_heads <= 64][AT_CH]
+    __shared__ int pidx[AT_CH];
+    const int b = blockIdx.y, nch = gridDim.x, c0 = blockIdx.x * AT_CH, tid = threadIdx.x;
+    q += (size_t)b * seq_q_stride;
+    idxs += (size_t)b * seq_idx_stride;
+    const int esz = kv_dt == DSV4B_DT_F32 ? 4 : kv_dt == DSV4B_DT_BF16 ? 2 : 1;
+    const char *kvb = reinterpret_cast<const char *>(kv) + (size_t)b * seq_kv_rows * d * esz;
+    const int npos = min(AT_CH, topk - c0);
+    if (tid < AT_CH) pidx[tid] = (tid < npos) ? idxs[c0 + tid] : -1;
+    __syncthreads();
+    for (int i = tid; i < AT_CH * d; i += blockDim.x) {
+        const int p = i / d, c = i % d;
+        const int r = pidx[p];
+        kvs[p * dp + c] = (r >= 0) ? load_elem(kvb, (size_t)r * d + c, kv_dt) : 0.0f;
+    }
+    // scores: thread -> position tid & 63, heads (tid >> 6) + 4j of each q tile
+    const int p = tid & 63, hq = tid >> 6;
+    for (int h0 = 0; h0 < n_heads; h0 += AT_HG) {
+        __syncthreads();
+        for (int i = tid; i < AT_HG * d; i += blockDim.x)
+            qs[i] = (h0 + i / d < n_heads) ? q[(size_t)h0 * d + i] : 0.0f;
+        __syncthreads();
+        float acc[AT_HG / 4];
+#pragma unroll
+        for (int j = 0; j < AT_HG / 4; j++) acc[j] = 0.0f;
+        const float *kr = kvs + p * dp;
+        for (int c = 0; c < d; c++) {
+            const float kvv = kr[c];
+#pragma unroll
+            for (int j = 0; j < AT_HG / 4; j++) acc[j] = __fmaf_rn(qs[(hq + 4 * j) * d + c], kvv, acc[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < AT_HG / 4; j++) {
+            const int h = h0 + hq + 4 * j;
+            if (h < n_heads) sc[h * AT_CH + p] = (pidx[p] >= 0) ? __fmul_rn(acc[j], scale) : -INFINITY;
+        }
+    }
+    __syncthreads();
+    // per head: chunk max over valid slots (the sink is not part of it), exp
+    // weights in place, exp-sum in double
+    const size_t prow = ((size_t)b * nch + blockIdx.x) * n_heads;
+    for (int h = tid >> 5; h < n_heads; h += blockDim.x >> 5) {
+        const int lane = tid & 31;
+        const float s0 = sc[h * AT_CH + lane], s1 = sc[h * AT_CH + lane + 32];
+        const float m = warp_max_f(fmaxf(s0, s1));
+        float e0 = 0.0f, e1 = 0.0f;
+        if (m != -INFINITY) {
+            e0 = (s0 == -INFINITY) ? 0.0f : expf(s0 - m);
+            e1 = (s1 == -INFINITY) ? 0.0f : expf(s1 - m);
+        }
+        const double ds = warp_sum_d((double)e0 + (double)e1);
+        __syncwarp();
+        sc[h * AT_CH + lane] = e0;
+        sc[h * AT_CH + lane + 32] = e1;
+        if (lane == 0) {
+            part.pm[prow + h] = m;
+            part.pden[prow + h] = ds;
+        }
+    }
+    __syncthreads();
+    // unnormalised value sums, positions in order
+    for (int i = tid; i < n_heads * d; i += blockDim.x) {
+        const int h = i / d, c = i % d;
+        float o = 0.0f;
+        for (int pp = 0; pp < AT_CH; pp++) {
+            const float e = sc[h * AT_CH + pp];
+            if (e != 0.0f) o = __fadd_rn(o, __fmul_rn(e, kvs[pp * dp + c]));
+        }
+        part.po[(prow + h) * d + c] = o;
+    }
+}
+
+// grid (n_heads, batch), 128 threads: rescale chunks in chunk order, add the
+// sink to the denominator only, normalise.
+__global__ void k_attn_combine(float *o, AttnPart part, const float *sink, int nch, int n_heads, int d,
+                               long seq_o_stride)
+{
+    const int h = blockIdx.x, b = blockIdx.y;
+    float M = -INFINITY;
+    for (int c = 0; c < nch; c++) M = fmaxf(M, part.pm[((size_t)b * nch + c) * n_heads + h]);
+    float *ob = o + (size_t)b * seq_o_stride + (size_t)h * d;
+    if (M == -INFINITY) {       // nothing valid: zero output (dsv4_attn.c:32-37)
+        for (int c = threadIdx.x; c < d; c += blockDim.x) ob[c] = 0.0f;
+        return;
+    }
+    double den = 0.0;
+    for (int c = 0; c < nch; c++) {
+        const size_t r = ((size_t)b * nch + c) * n_heads + h;
+        const float mc = part.pm[r];
+        if (mc != -INFINITY) den += part.pden[r] * (double)expf(mc - M);
+    }
+    den += (double)expf(sink[h] - M);
+    const float inv = (float)(1.0 / den);
+    for (int cc = threadIdx.x; cc < d; cc += blockDim.x) {
+        float acc = 0.0f;
+        for (int c = 0; c < nch; c++) {
+            const size_t r = ((size_t)b * nch + c) * n_heads + h;
+            const float mc = part.pm[r];
+            if (mc == -INFINITY) continue;
+            const float f = (mc == M) ? 1.0f : expf(mc - M);
+            acc = __fadd_rn(acc, __fmul_rn(part.po[r * d + cc], f));
+        }
+        ob[cc] = __fmul_rn(acc, inv);
+    }
+}
+
+// ------------------------------------------------------------------ launch
+
+int indexer_score(float *out, const float *q, const void *keys, int key_dt, long key_stride,
+                  long seq_key_stride, const float *w, int n_heads, int head_dim, int n_pos, float scale,
+                  int batch, cudaStream_t st)
+{
+    if (n_pos <= 0 || batch <= 0) return 0;
+    const size_t smem = ((size_t)n_heads * head_dim + (size_t)head_dim * IX_TP + (size_t)IX_TP * n_heads) * 8;
+    if (smem > 200 * 1024) return -1;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(k_indexer_score, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr = true;
+    }
+    dim3 grid((n_pos + IX_TP - 1) / IX_TP, batch);
+    k_indexer_score<<<grid, 256, smem, st>>>(out, q, keys, key_dt, key_stride, seq_key_stride, w, n_heads,
+                                             head_dim, n_pos, scale, (long)n_heads * head_dim, n_pos);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
+}
+
+int topk(int *idx, const float *scores, int n, int k, int batch, long seq_in_stride, long seq_out_stride,
+         cudaStream_t st)
+{
+    if (batch <= 0 || n <= 0 || k <= 0) return 0;
+    if (n > kTopkMaxN || k > kTopkMaxK) return -1;
+    int kp = 1;
+    while (kp < (k < n ? k : n)) kp <<= 1;
+    const size_t smem = (size_t)((n + 1) & ~1) * 4 + (size_t)kp * 8;
+    if (smem > 220 * 1024) return -1;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(k_topk, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        attr = true;
+    }
+    k_topk<<<dim3(1, batch), 1024, smem, st>>>(idx, scores, n, k, seq_in_stride, seq_out_stride);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
+}
+
+size_t attn_part_bytes(int n_heads, int d, int topk, int batch)
+{
+    const size_t nch = (topk + AT_CH - 1) / AT_CH;
+    return (size_t)batch * nch * n_heads * ((size_t)d * 4 + 4 + 8) + 64;
+}
+
+int sparse_attn(float *o, const float *q, const void *kv, int kv_dt, long seq_kv_rows, const float *sink,
+                const int *idxs, long seq_idx_stride, int n_heads, int d, int topk, float scale, int batch,
+                void *part_buf, cudaStream_t st)
+{
+    if (batch <= 0 || topk <= 0) return 0;
+    if (n_heads > 64 || d > 1024) return -1;
+    const int nch = (topk + AT_CH - 1) / AT_CH;
+    const size_t n = (size_t)batch * nch * n_heads;
+    AttnPart part;
+    part.pden = reinterpret_cast<double *>(part_buf);
+    part.pm = reinterpret_cast<float *>(part.pden + n);
+    part.po = part.pm + n + (n & 1);
+    const size_t smem = attn_smem_bytes(d);
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(k_attn_chunk, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        attr = true;
+    }
+    if (smem > 220 * 1024) return -1;
+    k_attn_chunk<<<dim3(nch, batch), 256, smem, st>>>(part, q, kv, kv_dt, seq_kv_rows, idxs, seq_idx_stride,
+                                                      n_heads, d, topk, scale, (long)n_heads * d);
+    k_attn_combine<<<dim3(n_heads, batch), 128, 0, st>>>(o, part, sink, nch, n_heads, d, (long)n_heads * d);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace dsv4b

@@ -1,0 +1,32 @@
+// mla.h - sparse MLA decode kernels (mla.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+#define DSV4B_DT_F32 0
+#define DSV4B_DT_BF16 1
+#define DSV4B_DT_E4M3 2
+
+namespace dsv4b {
+
+constexpr int kTopkMaxN = 49152;    // scores held in shared memory
+constexpr int kTopkMaxK = 4096;
+
+// out[b][t] for t < n_pos: the reference's indexer score of key row t.
+// keys of sequence b start at keys + b*seq_key_stride elements; row t at
+// t*key_stride elements; q is [batch][n_heads][head_dim], w [batch][n_heads].
+int indexer_score(float *out, const float *q, const void *keys, int key_dt, long key_stride,
+                  long seq_key_stride, const float *w, int n_heads, int head_dim, int n_pos,
+                  float scale, int batch, cudaStream_t st);
+// idx[b][i], i < min(k, n): descending scores, ties to the lower index.
+int topk(int *idx, const float *scores, int n, int k, int batch, long seq_in_stride,
+         long seq_out_stride, cudaStream_t st);
+size_t attn_part_bytes(int n_heads, int d, int topk, int batch);
+// o[b][h][d]; kv of sequence b is rows [b*seq_kv_rows, ...) of width d; idxs
+// [b][topk] with -1 = masked; part_buf holds attn_part_bytes().
+int sparse_attn(float *o, const float *q, const void *kv, int kv_dt, long seq_kv_rows,
+                const float *sink, const int *idxs, long seq_idx_stride, int n_heads, int d,
+                int topk, float scale, int batch, void *part_buf, cudaStream_t st);
+
+}  // namespace dsv4b

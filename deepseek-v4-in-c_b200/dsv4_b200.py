@@ -67,6 +67,13 @@ def _declare(L):
         "dsv4_cuda_moe": ([vp, vp, vp, vp, vp, vp], i),
         "dsv4_cuda_moe_free": ([vp], None),
         "dsv4b_moe_forward": ([vp, vp, vp, vp], i),
+        "dsv4_cuda_indexer_score": ([vp, vp, vp, vp, i, i, i], i),
+        "dsv4_cuda_topk": ([vp, vp, i, i], i),
+        "dsv4_cuda_sparse_attn": ([vp, vp, vp, vp, vp, i, i, i, f], i),
+        "dsv4b_indexer_score": ([vp, vp, vp, i, C.c_long, C.c_long, vp, i, i, i, f, i, vp], i),
+        "dsv4b_topk": ([vp, vp, i, i, i, vp], i),
+        "dsv4b_sparse_attn_scratch": ([i, i, i, i], sz),
+        "dsv4b_sparse_attn": ([vp, vp, vp, i, C.c_long, vp, vp, i, i, i, f, i, vp, sz, vp], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -234,3 +241,64 @@ class MoE:
             self.close()
         except Exception:
             pass
+
+
+# ------------------------------------------------------------- sparse MLA
+
+F32, BF16, E4M3 = 0, 1, 2
+
+
+def _f(a):
+    return np.ascontiguousarray(a, np.float32)
+
+
+def indexer_score(q, kv, weights):
+    """dsv4_cuda_indexer_score: reference signature, host buffers."""
+    q, kv, w = _f(q), _f(kv), _f(weights)
+    n_heads, head_dim = q.shape
+    out = np.empty(kv.shape[0], np.float32)
+    check(lib().dsv4_cuda_indexer_score(out.ctypes.data, q.ctypes.data, kv.ctypes.data, w.ctypes.data,
+                                        n_heads, head_dim, kv.shape[0]), "dsv4_cuda_indexer_score")
+    return out
+
+
+def topk(scores, k):
+    scores = _f(scores)
+    idx = np.empty(max(1, min(k, scores.size)), np.int32)
+    n = lib().dsv4_cuda_topk(idx.ctypes.data, scores.ctypes.data, scores.size, k)
+    if n < 0:
+        raise RuntimeError("dsv4_cuda_topk failed")
+    return idx[:n]
+
+
+def sparse_attn(q, kv, sink, idxs, scale):
+    q, kv, sink = _f(q), _f(kv), _f(sink)
+    idxs = np.ascontiguousarray(idxs, np.int32)
+    h, d = q.shape
+    o = np.empty((h, d), np.float32)
+    check(lib().dsv4_cuda_sparse_attn(o.ctypes.data, q.ctypes.data, kv.ctypes.data, sink.ctypes.data,
+                                      idxs.ctypes.data, h, d, idxs.size, scale), "dsv4_cuda_sparse_attn")
+    return o
+
+
+def indexer_score_dev(out, q, keys, key_dt, key_stride, seq_key_stride, w, n_heads, head_dim, n_pos,
+                      scale, batch, stream=None):
+    check(lib().dsv4b_indexer_score(ptr(out), ptr(q), ptr(keys), key_dt, key_stride, seq_key_stride,
+                                    ptr(w), n_heads, head_dim, n_pos, scale, batch, stream_ptr(stream)),
+          "dsv4b_indexer_score")
+
+
+def topk_dev(idx, scores, n, k, batch, stream=None):
+    check(lib().dsv4b_topk(ptr(idx), ptr(scores), n, k, batch, stream_ptr(stream)), "dsv4b_topk")
+
+
+def sparse_attn_scratch(n_heads, d, topk_n, batch):
+    return lib().dsv4b_sparse_attn_scratch(n_heads, d, topk_n, batch)
+
+
+def sparse_attn_dev(o, q, kv, kv_dt, seq_kv_rows, sink, idxs, n_heads, d, topk_n, scale, batch,
+                    scratch, stream=None):
+    nbytes = scratch.numel() * scratch.element_size()
+    check(lib().dsv4b_sparse_attn(ptr(o), ptr(q), ptr(kv), kv_dt, seq_kv_rows, ptr(sink), ptr(idxs),
+                                  n_heads, d, topk_n, scale, batch, ptr(scratch), nbytes,
+                                  stream_ptr(stream)), "dsv4b_sparse_attn")

@@ -122,12 +122,59 @@ int dsv4_cuda_moe(dsv4b_moe *m, float *out, const float *x,
 
 void dsv4_cuda_moe_free(dsv4b_moe *m);
 
+/* ---- sparse MLA, host buffers, synchronous ---- */
+
+/* src/core/dsv4_indexer.c:64-85 -- out[n_pos] = indexer scores of the f32
+ * key rows kv[n_pos][head_dim] for q[n_heads][head_dim] and the unscaled head
+ * weights; the d^-1/2 * h^-1/2 scale is applied inside, as there. The
+ * arithmetic is the reference's, so the scores are bit-identical. 0 or -1. */
+int dsv4_cuda_indexer_score(float *out, const float *q, const float *kv,
+                            const float *weights, int n_heads, int head_dim,
+                            int n_pos);
+
+/* src/core/dsv4_indexer.c:92-106 -- indices of the k largest scores,
+ * descending, ties to the lower index, k clamped to n. Returns the count
+ * written, or -1. */
+int dsv4_cuda_topk(int *idxs, const float *scores, int n, int k);
+
+/* src/core/dsv4_attn.c:60-108 -- o[h][d] = softmax attention of q[h][d] over
+ * the rows of kv[.][d] named by idxs[topk] (-1 = masked), one shared KV head,
+ * per-head sink in the denominator only. 0 or -1. */
+int dsv4_cuda_sparse_attn(float *o, const float *q, const float *kv,
+                          const float *sink, const int *idxs, int h, int d,
+                          int topk, float scale);
+
 /* ===================================================== 2. device API ====== */
 
 /* y[t*rows + o] = sum_c W[o][c] * x[t*cols + c] for t < nt; any nt >= 1.
  * W/S are device pointers in the storage format `wdt`. 0 or -1. */
 int dsv4b_gemv(int wdt, float *y, const float *x, const void *W, const void *S,
                int rows, int cols, int blk_r, int blk_c, int nt, void *stream);
+
+/* Element types of key / KV rows in the sparse-MLA device entries. */
+enum { DSV4B_F32 = 0, DSV4B_BF16 = 1, DSV4B_E4M3 = 2 };
+
+/* Indexer scores for `batch` sequences: out[b][t], t < n_pos, from
+ * q[b][n_heads][head_dim], head weights w[b][n_heads] and key rows of type
+ * key_dt at keys + b*seq_key_stride + t*key_stride (elements). `scale` is the
+ * reference's d^-1/2 * h^-1/2 (the caller computes it in float). */
+int dsv4b_indexer_score(float *out, const float *q, const void *keys,
+                        int key_dt, long key_stride, long seq_key_stride,
+                        const float *w, int n_heads, int head_dim, int n_pos,
+                        float scale, int batch, void *stream);
+
+/* Top-k per sequence: idx[b][min(k,n)] of scores[b][n]. n <= 47104, k <= 4096. */
+int dsv4b_topk(int *idx, const float *scores, int n, int k, int batch,
+               void *stream);
+
+/* Sparse attention per sequence: o[b][n_heads][d] over the KV rows
+ * (type kv_dt, seq_kv_rows rows of width d per sequence) named by
+ * idxs[b][topk]. `scratch` holds dsv4b_sparse_attn_scratch() bytes. */
+size_t dsv4b_sparse_attn_scratch(int n_heads, int d, int topk, int batch);
+int dsv4b_sparse_attn(float *o, const float *q, const void *kv, int kv_dt,
+                      long seq_kv_rows, const float *sink, const int *idxs,
+                      int n_heads, int d, int topk, float scale, int batch,
+                      void *scratch, size_t scratch_bytes, void *stream);
 
 /* The prepared MoE on device buffers x[hidden] -> out[hidden], stream-ordered. */
 int dsv4b_moe_forward(dsv4b_moe *m, float *out, const float *x, void *stream);

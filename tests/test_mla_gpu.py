@@ -109,7 +109,7 @@ def test_config3_pipeline(dev, port, batch):
         assert sc_h[b].tobytes() == rs.tobytes()
         ri = port.topk(rs, K)
         assert list(idx_h[b]) == list(ri)
-        ro = port.sparse_attn(seqs[b][2], kvf, seqs[b][5], ri, scale)
+        ro = port.sparse_attn(seqs[b][2], kvf, seqs[0][5], ri, scale)   # sinks: per head, shared
         assert vrel(o_h[b], ro) < TOL
     for b in range(2, batch):            # the rest: selection from the GPU's own scores
         assert list(idx_h[b]) == list(port.topk(sc_h[b], K))

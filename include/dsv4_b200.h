@@ -29,21 +29,10 @@
 #include <stddef.h>
 #include <stdint.h>
 
-#ifndef DSV4_H
-/* Layout-identical to the reference's DSV4QMat (include/dsv4/dsv4.h:208-214)
- * and storage tags (:92), so a pointer to the reference's struct can be passed
- * straight through. When the reference's dsv4.h is included first, its own
- * definitions are used. */
-typedef struct {
-    const void *w;
-    const void *s;
-    int wdt;
-    int rows, cols;
-    int blk_r, blk_c;
-} DSV4QMat;
-enum { DSV4_WF32 = 0, DSV4_WBF16 = 1, DSV4_WFP8 = 2, DSV4_WFP4 = 3 };
-#define DSV4_MAX_BATCH 64
-#endif
+/* DSV4QMat, DSV4Cfg, DSV4LayerW, ... : the reference's own types, mirrored
+ * layout-identically (include/dsv4/dsv4.h:94-295), so pointers to the structs
+ * the reference's binder fills pass straight through. */
+#include "dsv4_types.h"
 
 #ifdef __cplusplus
 extern "C" {

@@ -126,6 +126,14 @@ int dsv4o_compress_step(float *out, const float *kv_in, const float *score_in,
                         const float *ape, float *kv_state, float *score_state,
                         int pos, int ratio, int head_dim);
 
+/* ---- whole-token decode over the reference's structs (dsv4_oracle_model.c) ----
+ * Declared with opaque pointers so this header does not need dsv4_types.h. */
+typedef struct dsv4o_model dsv4o_model;
+dsv4o_model *dsv4o_model_create(const void *cfg, const void *mw, const void *layers,
+                                const void *experts, int max_pos);
+int dsv4o_model_step(dsv4o_model *m, int token, int pos, float *logits);
+void dsv4o_model_free(dsv4o_model *m);
+
 #ifdef __cplusplus
 }
 #endif

@@ -254,3 +254,51 @@ def moe(chk, x, gate, experts, shared, bias, topk, route_scale, score_func, swig
       None if tid is None else tid.ctypes.data, 0, arr, sh, n, topk, route_scale, score_func,
       hidden, inter, inter_shared, swiglu_limit, idx, w)
     return out, idx, w
+
+
+def _greedy(step, n_prompt, tokens, n_gen, vocab, keep_logits):
+    ids = list(tokens)
+    out, rows = [], []
+    lg = np.empty(vocab, np.float32)
+    for pos in range(n_prompt + n_gen):
+        best = step(ids[pos], pos, lg)
+        if best < 0:
+            raise RuntimeError("model step failed at position %d" % pos)
+        if pos + 1 >= n_prompt:
+            out.append(best)
+            if keep_logits:
+                rows.append(lg.copy())
+            if pos + 1 < n_prompt + n_gen:
+                ids.append(best)
+    return np.array(out, np.int32), (np.stack(rows) if keep_logits else None)
+
+
+def model_greedy_port(sm, tokens, n_gen, max_pos, keep_logits=True):
+    """Greedy decode through the oracle's restated model (dsv4_oracle_model.c)."""
+    lib = _Lib(build_oracle(), "dsv4o_")
+    create = lib.fn("model_create", [_vp, _vp, _vp, _vp, _i], _vp)
+    step = lib.fn("model_step", [_vp, _i, _i, _f32p], _i)
+    free = lib.fn("model_free", [_vp])
+    m = create(C.addressof(sm.cfg), C.addressof(sm.mw), C.addressof(sm.layers), C.addressof(sm.experts),
+               max_pos)
+    try:
+        return _greedy(lambda t, p, lg: step(m, t, p, lg), len(tokens), tokens, n_gen, sm.d["vocab"],
+                       keep_logits)
+    finally:
+        free(m)
+
+
+def model_greedy_ref(sm, tokens, n_gen, max_pos):
+    """Greedy decode through the REFERENCE's dsv4_layer_forward (oracle/_ref)."""
+    lib = C.CDLL(REF_SO)
+    f = lib.dsv4ref_greedy
+    f.argtypes = [_vp, _vp, _vp, _vp, _i, _i32p, _i, _i, _i32p, _f32p]
+    f.restype = _i
+    toks = np.ascontiguousarray(tokens, np.int32)
+    out = np.empty(n_gen + 1, np.int32)
+    lg = np.empty((n_gen + 1, sm.d["vocab"]), np.float32)
+    n = f(C.addressof(sm.cfg), C.addressof(sm.mw), C.addressof(sm.layers), C.addressof(sm.experts),
+          max_pos, toks, toks.size, n_gen, out, lg)
+    if n < 0:
+        raise RuntimeError("reference driver failed")
+    return out[:n], lg[:n]

@@ -1,0 +1,15 @@
+"""Record the reference's struct layout (sizeof/offsetof of its model-level
+types) into tests/golden/layout_ref.txt by compiling layout_probe.c against
+the reference's include/dsv4/dsv4.h. Needs the reference checkout."""
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+exe = "/tmp/layout_probe_ref"
+subprocess.run(["/usr/bin/gcc", "-DUSE_REF", "-I" + os.path.join(REF, "include", "dsv4"),
+                os.path.join(HERE, "layout_probe.c"), "-o", exe], check=True)
+out = subprocess.run([exe], check=True, capture_output=True, text=True).stdout
+open(os.path.join(HERE, "layout_ref.txt"), "w").write(out)
+print(out)

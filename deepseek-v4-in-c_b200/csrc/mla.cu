@@ -45,8 +45,10 @@ constexpr int IX_TP = 32;
 __global__ void __launch_bounds__(256)
 k_indexer_score(float *out, const float *q, const void *keys, int key_dt, long key_stride,
                 long seq_key_stride, const float *w, int n_heads, int head_dim, int n_pos,
-                float scale, long seq_q_stride, long seq_out_stride)
+                float scale, long seq_q_stride, long seq_out_stride, const int *dyn_n)
 {
+    if (dyn_n) n_pos = min(n_pos, *dyn_n);       // rows that exist this step
+    if ((int)blockIdx.x * IX_TP >= n_pos) return;
     extern __shared__ double ixs[];
     double *qs = ixs;                               // [n_heads][head_dim]
     double *kt = qs + n_heads * head_dim;           // [head_dim][IX_TP]
@@ -100,8 +102,10 @@ __device__ __forceinline__ uint32_t fkey(float v)
 // One CTA (1024 threads) per sequence. scores [n] -> idx [min(k, n)] in
 // descending order, ties to the lower index. n <= kTopkMaxN, k <= kTopkMaxK.
 __global__ void __launch_bounds__(1024)
-k_topk(int *idx_out, const float *scores, int n, int k, long seq_in_stride, long seq_out_stride)
+k_topk(int *idx_out, const float *scores, int n, int k, long seq_in_stride, long seq_out_stride,
+       const int *dyn_nk)
 {
+    if (dyn_nk) { n = min(n, dyn_nk[0]); k = dyn_nk[1]; }
     extern __shared__ uint32_t tks[];
     uint32_t *key = tks;                                   // [n]
     unsigned long long *sel = reinterpret_cast<unsigned long long *>(key + ((n + 1) & ~1)); // [kpow2]
@@ -334,7 +338,7 @@ __global__ void k_attn_combine(float *o, AttnPart part, const float *sink, int n
 
 int indexer_score(float *out, const float *q, const void *keys, int key_dt, long key_stride,
                   long seq_key_stride, const float *w, int n_heads, int head_dim, int n_pos, float scale,
-                  int batch, cudaStream_t st)
+                  int batch, cudaStream_t st, const int *dyn_n)
 {
     if (n_pos <= 0 || batch <= 0) return 0;
     const size_t smem = ((size_t)n_heads * head_dim + (size_t)head_dim * IX_TP + (size_t)IX_TP * n_heads) * 8;
@@ -346,12 +350,12 @@ int indexer_score(float *out, const float *q, const void *keys, int key_dt, long
     }
     dim3 grid((n_pos + IX_TP - 1) / IX_TP, batch);
     k_indexer_score<<<grid, 256, smem, st>>>(out, q, keys, key_dt, key_stride, seq_key_stride, w, n_heads,
-                                             head_dim, n_pos, scale, (long)n_heads * head_dim, n_pos);
+                                             head_dim, n_pos, scale, (long)n_heads * head_dim, n_pos, dyn_n);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 
 int topk(int *idx, const float *scores, int n, int k, int batch, long seq_in_stride, long seq_out_stride,
-         cudaStream_t st)
+         cudaStream_t st, const int *dyn_nk)
 {
     if (batch <= 0 || n <= 0 || k <= 0) return 0;
     if (n > kTopkMaxN || k > kTopkMaxK) return -1;
@@ -364,7 +368,7 @@ int topk(int *idx, const float *scores, int n, int k, int batch, long seq_in_str
         cudaFuncSetAttribute(k_topk, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
         attr = true;
     }
-    k_topk<<<dim3(1, batch), 1024, smem, st>>>(idx, scores, n, k, seq_in_stride, seq_out_stride);
+    k_topk<<<dim3(1, batch), 1024, smem, st>>>(idx, scores, n, k, seq_in_stride, seq_out_stride, dyn_nk);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 

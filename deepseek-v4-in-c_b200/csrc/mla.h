@@ -18,10 +18,12 @@ constexpr int kTopkMaxK = 4096;
 // t*key_stride elements; q is [batch][n_heads][head_dim], w [batch][n_heads].
 int indexer_score(float *out, const float *q, const void *keys, int key_dt, long key_stride,
                   long seq_key_stride, const float *w, int n_heads, int head_dim, int n_pos,
-                  float scale, int batch, cudaStream_t st);
+                  float scale, int batch, cudaStream_t st, const int *dyn_n = nullptr);
 // idx[b][i], i < min(k, n): descending scores, ties to the lower index.
+// dyn_nk (device, may be null): {n, k} of this step, n <= the launch's n and
+// k <= the launch's k (the launch sizes shared memory for the maxima).
 int topk(int *idx, const float *scores, int n, int k, int batch, long seq_in_stride,
-         long seq_out_stride, cudaStream_t st);
+         long seq_out_stride, cudaStream_t st, const int *dyn_nk = nullptr);
 size_t attn_part_bytes(int n_heads, int d, int topk, int batch);
 // o[b][h][d]; kv of sequence b is rows [b*seq_kv_rows, ...) of width d; idxs
 // [b][topk] with -1 = masked; part_buf holds attn_part_bytes().

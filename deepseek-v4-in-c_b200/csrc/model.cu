@@ -1,0 +1,526 @@
+// model.cu - whole-token decode with every weight resident in HBM.
+//
+// One decode token of src/cli/dsv4_run.c:444-483 (embed, every
+// dsv4_layer_forward, hc_head, final norm, LM head, argmax) as a fixed
+// sequence of device launches: the GEMVs of gemv.cu, moe_forward of moe.cu,
+// the sparse-MLA kernels of mla.cu and the support ops of model_kernels.cu.
+// Nothing in the sequence depends on the host: the position and token live in
+// a device StepState that the last kernel advances, so the sequence is
+// captured once into a CUDA graph and replayed for every position.
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+#include "mla.h"
+#include "model.h"
+#include "../../include/dsv4_b200.h"
+
+namespace dsv4b {
+
+struct DevLayer {
+    float *attn_norm, *ffn_norm, *sink, *q_norm, *kv_norm;
+    DevMat wq_a, wq_b, wkv, wo_a, wo_b;
+    int ratio, has_comp, has_idx, coff;
+    float *ape, *cnorm;
+    DevMat cwkv, cwgate, iwq_b, iwproj;
+    float *hca_fn, *hca_base, *hca_scale, *hcf_fn, *hcf_base, *hcf_scale;
+    MoeLayer moe;
+    float *kv_cache, *comp_kv, *comp_score;
+    int *dyn;
+    size_t kv_rows, comp_n;
+};
+
+}  // namespace dsv4b
+
+struct dsv4b_model {
+    DSV4Cfg c;
+    int ratios[DSV4_MAX_LAYERS];
+    int max_pos, nidx, ncomp4;
+    std::vector<dsv4b::DevLayer> L;
+    const void *embed;
+    int emb_wdt;
+    dsv4b::DevMat head;
+    float *norm, *hch_fn, *hch_base, *hch_scale;
+    float *cs_d, *sn_d, *cs_c, *sn_c;
+    float *h, *resid, *x1, *blk, *post, *comb, *mixes, *qr, *q, *kv, *o, *ogrp;
+    float *comp_in, *comp_sc, *idx_q, *idx_w, *idx_scores, *logits, *xh, *am_pv;
+    int *idxs, *isel, *am_pi, *prompt, *out_tokens;
+    void *attn_part;
+    dsv4b::MoeScratch ms;
+    dsv4b::StepState *st;
+    int n_prompt;
+    std::vector<void *> allocs;
+    cudaStream_t stream;
+    cudaGraph_t graph;
+    cudaGraphExec_t exec;
+    int graphed;
+};
+
+namespace dsv4b {
+
+static void *dalloc(dsv4b_model *m, size_t bytes)
+{
+    void *p = nullptr;
+    if (cudaMalloc(&p, bytes ? bytes : 16) != cudaSuccess) return nullptr;
+    m->allocs.push_back(p);
+    return p;
+}
+
+static void *dcopy(dsv4b_model *m, const void *host, size_t bytes, bool *ok)
+{
+    if (!*ok) return nullptr;
+    void *p = dalloc(m, bytes);
+    if (!p || (host && cudaMemcpy(p, host, bytes, cudaMemcpyHostToDevice) != cudaSuccess)) {
+        *ok = false;
+        return nullptr;
+    }
+    return p;
+}
+
+static size_t qmat_sbytes(const DSV4QMat &q)
+{
+    if (q.wdt < DSV4_WFP8) return 0;
+    return (size_t)((q.rows + q.blk_r - 1) / q.blk_r) * ((q.cols + q.blk_c - 1) / q.blk_c);
+}
+
+static DevMat up_mat(dsv4b_model *m, const DSV4QMat &q, bool *ok)
+{
+    DevMat d = {};
+    d.wdt = q.wdt;
+    d.rows = q.rows;
+    d.cols = q.cols;
+    d.blk_r = q.blk_r;
+    d.blk_c = q.blk_c;
+    if (!q.w) { *ok = false; return d; }
+    d.w = (const uint8_t *)dcopy(m, q.w, row_bytes(q.wdt, q.cols) * q.rows, ok);
+    if (q.wdt >= DSV4_WFP8) d.s = (const uint8_t *)dcopy(m, q.s, qmat_sbytes(q), ok);
+    return d;
+}
+
+static float *up_f32(dsv4b_model *m, const float *p, size_t n, bool *ok)
+{
+    return (float *)dcopy(m, p, n * 4, ok);
+}
+
+// RoPE cos/sin tables (src/core/dsv4_rope.c:48-99), computed on the host in
+// double exactly as the reference does, then copied to the device.
+static void rope_table(float *cs, float *sn, int dim, int seqlen, int orig, double base, double factor,
+                       double beta_fast, double beta_slow)
+{
+    const int half = dim / 2;
+    std::vector<double> f(half);
+    for (int i = 0; i < half; i++) f[i] = 1.0 / pow(base, (double)(2 * i) / (double)dim);
+    if (orig > 0) {
+        const double twopi = 2.0 * 3.14159265358979323846;
+        const double lo_d = (double)dim * log((double)orig / (beta_fast * twopi)) / (2.0 * log(base));
+        const double hi_d = (double)dim * log((double)orig / (beta_slow * twopi)) / (2.0 * log(base));
+        int lo = (int)floor(lo_d), hi = (int)ceil(hi_d);
+        if (lo < 0) lo = 0;
+        if (hi > dim - 1) hi = dim - 1;
+        double mn = (double)lo, mx = (double)hi;
+        if (mn == mx) mx += 0.001;
+        for (int i = 0; i < half; i++) {
+            double ramp = ((double)i - mn) / (mx - mn);
+            if (ramp < 0.0) ramp = 0.0;
+            if (ramp > 1.0) ramp = 1.0;
+            const double smooth = 1.0 - ramp;
+            f[i] = f[i] / factor * (1.0 - smooth) + f[i] * smooth;
+        }
+    }
+    for (int t = 0; t < seqlen; t++)
+        for (int i = 0; i < half; i++) {
+            const double th = (double)t * f[i];
+            cs[(size_t)t * half + i] = (float)cos(th);
+            sn[(size_t)t * half + i] = (float)sin(th);
+        }
+}
+
+// Allocate the activations, state and tables every model needs.
+static bool alloc_common(dsv4b_model *m)
+{
+    const DSV4Cfg &c = m->c;
+    bool ok = true;
+    const int hc = c.hc_mult, d = c.hidden, hd = c.head_dim, win = c.sliding_window;
+    const int half = c.qk_rope / 2;
+    std::vector<float> cs((size_t)m->max_pos * half), sn((size_t)m->max_pos * half);
+    rope_table(cs.data(), sn.data(), c.qk_rope, m->max_pos, 0, c.rope_theta, c.yarn_factor, c.yarn_beta_fast,
+               c.yarn_beta_slow);
+    m->cs_d = (float *)dcopy(m, cs.data(), cs.size() * 4, &ok);
+    m->sn_d = (float *)dcopy(m, sn.data(), sn.size() * 4, &ok);
+    rope_table(cs.data(), sn.data(), c.qk_rope, m->max_pos, c.yarn_orig_ctx, c.compress_rope_theta,
+               c.yarn_factor, c.yarn_beta_fast, c.yarn_beta_slow);
+    m->cs_c = (float *)dcopy(m, cs.data(), cs.size() * 4, &ok);
+    m->sn_c = (float *)dcopy(m, sn.data(), sn.size() * 4, &ok);
+    // the attention index list: window + the most compressed rows any layer adds
+    int extra = 0;
+    m->ncomp4 = 1;
+    for (int L = 0; L < c.n_layers; L++) {
+        const int r = m->ratios[L];
+        if (r == 4) m->ncomp4 = m->max_pos / 4 + 1;
+        const int add = r == 0 ? 0 : (r == 4 ? c.index_topk : m->max_pos / r + 1);
+        if (add > extra) extra = add;
+    }
+    m->nidx = win + extra;
+    const size_t big = (size_t)(d > c.q_lora ? d : c.q_lora);
+    auto F = [&](size_t n) { return (float *)dcopy(m, nullptr, n * 4, &ok); };
+    m->h = F((size_t)hc * d);
+    m->resid = F((size_t)hc * d);
+    m->x1 = F(d);
+    m->blk = F(d);
+    m->post = F(DSV4B_MAX_HC);
+    m->comb = F(DSV4B_MAX_HC * DSV4B_MAX_HC);
+    m->mixes = F((2 + DSV4B_MAX_HC) * DSV4B_MAX_HC);
+    m->qr = F(big);
+    m->q = F((size_t)c.n_heads * hd);
+    m->kv = F(hd);
+    m->o = F((size_t)c.n_heads * hd);
+    m->ogrp = F((size_t)c.o_groups * c.o_lora);
+    m->comp_in = F(2 * hd);
+    m->comp_sc = F(2 * hd);
+    m->idx_q = F((size_t)c.index_n_heads * c.index_head_dim);
+    m->idx_w = F(c.index_n_heads);
+    m->idx_scores = F(m->ncomp4);
+    m->logits = F(c.vocab);
+    m->xh = F(d);
+    m->am_pv = F(1024);
+    m->am_pi = (int *)dcopy(m, nullptr, 1024 * 4, &ok);
+    m->idxs = (int *)dcopy(m, nullptr, (size_t)m->nidx * 4, &ok);
+    m->isel = (int *)dcopy(m, nullptr, (size_t)(c.index_topk > 0 ? c.index_topk : 1) * 4, &ok);
+    m->prompt = (int *)dcopy(m, nullptr, (size_t)m->max_pos * 4, &ok);
+    m->out_tokens = (int *)dcopy(m, nullptr, (size_t)m->max_pos * 4, &ok);
+    m->st = (StepState *)dcopy(m, nullptr, sizeof(StepState), &ok);
+    m->attn_part = dcopy(m, nullptr, attn_part_bytes(c.n_heads, hd, m->nidx, 1), &ok);
+    const int inter_s = c.moe_inter * c.n_shared;
+    const size_t nf = moe_scratch_floats(d, c.moe_inter, inter_s, c.n_experts, c.topk);
+    float *msb = F(nf + kMoeMaxTopk);
+    if (ok) moe_scratch_carve(m->ms, msb, d, c.moe_inter, inter_s, c.n_experts, c.topk);
+    for (int L = 0; L < c.n_layers && ok; L++) {
+        DevLayer &l = m->L[L];
+        l.ratio = m->ratios[L];
+        l.coff = l.ratio == 4 ? 2 : 1;
+        const size_t ncomp = l.ratio ? (size_t)(m->max_pos / l.ratio + 1) : 0;
+        l.kv_rows = (size_t)win + ncomp;
+        l.kv_cache = F(l.kv_rows * hd);
+        l.comp_n = l.ratio ? (size_t)l.coff * l.ratio * l.coff * hd : 0;
+        l.comp_kv = l.comp_n ? F(l.comp_n) : nullptr;
+        l.comp_score = l.comp_n ? F(l.comp_n) : nullptr;
+        l.dyn = (int *)dcopy(m, nullptr, 8, &ok);
+    }
+    return ok;
+}
+
+__global__ void k_fill(float *p, size_t n, float v)
+{
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) p[i] = v;
+}
+
+// Empty caches and compressor windows (score -inf: an unfilled slot must
+// contribute nothing, src/model/dsv4_layer.c:100-106).
+static int reset_state(dsv4b_model *m)
+{
+    for (DevLayer &l : m->L) {
+        DSV4B_CUDA_OK(cudaMemsetAsync(l.kv_cache, 0, l.kv_rows * m->c.head_dim * 4, m->stream));
+        if (l.comp_n) {
+            DSV4B_CUDA_OK(cudaMemsetAsync(l.comp_kv, 0, l.comp_n * 4, m->stream));
+            k_fill<<<64, 256, 0, m->stream>>>(l.comp_score, l.comp_n, -INFINITY);
+        }
+        DSV4B_CUDA_OK(cudaMemsetAsync(l.dyn, 0, 8, m->stream));
+    }
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
+}
+
+static int G(const DevMat &w, float *y, const float *x, cudaStream_t st)
+{
+    return gemv(w.wdt, y, w.rows, x, w.cols, w.w, w.s, w.rows, w.cols, w.blk_r, w.blk_c, 1, st);
+}
+
+static int hc_pre(dsv4b_model *m, const float *fn, const float *base, const float *scale, cudaStream_t st)
+{
+    const DSV4Cfg &c = m->c;
+    const int hc = c.hc_mult, mix = (2 + hc) * hc, n = hc * c.hidden;
+    k_hc_mix<<<mix, 256, 0, st>>>(m->mixes, fn, m->h, n, c.rms_eps);
+    k_hc_finish<<<1, 256, 0, st>>>(m->x1, m->post, m->comb, m->mixes, m->h, scale, base, hc, c.hidden,
+                                   c.hc_sinkhorn_iters, c.hc_eps);
+    return 0;
+}
+
+// One token: enqueue only, no host synchronisation (graph-capturable).
+static int enqueue_step(dsv4b_model *m, cudaStream_t st)
+{
+    const DSV4Cfg &c = m->c;
+    const int hc = c.hc_mult, d = c.hidden, hd = c.head_dim, rd = c.qk_rope, H = c.n_heads;
+    const int win = c.sliding_window, wide = hc * d;
+    int rc = 0;
+    k_embed<<<16, 256, 0, st>>>(m->h, m->embed, m->emb_wdt, m->st, d, hc);
+    for (int Li = 0; Li < c.n_layers; Li++) {
+        DevLayer &l = m->L[Li];
+        const float *cs = l.ratio ? m->cs_c : m->cs_d, *sn = l.ratio ? m->sn_c : m->sn_d;
+        // ---- attention half (src/model/dsv4_layer.c:495-509)
+        cudaMemcpyAsync(m->resid, m->h, (size_t)wide * 4, cudaMemcpyDeviceToDevice, st);
+        hc_pre(m, l.hca_fn, l.hca_base, l.hca_scale, st);
+        k_rmsnorm<<<1, 1024, 0, st>>>(m->x1, m->x1, l.attn_norm, d, c.rms_eps);
+        rc |= G(l.wq_a, m->qr, m->x1, st);
+        k_rmsnorm<<<1, 1024, 0, st>>>(m->qr, m->qr, l.q_norm, c.q_lora, c.rms_eps);
+        rc |= G(l.wq_b, m->q, m->qr, st);
+        k_heads_norm_rope<<<H, 256, 0, st>>>(m->q, hd, rd, cs, sn, m->st, 0, 0, 1, c.rms_eps);
+        rc |= G(l.wkv, m->kv, m->x1, st);
+        k_kv_finish<<<1, 256, 0, st>>>(m->kv, l.kv_norm, hd, rd, cs, sn, m->st, c.rms_eps, l.kv_cache, win);
+        if (l.has_comp) {
+            rc |= G(l.cwkv, m->comp_in, m->x1, st);
+            rc |= G(l.cwgate, m->comp_sc, m->x1, st);
+            k_compress<<<1, 512, hd * 4, st>>>(l.kv_cache, l.comp_kv, l.comp_score, m->comp_in, m->comp_sc, l.ape,
+                                               l.cnorm, l.ratio, hd, rd, cs, sn, m->st, c.rms_eps, win,
+                                               c.index_topk, l.dyn);
+            if (l.has_idx) {
+                const int ih = c.index_n_heads, id = c.index_head_dim;
+                rc |= G(l.iwq_b, m->idx_q, m->qr, st);
+                k_heads_norm_rope<<<ih, 128, 0, st>>>(m->idx_q, id, rd, cs, sn, m->st, 0, 0, 0, c.rms_eps);
+                rc |= G(l.iwproj, m->idx_w, m->x1, st);
+                const float scale = (1.0f / sqrtf((float)id)) * (1.0f / sqrtf((float)ih));
+                // the compressed region read as contiguous rows of index_head_dim
+                // floats, as the reference does (dsv4_layer.c:286-289)
+                rc |= indexer_score(m->idx_scores, m->idx_q, l.kv_cache + (size_t)win * hd, DSV4B_DT_F32, id, 0,
+                                    m->idx_w, ih, id, m->ncomp4, scale, 1, st, l.dyn);
+                rc |= topk(m->isel, m->idx_scores, m->ncomp4, c.index_topk, 1, m->ncomp4, c.index_topk, st, l.dyn);
+            }
+        }
+        k_build_idxs<<<1, 256, 0, st>>>(m->idxs, m->nidx, m->st, win, l.has_comp, l.has_idx, l.dyn, m->isel);
+        rc |= sparse_attn(m->o, m->q, l.kv_cache, DSV4B_DT_F32, (long)l.kv_rows, l.sink, m->idxs, m->nidx, H, hd,
+                          m->nidx, 1.0f / sqrtf((float)hd), 1, m->attn_part, st);
+        k_heads_norm_rope<<<H, 256, 0, st>>>(m->o, hd, rd, cs, sn, m->st, 0, 1, 0, c.rms_eps);
+        // grouped low-rank output (dsv4_layer.c:303-335)
+        const int gw = H * hd / c.o_groups, gr = c.o_lora;
+        for (int g = 0; g < c.o_groups; g++) {
+            const DevMat &wa = l.wo_a;
+            const size_t rb = row_bytes(wa.wdt, wa.cols);
+            const uint8_t *ws = wa.w + (size_t)g * gr * rb;
+            const uint8_t *ss = wa.s ? wa.s + (size_t)(g * gr / wa.blk_r) * ((wa.cols + wa.blk_c - 1) / wa.blk_c) : nullptr;
+            rc |= gemv(wa.wdt, m->ogrp + (size_t)g * gr, gr, m->o + (size_t)g * gw, gw, ws, ss, gr, gw, wa.blk_r,
+                       wa.blk_c, 1, st);
+        }
+        rc |= G(l.wo_b, m->blk, m->ogrp, st);
+        k_hc_post<<<(wide + 255) / 256, 256, 0, st>>>(m->h, m->blk, m->resid, m->post, m->comb, hc, d);
+        // ---- FFN half: the residual is taken after attention (:511-522)
+        cudaMemcpyAsync(m->resid, m->h, (size_t)wide * 4, cudaMemcpyDeviceToDevice, st);
+        hc_pre(m, l.hcf_fn, l.hcf_base, l.hcf_scale, st);
+        k_rmsnorm<<<1, 1024, 0, st>>>(m->x1, m->x1, l.ffn_norm, d, c.rms_eps);
+        rc |= moe_forward(l.moe, m->ms, m->blk, m->x1, &m->st->token, st);
+        k_hc_post<<<(wide + 255) / 256, 256, 0, st>>>(m->h, m->blk, m->resid, m->post, m->comb, hc, d);
+    }
+    // ---- head (src/cli/dsv4_run.c:467-474)
+    k_hc_mix<<<hc, 256, 0, st>>>(m->mixes, m->hch_fn, m->h, wide, c.rms_eps);
+    k_hc_head_finish<<<1, 256, 0, st>>>(m->xh, m->mixes, m->h, m->hch_scale, m->hch_base, hc, d, c.hc_eps);
+    k_rmsnorm<<<1, 1024, 0, st>>>(m->xh, m->xh, m->norm, d, c.rms_eps);
+    rc |= G(m->head, m->logits, m->xh, st);
+    k_argmax_part<<<148, 256, 0, st>>>(m->am_pv, m->am_pi, m->logits, c.vocab);
+    k_argmax_final<<<1, 32, 0, st>>>(m->st, m->out_tokens, m->am_pv, m->am_pi, 148, m->prompt, m->n_prompt);
+    if (cudaPeekAtLastError() != cudaSuccess) rc = -1;
+    return rc ? -1 : 0;
+}
+
+static bool build_layer_from_host(dsv4b_model *m, int Li, const DSV4LayerW &w, const DSV4ExpertW *ex)
+{
+    const DSV4Cfg &c = m->c;
+    DevLayer &l = m->L[Li];
+    bool ok = true;
+    const int d = c.hidden, hd = c.head_dim, hc = c.hc_mult, mix = (2 + hc) * hc;
+    l.has_comp = w.has_comp;
+    l.has_idx = w.has_idx;
+    if ((l.ratio != 0) != (w.has_comp != 0) || (w.has_idx && l.ratio != 4)) return false;
+    l.attn_norm = up_f32(m, w.attn_norm, d, &ok);
+    l.ffn_norm = up_f32(m, w.ffn_norm, d, &ok);
+    l.sink = up_f32(m, w.attn.sink, c.n_heads, &ok);
+    l.q_norm = up_f32(m, w.attn.q_norm, c.q_lora, &ok);
+    l.kv_norm = up_f32(m, w.attn.kv_norm, hd, &ok);
+    l.wq_a = up_mat(m, w.attn.wq_a, &ok);
+    l.wq_b = up_mat(m, w.attn.wq_b, &ok);
+    l.wkv = up_mat(m, w.attn.wkv, &ok);
+    l.wo_a = up_mat(m, w.attn.wo_a, &ok);
+    l.wo_b = up_mat(m, w.attn.wo_b, &ok);
+    if (l.has_comp) {
+        l.ape = up_f32(m, w.attn.comp.ape, (size_t)l.ratio * l.coff * hd, &ok);
+        l.cnorm = up_f32(m, w.attn.comp.norm, hd, &ok);
+        l.cwkv = up_mat(m, w.attn.comp.wkv, &ok);
+        l.cwgate = up_mat(m, w.attn.comp.wgate, &ok);
+    }
+    if (l.has_idx) {
+        l.iwq_b = up_mat(m, w.attn.idx.wq_b, &ok);
+        l.iwproj = up_mat(m, w.attn.idx.weights_proj, &ok);
+    }
+    l.hca_fn = up_f32(m, w.hc_attn.fn, (size_t)mix * hc * d, &ok);
+    l.hca_base = up_f32(m, w.hc_attn.base, mix, &ok);
+    l.hca_scale = up_f32(m, w.hc_attn.scale, 3, &ok);
+    l.hcf_fn = up_f32(m, w.hc_ffn.fn, (size_t)mix * hc * d, &ok);
+    l.hcf_base = up_f32(m, w.hc_ffn.base, mix, &ok);
+    l.hcf_scale = up_f32(m, w.hc_ffn.scale, 3, &ok);
+    // MoE
+    MoeLayer &mo = l.moe;
+    mo.gate = up_mat(m, w.moe.gate, &ok);
+    mo.bias = w.moe.bias ? up_f32(m, w.moe.bias, c.n_experts, &ok) : nullptr;
+    mo.tid2eid = w.moe.tid2eid ? (const int64_t *)dcopy(m, w.moe.tid2eid, (size_t)c.vocab * c.topk * 8, &ok)
+                               : nullptr;
+    mo.fixed = nullptr;
+    std::vector<const uint8_t *> tab((size_t)6 * c.n_experts);
+    for (int e = 0; e < c.n_experts && ok; e++) {
+        const DSV4ExpertW &x = ex[(size_t)Li * c.n_experts + e];
+        const DSV4QMat *q3[3] = { &x.w1, &x.w3, &x.w2 };
+        for (int j = 0; j < 3; j++) {
+            const DevMat dm = up_mat(m, *q3[j], &ok);
+            tab[(size_t)(2 * j) * c.n_experts + e] = dm.w;
+            tab[(size_t)(2 * j + 1) * c.n_experts + e] = dm.s;
+            if (e == 0 && j == 0) { mo.efmt = dm.wdt; mo.eblk_r = dm.blk_r; mo.eblk_c = dm.blk_c; }
+        }
+    }
+    const uint8_t *const *t = (const uint8_t *const *)dcopy(m, tab.data(), tab.size() * sizeof(void *), &ok);
+    if (!ok) return false;
+    mo.w1tab = t; mo.s1tab = t + c.n_experts;
+    mo.w3tab = t + 2 * c.n_experts; mo.s3tab = t + 3 * c.n_experts;
+    mo.w2tab = t + 4 * c.n_experts; mo.s2tab = t + 5 * c.n_experts;
+    mo.sh[0] = up_mat(m, w.moe.shared.w1, &ok);
+    mo.sh[1] = up_mat(m, w.moe.shared.w3, &ok);
+    mo.sh[2] = up_mat(m, w.moe.shared.w2, &ok);
+    mo.has_shared = 1;
+    mo.n_experts = c.n_experts;
+    mo.topk = c.topk;
+    mo.hidden = d;
+    mo.inter = c.moe_inter;
+    mo.inter_shared = c.moe_inter * c.n_shared;
+    mo.score_func = c.scoring_func == DSV4_SCORE_SIGMOID ? 2 : 1;
+    mo.route_scale = c.routed_scale;
+    mo.swiglu_limit = c.swiglu_limit;
+    return ok;
+}
+
+}  // namespace dsv4b
+
+using namespace dsv4b;
+
+extern "C" void dsv4_cuda_model_free(dsv4b_model *m)
+{
+    if (!m) return;
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    if (m->graphed) {
+        cudaGraphExecDestroy(m->exec);
+        cudaGraphDestroy(m->graph);
+    }
+    for (void *p : m->allocs) cudaFree(p);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+static dsv4b_model *model_new(const DSV4Cfg *c, int max_pos)
+{
+    if (dsv4_cuda_init() != 0 || !c || c->n_layers < 1 || c->n_layers > DSV4_MAX_LAYERS || max_pos < 1 ||
+        c->hc_mult > DSV4B_MAX_HC || c->topk > kMoeMaxTopk || c->n_experts > kMoeMaxExperts || c->n_heads > 64 ||
+        c->index_topk > kTopkMaxK)
+        return nullptr;
+    dsv4b_model *m = new dsv4b_model();
+    m->c = *c;
+    for (int L = 0; L < c->n_layers; L++) m->ratios[L] = c->compress_ratios ? c->compress_ratios[L] : 0;
+    m->c.compress_ratios = m->ratios;
+    m->max_pos = max_pos;
+    m->L.resize(c->n_layers);
+    if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess || !alloc_common(m)) {
+        dsv4_cuda_model_free(m);
+        return nullptr;
+    }
+    if (m->ncomp4 > kTopkMaxN) {
+        dsv4_cuda_model_free(m);
+        return nullptr;
+    }
+    return m;
+}
+
+extern "C" dsv4b_model *dsv4_cuda_model_create(const DSV4Cfg *c, const DSV4ModelW *mw, const DSV4LayerW *layers,
+                                               const DSV4ExpertW *experts, int max_pos)
+{
+    if (!mw || !layers || !experts) return nullptr;
+    dsv4b_model *m = model_new(c, max_pos);
+    if (!m) return nullptr;
+    bool ok = true;
+    for (int L = 0; L < c->n_layers && ok; L++) ok = build_layer_from_host(m, L, layers[L], experts);
+    const int d = c->hidden, hc = c->hc_mult;
+    m->emb_wdt = mw->wdt;
+    m->embed = dcopy(m, mw->embed, (size_t)c->vocab * d * (mw->wdt == DSV4_WBF16 ? 2 : 4), &ok);
+    DSV4QMat hq = { mw->head, nullptr, mw->wdt, c->vocab, d, 0, 0 };
+    m->head = up_mat(m, hq, &ok);
+    m->norm = up_f32(m, mw->norm, d, &ok);
+    m->hch_fn = up_f32(m, mw->hc_head.fn, (size_t)hc * hc * d, &ok);
+    m->hch_base = up_f32(m, mw->hc_head.base, hc, &ok);
+    m->hch_scale = up_f32(m, mw->hc_head.scale, 1, &ok);
+    if (!ok || cudaDeviceSynchronize() != cudaSuccess) {
+        dsv4_cuda_model_free(m);
+        return nullptr;
+    }
+    return m;
+}
+
+extern "C" int dsv4_cuda_model_begin(dsv4b_model *m, const int *prompt, int n_prompt)
+{
+    if (!m || !prompt || n_prompt < 1 || n_prompt > m->max_pos) return -1;
+    for (int i = 0; i < n_prompt; i++)
+        if (prompt[i] < 0 || prompt[i] >= m->c.vocab) return -1;
+    m->n_prompt = n_prompt;
+    DSV4B_CUDA_OK(cudaMemcpyAsync(m->prompt, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, m->stream));
+    StepState s0 = { prompt[0], 0 };
+    if (reset_state(m)) return -1;
+    DSV4B_CUDA_OK(cudaMemcpyAsync(m->st, &s0, sizeof s0, cudaMemcpyHostToDevice, m->stream));
+    if (!m->graphed) {
+        // one eager step sets every kernel attribute, then the state is reset
+        // and the step is captured once for all positions
+        if (enqueue_step(m, m->stream)) return -1;
+        DSV4B_CUDA_OK(cudaStreamSynchronize(m->stream));
+        if (reset_state(m)) return -1;
+        DSV4B_CUDA_OK(cudaMemcpyAsync(m->st, &s0, sizeof s0, cudaMemcpyHostToDevice, m->stream));
+        DSV4B_CUDA_OK(cudaStreamSynchronize(m->stream));
+        DSV4B_CUDA_OK(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+        const int rc = enqueue_step(m, m->stream);
+        cudaGraph_t g = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+        if (rc || e != cudaSuccess) return -1;
+        DSV4B_CUDA_OK(cudaGraphInstantiate(&m->exec, g, 0));
+        m->graph = g;
+        m->graphed = 1;
+    }
+    DSV4B_CUDA_OK(cudaStreamSynchronize(m->stream));
+    return 0;
+}
+
+extern "C" int dsv4b_model_step_async(dsv4b_model *m, void *stream)
+{
+    if (!m || !m->graphed) return -1;
+    DSV4B_CUDA_OK(cudaGraphLaunch(m->exec, stream ? (cudaStream_t)stream : m->stream));
+    return 0;
+}
+
+extern "C" int dsv4_cuda_model_step(dsv4b_model *m, int *token, float *logits)
+{
+    if (!m || !m->graphed) return -1;
+    StepState s;
+    DSV4B_CUDA_OK(cudaMemcpyAsync(&s, m->st, sizeof s, cudaMemcpyDeviceToHost, m->stream));
+    DSV4B_CUDA_OK(cudaStreamSynchronize(m->stream));
+    if (s.pos >= m->max_pos) return -1;
+    DSV4B_CUDA_OK(cudaGraphLaunch(m->exec, m->stream));
+    if (token) DSV4B_CUDA_OK(cudaMemcpyAsync(token, m->out_tokens + s.pos, 4, cudaMemcpyDeviceToHost, m->stream));
+    if (logits)
+        DSV4B_CUDA_OK(cudaMemcpyAsync(logits, m->logits, (size_t)m->c.vocab * 4, cudaMemcpyDeviceToHost, m->stream));
+    DSV4B_CUDA_OK(cudaStreamSynchronize(m->stream));
+    return 0;
+}
+
+extern "C" int dsv4_cuda_model_generate(dsv4b_model *m, const int *prompt, int n_prompt, int n_gen, int *out)
+{
+    if (dsv4_cuda_model_begin(m, prompt, n_prompt) != 0) return -1;
+    const int steps = n_prompt + n_gen;
+    if (steps > m->max_pos) return -1;
+    for (int i = 0; i < steps; i++) DSV4B_CUDA_OK(cudaGraphLaunch(m->exec, m->stream));
+    // position p emits the token after it; the generated ones start at n_prompt-1
+    DSV4B_CUDA_OK(cudaMemcpyAsync(out, m->out_tokens + n_prompt - 1, (size_t)(n_gen + 1) * 4,
+                                  cudaMemcpyDeviceToHost, m->stream));
+    DSV4B_CUDA_OK(cudaStreamSynchronize(m->stream));
+    return n_gen + 1;
+}

@@ -1,0 +1,346 @@
+// model_kernels.cu - the support ops of one decode token on the device.
+//
+// Every position-dependent quantity (the RoPE row, the KV ring slot, the
+// compressor phase, how many compressed rows exist, the window list) is read
+// from a device StepState rather than passed by the host, so a whole token is
+// a fixed sequence of launches that one CUDA graph can replay for every
+// position. Each kernel restates its reference function (cited) with the same
+// operation order; reductions over a vector are block-wide in double where the
+// reference sums in double.
+#include "common.cuh"
+#include "model.h"
+
+namespace dsv4b {
+
+__device__ __forceinline__ double block_sum_d(double v, double *red)
+{
+    v = warp_sum_d(v);
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    __syncthreads();
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    double t = 0.0;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < nw; i++) t += red[i];
+        red[32] = t;
+    }
+    __syncthreads();
+    return red[32];
+}
+
+// dsv4_embed_row (include/dsv4/dsv4.h:300-314), replicated hc times
+// (src/cli/dsv4_run.c:449-450).
+__global__ void k_embed(float *h, const void *table, int wdt, const StepState *st, int hidden, int hc)
+{
+    const long tok = st->token;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < hidden; i += gridDim.x * blockDim.x) {
+        float v;
+        if (wdt == DSV4B_WBF16)
+            v = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(table)[tok * hidden + i] << 16);
+        else
+            v = reinterpret_cast<const float *>(table)[tok * hidden + i];
+        for (int j = 0; j < hc; j++) h[(size_t)j * hidden + i] = v;
+    }
+}
+
+// mixes[m] = (float)(fn[m] . x) * rs, rs = (float)(1/sqrt(mean(x^2) + eps)),
+// both sums in double over the flattened hc*hidden vector
+// (src/core/dsv4_hc.c:118-129, src/cli/dsv4_run.c:97-107). grid = rows.
+__global__ void k_hc_mix(float *mixes, const float *fn, const float *x, int n, float eps)
+{
+    __shared__ double red[33];
+    const float *row = fn + (size_t)blockIdx.x * n;
+    double sq = 0.0, dot = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const double xv = (double)x[i];
+        sq = __fma_rn(xv, xv, sq);
+        dot = __fma_rn((double)row[i], xv, dot);
+    }
+    sq = block_sum_d(sq, red);
+    dot = block_sum_d(dot, red);
+    if (threadIdx.x == 0) {
+        const float rs = (float)(1.0 / sqrt(sq / (double)n + (double)eps));
+        mixes[blockIdx.x] = __fmul_rn((float)dot, rs);
+    }
+}
+
+__device__ __forceinline__ float sigm(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))); }
+
+// dsv4_hc_split_sinkhorn (src/core/dsv4_hc.c:50-102) then y = sum_j pre[j] x[j]
+// in double (:135-140). One block.
+__global__ void k_hc_finish(float *y, float *post, float *comb, const float *mixes, const float *x,
+                            const float *scale, const float *base, int hc, int hidden, int iters, float eps)
+{
+    __shared__ float pre[DSV4B_MAX_HC], cb[DSV4B_MAX_HC * DSV4B_MAX_HC];
+    if (threadIdx.x == 0) {
+        for (int j = 0; j < hc; j++) pre[j] = __fadd_rn(sigm(__fadd_rn(__fmul_rn(mixes[j], scale[0]), base[j])), eps);
+        for (int j = 0; j < hc; j++)
+            post[j] = __fmul_rn(2.0f, sigm(__fadd_rn(__fmul_rn(mixes[j + hc], scale[1]), base[j + hc])));
+        for (int j = 0; j < hc; j++)
+            for (int k = 0; k < hc; k++) {
+                const int o = j * hc + k + hc * 2;
+                cb[j * hc + k] = __fadd_rn(__fmul_rn(mixes[o], scale[2]), base[o]);
+            }
+        for (int j = 0; j < hc; j++) {
+            float *r = cb + j * hc;
+            float mx = r[0];
+            for (int k = 1; k < hc; k++) if (r[k] > mx) mx = r[k];
+            double sum = 0.0;
+            for (int k = 0; k < hc; k++) { r[k] = expf(r[k] - mx); sum += (double)r[k]; }
+            const float inv = (float)(1.0 / sum);
+            for (int k = 0; k < hc; k++) r[k] = __fadd_rn(__fmul_rn(r[k], inv), eps);
+        }
+        const int npass = iters > 1 ? iters : 1;
+        for (int pass = 0; pass < npass; pass++) {
+            if (pass > 0)
+                for (int j = 0; j < hc; j++) {
+                    double rs = 0.0;
+                    for (int k = 0; k < hc; k++) rs += (double)cb[j * hc + k];
+                    const float d = __fadd_rn((float)rs, eps);
+                    for (int k = 0; k < hc; k++) cb[j * hc + k] = __fdiv_rn(cb[j * hc + k], d);
+                }
+            for (int k = 0; k < hc; k++) {
+                double cs = 0.0;
+                for (int j = 0; j < hc; j++) cs += (double)cb[j * hc + k];
+                const float d = __fadd_rn((float)cs, eps);
+                for (int j = 0; j < hc; j++) cb[j * hc + k] = __fdiv_rn(cb[j * hc + k], d);
+            }
+        }
+        for (int i = 0; i < hc * hc; i++) comb[i] = cb[i];
+    }
+    __syncthreads();
+    for (int d = blockIdx.x * blockDim.x + threadIdx.x; d < hidden; d += gridDim.x * blockDim.x) {
+        double acc = 0.0;
+        for (int j = 0; j < hc; j++) acc = __dadd_rn(acc, __dmul_rn((double)pre[j], (double)x[(size_t)j * hidden + d]));
+        y[d] = (float)acc;
+    }
+}
+
+// The head's reduction: a sigmoid gate per copy, one scalar scale, no
+// Sinkhorn (src/cli/dsv4_run.c:94-116). One block.
+__global__ void k_hc_head_finish(float *y, const float *mixes, const float *x, const float *scale,
+                                 const float *base, int hc, int hidden, float eps)
+{
+    __shared__ float pre[DSV4B_MAX_HC];
+    if (threadIdx.x < hc) {
+        const int j = threadIdx.x;
+        pre[j] = __fadd_rn(sigm(__fadd_rn(__fmul_rn(mixes[j], scale[0]), base[j])), eps);
+    }
+    __syncthreads();
+    for (int d = threadIdx.x; d < hidden; d += blockDim.x) {
+        double acc = 0.0;
+        for (int j = 0; j < hc; j++) acc = __dadd_rn(acc, __dmul_rn((double)pre[j], (double)x[(size_t)j * hidden + d]));
+        y[d] = (float)acc;
+    }
+}
+
+// y[k][d] = post[k] x[d] + sum_j comb[j][k] res[j][d], in double
+// (src/core/dsv4_hc.c:149-162).
+__global__ void k_hc_post(float *y, const float *x, const float *res, const float *post, const float *comb,
+                          int hc, int hidden)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= hc * hidden) return;
+    const int k = i / hidden, d = i % hidden;
+    double acc = __dmul_rn((double)post[k], (double)x[d]);
+    for (int j = 0; j < hc; j++)
+        acc = __dadd_rn(acc, __dmul_rn((double)comb[j * hc + k], (double)res[(size_t)j * hidden + d]));
+    y[i] = (float)acc;
+}
+
+// RMSNorm (src/core/dsv4_ops.c:25-32): double sum of squares, eps on the mean,
+// y = w * (x * inv). One block; y may alias x.
+__global__ void k_rmsnorm(float *y, const float *x, const float *w, int n, float eps)
+{
+    __shared__ double red[33];
+    double s = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s = __fma_rn((double)x[i], (double)x[i], s);
+    s = block_sum_d(s, red);
+    const float inv = (float)(1.0 / sqrt(s / (double)n + (double)eps));
+    for (int i = threadIdx.x; i < n; i += blockDim.x) y[i] = __fmul_rn(w[i], __fmul_rn(x[i], inv));
+}
+
+// Interleaved-pair RoPE of the last rd dims of a width-wide vector at table
+// row `pos` (src/core/dsv4_rope.c:106-120); inverse negates the sine.
+__device__ __forceinline__ void rope_tail(float *v, int width, int rd, const float *cs, const float *sn,
+                                          int pos, int inverse)
+{
+    float *tail = v + (width - rd);
+    const int half = rd / 2;
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+        const float re = tail[2 * i], im = tail[2 * i + 1];
+        const float ci = cs[(size_t)pos * half + i];
+        const float si = inverse ? -sn[(size_t)pos * half + i] : sn[(size_t)pos * half + i];
+        tail[2 * i] = __fsub_rn(__fmul_rn(re, ci), __fmul_rn(im, si));
+        tail[2 * i + 1] = __fadd_rn(__fmul_rn(re, si), __fmul_rn(im, ci));
+    }
+}
+
+// grid = heads. Optional unweighted per-head RMS (the q path,
+// src/model/dsv4_layer.c:224-231), then RoPE at st->pos + pos_off.
+__global__ void k_heads_norm_rope(float *v, int width, int rd, const float *cs, const float *sn,
+                                  const StepState *st, int pos_off, int inverse, int do_norm, float eps)
+{
+    __shared__ double red[33];
+    float *h = v + (size_t)blockIdx.x * width;
+    if (do_norm) {
+        double s = 0.0;
+        for (int i = threadIdx.x; i < width; i += blockDim.x) s = __fma_rn((double)h[i], (double)h[i], s);
+        s = block_sum_d(s, red);
+        const float inv = (float)(1.0 / sqrt(s / (double)width + (double)eps));
+        for (int i = threadIdx.x; i < width; i += blockDim.x) h[i] = __fmul_rn(h[i], inv);
+        __syncthreads();
+    }
+    rope_tail(h, width, rd, cs, sn, st->pos + pos_off, inverse);
+}
+
+// kv = RoPE(RMSNorm(kv)), written into the sliding ring at pos % win
+// (src/model/dsv4_layer.c:234-238). One block.
+__global__ void k_kv_finish(float *kv, const float *w, int hd, int rd, const float *cs, const float *sn,
+                            const StepState *st, float eps, float *cache, int win)
+{
+    __shared__ double red[33];
+    double s = 0.0;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) s = __fma_rn((double)kv[i], (double)kv[i], s);
+    s = block_sum_d(s, red);
+    const float inv = (float)(1.0 / sqrt(s / (double)hd + (double)eps));
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) kv[i] = __fmul_rn(w[i], __fmul_rn(kv[i], inv));
+    __syncthreads();
+    rope_tail(kv, hd, rd, cs, sn, st->pos, 0);
+    __syncthreads();
+    float *dst = cache + (size_t)(st->pos % win) * hd;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) dst[i] = kv[i];
+}
+
+// One HCA compressor step (src/core/dsv4_compress.c:78-138) and, when a
+// window closes, RMSNorm + RoPE at pos+1-ratio and the cache write
+// (src/model/dsv4_layer.c:250-260). Also publishes this step's compressed-row
+// count and the indexer's take: dyn[0] = avail, dyn[1] = min(avail, topk).
+// One block; kv_state / score_state are [coff*ratio][coff*hd].
+__global__ void k_compress(float *cache, float *kv_state, float *score_state, const float *kv_in,
+                           const float *sc_in, const float *ape, const float *norm, int ratio, int hd, int rd,
+                           const float *cs, const float *sn, const StepState *st, float eps, int win,
+                           int index_topk, int *dyn)
+{
+    extern __shared__ float cbuf[];     // [hd]
+    __shared__ double red[33];
+    const int pos = st->pos, overlap = (ratio == 4), coff = 1 + overlap, width = coff * hd;
+    const int phase = pos % ratio, slot = overlap ? ratio + phase : phase;
+    const float *apr = ape + (size_t)phase * width;
+    for (int c = threadIdx.x; c < width; c += blockDim.x) {
+        kv_state[(size_t)slot * width + c] = kv_in[c];
+        score_state[(size_t)slot * width + c] = __fadd_rn(sc_in[c], apr[c]);
+    }
+    const int avail = (pos + 1) / ratio;
+    if (threadIdx.x == 0) {
+        dyn[0] = avail;
+        dyn[1] = avail < index_topk ? avail : index_topk;
+    }
+    __syncthreads();
+    if ((pos + 1) % ratio != 0) return;
+    const int ns = overlap ? 2 * ratio : ratio;
+    for (int c = threadIdx.x; c < hd; c += blockDim.x) {
+        // slot s of the pool: overlap mode takes the previous window's first
+        // half-width and the current window's second half-width
+        float mx = -INFINITY;
+        for (int s = 0; s < ns; s++) {
+            const size_t off = overlap ? ((s < ratio) ? (size_t)s * width + c : (size_t)s * width + hd + c)
+                                       : (size_t)s * width + c;
+            const float v = score_state[off];
+            if (v > mx) mx = v;
+        }
+        float out = 0.0f;
+        if (mx != -INFINITY) {
+            double den = 0.0, acc = 0.0;
+            for (int s = 0; s < ns; s++) {
+                const size_t off = overlap ? ((s < ratio) ? (size_t)s * width + c : (size_t)s * width + hd + c)
+                                           : (size_t)s * width + c;
+                const float v = score_state[off];
+                if (v == -INFINITY) continue;
+                const double e = (double)expf(v - mx);
+                den = __dadd_rn(den, e);
+                acc = __dadd_rn(acc, __dmul_rn(e, (double)kv_state[off]));
+            }
+            out = (float)(acc / den);
+        }
+        cbuf[c] = out;
+    }
+    __syncthreads();
+    if (overlap) {       // slide: the current window becomes the previous one
+        for (int i = threadIdx.x; i < ratio * width; i += blockDim.x) {
+            kv_state[i] = kv_state[(size_t)ratio * width + i];
+            score_state[i] = score_state[(size_t)ratio * width + i];
+        }
+    }
+    double s = 0.0;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) s = __fma_rn((double)cbuf[i], (double)cbuf[i], s);
+    s = block_sum_d(s, red);
+    const float inv = (float)(1.0 / sqrt(s / (double)hd + (double)eps));
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) cbuf[i] = __fmul_rn(norm[i], __fmul_rn(cbuf[i], inv));
+    __syncthreads();
+    rope_tail(cbuf, hd, rd, cs, sn, pos + 1 - ratio, 0);
+    __syncthreads();
+    float *dst = cache + (size_t)(win + avail - 1) * hd;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) dst[i] = cbuf[i];
+}
+
+// The attention index list (src/model/dsv4_layer.c:504-505 and :278-297):
+// the window's ring slots of the last min(pos+1, win) positions, newest
+// first, then the compressed selections (top-k order, or 0..avail-1 without
+// an indexer) offset by win, then -1 up to nmax.
+__global__ void k_build_idxs(int *idxs, int nmax, const StepState *st, int win, int has_comp, int has_idx,
+                             const int *dyn, const int *sel)
+{
+    const int pos = st->pos;
+    const int n = (pos + 1 < win) ? pos + 1 : win;
+    const int take = has_comp ? (has_idx ? dyn[1] : dyn[0]) : 0;
+    for (int i = threadIdx.x; i < nmax; i += blockDim.x) {
+        int v = -1;
+        if (i < n) v = (pos - i) % win;
+        else if (i < n + take) v = (has_idx ? sel[i - n] : i - n) + win;
+        idxs[i] = v;
+    }
+}
+
+// Argmax, first maximum (src/cli/dsv4_run.c:472-473), two stages; the second
+// also advances the step state: next token = the prompt's while prompt
+// remains, else the argmax; out_tokens[pos] = the argmax.
+__global__ void k_argmax_part(float *pv, int *pi, const float *x, int n)
+{
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    float bv = -INFINITY;
+    int bi = -1;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        if (bi < 0 || x[i] > bv) { bv = x[i]; bi = i; }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (blockDim.x >> 5); w++)
+            if (si[w] >= 0 && (bi < 0 || sv[w] > bv || (sv[w] == bv && si[w] < bi))) { bv = sv[w]; bi = si[w]; }
+        pv[blockIdx.x] = bv;
+        pi[blockIdx.x] = bi;
+    }
+}
+
+__global__ void k_argmax_final(StepState *st, int *out_tokens, const float *pv, const int *pi, int nparts,
+                               const int *prompt, int n_prompt)
+{
+    if (threadIdx.x != 0) return;
+    float bv = pv[0];
+    int bi = pi[0];
+    for (int i = 1; i < nparts; i++)
+        if (pi[i] >= 0 && (bi < 0 || pv[i] > bv || (pv[i] == bv && pi[i] < bi))) { bv = pv[i]; bi = pi[i]; }
+    const int pos = st->pos;
+    out_tokens[pos] = bi;
+    const int next = pos + 1;
+    st->token = (next < n_prompt) ? prompt[next] : bi;
+    st->pos = next;
+}
+
+}  // namespace dsv4b

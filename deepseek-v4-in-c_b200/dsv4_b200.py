@@ -74,6 +74,12 @@ def _declare(L):
         "dsv4b_topk": ([vp, vp, i, i, i, vp], i),
         "dsv4b_sparse_attn_scratch": ([i, i, i, i], sz),
         "dsv4b_sparse_attn": ([vp, vp, vp, i, C.c_long, vp, vp, i, i, i, f, i, vp, sz, vp], i),
+        "dsv4_cuda_model_create": ([vp, vp, vp, vp, i], vp),
+        "dsv4_cuda_model_begin": ([vp, vp, i], i),
+        "dsv4_cuda_model_step": ([vp, vp, vp], i),
+        "dsv4_cuda_model_generate": ([vp, vp, i, i, vp], i),
+        "dsv4_cuda_model_free": ([vp], None),
+        "dsv4b_model_step_async": ([vp, vp], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -302,3 +308,51 @@ def sparse_attn_dev(o, q, kv, kv_dt, seq_kv_rows, sink, idxs, n_heads, d, topk_n
     check(lib().dsv4b_sparse_attn(ptr(o), ptr(q), ptr(kv), kv_dt, seq_kv_rows, ptr(sink), ptr(idxs),
                                   n_heads, d, topk_n, scale, batch, ptr(scratch), nbytes,
                                   stream_ptr(stream)), "dsv4b_sparse_attn")
+
+
+# ------------------------------------------------------------- whole model
+
+class Model:
+    """A whole model resident on the device (dsv4_cuda_model_create) from a
+    dsv4_model.SyntheticModel or any holder of cfg/mw/layers/experts structs."""
+
+    def __init__(self, sm, max_pos):
+        self.sm, self.max_pos = sm, max_pos
+        self.vocab = sm.d["vocab"]
+        self.h = lib().dsv4_cuda_model_create(C.addressof(sm.cfg), C.addressof(sm.mw),
+                                              C.addressof(sm.layers), C.addressof(sm.experts), max_pos)
+        if not self.h:
+            raise RuntimeError("dsv4_cuda_model_create failed")
+
+    def begin(self, prompt):
+        p = np.ascontiguousarray(prompt, np.int32)
+        check(lib().dsv4_cuda_model_begin(self.h, p.ctypes.data, p.size), "dsv4_cuda_model_begin")
+
+    def step(self, want_logits=False):
+        tok = np.zeros(1, np.int32)
+        lg = np.empty(self.vocab, np.float32) if want_logits else None
+        check(lib().dsv4_cuda_model_step(self.h, tok.ctypes.data, None if lg is None else lg.ctypes.data),
+              "dsv4_cuda_model_step")
+        return int(tok[0]), lg
+
+    def generate(self, prompt, n_gen):
+        p = np.ascontiguousarray(prompt, np.int32)
+        out = np.empty(n_gen + 1, np.int32)
+        n = lib().dsv4_cuda_model_generate(self.h, p.ctypes.data, p.size, n_gen, out.ctypes.data)
+        if n < 0:
+            raise RuntimeError("dsv4_cuda_model_generate failed")
+        return out[:n]
+
+    def step_async(self, stream=None):
+        check(lib().dsv4b_model_step_async(self.h, stream_ptr(stream)), "dsv4b_model_step_async")
+
+    def close(self):
+        if self.h:
+            lib().dsv4_cuda_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

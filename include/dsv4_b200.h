@@ -133,6 +133,36 @@ int dsv4_cuda_sparse_attn(float *o, const float *q, const float *kv,
                           const float *sink, const int *idxs, int h, int d,
                           int topk, float scale);
 
+/* ---- whole-token decode, every weight resident: the token loop of
+ * src/cli/dsv4_run.c:444-483 around dsv4_layer_forward
+ * (src/model/dsv4_layer.c:487-523), on the device. ---- */
+typedef struct dsv4b_model dsv4b_model;
+
+/* Copy a whole model to HBM: the structs the reference's binder fills
+ * (dsv4_bind_layer / dsv4_bind_model), with the routed experts given as an
+ * array experts[layer * n_experts + e] instead of the streaming cache. Host
+ * memory is only read during the call. max_pos bounds the context (the
+ * reference CLI uses sliding_window + 4096). NULL on failure. */
+dsv4b_model *dsv4_cuda_model_create(const DSV4Cfg *c, const DSV4ModelW *mw,
+                                    const DSV4LayerW *layers,
+                                    const DSV4ExpertW *experts, int max_pos);
+
+/* Start a sequence: empty caches, load the prompt, position 0. The first call
+ * also captures one decode step into a CUDA graph. 0 or -1. */
+int dsv4_cuda_model_begin(dsv4b_model *m, const int *prompt, int n_prompt);
+
+/* Run the next position. *token receives the greedy argmax at it; logits
+ * (vocab floats, may be NULL) its logits. The next position's input is the
+ * prompt's token while prompt remains, else this argmax. 0 or -1. */
+int dsv4_cuda_model_step(dsv4b_model *m, int *token, float *logits);
+
+/* begin + n_prompt + n_gen steps; out receives the n_gen + 1 tokens emitted
+ * from the last prompt position on. Returns that count, or -1. */
+int dsv4_cuda_model_generate(dsv4b_model *m, const int *prompt, int n_prompt,
+                             int n_gen, int *out);
+
+void dsv4_cuda_model_free(dsv4b_model *m);
+
 /* ===================================================== 2. device API ====== */
 
 /* y[t*rows + o] = sum_c W[o][c] * x[t*cols + c] for t < nt; any nt >= 1.
@@ -167,6 +197,10 @@ int dsv4b_sparse_attn(float *o, const float *q, const void *kv, int kv_dt,
 
 /* The prepared MoE on device buffers x[hidden] -> out[hidden], stream-ordered. */
 int dsv4b_moe_forward(dsv4b_moe *m, float *out, const float *x, void *stream);
+
+/* Enqueue one decode step (the captured graph) on `stream` without waiting;
+ * dsv4_cuda_model_begin must have run. 0 or -1. */
+int dsv4b_model_step_async(dsv4b_model *m, void *stream);
 
 #ifdef __cplusplus
 }

@@ -524,3 +524,178 @@ extern "C" int dsv4_cuda_model_generate(dsv4b_model *m, const int *prompt, int n
     DSV4B_CUDA_OK(cudaStreamSynchronize(m->stream));
     return n_gen + 1;
 }
+
+// ------------------------------------------------------- synthetic models
+
+namespace dsv4b {
+
+struct Synth {
+    dsv4b_model *m;
+    uint64_t seed, tensor = 0;
+    bool ok = true;
+    void *fill(size_t bytes, size_t n, int kind, float a, float b)
+    {
+        if (!ok) return nullptr;
+        void *p = dalloc(m, bytes);
+        if (!p) { ok = false; return nullptr; }
+        fillat(p, n, kind, a, b);
+        return p;
+    }
+    void fillat(void *p, size_t n, int kind, float a, float b)
+    {
+        const uint64_t key = (seed * 0x9E3779B97F4A7C15ull) ^ (++tensor * 0xD1B54A32D192ED03ull);
+        k_synth<<<1184, 256, 0, m->stream>>>(p, n, kind, a, b, key);
+        if (cudaPeekAtLastError() != cudaSuccess) ok = false;
+    }
+    float *f32n(size_t n, float a, float b) { return (float *)fill(n * 4, n, 0, a, b); }
+    float *f32u(size_t n, float a, float b) { return (float *)fill(n * 4, n, 1, a, b); }
+    DevMat fp8(int rows, int cols)
+    {
+        DevMat d = {nullptr, nullptr, DSV4_WFP8, rows, cols, 128, 128};
+        const size_t sb = (size_t)((rows + 127) / 128) * ((cols + 127) / 128);
+        d.w = (const uint8_t *)fill((size_t)rows * cols, (size_t)rows * cols, 3, 0.f, 0.02f / 0.0009765625f);
+        d.s = (const uint8_t *)fill(sb, sb, 5, 117.f, 0.f);           // 2^-10
+        return d;
+    }
+    DevMat bf16(int rows, int cols, float sigma)
+    {
+        DevMat d = {nullptr, nullptr, DSV4_WBF16, rows, cols, 0, 0};
+        d.w = (const uint8_t *)fill((size_t)rows * cols * 2, (size_t)rows * cols, 2, 0.f, sigma);
+        return d;
+    }
+};
+
+static bool synth_layer(Synth &S, int Li)
+{
+    dsv4b_model *m = S.m;
+    const DSV4Cfg &c = m->c;
+    DevLayer &l = m->L[Li];
+    const int d = c.hidden, hd = c.head_dim, hc = c.hc_mult, mix = (2 + hc) * hc, H = c.n_heads;
+    l.has_comp = l.ratio != 0;
+    l.has_idx = l.ratio == 4;
+    l.attn_norm = S.f32n(d, 1.f, 0.1f);
+    l.ffn_norm = S.f32n(d, 1.f, 0.1f);
+    l.sink = S.f32n(H, 0.f, 1.f);
+    l.q_norm = S.f32n(c.q_lora, 1.f, 0.1f);
+    l.kv_norm = S.f32n(hd, 1.f, 0.1f);
+    l.wq_a = S.fp8(c.q_lora, d);
+    l.wq_b = S.fp8(H * hd, c.q_lora);
+    l.wkv = S.fp8(hd, d);
+    l.wo_a = S.fp8(c.o_groups * c.o_lora, H * hd / c.o_groups);
+    l.wo_b = S.fp8(d, c.o_groups * c.o_lora);
+    if (l.has_comp) {
+        l.ape = S.f32n((size_t)l.ratio * l.coff * hd, 0.f, 0.1f);
+        l.cnorm = S.f32n(hd, 1.f, 0.1f);
+        l.cwkv = S.bf16(l.coff * hd, d, 0.02f);
+        l.cwgate = S.bf16(l.coff * hd, d, 0.02f);
+    }
+    if (l.has_idx) {
+        l.iwq_b = S.fp8(c.index_n_heads * c.index_head_dim, c.q_lora);
+        l.iwproj = S.bf16(c.index_n_heads, d, 0.02f);
+    }
+    l.hca_fn = S.f32n((size_t)mix * hc * d, 0.f, 0.02f);
+    l.hca_base = S.f32n(mix, 0.f, 0.5f);
+    l.hca_scale = S.f32u(3, 0.5f, 0.5f);
+    l.hcf_fn = S.f32n((size_t)mix * hc * d, 0.f, 0.02f);
+    l.hcf_base = S.f32n(mix, 0.f, 0.5f);
+    l.hcf_scale = S.f32u(3, 0.5f, 0.5f);
+    MoeLayer &mo = l.moe;
+    mo.gate = S.bf16(c.n_experts, d, 0.02f);
+    mo.fixed = nullptr;
+    if (Li < c.num_hash_layers) {
+        int64_t *t = (int64_t *)dalloc(m, (size_t)c.vocab * c.topk * 8);
+        if (!t) return false;
+        k_synth_tid2eid<<<256, 256, 0, m->stream>>>(t, c.vocab, c.topk, c.n_experts, S.seed + 77 * Li);
+        mo.tid2eid = t;
+        mo.bias = nullptr;
+    } else {
+        mo.tid2eid = nullptr;
+        mo.bias = S.f32n(c.n_experts, 0.f, 0.05f);
+    }
+    // routed experts: one block per layer, codes of every expert then scales
+    const size_t I = c.moe_inter, E = c.n_experts;
+    const size_t cw = I * d / 2, cper = 3 * cw, sw = I * d / 32, sper = 3 * sw;
+    uint8_t *codes = (uint8_t *)dalloc(m, E * cper), *scales = (uint8_t *)dalloc(m, E * sper);
+    if (!codes || !scales) return false;
+    S.fillat(codes, E * cper, 4, 0.f, 0.02f / 0.015625f);       // e2m1 of N(0,0.02) / 2^-6
+    S.fillat(scales, E * sper, 5, 121.f, 0.f);                  // 2^-6
+    std::vector<const uint8_t *> tab(6 * E);
+    for (size_t e = 0; e < E; e++) {
+        for (int j = 0; j < 3; j++) {
+            tab[(2 * j) * E + e] = codes + e * cper + j * cw;
+            tab[(2 * j + 1) * E + e] = scales + e * sper + j * sw;
+        }
+    }
+    bool ok = true;
+    const uint8_t *const *t = (const uint8_t *const *)dcopy(m, tab.data(), tab.size() * sizeof(void *), &ok);
+    if (!ok) return false;
+    mo.w1tab = t; mo.s1tab = t + E;
+    mo.w3tab = t + 2 * E; mo.s3tab = t + 3 * E;
+    mo.w2tab = t + 4 * E; mo.s2tab = t + 5 * E;
+    mo.efmt = DSV4_WFP4; mo.eblk_r = 1; mo.eblk_c = 32;
+    const int Is = c.moe_inter * c.n_shared;
+    mo.sh[0] = S.fp8(Is, d);
+    mo.sh[1] = S.fp8(Is, d);
+    mo.sh[2] = S.fp8(d, Is);
+    mo.has_shared = 1;
+    mo.n_experts = c.n_experts;
+    mo.topk = c.topk;
+    mo.hidden = d;
+    mo.inter = c.moe_inter;
+    mo.inter_shared = Is;
+    mo.score_func = c.scoring_func == DSV4_SCORE_SIGMOID ? 2 : 1;
+    mo.route_scale = c.routed_scale;
+    mo.swiglu_limit = c.swiglu_limit;
+    return S.ok;
+}
+
+}  // namespace dsv4b
+
+extern "C" dsv4b_model *dsv4_cuda_model_create_synthetic(const DSV4Cfg *c, int max_pos, unsigned long long seed)
+{
+    dsv4b_model *m = model_new(c, max_pos);
+    if (!m) return nullptr;
+    dsv4b::Synth S;
+    S.m = m;
+    S.seed = seed;
+    bool ok = true;
+    for (int L = 0; L < c->n_layers && ok; L++) ok = dsv4b::synth_layer(S, L);
+    const int d = c->hidden, hc = c->hc_mult;
+    if (ok) {
+        m->emb_wdt = DSV4_WBF16;
+        m->embed = S.bf16(c->vocab, d, 1.0f).w;
+        m->head = S.bf16(c->vocab, d, 0.02f);
+        m->norm = S.f32n(d, 1.f, 0.1f);
+        m->hch_fn = S.f32n((size_t)hc * hc * d, 0.f, 0.02f);
+        m->hch_base = S.f32n(hc, 0.f, 0.5f);
+        m->hch_scale = S.f32u(1, 0.5f, 0.5f);
+        ok = S.ok;
+    }
+    if (!ok || cudaStreamSynchronize(m->stream) != cudaSuccess) {
+        fprintf(stderr, "dsv4_b200: synthetic model did not fit or failed (%s)\n",
+                cudaGetErrorString(cudaGetLastError()));
+        dsv4_cuda_model_free(m);
+        return nullptr;
+    }
+    return m;
+}
+
+extern "C" int dsv4_cuda_model_decode(dsv4b_model *m, int token, int pos, int *next_token)
+{
+    if (!m || !m->graphed || pos < 0 || pos >= m->max_pos || token < 0 || token >= m->c.vocab) return -1;
+    const dsv4b::StepState s = { token, pos };
+    DSV4B_CUDA_OK(cudaMemcpyAsync(m->st, &s, sizeof s, cudaMemcpyHostToDevice, m->stream));
+    DSV4B_CUDA_OK(cudaGraphLaunch(m->exec, m->stream));
+    DSV4B_CUDA_OK(cudaMemcpyAsync(next_token, m->out_tokens + pos, 4, cudaMemcpyDeviceToHost, m->stream));
+    DSV4B_CUDA_OK(cudaStreamSynchronize(m->stream));
+    return 0;
+}
+
+extern "C" size_t dsv4_cuda_model_bytes(const dsv4b_model *m)
+{
+    size_t b = 0;
+    (void)m;
+    size_t fr = 0, tot = 0;
+    if (cudaMemGetInfo(&fr, &tot) == cudaSuccess) b = tot - fr;
+    return b;
+}

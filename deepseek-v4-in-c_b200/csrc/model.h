@@ -41,4 +41,7 @@ __global__ void k_argmax_part(float *pv, int *pi, const float *x, int n);
 __global__ void k_argmax_final(StepState *st, int *out_tokens, const float *pv, const int *pi, int nparts,
                                const int *prompt, int n_prompt);
 
+__global__ void k_synth(void *dst, size_t n, int kind, float a, float b, uint64_t key);
+__global__ void k_synth_tid2eid(int64_t *t, int vocab, int topk, int n_experts, uint64_t key);
+
 }  // namespace dsv4b

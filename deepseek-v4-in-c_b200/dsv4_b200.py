@@ -80,6 +80,9 @@ def _declare(L):
         "dsv4_cuda_model_generate": ([vp, vp, i, i, vp], i),
         "dsv4_cuda_model_free": ([vp], None),
         "dsv4b_model_step_async": ([vp, vp], i),
+        "dsv4_cuda_model_decode": ([vp, i, i, vp], i),
+        "dsv4_cuda_model_create_synthetic": ([vp, i, C.c_ulonglong], vp),
+        "dsv4_cuda_model_bytes": ([vp], sz),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -316,13 +319,27 @@ class Model:
     """A whole model resident on the device (dsv4_cuda_model_create) from a
     dsv4_model.SyntheticModel or any holder of cfg/mw/layers/experts structs."""
 
-    def __init__(self, sm, max_pos):
+    def __init__(self, sm, max_pos, synthetic_seed=None):
+        """sm: a dsv4_model.SyntheticModel (host weights), or with
+        synthetic_seed set, any holder of .cfg/.d for an on-device model."""
         self.sm, self.max_pos = sm, max_pos
         self.vocab = sm.d["vocab"]
-        self.h = lib().dsv4_cuda_model_create(C.addressof(sm.cfg), C.addressof(sm.mw),
-                                              C.addressof(sm.layers), C.addressof(sm.experts), max_pos)
+        if synthetic_seed is None:
+            self.h = lib().dsv4_cuda_model_create(C.addressof(sm.cfg), C.addressof(sm.mw),
+                                                  C.addressof(sm.layers), C.addressof(sm.experts), max_pos)
+        else:
+            self.h = lib().dsv4_cuda_model_create_synthetic(C.addressof(sm.cfg), max_pos, synthetic_seed)
         if not self.h:
-            raise RuntimeError("dsv4_cuda_model_create failed")
+            raise RuntimeError("model creation failed")
+
+    def decode(self, token, pos):
+        nxt = np.zeros(1, np.int32)
+        check(lib().dsv4_cuda_model_decode(self.h, int(token), int(pos), nxt.ctypes.data),
+              "dsv4_cuda_model_decode")
+        return int(nxt[0])
+
+    def device_bytes(self):
+        return lib().dsv4_cuda_model_bytes(self.h)
 
     def begin(self, prompt):
         p = np.ascontiguousarray(prompt, np.int32)

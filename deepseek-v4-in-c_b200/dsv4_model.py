@@ -233,3 +233,21 @@ class SyntheticModel:
         cw.wkv = self.bf16(coff * hd, hid, sigma)
         cw.wgate = self.bf16(coff * hd, hid, sigma)
         return cw
+
+
+class ConfigOnly:
+    """Just the config struct of a model, for on-device synthetic models."""
+
+    def __init__(self, d):
+        self.d = d
+        self.cfg, self._ratios = make_cfg(d)
+
+
+def flash_slice(n_layers=2, n_experts=16, ratios=(4, 128)):
+    """Flash geometry (hidden 4096, 64 heads of 512, indexer 64x128, experts
+    2048 wide) cut to a few layers and experts: the shapes of config 5 at a
+    size the CPU oracle can still run."""
+    d = flash_config()
+    d.update(n_layers=n_layers, n_experts=n_experts, compress_ratios=list(ratios) + [0],
+             num_hash_layers=1, max_pos=4096)
+    return d

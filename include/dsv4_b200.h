@@ -161,6 +161,22 @@ int dsv4_cuda_model_step(dsv4b_model *m, int *token, float *logits);
 int dsv4_cuda_model_generate(dsv4b_model *m, const int *prompt, int n_prompt,
                              int n_gen, int *out);
 
+/* One position driven by the host, the reference CLI's loop body
+ * (dsv4_run.c:445-474): token at pos in, the greedy next token out.
+ * Positions must follow each other from the last begin. 0 or -1. */
+int dsv4_cuda_model_decode(dsv4b_model *m, int token, int pos, int *next_token);
+
+/* A random-init model of configuration c generated directly in HBM (no host
+ * weights): FP8 128x128 trunk from N(0, 0.02) (scales 2^-10), FP4 1x32
+ * experts from N(0, 0.02) (scales 2^-6), BF16 router / compressor / indexer /
+ * head N(0, 0.02), BF16 embedding N(0, 1), deterministic in seed. NULL if
+ * it does not fit. */
+dsv4b_model *dsv4_cuda_model_create_synthetic(const DSV4Cfg *c, int max_pos,
+                                              unsigned long long seed);
+
+/* Device memory in use (bytes), for reporting the resident model size. */
+size_t dsv4_cuda_model_bytes(const dsv4b_model *m);
+
 void dsv4_cuda_model_free(dsv4b_model *m);
 
 /* ===================================================== 2. device API ====== */

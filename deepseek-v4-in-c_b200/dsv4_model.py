@@ -129,8 +129,12 @@ class SyntheticModel:
     n_experts, row = layer) are ready for dsv4_cuda_model_create, the oracle's
     dsv4o_model_create and the reference driver."""
 
-    def __init__(self, d, seed=0, sigma=0.02):
+    def __init__(self, d, seed=0, sigma=0.02, fast=False):
+        """fast=True draws FP8 / FP4 codes uniformly with fixed block scales
+        instead of quantising normals: same shapes and formats, for timing
+        runs where the values do not matter."""
         self.d = d
+        self.fast = fast
         self.rng = np.random.default_rng(seed)
         self.keep = []
         self.cfg, self._ratios = make_cfg(d)
@@ -207,12 +211,20 @@ class SyntheticModel:
         return h
 
     def fp8(self, rows, cols, sigma):
-        W, S = Q.quant_fp8(self.rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(sigma), 128)
+        if self.fast:
+            W = np.frombuffer(self.rng.bytes(rows * cols), np.uint8).reshape(rows, cols) & np.uint8(0xF7)
+            S = np.full((-(-rows // 128), -(-cols // 128)), 117, np.uint8)
+        else:
+            W, S = Q.quant_fp8(self.rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(sigma), 128)
         self.keep += [W, S]
         return QMat(W.ctypes.data, S.ctypes.data, WFP8, rows, cols, 128, 128)
 
     def fp4(self, rows, cols, sigma):
-        W, S = Q.quant_fp4(self.rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(sigma))
+        if self.fast:
+            W = np.frombuffer(self.rng.bytes(rows * cols // 2), np.uint8).reshape(rows, cols // 2)
+            S = np.full((rows, cols // 32), 121, np.uint8)
+        else:
+            W, S = Q.quant_fp4(self.rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(sigma))
         self.keep += [W, S]
         return QMat(W.ctypes.data, S.ctypes.data, WFP4, rows, cols, 1, 32)
 

@@ -211,6 +211,21 @@ int dsv4b_sparse_attn(float *o, const float *q, const void *kv, int kv_dt,
                       int n_heads, int d, int topk, float scale, int batch,
                       void *scratch, size_t scratch_bytes, void *stream);
 
+/* dsv4b_sparse_attn with its scratch in a fixed 8 MiB device array instead
+ * of caller memory: no call allocates. No reference counterpart (the
+ * reference's attention runs on the host); it is for callers with no device
+ * allocator of their own or no HBM left to give. The first call on a device
+ * sets up (looks up the array's address) and should come before any stream
+ * capture; calls in flight at the same time on one device race on the one
+ * array. Returns 0, -1 on a bad argument or CUDA error, -2 when
+ * dsv4b_sparse_attn_scratch(n_heads, d, topk, batch) exceeds
+ * DSV4B_SPARSE_ATTN_STATIC_SCRATCH. */
+#define DSV4B_SPARSE_ATTN_STATIC_SCRATCH ((size_t)8 << 20)
+int dsv4b_sparse_attn_static(float *o, const float *q, const void *kv, int kv_dt,
+                             long seq_kv_rows, const float *sink, const int *idxs,
+                             int n_heads, int d, int topk, float scale, int batch,
+                             void *stream);
+
 /* The prepared MoE on device buffers x[hidden] -> out[hidden], stream-ordered. */
 int dsv4b_moe_forward(dsv4b_moe *m, float *out, const float *x, void *stream);
 

@@ -1,21 +1,32 @@
 """Benchmark of the B200 decode backend (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload gemv_fp8]
+                    [--workload decode|gemv_fp8] [--context 512] [--no-cpu]
 
-Workload `gemv_fp8` (BASELINE config 1): y = W x with W 4096x7168 e4m3 in
-128x128 E8M0 blocks, x f32, batch 1. One step is one GEMV over a different
-resident weight copy (8 copies, 235 MB, rotate so no step finds its weights in
-the 126 MB L2). `value` is algorithmic HBM GB/s with inputs resident, timed
-with CUDA events on the launching stream; `e2e` is the same metric through the
-reference-facing C ABI (dsv4_cuda_mmq: host x in, host y out, copies inside
-the timed region). Under torchrun every rank runs its own replica (the GEMV
-does not shard at batch 1 without an exchange; weak scaling) and the slowest
+Workload `decode` (default): batch-1 greedy decode of the
+Flash-scale model -- 43 layers, hidden 4096, 256 FP4 routed experts (inter
+2048, top-6) + 1 shared FP8 expert per layer, MLA with the lightning indexer,
+vocab 129280 -- with random-init weights generated directly in HBM (≈157 GB,
+every weight resident). A 512-token random prompt is run first (untimed,
+token by token through the same captured step), then W untimed and K timed
+decode steps. One step = one token = one replay of the captured CUDA graph;
+steps are timed with CUDA events on the model's stream. Every step streams
+≈11.1 GB of distinct weights, far more than the 126 MB L2, so no flush is
+needed between steps. `value` is tokens/s over all ranks; `e2e` times the
+reference-facing call dsv4_cuda_model_decode (host token and position in,
+host next token out) with the host wall clock. Under torchrun each GPU holds
+its own full replica and decodes its own stream (weak scaling); the slowest
 rank's time is reported.
 
---impl reference times the reference's own CPU kernel (dsv4_matmul_fp8 from
-oracle/_ref, or the oracle restatement where that was not built) on the host
-cores, on the same config.
+Workload `gemv_fp8` (BASELINE config 1): y = W x with W 4096x7168 e4m3 in
+128x128 E8M0 blocks, one GEMV per step over 8 rotating resident copies (235 MB
+> L2), graph-launched; value in algorithmic HBM GB/s.
+
+--impl reference times the reference's own CPU code (oracle/_ref, built from
+its sources) on the host cores on the same workload: for `decode`, its
+dsv4_layer_forward on a 3-layer Flash-geometry sample (one layer of each
+compress ratio 0 / 4 / 128, all 256 experts, the full-vocab head), scaled to
+the 43-layer mix; for `gemv_fp8`, dsv4_matmul_fp8.
 """
 import argparse
 import json
@@ -35,6 +46,14 @@ C1_ROWS, C1_COLS = 4096, 7168
 # algorithmic bytes of one config-1 GEMV: W + S + x + y
 C1_BYTES = C1_ROWS * C1_COLS + 32 * 56 + C1_COLS * 4 + C1_ROWS * 4
 NCOPY = 8
+
+DECODE_METRIC = "batch-1 decode tok/s (Flash-scale synthetic, config 5)"
+GEMV_METRIC = "FP8 block-scaled GEMV HBM GB/s (config 1, 4096x7168 e4m3, batch 1)"
+
+# DRAM bytes (read + write) per unit from ncu, or None while no capture of
+# that kernel and workload has been summarised under profiles/.
+TRAFFIC_C1 = None
+TRAFFIC_DECODE = None
 
 
 def peaks():
@@ -99,10 +118,203 @@ def dist_setup(n):
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
     os.environ["DSV4_DEVICE"] = str(local)
-    dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                             device_id=torch.device("cuda", local))
     return rank, world, dist
 
+
+def max_over_ranks(dist, ms):
+    if not dist:
+        return ms
+    import torch
+    t = torch.tensor([ms], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------ decode model
+
+def flash_cfg():
+    import dsv4_model as M
+    return M.flash_config()
+
+
+def layer_ratios(d):
+    return list(d["compress_ratios"][:d["n_layers"]])
+
+
+def fp8_bytes(rows, cols):
+    return rows * cols + -(-rows // 128) * -(-cols // 128)
+
+
+def fp4_bytes(rows, cols):
+    return rows * cols // 2 + rows * cols // 32
+
+
+def decode_bytes_per_token(d, pos):
+    """Algorithmic HBM bytes of one batch-1 decode token at position pos: every
+    weight the token reads once (trunk, router, the top-k routed and the
+    shared experts, compressor / indexer weights, mHC, norms, LM head, the
+    embedding row) plus the cached KV / key rows it attends over. Activations
+    (< 1 MB) are left out."""
+    hid, H, hd, ql = d["hidden"], d["n_heads"], d["head_dim"], d["q_lora"]
+    og, ol, I, E, K = d["o_groups"], d["o_lora"], d["moe_inter"], d["n_experts"], d["topk"]
+    hc, win = d["hc_mult"], d["sliding_window"]
+    ih, idim, itop = d["index_n_heads"], d["index_head_dim"], d["index_topk"]
+    mix = (2 + hc) * hc
+    total = 0
+    for r in layer_ratios(d):
+        b = fp8_bytes(ql, hid) + fp8_bytes(H * hd, ql) + fp8_bytes(hd, hid)
+        b += fp8_bytes(og * ol, H * hd // og) + fp8_bytes(hid, og * ol)
+        b += 2 * mix * hc * hid * 4 + 2 * mix * 4 + 2 * 3 * 4          # mHC fn, base, scale
+        b += (2 * hid + ql + hd + H) * 4                                # norms, sinks
+        n_win = min(pos + 1, win)
+        n_sel = 0
+        if r:
+            coff = 2 if r == 4 else 1
+            b += 2 * (coff * hd * hid * 2) + coff * hd * 4 + hd * 4     # wkv / wgate bf16, ape row, norm
+            n_comp = (pos + 1) // r
+            n_sel = n_comp
+            if r == 4:
+                b += fp8_bytes(ih * idim, ql) + ih * hid * 2            # indexer wq_b, weights_proj
+                b += n_comp * idim * 4                                  # indexer keys
+                n_sel = min(n_comp, itop)
+        b += (n_win + n_sel) * hd * 4                                   # attended KV rows (f32)
+        b += E * hid * 2 + E * 4                                        # router bf16, bias
+        b += K * (2 * fp4_bytes(I, hid) + fp4_bytes(hid, I))           # routed experts
+        b += 2 * fp8_bytes(I, hid) + fp8_bytes(hid, I)                 # shared expert
+        total += b
+    total += hc * hc * hid * 4 + hid * 4 + d["vocab"] * hid * 2 + hid * 2  # hc_head, norm, head, embed row
+    return total
+
+
+def cpu_decode_sample(n_pos, warm=2):
+    """The reference's dsv4_layer_forward on a 3-layer Flash-geometry model
+    (compress ratios 0 / 4 / 128, all 256 experts, vocab 129280) for n_pos
+    positions from a one-token prompt. Returns (seconds per 43-layer token,
+    per-position times, description)."""
+    import oracle as O
+    import dsv4_model as M
+    d = M.flash_config()
+    full = layer_ratios(d)
+    count = {r: full.count(r) for r in set(full)}
+    d.update(n_layers=3, compress_ratios=[0, 4, 128, 0], num_hash_layers=1, max_pos=4096)
+    t0 = time.perf_counter()
+    sm = M.SyntheticModel(d, seed=0, fast=True)
+    t_build = time.perf_counter() - t0
+    tl, th, _ = O.model_decode_timed_ref(sm, n_pos + warm)
+    tl, th = tl[warm:], th[warm:]
+    per = tl[:, 0] * count[0] + tl[:, 1] * count[4] + tl[:, 2] * count[128] + th
+    desc = ("reference dsv4_layer_forward + hc_head/norm/LM head/argmax (oracle/_ref) on a 3-layer "
+            "Flash-geometry sample (ratios 0/4/128, 256 experts, vocab 129280), %d positions after %d "
+            "warm-up from position 0, per-layer times scaled to the 43-layer mix (%d/%d/%d); "
+            "OMP_NUM_THREADS=%s; sample build %.0f s"
+            % (n_pos, warm, count[0], count[4], count[128],
+               os.environ.get("OMP_NUM_THREADS", "all %d" % os.cpu_count()), t_build))
+    return float(np.sum(per) / n_pos), per, desc
+
+
+def run_decode(a):
+    import torch
+    import dsv4_b200 as B
+    import dsv4_model as M
+    rank, world, dist = dist_setup(a.gpus)
+    L = B.init()
+    d = M.flash_config()
+    W, K, P = max(a.warmup, 3), a.steps, a.context
+    n_e2e = max(16, min(K, 128))
+    max_pos = P + W + K + n_e2e + 8
+    cfg = M.ConfigOnly(d)
+    t0 = time.perf_counter()
+    model = B.Model(cfg, max_pos, synthetic_seed=1234 + rank)
+    t_create = time.perf_counter() - t0
+    resident = model.device_bytes()
+    prompt = np.random.default_rng(rank).integers(0, d["vocab"], P).astype(np.int32)
+    model.begin(prompt)
+    launches_per_step = L.dsv4_cuda_model_step_kernels(model.h)
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+
+    def replay(n):
+        for _ in range(n):
+            B.check(L.dsv4b_model_step_async(model.h, sp), "dsv4b_model_step_async")
+
+    replay(P)                  # the prompt, token by token (untimed)
+    replay(W)                  # warm-up decode steps
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(torch.cuda.current_device()) as clk:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        replay(K)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = max_over_ranks(dist, e0.elapsed_time(e1))
+    if dist:
+        dist.barrier()
+    ms_step = ms / K
+    value = world * K / (ms * 1e-3)
+
+    # e2e through the host-driven entry (host token/pos in, host token out)
+    tok = np.zeros(1, np.int32)
+    B.check(L.dsv4_cuda_model_step(model.h, tok.ctypes.data, None), "dsv4_cuda_model_step")
+    pos = P + W + K + 1
+    t = int(tok[0])
+    for _ in range(3):
+        t = model.decode(t, pos)
+        pos += 1
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        t = model.decode(t, pos)
+        pos += 1
+    e2e_s = (time.perf_counter() - t0) / n_e2e
+    e2e_s = max_over_ranks(dist, e2e_s)
+
+    peak, src = peaks()
+    bytes_tok = np.mean([decode_bytes_per_token(d, P + W + i) for i in range(0, K, max(1, K // 16))])
+    ach = bytes_tok / (ms_step * 1e-3) / 1e9
+    out = {
+        "metric": DECODE_METRIC,
+        "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp8 e4m3 / fp4 e2m1 / bf16 weights, f32 activations, f64 row sums",
+        "data": "synthetic (random-init weights generated on device, random 512-token prompt)",
+        "config": {"workload": "decode config 5 (Flash-scale synthetic)", "batch": 1,
+                   "context": "%d-token prompt, decode positions %d..%d" % (P, P + W, P + W + K - 1),
+                   "layers": d["n_layers"], "hidden": d["hidden"], "experts": d["n_experts"],
+                   "topk": d["topk"], "vocab": d["vocab"],
+                   "resident_gb": round(resident / 1e9, 1), "create_s": round(t_create, 1),
+                   "l2": "no flush: each step streams %.1f GB of distinct weights (> 126 MB L2)"
+                         % (bytes_tok / 1e9),
+                   "parallelism": ("replica per GPU, one stream each" if world > 1 else "single GPU")},
+        "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
+                     "frac": ach / peak, "peak_source": src + " burst hbm_gbs",
+                     "scope": "whole decode token (one graph replay, %d kernels)" % launches_per_step,
+                     "bytes_per_unit": bytes_tok, "traffic": TRAFFIC_DECODE},
+        "gpu_launches": launches_per_step * K,
+        "clocks": clk.summary(),
+        "e2e": {"value": world / e2e_s, "unit": "tok/s", "ms_per_step": e2e_s * 1e3,
+                "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
+                "api": "dsv4_cuda_model_decode (host token, pos -> host next token), wall clock"},
+    }
+    if rank == 0 and world == 1 and not a.no_cpu:
+        s_tok, _, desc = cpu_decode_sample(8)
+        out["cpu_baseline"] = {"value": 1.0 / s_tok, "unit": "tok/s",
+                               "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count())),
+                               "kind": "reference", "sample": desc}
+    if rank == 0:
+        print(json.dumps(out))
+    model.close()
+    L.dsv4_cuda_shutdown()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# -------------------------------------------------------------- GEMV (C1)
 
 def cpu_reference_gemv(seconds, threads=None):
     """The reference's CPU dsv4_matmul_fp8 on config 1, cycling weight copies
@@ -126,30 +338,7 @@ def cpu_reference_gemv(seconds, threads=None):
                       "OMP_NUM_THREADS=%s" % (n, len(copies), os.environ.get("OMP_NUM_THREADS", cores))}
 
 
-def run_reference(a):
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
-    secs = max(2.0, 20.0 / max(a.steps, 1))
-    vals = []
-    for _ in range(a.warmup):
-        cpu_reference_gemv(0.5)
-    base = None
-    for _ in range(a.steps):
-        base = cpu_reference_gemv(secs)
-        vals.append(base["value"])
-    v = float(np.median(vals))
-    base["value"] = v
-    print(json.dumps({
-        "metric": "FP8 block-scaled GEMV HBM GB/s (config 1, 4096x7168 e4m3, batch 1)",
-        "value": v, "unit": "GB/s", "impl": "reference", "n_gpus": a.gpus, "steps": a.steps,
-        "warmup": a.warmup, "higher_is_better": True, "dtype": "e4m3 weights, f32 x, f64 accumulation",
-        "data": "synthetic", "config": {"workload": "gemv_fp8 config 1", "rows": C1_ROWS, "cols": C1_COLS},
-        "cpu_baseline": base,
-        "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
-
-
-def run_ours(a):
+def run_gemv(a):
     import torch
     import dsv4_b200 as B
     import dsv4_quant as Q
@@ -204,31 +393,26 @@ def run_ours(a):
                     gr.replay()
             e1.record(stream)
         torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(dist, e0.elapsed_time(e1))
     ms_step = ms / a.steps
     value = world * C1_BYTES / (ms_step * 1e-3) / 1e9
 
     # e2e: the reference-facing call, host buffers, copies inside the region
     for i in range(3):
         mats[i % NCOPY].mmq(x)
-    ke = max(50, a.steps // 4)
+    ke = max(50, min(a.steps // 4, 2000))
     t0 = time.perf_counter()
     for i in range(ke):
-        y = mats[i % NCOPY].mmq(x)
-    e2e_s = (time.perf_counter() - t0) / ke
-    e2e = {"value": C1_BYTES / e2e_s / 1e9, "unit": "GB/s", "ms_per_step": e2e_s * 1e3,
+        mats[i % NCOPY].mmq(x)
+    e2e_s = max_over_ranks(dist, (time.perf_counter() - t0) / ke)
+    e2e = {"value": world * C1_BYTES / e2e_s / 1e9, "unit": "GB/s", "ms_per_step": e2e_s * 1e3,
            "h2d_bytes_per_step": C1_COLS * 4, "d2h_bytes_per_step": C1_ROWS * 4,
            "api": "dsv4_cuda_mmq (host x -> host y), wall clock"}
-    del y
 
     peak, src = peaks()
     ach = C1_BYTES / (ms_step * 1e-3) / 1e9
     out = {
-        "metric": "FP8 block-scaled GEMV HBM GB/s (config 1, 4096x7168 e4m3, batch 1)",
+        "metric": GEMV_METRIC,
         "value": value, "unit": "GB/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "e4m3 weights, f32 x, f64 accumulation", "data": "synthetic",
@@ -237,6 +421,7 @@ def run_ours(a):
                    "parallelism": "replica per GPU" if world > 1 else "single GPU"},
         "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
                      "frac": ach / peak, "peak_source": src + " burst hbm_gbs",
+                     "scope": "k_gemv_reg, one launch per step", "bytes_per_unit": C1_BYTES,
                      "traffic": TRAFFIC_C1},
         "gpu_launches": a.steps,
         "clocks": clk.summary(),
@@ -252,24 +437,65 @@ def run_ours(a):
         dist.destroy_process_group()
 
 
-# dram bytes (read + write) of one k_gemv launch at config 1 from ncu, or None
-# while no capture has been summarised (profiles/gemv_fp8_c1.md).
-TRAFFIC_C1 = None
+# ------------------------------------------------------- reference arm
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    if a.workload == "decode":
+        n = max(4, min(a.steps, 32))                 # bounded sample: minutes, not hours
+        s_tok, per, desc = cpu_decode_sample(n, warm=max(1, min(a.warmup, 4)))
+        v = 1.0 / s_tok
+        print(json.dumps({
+            "metric": DECODE_METRIC, "value": v, "unit": "tok/s", "impl": "reference",
+            "n_gpus": a.gpus, "steps": n, "warmup": a.warmup, "ms_per_step": s_tok * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp8 e4m3 / fp4 e2m1 / bf16 weights, f32 activations, f64 row sums",
+            "data": "synthetic", "config": {"workload": "decode config 5 (Flash-scale synthetic)", "batch": 1},
+            "cpu_baseline": {"value": v, "unit": "tok/s",
+                             "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count())),
+                             "kind": "reference", "sample": desc},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+    secs = max(2.0, 20.0 / max(a.steps, 1))
+    vals = []
+    for _ in range(min(a.warmup, 3)):
+        cpu_reference_gemv(0.5)
+    base = None
+    for _ in range(min(a.steps, 20)):
+        base = cpu_reference_gemv(secs)
+        vals.append(base["value"])
+    v = float(np.median(vals))
+    base["value"] = v
+    print(json.dumps({
+        "metric": GEMV_METRIC,
+        "value": v, "unit": "GB/s", "impl": "reference", "n_gpus": a.gpus, "steps": a.steps,
+        "warmup": a.warmup, "higher_is_better": True, "dtype": "e4m3 weights, f32 x, f64 accumulation",
+        "data": "synthetic", "config": {"workload": "gemv_fp8 config 1", "rows": C1_ROWS, "cols": C1_COLS},
+        "cpu_baseline": base,
+        "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20000)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default 256 decode tokens / 20000 GEMVs)")
+    ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="gemv_fp8", choices=["gemv_fp8"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv_fp8"])
+    ap.add_argument("--context", type=int, default=512, help="decode: prompt tokens before timing")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     a = ap.parse_args()
+    if a.steps is None:
+        a.steps = 256 if a.workload == "decode" else 20000
     if a.impl == "reference":
         run_reference(a)
+    elif a.workload == "decode":
+        run_decode(a)
     else:
-        run_ours(a)
+        run_gemv(a)
 
 
 if __name__ == "__main__":

@@ -150,7 +150,6 @@ extern "C" int dsv4_cuda_init(void)
         return -1;
     }
     DSV4B_CUDA_OK(cudaStreamCreateWithFlags(&g.st, cudaStreamNonBlocking));
-    if (workspace_init() != 0) { fprintf(stderr, "dsv4_b200: workspace allocation failed\n"); return -1; }
     size_t fr = 0, tot = 0;
     DSV4B_CUDA_OK(cudaMemGetInfo(&fr, &tot));
     printf("cuda: %s, sm_%d%d, %d SMs, %.2f GB free of %.2f GB\n", p.name, p.major, p.minor,
@@ -268,7 +267,6 @@ extern "C" void dsv4_cuda_shutdown(void)
     if (g.hy) cudaFreeHost(g.hy);
     g.dx = g.dy = g.hx = g.hy = nullptr;
     g.xcap = g.ycap = g.hxcap = g.hycap = 0;
-    workspace_free();
     cudaStreamDestroy(g.st);
     g.st = nullptr;
     g.ready = 0;

@@ -1,129 +1,280 @@
-// gemv.cu - GEMV / skinny GEMM against HBM-resident weights: the register
-// kernel (batched tokens, and shapes the TMA pipeline does not take), the
-// generic any-shape kernel, and the dispatch.
+// gemv.cu - GEMV / skinny GEMM against HBM-resident weights in the
+// checkpoint's storage formats: FP8 128x128, FP4 1x32, BF16, F32.
 //
-// Replaces the reference's k_mmq_fp8 / k_mmq_fp8_n (src/cuda/dsv4_cuda.cu:93-230)
-// and widens it to the four storage formats dsv4_mmq dispatches on
-// (src/core/dsv4_matmul.c:516-591): FP8 128x128, FP4 1x32, BF16 and F32.
-// Batch-1 calls go to the TMA pipeline in gemv_tma.cu; every kernel sums in
-// the order fixed by gemv_core.cuh, so a token's result never depends on the
-// kernel, the grid or the batch it ran in.
+// Replaces the reference's k_mmq_fp8 / k_mmq_fp8_n (src/cuda/dsv4_cuda.cu:
+// 93-230) and widens it to the four formats dsv4_mmq dispatches on
+// (src/core/dsv4_matmul.c:516-591). Three kernels, one summation order
+// (gemv_core.cuh), so a token's result never depends on the kernel, the grid,
+// the batch or the group it ran in:
+//   k_gemv_group  batch 1, up to 16 matrices per launch (mixed formats,
+//                 routed experts picked on the device, optional SwiGLU pair
+//                 epilogue). Each block streams a tile of rows: every
+//                 half-warp owns one or two 256-byte segments of the row, keeps
+//                 their x in registers and walks the tile's rows with eight
+//                 16-byte weight loads in flight per thread; segment sums meet
+//                 in shared memory and are added in double in segment order.
+//   k_gemv_nt     nt tokens per weight pass (the batched dsv4_cuda_mmq_n), and
+//                 batch-1 shapes whose scale blocks are narrower than a lane.
+//   k_gemv_generic any other shape (rows not a multiple of 16 bytes).
 #include <stdlib.h>
+#include <string.h>
 
 #include "gemv_core.cuh"
 #include "internal.h"
 
 namespace dsv4b {
 
-// One warp: R rows x NT tokens. Half-warp h takes segments j = h, h+2, ...;
-// lane li = l & 15 takes the NSTEP steps of gemv_core.cuh in that segment.
-// Segment sums fold into lane 0's double totals in segment order (seg 2m from
-// half 0, then 2m+1 from half 1). x is read once per (segment, token) and
-// reused by the R rows.
-template <int FMT, int NT, int R, int UP>
-__global__ void __launch_bounds__(64)
-k_gemv_reg(GemvArgs g)
+constexpr int kGemvThreads = 256;           // 16 half-warps per block
+constexpr int kGemvSmem = 48 * 1024;        // a block's segment sums
+constexpr int kGemvMaxTr = 512;
+
+// SwiGLU with the reference's asymmetric clamp (src/core/dsv4_ops.c:60-78):
+// up clamped to +-limit, gate from above only; limit <= 0 disables both.
+__device__ __forceinline__ float swiglu_pair(float g, float u, float limit)
+{
+    if (limit > 0.0f) {
+        u = fmaxf(fminf(u, limit), -limit);
+        g = fminf(g, limit);
+    }
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
+__device__ __forceinline__ uint8_t ld_nc_u8(const uint8_t *p)
+{
+    unsigned short v;
+    asm volatile("ld.global.nc.u8 %0, [%1];" : "=h"(v) : "l"(p));
+    return (uint8_t)v;
+}
+
+// The lane's q when its E elements lie in one scale block (one flush).
+template <int FMT>
+__device__ __forceinline__ float lane_q1(const uint4 &w, const float4 *x, float s)
+{
+    float sv[8] = {s, s, s, s, s, s, s, s};
+    return lane_q<FMT>(w, x, sv, 1u << (Fmt<FMT>::NS - 1));
+}
+
+// ------------------------------------------------------------ k_gemv_group
+
+struct TilePtrs {
+    const uint8_t *W, *S, *W2, *S2;
+};
+
+// Rows per pass: U * SPH 16-byte loads in flight per thread.
+template <int FMT, int SPH>
+constexpr int kRowsPerPass = 8 / SPH;
+// Segments per chunk (16 half-warps x SPH): FP4 keeps one segment per
+// half-warp, since two segments' x would take 64 registers.
+template <int FMT>
+constexpr int kChunkSegs = FMT == DSV4B_WFP4 ? 16 : 32;
+
+// Segments [chunk0, chunk0 + cseg) of every virtual row of one tile. SPH
+// segments per half-warp; U rows per pass, so U * SPH loads are in flight.
+template <int FMT, int SPH>
+__device__ __forceinline__ void group_chunk(const GemvItem &it, const TilePtrs &t, int tile, int nvr,
+                                            int chunk0, int cseg, int nseg, float *ssum)
 {
     using F = Fmt<FMT>;
-    constexpr int NS = F::NSTEP, SB = F::SB;
-    const int lane = threadIdx.x & 31, half = lane >> 4, li = lane & 15;
-    const int warp = (int)((blockIdx.x * (unsigned)blockDim.x + threadIdx.x) >> 5);
-    const int row0 = warp * R;
-    if (row0 >= g.rows) return;
-    const int rb = g.rowbytes, nseg = (rb + 255) >> 8;
-
-    const uint8_t *W = g.W, *Sg = g.S;
-    if (g.wtab) {
-        const int e = g.sel[g.slot];
-        W = g.wtab[e];
-        Sg = g.stab ? g.stab[e] : nullptr;
+    constexpr int NS = F::NS, E = F::E, U = kRowsPerPass<FMT, SPH>;
+    const int hws = (cseg + SPH - 1) / SPH, rs = 16 / hws;
+    const int hw = threadIdx.x >> 4, li = threadIdx.x & 15;
+    const int slot = hw / hws, grp = hw - slot * hws;
+    if (slot >= rs) return;
+    const unsigned hm = half_mask();
+    const int rb = it.rowbytes, trh = it.tr >> 1;
+    int seg[SPH], off[SPH], scol[SPH];
+    bool lv[SPH], sv[SPH];
+    float4 xr[SPH][NS];
+#pragma unroll
+    for (int j = 0; j < SPH; j++) {
+        seg[j] = chunk0 + grp * SPH + j;
+        sv[j] = seg[j] < chunk0 + cseg;
+        off[j] = seg[j] * 256 + 16 * li;
+        lv[j] = sv[j] && off[j] < rb;
+        const int e0 = (off[j] >> 4) * E;
+        scol[j] = F::SC ? (e0 >> it.lbc) : 0;
+#pragma unroll
+        for (int k = 0; k < NS; k++)
+            xr[j][k] = lv[j] ? ld_f4(it.x + e0 + 4 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    const uint8_t *wr[R];
-    int srow[R];
+    for (int v0 = slot; v0 < nvr; v0 += rs * U) {
+        uint4 w[U][SPH];
+        float s[U][SPH];
+        bool rv[U];
 #pragma unroll
-    for (int r = 0; r < R; r++) {
-        const int o = min(row0 + r, g.rows - 1);
-        wr[r] = W + (size_t)o * rb;
-        srow[r] = F::SC ? (o >> g.lbr) * g.sc : 0;
-    }
-    double tot[R][NT];
+        for (int u = 0; u < U; u++) {
+            const int v = v0 + u * rs;
+            const bool second = it.pair && v >= trh;
+            const int row = it.pair ? tile * trh + (second ? v - trh : v) : tile * it.tr + v;
+            rv[u] = v < nvr && row < it.rows;
+            const uint8_t *Wm = second ? t.W2 : t.W;
+            const uint8_t *Sm = second ? t.S2 : t.S;
 #pragma unroll
-    for (int r = 0; r < R; r++)
-#pragma unroll
-        for (int t = 0; t < NT; t++) tot[r][t] = 0.0;
-
-    for (int m0 = 0; m0 < nseg; m0 += 2 * UP) {
-        uint4 wv[UP][R][NS];
-#pragma unroll
-        for (int j = 0; j < UP; j++) {
-            const int seg = m0 + 2 * j + half;
-#pragma unroll
-            for (int k = 0; k < NS; k++) {
-                const int off = seg * 256 + SB * (16 * k + li);
-#pragma unroll
-                for (int r = 0; r < R; r++)
-                    wv[j][r][k] = (seg < nseg && off < rb) ? ldg_step<FMT>(wr[r] + off) : make_uint4(0u, 0u, 0u, 0u);
+            for (int j = 0; j < SPH; j++) {
+                const bool ok = rv[u] && lv[j];
+                w[u][j] = ok ? ld_stream16(Wm + (size_t)row * rb + off[j]) : make_uint4(0u, 0u, 0u, 0u);
+                s[u][j] = (F::SC && ok) ? e8m0(ld_nc_u8(Sm + (size_t)(row >> it.lbr) * it.sc + scol[j])) : 1.0f;
             }
         }
 #pragma unroll
-        for (int j = 0; j < UP; j++) {
-            const int seg = m0 + 2 * j + half;
-            float q[R][NT];
+        for (int u = 0; u < U; u++) {
+            const int v = v0 + u * rs;
 #pragma unroll
-            for (int r = 0; r < R; r++)
+            for (int j = 0; j < SPH; j++) {
+                float q = lane_q1<FMT>(w[u][j], xr[j], s[u][j]);
+                q = seg_sum16(q, hm);
+                if (li == 0 && rv[u] && sv[j]) ssum[v * (nseg + 1) + seg[j]] = q;
+            }
+        }
+    }
+}
+
+template <int FMT>
+__device__ __forceinline__ void group_tile(const GemvItem &it, int tile, float *ssum)
+{
+    TilePtrs t = {it.W, it.S, it.W2, it.S2};
+    if (it.wtab) {
+        const int e = it.sel[it.slot];
+        t.W = it.wtab[e];
+        t.S = it.stab ? it.stab[e] : nullptr;
+        if (it.pair) {
+            t.W2 = it.w2tab[e];
+            t.S2 = it.s2tab ? it.s2tab[e] : nullptr;
+        }
+    }
+    const int nseg = (it.rowbytes + 255) >> 8;
+    const int nvr = it.tr;
+    constexpr int CMAX = kChunkSegs<FMT>;
+    for (int c0 = 0; c0 < nseg; c0 += CMAX) {
+        const int cseg = min(CMAX, nseg - c0);
+        if constexpr (CMAX > 16) {
+            if (cseg > 16) {
+                group_chunk<FMT, 2>(it, t, tile, nvr, c0, cseg, nseg, ssum);
+                continue;
+            }
+        }
+        group_chunk<FMT, 1>(it, t, tile, nvr, c0, cseg, nseg, ssum);
+    }
+    __syncthreads();
+    const int nreal = it.pair ? it.tr >> 1 : it.tr;
+    for (int r = threadIdx.x; r < nreal; r += blockDim.x) {
+        const int row = tile * nreal + r;
+        if (row >= it.rows) break;
+        const float *sr = ssum + r * (nseg + 1);
+        double tot = 0.0;
+        for (int s = 0; s < nseg; s++) tot = __dadd_rn(tot, (double)sr[s]);
+        float a = (float)tot;
+        if (it.pair) {
+            const float *s2 = ssum + (r + nreal) * (nseg + 1);
+            double t2 = 0.0;
+            for (int s = 0; s < nseg; s++) t2 = __dadd_rn(t2, (double)s2[s]);
+            a = swiglu_pair(a, (float)t2, it.limit);
+        }
+        it.y[row] = a;
+    }
+}
+
+__global__ void __launch_bounds__(kGemvThreads, 2)
+k_gemv_group(const __grid_constant__ GemvBatch b)
+{
+    extern __shared__ float ssum[];
+    int i = 0;
+    while (i + 1 < b.n && (int)blockIdx.x >= b.it[i + 1].tile0) i++;
+    const GemvItem &it = b.it[i];
+    const int tile = (int)blockIdx.x - it.tile0;
+    switch (it.fmt) {
+    case DSV4B_WF32: group_tile<DSV4B_WF32>(it, tile, ssum); break;
+    case DSV4B_WBF16: group_tile<DSV4B_WBF16>(it, tile, ssum); break;
+    case DSV4B_WFP8: group_tile<DSV4B_WFP8>(it, tile, ssum); break;
+    default: group_tile<DSV4B_WFP4>(it, tile, ssum); break;
+    }
+}
+
+// --------------------------------------------------------------- k_gemv_nt
+
+struct NtArgs {
+    const uint8_t *W, *S;
+    const float *x;
+    float *y;
+    int rows, cols, sc, lbr, lbc, rowbytes;
+    long xstride, ystride;
+};
+
+// One warp: one row x NT tokens. Half-warp h takes segments h, h+2, ...;
+// lane li its 16 bytes of each. Segment sums fold into lane 0's double totals
+// in segment order (segment 2m from half 0, then 2m+1 from half 1).
+template <int FMT, int NT>
+__global__ void __launch_bounds__(128)
+k_gemv_nt(NtArgs g)
+{
+    using F = Fmt<FMT>;
+    constexpr int NS = F::NS, E = F::E;
+    const int lane = threadIdx.x & 31, half = lane >> 4, li = lane & 15;
+    const int row = (int)((blockIdx.x * (unsigned)blockDim.x + threadIdx.x) >> 5);
+    if (row >= g.rows) return;
+    const int rb = g.rowbytes, nseg = (rb + 255) >> 8;
+    const uint8_t *wr = g.W + (size_t)row * rb;
+    double tot[NT];
 #pragma unroll
-                for (int t = 0; t < NT; t++) q[r][t] = 0.0f;
-            if (seg < nseg) {
-                const int e0 = seg * 256 * 4 / SB;
-                int nvalid = 0;
+    for (int t = 0; t < NT; t++) tot[t] = 0.0;
+    for (int m0 = 0; m0 < nseg; m0 += 4) {
+        uint4 w[2];
+        bool lv[2];
+        int e0[2];
 #pragma unroll
-                for (int k = 0; k < NS; k++) nvalid += (seg * 256 + SB * (16 * k + li) < rb) ? 1 : 0;
-                const StepMasks m = step_masks<FMT>(e0, li, nvalid, g.lbc);
-                float s[R][NS];
+        for (int j = 0; j < 2; j++) {
+            const int seg = m0 + 2 * j + half, off = seg * 256 + 16 * li;
+            lv[j] = seg < nseg && off < rb;
+            e0[j] = (off >> 4) * E;
+            w[j] = lv[j] ? ld_stream16(wr + off) : make_uint4(0u, 0u, 0u, 0u);
+        }
 #pragma unroll
-                for (int r = 0; r < R; r++)
+        for (int j = 0; j < 2; j++) {
+            float s[NS];
+            uint32_t fm = 1u << (NS - 1);
+            if (F::SC) {
+                fm = flush_mask<FMT>(e0[j], g.lbc);
 #pragma unroll
-                    for (int k = 0; k < NS; k++)
-                        s[r][k] = (F::SC && k < nvalid) ? e8m0(__ldg(Sg + srow[r] + ((e0 + 4 * (16 * k + li)) >> g.lbc)))
-                                                        : 1.0f;
+                for (int k = 0; k < NS; k++)
+                    s[k] = lv[j] ? e8m0(ld_nc_u8(g.S + (size_t)(row >> g.lbr) * g.sc + ((e0[j] + 4 * k) >> g.lbc)))
+                                 : 1.0f;
+            } else {
 #pragma unroll
-                for (int t = 0; t < NT; t++) {
-                    float4 xv[NS];
+                for (int k = 0; k < NS; k++) s[k] = 1.0f;
+            }
+            float q[NT];
 #pragma unroll
-                    for (int k = 0; k < NS; k++)
-                        xv[k] = (k < nvalid) ? __ldg(reinterpret_cast<const float4 *>(
-                                                   g.x + (size_t)t * g.xstride + e0 + 4 * (16 * k + li)))
-                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int t = 0; t < NT; t++) {
+                float4 xv[NS];
 #pragma unroll
-                    for (int r = 0; r < R; r++) q[r][t] = lane_q<FMT>(wv[j][r], xv, s[r], m);
-                }
+                for (int k = 0; k < NS; k++)
+                    xv[k] = lv[j] ? ld_f4(g.x + (size_t)t * g.xstride + e0[j] + 4 * k)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                q[t] = lv[j] ? lane_q<FMT>(w[j], xv, s, fm) : 0.0f;
             }
             const int sev = m0 + 2 * j;
 #pragma unroll
-            for (int r = 0; r < R; r++)
-#pragma unroll
-                for (int t = 0; t < NT; t++) {
-                    const float v = seg_sum16(q[r][t]);
-                    const float vodd = __shfl_sync(0xffffffffu, v, 16);
-                    if (lane == 0) {
-                        if (sev < nseg) tot[r][t] = __dadd_rn(tot[r][t], (double)v);
-                        if (sev + 1 < nseg) tot[r][t] = __dadd_rn(tot[r][t], (double)vodd);
-                    }
+            for (int t = 0; t < NT; t++) {
+                const float v = seg_sum16(q[t], 0xffffffffu);
+                const float vodd = __shfl_sync(0xffffffffu, v, 16);
+                if (lane == 0) {
+                    if (sev < nseg) tot[t] = __dadd_rn(tot[t], (double)v);
+                    if (sev + 1 < nseg) tot[t] = __dadd_rn(tot[t], (double)vodd);
                 }
+            }
         }
     }
     if (lane == 0)
 #pragma unroll
-        for (int r = 0; r < R; r++)
-#pragma unroll
-            for (int t = 0; t < NT; t++)
-                if (row0 + r < g.rows) g.y[(size_t)t * g.ystride + row0 + r] = (float)tot[r][t];
+        for (int t = 0; t < NT; t++) g.y[(size_t)t * g.ystride + row] = (float)tot[t];
 }
+
+// ----------------------------------------------------------- k_gemv_generic
 
 // Any shape: one warp per (row, token), scalar loads, exact products summed in
 // double. Only reached by shapes whose rows are not 16-byte multiples (the
 // reference's hand-sized test matrices); every model matrix takes the others.
-__global__ void k_gemv_generic(GemvArgs g, int fmt, int nt)
+__global__ void k_gemv_generic(NtArgs g, int fmt, int blk_r, int blk_c, int nt)
 {
     const int lane = threadIdx.x & 31;
     const long warp = (long)((blockIdx.x * (unsigned)blockDim.x + threadIdx.x) >> 5);
@@ -139,67 +290,20 @@ __global__ void k_gemv_generic(GemvArgs g, int fmt, int nt)
         else if (fmt == DSV4B_WFP8) w = e4m3x2((uint16_t)row[c]).x;
         else { const uint8_t b = row[c >> 1]; w = e2m1x2((uint8_t)((c & 1) ? (b >> 4) : (b & 15))).x; }
         double s = 1.0;
-        if (fmt >= DSV4B_WFP8) s = (double)e8m0(g.S[(o / g.blk_r) * g.sc + c / g.blk_c]);
+        if (fmt >= DSV4B_WFP8) s = (double)e8m0(g.S[(o / blk_r) * g.sc + c / blk_c]);
         acc = __fma_rn((double)w * s, (double)x[c], acc);
     }
     acc = warp_sum_d(acc);
     if (lane == 0) g.y[(size_t)t * g.ystride + o] = (float)acc;
 }
 
-template <int FMT, int NT, int R, int UP>
-static void launch_ru(const GemvArgs &g, cudaStream_t st)
-{
-    const int warps = (g.rows + R - 1) / R;
-    const int threads = 64;
-    const int blocks = (warps * 32 + threads - 1) / threads;
-    k_gemv_reg<FMT, NT, R, UP><<<blocks, threads, 0, st>>>(g);
-}
+// --------------------------------------------------------------------- host
 
-template <int FMT, int NT>
-static void launch_nt(const GemvArgs &g, cudaStream_t st)
-{
-    if constexpr (NT == 1) {
-        // rows per warp x segment pairs in flight, chosen by measurement
-        static const int ru = [] {
-            const char *e = getenv("DSV4B_GEMV_RU");
-            return e ? atoi(e) : 22;
-        }();
-        switch (ru) {
-        case 11: launch_ru<FMT, 1, 1, 1>(g, st); return;
-        case 12: launch_ru<FMT, 1, 1, 2>(g, st); return;
-        case 14: launch_ru<FMT, 1, 1, 4>(g, st); return;
-        case 18: launch_ru<FMT, 1, 1, 8>(g, st); return;
-        case 22: launch_ru<FMT, 1, 2, 2>(g, st); return;
-        case 24: launch_ru<FMT, 1, 2, 4>(g, st); return;
-        case 42: launch_ru<FMT, 1, 4, 2>(g, st); return;
-        default: launch_ru<FMT, 1, 2, 2>(g, st); return;
-        }
-    } else {
-        constexpr int R = (NT <= 2) ? 2 : 1;
-        constexpr int UP = (NT <= 2) ? 2 : 1;
-        launch_ru<FMT, NT, R, UP>(g, st);
-    }
-}
-
-template <int FMT>
-static void launch_fmt(const GemvArgs &g, int nt, cudaStream_t st)
-{
-    switch (nt) {
-    case 1: launch_nt<FMT, 1>(g, st); break;
-    case 2: launch_nt<FMT, 2>(g, st); break;
-    case 3: launch_nt<FMT, 3>(g, st); break;
-    case 4: launch_nt<FMT, 4>(g, st); break;
-    case 5: launch_nt<FMT, 5>(g, st); break;
-    case 6: launch_nt<FMT, 6>(g, st); break;
-    case 7: launch_nt<FMT, 7>(g, st); break;
-    default: launch_nt<FMT, 8>(g, st); break;
-    }
-}
-
-static int epu_of(int fmt)
+static int lane_elems(int fmt)
 {
     return fmt == DSV4B_WF32 ? 4 : fmt == DSV4B_WBF16 ? 8 : fmt == DSV4B_WFP8 ? 16 : 32;
 }
+
 static int log2_exact(int v)
 {
     if (v <= 0 || (v & (v - 1))) return -1;
@@ -222,83 +326,155 @@ bool gemv_vectorizable(int fmt, const void *W, int cols, int blk_r, int blk_c, c
 {
     const size_t rb = row_bytes(fmt, cols);
     if (rb % 16 || ((uintptr_t)W & 15) || ((uintptr_t)x & 15) || (xstride & 3)) return false;
-    // scale blocks: powers of two, and a step's 4 elements inside one block
+    // scale blocks: powers of two, and a sub-step's 4 elements inside one block
     if (fmt >= DSV4B_WFP8 && (log2_exact(blk_c) < 2 || log2_exact(blk_r) < 0)) return false;
-    (void)epu_of;
     return true;
 }
 
-int gemv_reg(const GemvArgs &g0, int fmt, int nt, cudaStream_t st)
+bool gemv_item(GemvItem &it, int fmt, const void *W, const uint8_t *S, int rows, int cols, int blk_r,
+               int blk_c, const float *x, float *y)
 {
-    GemvArgs g = g0;
-    for (int t0 = 0; t0 < nt; t0 += 8) {
-        const int n = (nt - t0 < 8) ? nt - t0 : 8;
-        g.x = g0.x + (size_t)t0 * g0.xstride;
-        g.y = g0.y + (size_t)t0 * g0.ystride;
-        switch (fmt) {
-        case DSV4B_WF32: launch_fmt<DSV4B_WF32>(g, n, st); break;
-        case DSV4B_WBF16: launch_fmt<DSV4B_WBF16>(g, n, st); break;
-        case DSV4B_WFP8: launch_fmt<DSV4B_WFP8>(g, n, st); break;
-        default: launch_fmt<DSV4B_WFP4>(g, n, st); break;
-        }
+    memset(&it, 0, sizeof it);
+    blk_r = blk_r > 0 ? blk_r : 1;
+    blk_c = blk_c > 0 ? blk_c : 1;
+    if (!gemv_vectorizable(fmt, W, cols, blk_r, blk_c, x, 0)) return false;
+    if (fmt >= DSV4B_WFP8 && blk_c < lane_elems(fmt)) return false;   // a lane's elements share one scale
+    it.W = (const uint8_t *)W;
+    it.S = S;
+    it.x = x;
+    it.y = y;
+    it.fmt = fmt;
+    it.rows = rows;
+    it.cols = cols;
+    it.rowbytes = (int)row_bytes(fmt, cols);
+    it.sc = fmt >= DSV4B_WFP8 ? (cols + blk_c - 1) / blk_c : 0;
+    it.lbr = fmt >= DSV4B_WFP8 ? log2_exact(blk_r) : 0;
+    it.lbc = fmt >= DSV4B_WFP8 ? log2_exact(blk_c) : 30;
+    return true;
+}
+
+int gemv_group(GemvItem *items, int n, cudaStream_t st)
+{
+    if (n <= 0) return 0;
+    if (n > kGemvMaxItems) return -1;
+    static int nsm = 0;
+    if (!nsm) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+        if (nsm <= 0) nsm = 148;
     }
+    double total = 0.0;
+    for (int i = 0; i < n; i++) total += (double)items[i].rows * items[i].rowbytes * (items[i].pair ? 2 : 1);
+    // about four blocks per SM, each streaming 16-128 KB
+    double target = total / (4.0 * nsm);
+    target = target < 16384.0 ? 16384.0 : (target > 131072.0 ? 131072.0 : target);
+    GemvBatch b;
+    b.n = n;
+    int blocks = 0;
+    size_t smem = 0;
+    for (int i = 0; i < n; i++) {
+        GemvItem &it = items[i];
+        it.tile0 = blocks;
+        if (it.rows <= 0) {
+            it.tr = 2;
+            b.it[i] = it;
+            continue;
+        }
+        const int nseg = (it.rowbytes + 255) >> 8;
+        const int cmax = it.fmt == DSV4B_WFP4 ? 16 : 32;
+        const int cseg = nseg < cmax ? nseg : cmax, sph = cseg > 16 ? 2 : 1;
+        const int hws = (cseg + sph - 1) / sph, gran = (16 / hws) * (8 / sph);   // virtual rows per pass
+        int cap = (int)(kGemvSmem / ((size_t)(nseg + 1) * 4));
+        cap = cap < kGemvMaxTr ? cap : kGemvMaxTr;
+        if (cap < 2) return -1;
+        int tr = (int)(target / it.rowbytes);
+        tr = tr < 1 ? 1 : tr;
+        tr = (tr + gran - 1) / gran * gran;
+        tr = tr < cap ? tr : cap;
+        if (it.pair) {
+            tr &= ~1;
+            if (tr < 2) tr = 2;
+            if (tr / 2 > it.rows) tr = 2 * it.rows;
+        } else if (tr > it.rows) {
+            tr = it.rows;
+        }
+        it.tr = tr;
+        const int per = it.pair ? tr / 2 : tr;      // real rows per block
+        blocks += (it.rows + per - 1) / per;
+        const size_t sm = (size_t)tr * (nseg + 1) * 4;
+        if (sm > smem) smem = sm;
+        b.it[i] = it;
+    }
+    if (!blocks) return 0;
+    k_gemv_group<<<blocks, kGemvThreads, smem, st>>>(b);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 
-int gemv_sel(int fmt, float *y, const float *x, const uint8_t *const *wtab,
-             const uint8_t *const *stab, const int *sel, int slot, int rows,
-             int cols, int blk_r, int blk_c, cudaStream_t st)
+template <int FMT, int NT>
+static void launch_nt(const NtArgs &a, cudaStream_t st)
 {
-    GemvArgs g = {};
-    g.rows = rows; g.cols = cols;
-    g.blk_r = blk_r > 0 ? blk_r : 1; g.blk_c = blk_c > 0 ? blk_c : 1;
-    g.sc = fmt >= DSV4B_WFP8 ? (cols + g.blk_c - 1) / g.blk_c : 0;
-    g.rowbytes = (int)row_bytes(fmt, cols);
-    g.xstride = cols; g.ystride = rows;
-    g.x = x; g.y = y;
-    g.lbr = fmt >= DSV4B_WFP8 ? log2_exact(g.blk_r) : 0;
-    g.lbc = fmt >= DSV4B_WFP8 ? log2_exact(g.blk_c) : 30;
-    g.wtab = wtab; g.stab = stab; g.sel = sel; g.slot = slot;
-    // the table's matrices are uploaded (256-byte aligned); the shape decides
-    if (g.rowbytes % 16 || ((uintptr_t)x & 15)) return -1;
-    if (fmt >= DSV4B_WFP8 && (g.lbc < 2 || g.lbr < 0)) return -1;
-    return gemv_reg(g, fmt, 1, st);
+    const int blocks = (a.rows + 3) / 4;
+    k_gemv_nt<FMT, NT><<<blocks, 128, 0, st>>>(a);
 }
 
-int gemv(int fmt, float *y, long ystride, const float *x, long xstride,
-         const void *W, const uint8_t *S, int rows, int cols, int blk_r,
-         int blk_c, int nt, cudaStream_t st)
+template <int FMT>
+static void launch_fmt(const NtArgs &a, int nt, cudaStream_t st)
+{
+    switch (nt) {
+    case 1: launch_nt<FMT, 1>(a, st); break;
+    case 2: launch_nt<FMT, 2>(a, st); break;
+    case 3: launch_nt<FMT, 3>(a, st); break;
+    case 4: launch_nt<FMT, 4>(a, st); break;
+    case 5: launch_nt<FMT, 5>(a, st); break;
+    case 6: launch_nt<FMT, 6>(a, st); break;
+    case 7: launch_nt<FMT, 7>(a, st); break;
+    default: launch_nt<FMT, 8>(a, st); break;
+    }
+}
+
+int gemv(int fmt, float *y, long ystride, const float *x, long xstride, const void *W, const uint8_t *S,
+         int rows, int cols, int blk_r, int blk_c, int nt, cudaStream_t st)
 {
     if (rows <= 0 || cols <= 0 || nt <= 0) return 0;
     if (fmt == DSV4B_WFP4 && (cols & 1)) return -1;
-    GemvArgs g = {};
-    g.W = (const uint8_t *)W; g.S = S;
-    g.rows = rows; g.cols = cols;
-    g.blk_r = blk_r > 0 ? blk_r : 1; g.blk_c = blk_c > 0 ? blk_c : 1;
-    g.sc = fmt >= DSV4B_WFP8 ? (cols + g.blk_c - 1) / g.blk_c : 0;
-    g.rowbytes = (int)row_bytes(fmt, cols);
-    g.xstride = xstride; g.ystride = ystride;
-    g.x = x; g.y = y;
-    g.lbr = fmt >= DSV4B_WFP8 ? log2_exact(g.blk_r) : 0;
-    g.lbc = fmt >= DSV4B_WFP8 ? log2_exact(g.blk_c) : 30;
-    if (!gemv_vectorizable(fmt, W, cols, g.blk_r, blk_c, x, xstride)) {
+    blk_r = blk_r > 0 ? blk_r : 1;
+    blk_c = blk_c > 0 ? blk_c : 1;
+    NtArgs a = {};
+    a.W = (const uint8_t *)W;
+    a.S = S;
+    a.x = x;
+    a.y = y;
+    a.rows = rows;
+    a.cols = cols;
+    a.rowbytes = (int)row_bytes(fmt, cols);
+    a.sc = fmt >= DSV4B_WFP8 ? (cols + blk_c - 1) / blk_c : 0;
+    a.lbr = fmt >= DSV4B_WFP8 ? log2_exact(blk_r) : 0;
+    a.lbc = fmt >= DSV4B_WFP8 ? log2_exact(blk_c) : 30;
+    a.xstride = xstride;
+    a.ystride = ystride;
+    if (!gemv_vectorizable(fmt, W, cols, blk_r, blk_c, x, xstride)) {
         const long warps = (long)rows * nt;
-        k_gemv_generic<<<(unsigned)((warps * 32 + 127) / 128), 128, 0, st>>>(g, fmt, nt);
+        k_gemv_generic<<<(unsigned)((warps * 32 + 127) / 128), 128, 0, st>>>(a, fmt, blk_r, blk_c, nt);
         return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
     }
-    // Batch-1 path: the register kernel measured faster than the TMA stream
-    // on every model shape (both are bound by CUDA-core dequantisation, not
-    // HBM); DSV4B_GEMV_PATH=tma selects the stream.
-    static const int use_tma = [] {
-        const char *e = getenv("DSV4B_GEMV_PATH");
-        return (e && e[0] == 't') ? 1 : 0;
-    }();
-    if (nt == 1 && use_tma && gemv_tma_ok(fmt, g)) {
-        TmaGroup grp = {};
-        grp.W = g.W; grp.S = g.S; grp.x = x; grp.y = y; grp.rows = rows; grp.sel = -1;
-        return gemv_tma(fmt, &grp, 1, cols, g.blk_r, g.blk_c, nullptr, st);
+    if (nt == 1 && ystride >= rows) {
+        GemvItem it;
+        if (gemv_item(it, fmt, W, S, rows, cols, blk_r, blk_c, x, y)) return gemv_group(&it, 1, st);
     }
-    return gemv_reg(g, fmt, nt, st);
+    for (int t0 = 0; t0 < nt; t0 += 8) {
+        const int k = (nt - t0 < 8) ? nt - t0 : 8;
+        NtArgs b = a;
+        b.x = x + (size_t)t0 * xstride;
+        b.y = y + (size_t)t0 * ystride;
+        switch (fmt) {
+        case DSV4B_WF32: launch_fmt<DSV4B_WF32>(b, k, st); break;
+        case DSV4B_WBF16: launch_fmt<DSV4B_WBF16>(b, k, st); break;
+        case DSV4B_WFP8: launch_fmt<DSV4B_WFP8>(b, k, st); break;
+        default: launch_fmt<DSV4B_WFP4>(b, k, st); break;
+        }
+    }
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 
 // Device decoder dump for the all-codes gate (reference dsv4_cuda.cu:454-469).

@@ -1,145 +1,112 @@
 // gemv_core.cuh - the one summation order every GEMV kernel in this backend
-// uses, so results never depend on which kernel, grid or batch size ran.
+// uses, so a result never depends on which kernel, grid or batch size ran.
 //
 // A row is cut into SEGMENTS of 256 weight bytes (64 f32 / 128 bf16 / 256 fp8
-// / 512 fp4 elements), each owned by 16 lanes. Lane li (0..15) of a segment
-// takes NSTEP steps (1 / 2 / 4 / 8); step k covers the 4 elements
-// [4(16k+li), 4(16k+li)+4) of the segment, so at every step the 16 lanes read
-// 16 consecutive float4 of x (bank-conflict-free in shared memory) and
-// consecutive weight bytes. For row o, token t, lane li:
-//   c     = a float2 accumulator: per step, fma of elements (0,1) then (2,3)
-//           into (c.x, c.y);
-//   q     = at the lane's last step inside each scale block (every step for
-//           unscaled formats ends the single block at the lane's last step):
-//           q = fma(c.x + c.y, scale, q) and c restarts at 0 (the scale is a
-//           power of two, so the product is exact);
+// / 512 fp4 elements), each owned by 16 lanes. Lane li (0..15) owns the 16
+// contiguous bytes [16 li, 16 li + 16) of its segment -- E = 4 / 8 / 16 / 32
+// elements, one 128-bit load -- and walks them in NS = E / 4 sub-steps of 4
+// elements. For row o, token t, lane li:
+//   c     = a float2 accumulator: per sub-step, fma of elements (0,1) then
+//           (2,3) into (c.x, c.y);
+//   q     = at the lane's last sub-step inside each scale block (for unscaled
+//           formats: at its last sub-step): q = fma(c.x + c.y, scale, q), and
+//           c restarts at 0 (scales are powers of two, so the product is
+//           exact);
 //   seg   = the 16 lanes' q summed in float by the xor butterfly 8,4,2,1;
 //   total = ((0 + seg_0) + seg_1) + ...   in DOUBLE, in segment order;
 //   y     = (float)total.
-// Missing elements of a short last segment contribute nothing. Block sizes are
-// powers of two. Against the reference CPU's 16-lane double tree
-// (src/core/dsv4_matmul.c:51-64) this agrees to ~1e-7 of the vector scale;
-// between kernels of this backend it is bit-identical, which is what makes
-// mmq_n equal nt separate mmq calls.
+// Lanes past the end of a short last segment contribute 0. Against the
+// reference CPU's 16-lane double tree (src/core/dsv4_matmul.c:51-64) this
+// agrees to ~1e-7 of the vector scale; between kernels of this backend it is
+// bit-identical, which is what makes mmq_n equal nt separate mmq calls.
 #pragma once
 
 #include "common.cuh"
 
 namespace dsv4b {
 
+// E: elements per lane (16 bytes); NS: 4-element sub-steps; LE: log2(E).
 template <int FMT> struct Fmt;
-// NSTEP: steps per lane per segment; SB: weight bytes per step; EPU kept for
-// element <-> byte arithmetic (elements per 16 weight bytes).
-template <> struct Fmt<DSV4B_WF32> { static constexpr int NSTEP = 1, SB = 16, EPU = 4; static constexpr bool SC = false; };
-template <> struct Fmt<DSV4B_WBF16> { static constexpr int NSTEP = 2, SB = 8, EPU = 8; static constexpr bool SC = false; };
-template <> struct Fmt<DSV4B_WFP8> { static constexpr int NSTEP = 4, SB = 4, EPU = 16; static constexpr bool SC = true; };
-template <> struct Fmt<DSV4B_WFP4> { static constexpr int NSTEP = 8, SB = 2, EPU = 32; static constexpr bool SC = true; };
+template <> struct Fmt<DSV4B_WF32> { static constexpr int E = 4, NS = 1, LE = 2; static constexpr bool SC = false; };
+template <> struct Fmt<DSV4B_WBF16> { static constexpr int E = 8, NS = 2, LE = 3; static constexpr bool SC = false; };
+template <> struct Fmt<DSV4B_WFP8> { static constexpr int E = 16, NS = 4, LE = 4; static constexpr bool SC = true; };
+template <> struct Fmt<DSV4B_WFP4> { static constexpr int E = 32, NS = 8, LE = 5; static constexpr bool SC = true; };
 
-// The raw weight bytes of one step, widened to 16 bytes (unused words 0).
-template <int FMT>
-__device__ __forceinline__ uint4 load_step(const uint8_t *p)
+__device__ __forceinline__ uint32_t word_of(const uint4 &w, int i)
 {
-    if constexpr (FMT == DSV4B_WF32) return *reinterpret_cast<const uint4 *>(p);
-    else if constexpr (FMT == DSV4B_WBF16) {
-        const uint2 v = *reinterpret_cast<const uint2 *>(p);
-        return make_uint4(v.x, v.y, 0u, 0u);
-    } else if constexpr (FMT == DSV4B_WFP8) return make_uint4(*reinterpret_cast<const uint32_t *>(p), 0u, 0u, 0u);
-    else return make_uint4((uint32_t)*reinterpret_cast<const uint16_t *>(p), 0u, 0u, 0u);
+    return i == 0 ? w.x : i == 1 ? w.y : i == 2 ? w.z : w.w;
 }
 
-// Streaming (L1 no-allocate) global form of load_step, for weights read once.
-template <int FMT>
-__device__ __forceinline__ uint4 ldg_step(const uint8_t *p)
-{
-    uint4 r = make_uint4(0u, 0u, 0u, 0u);
-    if constexpr (FMT == DSV4B_WF32)
-        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                     : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
-    else if constexpr (FMT == DSV4B_WBF16)
-        asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
-    else if constexpr (FMT == DSV4B_WFP8)
-        asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r.x) : "l"(p));
-    else {
-        unsigned short h;
-        asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(h) : "l"(p));
-        r.x = h;
-    }
-    return r;
-}
-
-// Two float pairs of one step's 4 weights.
-template <int FMT>
-__device__ __forceinline__ void step_decode(const uint4 &w, float2 &a, float2 &b)
+// The 4 weights of sub-step K of a lane's 16 bytes, as two float pairs.
+template <int FMT, int K>
+__device__ __forceinline__ void sub_decode(const uint4 &w, float2 &a, float2 &b)
 {
     if constexpr (FMT == DSV4B_WF32) {
         a = make_float2(__uint_as_float(w.x), __uint_as_float(w.y));
         b = make_float2(__uint_as_float(w.z), __uint_as_float(w.w));
     } else if constexpr (FMT == DSV4B_WBF16) {
-        a = bf16x2(w.x);
-        b = bf16x2(w.y);
+        a = bf16x2(word_of(w, 2 * K));
+        b = bf16x2(word_of(w, 2 * K + 1));
     } else if constexpr (FMT == DSV4B_WFP8) {
-        a = e4m3x2((uint16_t)(w.x & 0xFFFFu));
-        b = e4m3x2((uint16_t)(w.x >> 16));
+        const uint32_t v = word_of(w, K);
+        a = e4m3x2((uint16_t)(v & 0xFFFFu));
+        b = e4m3x2((uint16_t)(v >> 16));
     } else {
-        a = e2m1x2((uint8_t)(w.x & 0xFFu));
-        b = e2m1x2((uint8_t)((w.x >> 8) & 0xFFu));
+        const uint32_t v = word_of(w, K >> 1);
+        const uint32_t h = (K & 1) ? (v >> 16) : (v & 0xFFFFu);
+        a = e2m1x2((uint8_t)(h & 0xFFu));
+        b = e2m1x2((uint8_t)(h >> 8));
     }
 }
 
-// Which of a lane's NS steps exist (a prefix) and which of them close a scale
-// block, for the segment starting at row element `e0` (power-of-two blocks of
-// 2^lbc elements; unscaled formats pass a huge lbc). `nvalid` = valid steps.
-struct StepMasks {
-    uint32_t flush;
-    int nvalid;
-};
+// Which sub-steps close a scale block, for a lane whose first element is e
+// (row element index) in blocks of 2^lbc elements; unscaled formats pass a
+// huge lbc, so only the last sub-step flushes.
 template <int FMT>
-__device__ __forceinline__ StepMasks step_masks(int e0, int li, int nvalid, int lbc)
+__device__ __forceinline__ uint32_t flush_mask(int e, int lbc)
 {
-    constexpr int NS = Fmt<FMT>::NSTEP;
-    StepMasks m;
-    m.nvalid = nvalid;
-    m.flush = 0u;
+    constexpr int NS = Fmt<FMT>::NS;
+    uint32_t m = 1u << (NS - 1);
 #pragma unroll
-    for (int k = 0; k < NS; k++) {
-        const int ek = e0 + 4 * (16 * k + li), en = e0 + 4 * (16 * (k + 1) + li);
-        if (k < nvalid && (k + 1 == nvalid || (ek >> lbc) != (en >> lbc))) m.flush |= 1u << k;
-    }
+    for (int k = 0; k + 1 < NS; k++)
+        if (((e + 4 * k) >> lbc) != ((e + 4 * k + 4) >> lbc)) m |= 1u << k;
     return m;
 }
 
-// q of one lane for one row and token (see the order above). w[k], x[k] are
-// the step's weights and x; s[k] the scale of step k's block.
+// q of one lane for one row and token (the order above). x[k] is sub-step
+// k's float4 of x; s[k] the scale of sub-step k's block.
 template <int FMT>
-__device__ __forceinline__ float lane_q(const uint4 *w, const float4 *x, const float *s, const StepMasks &m)
+__device__ __forceinline__ float lane_q(const uint4 &w, const float4 *x, const float *s, uint32_t flush)
 {
-    constexpr int NS = Fmt<FMT>::NSTEP;
     float q = 0.0f;
     float2 c = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int k = 0; k < NS; k++) {
-        if (k < m.nvalid) {
-            float2 a, b;
-            step_decode<FMT>(w[k], a, b);
-            c = fma2(a, make_float2(x[k].x, x[k].y), c);
-            c = fma2(b, make_float2(x[k].z, x[k].w), c);
-            if (m.flush & (1u << k)) {
-                q = __fmaf_rn(__fadd_rn(c.x, c.y), s[k], q);
-                c = make_float2(0.f, 0.f);
-            }
-        }
+    float2 a, b;
+#define DSV4B_SUB(K)                                                                \
+    if constexpr ((K) < Fmt<FMT>::NS) {                                             \
+        sub_decode<FMT, (K)>(w, a, b);                                              \
+        c = fma2(a, make_float2(x[K].x, x[K].y), c);                                \
+        c = fma2(b, make_float2(x[K].z, x[K].w), c);                                \
+        if (flush & (1u << (K))) {                                                  \
+            q = __fmaf_rn(__fadd_rn(c.x, c.y), s[K], q);                            \
+            c = make_float2(0.f, 0.f);                                              \
+        }                                                                           \
     }
+    DSV4B_SUB(0) DSV4B_SUB(1) DSV4B_SUB(2) DSV4B_SUB(3)
+    DSV4B_SUB(4) DSV4B_SUB(5) DSV4B_SUB(6) DSV4B_SUB(7)
+#undef DSV4B_SUB
     return q;
 }
 
-// The segment sum: xor butterfly over the 16 lanes of a half-warp. Every lane
-// of the warp must call it (full-mask shuffles); offsets < 16 keep each half
-// separate, and every lane of a half ends with the same bits.
-__device__ __forceinline__ float seg_sum16(float v)
+// The segment sum: xor butterfly over the 16 lanes of a half-warp. `mask`
+// names the calling half-warp's lanes (offsets < 16 never leave it), so the
+// two halves of a warp may run different code.
+__device__ __forceinline__ float seg_sum16(float v, unsigned mask)
 {
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    for (int o = 8; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(mask, v, o));
     return v;
 }
+
+__device__ __forceinline__ unsigned half_mask() { return 0xFFFFu << (threadIdx.x & 16); }
 
 }  // namespace dsv4b

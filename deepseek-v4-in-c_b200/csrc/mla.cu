@@ -205,20 +205,23 @@ k_topk(int *idx_out, const float *scores, int n, int k, long seq_in_stride, long
 }
 
 // --------------------------------------------------------------- attention
-constexpr int AT_CH = 64;      // selected positions per chunk
-constexpr int AT_HG = 16;      // heads per q tile in shared memory
+constexpr int AT_CH = 32;      // selected positions per chunk
+constexpr int AT_HB = 8;       // heads per block (one warp each in the scores)
 
 // Per (sequence, chunk, head) partials: chunk max pm, exp-sum pden (double)
-// and the unnormalised value sum po[d].
+// and the unnormalised value sum po[d]. A chunk with no valid position has
+// pm = -inf and no po.
 struct AttnPart {
     float *po;
     float *pm;
     double *pden;
 };
 
-size_t attn_smem_bytes(int d) { return ((size_t)AT_CH * (d + 1) + (size_t)AT_HG * d) * 4 + (size_t)64 * AT_CH * 4; }
+size_t attn_smem_bytes(int d) { return ((size_t)AT_CH * (d + 1) + (size_t)AT_HB * d + AT_HB * AT_CH) * 4; }
 
-// grid (nchunk, batch), 256 threads.
+// grid (nchunk, ceil(n_heads / AT_HB), batch), 256 threads. The index list
+// holds its valid entries first, so the chunks past them only mark
+// themselves empty.
 __global__ void __launch_bounds__(256)
 k_attn_chunk(AttnPart part, const float *q, const void *kv, int kv_dt, long seq_kv_rows,
              const int *idxs, long seq_idx_stride, int n_heads, int d, int topk, float scale,
@@ -227,71 +230,58 @@ k_attn_chunk(AttnPart part, const float *q, const void *kv, int kv_dt, long seq_
     extern __shared__ float ats[];
     const int dp = d + 1;                                   // padded row: conflict-free
     float *kvs = ats;                                       // [AT_CH][dp]
-    float *qs = kvs + AT_CH * dp;                           // [AT_HG][d]
-    float *sc = qs + AT_HG * d;                             // [n_heads <= 64][AT_CH]
+    float *qs = kvs + AT_CH * dp;                           // [AT_HB][d]
+    float *sc = qs + AT_HB * d;                             // [AT_HB][AT_CH]
     __shared__ int pidx[AT_CH];
-    const int b = blockIdx.y, nch = gridDim.x, c0 = blockIdx.x * AT_CH, tid = threadIdx.x;
-    q += (size_t)b * seq_q_stride;
+    const int b = blockIdx.z, nch = gridDim.x, c0 = blockIdx.x * AT_CH, tid = threadIdx.x;
+    const int h0 = blockIdx.y * AT_HB, nh = min(AT_HB, n_heads - h0);
+    q += (size_t)b * seq_q_stride + (size_t)h0 * d;
     idxs += (size_t)b * seq_idx_stride;
     const int esz = kv_dt == DSV4B_DT_F32 ? 4 : kv_dt == DSV4B_DT_BF16 ? 2 : 1;
     const char *kvb = reinterpret_cast<const char *>(kv) + (size_t)b * seq_kv_rows * d * esz;
     const int npos = min(AT_CH, topk - c0);
-    if (tid < AT_CH) pidx[tid] = (tid < npos) ? idxs[c0 + tid] : -1;
-    __syncthreads();
-    for (int i = tid; i < AT_CH * d; i += blockDim.x) {
-        const int p = i / d, c = i % d;
+    const int pi = (tid < npos) ? idxs[c0 + tid] : -1;
+    if (tid < AT_CH) pidx[tid] = pi;
+    const size_t prow = ((size_t)b * nch + blockIdx.x) * n_heads + h0;
+    if (!__syncthreads_or(tid < AT_CH && pi >= 0)) {
+        if (tid < nh) {
+            part.pm[prow + tid] = -INFINITY;
+            part.pden[prow + tid] = 0.0;
+        }
+        return;
+    }
+    for (int p = tid >> 5; p < AT_CH; p += blockDim.x >> 5) {   // valid rows only
         const int r = pidx[p];
-        kvs[p * dp + c] = (r >= 0) ? load_elem(kvb, (size_t)r * d + c, kv_dt) : 0.0f;
+        if (r < 0) continue;
+        for (int c = tid & 31; c < d; c += 32) kvs[p * dp + c] = load_elem(kvb, (size_t)r * d + c, kv_dt);
     }
-    // scores: thread -> position tid & 63, heads (tid >> 6) + 4j of each q tile
-    const int p = tid & 63, hq = tid >> 6;
-    for (int h0 = 0; h0 < n_heads; h0 += AT_HG) {
-        __syncthreads();
-        for (int i = tid; i < AT_HG * d; i += blockDim.x)
-            qs[i] = (h0 + i / d < n_heads) ? q[(size_t)h0 * d + i] : 0.0f;
-        __syncthreads();
-        float acc[AT_HG / 4];
-#pragma unroll
-        for (int j = 0; j < AT_HG / 4; j++) acc[j] = 0.0f;
-        const float *kr = kvs + p * dp;
-        for (int c = 0; c < d; c++) {
-            const float kvv = kr[c];
-#pragma unroll
-            for (int j = 0; j < AT_HG / 4; j++) acc[j] = __fmaf_rn(qs[(hq + 4 * j) * d + c], kvv, acc[j]);
-        }
-#pragma unroll
-        for (int j = 0; j < AT_HG / 4; j++) {
-            const int h = h0 + hq + 4 * j;
-            if (h < n_heads) sc[h * AT_CH + p] = (pidx[p] >= 0) ? __fmul_rn(acc[j], scale) : -INFINITY;
-        }
-    }
+    for (int i = tid; i < nh * d; i += blockDim.x) qs[i] = q[i];
     __syncthreads();
-    // per head: chunk max over valid slots (the sink is not part of it), exp
-    // weights in place, exp-sum in double
-    const size_t prow = ((size_t)b * nch + blockIdx.x) * n_heads;
-    for (int h = tid >> 5; h < n_heads; h += blockDim.x >> 5) {
-        const int lane = tid & 31;
-        const float s0 = sc[h * AT_CH + lane], s1 = sc[h * AT_CH + lane + 32];
-        const float m = warp_max_f(fmaxf(s0, s1));
-        float e0 = 0.0f, e1 = 0.0f;
-        if (m != -INFINITY) {
-            e0 = (s0 == -INFINITY) ? 0.0f : expf(s0 - m);
-            e1 = (s1 == -INFINITY) ? 0.0f : expf(s1 - m);
-        }
-        const double ds = warp_sum_d((double)e0 + (double)e1);
-        __syncwarp();
-        sc[h * AT_CH + lane] = e0;
-        sc[h * AT_CH + lane + 32] = e1;
-        if (lane == 0) {
-            part.pm[prow + h] = m;
-            part.pden[prow + h] = ds;
+    // scores: warp = head, lane = position; then the chunk max over valid
+    // slots (the sink is not part of it), exp weights, exp-sum in double
+    {
+        const int h = tid >> 5, p = tid & 31;
+        if (h < nh) {
+            float acc = 0.0f;
+            const float *kr = kvs + p * dp, *qr = qs + h * d;
+            for (int c = 0; c < d; c++) acc = __fmaf_rn(qr[c], kr[c], acc);
+            const float s = (pidx[p] >= 0) ? __fmul_rn(acc, scale) : -INFINITY;
+            const float m = warp_max_f(s);
+            const float e = (m == -INFINITY || s == -INFINITY) ? 0.0f : expf(s - m);
+            const double ds = warp_sum_d((double)e);
+            sc[h * AT_CH + p] = e;
+            if (p == 0) {
+                part.pm[prow + h] = m;
+                part.pden[prow + h] = ds;
+            }
         }
     }
     __syncthreads();
     // unnormalised value sums, positions in order
-    for (int i = tid; i < n_heads * d; i += blockDim.x) {
-        const int h = i / d, c = i % d;
+    for (int i = tid; i < nh * d; i += blockDim.x) {
+        const int h = i / d, c = i - h * d;
         float o = 0.0f;
+#pragma unroll 8
         for (int pp = 0; pp < AT_CH; pp++) {
             const float e = sc[h * AT_CH + pp];
             if (e != 0.0f) o = __fadd_rn(o, __fmul_rn(e, kvs[pp * dp + c]));
@@ -383,7 +373,7 @@ int sparse_attn(float *o, const float *q, const void *kv, int kv_dt, long seq_kv
                 void *part_buf, cudaStream_t st)
 {
     if (batch <= 0 || topk <= 0) return 0;
-    if (n_heads > 64 || d > 1024) return -1;
+    if (n_heads <= 0 || d > 1024) return -1;
     const int nch = (topk + AT_CH - 1) / AT_CH;
     const size_t n = (size_t)batch * nch * n_heads;
     AttnPart part;
@@ -397,7 +387,7 @@ int sparse_attn(float *o, const float *q, const void *kv, int kv_dt, long seq_kv
         attr = true;
     }
     if (smem > 220 * 1024) return -1;
-    k_attn_chunk<<<dim3(nch, batch), 256, smem, st>>>(part, q, kv, kv_dt, seq_kv_rows, idxs, seq_idx_stride,
+    k_attn_chunk<<<dim3(nch, (n_heads + AT_HB - 1) / AT_HB, batch), 256, smem, st>>>(part, q, kv, kv_dt, seq_kv_rows, idxs, seq_idx_stride,
                                                       n_heads, d, topk, scale, (long)n_heads * d);
     k_attn_combine<<<dim3(n_heads, batch), 128, 0, st>>>(o, part, sink, nch, n_heads, d, (long)n_heads * d);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;

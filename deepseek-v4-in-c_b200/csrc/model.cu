@@ -50,6 +50,8 @@ struct dsv4b_model {
     float *comp_in, *comp_sc, *idx_q, *idx_w, *idx_scores, *logits, *xh, *am_pv;
     int *idxs, *isel, *am_pi, *prompt, *out_tokens;
     void *attn_part;
+    double *hc_part;
+    unsigned *hc_cnt;
     dsv4b::MoeScratch ms;
     dsv4b::StepState *st;
     int n_prompt;
@@ -194,6 +196,9 @@ static bool alloc_common(dsv4b_model *m)
     m->out_tokens = (int *)dcopy(m, nullptr, (size_t)m->max_pos * 4, &ok);
     m->st = (StepState *)dcopy(m, nullptr, sizeof(StepState), &ok);
     m->attn_part = dcopy(m, nullptr, attn_part_bytes(c.n_heads, hd, m->nidx, 1), &ok);
+    m->hc_part = (double *)dcopy(m, nullptr, (size_t)kHcPreBlocks * (kHcPreMixMax + 1) * 8, &ok);
+    m->hc_cnt = (unsigned *)dcopy(m, nullptr, 4, &ok);
+    if (ok && cudaMemset(m->hc_cnt, 0, 4) != cudaSuccess) ok = false;
     const int inter_s = c.moe_inter * c.n_shared;
     const size_t nf = moe_scratch_floats(d, c.moe_inter, inter_s, c.n_experts, c.topk);
     float *msb = F(nf + kMoeMaxTopk);
@@ -238,13 +243,39 @@ static int G(const DevMat &w, float *y, const float *x, cudaStream_t st)
     return gemv(w.wdt, y, w.rows, x, w.cols, w.w, w.s, w.rows, w.cols, w.blk_r, w.blk_c, 1, st);
 }
 
-static int hc_pre(dsv4b_model *m, const float *fn, const float *base, const float *scale, cudaStream_t st)
+// x1 = RMSNorm(mHC pre-mix of h) with the sub-layer's norm weights.
+// A grouped GEMV launch under construction; shapes the streaming kernel
+// cannot take run on their own at once.
+struct Grp {
+    GemvItem it[kGemvMaxItems];
+    int n = 0, rc = 0;
+};
+
+static void grp_add(Grp &g, const DevMat &w, const float *x, float *y, cudaStream_t st)
+{
+    if (g.n < kGemvMaxItems && gemv_item(g.it[g.n], w.wdt, w.w, w.s, w.rows, w.cols, w.blk_r, w.blk_c, x, y))
+        g.n++;
+    else
+        g.rc |= G(w, y, x, st);
+}
+
+static int grp_run(Grp &g, cudaStream_t st) { return g.rc | gemv_group(g.it, g.n, st); }
+
+static int hc_pre(dsv4b_model *m, const float *fn, const float *base, const float *scale, const float *norm,
+                  cudaStream_t st)
 {
     const DSV4Cfg &c = m->c;
     const int hc = c.hc_mult, mix = (2 + hc) * hc, n = hc * c.hidden;
+    if (mix <= kHcPreMixMax) {
+        k_hc_pre<<<kHcPreBlocks, 256, 0, st>>>(m->x1, m->post, m->comb, m->h, fn, scale, base, norm, m->hc_part,
+                                               m->hc_cnt, hc, c.hidden, c.hc_sinkhorn_iters, c.hc_eps,
+                                               c.rms_eps);
+        return 0;
+    }
     k_hc_mix<<<mix, 256, 0, st>>>(m->mixes, fn, m->h, n, c.rms_eps);
     k_hc_finish<<<1, 256, 0, st>>>(m->x1, m->post, m->comb, m->mixes, m->h, scale, base, hc, c.hidden,
                                    c.hc_sinkhorn_iters, c.hc_eps);
+    k_rmsnorm<<<1, 1024, 0, st>>>(m->x1, m->x1, norm, c.hidden, c.rms_eps);
     return 0;
 }
 
@@ -261,25 +292,35 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
         const float *cs = l.ratio ? m->cs_c : m->cs_d, *sn = l.ratio ? m->sn_c : m->sn_d;
         // ---- attention half (src/model/dsv4_layer.c:495-509)
         cudaMemcpyAsync(m->resid, m->h, (size_t)wide * 4, cudaMemcpyDeviceToDevice, st);
-        hc_pre(m, l.hca_fn, l.hca_base, l.hca_scale, st);
-        k_rmsnorm<<<1, 1024, 0, st>>>(m->x1, m->x1, l.attn_norm, d, c.rms_eps);
-        rc |= G(l.wq_a, m->qr, m->x1, st);
+        hc_pre(m, l.hca_fn, l.hca_base, l.hca_scale, l.attn_norm, st);
+        // every projection of x1 in one launch, then both of the normalised q latent
+        {
+            Grp ga;
+            grp_add(ga, l.wq_a, m->x1, m->qr, st);
+            grp_add(ga, l.wkv, m->x1, m->kv, st);
+            if (l.has_comp) {
+                grp_add(ga, l.cwkv, m->x1, m->comp_in, st);
+                grp_add(ga, l.cwgate, m->x1, m->comp_sc, st);
+            }
+            if (l.has_idx) grp_add(ga, l.iwproj, m->x1, m->idx_w, st);
+            rc |= grp_run(ga, st);
+        }
         k_rmsnorm<<<1, 1024, 0, st>>>(m->qr, m->qr, l.q_norm, c.q_lora, c.rms_eps);
-        rc |= G(l.wq_b, m->q, m->qr, st);
+        {
+            Grp gb;
+            grp_add(gb, l.wq_b, m->qr, m->q, st);
+            if (l.has_idx) grp_add(gb, l.iwq_b, m->qr, m->idx_q, st);
+            rc |= grp_run(gb, st);
+        }
         k_heads_norm_rope<<<H, 256, 0, st>>>(m->q, hd, rd, cs, sn, m->st, 0, 0, 1, c.rms_eps);
-        rc |= G(l.wkv, m->kv, m->x1, st);
         k_kv_finish<<<1, 256, 0, st>>>(m->kv, l.kv_norm, hd, rd, cs, sn, m->st, c.rms_eps, l.kv_cache, win);
         if (l.has_comp) {
-            rc |= G(l.cwkv, m->comp_in, m->x1, st);
-            rc |= G(l.cwgate, m->comp_sc, m->x1, st);
             k_compress<<<1, 512, hd * 4, st>>>(l.kv_cache, l.comp_kv, l.comp_score, m->comp_in, m->comp_sc, l.ape,
                                                l.cnorm, l.ratio, hd, rd, cs, sn, m->st, c.rms_eps, win,
                                                c.index_topk, l.dyn);
             if (l.has_idx) {
                 const int ih = c.index_n_heads, id = c.index_head_dim;
-                rc |= G(l.iwq_b, m->idx_q, m->qr, st);
                 k_heads_norm_rope<<<ih, 128, 0, st>>>(m->idx_q, id, rd, cs, sn, m->st, 0, 0, 0, c.rms_eps);
-                rc |= G(l.iwproj, m->idx_w, m->x1, st);
                 const float scale = (1.0f / sqrtf((float)id)) * (1.0f / sqrtf((float)ih));
                 // the compressed region read as contiguous rows of index_head_dim
                 // floats, as the reference does (dsv4_layer.c:286-289)
@@ -292,22 +333,28 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
         rc |= sparse_attn(m->o, m->q, l.kv_cache, DSV4B_DT_F32, (long)l.kv_rows, l.sink, m->idxs, m->nidx, H, hd,
                           m->nidx, 1.0f / sqrtf((float)hd), 1, m->attn_part, st);
         k_heads_norm_rope<<<H, 256, 0, st>>>(m->o, hd, rd, cs, sn, m->st, 0, 1, 0, c.rms_eps);
-        // grouped low-rank output (dsv4_layer.c:303-335)
-        const int gw = H * hd / c.o_groups, gr = c.o_lora;
-        for (int g = 0; g < c.o_groups; g++) {
+        // grouped low-rank output (dsv4_layer.c:303-335): the o_groups row
+        // slices of wo_a, each on its own slice of o, in one launch
+        {
+            const int gw = H * hd / c.o_groups, gr = c.o_lora;
             const DevMat &wa = l.wo_a;
             const size_t rb = row_bytes(wa.wdt, wa.cols);
-            const uint8_t *ws = wa.w + (size_t)g * gr * rb;
-            const uint8_t *ss = wa.s ? wa.s + (size_t)(g * gr / wa.blk_r) * ((wa.cols + wa.blk_c - 1) / wa.blk_c) : nullptr;
-            rc |= gemv(wa.wdt, m->ogrp + (size_t)g * gr, gr, m->o + (size_t)g * gw, gw, ws, ss, gr, gw, wa.blk_r,
-                       wa.blk_c, 1, st);
+            Grp go;
+            for (int g = 0; g < c.o_groups; g++) {
+                DevMat sl = wa;
+                sl.w = wa.w + (size_t)g * gr * rb;
+                sl.s = wa.s ? wa.s + (size_t)(g * gr / wa.blk_r) * ((wa.cols + wa.blk_c - 1) / wa.blk_c) : nullptr;
+                sl.rows = gr;
+                sl.cols = gw;
+                grp_add(go, sl, m->o + (size_t)g * gw, m->ogrp + (size_t)g * gr, st);
+            }
+            rc |= grp_run(go, st);
         }
         rc |= G(l.wo_b, m->blk, m->ogrp, st);
         k_hc_post<<<(wide + 255) / 256, 256, 0, st>>>(m->h, m->blk, m->resid, m->post, m->comb, hc, d);
         // ---- FFN half: the residual is taken after attention (:511-522)
         cudaMemcpyAsync(m->resid, m->h, (size_t)wide * 4, cudaMemcpyDeviceToDevice, st);
-        hc_pre(m, l.hcf_fn, l.hcf_base, l.hcf_scale, st);
-        k_rmsnorm<<<1, 1024, 0, st>>>(m->x1, m->x1, l.ffn_norm, d, c.rms_eps);
+        hc_pre(m, l.hcf_fn, l.hcf_base, l.hcf_scale, l.ffn_norm, st);
         rc |= moe_forward(l.moe, m->ms, m->blk, m->x1, &m->st->token, st);
         k_hc_post<<<(wide + 255) / 256, 256, 0, st>>>(m->h, m->blk, m->resid, m->post, m->comb, hc, d);
     }
@@ -689,6 +736,22 @@ extern "C" int dsv4_cuda_model_decode(dsv4b_model *m, int token, int pos, int *n
     DSV4B_CUDA_OK(cudaMemcpyAsync(next_token, m->out_tokens + pos, 4, cudaMemcpyDeviceToHost, m->stream));
     DSV4B_CUDA_OK(cudaStreamSynchronize(m->stream));
     return 0;
+}
+
+extern "C" int dsv4_cuda_model_step_kernels(const dsv4b_model *m)
+{
+    if (!m || !m->graphed) return -1;
+    size_t n = 0;
+    if (cudaGraphGetNodes(m->graph, nullptr, &n) != cudaSuccess) return -1;
+    std::vector<cudaGraphNode_t> nodes(n);
+    if (n && cudaGraphGetNodes(m->graph, nodes.data(), &n) != cudaSuccess) return -1;
+    int k = 0;
+    for (size_t i = 0; i < n; i++) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(nodes[i], &t) != cudaSuccess) return -1;
+        k += t == cudaGraphNodeTypeKernel;
+    }
+    return k;
 }
 
 extern "C" size_t dsv4_cuda_model_bytes(const dsv4b_model *m)

@@ -22,6 +22,11 @@ __global__ void k_embed(float *h, const void *table, int wdt, const StepState *s
 __global__ void k_hc_mix(float *mixes, const float *fn, const float *x, int n, float eps);
 __global__ void k_hc_finish(float *y, float *post, float *comb, const float *mixes, const float *x,
                             const float *scale, const float *base, int hc, int hidden, int iters, float eps);
+constexpr int kHcPreMixMax = 24;   // (2 + hc) * hc for hc <= 4
+constexpr int kHcPreBlocks = 64;
+__global__ void k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, const float *scale,
+                         const float *base, const float *norm_w, double *part, unsigned *count, int hc, int hidden,
+                         int iters, float hc_eps, float rms_eps);
 __global__ void k_hc_head_finish(float *y, const float *mixes, const float *x, const float *scale,
                                  const float *base, int hc, int hidden, float eps);
 __global__ void k_hc_post(float *y, const float *x, const float *res, const float *post, const float *comb,

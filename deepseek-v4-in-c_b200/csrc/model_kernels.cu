@@ -116,6 +116,116 @@ __global__ void k_hc_finish(float *y, float *post, float *comb, const float *mix
     }
 }
 
+// The whole mHC pre-mix of one sub-layer in one launch, with the sub-layer's
+// RMSNorm folded in (src/core/dsv4_hc.c:118-140 with dsv4_hc_split_sinkhorn
+// :50-102, then src/core/dsv4_ops.c:25-32 when norm_w is given):
+//   every block: double partial sums of x.x and fn[m].x over its columns,
+//                written to part[block][0..mix];
+//   last block:  the partials summed in block order, mixes, the Sinkhorn
+//                split (lanes of one warp, each lane one comb entry; every
+//                row / column sum is gathered by shuffles and added in the
+//                serial order), y = sum_j pre[j] x[j] in double, RMSNorm.
+// The last block is the one whose arrival at *count completes the grid; it
+// resets *count, so the kernel is replayable. hc * hc <= 32.
+__global__ void __launch_bounds__(256)
+k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, const float *scale,
+         const float *base, const float *norm_w, double *part, unsigned *count, int hc, int hidden,
+         int iters, float hc_eps, float rms_eps)
+{
+    constexpr int MIXMAX = kHcPreMixMax;
+    __shared__ double red[8][MIXMAX + 1];
+    __shared__ double tot[MIXMAX + 1];
+    __shared__ float mixes[MIXMAX], pre[DSV4B_MAX_HC];
+    __shared__ bool last;
+    const int n = hc * hidden, mix = (2 + hc) * hc, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    double acc[MIXMAX + 1];
+#pragma unroll
+    for (int m = 0; m <= MIXMAX; m++) acc[m] = 0.0;
+    for (int i = blockIdx.x * blockDim.x + tid; i < n; i += gridDim.x * blockDim.x) {
+        const double xv = (double)x[i];
+        acc[MIXMAX] = __fma_rn(xv, xv, acc[MIXMAX]);
+#pragma unroll
+        for (int m = 0; m < MIXMAX; m++)
+            if (m < mix) acc[m] = __fma_rn((double)__ldg(fn + (size_t)m * n + i), xv, acc[m]);
+    }
+#pragma unroll
+    for (int m = 0; m <= MIXMAX; m++) {
+        const double v = warp_sum_d(acc[m]);
+        if (lane == 0) red[w][m] = v;
+    }
+    __syncthreads();
+    if (tid <= MIXMAX) {
+        double t = 0.0;
+        for (int k = 0; k < (int)(blockDim.x >> 5); k++) t += red[k][tid];
+        part[(size_t)blockIdx.x * (MIXMAX + 1) + tid] = t;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = atomicAdd(count, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (tid <= MIXMAX) {
+        double t = 0.0;
+        for (int b = 0; b < (int)gridDim.x; b++) t += __ldcg(part + (size_t)b * (MIXMAX + 1) + tid);
+        tot[tid] = t;
+    }
+    __syncthreads();
+    if (tid == 0) *count = 0u;
+    if (tid < 32) {
+        const float rs = (float)(1.0 / sqrt(tot[MIXMAX] / (double)n + (double)rms_eps));
+        if (tid < mix) mixes[tid] = __fmul_rn((float)tot[tid], rs);
+    }
+    __syncwarp();
+    if (tid < 32) {
+        const int l = tid, j = l / hc, k = l % hc;
+        const bool act = l < hc * hc;
+        if (l < hc) {
+            pre[l] = __fadd_rn(sigm(__fadd_rn(__fmul_rn(mixes[l], scale[0]), base[l])), hc_eps);
+            post[l] = __fmul_rn(2.0f, sigm(__fadd_rn(__fmul_rn(mixes[l + hc], scale[1]), base[l + hc])));
+        }
+        const int o = 2 * hc + (act ? l : 0);
+        float v = __fadd_rn(__fmul_rn(mixes[o], scale[2]), base[o]);
+        // row softmax: max, exp, double sum in k order, scale, + eps
+        float mx = __shfl_sync(0xffffffffu, v, (j * hc) & 31);
+        for (int kk = 1; kk < hc; kk++) {
+            const float r = __shfl_sync(0xffffffffu, v, (j * hc + kk) & 31);
+            if (r > mx) mx = r;
+        }
+        const float e = expf(v - mx);
+        double sum = 0.0;
+        for (int kk = 0; kk < hc; kk++) sum += (double)__shfl_sync(0xffffffffu, e, (j * hc + kk) & 31);
+        const float inv = (float)(1.0 / sum);
+        v = __fadd_rn(__fmul_rn(e, inv), hc_eps);
+        const int npass = iters > 1 ? iters : 1;
+        for (int pass = 0; pass < npass; pass++) {
+            if (pass > 0) {
+                double r = 0.0;
+                for (int kk = 0; kk < hc; kk++) r += (double)__shfl_sync(0xffffffffu, v, (j * hc + kk) & 31);
+                v = __fdiv_rn(v, __fadd_rn((float)r, hc_eps));
+            }
+            double c = 0.0;
+            for (int jj = 0; jj < hc; jj++) c += (double)__shfl_sync(0xffffffffu, v, (jj * hc + k) & 31);
+            v = __fdiv_rn(v, __fadd_rn((float)c, hc_eps));
+        }
+        if (act) comb[l] = v;
+    }
+    __syncthreads();
+    double sq = 0.0;
+    for (int d = tid; d < hidden; d += blockDim.x) {
+        double a = 0.0;
+        for (int j = 0; j < hc; j++) a = __dadd_rn(a, __dmul_rn((double)pre[j], (double)x[(size_t)j * hidden + d]));
+        const float yv = (float)a;
+        y[d] = yv;
+        sq = __fma_rn((double)yv, (double)yv, sq);
+    }
+    if (!norm_w) return;
+    __shared__ double nred[33];
+    sq = block_sum_d(sq, nred);
+    const float inv = (float)(1.0 / sqrt(sq / (double)hidden + (double)rms_eps));
+    for (int d = tid; d < hidden; d += blockDim.x) y[d] = __fmul_rn(norm_w[d], __fmul_rn(y[d], inv));
+}
+
 // The head's reduction: a sigmoid gate per copy, one scalar scale, no
 // Sinkhorn (src/cli/dsv4_run.c:94-116). One block.
 __global__ void k_hc_head_finish(float *y, const float *mixes, const float *x, const float *scale,

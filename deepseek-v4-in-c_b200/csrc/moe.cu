@@ -82,23 +82,6 @@ __global__ void k_route(const float *logits, const float *bias, const int *fixed
     }
 }
 
-// SwiGLU with the reference's asymmetric clamp (dsv4_ops.c:60-78): up is
-// clamped to +-limit, gate from above only; limit <= 0 disables both.
-__device__ __forceinline__ float swiglu1(float g, float u, float limit)
-{
-    if (limit > 0.0f) {
-        u = fmaxf(fminf(u, limit), -limit);
-        g = fminf(g, limit);
-    }
-    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
-}
-
-__global__ void k_swiglu(float *h, const float *g, const float *u, int n, float limit)
-{
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) h[i] = swiglu1(g[i], u[i], limit);
-}
-
 // out[i] = sum_k w[k] * acc[k][i] in k order, each product and sum rounded
 // separately (dsv4_layer.c:471-475), then + shared[i] (:479-483).
 __global__ void k_combine(float *out, const float *acc, const float *w, int topk, int hidden,
@@ -116,36 +99,51 @@ int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float 
                 const int *token, cudaStream_t st)
 {
     const int H = L.hidden, I = L.inter, K = L.topk;
-    if (K < 1 || K > kMoeMaxTopk || L.n_experts > kMoeMaxExperts) return -1;
+    if (K < 1 || K + 1 > kGemvMaxItems || K > kMoeMaxTopk || L.n_experts > kMoeMaxExperts) return -1;
     // router
     if (gemv(L.gate.wdt, S.logits, L.n_experts, x, H, L.gate.w, L.gate.s, L.n_experts, H,
              L.gate.blk_r, L.gate.blk_c, 1, st))
         return -1;
     k_route<<<1, 256, 0, st>>>(S.logits, L.bias, L.fixed, L.tid2eid, token, L.n_experts, K,
                                L.route_scale, L.score_func, S.sel, S.wts);
-    // gate / up of the selected experts
-    for (int k = 0; k < K; k++) {
-        if (gemv_sel(L.efmt, S.g + (size_t)k * I, x, L.w1tab, L.s1tab, S.sel, k, I, H, L.eblk_r, L.eblk_c, st))
-            return -1;
-        if (gemv_sel(L.efmt, S.u + (size_t)k * I, x, L.w3tab, L.s3tab, S.sel, k, I, H, L.eblk_r, L.eblk_c, st))
-            return -1;
-    }
     const int Is = L.has_shared ? L.inter_shared : 0;
-    float *gs = S.g + (size_t)K * I, *us = S.u + (size_t)K * I, *hs = S.h + (size_t)K * I;
-    if (Is) {
-        if (gemv(L.sh[0].wdt, gs, Is, x, H, L.sh[0].w, L.sh[0].s, Is, H, L.sh[0].blk_r, L.sh[0].blk_c, 1, st)) return -1;
-        if (gemv(L.sh[1].wdt, us, Is, x, H, L.sh[1].w, L.sh[1].s, Is, H, L.sh[1].blk_r, L.sh[1].blk_c, 1, st)) return -1;
-    }
-    const int n = K * I + Is;
-    k_swiglu<<<(n + 255) / 256, 256, 0, st>>>(S.h, S.g, S.u, n, L.swiglu_limit);
-    // down
-    for (int k = 0; k < K; k++)
-        if (gemv_sel(L.efmt, S.acc + (size_t)k * H, S.h + (size_t)k * I, L.w2tab, L.s2tab, S.sel, k, H, I,
-                     L.eblk_r, L.eblk_c, st))
+    float *hs = S.h + (size_t)K * I, *accs = S.acc + (size_t)K * H;
+    GemvItem it[kGemvMaxItems];
+    // gate / up of every selected expert and the shared one, SwiGLU in the
+    // epilogue: h[k] = swiglu(w1 x, w3 x) (dsv4_layer.c:199-206)
+    for (int k = 0; k < K; k++) {
+        if (!gemv_item(it[k], L.efmt, nullptr, nullptr, I, H, L.eblk_r, L.eblk_c, x, S.h + (size_t)k * I))
             return -1;
-    float *accs = S.acc + (size_t)K * H;
-    if (Is && gemv(L.sh[2].wdt, accs, H, hs, Is, L.sh[2].w, L.sh[2].s, H, Is, L.sh[2].blk_r, L.sh[2].blk_c, 1, st))
-        return -1;
+        it[k].wtab = L.w1tab; it[k].stab = L.s1tab;
+        it[k].w2tab = L.w3tab; it[k].s2tab = L.s3tab;
+        it[k].sel = S.sel; it[k].slot = k;
+        it[k].pair = 1; it[k].limit = L.swiglu_limit;
+    }
+    int n = K;
+    if (Is) {
+        if (!gemv_item(it[n], L.sh[0].wdt, L.sh[0].w, L.sh[0].s, Is, H, L.sh[0].blk_r, L.sh[0].blk_c, x, hs) ||
+            L.sh[1].wdt != L.sh[0].wdt)
+            return -1;
+        it[n].W2 = L.sh[1].w; it[n].S2 = L.sh[1].s;
+        it[n].pair = 1; it[n].limit = L.swiglu_limit;
+        n++;
+    }
+    if (gemv_group(it, n, st)) return -1;
+    // down projections into the per-k accumulators
+    for (int k = 0; k < K; k++) {
+        if (!gemv_item(it[k], L.efmt, nullptr, nullptr, H, I, L.eblk_r, L.eblk_c, S.h + (size_t)k * I,
+                       S.acc + (size_t)k * H))
+            return -1;
+        it[k].wtab = L.w2tab; it[k].stab = L.s2tab;
+        it[k].sel = S.sel; it[k].slot = k;
+    }
+    n = K;
+    if (Is) {
+        if (!gemv_item(it[n], L.sh[2].wdt, L.sh[2].w, L.sh[2].s, H, Is, L.sh[2].blk_r, L.sh[2].blk_c, hs, accs))
+            return -1;
+        n++;
+    }
+    if (gemv_group(it, n, st)) return -1;
     k_combine<<<(H + 255) / 256, 256, 0, st>>>(out, S.acc, S.wts, K, H, Is ? accs : nullptr);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }

@@ -83,6 +83,7 @@ def _declare(L):
         "dsv4_cuda_model_decode": ([vp, i, i, vp], i),
         "dsv4_cuda_model_create_synthetic": ([vp, i, C.c_ulonglong], vp),
         "dsv4_cuda_model_bytes": ([vp], sz),
+        "dsv4_cuda_model_step_kernels": ([vp], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

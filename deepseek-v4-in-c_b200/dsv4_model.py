@@ -212,7 +212,7 @@ class SyntheticModel:
 
     def fp8(self, rows, cols, sigma):
         if self.fast:
-            W = np.frombuffer(self.rng.bytes(rows * cols), np.uint8).reshape(rows, cols) & np.uint8(0xF7)
+            W = self.fast_bytes(rows * cols).reshape(rows, cols) & np.uint8(0xF7)
             S = np.full((-(-rows // 128), -(-cols // 128)), 117, np.uint8)
         else:
             W, S = Q.quant_fp8(self.rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(sigma), 128)
@@ -221,15 +221,36 @@ class SyntheticModel:
 
     def fp4(self, rows, cols, sigma):
         if self.fast:
-            W = np.frombuffer(self.rng.bytes(rows * cols // 2), np.uint8).reshape(rows, cols // 2)
+            W = self.fast_bytes(rows * cols // 2).reshape(rows, cols // 2)
             S = np.full((rows, cols // 32), 121, np.uint8)
         else:
             W, S = Q.quant_fp4(self.rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(sigma))
         self.keep += [W, S]
         return QMat(W.ctypes.data, S.ctypes.data, WFP4, rows, cols, 1, 32)
 
+    _POOL = 1 << 26
+
+    def fast_bytes(self, n):
+        """n pseudo-random bytes: a window of a 64 MiB random pool at a random
+        offset (fast mode; distinct buffers, values irrelevant)."""
+        if not hasattr(self, "_pool"):
+            self._pool = np.frombuffer(self.rng.bytes(self._POOL), np.uint8)
+        out = np.empty(n, np.uint8)
+        i = 0
+        while i < n:
+            off = int(self.rng.integers(0, self._POOL))
+            k = min(n - i, self._POOL - off)
+            out[i:i + k] = self._pool[off:off + k]
+            i += k
+        return out
+
     def bf16raw(self, rows, cols, sigma):
-        W = Q.bf16_encode(self.rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(sigma))
+        if self.fast:       # random sign and mantissa, magnitude in [sigma/2, sigma) rounded to a power of 2
+            e = int(np.clip(np.floor(np.log2(sigma)) + 127, 1, 254))
+            W = (self.fast_bytes(rows * cols * 2).view(np.uint16).reshape(rows, cols)
+                 & np.uint16(0x807F)) | np.uint16(e << 7)
+        else:
+            W = Q.bf16_encode(self.rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(sigma))
         self.keep.append(W)
         return W.ctypes.data
 

@@ -302,3 +302,25 @@ def model_greedy_ref(sm, tokens, n_gen, max_pos):
     if n < 0:
         raise RuntimeError("reference driver failed")
     return out[:n], lg[:n]
+
+
+def model_decode_timed_ref(sm, n_pos, first_token=1, max_pos=None):
+    """Per-layer and head wall times (seconds) of the REFERENCE's decode loop
+    (dsv4_layer_forward per layer, then hc_head + norm + LM head + argmax)
+    over positions 0..n_pos-1 of model sm. Returns (t_layer [n_pos][n_layers],
+    t_head [n_pos], tokens)."""
+    lib = C.CDLL(REF_SO)
+    f = lib.dsv4ref_decode_timed
+    f.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i, _i32p,
+                  np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS"),
+                  np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")]
+    f.restype = _i
+    nl = sm.d["n_layers"]
+    tl = np.zeros((n_pos, nl), np.float64)
+    th = np.zeros(n_pos, np.float64)
+    out = np.empty(n_pos, np.int32)
+    n = f(C.addressof(sm.cfg), C.addressof(sm.mw), C.addressof(sm.layers), C.addressof(sm.experts),
+          max_pos or n_pos + 1, int(first_token), n_pos, out, tl, th)
+    if n < 0:
+        raise RuntimeError("reference driver failed")
+    return tl, th, out[:n]

@@ -10,6 +10,7 @@
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
 
 #include "dsv4.h"
 #include "dsv4_layer.h"
@@ -47,11 +48,16 @@ static void hc_head(float *y, const float *x, const DSV4HcW *w, int hc, int hidd
     }
 }
 
-/* tokens[0..n_prompt) is the prompt; positions run 0..n_prompt+n_gen-1 and
- * every position from n_prompt-1 on emits a greedy token into out_tokens and
- * (if logits != NULL) its logits row. Returns the number of tokens emitted. */
-int dsv4ref_greedy(const DSV4Cfg *c, const DSV4ModelW *mw, const DSV4LayerW *lw, const DSV4ExpertW *ex,
-                   int max_pos, const int *tokens, int n_prompt, int n_gen, int *out_tokens, float *logits)
+static double now_s(void)
+{
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return (double)ts.tv_sec + 1e-9 * (double)ts.tv_nsec;
+}
+
+static int run(const DSV4Cfg *c, const DSV4ModelW *mw, const DSV4LayerW *lw, const DSV4ExpertW *ex, int max_pos,
+               const int *tokens, int n_prompt, int n_gen, int *out_tokens, float *logits, double *t_layer,
+               double *t_head)
 {
     const int hc = c->hc_mult, d = c->hidden, half = c->qk_rope / 2;
     float *cs_d = malloc((size_t)max_pos * half * 4), *sn_d = malloc((size_t)max_pos * half * 4);
@@ -77,9 +83,12 @@ int dsv4ref_greedy(const DSV4Cfg *c, const DSV4ModelW *mw, const DSV4LayerW *lw,
         for (int j = 0; j < hc; j++) memcpy(h + (size_t)j * d, xh, (size_t)d * 4);
         for (int L = 0; L < c->n_layers; L++) {
             const int comp = dsv4_compress_ratio(c, L) != 0;
+            const double t0 = t_layer ? now_s() : 0.0;
             dsv4_layer_forward(h, &lw[L], c, &s, &es, &st[L], comp ? cs_c : cs_d, comp ? sn_c : sn_d, pos, tid);
+            if (t_layer) t_layer[(size_t)pos * c->n_layers + L] = now_s() - t0;
         }
         if (pos + 1 >= n_prompt) {
+            const double t0 = t_head ? now_s() : 0.0;
             hc_head(xh, h, &mw->hc_head, hc, d, c->rms_eps, c->hc_eps);
             dsv4_rmsnorm(xh, xh, mw->norm, d, c->rms_eps);
             DSV4QMat head = { mw->head, NULL, mw->wdt, c->vocab, d, 0, 0 };
@@ -90,10 +99,29 @@ int dsv4ref_greedy(const DSV4Cfg *c, const DSV4ModelW *mw, const DSV4LayerW *lw,
             out_tokens[emitted] = best;
             if (logits) memcpy(logits + (size_t)emitted * c->vocab, lg, (size_t)c->vocab * 4);
             emitted++;
+            if (t_head) t_head[pos] = now_s() - t0;
         }
     }
     for (int L = 0; L < c->n_layers; L++) dsv4_state_free(&st[L]);
     free(st); dsv4_scratch_free(&s);
     free(cs_d); free(sn_d); free(cs_c); free(sn_c); free(h); free(xh); free(lg); free(ids);
     return emitted;
+}
+
+/* tokens[0..n_prompt) is the prompt; positions run 0..n_prompt+n_gen-1 and
+ * every position from n_prompt-1 on emits a greedy token into out_tokens and
+ * (if logits != NULL) its logits row. Returns the number of tokens emitted. */
+int dsv4ref_greedy(const DSV4Cfg *c, const DSV4ModelW *mw, const DSV4LayerW *lw, const DSV4ExpertW *ex,
+                   int max_pos, const int *tokens, int n_prompt, int n_gen, int *out_tokens, float *logits)
+{
+    return run(c, mw, lw, ex, max_pos, tokens, n_prompt, n_gen, out_tokens, logits, NULL, NULL);
+}
+
+/* The same loop from a one-token prompt for n_pos positions, timing each
+ * layer call (t_layer[pos * n_layers + L], seconds) and each head + argmax
+ * (t_head[pos]): the CPU baseline of the decode benchmark. */
+int dsv4ref_decode_timed(const DSV4Cfg *c, const DSV4ModelW *mw, const DSV4LayerW *lw, const DSV4ExpertW *ex,
+                         int max_pos, int first_token, int n_pos, int *out_tokens, double *t_layer, double *t_head)
+{
+    return run(c, mw, lw, ex, max_pos, &first_token, 1, n_pos - 1, out_tokens, NULL, t_layer, t_head);
 }

@@ -159,8 +159,9 @@ def test_misuse_is_refused(dev):
                                            (B.WF32, 70, 1000), (B.WFP4, 260, 4096),
                                            (B.WFP8, 16, 16384), (B.WBF16, 1000, 4096)])
 def test_single_and_batched_bit_identical_all_formats(dev, port, fmt, rows, cols):
-    """Batch-1 calls take the TMA stream, batched calls the register kernel;
-    both sum in the same fixed order, so every token must match bitwise.
+    """Batch-1 calls take the grouped streaming kernel, batched calls the
+    nt-token kernel; both sum in the same fixed order, so every token must
+    match bitwise.
     Shapes include partial chunks and partial 256-byte segments."""
     rng = np.random.default_rng(rows + cols)
     if fmt == B.WFP8:

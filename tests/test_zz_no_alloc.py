@@ -35,7 +35,7 @@ def _case(torch, seed, batch, H, D, N, K):
     return kv, q, sink, idx.cuda()
 
 
-@pytest.mark.parametrize("batch,H,D,N,K", [(1, 64, 576, 4096, 640), (3, 64, 512, 2048, 1024)])
+@pytest.mark.parametrize("batch,H,D,N,K", [(1, 64, 576, 4096, 640), (2, 64, 512, 2048, 512)])
 def test_static_scratch_matches_caller_scratch(batch, H, D, N, K):
     import torch
     B.init()
@@ -62,7 +62,7 @@ def test_static_scratch_rejects_oversize():
     B.init()
     fn = _static_fn()
     H, D, K = 64, 576, 2048
-    batch = 8                                              # 32 chunks x 64 heads x 2316 B x 8 > 8 MiB
+    batch = 8                                              # 64 chunks x 64 heads x 2316 B x 8 > 8 MiB
     assert B.sparse_attn_scratch(H, D, K, batch) > (8 << 20)
     o = torch.empty((batch, H, D), device="cuda")
     rc = fn(o.data_ptr(), o.data_ptr(), o.data_ptr(), B.F32, 1, o.data_ptr(), o.data_ptr(), H, D, K, 1.0, batch,

@@ -177,6 +177,10 @@ dsv4b_model *dsv4_cuda_model_create_synthetic(const DSV4Cfg *c, int max_pos,
 /* Device memory in use (bytes), for reporting the resident model size. */
 size_t dsv4_cuda_model_bytes(const dsv4b_model *m);
 
+/* Kernel launches in one decode step: the kernel nodes of the captured step
+ * graph (copies excluded). -1 before the first dsv4_cuda_model_begin. */
+int dsv4_cuda_model_step_kernels(const dsv4b_model *m);
+
 void dsv4_cuda_model_free(dsv4b_model *m);
 
 /* ===================================================== 2. device API ====== */

@@ -24,6 +24,7 @@ struct Resident {
     uint8_t *dw, *ds;       // device copies
     int wdt, rows, cols, blk_r, blk_c, sc;
     size_t wbytes, sbytes, rowbytes;
+    bool f16s;              // FP4: every scale f16-safe (checked at upload)
 };
 
 struct State {
@@ -36,6 +37,18 @@ struct State {
 State g;
 
 cudaStream_t stream_of(void *s) { return s ? (cudaStream_t)s : g.st; }
+
+thread_local int t_chain = 0;
+thread_local bool t_pdl = false;
+
+bool pdl_enabled()
+{
+    static const bool on = [] {
+        const char *e = getenv("DSV4B_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
 
 static int scale_rows(int rows, int blk_r) { return (rows + blk_r - 1) / blk_r; }
 
@@ -109,7 +122,7 @@ static int host_gemv(float *y, const float *x, const Resident &r, int row0, int 
     DSV4B_CUDA_OK(cudaMemcpyAsync(g.dx, g.hx, xn * sizeof(float), cudaMemcpyHostToDevice, g.st));
     const uint8_t *dw = r.dw + (size_t)row0 * r.rowbytes;
     const uint8_t *ds = r.ds ? r.ds + (size_t)(row0 / r.blk_r) * r.sc : nullptr;
-    if (gemv(r.wdt, g.dy, rows, g.dx, r.cols, dw, ds, rows, r.cols, r.blk_r, r.blk_c, nt, g.st) != 0)
+    if (gemv(r.wdt, g.dy, rows, g.dx, r.cols, dw, ds, rows, r.cols, r.blk_r, r.blk_c, nt, g.st, r.f16s) != 0)
         return -1;
     DSV4B_CUDA_OK(cudaMemcpyAsync(g.hy, g.dy, yn * sizeof(float), cudaMemcpyDeviceToHost, g.st));
     DSV4B_CUDA_OK(cudaStreamSynchronize(g.st));
@@ -190,6 +203,7 @@ extern "C" int dsv4_cuda_upload(const DSV4QMat *m)
     r.rowbytes = row_bytes(m->wdt, m->cols);
     r.wbytes = r.rowbytes * (size_t)m->rows;
     r.sbytes = scaled ? (size_t)scale_rows(m->rows, m->blk_r) * r.sc : 0;
+    r.f16s = m->wdt == DSV4_WFP4 && scaled && fp4_scales_f16((const uint8_t *)m->s, r.sbytes);
     // Headroom, as the reference keeps (dsv4_cuda.cu:317-320).
     if (r.wbytes + r.sbytes + (256u << 20) > dsv4_cuda_free_vram()) return -1;
     if (cudaMalloc(&r.dw, r.wbytes) != cudaSuccess) return -1;
@@ -309,6 +323,7 @@ static bool devmat(const DSV4QMat *m, DevMat &d)
     d.cols = m->cols;
     d.blk_r = r->blk_r;
     d.blk_c = r->blk_c;
+    d.f16s = r->f16s ? 1 : 0;
     return true;
 }
 
@@ -348,6 +363,7 @@ extern "C" dsv4b_moe *dsv4_cuda_moe_prepare(const DSV4QMat *gate, const float *b
     L.score_func = score_func;
     L.swiglu_limit = swiglu_limit;
     std::vector<const uint8_t *> tab((size_t)6 * n_experts, nullptr);
+    L.ef16s = 1;
     for (int e = 0; ok && e < n_experts; e++) {
         const DSV4QMat *x3 = experts + 3 * e;
         for (int j = 0; j < 3 && ok; j++) {
@@ -358,6 +374,7 @@ extern "C" dsv4b_moe *dsv4_cuda_moe_prepare(const DSV4QMat *gate, const float *b
             ok = (d.rows == want_rows && d.cols == want_cols);
             tab[(size_t)(2 * j) * n_experts + e] = d.w;
             tab[(size_t)(2 * j + 1) * n_experts + e] = d.s;
+            L.ef16s &= d.f16s;
         }
     }
     if (ok && shared) {

@@ -65,10 +65,15 @@ __device__ __forceinline__ uint4 ld_stream16(const void *p)
     return r;
 }
 
+// Activations written by the previous kernel: coherent L2 loads. Under
+// programmatic dependent launch a kernel is already running while its
+// predecessor writes, so the read-only (.nc) path, whose contract is data
+// unchanged for the kernel's lifetime, is reserved for weights.
 __device__ __forceinline__ float4 ld_f4(const float *p)
 {
-    return __ldg(reinterpret_cast<const float4 *>(p));
+    return __ldcg(reinterpret_cast<const float4 *>(p));
 }
+__device__ __forceinline__ float ld_act(const float *p) { return __ldcg(p); }
 
 // Packed two-lane FMA (Blackwell FFMA2): c.x += a.x*b.x, c.y += a.y*b.y, each
 // lane a single correctly rounded fma.
@@ -102,6 +107,16 @@ __device__ __forceinline__ float warp_max_f(float v)
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
+
+// ---------------------------------------------- programmatic dependent launch
+// Kernels of a decode step are launched with programmatic stream
+// serialization: each lets its dependents be scheduled as soon as all of its
+// blocks are running (pdl_trigger), and waits for its predecessor to finish
+// and flush (pdl_wait) before reading anything the predecessor wrote or
+// writing anything it may still read. Launched without the attribute, both
+// are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 }  // namespace dsv4b
 

@@ -25,7 +25,8 @@
 namespace dsv4b {
 
 constexpr int kGemvThreads = 256;           // 16 half-warps per block
-constexpr int kGemvSmem = 48 * 1024;        // a block's segment sums
+constexpr int kGemvSmem = 32 * 1024;        // a block's segment sums
+constexpr int kMmaTileSmem = 112 * 1024;    // a tensor-core tile's whole shared memory (two blocks per SM)
 constexpr int kGemvMaxTr = 512;
 
 // SwiGLU with the reference's asymmetric clamp (src/core/dsv4_ops.c:60-78):
@@ -60,24 +61,44 @@ struct TilePtrs {
     const uint8_t *W, *S, *W2, *S2;
 };
 
-// Rows per pass: U * SPH 16-byte loads in flight per thread.
-template <int FMT, int SPH>
-constexpr int kRowsPerPass = 8 / SPH;
+// Async copy of 16 bytes global -> shared, L1 bypassed; valid == false
+// zero-fills the destination and reads nothing.
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool valid)
+{
+    const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sa), "l"(gmem), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Pipeline depth in row steps: NST * SPH 16-byte copies in flight per thread.
+template <int SPH>
+constexpr int kStages = 8 / SPH;
 // Segments per chunk (16 half-warps x SPH): FP4 keeps one segment per
 // half-warp, since two segments' x would take 64 registers.
 template <int FMT>
 constexpr int kChunkSegs = FMT == DSV4B_WFP4 ? 16 : 32;
+constexpr int kGemvRing = 8 * kGemvThreads * 16;        // weight ring bytes
+constexpr int kGemvSRing = 8 * 16 * 16;                 // FP4 scale ring bytes
 
-// Segments [chunk0, chunk0 + cseg) of every virtual row of one tile. SPH
-// segments per half-warp; U rows per pass, so U * SPH loads are in flight.
+// Segments [chunk0, chunk0 + cseg) of every virtual row of one tile. Each
+// half-warp owns SPH segments (their x in registers) and walks its rows
+// through a ring of kStages<SPH> row steps: every lane copies its own 16
+// bytes of each row into the ring and later reads back exactly those bytes,
+// so a lane only waits for its own copies. FP4 scales (16 contiguous bytes
+// per row and segment) are copied by lane 0 of the half-warp and shared
+// after a __syncwarp.
 template <int FMT, int SPH>
 __device__ __forceinline__ void group_chunk(const GemvItem &it, const TilePtrs &t, int tile, int nvr,
-                                            int chunk0, int cseg, int nseg, float *ssum)
+                                            int chunk0, int cseg, int nseg, float *ssum, uint4 *wring,
+                                            uint4 *sring, bool sasync)
 {
     using F = Fmt<FMT>;
-    constexpr int NS = F::NS, E = F::E, U = kRowsPerPass<FMT, SPH>;
+    constexpr int NS = F::NS, E = F::E, NST = kStages<SPH>;
     const int hws = (cseg + SPH - 1) / SPH, rs = 16 / hws;
-    const int hw = threadIdx.x >> 4, li = threadIdx.x & 15;
+    const int tid = threadIdx.x, hw = tid >> 4, li = tid & 15;
     const int slot = hw / hws, grp = hw - slot * hws;
     if (slot >= rs) return;
     const unsigned hm = half_mask();
@@ -91,50 +112,88 @@ __device__ __forceinline__ void group_chunk(const GemvItem &it, const TilePtrs &
         sv[j] = seg[j] < chunk0 + cseg;
         off[j] = seg[j] * 256 + 16 * li;
         lv[j] = sv[j] && off[j] < rb;
+        scol[j] = F::SC ? (((off[j] >> 4) * E) >> it.lbc) : 0;
+    }
+    const int K = slot < nvr ? (nvr - slot + rs - 1) / rs : 0;   // row steps of this slot
+    auto locate = [&](int k, int &row, const uint8_t *&Wm, const uint8_t *&Sm) -> bool {
+        const int v = slot + k * rs;
+        const bool second = it.pair && v >= trh;
+        row = it.pair ? tile * trh + (second ? v - trh : v) : tile * it.tr + v;
+        Wm = second ? t.W2 : t.W;
+        Sm = second ? t.S2 : t.S;
+        return v < nvr && row < it.rows;
+    };
+    auto issue = [&](int k) {
+        if (k < K) {
+            int row;
+            const uint8_t *Wm, *Sm;
+            const bool rv = locate(k, row, Wm, Sm);
+            const int st = k % NST;
+#pragma unroll
+            for (int j = 0; j < SPH; j++) {
+                const bool ok = rv && lv[j];
+                cp_async16(&wring[(st * SPH + j) * kGemvThreads + tid], ok ? Wm + (size_t)row * rb + off[j] : t.W, ok);
+                if (FMT == DSV4B_WFP4 && sasync && li == 0) {
+                    const bool oks = rv && sv[j];
+                    cp_async16(&sring[(st * SPH + j) * 16 + hw], oks ? Sm + (size_t)row * it.sc + scol[j] : t.W, oks);
+                }
+            }
+        }
+        cp_commit();
+    };
+    // the weights do not depend on the previous kernel: start streaming them,
+    // then wait for it before reading x
+#pragma unroll
+    for (int k = 0; k < NST - 1; k++) issue(k);
+    pdl_wait();
+#pragma unroll
+    for (int j = 0; j < SPH; j++) {
         const int e0 = (off[j] >> 4) * E;
-        scol[j] = F::SC ? (e0 >> it.lbc) : 0;
 #pragma unroll
         for (int k = 0; k < NS; k++)
             xr[j][k] = lv[j] ? ld_f4(it.x + e0 + 4 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    for (int v0 = slot; v0 < nvr; v0 += rs * U) {
-        uint4 w[U][SPH];
-        float s[U][SPH];
-        bool rv[U];
+    for (int k = 0; k < K; k++) {
+        issue(k + NST - 1);
+        cp_wait<NST - 1>();
+        __syncwarp(hm);
+        int row;
+        const uint8_t *Wm, *Sm;
+        const bool rv = locate(k, row, Wm, Sm);
+        const int v = slot + k * rs, st = k % NST;
 #pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int v = v0 + u * rs;
-            const bool second = it.pair && v >= trh;
-            const int row = it.pair ? tile * trh + (second ? v - trh : v) : tile * it.tr + v;
-            rv[u] = v < nvr && row < it.rows;
-            const uint8_t *Wm = second ? t.W2 : t.W;
-            const uint8_t *Sm = second ? t.S2 : t.S;
-#pragma unroll
-            for (int j = 0; j < SPH; j++) {
-                const bool ok = rv[u] && lv[j];
-                w[u][j] = ok ? ld_stream16(Wm + (size_t)row * rb + off[j]) : make_uint4(0u, 0u, 0u, 0u);
-                s[u][j] = (F::SC && ok) ? e8m0(ld_nc_u8(Sm + (size_t)(row >> it.lbr) * it.sc + scol[j])) : 1.0f;
+        for (int j = 0; j < SPH; j++) {
+            const bool ok = rv && lv[j];
+            const uint4 w = wring[(st * SPH + j) * kGemvThreads + tid];
+            float s = 1.0f;
+            if (F::SC && ok) {
+                if (FMT == DSV4B_WFP4 && sasync)
+                    s = e8m0(reinterpret_cast<const uint8_t *>(&sring[(st * SPH + j) * 16 + hw])[li]);
+                else
+                    s = e8m0(__ldg(Sm + (size_t)(row >> it.lbr) * it.sc + scol[j]));
             }
+            float q = lane_q1<FMT>(w, xr[j], s);
+            q = seg_sum16(q, hm);
+            if (li == 0 && rv && sv[j]) ssum[v * (nseg + 1) + seg[j]] = q;
         }
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int v = v0 + u * rs;
-#pragma unroll
-            for (int j = 0; j < SPH; j++) {
-                float q = lane_q1<FMT>(w[u][j], xr[j], s[u][j]);
-                q = seg_sum16(q, hm);
-                if (li == 0 && rv[u] && sv[j]) ssum[v * (nseg + 1) + seg[j]] = q;
-            }
-        }
+        __syncwarp(hm);
     }
+    cp_wait<0>();
 }
 
+}  // namespace dsv4b
+
+#include "gemv_mma.cuh"
+
+namespace dsv4b {
+
 template <int FMT>
-__device__ __forceinline__ void group_tile(const GemvItem &it, int tile, float *ssum)
+__device__ __forceinline__ void group_tile(const GemvItem &it, int tile, unsigned char *smem)
 {
     TilePtrs t = {it.W, it.S, it.W2, it.S2};
     if (it.wtab) {
-        const int e = it.sel[it.slot];
+        pdl_wait();                  // the selection comes from the previous kernel
+        const int e = __ldcg(it.sel + it.slot);
         t.W = it.wtab[e];
         t.S = it.stab ? it.stab[e] : nullptr;
         if (it.pair) {
@@ -144,17 +203,24 @@ __device__ __forceinline__ void group_tile(const GemvItem &it, int tile, float *
     }
     const int nseg = (it.rowbytes + 255) >> 8;
     const int nvr = it.tr;
+    uint4 *wring = reinterpret_cast<uint4 *>(smem);
+    uint4 *sring = reinterpret_cast<uint4 *>(smem + kGemvRing);
+    float *ssum = reinterpret_cast<float *>(smem + kGemvRing + kGemvSRing);
+    // FP4 scale rows copy 16 bytes per segment when every segment is whole
+    const bool sasync = FMT == DSV4B_WFP4 && (it.sc & 15) == 0 && ((uintptr_t)t.S & 15) == 0 &&
+                        (!it.pair || ((uintptr_t)t.S2 & 15) == 0);
     constexpr int CMAX = kChunkSegs<FMT>;
     for (int c0 = 0; c0 < nseg; c0 += CMAX) {
         const int cseg = min(CMAX, nseg - c0);
         if constexpr (CMAX > 16) {
             if (cseg > 16) {
-                group_chunk<FMT, 2>(it, t, tile, nvr, c0, cseg, nseg, ssum);
+                group_chunk<FMT, 2>(it, t, tile, nvr, c0, cseg, nseg, ssum, wring, sring, sasync);
                 continue;
             }
         }
-        group_chunk<FMT, 1>(it, t, tile, nvr, c0, cseg, nseg, ssum);
+        group_chunk<FMT, 1>(it, t, tile, nvr, c0, cseg, nseg, ssum, wring, sring, sasync);
     }
+    pdl_wait();                      // idle half-warps too: y is written below
     __syncthreads();
     const int nreal = it.pair ? it.tr >> 1 : it.tr;
     for (int r = threadIdx.x; r < nreal; r += blockDim.x) {
@@ -177,16 +243,23 @@ __device__ __forceinline__ void group_tile(const GemvItem &it, int tile, float *
 __global__ void __launch_bounds__(kGemvThreads, 2)
 k_gemv_group(const __grid_constant__ GemvBatch b)
 {
-    extern __shared__ float ssum[];
+    extern __shared__ __align__(16) unsigned char gsm[];
+    pdl_trigger();
     int i = 0;
     while (i + 1 < b.n && (int)blockIdx.x >= b.it[i + 1].tile0) i++;
     const GemvItem &it = b.it[i];
     const int tile = (int)blockIdx.x - it.tile0;
+    if (it.mma) {
+        if (it.fmt == DSV4B_WFP8) mma_tile<DSV4B_WFP8>(it, tile, gsm);
+        else if (it.fmt == DSV4B_WFP4) mma_tile<DSV4B_WFP4>(it, tile, gsm);
+        else mma_tile<DSV4B_WBF16>(it, tile, gsm);
+        return;
+    }
     switch (it.fmt) {
-    case DSV4B_WF32: group_tile<DSV4B_WF32>(it, tile, ssum); break;
-    case DSV4B_WBF16: group_tile<DSV4B_WBF16>(it, tile, ssum); break;
-    case DSV4B_WFP8: group_tile<DSV4B_WFP8>(it, tile, ssum); break;
-    default: group_tile<DSV4B_WFP4>(it, tile, ssum); break;
+    case DSV4B_WF32: group_tile<DSV4B_WF32>(it, tile, gsm); break;
+    case DSV4B_WBF16: group_tile<DSV4B_WBF16>(it, tile, gsm); break;
+    case DSV4B_WFP8: group_tile<DSV4B_WFP8>(it, tile, gsm); break;
+    default: group_tile<DSV4B_WFP4>(it, tile, gsm); break;
     }
 }
 
@@ -207,6 +280,8 @@ template <int FMT, int NT>
 __global__ void __launch_bounds__(128)
 k_gemv_nt(NtArgs g)
 {
+    pdl_trigger();
+    pdl_wait();
     using F = Fmt<FMT>;
     constexpr int NS = F::NS, E = F::E;
     const int lane = threadIdx.x & 31, half = lane >> 4, li = lane & 15;
@@ -276,6 +351,8 @@ k_gemv_nt(NtArgs g)
 // reference's hand-sized test matrices); every model matrix takes the others.
 __global__ void k_gemv_generic(NtArgs g, int fmt, int blk_r, int blk_c, int nt)
 {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const long warp = (long)((blockIdx.x * (unsigned)blockDim.x + threadIdx.x) >> 5);
     if (warp >= (long)g.rows * nt) return;
@@ -332,7 +409,7 @@ bool gemv_vectorizable(int fmt, const void *W, int cols, int blk_r, int blk_c, c
 }
 
 bool gemv_item(GemvItem &it, int fmt, const void *W, const uint8_t *S, int rows, int cols, int blk_r,
-               int blk_c, const float *x, float *y)
+               int blk_c, const float *x, float *y, bool f16s)
 {
     memset(&it, 0, sizeof it);
     blk_r = blk_r > 0 ? blk_r : 1;
@@ -350,6 +427,24 @@ bool gemv_item(GemvItem &it, int fmt, const void *W, const uint8_t *S, int rows,
     it.sc = fmt >= DSV4B_WFP8 ? (cols + blk_c - 1) / blk_c : 0;
     it.lbr = fmt >= DSV4B_WFP8 ? log2_exact(blk_r) : 0;
     it.lbc = fmt >= DSV4B_WFP8 ? log2_exact(blk_c) : 30;
+    it.mma = gemv_mma_shape(fmt, cols, blk_r, blk_c, f16s) ? 1 : 0;
+    return true;
+}
+
+bool gemv_mma_shape(int fmt, int cols, int blk_r, int blk_c, bool f16s)
+{
+    if (fmt == DSV4B_WF32) return false;
+    const int uc = mma_unit_cols(fmt);
+    if (cols % uc || cols / uc > kMmaMaxBlocks) return false;
+    if (fmt == DSV4B_WFP8) return blk_c >= 128 && log2_exact(blk_c) >= 0 && log2_exact(blk_r) >= 0;
+    if (fmt == DSV4B_WFP4) return f16s && blk_c == 32 && blk_r == 1;
+    return true;
+}
+
+bool fp4_scales_f16(const uint8_t *s, size_t n)
+{
+    for (size_t i = 0; i < n; i++)
+        if (s[i] < 127 - 23 || s[i] > 127 + 12) return false;
     return true;
 }
 
@@ -381,6 +476,30 @@ int gemv_group(GemvItem *items, int n, cudaStream_t st)
             b.it[i] = it;
             continue;
         }
+        if (it.mma) {
+            const int nb = it.cols / mma_unit_cols(it.fmt);
+            // a multiple of 16 virtual rows, within the shared memory budget
+            int cap = (int)((kMmaTileSmem - mma_smem(it.fmt, nb, 0)) / ((size_t)(nb + 1) * 4)) & ~15;
+            cap = cap < 512 ? cap : 512;
+            if (cap < 16) return -1;
+            int tr = ((int)(target / it.rowbytes) + 15) & ~15;
+            tr = tr < 16 ? 16 : (tr > cap ? cap : tr);
+            if (it.pair) {
+                tr = (tr + 31) & ~31;
+                if (tr > cap) tr = cap & ~31;
+                if (tr < 32) tr = 32;
+                if (tr / 2 > it.rows) tr = ((2 * it.rows + 31) & ~31);
+            } else if (tr > it.rows) {
+                tr = (it.rows + 15) & ~15;
+            }
+            it.tr = tr;
+            const int per = it.pair ? tr / 2 : tr;
+            blocks += (it.rows + per - 1) / per;
+            const size_t sm = mma_smem(it.fmt, nb, tr);
+            if (sm > smem) smem = sm;
+            b.it[i] = it;
+            continue;
+        }
         const int nseg = (it.rowbytes + 255) >> 8;
         const int cmax = it.fmt == DSV4B_WFP4 ? 16 : 32;
         const int cseg = nseg < cmax ? nseg : cmax, sph = cseg > 16 ? 2 : 1;
@@ -402,20 +521,27 @@ int gemv_group(GemvItem *items, int n, cudaStream_t st)
         it.tr = tr;
         const int per = it.pair ? tr / 2 : tr;      // real rows per block
         blocks += (it.rows + per - 1) / per;
-        const size_t sm = (size_t)tr * (nseg + 1) * 4;
+        const size_t sm = kGemvRing + kGemvSRing + (size_t)tr * (nseg + 1) * 4;
         if (sm > smem) smem = sm;
         b.it[i] = it;
     }
     if (!blocks) return 0;
-    k_gemv_group<<<blocks, kGemvThreads, smem, st>>>(b);
-    return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(k_gemv_group, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaTileSmem);
+        attr = true;
+    }
+    return launch(k_gemv_group, dim3(blocks), dim3(kGemvThreads), smem, st, b) ==
+                   cudaSuccess
+               ? 0
+               : -1;
 }
 
 template <int FMT, int NT>
 static void launch_nt(const NtArgs &a, cudaStream_t st)
 {
     const int blocks = (a.rows + 3) / 4;
-    k_gemv_nt<FMT, NT><<<blocks, 128, 0, st>>>(a);
+    launch(k_gemv_nt<FMT, NT>, dim3(blocks), dim3(128), 0, st, a);
 }
 
 template <int FMT>
@@ -434,7 +560,7 @@ static void launch_fmt(const NtArgs &a, int nt, cudaStream_t st)
 }
 
 int gemv(int fmt, float *y, long ystride, const float *x, long xstride, const void *W, const uint8_t *S,
-         int rows, int cols, int blk_r, int blk_c, int nt, cudaStream_t st)
+         int rows, int cols, int blk_r, int blk_c, int nt, cudaStream_t st, bool f16s)
 {
     if (rows <= 0 || cols <= 0 || nt <= 0) return 0;
     if (fmt == DSV4B_WFP4 && (cols & 1)) return -1;
@@ -455,12 +581,26 @@ int gemv(int fmt, float *y, long ystride, const float *x, long xstride, const vo
     a.ystride = ystride;
     if (!gemv_vectorizable(fmt, W, cols, blk_r, blk_c, x, xstride)) {
         const long warps = (long)rows * nt;
-        k_gemv_generic<<<(unsigned)((warps * 32 + 127) / 128), 128, 0, st>>>(a, fmt, blk_r, blk_c, nt);
+        launch(k_gemv_generic, dim3((unsigned)((warps * 32 + 127) / 128)), dim3(128), 0, st, a, fmt, blk_r, blk_c, nt);
         return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
     }
     if (nt == 1 && ystride >= rows) {
         GemvItem it;
-        if (gemv_item(it, fmt, W, S, rows, cols, blk_r, blk_c, x, y)) return gemv_group(&it, 1, st);
+        if (gemv_item(it, fmt, W, S, rows, cols, blk_r, blk_c, x, y, f16s)) return gemv_group(&it, 1, st);
+    }
+    if (gemv_mma_shape(fmt, cols, blk_r, blk_c, f16s)) {
+        // the tensor-core order: every token as its own item (same kernel and
+        // arithmetic as a batch-1 call), up to 16 per launch
+        for (int t0 = 0; t0 < nt; t0 += kGemvMaxItems) {
+            const int k = (nt - t0 < kGemvMaxItems) ? nt - t0 : kGemvMaxItems;
+            GemvItem it[kGemvMaxItems];
+            for (int t = 0; t < k; t++)
+                if (!gemv_item(it[t], fmt, W, S, rows, cols, blk_r, blk_c, x + (size_t)(t0 + t) * xstride,
+                               y + (size_t)(t0 + t) * ystride, f16s))
+                    return -1;
+            if (gemv_group(it, k, st)) return -1;
+        }
+        return 0;
     }
     for (int t0 = 0; t0 < nt; t0 += 8) {
         const int k = (nt - t0 < 8) ? nt - t0 : 8;

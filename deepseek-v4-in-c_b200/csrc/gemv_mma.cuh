@@ -1,0 +1,334 @@
+// gemv_mma.cuh - batch-1 GEMV of FP8 (e4m3, 128x128 E8M0 blocks) and BF16
+// weights on the tensor cores: warp-level mma.sync m16n8k16, f32 accumulate.
+//
+// The weights are the A operand: e4m3 codes widen exactly to f16 (one cvt
+// per pair), bf16 weights are used as they are. x is the B operand, split
+// into three pieces that add back to x exactly enough for an f32 dot:
+//   FP8 path:  xs = x * 2^k (k per 128-column block, so that max|xs| lies in
+//              [2^14, 2^15)), hi = f16(xs), lo = f16(xs - hi),
+//              lo2 = f16(xs - hi - lo);
+//   BF16 path: hi = bf16(x), lo = bf16(x - hi), lo2 = bf16(x - hi - lo).
+// The pieces occupy B columns n = 0, 1, 2; every product is exact.
+//
+// Order (the canonical one for these formats, used by every kernel that
+// computes them): a row is cut into blocks of 128 columns. For each block b
+// the tensor core accumulates, from zero, the block's 8 k16-steps into C[n];
+// q_b = (((C[0] + C[1]) + C[2]) * 2^-k) * scale_b in float; the row total is
+// ((0 + q_0) + q_1) + ... in double, in block order; y = (float)total.
+//
+// Work: a block of 8 warps streams a tile of rows (a multiple of 16); a unit
+// is 16 rows x one 128-column block, taken by the warps in turn. Lane
+// (g = lane/4, t = lane%4) loads rows g and g+8 at bytes 64 j + 16 t of the
+// unit row (chunks j = 0..CPL-1) through a ring of cp.async stages it alone
+// reads back; the k index inside a unit is permuted (the dot product does not
+// care) so that these 16-byte chunks are exactly the lane's A fragments.
+#pragma once
+
+#include "gemv_core.cuh"
+#include "internal.h"
+
+namespace dsv4b {
+
+constexpr int kMmaMaxBlocks = 64;                           // blocks per row
+constexpr int kMmaStages = 3;                               // ring steps in flight + 1
+constexpr int kMmaRing = kMmaStages * 4 * 16 * 256;         // 4 chunks of 16 B per lane per step
+constexpr int kMmaSRing = 8 * kMmaStages * 8 * 16;          // FP4 scales: per warp, step and row pair, 16 B
+constexpr int kMmaXpPerMma = 12 * 8;                        // x fragment bytes per mma: (t, piece)
+
+template <int FMT> struct MmaFmt;
+// E: elements per 16 bytes; CPL: 16-byte chunks per lane and row in a unit;
+// STEPS: ring steps per unit (two chunks per row and step); COLS: columns of
+// a unit (one flush block); MPU: k16 steps per unit.
+template <> struct MmaFmt<DSV4B_WFP8> { static constexpr int E = 16, CPL = 2, STEPS = 1, COLS = 128, MPU = 8; };
+template <> struct MmaFmt<DSV4B_WBF16> { static constexpr int E = 8, CPL = 4, STEPS = 2, COLS = 128, MPU = 8; };
+template <> struct MmaFmt<DSV4B_WFP4> { static constexpr int E = 32, CPL = 2, STEPS = 1, COLS = 256, MPU = 16; };
+
+__host__ __device__ inline int mma_unit_cols(int fmt) { return fmt == DSV4B_WFP4 ? 256 : 128; }
+__host__ __device__ inline int mma_unit_mmas(int fmt) { return fmt == DSV4B_WFP4 ? 16 : 8; }
+
+// Dynamic shared memory of a tile of tr virtual rows over nb units.
+__host__ __device__ inline size_t mma_smem(int fmt, int nb, int tr)
+{
+    return (size_t)kMmaRing + kMmaSRing + (size_t)nb * mma_unit_mmas(fmt) * kMmaXpPerMma +
+           (((size_t)nb * 4 + 15) & ~(size_t)15) + (size_t)tr * (nb + 1) * 4;
+}
+
+__device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Two e4m3 codes (low byte first) -> f16x2 bits, exact.
+__device__ __forceinline__ uint32_t e4m3x2_h2(uint32_t v)
+{
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(v & 0xFFFFu), __NV_E4M3);
+    return (uint32_t)h.x | ((uint32_t)h.y << 16);
+}
+
+// One byte of two e2m1 codes (low nibble first) -> f16x2 bits, times the
+// half2 power of two sc (exact while the result stays a normal or subnormal
+// f16: scale exponents -23..12).
+__device__ __forceinline__ uint32_t e2m1x2_h2s(uint32_t v, uint32_t sc)
+{
+    const __half2_raw h = __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)(v & 0xFFu), __NV_E2M1);
+    uint32_t r = (uint32_t)h.x | ((uint32_t)h.y << 16), o;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o) : "r"(r), "r"(sc));
+    return o;
+}
+
+// E8M0 byte -> the f16x2 pair (2^e, 2^e); only called for e in [-24, 15].
+__device__ __forceinline__ uint32_t e8m0_h2(uint32_t b)
+{
+    const int e = (int)b - 127;
+    const uint32_t h = e >= -14 ? (uint32_t)(e + 15) << 10 : (1u << (e + 24));
+    return h | (h << 16);
+}
+
+// 2^e as a float for e in [-126, 127].
+__device__ __forceinline__ float pow2f(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
+
+// The three pieces of four x values, as f16x2 (x pre-scaled by a power of
+// two) or bf16x2 pairs: out[p] = {pair(e0, e1), pair(e2, e3)}.
+template <bool BF>
+__device__ __forceinline__ void x_pieces(const float4 &x, float sc, uint2 (&out)[3])
+{
+    const float v[4] = {x.x * sc, x.y * sc, x.z * sc, x.w * sc};   // sc is a power of two: exact
+    uint16_t p[3][4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        if constexpr (!BF) {
+            const __half h0 = __float2half_rn(v[e]);
+            const float r1 = __fsub_rn(v[e], __half2float(h0));
+            const __half h1 = __float2half_rn(r1);
+            const __half h2 = __float2half_rn(__fsub_rn(r1, __half2float(h1)));
+            p[0][e] = __half_as_ushort(h0);
+            p[1][e] = __half_as_ushort(h1);
+            p[2][e] = __half_as_ushort(h2);
+        } else {
+            const __nv_bfloat16 h0 = __float2bfloat16_rn(v[e]);
+            const float r1 = __fsub_rn(v[e], __bfloat162float(h0));
+            const __nv_bfloat16 h1 = __float2bfloat16_rn(r1);
+            const __nv_bfloat16 h2 = __float2bfloat16_rn(__fsub_rn(r1, __bfloat162float(h1)));
+            p[0][e] = __bfloat16_as_ushort(h0);
+            p[1][e] = __bfloat16_as_ushort(h1);
+            p[2][e] = __bfloat16_as_ushort(h2);
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < 3; q++)
+        out[q] = make_uint2((uint32_t)p[q][0] | ((uint32_t)p[q][1] << 16), (uint32_t)p[q][2] | ((uint32_t)p[q][3] << 16));
+}
+
+template <int FMT>
+__device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned char *smem)
+{
+    using F = MmaFmt<FMT>;
+    constexpr int E = F::E, STEPS = F::STEPS, MPC = E / 4, MPU = F::MPU, UB = F::COLS * 16 / E;   // unit bytes/row
+    constexpr bool BF = FMT == DSV4B_WBF16;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+    const int nb = it.cols / F::COLS, rb = it.rowbytes, trh = it.tr >> 1;
+    uint4 *ring = reinterpret_cast<uint4 *>(smem);
+    uint2 *sring = reinterpret_cast<uint2 *>(smem + kMmaRing);
+    uint2 *xp = reinterpret_cast<uint2 *>(smem + kMmaRing + kMmaSRing);
+    int *kbs = reinterpret_cast<int *>(smem + kMmaRing + kMmaSRing + (size_t)nb * MPU * kMmaXpPerMma);
+    float *qs = reinterpret_cast<float *>(smem + kMmaRing + kMmaSRing + (size_t)nb * MPU * kMmaXpPerMma +
+                                          (((size_t)nb * 4 + 15) & ~(size_t)15));
+
+    const uint8_t *W = it.W, *S = it.S, *W2 = it.W2, *S2 = it.S2;
+    if (it.wtab) {
+        pdl_wait();                  // the selection comes from the previous kernel
+        const int e = __ldcg(it.sel + it.slot);
+        W = it.wtab[e];
+        S = it.stab ? it.stab[e] : nullptr;
+        if (it.pair) {
+            W2 = it.w2tab[e];
+            S2 = it.s2tab ? it.s2tab[e] : nullptr;
+        }
+    }
+    const int nunits = (it.tr >> 4) * nb;
+    const int K = warp < nunits ? (nunits - warp + 7) / 8 : 0;   // units of this warp
+    const int nsteps = K * STEPS;
+
+    // the matrix row of virtual row v, or -1 past the matrix; *second: W2
+    auto row_of = [&](int v, bool &second) -> int {
+        second = it.pair && v >= trh;
+        const int row = it.pair ? tile * trh + (second ? v - trh : v) : tile * it.tr + v;
+        return row < it.rows ? row : -1;
+    };
+    // the unit walk: u = warp + 8k, as (row group, block) without divisions
+    int i_rg = 0, i_cb = warp, i_s = 0, i_q = 0;
+    while (i_cb >= nb) { i_cb -= nb; i_rg++; }
+    auto issue_next = [&]() {
+        if (i_q < nsteps) {
+            const int slot = i_q % kMmaStages;
+#pragma unroll
+            for (int h = 0; h < 2; h++) {                 // rows g, g + 8
+                bool second;
+                const int row = row_of(i_rg * 16 + g + 8 * h, second);
+                const bool ok = row >= 0;
+                const uint8_t *base = (second ? W2 : W) + (size_t)(ok ? row : 0) * rb + (size_t)i_cb * UB;
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    const int j = 2 * i_s + c;
+                    cp_async16(&ring[(slot * 4 + h * 2 + c) * 256 + tid], ok ? base + 64 * j + 16 * t : W, ok);
+                }
+                if (FMT == DSV4B_WFP4 && t == 0) {        // the row's 8 scale bytes of this unit
+                    const uint8_t *sb = (second ? S2 : S) + (size_t)(ok ? row : 0) * it.sc + (size_t)i_cb * 8;
+                    const unsigned sa =
+                        (unsigned)__cvta_generic_to_shared(&sring[((warp * kMmaStages + slot) * 8 + g) * 2 + h]);
+                    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(sa), "l"(ok ? sb : S),
+                                 "r"(ok ? 8 : 0) : "memory");
+                }
+            }
+            if (++i_s == STEPS) {
+                i_s = 0;
+                i_cb += 8;
+                while (i_cb >= nb) { i_cb -= nb; i_rg++; }
+            }
+        }
+        i_q++;
+        cp_commit();
+    };
+#pragma unroll
+    for (int q = 0; q < kMmaStages - 1; q++) issue_next();
+    pdl_wait();
+
+    // x fragments: warp w builds those of units w, w+8, ...; lane = (mma, t)
+    // in two passes for the 16 k16-steps of an FP4 unit
+    for (int cb = warp; cb < nb; cb += 8) {
+        float4 xv[MPU / 8];
+        float mx = 0.0f;
+#pragma unroll
+        for (int h = 0; h < MPU / 8; h++) {
+            const int m = h * 8 + (lane >> 2), tt = lane & 3, j = m / MPC, i = m - j * MPC;
+            xv[h] = ld_f4(it.x + cb * F::COLS + 4 * E * j + E * tt + 4 * i);
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(xv[h].x), fabsf(xv[h].y)), fmaxf(fabsf(xv[h].z), fabsf(xv[h].w))));
+        }
+        mx = warp_max_f(mx);
+        int k = 0;
+        if (!BF && mx > 0.0f && mx == mx) {
+            const int ex = (int)((__float_as_uint(mx) >> 23) & 0xFFu) - 127;   // floor(log2 mx), normal mx
+            k = 14 - (ex < -126 ? -126 : ex);
+            k = k > 126 ? 126 : (k < -126 ? -126 : k);
+        }
+#pragma unroll
+        for (int h = 0; h < MPU / 8; h++) {
+            const int m = h * 8 + (lane >> 2), tt = lane & 3;
+            uint2 pc[3];
+            x_pieces<BF>(xv[h], BF ? 1.0f : pow2f(k), pc);
+#pragma unroll
+            for (int p = 0; p < 3; p++) xp[(cb * MPU + m) * 12 + tt * 3 + p] = pc[p];
+        }
+        if (lane == 0) kbs[cb] = k;
+    }
+    __syncthreads();
+
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    int c_rg = 0, c_cb = warp, c_s = 0;
+    while (c_cb >= nb) { c_cb -= nb; c_rg++; }
+    for (int q = 0; q < nsteps; q++) {
+        issue_next();
+        cp_wait<kMmaStages - 1>();
+        if (FMT == DSV4B_WFP4) __syncwarp();
+        const int slot = q % kMmaStages;
+        // FP8 block scales of the unit's two rows, fetched before the math
+        float sa = 1.0f, sbv = 1.0f;
+        bool s2a = false, s2b = false;
+        const int ra = row_of(c_rg * 16 + g, s2a), rbw = row_of(c_rg * 16 + g + 8, s2b);
+        if (FMT == DSV4B_WFP8 && t == 0 && c_s == STEPS - 1) {
+            const int col = (c_cb * F::COLS) >> it.lbc;
+            sa = ra >= 0 ? e8m0(__ldg((s2a ? S2 : S) + (size_t)(ra >> it.lbr) * it.sc + col)) : 0.0f;
+            sbv = rbw >= 0 ? e8m0(__ldg((s2b ? S2 : S) + (size_t)(rbw >> it.lbr) * it.sc + col)) : 0.0f;
+        }
+        uint4 wv[4];
+#pragma unroll
+        for (int r = 0; r < 4; r++) wv[r] = ring[(slot * 4 + r) * 256 + tid];
+        uint32_t s4a = 0, s4b = 0;
+        if (FMT == DSV4B_WFP4) {                          // scale bytes 4 j + t of rows g, g + 8
+            const uint2 *sr = sring + ((warp * kMmaStages + slot) * 8 + g) * 2;
+            const uint2 sp = sr[0], sq = sr[1];
+            s4a = ((t < 4 ? sp.x >> (8 * t) : 0) & 0xFFu) | (((sp.y >> (8 * t)) & 0xFFu) << 8);
+            s4b = ((sq.x >> (8 * t)) & 0xFFu) | (((sq.y >> (8 * t)) & 0xFFu) << 8);
+        }
+#pragma unroll
+        for (int cc = 0; cc < 2; cc++) {
+            const int j = 2 * c_s + cc;
+            const uint4 &wa = wv[cc], &wb = wv[2 + cc];   // rows g, g + 8
+            uint32_t ha = 0, hb = 0;
+            if (FMT == DSV4B_WFP4) {
+                ha = e8m0_h2((s4a >> (8 * cc)) & 0xFFu);
+                hb = e8m0_h2((s4b >> (8 * cc)) & 0xFFu);
+            }
+#pragma unroll
+            for (int i = 0; i < MPC; i++) {
+                const int m = j * MPC + i;
+                uint2 b = make_uint2(0u, 0u);
+                if (g < 3) b = xp[(c_cb * MPU + m) * 12 + t * 3 + g];
+                if constexpr (FMT == DSV4B_WFP8) {
+                    const uint32_t va = word_of(wa, i), vb = word_of(wb, i);
+                    mma_f16(c, e4m3x2_h2(va), e4m3x2_h2(vb), e4m3x2_h2(va >> 16), e4m3x2_h2(vb >> 16), b.x, b.y);
+                } else if constexpr (FMT == DSV4B_WFP4) {
+                    const uint32_t va = word_of(wa, i >> 1) >> (16 * (i & 1)), vb = word_of(wb, i >> 1) >> (16 * (i & 1));
+                    mma_f16(c, e2m1x2_h2s(va, ha), e2m1x2_h2s(vb, hb), e2m1x2_h2s(va >> 8, ha),
+                            e2m1x2_h2s(vb >> 8, hb), b.x, b.y);
+                } else {
+                    mma_bf16(c, word_of(wa, 2 * i), word_of(wb, 2 * i), word_of(wa, 2 * i + 1),
+                             word_of(wb, 2 * i + 1), b.x, b.y);
+                }
+            }
+        }
+        if (FMT == DSV4B_WFP4) __syncwarp();
+        if (c_s == STEPS - 1) {
+            // flush the unit: rows g and g + 8 sit on lane t = 0 (n = 0, 1)
+            // and lane t = 1 (n = 2)
+            const float n2a = __shfl_sync(0xffffffffu, c[0], lane | 1);
+            const float n2b = __shfl_sync(0xffffffffu, c[2], lane | 1);
+            if (t == 0) {
+                const float un = pow2f(-kbs[c_cb]);
+                const float qa = __fmul_rn(__fmul_rn(__fadd_rn(__fadd_rn(c[0], c[1]), n2a), un), sa);
+                const float qb = __fmul_rn(__fmul_rn(__fadd_rn(__fadd_rn(c[2], c[3]), n2b), un), sbv);
+                qs[(c_rg * 16 + g) * (nb + 1) + c_cb] = qa;
+                qs[(c_rg * 16 + g + 8) * (nb + 1) + c_cb] = qb;
+            }
+            c[0] = c[1] = c[2] = c[3] = 0.f;
+        }
+        if (++c_s == STEPS) {
+            c_s = 0;
+            c_cb += 8;
+            while (c_cb >= nb) { c_cb -= nb; c_rg++; }
+        }
+    }
+    cp_wait<0>();
+    __syncthreads();
+    const int nreal = it.pair ? trh : it.tr;
+    for (int r = tid; r < nreal; r += blockDim.x) {
+        const int row = tile * nreal + r;
+        if (row >= it.rows) break;
+        const float *sr = qs + r * (nb + 1);
+        double tot = 0.0;
+        for (int b = 0; b < nb; b++) tot = __dadd_rn(tot, (double)sr[b]);
+        float a = (float)tot;
+        if (it.pair) {
+            const float *s2 = qs + (r + trh) * (nb + 1);
+            double t2 = 0.0;
+            for (int b = 0; b < nb; b++) t2 = __dadd_rn(t2, (double)s2[b]);
+            a = swiglu_pair(a, (float)t2, it.limit);
+        }
+        it.y[row] = a;
+    }
+}
+
+}  // namespace dsv4b

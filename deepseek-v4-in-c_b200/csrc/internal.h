@@ -21,6 +21,7 @@ struct GemvItem {
     const float *x;
     float *y;
     int fmt, rows, cols, sc, lbr, lbc, rowbytes, slot, pair;
+    int mma;                // on the tensor cores (gemv_mma.cuh)
     float limit;
     int tile0, tr;          // first block of this item; virtual rows per block
 };
@@ -31,21 +32,75 @@ struct GemvBatch {
 };
 
 size_t row_bytes(int fmt, int cols);
+// Whether a matrix takes the tensor-core path: FP8 (column blocks of 128 or
+// more) or BF16 in whole 128-column units, FP4 (1x32 blocks) in whole
+// 256-column units whose scales all lie in 2^-23..2^12 (f16s: the holder of
+// the scales has checked), at most 64 units per row. A function of the
+// matrix only, so one matrix always sums in one order, whatever the batch.
+bool gemv_mma_shape(int fmt, int cols, int blk_r, int blk_c, bool f16s);
+// Whether every E8M0 scale byte lets an e2m1 value times the scale be an
+// exact f16 (exponents -23..12).
+bool fp4_scales_f16(const uint8_t *s, size_t n);
 // An item for W (or the table triple, when W is null) of the given shape;
 // false when the shape cannot take the 128-bit streaming kernels (rows not a
 // multiple of 16 bytes, unaligned pointers, scale blocks not powers of two
 // of at least 4 columns).
 bool gemv_item(GemvItem &it, int fmt, const void *W, const uint8_t *S, int rows, int cols, int blk_r,
-               int blk_c, const float *x, float *y);
+               int blk_c, const float *x, float *y, bool f16s = false);
 // One launch over n <= kGemvMaxItems items (blocks planned here).
 int gemv_group(GemvItem *items, int n, cudaStream_t st);
 bool gemv_vectorizable(int fmt, const void *W, int cols, int blk_r, int blk_c, const float *x, long xstride);
 // y[t*ystride + o] = sum_c W[o][c] * x[t*xstride + c], t < nt, o < rows.
 int gemv(int fmt, float *y, long ystride, const float *x, long xstride, const void *W, const uint8_t *S,
-         int rows, int cols, int blk_r, int blk_c, int nt, cudaStream_t st);
+         int rows, int cols, int blk_r, int blk_c, int nt, cudaStream_t st, bool f16s = false);
 int dump_e4m3(float *dev_out, cudaStream_t st);
 
 // The backend's own stream (NULL stream arguments of the device API).
 cudaStream_t stream_of(void *s);
+
+// Whether kernels are launched as programmatic dependents of their
+// predecessor ($DSV4B_PDL=0 turns it off).
+bool pdl_enabled();
+
+// Programmatic dependent launch is used only inside kernel chains this
+// backend enqueues itself (a decode step, an MoE forward): the first launch
+// of a chain is ordinary -- its predecessor may be a copy, which
+// griddepcontrol.wait does not wait for, or a caller's kernel -- and every
+// later launch of the chain may overlap the kernel before it. Chains nest.
+extern thread_local int t_chain;    // depth of chains being enqueued
+extern thread_local bool t_pdl;     // the next launch follows a kernel of this chain
+struct PdlChain {
+    PdlChain()
+    {
+        if (t_chain++ == 0) t_pdl = false;
+    }
+    ~PdlChain()
+    {
+        if (--t_chain == 0) t_pdl = false;
+    }
+};
+
+// kernel<<<grid, block, smem, st>>>(args...), as a programmatic dependent of
+// the previous kernel when inside a chain; every kernel launched this way
+// starts with pdl_trigger() and calls pdl_wait() before touching its
+// predecessor's data.
+template <typename... KArgs, typename... Args>
+static inline cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                 cudaStream_t st, Args... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = (t_chain > 0 && t_pdl && pdl_enabled()) ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, (KArgs)args...);
+    if (t_chain > 0) t_pdl = true;
+    return e;
+}
 
 }  // namespace dsv4b

@@ -47,6 +47,8 @@ k_indexer_score(float *out, const float *q, const void *keys, int key_dt, long k
                 long seq_key_stride, const float *w, int n_heads, int head_dim, int n_pos,
                 float scale, long seq_q_stride, long seq_out_stride, const int *dyn_n)
 {
+    pdl_trigger();
+    pdl_wait();
     if (dyn_n) n_pos = min(n_pos, *dyn_n);       // rows that exist this step
     if ((int)blockIdx.x * IX_TP >= n_pos) return;
     extern __shared__ double ixs[];
@@ -59,10 +61,35 @@ k_indexer_score(float *out, const float *q, const void *keys, int key_dt, long k
     const char *kb = reinterpret_cast<const char *>(keys);
     const int esz = key_dt == DSV4B_DT_F32 ? 4 : key_dt == DSV4B_DT_BF16 ? 2 : 1;
     kb += (size_t)b * seq_key_stride * esz;
-    for (int i = threadIdx.x; i < n_heads * head_dim; i += blockDim.x) qs[i] = (double)q[i];
-    for (int i = threadIdx.x; i < head_dim * IX_TP; i += blockDim.x) {
-        const int p = i / head_dim, c = i % head_dim;
-        kt[c * IX_TP + p] = (t0 + p < n_pos) ? (double)load_elem(kb, (size_t)(t0 + p) * key_stride + c, key_dt) : 0.0;
+    constexpr int LB = 16;                          // loads in flight per thread
+    const int nq = n_heads * head_dim, nk = head_dim * IX_TP;
+    for (int i0 = threadIdx.x; i0 < nq; i0 += LB * (int)blockDim.x) {
+        float v[LB];
+#pragma unroll
+        for (int u = 0; u < LB; u++) {
+            const int i = i0 + u * (int)blockDim.x;
+            v[u] = i < nq ? ld_act(q + i) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < LB; u++) {
+            const int i = i0 + u * (int)blockDim.x;
+            if (i < nq) qs[i] = (double)v[u];
+        }
+    }
+    for (int i0 = threadIdx.x; i0 < nk; i0 += LB * (int)blockDim.x) {
+        float v[LB];
+#pragma unroll
+        for (int u = 0; u < LB; u++) {
+            const int i = i0 + u * (int)blockDim.x;
+            const int p = i / head_dim, c = i - p * head_dim;
+            v[u] = (i < nk && t0 + p < n_pos) ? load_elem(kb, (size_t)(t0 + p) * key_stride + c, key_dt) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < LB; u++) {
+            const int i = i0 + u * (int)blockDim.x;
+            const int p = i / head_dim, c = i - p * head_dim;
+            if (i < nk) kt[c * IX_TP + p] = (double)v[u];
+        }
     }
     __syncthreads();
     const int p = threadIdx.x & 31, hg = threadIdx.x >> 5;
@@ -105,6 +132,8 @@ __global__ void __launch_bounds__(1024)
 k_topk(int *idx_out, const float *scores, int n, int k, long seq_in_stride, long seq_out_stride,
        const int *dyn_nk)
 {
+    pdl_trigger();
+    pdl_wait();
     if (dyn_nk) { n = min(n, dyn_nk[0]); k = dyn_nk[1]; }
     extern __shared__ uint32_t tks[];
     uint32_t *key = tks;                                   // [n]
@@ -119,28 +148,47 @@ k_topk(int *idx_out, const float *scores, int n, int k, long seq_in_stride, long
     for (int i = tid; i < n; i += nt) key[i] = fkey(scores[i]);
     if (tid == 0) { s_prefix = 0; s_want = (uint32_t)k; }
     __syncthreads();
-    // radix select, 8 bits at a time from the top: find the k-th largest key
+    // radix select, 8 bits at a time from the top: find the k-th largest key.
+    // With k == n every key is taken: threshold 0 (below every non-NaN key).
     uint32_t mask = 0;
-    for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int shift = 24; shift >= 0 && k < n; shift -= 8) {
         for (int i = tid; i < 256; i += nt) hist[i] = 0;
         __syncthreads();
         const uint32_t pre = s_prefix;
         for (int i = tid; i < n; i += nt)
             if ((key[i] & mask) == pre) atomicAdd(&hist[(key[i] >> shift) & 255u], 1u);
         __syncthreads();
-        if (tid == 0) {
-            uint32_t want = s_want, acc = 0;
-            int bin = 255;
-            for (; bin > 0; bin--) {
-                if (acc + hist[bin] >= want) break;
-                acc += hist[bin];
+        // the bin holding the want-th largest: lane l owns bins 255-8l .. 248-8l,
+        // an exclusive scan over lanes finds the lane, the lane walks its bins
+        if (tid < 32) {
+            const uint32_t want = s_want;
+            uint32_t cnt[8], sum = 0;
+#pragma unroll
+            for (int j = 0; j < 8; j++) { cnt[j] = hist[255 - 8 * tid - j]; sum += cnt[j]; }
+            uint32_t incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t u = __shfl_up_sync(0xffffffffu, incl, o);
+                if (tid >= o) incl += u;
             }
-            s_want = want - acc;
-            s_prefix = pre | ((uint32_t)bin << shift);
+            const uint32_t excl = incl - sum;
+            if (excl < want && want <= incl) {
+                uint32_t acc = excl;
+                int bin = 255 - 8 * tid;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    if (j == 7 || acc + cnt[j] >= want) { bin = 255 - 8 * tid - j; break; }
+                    acc += cnt[j];
+                }
+                s_want = want - acc;
+                s_prefix = pre | ((uint32_t)bin << shift);
+            }
         }
         mask |= 255u << shift;
         __syncthreads();
     }
+    if (k == n && tid == 0) s_want = 0;
+    __syncthreads();
     const uint32_t kth = s_prefix;            // key of the k-th largest
     const uint32_t need_eq = s_want;          // how many == kth are taken (lowest indices)
     // count > kth, collect them; then the first need_eq indices with == kth
@@ -227,6 +275,8 @@ k_attn_chunk(AttnPart part, const float *q, const void *kv, int kv_dt, long seq_
              const int *idxs, long seq_idx_stride, int n_heads, int d, int topk, float scale,
              long seq_q_stride)
 {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float ats[];
     const int dp = d + 1;                                   // padded row: conflict-free
     float *kvs = ats;                                       // [AT_CH][dp]
@@ -250,12 +300,39 @@ k_attn_chunk(AttnPart part, const float *q, const void *kv, int kv_dt, long seq_
         }
         return;
     }
-    for (int p = tid >> 5; p < AT_CH; p += blockDim.x >> 5) {   // valid rows only
-        const int r = pidx[p];
-        if (r < 0) continue;
-        for (int c = tid & 31; c < d; c += 32) kvs[p * dp + c] = load_elem(kvb, (size_t)r * d + c, kv_dt);
+    // valid rows and the block's q tile into shared memory, 16 loads in
+    // flight per thread (masked rows stay unwritten: their scores become
+    // -inf and their weights 0, so they are never read)
+    constexpr int LB = 16;
+    const int total = AT_CH * d;
+    for (int i0 = tid; i0 < total; i0 += LB * (int)blockDim.x) {
+        float v[LB];
+        int dst[LB];
+#pragma unroll
+        for (int u = 0; u < LB; u++) {
+            const int i = i0 + u * (int)blockDim.x;
+            const int p = i / d, c = i - p * d;
+            const int r = (i < total) ? pidx[p] : -1;
+            dst[u] = r >= 0 ? p * dp + c : -1;
+            v[u] = r >= 0 ? load_elem(kvb, (size_t)r * d + c, kv_dt) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < LB; u++)
+            if (dst[u] >= 0) kvs[dst[u]] = v[u];
     }
-    for (int i = tid; i < nh * d; i += blockDim.x) qs[i] = q[i];
+    for (int i0 = tid; i0 < nh * d; i0 += LB * (int)blockDim.x) {
+        float v[LB];
+#pragma unroll
+        for (int u = 0; u < LB; u++) {
+            const int i = i0 + u * (int)blockDim.x;
+            v[u] = i < nh * d ? ld_act(q + i) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < LB; u++) {
+            const int i = i0 + u * (int)blockDim.x;
+            if (i < nh * d) qs[i] = v[u];
+        }
+    }
     __syncthreads();
     // scores: warp = head, lane = position; then the chunk max over valid
     // slots (the sink is not part of it), exp weights, exp-sum in double
@@ -291,34 +368,55 @@ k_attn_chunk(AttnPart part, const float *q, const void *kv, int kv_dt, long seq_
 }
 
 // grid (n_heads, batch), 128 threads: rescale chunks in chunk order, add the
-// sink to the denominator only, normalise.
+// sink to the denominator only, normalise. The chunk factors are computed
+// once into shared memory; empty chunks (pm = -inf) are skipped.
+constexpr int AT_MAXCH = 512;
+
 __global__ void k_attn_combine(float *o, AttnPart part, const float *sink, int nch, int n_heads, int d,
                                long seq_o_stride)
 {
-    const int h = blockIdx.x, b = blockIdx.y;
-    float M = -INFINITY;
-    for (int c = 0; c < nch; c++) M = fmaxf(M, part.pm[((size_t)b * nch + c) * n_heads + h]);
+    pdl_trigger();
+    pdl_wait();
+    __shared__ float fac[AT_MAXCH];
+    __shared__ float s_inv, s_M;
+    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
     float *ob = o + (size_t)b * seq_o_stride + (size_t)h * d;
-    if (M == -INFINITY) {       // nothing valid: zero output (dsv4_attn.c:32-37)
-        for (int c = threadIdx.x; c < d; c += blockDim.x) ob[c] = 0.0f;
+    const size_t r0 = (size_t)b * nch * n_heads + h;
+    if (tid < 32) {
+        float M = -INFINITY;
+        for (int c = tid; c < nch; c += 32) M = fmaxf(M, ld_act(part.pm + r0 + (size_t)c * n_heads));
+        M = warp_max_f(M);
+        for (int c = tid; c < nch; c += 32) {
+            const float mc = ld_act(part.pm + r0 + (size_t)c * n_heads);
+            fac[c] = (mc == -INFINITY) ? 0.0f : ((mc == M) ? 1.0f : expf(mc - M));
+        }
+        __syncwarp();
+        if (tid == 0) {
+            s_M = M;
+            if (M != -INFINITY) {
+                double den = 0.0;
+                for (int c = 0; c < nch; c++) {
+                    const float mc = part.pm[r0 + (size_t)c * n_heads];
+                    if (mc != -INFINITY) den += part.pden[r0 + (size_t)c * n_heads] * (double)expf(mc - M);
+                }
+                den += (double)expf(sink[h] - M);
+                s_inv = (float)(1.0 / den);
+            }
+        }
+    }
+    __syncthreads();
+    if (s_M == -INFINITY) {       // nothing valid: zero output (dsv4_attn.c:32-37)
+        for (int c = tid; c < d; c += blockDim.x) ob[c] = 0.0f;
         return;
     }
-    double den = 0.0;
-    for (int c = 0; c < nch; c++) {
-        const size_t r = ((size_t)b * nch + c) * n_heads + h;
-        const float mc = part.pm[r];
-        if (mc != -INFINITY) den += part.pden[r] * (double)expf(mc - M);
-    }
-    den += (double)expf(sink[h] - M);
-    const float inv = (float)(1.0 / den);
-    for (int cc = threadIdx.x; cc < d; cc += blockDim.x) {
+    const float inv = s_inv;
+    for (int cc = tid; cc < d; cc += blockDim.x) {
         float acc = 0.0f;
+#pragma unroll 4
         for (int c = 0; c < nch; c++) {
-            const size_t r = ((size_t)b * nch + c) * n_heads + h;
-            const float mc = part.pm[r];
-            if (mc == -INFINITY) continue;
-            const float f = (mc == M) ? 1.0f : expf(mc - M);
-            acc = __fadd_rn(acc, __fmul_rn(part.po[r * d + cc], f));
+            const float f = fac[c];
+            if (f == 0.0f && part.pm[r0 + (size_t)c * n_heads] == -INFINITY) continue;
+            acc = __fadd_rn(acc, __fmul_rn(ld_act(part.po + (r0 + (size_t)c * n_heads) * d + cc), f));
         }
         ob[cc] = __fmul_rn(acc, inv);
     }
@@ -339,7 +437,7 @@ int indexer_score(float *out, const float *q, const void *keys, int key_dt, long
         attr = true;
     }
     dim3 grid((n_pos + IX_TP - 1) / IX_TP, batch);
-    k_indexer_score<<<grid, 256, smem, st>>>(out, q, keys, key_dt, key_stride, seq_key_stride, w, n_heads,
+    launch(k_indexer_score, dim3(grid), dim3(256), smem, st, out, q, keys, key_dt, key_stride, seq_key_stride, w, n_heads,
                                              head_dim, n_pos, scale, (long)n_heads * head_dim, n_pos, dyn_n);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
@@ -358,7 +456,7 @@ int topk(int *idx, const float *scores, int n, int k, int batch, long seq_in_str
         cudaFuncSetAttribute(k_topk, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
         attr = true;
     }
-    k_topk<<<dim3(1, batch), 1024, smem, st>>>(idx, scores, n, k, seq_in_stride, seq_out_stride, dyn_nk);
+    launch(k_topk, dim3(dim3(1, batch)), dim3(1024), smem, st, idx, scores, n, k, seq_in_stride, seq_out_stride, dyn_nk);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -375,6 +473,7 @@ int sparse_attn(float *o, const float *q, const void *kv, int kv_dt, long seq_kv
     if (batch <= 0 || topk <= 0) return 0;
     if (n_heads <= 0 || d > 1024) return -1;
     const int nch = (topk + AT_CH - 1) / AT_CH;
+    if (nch > AT_MAXCH) return -1;
     const size_t n = (size_t)batch * nch * n_heads;
     AttnPart part;
     part.pden = reinterpret_cast<double *>(part_buf);
@@ -387,9 +486,9 @@ int sparse_attn(float *o, const float *q, const void *kv, int kv_dt, long seq_kv
         attr = true;
     }
     if (smem > 220 * 1024) return -1;
-    k_attn_chunk<<<dim3(nch, (n_heads + AT_HB - 1) / AT_HB, batch), 256, smem, st>>>(part, q, kv, kv_dt, seq_kv_rows, idxs, seq_idx_stride,
+    launch(k_attn_chunk, dim3(dim3(nch, (n_heads + AT_HB - 1) / AT_HB, batch)), dim3(256), smem, st, part, q, kv, kv_dt, seq_kv_rows, idxs, seq_idx_stride,
                                                       n_heads, d, topk, scale, (long)n_heads * d);
-    k_attn_combine<<<dim3(n_heads, batch), 128, 0, st>>>(o, part, sink, nch, n_heads, d, (long)n_heads * d);
+    launch(k_attn_combine, dim3(dim3(n_heads, batch)), dim3(128), 0, st, o, part, sink, nch, n_heads, d, (long)n_heads * d);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -11,6 +11,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <utility>
 #include <vector>
 
 #include "common.cuh"
@@ -100,6 +101,7 @@ static DevMat up_mat(dsv4b_model *m, const DSV4QMat &q, bool *ok)
     if (!q.w) { *ok = false; return d; }
     d.w = (const uint8_t *)dcopy(m, q.w, row_bytes(q.wdt, q.cols) * q.rows, ok);
     if (q.wdt >= DSV4_WFP8) d.s = (const uint8_t *)dcopy(m, q.s, qmat_sbytes(q), ok);
+    d.f16s = q.wdt == DSV4_WFP4 && q.s && fp4_scales_f16((const uint8_t *)q.s, qmat_sbytes(q));
     return d;
 }
 
@@ -240,7 +242,7 @@ static int reset_state(dsv4b_model *m)
 
 static int G(const DevMat &w, float *y, const float *x, cudaStream_t st)
 {
-    return gemv(w.wdt, y, w.rows, x, w.cols, w.w, w.s, w.rows, w.cols, w.blk_r, w.blk_c, 1, st);
+    return gemv(w.wdt, y, w.rows, x, w.cols, w.w, w.s, w.rows, w.cols, w.blk_r, w.blk_c, 1, st, w.f16s != 0);
 }
 
 // x1 = RMSNorm(mHC pre-mix of h) with the sub-layer's norm weights.
@@ -253,7 +255,8 @@ struct Grp {
 
 static void grp_add(Grp &g, const DevMat &w, const float *x, float *y, cudaStream_t st)
 {
-    if (g.n < kGemvMaxItems && gemv_item(g.it[g.n], w.wdt, w.w, w.s, w.rows, w.cols, w.blk_r, w.blk_c, x, y))
+    if (g.n < kGemvMaxItems &&
+        gemv_item(g.it[g.n], w.wdt, w.w, w.s, w.rows, w.cols, w.blk_r, w.blk_c, x, y, w.f16s != 0))
         g.n++;
     else
         g.rc |= G(w, y, x, st);
@@ -261,21 +264,21 @@ static void grp_add(Grp &g, const DevMat &w, const float *x, float *y, cudaStrea
 
 static int grp_run(Grp &g, cudaStream_t st) { return g.rc | gemv_group(g.it, g.n, st); }
 
-static int hc_pre(dsv4b_model *m, const float *fn, const float *base, const float *scale, const float *norm,
-                  cudaStream_t st)
+static int hc_pre(dsv4b_model *m, const float *h, const float *fn, const float *base, const float *scale,
+                  const float *norm, cudaStream_t st)
 {
     const DSV4Cfg &c = m->c;
     const int hc = c.hc_mult, mix = (2 + hc) * hc, n = hc * c.hidden;
-    if (mix <= kHcPreMixMax) {
-        k_hc_pre<<<kHcPreBlocks, 256, 0, st>>>(m->x1, m->post, m->comb, m->h, fn, scale, base, norm, m->hc_part,
+    if (mix <= kHcPreMixMax && c.hidden % 4 == 0 && c.hidden <= 256 * 4 * kHcPreYPT) {
+        launch(k_hc_pre, dim3(kHcPreBlocks), dim3(256), 0, st, m->x1, m->post, m->comb, h, fn, scale, base, norm, m->hc_part,
                                                m->hc_cnt, hc, c.hidden, c.hc_sinkhorn_iters, c.hc_eps,
                                                c.rms_eps);
         return 0;
     }
-    k_hc_mix<<<mix, 256, 0, st>>>(m->mixes, fn, m->h, n, c.rms_eps);
-    k_hc_finish<<<1, 256, 0, st>>>(m->x1, m->post, m->comb, m->mixes, m->h, scale, base, hc, c.hidden,
+    launch(k_hc_mix, dim3(mix), dim3(256), 0, st, m->mixes, fn, h, n, c.rms_eps);
+    launch(k_hc_finish, dim3(1), dim3(256), 0, st, m->x1, m->post, m->comb, m->mixes, h, scale, base, hc, c.hidden,
                                    c.hc_sinkhorn_iters, c.hc_eps);
-    k_rmsnorm<<<1, 1024, 0, st>>>(m->x1, m->x1, norm, c.hidden, c.rms_eps);
+    launch(k_rmsnorm, dim3(1), dim3(1024), 0, st, m->x1, m->x1, norm, c.hidden, c.rms_eps);
     return 0;
 }
 
@@ -286,13 +289,15 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
     const int hc = c.hc_mult, d = c.hidden, hd = c.head_dim, rd = c.qk_rope, H = c.n_heads;
     const int win = c.sliding_window, wide = hc * d;
     int rc = 0;
-    k_embed<<<16, 256, 0, st>>>(m->h, m->embed, m->emb_wdt, m->st, d, hc);
+    PdlChain chain;
+    float *hin = m->h, *hout = m->resid;
+    launch(k_embed, dim3(16), dim3(256), 0, st, hin, m->embed, m->emb_wdt, m->st, d, hc);
     for (int Li = 0; Li < c.n_layers; Li++) {
         DevLayer &l = m->L[Li];
         const float *cs = l.ratio ? m->cs_c : m->cs_d, *sn = l.ratio ? m->sn_c : m->sn_d;
-        // ---- attention half (src/model/dsv4_layer.c:495-509)
-        cudaMemcpyAsync(m->resid, m->h, (size_t)wide * 4, cudaMemcpyDeviceToDevice, st);
-        hc_pre(m, l.hca_fn, l.hca_base, l.hca_scale, l.attn_norm, st);
+        // ---- attention half (src/model/dsv4_layer.c:495-509); the residual
+        // stream ping-pongs between two buffers, so no copy is needed
+        hc_pre(m, hin, l.hca_fn, l.hca_base, l.hca_scale, l.attn_norm, st);
         // every projection of x1 in one launch, then both of the normalised q latent
         {
             Grp ga;
@@ -305,22 +310,22 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
             if (l.has_idx) grp_add(ga, l.iwproj, m->x1, m->idx_w, st);
             rc |= grp_run(ga, st);
         }
-        k_rmsnorm<<<1, 1024, 0, st>>>(m->qr, m->qr, l.q_norm, c.q_lora, c.rms_eps);
+        launch(k_rmsnorm, dim3(1), dim3(1024), 0, st, m->qr, m->qr, l.q_norm, c.q_lora, c.rms_eps);
         {
             Grp gb;
             grp_add(gb, l.wq_b, m->qr, m->q, st);
             if (l.has_idx) grp_add(gb, l.iwq_b, m->qr, m->idx_q, st);
             rc |= grp_run(gb, st);
         }
-        k_heads_norm_rope<<<H, 256, 0, st>>>(m->q, hd, rd, cs, sn, m->st, 0, 0, 1, c.rms_eps);
-        k_kv_finish<<<1, 256, 0, st>>>(m->kv, l.kv_norm, hd, rd, cs, sn, m->st, c.rms_eps, l.kv_cache, win);
+        launch(k_heads_norm_rope, dim3(H), dim3(256), 0, st, m->q, hd, rd, cs, sn, m->st, 0, 0, 1, c.rms_eps);
+        launch(k_kv_finish, dim3(1), dim3(256), 0, st, m->kv, l.kv_norm, hd, rd, cs, sn, m->st, c.rms_eps, l.kv_cache, win);
         if (l.has_comp) {
-            k_compress<<<1, 512, hd * 4, st>>>(l.kv_cache, l.comp_kv, l.comp_score, m->comp_in, m->comp_sc, l.ape,
+            launch(k_compress, dim3(1), dim3(512), hd * 4, st, l.kv_cache, l.comp_kv, l.comp_score, m->comp_in, m->comp_sc, l.ape,
                                                l.cnorm, l.ratio, hd, rd, cs, sn, m->st, c.rms_eps, win,
                                                c.index_topk, l.dyn);
             if (l.has_idx) {
                 const int ih = c.index_n_heads, id = c.index_head_dim;
-                k_heads_norm_rope<<<ih, 128, 0, st>>>(m->idx_q, id, rd, cs, sn, m->st, 0, 0, 0, c.rms_eps);
+                launch(k_heads_norm_rope, dim3(ih), dim3(128), 0, st, m->idx_q, id, rd, cs, sn, m->st, 0, 0, 0, c.rms_eps);
                 const float scale = (1.0f / sqrtf((float)id)) * (1.0f / sqrtf((float)ih));
                 // the compressed region read as contiguous rows of index_head_dim
                 // floats, as the reference does (dsv4_layer.c:286-289)
@@ -329,10 +334,10 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
                 rc |= topk(m->isel, m->idx_scores, m->ncomp4, c.index_topk, 1, m->ncomp4, c.index_topk, st, l.dyn);
             }
         }
-        k_build_idxs<<<1, 256, 0, st>>>(m->idxs, m->nidx, m->st, win, l.has_comp, l.has_idx, l.dyn, m->isel);
+        launch(k_build_idxs, dim3(1), dim3(256), 0, st, m->idxs, m->nidx, m->st, win, l.has_comp, l.has_idx, l.dyn, m->isel);
         rc |= sparse_attn(m->o, m->q, l.kv_cache, DSV4B_DT_F32, (long)l.kv_rows, l.sink, m->idxs, m->nidx, H, hd,
                           m->nidx, 1.0f / sqrtf((float)hd), 1, m->attn_part, st);
-        k_heads_norm_rope<<<H, 256, 0, st>>>(m->o, hd, rd, cs, sn, m->st, 0, 1, 0, c.rms_eps);
+        launch(k_heads_norm_rope, dim3(H), dim3(256), 0, st, m->o, hd, rd, cs, sn, m->st, 0, 1, 0, c.rms_eps);
         // grouped low-rank output (dsv4_layer.c:303-335): the o_groups row
         // slices of wo_a, each on its own slice of o, in one launch
         {
@@ -351,20 +356,21 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
             rc |= grp_run(go, st);
         }
         rc |= G(l.wo_b, m->blk, m->ogrp, st);
-        k_hc_post<<<(wide + 255) / 256, 256, 0, st>>>(m->h, m->blk, m->resid, m->post, m->comb, hc, d);
+        launch(k_hc_post, dim3((wide + 255) / 256), dim3(256), 0, st, hout, m->blk, hin, m->post, m->comb, hc, d);
+        std::swap(hin, hout);
         // ---- FFN half: the residual is taken after attention (:511-522)
-        cudaMemcpyAsync(m->resid, m->h, (size_t)wide * 4, cudaMemcpyDeviceToDevice, st);
-        hc_pre(m, l.hcf_fn, l.hcf_base, l.hcf_scale, l.ffn_norm, st);
+        hc_pre(m, hin, l.hcf_fn, l.hcf_base, l.hcf_scale, l.ffn_norm, st);
         rc |= moe_forward(l.moe, m->ms, m->blk, m->x1, &m->st->token, st);
-        k_hc_post<<<(wide + 255) / 256, 256, 0, st>>>(m->h, m->blk, m->resid, m->post, m->comb, hc, d);
+        launch(k_hc_post, dim3((wide + 255) / 256), dim3(256), 0, st, hout, m->blk, hin, m->post, m->comb, hc, d);
+        std::swap(hin, hout);
     }
     // ---- head (src/cli/dsv4_run.c:467-474)
-    k_hc_mix<<<hc, 256, 0, st>>>(m->mixes, m->hch_fn, m->h, wide, c.rms_eps);
-    k_hc_head_finish<<<1, 256, 0, st>>>(m->xh, m->mixes, m->h, m->hch_scale, m->hch_base, hc, d, c.hc_eps);
-    k_rmsnorm<<<1, 1024, 0, st>>>(m->xh, m->xh, m->norm, d, c.rms_eps);
+    launch(k_hc_mix, dim3(hc), dim3(256), 0, st, m->mixes, m->hch_fn, hin, wide, c.rms_eps);
+    launch(k_hc_head_finish, dim3(1), dim3(256), 0, st, m->xh, m->mixes, hin, m->hch_scale, m->hch_base, hc, d, c.hc_eps);
+    launch(k_rmsnorm, dim3(1), dim3(1024), 0, st, m->xh, m->xh, m->norm, d, c.rms_eps);
     rc |= G(m->head, m->logits, m->xh, st);
-    k_argmax_part<<<148, 256, 0, st>>>(m->am_pv, m->am_pi, m->logits, c.vocab);
-    k_argmax_final<<<1, 32, 0, st>>>(m->st, m->out_tokens, m->am_pv, m->am_pi, 148, m->prompt, m->n_prompt);
+    launch(k_argmax_part, dim3(148), dim3(256), 0, st, m->am_pv, m->am_pi, m->logits, c.vocab);
+    launch(k_argmax_final, dim3(1), dim3(32), 0, st, m->st, m->out_tokens, m->am_pv, m->am_pi, 148, m->prompt, m->n_prompt);
     if (cudaPeekAtLastError() != cudaSuccess) rc = -1;
     return rc ? -1 : 0;
 }
@@ -412,6 +418,7 @@ static bool build_layer_from_host(dsv4b_model *m, int Li, const DSV4LayerW &w, c
                                : nullptr;
     mo.fixed = nullptr;
     std::vector<const uint8_t *> tab((size_t)6 * c.n_experts);
+    mo.ef16s = 1;
     for (int e = 0; e < c.n_experts && ok; e++) {
         const DSV4ExpertW &x = ex[(size_t)Li * c.n_experts + e];
         const DSV4QMat *q3[3] = { &x.w1, &x.w3, &x.w2 };
@@ -420,6 +427,7 @@ static bool build_layer_from_host(dsv4b_model *m, int Li, const DSV4LayerW &w, c
             tab[(size_t)(2 * j) * c.n_experts + e] = dm.w;
             tab[(size_t)(2 * j + 1) * c.n_experts + e] = dm.s;
             if (e == 0 && j == 0) { mo.efmt = dm.wdt; mo.eblk_r = dm.blk_r; mo.eblk_c = dm.blk_c; }
+            mo.ef16s &= dm.f16s;
         }
     }
     const uint8_t *const *t = (const uint8_t *const *)dcopy(m, tab.data(), tab.size() * sizeof(void *), &ok);
@@ -680,6 +688,7 @@ static bool synth_layer(Synth &S, int Li)
     mo.w3tab = t + 2 * E; mo.s3tab = t + 3 * E;
     mo.w2tab = t + 4 * E; mo.s2tab = t + 5 * E;
     mo.efmt = DSV4_WFP4; mo.eblk_r = 1; mo.eblk_c = 32;
+    mo.ef16s = 1;                                               // every scale is 2^-6
     const int Is = c.moe_inter * c.n_shared;
     mo.sh[0] = S.fp8(Is, d);
     mo.sh[1] = S.fp8(Is, d);

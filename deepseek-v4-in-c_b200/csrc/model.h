@@ -24,6 +24,7 @@ __global__ void k_hc_finish(float *y, float *post, float *comb, const float *mix
                             const float *scale, const float *base, int hc, int hidden, int iters, float eps);
 constexpr int kHcPreMixMax = 24;   // (2 + hc) * hc for hc <= 4
 constexpr int kHcPreBlocks = 64;
+constexpr int kHcPreYPT = 8;       // float4 columns of y per thread: hidden <= 256 * 4 * 8
 __global__ void k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, const float *scale,
                          const float *base, const float *norm_w, double *part, unsigned *count, int hc, int hidden,
                          int iters, float hc_eps, float rms_eps);

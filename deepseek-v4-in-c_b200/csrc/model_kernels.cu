@@ -32,6 +32,8 @@ __device__ __forceinline__ double block_sum_d(double v, double *red)
 // (src/cli/dsv4_run.c:449-450).
 __global__ void k_embed(float *h, const void *table, int wdt, const StepState *st, int hidden, int hc)
 {
+    pdl_trigger();
+    pdl_wait();
     const long tok = st->token;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < hidden; i += gridDim.x * blockDim.x) {
         float v;
@@ -48,6 +50,8 @@ __global__ void k_embed(float *h, const void *table, int wdt, const StepState *s
 // (src/core/dsv4_hc.c:118-129, src/cli/dsv4_run.c:97-107). grid = rows.
 __global__ void k_hc_mix(float *mixes, const float *fn, const float *x, int n, float eps)
 {
+    pdl_trigger();
+    pdl_wait();
     __shared__ double red[33];
     const float *row = fn + (size_t)blockIdx.x * n;
     double sq = 0.0, dot = 0.0;
@@ -71,6 +75,8 @@ __device__ __forceinline__ float sigm(float x) { return __fdiv_rn(1.0f, __fadd_r
 __global__ void k_hc_finish(float *y, float *post, float *comb, const float *mixes, const float *x,
                             const float *scale, const float *base, int hc, int hidden, int iters, float eps)
 {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float pre[DSV4B_MAX_HC], cb[DSV4B_MAX_HC * DSV4B_MAX_HC];
     if (threadIdx.x == 0) {
         for (int j = 0; j < hc; j++) pre[j] = __fadd_rn(sigm(__fadd_rn(__fmul_rn(mixes[j], scale[0]), base[j])), eps);
@@ -138,15 +144,26 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
     __shared__ float mixes[MIXMAX], pre[DSV4B_MAX_HC];
     __shared__ bool last;
     const int n = hc * hidden, mix = (2 + hc) * hc, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    pdl_trigger();
     double acc[MIXMAX + 1];
 #pragma unroll
     for (int m = 0; m <= MIXMAX; m++) acc[m] = 0.0;
-    for (int i = blockIdx.x * blockDim.x + tid; i < n; i += gridDim.x * blockDim.x) {
+    // the fn column is a weight: fetched before waiting for x
+    const int stride = gridDim.x * blockDim.x;
+    int i = blockIdx.x * blockDim.x + tid;
+    float fv[MIXMAX];
+#pragma unroll
+    for (int m = 0; m < MIXMAX; m++) fv[m] = (m < mix && i < n) ? __ldg(fn + (size_t)m * n + i) : 0.0f;
+    pdl_wait();
+    for (; i < n; i += stride) {
         const double xv = (double)x[i];
         acc[MIXMAX] = __fma_rn(xv, xv, acc[MIXMAX]);
 #pragma unroll
         for (int m = 0; m < MIXMAX; m++)
-            if (m < mix) acc[m] = __fma_rn((double)__ldg(fn + (size_t)m * n + i), xv, acc[m]);
+            if (m < mix) acc[m] = __fma_rn((double)fv[m], xv, acc[m]);
+        const int i2 = i + stride;
+#pragma unroll
+        for (int m = 0; m < MIXMAX; m++) fv[m] = (m < mix && i2 < n) ? __ldg(fn + (size_t)m * n + i2) : 0.0f;
     }
 #pragma unroll
     for (int m = 0; m <= MIXMAX; m++) {
@@ -167,6 +184,7 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
     __threadfence();
     if (tid <= MIXMAX) {
         double t = 0.0;
+#pragma unroll 8
         for (int b = 0; b < (int)gridDim.x; b++) t += __ldcg(part + (size_t)b * (MIXMAX + 1) + tid);
         tot[tid] = t;
     }
@@ -211,19 +229,54 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
         if (act) comb[l] = v;
     }
     __syncthreads();
+    // y = sum_j pre[j] x[j] in double, four columns per float4, all loads of
+    // a thread issued together; then RMSNorm from the registers
+    const int h4 = hidden >> 2;
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    float4 yv[kHcPreYPT];
     double sq = 0.0;
-    for (int d = tid; d < hidden; d += blockDim.x) {
-        double a = 0.0;
-        for (int j = 0; j < hc; j++) a = __dadd_rn(a, __dmul_rn((double)pre[j], (double)x[(size_t)j * hidden + d]));
-        const float yv = (float)a;
-        y[d] = yv;
-        sq = __fma_rn((double)yv, (double)yv, sq);
+#pragma unroll
+    for (int u = 0; u < kHcPreYPT; u++) {
+        const int d4 = tid + u * (int)blockDim.x;
+        yv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (d4 < h4) {
+            double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+            for (int j = 0; j < hc; j++) {
+                const float4 v = __ldcg(x4 + (size_t)j * h4 + d4);
+                const double pj = (double)pre[j];
+                a0 = __dadd_rn(a0, __dmul_rn(pj, (double)v.x));
+                a1 = __dadd_rn(a1, __dmul_rn(pj, (double)v.y));
+                a2 = __dadd_rn(a2, __dmul_rn(pj, (double)v.z));
+                a3 = __dadd_rn(a3, __dmul_rn(pj, (double)v.w));
+            }
+            yv[u] = make_float4((float)a0, (float)a1, (float)a2, (float)a3);
+            sq = __fma_rn((double)yv[u].x, (double)yv[u].x, sq);
+            sq = __fma_rn((double)yv[u].y, (double)yv[u].y, sq);
+            sq = __fma_rn((double)yv[u].z, (double)yv[u].z, sq);
+            sq = __fma_rn((double)yv[u].w, (double)yv[u].w, sq);
+        }
     }
-    if (!norm_w) return;
-    __shared__ double nred[33];
-    sq = block_sum_d(sq, nred);
-    const float inv = (float)(1.0 / sqrt(sq / (double)hidden + (double)rms_eps));
-    for (int d = tid; d < hidden; d += blockDim.x) y[d] = __fmul_rn(norm_w[d], __fmul_rn(y[d], inv));
+    float inv = 1.0f;
+    if (norm_w) {
+        __shared__ double nred[33];
+        sq = block_sum_d(sq, nred);
+        inv = (float)(1.0 / sqrt(sq / (double)hidden + (double)rms_eps));
+    }
+    float4 *y4 = reinterpret_cast<float4 *>(y);
+    const float4 *w4 = reinterpret_cast<const float4 *>(norm_w);
+#pragma unroll
+    for (int u = 0; u < kHcPreYPT; u++) {
+        const int d4 = tid + u * (int)blockDim.x;
+        if (d4 < h4) {
+            float4 o = yv[u];
+            if (norm_w) {
+                const float4 wv = __ldg(w4 + d4);
+                o = make_float4(__fmul_rn(wv.x, __fmul_rn(o.x, inv)), __fmul_rn(wv.y, __fmul_rn(o.y, inv)),
+                                __fmul_rn(wv.z, __fmul_rn(o.z, inv)), __fmul_rn(wv.w, __fmul_rn(o.w, inv)));
+            }
+            y4[d4] = o;
+        }
+    }
 }
 
 // The head's reduction: a sigmoid gate per copy, one scalar scale, no
@@ -231,6 +284,8 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
 __global__ void k_hc_head_finish(float *y, const float *mixes, const float *x, const float *scale,
                                  const float *base, int hc, int hidden, float eps)
 {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float pre[DSV4B_MAX_HC];
     if (threadIdx.x < hc) {
         const int j = threadIdx.x;
@@ -249,6 +304,8 @@ __global__ void k_hc_head_finish(float *y, const float *mixes, const float *x, c
 __global__ void k_hc_post(float *y, const float *x, const float *res, const float *post, const float *comb,
                           int hc, int hidden)
 {
+    pdl_trigger();
+    pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= hc * hidden) return;
     const int k = i / hidden, d = i % hidden;
@@ -262,6 +319,8 @@ __global__ void k_hc_post(float *y, const float *x, const float *res, const floa
 // y = w * (x * inv). One block; y may alias x.
 __global__ void k_rmsnorm(float *y, const float *x, const float *w, int n, float eps)
 {
+    pdl_trigger();
+    pdl_wait();
     __shared__ double red[33];
     double s = 0.0;
     for (int i = threadIdx.x; i < n; i += blockDim.x) s = __fma_rn((double)x[i], (double)x[i], s);
@@ -291,6 +350,8 @@ __device__ __forceinline__ void rope_tail(float *v, int width, int rd, const flo
 __global__ void k_heads_norm_rope(float *v, int width, int rd, const float *cs, const float *sn,
                                   const StepState *st, int pos_off, int inverse, int do_norm, float eps)
 {
+    pdl_trigger();
+    pdl_wait();
     __shared__ double red[33];
     float *h = v + (size_t)blockIdx.x * width;
     if (do_norm) {
@@ -309,6 +370,8 @@ __global__ void k_heads_norm_rope(float *v, int width, int rd, const float *cs, 
 __global__ void k_kv_finish(float *kv, const float *w, int hd, int rd, const float *cs, const float *sn,
                             const StepState *st, float eps, float *cache, int win)
 {
+    pdl_trigger();
+    pdl_wait();
     __shared__ double red[33];
     double s = 0.0;
     for (int i = threadIdx.x; i < hd; i += blockDim.x) s = __fma_rn((double)kv[i], (double)kv[i], s);
@@ -332,6 +395,8 @@ __global__ void k_compress(float *cache, float *kv_state, float *score_state, co
                            const float *cs, const float *sn, const StepState *st, float eps, int win,
                            int index_topk, int *dyn)
 {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float cbuf[];     // [hd]
     __shared__ double red[33];
     const int pos = st->pos, overlap = (ratio == 4), coff = 1 + overlap, width = coff * hd;
@@ -401,6 +466,8 @@ __global__ void k_compress(float *cache, float *kv_state, float *score_state, co
 __global__ void k_build_idxs(int *idxs, int nmax, const StepState *st, int win, int has_comp, int has_idx,
                              const int *dyn, const int *sel)
 {
+    pdl_trigger();
+    pdl_wait();
     const int pos = st->pos;
     const int n = (pos + 1 < win) ? pos + 1 : win;
     const int take = has_comp ? (has_idx ? dyn[1] : dyn[0]) : 0;
@@ -417,6 +484,8 @@ __global__ void k_build_idxs(int *idxs, int nmax, const StepState *st, int win, 
 // remains, else the argmax; out_tokens[pos] = the argmax.
 __global__ void k_argmax_part(float *pv, int *pi, const float *x, int n)
 {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float sv[32];
     __shared__ int si[32];
     float bv = -INFINITY;
@@ -441,6 +510,8 @@ __global__ void k_argmax_part(float *pv, int *pi, const float *x, int n)
 __global__ void k_argmax_final(StepState *st, int *out_tokens, const float *pv, const int *pi, int nparts,
                                const int *prompt, int n_prompt)
 {
+    pdl_trigger();
+    pdl_wait();
     if (threadIdx.x != 0) return;
     float bv = pv[0];
     int bi = pi[0];

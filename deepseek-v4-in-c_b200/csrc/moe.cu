@@ -25,11 +25,11 @@ __global__ void k_route(const float *logits, const float *bias, const int *fixed
                         const int64_t *tid2eid, const int *token, int n, int topk,
                         float route_scale, int score_func, int *sel_out, float *w_out)
 {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float orig[kMoeMaxExperts], sc[kMoeMaxExperts];
     __shared__ unsigned char taken[kMoeMaxExperts];
     __shared__ int chosen[kMoeMaxTopk];
-    __shared__ float wv[32];
-    __shared__ int wi[32];
     const int tid = threadIdx.x, nthr = blockDim.x;
     for (int e = tid; e < n; e += nthr) {
         const float l = logits[e];
@@ -43,30 +43,24 @@ __global__ void k_route(const float *logits, const float *bias, const int *fixed
     __syncthreads();
     if (fixed || tid2eid) {
         if (tid < topk) chosen[tid] = fixed ? fixed[tid] : (int)tid2eid[(long)token[0] * topk + tid];
-    } else {
-        // topk rounds of block argmax: value descending, ties to the lower
+    } else if (tid < 32) {
+        // topk rounds of warp argmax: value descending, ties to the lower
         // index -- the order of the reference's repeated-argmax selection.
         for (int k = 0; k < topk; k++) {
             float bv = 0.0f;
             int bi = -1;
-            for (int e = tid; e < n; e += nthr)
+            for (int e = tid; e < n; e += 32)
                 if (!taken[e] && (bi < 0 || sc[e] > bv || (sc[e] == bv && e < bi))) { bv = sc[e]; bi = e; }
             for (int o = 16; o > 0; o >>= 1) {
                 const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
                 const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
                 if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
             }
-            if ((tid & 31) == 0) { wv[tid >> 5] = bv; wi[tid >> 5] = bi; }
-            __syncthreads();
             if (tid == 0) {
-                float v = 0.0f;
-                int b = -1;
-                for (int w = 0; w < (nthr + 31) / 32; w++)
-                    if (wi[w] >= 0 && (b < 0 || wv[w] > v || (wv[w] == v && wi[w] < b))) { v = wv[w]; b = wi[w]; }
-                chosen[k] = b;
-                taken[b] = 1;
+                chosen[k] = bi;
+                taken[bi] = 1;
             }
-            __syncthreads();
+            __syncwarp();
         }
     }
     __syncthreads();
@@ -87,6 +81,8 @@ __global__ void k_route(const float *logits, const float *bias, const int *fixed
 __global__ void k_combine(float *out, const float *acc, const float *w, int topk, int hidden,
                           const float *shared)
 {
+    pdl_trigger();
+    pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= hidden) return;
     float o = 0.0f;
@@ -99,12 +95,13 @@ int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float 
                 const int *token, cudaStream_t st)
 {
     const int H = L.hidden, I = L.inter, K = L.topk;
+    PdlChain chain;
     if (K < 1 || K + 1 > kGemvMaxItems || K > kMoeMaxTopk || L.n_experts > kMoeMaxExperts) return -1;
     // router
     if (gemv(L.gate.wdt, S.logits, L.n_experts, x, H, L.gate.w, L.gate.s, L.n_experts, H,
-             L.gate.blk_r, L.gate.blk_c, 1, st))
+             L.gate.blk_r, L.gate.blk_c, 1, st, L.gate.f16s != 0))
         return -1;
-    k_route<<<1, 256, 0, st>>>(S.logits, L.bias, L.fixed, L.tid2eid, token, L.n_experts, K,
+    launch(k_route, dim3(1), dim3(256), 0, st, S.logits, L.bias, L.fixed, L.tid2eid, token, L.n_experts, K,
                                L.route_scale, L.score_func, S.sel, S.wts);
     const int Is = L.has_shared ? L.inter_shared : 0;
     float *hs = S.h + (size_t)K * I, *accs = S.acc + (size_t)K * H;
@@ -112,7 +109,8 @@ int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float 
     // gate / up of every selected expert and the shared one, SwiGLU in the
     // epilogue: h[k] = swiglu(w1 x, w3 x) (dsv4_layer.c:199-206)
     for (int k = 0; k < K; k++) {
-        if (!gemv_item(it[k], L.efmt, nullptr, nullptr, I, H, L.eblk_r, L.eblk_c, x, S.h + (size_t)k * I))
+        if (!gemv_item(it[k], L.efmt, nullptr, nullptr, I, H, L.eblk_r, L.eblk_c, x, S.h + (size_t)k * I,
+                       L.ef16s != 0))
             return -1;
         it[k].wtab = L.w1tab; it[k].stab = L.s1tab;
         it[k].w2tab = L.w3tab; it[k].s2tab = L.s3tab;
@@ -121,7 +119,8 @@ int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float 
     }
     int n = K;
     if (Is) {
-        if (!gemv_item(it[n], L.sh[0].wdt, L.sh[0].w, L.sh[0].s, Is, H, L.sh[0].blk_r, L.sh[0].blk_c, x, hs) ||
+        if (!gemv_item(it[n], L.sh[0].wdt, L.sh[0].w, L.sh[0].s, Is, H, L.sh[0].blk_r, L.sh[0].blk_c, x, hs,
+                       L.sh[0].f16s && L.sh[1].f16s) ||
             L.sh[1].wdt != L.sh[0].wdt)
             return -1;
         it[n].W2 = L.sh[1].w; it[n].S2 = L.sh[1].s;
@@ -132,19 +131,20 @@ int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float 
     // down projections into the per-k accumulators
     for (int k = 0; k < K; k++) {
         if (!gemv_item(it[k], L.efmt, nullptr, nullptr, H, I, L.eblk_r, L.eblk_c, S.h + (size_t)k * I,
-                       S.acc + (size_t)k * H))
+                       S.acc + (size_t)k * H, L.ef16s != 0))
             return -1;
         it[k].wtab = L.w2tab; it[k].stab = L.s2tab;
         it[k].sel = S.sel; it[k].slot = k;
     }
     n = K;
     if (Is) {
-        if (!gemv_item(it[n], L.sh[2].wdt, L.sh[2].w, L.sh[2].s, H, Is, L.sh[2].blk_r, L.sh[2].blk_c, hs, accs))
+        if (!gemv_item(it[n], L.sh[2].wdt, L.sh[2].w, L.sh[2].s, H, Is, L.sh[2].blk_r, L.sh[2].blk_c, hs, accs,
+                       L.sh[2].f16s != 0))
             return -1;
         n++;
     }
     if (gemv_group(it, n, st)) return -1;
-    k_combine<<<(H + 255) / 256, 256, 0, st>>>(out, S.acc, S.wts, K, H, Is ? accs : nullptr);
+    launch(k_combine, dim3((H + 255) / 256), dim3(256), 0, st, out, S.acc, S.wts, K, H, Is ? accs : nullptr);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -14,6 +14,7 @@ constexpr int kMoeMaxTopk = 16;
 struct DevMat {
     const uint8_t *w, *s;
     int wdt, rows, cols, blk_r, blk_c;
+    int f16s;                       // FP4: every scale f16-safe (gemv_mma_shape)
 };
 
 struct MoeLayer {
@@ -26,6 +27,7 @@ struct MoeLayer {
     const uint8_t *const *w3tab, *const *s3tab;
     const uint8_t *const *w2tab, *const *s2tab;
     int efmt, eblk_r, eblk_c;
+    int ef16s;                      // FP4 experts: every scale f16-safe
     DevMat sh[3];                   // shared expert w1, w3, w2
     int has_shared;
     int n_experts, topk, hidden, inter, inter_shared, score_func;

@@ -74,6 +74,7 @@ __device__ __forceinline__ float4 ld_f4(const float *p)
     return __ldcg(reinterpret_cast<const float4 *>(p));
 }
 __device__ __forceinline__ float ld_act(const float *p) { return __ldcg(p); }
+__device__ __forceinline__ double ld_act_d(const double *p) { return __ldcg(p); }
 
 // Packed two-lane FMA (Blackwell FFMA2): c.x += a.x*b.x, c.y += a.y*b.y, each
 // lane a single correctly rounded fma.

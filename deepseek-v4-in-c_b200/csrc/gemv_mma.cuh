@@ -206,17 +206,30 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
     for (int q = 0; q < kMmaStages - 1; q++) issue_next();
     pdl_wait();
 
-    // x fragments: warp w builds those of units w, w+8, ...; lane = (mma, t)
-    // in two passes for the 16 k16-steps of an FP4 unit
-    for (int cb = warp; cb < nb; cb += 8) {
-        float4 xv[MPU / 8];
+    // x fragments: warp w builds those of units w, w+8, ...; lane = (mma, t),
+    // two passes for the 16 k16-steps of an FP4 unit. All of a warp's x
+    // loads are issued before any is used.
+    constexpr int XU = kMmaMaxBlocks / 8, XH = MPU / 8;
+    float4 xv[XU][XH];
+#pragma unroll
+    for (int u = 0; u < XU; u++) {
+        const int cb = warp + 8 * u;
+#pragma unroll
+        for (int h = 0; h < XH; h++) {
+            const int m = h * 8 + (lane >> 2), tt = lane & 3, j = m / MPC, i = m - j * MPC;
+            xv[u][h] = cb < nb ? ld_f4(it.x + cb * F::COLS + 4 * E * j + E * tt + 4 * i)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < XU; u++) {
+        const int cb = warp + 8 * u;
+        if (cb >= nb) break;
         float mx = 0.0f;
 #pragma unroll
-        for (int h = 0; h < MPU / 8; h++) {
-            const int m = h * 8 + (lane >> 2), tt = lane & 3, j = m / MPC, i = m - j * MPC;
-            xv[h] = ld_f4(it.x + cb * F::COLS + 4 * E * j + E * tt + 4 * i);
-            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(xv[h].x), fabsf(xv[h].y)), fmaxf(fabsf(xv[h].z), fabsf(xv[h].w))));
-        }
+        for (int h = 0; h < XH; h++)
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(xv[u][h].x), fabsf(xv[u][h].y)),
+                                 fmaxf(fabsf(xv[u][h].z), fabsf(xv[u][h].w))));
         mx = warp_max_f(mx);
         int k = 0;
         if (!BF && mx > 0.0f && mx == mx) {
@@ -225,10 +238,10 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
             k = k > 126 ? 126 : (k < -126 ? -126 : k);
         }
 #pragma unroll
-        for (int h = 0; h < MPU / 8; h++) {
+        for (int h = 0; h < XH; h++) {
             const int m = h * 8 + (lane >> 2), tt = lane & 3;
             uint2 pc[3];
-            x_pieces<BF>(xv[h], BF ? 1.0f : pow2f(k), pc);
+            x_pieces<BF>(xv[u][h], BF ? 1.0f : pow2f(k), pc);
 #pragma unroll
             for (int p = 0; p < 3; p++) xp[(cb * MPU + m) * 12 + tt * 3 + p] = pc[p];
         }

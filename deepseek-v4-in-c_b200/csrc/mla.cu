@@ -29,12 +29,17 @@
 
 namespace dsv4b {
 
-__device__ __forceinline__ float load_elem(const void *base, size_t i, int dt)
+// Element i of a row store of type DT (compile-time, so batches of these
+// loads carry no branches and issue together).
+template <int DT>
+__device__ __forceinline__ float load_t(const void *base, size_t i)
 {
-    if (dt == DSV4B_DT_F32) return reinterpret_cast<const float *>(base)[i];
-    if (dt == DSV4B_DT_BF16) return __uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(base)[i] << 16);
-    return e4m3x2((uint16_t)reinterpret_cast<const uint8_t *>(base)[i]).x;
+    if constexpr (DT == DSV4B_DT_F32) return __ldcg(reinterpret_cast<const float *>(base) + i);
+    else if constexpr (DT == DSV4B_DT_BF16)
+        return __uint_as_float((uint32_t)__ldcg(reinterpret_cast<const unsigned short *>(base) + i) << 16);
+    else return e4m3x2((uint16_t)__ldcg(reinterpret_cast<const unsigned char *>(base) + i)).x;
 }
+template <int DT> constexpr int dt_bytes = DT == DSV4B_DT_F32 ? 4 : DT == DSV4B_DT_BF16 ? 2 : 1;
 
 // ---------------------------------------------------------------- indexer
 // grid (ceil(n_pos / 32), batch), 256 threads. Thread t: position t & 31 of
@@ -42,8 +47,9 @@ __device__ __forceinline__ float load_elem(const void *base, size_t i, int dt)
 // memory as double (keys transposed so a warp reads 32 consecutive doubles).
 constexpr int IX_TP = 32;
 
+template <int KDT>
 __global__ void __launch_bounds__(256)
-k_indexer_score(float *out, const float *q, const void *keys, int key_dt, long key_stride,
+k_indexer_score(float *out, const float *q, const void *keys, long key_stride,
                 long seq_key_stride, const float *w, int n_heads, int head_dim, int n_pos,
                 float scale, long seq_q_stride, long seq_out_stride, const int *dyn_n)
 {
@@ -54,15 +60,16 @@ k_indexer_score(float *out, const float *q, const void *keys, int key_dt, long k
     extern __shared__ double ixs[];
     double *qs = ixs;                               // [n_heads][head_dim]
     double *kt = qs + n_heads * head_dim;           // [head_dim][IX_TP]
-    double *dots = kt + head_dim * IX_TP;           // [IX_TP][n_heads]
+    double *dots = kt + head_dim * IX_TP;           // [IX_TP][n_heads + 1]
+    double *ws = dots + IX_TP * (n_heads + 1);      // [n_heads]
     const int b = blockIdx.y, t0 = blockIdx.x * IX_TP;
     q += (size_t)b * seq_q_stride;
     w += (size_t)b * n_heads;
     const char *kb = reinterpret_cast<const char *>(keys);
-    const int esz = key_dt == DSV4B_DT_F32 ? 4 : key_dt == DSV4B_DT_BF16 ? 2 : 1;
-    kb += (size_t)b * seq_key_stride * esz;
+    kb += (size_t)b * seq_key_stride * dt_bytes<KDT>;
     constexpr int LB = 16;                          // loads in flight per thread
     const int nq = n_heads * head_dim, nk = head_dim * IX_TP;
+    for (int h = threadIdx.x; h < n_heads; h += blockDim.x) ws[h] = (double)ld_act(w + h);
     for (int i0 = threadIdx.x; i0 < nq; i0 += LB * (int)blockDim.x) {
         float v[LB];
 #pragma unroll
@@ -82,7 +89,7 @@ k_indexer_score(float *out, const float *q, const void *keys, int key_dt, long k
         for (int u = 0; u < LB; u++) {
             const int i = i0 + u * (int)blockDim.x;
             const int p = i / head_dim, c = i - p * head_dim;
-            v[u] = (i < nk && t0 + p < n_pos) ? load_elem(kb, (size_t)(t0 + p) * key_stride + c, key_dt) : 0.0f;
+            v[u] = (i < nk && t0 + p < n_pos) ? load_t<KDT>(kb, (size_t)(t0 + p) * key_stride + c) : 0.0f;
         }
 #pragma unroll
         for (int u = 0; u < LB; u++) {
@@ -105,14 +112,14 @@ k_indexer_score(float *out, const float *q, const void *keys, int key_dt, long k
         }
 #pragma unroll
         for (int j = 0; j < 8; j++)
-            if (h0 + j < n_heads) dots[p * n_heads + h0 + j] = acc[j];
+            if (h0 + j < n_heads) dots[p * (n_heads + 1) + h0 + j] = acc[j];
     }
     __syncthreads();
     if (threadIdx.x < IX_TP && t0 + threadIdx.x < n_pos) {
         double total = 0.0;
         for (int h = 0; h < n_heads; h++) {
-            const double d = dots[threadIdx.x * n_heads + h];
-            if (d > 0.0) total = __dadd_rn(total, __dmul_rn(d, (double)w[h]));
+            const double d = dots[threadIdx.x * (n_heads + 1) + h];
+            if (d > 0.0) total = __dadd_rn(total, __dmul_rn(d, ws[h]));
         }
         out[(size_t)b * seq_out_stride + t0 + threadIdx.x] = __fmul_rn((float)total, scale);
     }
@@ -270,8 +277,9 @@ size_t attn_smem_bytes(int d) { return ((size_t)AT_CH * (d + 1) + (size_t)AT_HB 
 // grid (nchunk, ceil(n_heads / AT_HB), batch), 256 threads. The index list
 // holds its valid entries first, so the chunks past them only mark
 // themselves empty.
+template <int KDT>
 __global__ void __launch_bounds__(256)
-k_attn_chunk(AttnPart part, const float *q, const void *kv, int kv_dt, long seq_kv_rows,
+k_attn_chunk(AttnPart part, const float *q, const void *kv, long seq_kv_rows,
              const int *idxs, long seq_idx_stride, int n_heads, int d, int topk, float scale,
              long seq_q_stride)
 {
@@ -287,8 +295,7 @@ k_attn_chunk(AttnPart part, const float *q, const void *kv, int kv_dt, long seq_
     const int h0 = blockIdx.y * AT_HB, nh = min(AT_HB, n_heads - h0);
     q += (size_t)b * seq_q_stride + (size_t)h0 * d;
     idxs += (size_t)b * seq_idx_stride;
-    const int esz = kv_dt == DSV4B_DT_F32 ? 4 : kv_dt == DSV4B_DT_BF16 ? 2 : 1;
-    const char *kvb = reinterpret_cast<const char *>(kv) + (size_t)b * seq_kv_rows * d * esz;
+    const char *kvb = reinterpret_cast<const char *>(kv) + (size_t)b * seq_kv_rows * d * dt_bytes<KDT>;
     const int npos = min(AT_CH, topk - c0);
     const int pi = (tid < npos) ? idxs[c0 + tid] : -1;
     if (tid < AT_CH) pidx[tid] = pi;
@@ -314,7 +321,7 @@ k_attn_chunk(AttnPart part, const float *q, const void *kv, int kv_dt, long seq_
             const int p = i / d, c = i - p * d;
             const int r = (i < total) ? pidx[p] : -1;
             dst[u] = r >= 0 ? p * dp + c : -1;
-            v[u] = r >= 0 ? load_elem(kvb, (size_t)r * d + c, kv_dt) : 0.0f;
+            v[u] = r >= 0 ? load_t<KDT>(kvb, (size_t)r * d + c) : 0.0f;
         }
 #pragma unroll
         for (int u = 0; u < LB; u++)
@@ -339,9 +346,19 @@ k_attn_chunk(AttnPart part, const float *q, const void *kv, int kv_dt, long seq_
     {
         const int h = tid >> 5, p = tid & 31;
         if (h < nh) {
-            float acc = 0.0f;
+            // four interleaved partial sums (c mod 4), then (a0 + a1) + (a2 + a3)
+            float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
             const float *kr = kvs + p * dp, *qr = qs + h * d;
-            for (int c = 0; c < d; c++) acc = __fmaf_rn(qr[c], kr[c], acc);
+            int c = 0;
+#pragma unroll 4
+            for (; c + 3 < d; c += 4) {
+                a0 = __fmaf_rn(qr[c], kr[c], a0);
+                a1 = __fmaf_rn(qr[c + 1], kr[c + 1], a1);
+                a2 = __fmaf_rn(qr[c + 2], kr[c + 2], a2);
+                a3 = __fmaf_rn(qr[c + 3], kr[c + 3], a3);
+            }
+            for (; c < d; c++) a0 = __fmaf_rn(qr[c], kr[c], a0);
+            const float acc = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
             const float s = (pidx[p] >= 0) ? __fmul_rn(acc, scale) : -INFINITY;
             const float m = warp_max_f(s);
             const float e = (m == -INFINITY || s == -INFINITY) ? 0.0f : expf(s - m);
@@ -378,30 +395,36 @@ __global__ void k_attn_combine(float *o, AttnPart part, const float *sink, int n
     pdl_trigger();
     pdl_wait();
     __shared__ float fac[AT_MAXCH];
+    __shared__ unsigned char live[AT_MAXCH];
+    __shared__ double dterm[AT_MAXCH];
     __shared__ float s_inv, s_M;
     const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
     float *ob = o + (size_t)b * seq_o_stride + (size_t)h * d;
     const size_t r0 = (size_t)b * nch * n_heads + h;
+    // chunk maxima, factors and exp-sum terms, all chunks at once; the terms
+    // are then added in chunk order
+    for (int c = tid; c < nch; c += blockDim.x) fac[c] = ld_act(part.pm + r0 + (size_t)c * n_heads);
+    __syncthreads();
     if (tid < 32) {
         float M = -INFINITY;
-        for (int c = tid; c < nch; c += 32) M = fmaxf(M, ld_act(part.pm + r0 + (size_t)c * n_heads));
+        for (int c = tid; c < nch; c += 32) M = fmaxf(M, fac[c]);
         M = warp_max_f(M);
+        if (tid == 0) s_M = M;
+        __syncwarp();
         for (int c = tid; c < nch; c += 32) {
-            const float mc = ld_act(part.pm + r0 + (size_t)c * n_heads);
-            fac[c] = (mc == -INFINITY) ? 0.0f : ((mc == M) ? 1.0f : expf(mc - M));
+            const float mc = fac[c];
+            const bool lv = mc != -INFINITY;
+            live[c] = lv;
+            dterm[c] = lv ? ld_act_d(part.pden + r0 + (size_t)c * n_heads) * (double)expf(mc - M) : 0.0;
+            fac[c] = lv ? ((mc == M) ? 1.0f : expf(mc - M)) : 0.0f;
         }
         __syncwarp();
-        if (tid == 0) {
-            s_M = M;
-            if (M != -INFINITY) {
-                double den = 0.0;
-                for (int c = 0; c < nch; c++) {
-                    const float mc = part.pm[r0 + (size_t)c * n_heads];
-                    if (mc != -INFINITY) den += part.pden[r0 + (size_t)c * n_heads] * (double)expf(mc - M);
-                }
-                den += (double)expf(sink[h] - M);
-                s_inv = (float)(1.0 / den);
-            }
+        if (tid == 0 && M != -INFINITY) {
+            double den = 0.0;
+            for (int c = 0; c < nch; c++)
+                if (live[c]) den += dterm[c];
+            den += (double)expf(sink[h] - M);
+            s_inv = (float)(1.0 / den);
         }
     }
     __syncthreads();
@@ -414,9 +437,8 @@ __global__ void k_attn_combine(float *o, AttnPart part, const float *sink, int n
         float acc = 0.0f;
 #pragma unroll 4
         for (int c = 0; c < nch; c++) {
-            const float f = fac[c];
-            if (f == 0.0f && part.pm[r0 + (size_t)c * n_heads] == -INFINITY) continue;
-            acc = __fadd_rn(acc, __fmul_rn(ld_act(part.po + (r0 + (size_t)c * n_heads) * d + cc), f));
+            if (!live[c]) continue;
+            acc = __fadd_rn(acc, __fmul_rn(ld_act(part.po + (r0 + (size_t)c * n_heads) * d + cc), fac[c]));
         }
         ob[cc] = __fmul_rn(acc, inv);
     }
@@ -429,16 +451,27 @@ int indexer_score(float *out, const float *q, const void *keys, int key_dt, long
                   int batch, cudaStream_t st, const int *dyn_n)
 {
     if (n_pos <= 0 || batch <= 0) return 0;
-    const size_t smem = ((size_t)n_heads * head_dim + (size_t)head_dim * IX_TP + (size_t)IX_TP * n_heads) * 8;
+    const size_t smem = ((size_t)n_heads * head_dim + (size_t)head_dim * IX_TP + (size_t)IX_TP * (n_heads + 1) +
+                         (size_t)n_heads) * 8;
     if (smem > 200 * 1024) return -1;
     static bool attr = false;
     if (!attr) {
-        cudaFuncSetAttribute(k_indexer_score, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(k_indexer_score<DSV4B_DT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(k_indexer_score<DSV4B_DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(k_indexer_score<DSV4B_DT_E4M3>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         attr = true;
     }
     dim3 grid((n_pos + IX_TP - 1) / IX_TP, batch);
-    launch(k_indexer_score, dim3(grid), dim3(256), smem, st, out, q, keys, key_dt, key_stride, seq_key_stride, w, n_heads,
-                                             head_dim, n_pos, scale, (long)n_heads * head_dim, n_pos, dyn_n);
+    const long sq = (long)n_heads * head_dim;
+    if (key_dt == DSV4B_DT_F32)
+        launch(k_indexer_score<DSV4B_DT_F32>, grid, dim3(256), smem, st, out, q, keys, key_stride, seq_key_stride, w,
+               n_heads, head_dim, n_pos, scale, sq, n_pos, dyn_n);
+    else if (key_dt == DSV4B_DT_BF16)
+        launch(k_indexer_score<DSV4B_DT_BF16>, grid, dim3(256), smem, st, out, q, keys, key_stride, seq_key_stride, w,
+               n_heads, head_dim, n_pos, scale, sq, n_pos, dyn_n);
+    else
+        launch(k_indexer_score<DSV4B_DT_E4M3>, grid, dim3(256), smem, st, out, q, keys, key_stride, seq_key_stride, w,
+               n_heads, head_dim, n_pos, scale, sq, n_pos, dyn_n);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -482,12 +515,23 @@ int sparse_attn(float *o, const float *q, const void *kv, int kv_dt, long seq_kv
     const size_t smem = attn_smem_bytes(d);
     static bool attr = false;
     if (!attr) {
-        cudaFuncSetAttribute(k_attn_chunk, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        cudaFuncSetAttribute(k_attn_chunk<DSV4B_DT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        cudaFuncSetAttribute(k_attn_chunk<DSV4B_DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        cudaFuncSetAttribute(k_attn_chunk<DSV4B_DT_E4M3>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
         attr = true;
     }
     if (smem > 220 * 1024) return -1;
-    launch(k_attn_chunk, dim3(dim3(nch, (n_heads + AT_HB - 1) / AT_HB, batch)), dim3(256), smem, st, part, q, kv, kv_dt, seq_kv_rows, idxs, seq_idx_stride,
-                                                      n_heads, d, topk, scale, (long)n_heads * d);
+    const dim3 grid(nch, (n_heads + AT_HB - 1) / AT_HB, batch);
+    const long sq = (long)n_heads * d;
+    if (kv_dt == DSV4B_DT_F32)
+        launch(k_attn_chunk<DSV4B_DT_F32>, grid, dim3(256), smem, st, part, q, kv, seq_kv_rows, idxs, seq_idx_stride,
+               n_heads, d, topk, scale, sq);
+    else if (kv_dt == DSV4B_DT_BF16)
+        launch(k_attn_chunk<DSV4B_DT_BF16>, grid, dim3(256), smem, st, part, q, kv, seq_kv_rows, idxs, seq_idx_stride,
+               n_heads, d, topk, scale, sq);
+    else
+        launch(k_attn_chunk<DSV4B_DT_E4M3>, grid, dim3(256), smem, st, part, q, kv, seq_kv_rows, idxs, seq_idx_stride,
+               n_heads, d, topk, scale, sq);
     launch(k_attn_combine, dim3(dim3(n_heads, batch)), dim3(128), 0, st, o, part, sink, nch, n_heads, d, (long)n_heads * d);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }

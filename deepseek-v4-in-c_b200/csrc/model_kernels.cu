@@ -141,10 +141,13 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
     constexpr int MIXMAX = kHcPreMixMax;
     __shared__ double red[8][MIXMAX + 1];
     __shared__ double tot[MIXMAX + 1];
-    __shared__ float mixes[MIXMAX], pre[DSV4B_MAX_HC];
+    __shared__ float mixes[MIXMAX], pre[DSV4B_MAX_HC], sbase[MIXMAX], sscale[3];
+    __shared__ double pbuf[kHcPreBlocks * (MIXMAX + 1)];
     __shared__ bool last;
     const int n = hc * hidden, mix = (2 + hc) * hc, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     pdl_trigger();
+    if (tid < mix) sbase[tid] = __ldg(base + tid);        // weights: before the wait
+    if (tid < 3) sscale[tid] = __ldg(scale + tid);
     double acc[MIXMAX + 1];
 #pragma unroll
     for (int m = 0; m <= MIXMAX; m++) acc[m] = 0.0;
@@ -182,10 +185,13 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
     __syncthreads();
     if (!last) return;
     __threadfence();
+    // every block's partials in one batch of loads, then summed in block order
+    const int np = (int)gridDim.x * (MIXMAX + 1);
+    for (int k = tid; k < np; k += blockDim.x) pbuf[k] = __ldcg(part + k);
+    __syncthreads();
     if (tid <= MIXMAX) {
         double t = 0.0;
-#pragma unroll 8
-        for (int b = 0; b < (int)gridDim.x; b++) t += __ldcg(part + (size_t)b * (MIXMAX + 1) + tid);
+        for (int b = 0; b < (int)gridDim.x; b++) t += pbuf[b * (MIXMAX + 1) + tid];
         tot[tid] = t;
     }
     __syncthreads();
@@ -199,11 +205,11 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
         const int l = tid, j = l / hc, k = l % hc;
         const bool act = l < hc * hc;
         if (l < hc) {
-            pre[l] = __fadd_rn(sigm(__fadd_rn(__fmul_rn(mixes[l], scale[0]), base[l])), hc_eps);
-            post[l] = __fmul_rn(2.0f, sigm(__fadd_rn(__fmul_rn(mixes[l + hc], scale[1]), base[l + hc])));
+            pre[l] = __fadd_rn(sigm(__fadd_rn(__fmul_rn(mixes[l], sscale[0]), sbase[l])), hc_eps);
+            post[l] = __fmul_rn(2.0f, sigm(__fadd_rn(__fmul_rn(mixes[l + hc], sscale[1]), sbase[l + hc])));
         }
         const int o = 2 * hc + (act ? l : 0);
-        float v = __fadd_rn(__fmul_rn(mixes[o], scale[2]), base[o]);
+        float v = __fadd_rn(__fmul_rn(mixes[o], sscale[2]), sbase[o]);
         // row softmax: max, exp, double sum in k order, scale, + eps
         float mx = __shfl_sync(0xffffffffu, v, (j * hc) & 31);
         for (int kk = 1; kk < hc; kk++) {
@@ -235,25 +241,39 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
     const float4 *x4 = reinterpret_cast<const float4 *>(x);
     float4 yv[kHcPreYPT];
     double sq = 0.0;
+    constexpr int YB = kHcPreYPT / 2;         // column groups per batch of loads
 #pragma unroll
-    for (int u = 0; u < kHcPreYPT; u++) {
-        const int d4 = tid + u * (int)blockDim.x;
-        yv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (d4 < h4) {
-            double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
-            for (int j = 0; j < hc; j++) {
-                const float4 v = __ldcg(x4 + (size_t)j * h4 + d4);
-                const double pj = (double)pre[j];
-                a0 = __dadd_rn(a0, __dmul_rn(pj, (double)v.x));
-                a1 = __dadd_rn(a1, __dmul_rn(pj, (double)v.y));
-                a2 = __dadd_rn(a2, __dmul_rn(pj, (double)v.z));
-                a3 = __dadd_rn(a3, __dmul_rn(pj, (double)v.w));
+    for (int half = 0; half < 2; half++) {
+        float4 xv[YB][4];
+#pragma unroll
+        for (int uu = 0; uu < YB; uu++) {
+            const int d4 = tid + (half * YB + uu) * (int)blockDim.x;
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                xv[uu][j] = (d4 < h4 && j < hc) ? __ldcg(x4 + (size_t)j * h4 + d4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int uu = 0; uu < YB; uu++) {
+            const int u = half * YB + uu, d4 = tid + u * (int)blockDim.x;
+            yv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (d4 < h4) {
+                double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    if (j < hc) {
+                        const double pj = (double)pre[j];
+                        a0 = __dadd_rn(a0, __dmul_rn(pj, (double)xv[uu][j].x));
+                        a1 = __dadd_rn(a1, __dmul_rn(pj, (double)xv[uu][j].y));
+                        a2 = __dadd_rn(a2, __dmul_rn(pj, (double)xv[uu][j].z));
+                        a3 = __dadd_rn(a3, __dmul_rn(pj, (double)xv[uu][j].w));
+                    }
+                }
+                yv[u] = make_float4((float)a0, (float)a1, (float)a2, (float)a3);
+                sq = __fma_rn((double)yv[u].x, (double)yv[u].x, sq);
+                sq = __fma_rn((double)yv[u].y, (double)yv[u].y, sq);
+                sq = __fma_rn((double)yv[u].z, (double)yv[u].z, sq);
+                sq = __fma_rn((double)yv[u].w, (double)yv[u].w, sq);
             }
-            yv[u] = make_float4((float)a0, (float)a1, (float)a2, (float)a3);
-            sq = __fma_rn((double)yv[u].x, (double)yv[u].x, sq);
-            sq = __fma_rn((double)yv[u].y, (double)yv[u].y, sq);
-            sq = __fma_rn((double)yv[u].z, (double)yv[u].z, sq);
-            sq = __fma_rn((double)yv[u].w, (double)yv[u].w, sq);
         }
     }
     float inv = 1.0f;

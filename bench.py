@@ -50,9 +50,9 @@ NCOPY = 8
 DECODE_METRIC = "batch-1 decode tok/s (Flash-scale synthetic, config 5)"
 GEMV_METRIC = "FP8 block-scaled GEMV HBM GB/s (config 1, 4096x7168 e4m3, batch 1)"
 
-# DRAM bytes (read + write) per unit from ncu, or None while no capture of
-# that kernel and workload has been summarised under profiles/.
-TRAFFIC_C1 = None
+# DRAM bytes (read + write) per unit from an ncu capture of the same kernel
+# and workload, or None where none was taken.
+TRAFFIC_C1 = 29456384          # one config-1 GEMV launch
 TRAFFIC_DECODE = None
 
 
@@ -123,11 +123,12 @@ def dist_setup(n):
     return rank, world, dist
 
 
-def max_over_ranks(dist, ms):
+def max_over_ranks(dist, ms, device="cuda"):
+    """The slowest rank's value (every rank calls it, in the same order)."""
     if not dist:
         return ms
     import torch
-    t = torch.tensor([ms], device="cuda")
+    t = torch.tensor([float(ms)], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 

@@ -461,9 +461,11 @@ int gemv_group(GemvItem *items, int n, cudaStream_t st)
     }
     double total = 0.0;
     for (int i = 0; i < n; i++) total += (double)items[i].rows * items[i].rowbytes * (items[i].pair ? 2 : 1);
-    // about four blocks per SM, each streaming 16-128 KB
-    double target = total / (4.0 * nsm);
-    target = target < 16384.0 ? 16384.0 : (target > 131072.0 ? 131072.0 : target);
+    // one wave of two resident blocks per SM, each streaming 16-256 KB: a
+    // block's prologue (x fragments, pipeline fill) is paid once for as much
+    // streaming as it can get, and no second wave leaves SMs idle at the end
+    double target = total / (2.0 * nsm);
+    target = target < 16384.0 ? 16384.0 : (target > 262144.0 ? 262144.0 : target);
     GemvBatch b;
     b.n = n;
     int blocks = 0;

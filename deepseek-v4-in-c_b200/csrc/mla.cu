@@ -272,11 +272,31 @@ struct AttnPart {
     double *pden;
 };
 
-size_t attn_smem_bytes(int d) { return ((size_t)AT_CH * (d + 1) + (size_t)AT_HB * d + AT_HB * AT_CH) * 4; }
+// Rows of the KV tile are padded to d + 4 floats: 16-byte aligned, and the
+// float4 reads of 8 consecutive lanes (one shared-memory phase) of rows p..p+7
+// fall in distinct banks.
+size_t attn_smem_bytes(int d) { return ((size_t)AT_CH * (d + 4) + (size_t)AT_HB * d + AT_CH * AT_HB) * 4; }
+
+// Four consecutive elements of a row store of type DT as a float4 (the row
+// offset e is a multiple of 4 and the store is aligned for it).
+template <int DT>
+__device__ __forceinline__ float4 load4_t(const void *base, size_t e)
+{
+    if constexpr (DT == DSV4B_DT_F32) return __ldcg(reinterpret_cast<const float4 *>(base) + (e >> 2));
+    else if constexpr (DT == DSV4B_DT_BF16) {
+        const uint2 v = __ldcg(reinterpret_cast<const uint2 *>(base) + (e >> 2));
+        const float2 a = bf16x2(v.x), b = bf16x2(v.y);
+        return make_float4(a.x, a.y, b.x, b.y);
+    } else {
+        const uint32_t v = __ldcg(reinterpret_cast<const unsigned int *>(base) + (e >> 2));
+        const float2 a = e4m3x2((uint16_t)(v & 0xFFFFu)), b = e4m3x2((uint16_t)(v >> 16));
+        return make_float4(a.x, a.y, b.x, b.y);
+    }
+}
 
 // grid (nchunk, ceil(n_heads / AT_HB), batch), 256 threads. The index list
 // holds its valid entries first, so the chunks past them only mark
-// themselves empty.
+// themselves empty. d is a multiple of 4.
 template <int KDT>
 __global__ void __launch_bounds__(256)
 k_attn_chunk(AttnPart part, const float *q, const void *kv, long seq_kv_rows,
@@ -285,11 +305,11 @@ k_attn_chunk(AttnPart part, const float *q, const void *kv, long seq_kv_rows,
 {
     pdl_trigger();
     pdl_wait();
-    extern __shared__ float ats[];
-    const int dp = d + 1;                                   // padded row: conflict-free
+    extern __shared__ __align__(16) float ats[];
+    const int dp = d + 4, nd4 = d >> 2;
     float *kvs = ats;                                       // [AT_CH][dp]
     float *qs = kvs + AT_CH * dp;                           // [AT_HB][d]
-    float *sc = qs + AT_HB * d;                             // [AT_HB][AT_CH]
+    float *scT = qs + AT_HB * d;                            // [AT_CH][AT_HB]: weights, transposed
     __shared__ int pidx[AT_CH];
     const int b = blockIdx.z, nch = gridDim.x, c0 = blockIdx.x * AT_CH, tid = threadIdx.x;
     const int h0 = blockIdx.y * AT_HB, nh = min(AT_HB, n_heads - h0);
@@ -307,80 +327,96 @@ k_attn_chunk(AttnPart part, const float *q, const void *kv, long seq_kv_rows,
         }
         return;
     }
-    // valid rows and the block's q tile into shared memory, 16 loads in
-    // flight per thread (masked rows stay unwritten: their scores become
-    // -inf and their weights 0, so they are never read)
-    constexpr int LB = 16;
-    const int total = AT_CH * d;
-    for (int i0 = tid; i0 < total; i0 += LB * (int)blockDim.x) {
-        float v[LB];
-        int dst[LB];
+    // KV rows: thread (row tid/8, lane group tid%8) moves float4 groups
+    // g = tid%8 + 8k of its row, 8 loads in flight; masked rows are skipped
+    // (their scores become -inf and their weights 0, so they are never read)
+    {
+        const int p = tid >> 3, part8 = tid & 7, r = pidx[p];
+        if (r >= 0) {
+            for (int g0 = part8; g0 < nd4; g0 += 64) {
+                float4 v[8];
 #pragma unroll
-        for (int u = 0; u < LB; u++) {
-            const int i = i0 + u * (int)blockDim.x;
-            const int p = i / d, c = i - p * d;
-            const int r = (i < total) ? pidx[p] : -1;
-            dst[u] = r >= 0 ? p * dp + c : -1;
-            v[u] = r >= 0 ? load_t<KDT>(kvb, (size_t)r * d + c) : 0.0f;
+                for (int u = 0; u < 8; u++) {
+                    const int g = g0 + 8 * u;
+                    v[u] = g < nd4 ? load4_t<KDT>(kvb, (size_t)r * d + 4 * g) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const int g = g0 + 8 * u;
+                    if (g < nd4) *reinterpret_cast<float4 *>(kvs + p * dp + 4 * g) = v[u];
+                }
+            }
         }
-#pragma unroll
-        for (int u = 0; u < LB; u++)
-            if (dst[u] >= 0) kvs[dst[u]] = v[u];
     }
-    for (int i0 = tid; i0 < nh * d; i0 += LB * (int)blockDim.x) {
-        float v[LB];
+    // the block's q tile
+    {
+        const int n4 = nh * nd4;
+        for (int i0 = tid; i0 < n4; i0 += 8 * (int)blockDim.x) {
+            float4 v[8];
 #pragma unroll
-        for (int u = 0; u < LB; u++) {
-            const int i = i0 + u * (int)blockDim.x;
-            v[u] = i < nh * d ? ld_act(q + i) : 0.0f;
-        }
+            for (int u = 0; u < 8; u++) {
+                const int i = i0 + u * (int)blockDim.x;
+                v[u] = i < n4 ? __ldcg(reinterpret_cast<const float4 *>(q) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
 #pragma unroll
-        for (int u = 0; u < LB; u++) {
-            const int i = i0 + u * (int)blockDim.x;
-            if (i < nh * d) qs[i] = v[u];
+            for (int u = 0; u < 8; u++) {
+                const int i = i0 + u * (int)blockDim.x;
+                if (i < n4) reinterpret_cast<float4 *>(qs)[i] = v[u];
+            }
         }
     }
     __syncthreads();
-    // scores: warp = head, lane = position; then the chunk max over valid
-    // slots (the sink is not part of it), exp weights, exp-sum in double
+    // scores: warp = head, lane = position; four partial sums over c mod 4,
+    // then (a0 + a1) + (a2 + a3); the chunk max over valid slots (the sink is
+    // not part of it), exp weights, exp-sum in double
     {
         const int h = tid >> 5, p = tid & 31;
         if (h < nh) {
-            // four interleaved partial sums (c mod 4), then (a0 + a1) + (a2 + a3)
             float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-            const float *kr = kvs + p * dp, *qr = qs + h * d;
-            int c = 0;
+            const float4 *k4 = reinterpret_cast<const float4 *>(kvs + p * dp);
+            const float4 *q4 = reinterpret_cast<const float4 *>(qs + h * d);
 #pragma unroll 4
-            for (; c + 3 < d; c += 4) {
-                a0 = __fmaf_rn(qr[c], kr[c], a0);
-                a1 = __fmaf_rn(qr[c + 1], kr[c + 1], a1);
-                a2 = __fmaf_rn(qr[c + 2], kr[c + 2], a2);
-                a3 = __fmaf_rn(qr[c + 3], kr[c + 3], a3);
+            for (int g = 0; g < nd4; g++) {
+                const float4 qv = q4[g], kv4 = k4[g];
+                a0 = __fmaf_rn(qv.x, kv4.x, a0);
+                a1 = __fmaf_rn(qv.y, kv4.y, a1);
+                a2 = __fmaf_rn(qv.z, kv4.z, a2);
+                a3 = __fmaf_rn(qv.w, kv4.w, a3);
             }
-            for (; c < d; c++) a0 = __fmaf_rn(qr[c], kr[c], a0);
             const float acc = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
             const float s = (pidx[p] >= 0) ? __fmul_rn(acc, scale) : -INFINITY;
             const float m = warp_max_f(s);
             const float e = (m == -INFINITY || s == -INFINITY) ? 0.0f : expf(s - m);
             const double ds = warp_sum_d((double)e);
-            sc[h * AT_CH + p] = e;
+            scT[p * AT_HB + h] = e;
             if (p == 0) {
                 part.pm[prow + h] = m;
                 part.pden[prow + h] = ds;
             }
+        } else if (tid - 32 * nh < 32 * (AT_HB - nh) && (tid & 31) < AT_CH) {
+            scT[(tid & 31) * AT_HB + h] = 0.0f;         // heads past n_heads
         }
     }
     __syncthreads();
-    // unnormalised value sums, positions in order
-    for (int i = tid; i < nh * d; i += blockDim.x) {
-        const int h = i / d, c = i - h * d;
-        float o = 0.0f;
-#pragma unroll 8
+    // unnormalised value sums: a thread owns columns c and every head of the
+    // block; positions in order, each product and sum rounded separately
+    for (int c = tid; c < d; c += blockDim.x) {
+        float o[AT_HB];
+#pragma unroll
+        for (int h = 0; h < AT_HB; h++) o[h] = 0.0f;
+#pragma unroll 4
         for (int pp = 0; pp < AT_CH; pp++) {
-            const float e = sc[h * AT_CH + pp];
-            if (e != 0.0f) o = __fadd_rn(o, __fmul_rn(e, kvs[pp * dp + c]));
+            const float4 ea = *reinterpret_cast<const float4 *>(scT + pp * AT_HB);
+            const float4 eb = *reinterpret_cast<const float4 *>(scT + pp * AT_HB + 4);
+            const float e[AT_HB] = {ea.x, ea.y, ea.z, ea.w, eb.x, eb.y, eb.z, eb.w};
+            const float kvv = kvs[pp * dp + c];
+#pragma unroll
+            for (int h = 0; h < AT_HB; h++)
+                o[h] = (e[h] != 0.0f) ? __fadd_rn(o[h], __fmul_rn(e[h], kvv)) : o[h];
         }
-        part.po[(prow + h) * d + c] = o;
+#pragma unroll
+        for (int h = 0; h < AT_HB; h++)
+            if (h < nh) part.po[(prow + h) * d + c] = o[h];
     }
 }
 
@@ -504,7 +540,7 @@ int sparse_attn(float *o, const float *q, const void *kv, int kv_dt, long seq_kv
                 void *part_buf, cudaStream_t st)
 {
     if (batch <= 0 || topk <= 0) return 0;
-    if (n_heads <= 0 || d > 1024) return -1;
+    if (n_heads <= 0 || d > 1024 || (d & 3)) return -1;
     const int nch = (topk + AT_CH - 1) / AT_CH;
     if (nch > AT_MAXCH) return -1;
     const size_t n = (size_t)batch * nch * n_heads;

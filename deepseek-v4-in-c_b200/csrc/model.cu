@@ -269,8 +269,9 @@ static int hc_pre(dsv4b_model *m, const float *h, const float *fn, const float *
 {
     const DSV4Cfg &c = m->c;
     const int hc = c.hc_mult, mix = (2 + hc) * hc, n = hc * c.hidden;
-    if (mix <= kHcPreMixMax && c.hidden % 4 == 0 && c.hidden <= 256 * 4 * kHcPreYPT) {
-        launch(k_hc_pre, dim3(kHcPreBlocks), dim3(256), 0, st, m->x1, m->post, m->comb, h, fn, scale, base, norm, m->hc_part,
+    if (mix <= kHcPreMixMax && c.hidden % 4 == 0 && c.hidden <= 256 * 4 * kHcPreYPT && n % 256 == 0 &&
+        n / 256 <= kHcPreBlocks) {
+        launch(k_hc_pre, dim3(n / 256), dim3(256), 0, st, m->x1, m->post, m->comb, h, fn, scale, base, norm, m->hc_part,
                                                m->hc_cnt, hc, c.hidden, c.hc_sinkhorn_iters, c.hc_eps,
                                                c.rms_eps);
         return 0;

@@ -125,59 +125,58 @@ __global__ void k_hc_finish(float *y, float *post, float *comb, const float *mix
 // The whole mHC pre-mix of one sub-layer in one launch, with the sub-layer's
 // RMSNorm folded in (src/core/dsv4_hc.c:118-140 with dsv4_hc_split_sinkhorn
 // :50-102, then src/core/dsv4_ops.c:25-32 when norm_w is given):
-//   every block: double partial sums of x.x and fn[m].x over its columns,
-//                written to part[block][0..mix];
-//   last block:  the partials summed in block order, mixes, the Sinkhorn
-//                split (lanes of one warp, each lane one comb entry; every
-//                row / column sum is gathered by shuffles and added in the
-//                serial order), y = sum_j pre[j] x[j] in double, RMSNorm.
-// The last block is the one whose arrival at *count completes the grid; it
-// resets *count, so the kernel is replayable. hc * hc <= 32.
+//   every block: per column the products fn[m][i] * x[i] and x[i]^2 (float),
+//                summed per block in a fixed order (32 columns in float, then
+//                8 such sums in double), written to part[block][0..mix];
+//   last block:  the partials summed in block order (double), mixes, the
+//                Sinkhorn split (lanes of one warp, each lane one comb entry;
+//                every row / column sum gathered by shuffles and added in the
+//                serial order), y = sum_j pre[j] x[j], RMSNorm.
+// The reference sums these in double; here only the short sums across warps
+// and blocks are, which keeps the result within ~1e-7 of it while avoiding
+// long chains of double operations. The last block is the one whose arrival
+// at *count completes the grid; it resets *count, so the kernel is
+// replayable. hc * hc <= 32.
 __global__ void __launch_bounds__(256)
 k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, const float *scale,
          const float *base, const float *norm_w, double *part, unsigned *count, int hc, int hidden,
          int iters, float hc_eps, float rms_eps)
 {
-    constexpr int MIXMAX = kHcPreMixMax;
-    __shared__ double red[8][MIXMAX + 1];
-    __shared__ double tot[MIXMAX + 1];
+    constexpr int MIXMAX = kHcPreMixMax, NV = MIXMAX + 1;
+    __shared__ float prod[NV][256];
+    __shared__ double red8[NV][8];
+    __shared__ double tot[NV];
     __shared__ float mixes[MIXMAX], pre[DSV4B_MAX_HC], sbase[MIXMAX], sscale[3];
-    __shared__ double pbuf[kHcPreBlocks * (MIXMAX + 1)];
     __shared__ bool last;
-    const int n = hc * hidden, mix = (2 + hc) * hc, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int n = hc * hidden, mix = (2 + hc) * hc, tid = threadIdx.x;
     pdl_trigger();
     if (tid < mix) sbase[tid] = __ldg(base + tid);        // weights: before the wait
     if (tid < 3) sscale[tid] = __ldg(scale + tid);
-    double acc[MIXMAX + 1];
-#pragma unroll
-    for (int m = 0; m <= MIXMAX; m++) acc[m] = 0.0;
-    // the fn column is a weight: fetched before waiting for x
-    const int stride = gridDim.x * blockDim.x;
-    int i = blockIdx.x * blockDim.x + tid;
+    // one column per thread (the launcher sizes the grid to n / 256); its fn
+    // column is a weight, fetched before waiting for x
+    const int i = blockIdx.x * blockDim.x + tid;
     float fv[MIXMAX];
 #pragma unroll
     for (int m = 0; m < MIXMAX; m++) fv[m] = (m < mix && i < n) ? __ldg(fn + (size_t)m * n + i) : 0.0f;
     pdl_wait();
-    for (; i < n; i += stride) {
-        const double xv = (double)x[i];
-        acc[MIXMAX] = __fma_rn(xv, xv, acc[MIXMAX]);
+    const float xv = i < n ? __ldcg(x + i) : 0.0f;
 #pragma unroll
-        for (int m = 0; m < MIXMAX; m++)
-            if (m < mix) acc[m] = __fma_rn((double)fv[m], xv, acc[m]);
-        const int i2 = i + stride;
-#pragma unroll
-        for (int m = 0; m < MIXMAX; m++) fv[m] = (m < mix && i2 < n) ? __ldg(fn + (size_t)m * n + i2) : 0.0f;
-    }
-#pragma unroll
-    for (int m = 0; m <= MIXMAX; m++) {
-        const double v = warp_sum_d(acc[m]);
-        if (lane == 0) red[w][m] = v;
+    for (int m = 0; m < MIXMAX; m++) prod[m][tid] = __fmul_rn(fv[m], xv);
+    prod[MIXMAX][tid] = __fmul_rn(xv, xv);
+    __syncthreads();
+    if (tid < NV * 8) {
+        const int m = tid >> 3, w = tid & 7;
+        float sacc = 0.0f;
+#pragma unroll 8
+        for (int k = 0; k < 32; k++) sacc = __fadd_rn(sacc, prod[m][w * 32 + k]);
+        red8[m][w] = (double)sacc;
     }
     __syncthreads();
-    if (tid <= MIXMAX) {
+    if (tid < NV) {
         double t = 0.0;
-        for (int k = 0; k < (int)(blockDim.x >> 5); k++) t += red[k][tid];
-        part[(size_t)blockIdx.x * (MIXMAX + 1) + tid] = t;
+#pragma unroll
+        for (int w = 0; w < 8; w++) t += red8[tid][w];
+        part[(size_t)blockIdx.x * NV + tid] = t;
     }
     __threadfence();
     __syncthreads();
@@ -185,13 +184,23 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
     __syncthreads();
     if (!last) return;
     __threadfence();
-    // every block's partials in one batch of loads, then summed in block order
-    const int np = (int)gridDim.x * (MIXMAX + 1);
-    for (int k = tid; k < np; k += blockDim.x) pbuf[k] = __ldcg(part + k);
-    __syncthreads();
-    if (tid <= MIXMAX) {
+    // every block's partials: 8 threads per value each add gridDim/8 blocks,
+    // then the 8 sums in order
+    const int nblk = (int)gridDim.x, per = (nblk + 7) >> 3;
+    if (tid < NV * 8) {
+        const int m = tid >> 3, w = tid & 7;
         double t = 0.0;
-        for (int b = 0; b < (int)gridDim.x; b++) t += pbuf[b * (MIXMAX + 1) + tid];
+        for (int k = 0; k < per; k++) {
+            const int bb = w * per + k;
+            if (bb < nblk) t += __ldcg(part + (size_t)bb * NV + m);
+        }
+        red8[m][w] = t;
+    }
+    __syncthreads();
+    if (tid < NV) {
+        double t = 0.0;
+#pragma unroll
+        for (int w = 0; w < 8; w++) t += red8[tid][w];
         tot[tid] = t;
     }
     __syncthreads();
@@ -210,77 +219,76 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
         }
         const int o = 2 * hc + (act ? l : 0);
         float v = __fadd_rn(__fmul_rn(mixes[o], sscale[2]), sbase[o]);
-        // row softmax: max, exp, double sum in k order, scale, + eps
+        // row softmax: max, exp, sum in k order, scale, + eps
         float mx = __shfl_sync(0xffffffffu, v, (j * hc) & 31);
         for (int kk = 1; kk < hc; kk++) {
             const float r = __shfl_sync(0xffffffffu, v, (j * hc + kk) & 31);
             if (r > mx) mx = r;
         }
         const float e = expf(v - mx);
-        double sum = 0.0;
-        for (int kk = 0; kk < hc; kk++) sum += (double)__shfl_sync(0xffffffffu, e, (j * hc + kk) & 31);
-        const float inv = (float)(1.0 / sum);
+        float sum = 0.0f;
+        for (int kk = 0; kk < hc; kk++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, e, (j * hc + kk) & 31));
+        const float inv = __fdiv_rn(1.0f, sum);
         v = __fadd_rn(__fmul_rn(e, inv), hc_eps);
         const int npass = iters > 1 ? iters : 1;
         for (int pass = 0; pass < npass; pass++) {
             if (pass > 0) {
-                double r = 0.0;
-                for (int kk = 0; kk < hc; kk++) r += (double)__shfl_sync(0xffffffffu, v, (j * hc + kk) & 31);
-                v = __fdiv_rn(v, __fadd_rn((float)r, hc_eps));
+                float r = 0.0f;
+                for (int kk = 0; kk < hc; kk++) r = __fadd_rn(r, __shfl_sync(0xffffffffu, v, (j * hc + kk) & 31));
+                v = __fdiv_rn(v, __fadd_rn(r, hc_eps));
             }
-            double c = 0.0;
-            for (int jj = 0; jj < hc; jj++) c += (double)__shfl_sync(0xffffffffu, v, (jj * hc + k) & 31);
-            v = __fdiv_rn(v, __fadd_rn((float)c, hc_eps));
+            float c = 0.0f;
+            for (int jj = 0; jj < hc; jj++) c = __fadd_rn(c, __shfl_sync(0xffffffffu, v, (jj * hc + k) & 31));
+            v = __fdiv_rn(v, __fadd_rn(c, hc_eps));
         }
         if (act) comb[l] = v;
     }
     __syncthreads();
-    // y = sum_j pre[j] x[j] in double, four columns per float4, all loads of
-    // a thread issued together; then RMSNorm from the registers
+    // y = sum_j pre[j] x[j], four columns per float4, in two batches of loads;
+    // then RMSNorm from the registers
     const int h4 = hidden >> 2;
     const float4 *x4 = reinterpret_cast<const float4 *>(x);
     float4 yv[kHcPreYPT];
-    double sq = 0.0;
-    constexpr int YB = kHcPreYPT / 2;         // column groups per batch of loads
+    float sq = 0.0f;
+    constexpr int YB = kHcPreYPT / 2;
 #pragma unroll
     for (int half = 0; half < 2; half++) {
-        float4 xv[YB][4];
+        float4 xw[YB][4];
 #pragma unroll
         for (int uu = 0; uu < YB; uu++) {
             const int d4 = tid + (half * YB + uu) * (int)blockDim.x;
 #pragma unroll
             for (int j = 0; j < 4; j++)
-                xv[uu][j] = (d4 < h4 && j < hc) ? __ldcg(x4 + (size_t)j * h4 + d4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                xw[uu][j] = (d4 < h4 && j < hc) ? __ldcg(x4 + (size_t)j * h4 + d4) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int uu = 0; uu < YB; uu++) {
             const int u = half * YB + uu, d4 = tid + u * (int)blockDim.x;
-            yv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
             if (d4 < h4) {
-                double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
                     if (j < hc) {
-                        const double pj = (double)pre[j];
-                        a0 = __dadd_rn(a0, __dmul_rn(pj, (double)xv[uu][j].x));
-                        a1 = __dadd_rn(a1, __dmul_rn(pj, (double)xv[uu][j].y));
-                        a2 = __dadd_rn(a2, __dmul_rn(pj, (double)xv[uu][j].z));
-                        a3 = __dadd_rn(a3, __dmul_rn(pj, (double)xv[uu][j].w));
+                        const float pj = pre[j];
+                        a.x = __fmaf_rn(pj, xw[uu][j].x, a.x);
+                        a.y = __fmaf_rn(pj, xw[uu][j].y, a.y);
+                        a.z = __fmaf_rn(pj, xw[uu][j].z, a.z);
+                        a.w = __fmaf_rn(pj, xw[uu][j].w, a.w);
                     }
                 }
-                yv[u] = make_float4((float)a0, (float)a1, (float)a2, (float)a3);
-                sq = __fma_rn((double)yv[u].x, (double)yv[u].x, sq);
-                sq = __fma_rn((double)yv[u].y, (double)yv[u].y, sq);
-                sq = __fma_rn((double)yv[u].z, (double)yv[u].z, sq);
-                sq = __fma_rn((double)yv[u].w, (double)yv[u].w, sq);
+                sq = __fmaf_rn(a.x, a.x, sq);
+                sq = __fmaf_rn(a.y, a.y, sq);
+                sq = __fmaf_rn(a.z, a.z, sq);
+                sq = __fmaf_rn(a.w, a.w, sq);
             }
+            yv[u] = a;
         }
     }
     float inv = 1.0f;
     if (norm_w) {
         __shared__ double nred[33];
-        sq = block_sum_d(sq, nred);
-        inv = (float)(1.0 / sqrt(sq / (double)hidden + (double)rms_eps));
+        const double ssq = block_sum_d((double)sq, nred);
+        inv = (float)(1.0 / sqrt(ssq / (double)hidden + (double)rms_eps));
     }
     float4 *y4 = reinterpret_cast<float4 *>(y);
     const float4 *w4 = reinterpret_cast<const float4 *>(norm_w);

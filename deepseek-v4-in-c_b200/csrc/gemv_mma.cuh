@@ -13,8 +13,10 @@
 // Order (the canonical one for these formats, used by every kernel that
 // computes them): a row is cut into blocks of 128 columns. For each block b
 // the tensor core accumulates, from zero, the block's 8 k16-steps into C[n];
-// q_b = (((C[0] + C[1]) + C[2]) * 2^-k) * scale_b in float; the row total is
-// ((0 + q_0) + q_1) + ... in double, in block order; y = (float)total.
+// q_b = (((C[0] + C[1]) + C[2]) * 2^-k) * scale_b in float; the blocks are
+// cut into eight contiguous runs of ceil(nb / 8), each run summed from zero
+// in double in block order, the eight run sums added in order in double;
+// y = (float)total.
 //
 // Work: a block of 8 warps streams a tile of rows (a multiple of 16); a unit
 // is 16 rows x one 128-column block, taken by the warps in turn. Lane
@@ -326,20 +328,33 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
     }
     cp_wait<0>();
     __syncthreads();
+    // row totals: 8 lanes per virtual row each add a contiguous eighth of the
+    // blocks in double, then the eight sums in order; the total lands in the
+    // row's spare slot qs[v][nb]
+    {
+        const int per = (nb + 7) >> 3, w8 = tid & 7;
+        for (int v0 = 0; v0 < it.tr; v0 += (int)blockDim.x >> 3) {
+            const int v = v0 + (tid >> 3);
+            double tw = 0.0;
+            if (v < it.tr) {
+                const float *sr = qs + v * (nb + 1) + w8 * per;
+                const int cnt = min(per, nb - w8 * per);
+                for (int k = 0; k < cnt; k++) tw = __dadd_rn(tw, (double)sr[k]);
+            }
+            double tot = 0.0;
+#pragma unroll
+            for (int w = 0; w < 8; w++) tot = __dadd_rn(tot, __shfl_sync(0xffffffffu, tw, (lane & ~7) | w));
+            __syncwarp();
+            if (w8 == 0 && v < it.tr) qs[v * (nb + 1) + nb] = (float)tot;
+        }
+    }
+    __syncthreads();
     const int nreal = it.pair ? trh : it.tr;
     for (int r = tid; r < nreal; r += blockDim.x) {
         const int row = tile * nreal + r;
         if (row >= it.rows) break;
-        const float *sr = qs + r * (nb + 1);
-        double tot = 0.0;
-        for (int b = 0; b < nb; b++) tot = __dadd_rn(tot, (double)sr[b]);
-        float a = (float)tot;
-        if (it.pair) {
-            const float *s2 = qs + (r + trh) * (nb + 1);
-            double t2 = 0.0;
-            for (int b = 0; b < nb; b++) t2 = __dadd_rn(t2, (double)s2[b]);
-            a = swiglu_pair(a, (float)t2, it.limit);
-        }
+        float a = qs[r * (nb + 1) + nb];
+        if (it.pair) a = swiglu_pair(a, qs[(r + trh) * (nb + 1) + nb], it.limit);
         it.y[row] = a;
     }
 }

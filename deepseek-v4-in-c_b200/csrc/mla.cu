@@ -41,6 +41,24 @@ __device__ __forceinline__ float load_t(const void *base, size_t i)
 }
 template <int DT> constexpr int dt_bytes = DT == DSV4B_DT_F32 ? 4 : DT == DSV4B_DT_BF16 ? 2 : 1;
 
+// Four consecutive elements of a row store of type DT as a float4 (the row
+// offset e is a multiple of 4 and the store is aligned for it).
+template <int DT>
+__device__ __forceinline__ float4 load4_t(const void *base, size_t e)
+{
+    if constexpr (DT == DSV4B_DT_F32) return __ldcg(reinterpret_cast<const float4 *>(base) + (e >> 2));
+    else if constexpr (DT == DSV4B_DT_BF16) {
+        const uint2 v = __ldcg(reinterpret_cast<const uint2 *>(base) + (e >> 2));
+        const float2 a = bf16x2(v.x), b = bf16x2(v.y);
+        return make_float4(a.x, a.y, b.x, b.y);
+    } else {
+        const uint32_t v = __ldcg(reinterpret_cast<const unsigned int *>(base) + (e >> 2));
+        const float2 a = e4m3x2((uint16_t)(v & 0xFFFFu)), b = e4m3x2((uint16_t)(v >> 16));
+        return make_float4(a.x, a.y, b.x, b.y);
+    }
+}
+
+
 // ---------------------------------------------------------------- indexer
 // grid (ceil(n_pos / 32), batch), 256 threads. Thread t: position t & 31 of
 // the tile, heads (t >> 5) * 8 .. +8. q and the key tile live in shared
@@ -67,35 +85,50 @@ k_indexer_score(float *out, const float *q, const void *keys, long key_stride,
     w += (size_t)b * n_heads;
     const char *kb = reinterpret_cast<const char *>(keys);
     kb += (size_t)b * seq_key_stride * dt_bytes<KDT>;
-    constexpr int LB = 16;                          // loads in flight per thread
-    const int nq = n_heads * head_dim, nk = head_dim * IX_TP;
     for (int h = threadIdx.x; h < n_heads; h += blockDim.x) ws[h] = (double)ld_act(w + h);
-    for (int i0 = threadIdx.x; i0 < nq; i0 += LB * (int)blockDim.x) {
-        float v[LB];
+    // q as float4 groups, 8 loads in flight per thread
+    const int nq4 = (n_heads * head_dim) >> 2;
+    for (int i0 = threadIdx.x; i0 < nq4; i0 += 8 * (int)blockDim.x) {
+        float4 v[8];
 #pragma unroll
-        for (int u = 0; u < LB; u++) {
+        for (int u = 0; u < 8; u++) {
             const int i = i0 + u * (int)blockDim.x;
-            v[u] = i < nq ? ld_act(q + i) : 0.0f;
+            v[u] = i < nq4 ? __ldcg(reinterpret_cast<const float4 *>(q) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
-        for (int u = 0; u < LB; u++) {
+        for (int u = 0; u < 8; u++) {
             const int i = i0 + u * (int)blockDim.x;
-            if (i < nq) qs[i] = (double)v[u];
+            if (i < nq4) {
+                qs[4 * i] = (double)v[u].x;
+                qs[4 * i + 1] = (double)v[u].y;
+                qs[4 * i + 2] = (double)v[u].z;
+                qs[4 * i + 3] = (double)v[u].w;
+            }
         }
     }
-    for (int i0 = threadIdx.x; i0 < nk; i0 += LB * (int)blockDim.x) {
-        float v[LB];
+    // the key tile: thread (position tid/8, lane group tid%8) moves float4
+    // groups g = tid%8 + 8k of its row into kt[c][p]
+    {
+        const int p = threadIdx.x >> 3, part8 = threadIdx.x & 7, nd4 = head_dim >> 2;
+        const bool live = p < IX_TP && t0 + p < n_pos;
+        for (int g0 = part8; g0 < nd4; g0 += 32) {
+            float4 v[4];
 #pragma unroll
-        for (int u = 0; u < LB; u++) {
-            const int i = i0 + u * (int)blockDim.x;
-            const int p = i / head_dim, c = i - p * head_dim;
-            v[u] = (i < nk && t0 + p < n_pos) ? load_t<KDT>(kb, (size_t)(t0 + p) * key_stride + c) : 0.0f;
-        }
+            for (int u = 0; u < 4; u++) {
+                const int g = g0 + 8 * u;
+                v[u] = (live && g < nd4) ? load4_t<KDT>(kb, (size_t)(t0 + p) * key_stride + 4 * g)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
 #pragma unroll
-        for (int u = 0; u < LB; u++) {
-            const int i = i0 + u * (int)blockDim.x;
-            const int p = i / head_dim, c = i - p * head_dim;
-            if (i < nk) kt[c * IX_TP + p] = (double)v[u];
+            for (int u = 0; u < 4; u++) {
+                const int g = g0 + 8 * u;
+                if (p < IX_TP && g < nd4) {
+                    kt[(4 * g) * IX_TP + p] = (double)v[u].x;
+                    kt[(4 * g + 1) * IX_TP + p] = (double)v[u].y;
+                    kt[(4 * g + 2) * IX_TP + p] = (double)v[u].z;
+                    kt[(4 * g + 3) * IX_TP + p] = (double)v[u].w;
+                }
+            }
         }
     }
     __syncthreads();
@@ -276,23 +309,6 @@ struct AttnPart {
 // float4 reads of 8 consecutive lanes (one shared-memory phase) of rows p..p+7
 // fall in distinct banks.
 size_t attn_smem_bytes(int d) { return ((size_t)AT_CH * (d + 4) + (size_t)AT_HB * d + AT_CH * AT_HB) * 4; }
-
-// Four consecutive elements of a row store of type DT as a float4 (the row
-// offset e is a multiple of 4 and the store is aligned for it).
-template <int DT>
-__device__ __forceinline__ float4 load4_t(const void *base, size_t e)
-{
-    if constexpr (DT == DSV4B_DT_F32) return __ldcg(reinterpret_cast<const float4 *>(base) + (e >> 2));
-    else if constexpr (DT == DSV4B_DT_BF16) {
-        const uint2 v = __ldcg(reinterpret_cast<const uint2 *>(base) + (e >> 2));
-        const float2 a = bf16x2(v.x), b = bf16x2(v.y);
-        return make_float4(a.x, a.y, b.x, b.y);
-    } else {
-        const uint32_t v = __ldcg(reinterpret_cast<const unsigned int *>(base) + (e >> 2));
-        const float2 a = e4m3x2((uint16_t)(v & 0xFFFFu)), b = e4m3x2((uint16_t)(v >> 16));
-        return make_float4(a.x, a.y, b.x, b.y);
-    }
-}
 
 // grid (nchunk, ceil(n_heads / AT_HB), batch), 256 threads. The index list
 // holds its valid entries first, so the chunks past them only mark
@@ -487,6 +503,11 @@ int indexer_score(float *out, const float *q, const void *keys, int key_dt, long
                   int batch, cudaStream_t st, const int *dyn_n)
 {
     if (n_pos <= 0 || batch <= 0) return 0;
+    // float4 groups of q and of key rows
+    const int kal = key_dt == DSV4B_DT_F32 ? 16 : key_dt == DSV4B_DT_BF16 ? 8 : 4;
+    if ((head_dim & 3) || (key_stride & 3) || (seq_key_stride & 3) || ((uintptr_t)keys % kal) ||
+        ((uintptr_t)q & 15))
+        return -1;
     const size_t smem = ((size_t)n_heads * head_dim + (size_t)head_dim * IX_TP + (size_t)IX_TP * (n_heads + 1) +
                          (size_t)n_heads) * 8;
     if (smem > 200 * 1024) return -1;

@@ -155,6 +155,13 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
     // one column per thread (the launcher sizes the grid to n / 256); its fn
     // column is a weight, fetched before waiting for x
     const int i = blockIdx.x * blockDim.x + tid;
+    const int h4 = hidden >> 2;
+    float4 wn[kHcPreYPT];                                // the norm weights of this thread's columns
+#pragma unroll
+    for (int u = 0; u < kHcPreYPT; u++) {
+        const int d4 = tid + u * (int)blockDim.x;
+        wn[u] = (norm_w && d4 < h4) ? __ldg(reinterpret_cast<const float4 *>(norm_w) + d4) : make_float4(1.f, 1.f, 1.f, 1.f);
+    }
     float fv[MIXMAX];
 #pragma unroll
     for (int m = 0; m < MIXMAX; m++) fv[m] = (m < mix && i < n) ? __ldg(fn + (size_t)m * n + i) : 0.0f;
@@ -206,11 +213,14 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
     __syncthreads();
     if (tid == 0) *count = 0u;
     if (tid < 32) {
-        const float rs = (float)(1.0 / sqrt(tot[MIXMAX] / (double)n + (double)rms_eps));
+        const float rs = __fdiv_rn(1.0f, __fsqrt_rn((float)(tot[MIXMAX] / (double)n) + rms_eps));
         if (tid < mix) mixes[tid] = __fmul_rn((float)tot[tid], rs);
     }
     __syncwarp();
     if (tid < 32) {
+        // lane l = one comb entry (row j, column k); a row's or a column's
+        // values are gathered through shared memory and added in order
+        __shared__ float cm[32];
         const int l = tid, j = l / hc, k = l % hc;
         const bool act = l < hc * hc;
         if (l < hc) {
@@ -219,26 +229,34 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
         }
         const int o = 2 * hc + (act ? l : 0);
         float v = __fadd_rn(__fmul_rn(mixes[o], sscale[2]), sbase[o]);
+        const int rj = act ? j * hc : 0, ck = act ? k : 0;
         // row softmax: max, exp, sum in k order, scale, + eps
-        float mx = __shfl_sync(0xffffffffu, v, (j * hc) & 31);
-        for (int kk = 1; kk < hc; kk++) {
-            const float r = __shfl_sync(0xffffffffu, v, (j * hc + kk) & 31);
-            if (r > mx) mx = r;
-        }
+        cm[l] = v;
+        __syncwarp();
+        float mx = cm[rj];
+        for (int kk = 1; kk < hc; kk++) mx = fmaxf(mx, cm[rj + kk]);
         const float e = expf(v - mx);
+        __syncwarp();
+        cm[l] = e;
+        __syncwarp();
         float sum = 0.0f;
-        for (int kk = 0; kk < hc; kk++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, e, (j * hc + kk) & 31));
-        const float inv = __fdiv_rn(1.0f, sum);
-        v = __fadd_rn(__fmul_rn(e, inv), hc_eps);
+        for (int kk = 0; kk < hc; kk++) sum = __fadd_rn(sum, cm[rj + kk]);
+        v = __fadd_rn(__fmul_rn(e, __fdiv_rn(1.0f, sum)), hc_eps);
         const int npass = iters > 1 ? iters : 1;
         for (int pass = 0; pass < npass; pass++) {
             if (pass > 0) {
+                __syncwarp();
+                cm[l] = v;
+                __syncwarp();
                 float r = 0.0f;
-                for (int kk = 0; kk < hc; kk++) r = __fadd_rn(r, __shfl_sync(0xffffffffu, v, (j * hc + kk) & 31));
+                for (int kk = 0; kk < hc; kk++) r = __fadd_rn(r, cm[rj + kk]);
                 v = __fdiv_rn(v, __fadd_rn(r, hc_eps));
             }
+            __syncwarp();
+            cm[l] = v;
+            __syncwarp();
             float c = 0.0f;
-            for (int jj = 0; jj < hc; jj++) c = __fadd_rn(c, __shfl_sync(0xffffffffu, v, (jj * hc + k) & 31));
+            for (int jj = 0; jj < hc; jj++) c = __fadd_rn(c, cm[jj * hc + ck]);
             v = __fdiv_rn(v, __fadd_rn(c, hc_eps));
         }
         if (act) comb[l] = v;
@@ -246,7 +264,6 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
     __syncthreads();
     // y = sum_j pre[j] x[j], four columns per float4, in two batches of loads;
     // then RMSNorm from the registers
-    const int h4 = hidden >> 2;
     const float4 *x4 = reinterpret_cast<const float4 *>(x);
     float4 yv[kHcPreYPT];
     float sq = 0.0f;
@@ -288,17 +305,16 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
     if (norm_w) {
         __shared__ double nred[33];
         const double ssq = block_sum_d((double)sq, nred);
-        inv = (float)(1.0 / sqrt(ssq / (double)hidden + (double)rms_eps));
+        inv = __fdiv_rn(1.0f, __fsqrt_rn((float)(ssq / (double)hidden) + rms_eps));
     }
     float4 *y4 = reinterpret_cast<float4 *>(y);
-    const float4 *w4 = reinterpret_cast<const float4 *>(norm_w);
 #pragma unroll
     for (int u = 0; u < kHcPreYPT; u++) {
         const int d4 = tid + u * (int)blockDim.x;
         if (d4 < h4) {
             float4 o = yv[u];
             if (norm_w) {
-                const float4 wv = __ldg(w4 + d4);
+                const float4 wv = wn[u];
                 o = make_float4(__fmul_rn(wv.x, __fmul_rn(o.x, inv)), __fmul_rn(wv.y, __fmul_rn(o.y, inv)),
                                 __fmul_rn(wv.z, __fmul_rn(o.z, inv)), __fmul_rn(wv.w, __fmul_rn(o.w, inv)));
             }

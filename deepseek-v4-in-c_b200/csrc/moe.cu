@@ -68,7 +68,7 @@ __global__ void k_route(const float *logits, const float *bias, const int *fixed
         float wts[kMoeMaxTopk];
         double sum = 0.0;
         for (int k = 0; k < topk; k++) { wts[k] = orig[chosen[k]]; sum += (double)wts[k]; }
-        const float inv = (sum != 0.0) ? (float)(1.0 / sum) : 0.0f;
+        const float inv = (sum != 0.0) ? __fdiv_rn(1.0f, (float)sum) : 0.0f;
         for (int k = 0; k < topk; k++) {
             w_out[k] = __fmul_rn(__fmul_rn(wts[k], inv), route_scale);
             sel_out[k] = chosen[k];

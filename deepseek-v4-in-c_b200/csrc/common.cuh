@@ -73,6 +73,10 @@ __device__ __forceinline__ float4 ld_f4(const float *p)
 {
     return __ldcg(reinterpret_cast<const float4 *>(p));
 }
+__device__ __forceinline__ float2 ld_f2(const float *p)
+{
+    return __ldcg(reinterpret_cast<const float2 *>(p));
+}
 __device__ __forceinline__ float ld_act(const float *p) { return __ldcg(p); }
 __device__ __forceinline__ double ld_act_d(const double *p) { return __ldcg(p); }
 

@@ -444,7 +444,7 @@ bool gemv_mma_shape(int fmt, int cols, int blk_r, int blk_c, bool f16s)
 bool fp4_scales_f16(const uint8_t *s, size_t n)
 {
     for (size_t i = 0; i < n; i++)
-        if (s[i] < 127 - 23 || s[i] > 127 + 12) return false;
+        if (s[i] < 127 - 23 || s[i] > 127 + 1) return false;
     return true;
 }
 

@@ -1,22 +1,25 @@
-// gemv_mma.cuh - batch-1 GEMV of FP8 (e4m3, 128x128 E8M0 blocks) and BF16
-// weights on the tensor cores: warp-level mma.sync m16n8k16, f32 accumulate.
+// gemv_mma.cuh - batch-1 GEMV of FP8 (e4m3, 128x128 E8M0 blocks), FP4 (e2m1,
+// 1x32 E8M0 blocks) and BF16 weights on the tensor cores: warp-level mma.sync
+// m16n8k16, f32 accumulate.
 //
 // The weights are the A operand: e4m3 codes widen exactly to f16 (one cvt
-// per pair), bf16 weights are used as they are. x is the B operand, split
+// per pair); e2m1 codes are placed in f16 bit fields (e2m1_pair) and
+// multiplied by their block scale, exact while the scale exponent lies in
+// [-23, 1]; bf16 weights are used as they are. x is the B operand, split
 // into three pieces that add back to x exactly enough for an f32 dot:
-//   FP8 path:  xs = x * 2^k (k per 128-column block, so that max|xs| lies in
+//   f16 paths: xs = x * 2^k (k per unit, so that max|xs| lies in
 //              [2^14, 2^15)), hi = f16(xs), lo = f16(xs - hi),
 //              lo2 = f16(xs - hi - lo);
 //   BF16 path: hi = bf16(x), lo = bf16(x - hi), lo2 = bf16(x - hi - lo).
 // The pieces occupy B columns n = 0, 1, 2; every product is exact.
 //
 // Order (the canonical one for these formats, used by every kernel that
-// computes them): a row is cut into blocks of 128 columns. For each block b
-// the tensor core accumulates, from zero, the block's 8 k16-steps into C[n];
-// q_b = (((C[0] + C[1]) + C[2]) * 2^-k) * scale_b in float; the blocks are
-// cut into eight contiguous runs of ceil(nb / 8), each run summed from zero
-// in double in block order, the eight run sums added in order in double;
-// y = (float)total.
+// computes them): a row is cut into units of 128 columns (256 for FP4). For
+// each unit b the tensor core accumulates, from zero, the unit's k16-steps
+// into C[n]; q_b = (((C[0] + C[1]) + C[2]) * 2^-k) * scale_b in float (FP4:
+// the scales are already in A, scale_b = 1); the units are cut into eight
+// contiguous runs of ceil(nb / 8), each run summed from zero in double in
+// unit order, the eight run sums added in order in double; y = (float)total.
 //
 // Work: a block of 8 warps streams a tile of rows (a multiple of 16); a unit
 // is 16 rows x one 128-column block, taken by the warps in turn. Lane
@@ -80,22 +83,34 @@ __device__ __forceinline__ uint32_t e4m3x2_h2(uint32_t v)
     return (uint32_t)h.x | ((uint32_t)h.y << 16);
 }
 
-// One byte of two e2m1 codes (low nibble first) -> f16x2 bits, times the
-// half2 power of two sc (exact while the result stays a normal or subnormal
-// f16: scale exponents -23..12).
-__device__ __forceinline__ uint32_t e2m1x2_h2s(uint32_t v, uint32_t sc)
+// Nibbles q and q + 4 of a word of eight e2m1 codes (nibble 0 lowest) as the
+// f16x2 pair (value(q), value(q + 4)) * 2^-14, exactly. An e2m1 code s|e1 e0|m
+// placed at f16 bits 12..9 reads as 2^(e-15) (1 + m/2) for e > 0 and as the
+// subnormal m 2^-15 for e = 0, i.e. the code's value times 2^-14 in both
+// cases, once its sign moves from bit 12 to bit 15 (adding 7 * 2^12 does
+// that: bits 13 and 14 are clear). Shifts, masks and one multiply-add per
+// pair, in place of a conversion per byte.
+// q is a constant once the caller's loop is unrolled.
+__device__ __forceinline__ uint32_t e2m1_pair(uint32_t w, int q)
 {
-    const __half2_raw h = __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)(v & 0xFFu), __NV_E2M1);
-    uint32_t r = (uint32_t)h.x | ((uint32_t)h.y << 16), o;
-    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o) : "r"(r), "r"(sc));
+    uint32_t t = (q == 0 ? w << 9 : q == 1 ? w << 5 : q == 2 ? w << 1 : w >> 3) & 0x1E001E00u;
+    return t + 7u * (t & 0x10001000u);
+}
+
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b)
+{
+    uint32_t o;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o) : "r"(a), "r"(b));
     return o;
 }
 
-// E8M0 byte -> the f16x2 pair (2^e, 2^e); only called for e in [-24, 15].
-__device__ __forceinline__ uint32_t e8m0_h2(uint32_t b)
+// E8M0 byte b (scale 2^e, e = b - 127) -> the f16x2 pair (2^(e+14), 2^(e+14)),
+// the multiplier that turns an e2m1_pair() into value * 2^e. Called only for
+// e in [-23, 1]: the multiplier is a normal f16 and every code times 2^e is an
+// exact f16 (0.5 * 2^-23 = 2^-24 is the smallest subnormal).
+__device__ __forceinline__ uint32_t e8m0_h2x(uint32_t b)
 {
-    const int e = (int)b - 127;
-    const uint32_t h = e >= -14 ? (uint32_t)(e + 15) << 10 : (1u << (e + 24));
+    const uint32_t h = (b - 98u) << 10;
     return h | (h << 16);
 }
 
@@ -219,8 +234,17 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
 #pragma unroll
         for (int h = 0; h < XH; h++) {
             const int m = h * 8 + (lane >> 2), tt = lane & 3, j = m / MPC, i = m - j * MPC;
-            xv[u][h] = cb < nb ? ld_f4(it.x + cb * F::COLS + 4 * E * j + E * tt + 4 * i)
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (cb >= nb) {
+                xv[u][h] = make_float4(0.f, 0.f, 0.f, 0.f);
+            } else if constexpr (FMT == DSV4B_WFP4) {
+                // k16 step i pairs elements (8 (i/2) + 2 (i%2) + {0, 4}) and
+                // (... + {1, 5}) of the lane's 32, as e2m1_pair() decodes them
+                const float *xb = it.x + cb * F::COLS + 4 * E * j + E * tt + 8 * (i >> 1) + 2 * (i & 1);
+                const float2 lo = ld_f2(xb), hi = ld_f2(xb + 4);
+                xv[u][h] = make_float4(lo.x, hi.x, lo.y, hi.y);
+            } else {
+                xv[u][h] = ld_f4(it.x + cb * F::COLS + 4 * E * j + E * tt + 4 * i);
+            }
         }
     }
 #pragma unroll
@@ -284,8 +308,8 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
             const uint4 &wa = wv[cc], &wb = wv[2 + cc];   // rows g, g + 8
             uint32_t ha = 0, hb = 0;
             if (FMT == DSV4B_WFP4) {
-                ha = e8m0_h2((s4a >> (8 * cc)) & 0xFFu);
-                hb = e8m0_h2((s4b >> (8 * cc)) & 0xFFu);
+                ha = e8m0_h2x((s4a >> (8 * cc)) & 0xFFu);
+                hb = e8m0_h2x((s4b >> (8 * cc)) & 0xFFu);
             }
 #pragma unroll
             for (int i = 0; i < MPC; i++) {
@@ -296,9 +320,12 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
                     const uint32_t va = word_of(wa, i), vb = word_of(wb, i);
                     mma_f16(c, e4m3x2_h2(va), e4m3x2_h2(vb), e4m3x2_h2(va >> 16), e4m3x2_h2(vb >> 16), b.x, b.y);
                 } else if constexpr (FMT == DSV4B_WFP4) {
-                    const uint32_t va = word_of(wa, i >> 1) >> (16 * (i & 1)), vb = word_of(wb, i >> 1) >> (16 * (i & 1));
-                    mma_f16(c, e2m1x2_h2s(va, ha), e2m1x2_h2s(vb, hb), e2m1x2_h2s(va >> 8, ha),
-                            e2m1x2_h2s(vb >> 8, hb), b.x, b.y);
+                    // word i/2 of each row; step i takes nibble pairs
+                    // (2 (i%2), +4) and (2 (i%2) + 1, +4)
+                    const uint32_t va = word_of(wa, i >> 1), vb = word_of(wb, i >> 1);
+                    const int q0 = 2 * (i & 1);
+                    mma_f16(c, hmul2(e2m1_pair(va, q0), ha), hmul2(e2m1_pair(vb, q0), hb),
+                            hmul2(e2m1_pair(va, q0 + 1), ha), hmul2(e2m1_pair(vb, q0 + 1), hb), b.x, b.y);
                 } else {
                     mma_bf16(c, word_of(wa, 2 * i), word_of(wb, 2 * i), word_of(wa, 2 * i + 1),
                              word_of(wb, 2 * i + 1), b.x, b.y);

@@ -34,12 +34,12 @@ struct GemvBatch {
 size_t row_bytes(int fmt, int cols);
 // Whether a matrix takes the tensor-core path: FP8 (column blocks of 128 or
 // more) or BF16 in whole 128-column units, FP4 (1x32 blocks) in whole
-// 256-column units whose scales all lie in 2^-23..2^12 (f16s: the holder of
+// 256-column units whose scales all lie in 2^-23..2^1 (f16s: the holder of
 // the scales has checked), at most 64 units per row. A function of the
 // matrix only, so one matrix always sums in one order, whatever the batch.
 bool gemv_mma_shape(int fmt, int cols, int blk_r, int blk_c, bool f16s);
 // Whether every E8M0 scale byte lets an e2m1 value times the scale be an
-// exact f16 (exponents -23..12).
+// exact f16 through the tensor-core decode (exponents -23..1).
 bool fp4_scales_f16(const uint8_t *s, size_t n);
 // An item for W (or the table triple, when W is null) of the given shape;
 // false when the shape cannot take the 128-bit streaming kernels (rows not a

@@ -123,6 +123,22 @@ __device__ __forceinline__ float warp_max_f(float v)
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Interleaved-pair RoPE of the last rd dims of a width-wide vector at table
+// row `pos` (src/core/dsv4_rope.c:106-120); inverse negates the sine.
+__device__ __forceinline__ void rope_tail(float *v, int width, int rd, const float *cs, const float *sn,
+                                          int pos, int inverse)
+{
+    float *tail = v + (width - rd);
+    const int half = rd / 2;
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+        const float re = tail[2 * i], im = tail[2 * i + 1];
+        const float ci = cs[(size_t)pos * half + i];
+        const float si = inverse ? -sn[(size_t)pos * half + i] : sn[(size_t)pos * half + i];
+        tail[2 * i] = __fsub_rn(__fmul_rn(re, ci), __fmul_rn(im, si));
+        tail[2 * i + 1] = __fadd_rn(__fmul_rn(re, si), __fmul_rn(im, ci));
+    }
+}
+
 }  // namespace dsv4b
 
 #define DSV4B_CUDA_OK(call)                                                     \

@@ -442,7 +442,7 @@ k_attn_chunk(AttnPart part, const float *q, const void *kv, long seq_kv_rows,
 constexpr int AT_MAXCH = 512;
 
 __global__ void k_attn_combine(float *o, AttnPart part, const float *sink, int nch, int n_heads, int d,
-                               long seq_o_stride)
+                               long seq_o_stride, AttnRope rope)
 {
     pdl_trigger();
     pdl_wait();
@@ -493,6 +493,10 @@ __global__ void k_attn_combine(float *o, AttnPart part, const float *sink, int n
             acc = __fadd_rn(acc, __fmul_rn(ld_act(part.po + (r0 + (size_t)c * n_heads) * d + cc), fac[c]));
         }
         ob[cc] = __fmul_rn(acc, inv);
+    }
+    if (rope.cs) {          // de-rotate the head (src/model/dsv4_layer.c:303-305)
+        __syncthreads();
+        rope_tail(ob, d, rope.rd, rope.cs, rope.sn, __ldcg(rope.pos), 1);
     }
 }
 
@@ -558,7 +562,7 @@ size_t attn_part_bytes(int n_heads, int d, int topk, int batch)
 
 int sparse_attn(float *o, const float *q, const void *kv, int kv_dt, long seq_kv_rows, const float *sink,
                 const int *idxs, long seq_idx_stride, int n_heads, int d, int topk, float scale, int batch,
-                void *part_buf, cudaStream_t st)
+                void *part_buf, cudaStream_t st, const AttnRope *rope)
 {
     if (batch <= 0 || topk <= 0) return 0;
     if (n_heads <= 0 || d > 1024 || (d & 3)) return -1;
@@ -589,7 +593,9 @@ int sparse_attn(float *o, const float *q, const void *kv, int kv_dt, long seq_kv
     else
         launch(k_attn_chunk<DSV4B_DT_E4M3>, grid, dim3(256), smem, st, part, q, kv, seq_kv_rows, idxs, seq_idx_stride,
                n_heads, d, topk, scale, sq);
-    launch(k_attn_combine, dim3(dim3(n_heads, batch)), dim3(128), 0, st, o, part, sink, nch, n_heads, d, (long)n_heads * d);
+    const AttnRope rp = rope ? *rope : AttnRope{nullptr, nullptr, nullptr, 0};
+    launch(k_attn_combine, dim3(dim3(n_heads, batch)), dim3(128), 0, st, o, part, sink, nch, n_heads, d,
+           (long)n_heads * d, rp);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -27,8 +27,16 @@ int topk(int *idx, const float *scores, int n, int k, int batch, long seq_in_str
 size_t attn_part_bytes(int n_heads, int d, int topk, int batch);
 // o[b][h][d]; kv of sequence b is rows [b*seq_kv_rows, ...) of width d; idxs
 // [b][topk] with -1 = masked; part_buf holds attn_part_bytes().
+// Optional de-rotation of every output head (inverse RoPE of its last rd
+// dims at table row *pos), done by the kernel that writes the head.
+struct AttnRope {
+    const float *cs, *sn;
+    const int *pos;
+    int rd;
+};
 int sparse_attn(float *o, const float *q, const void *kv, int kv_dt, long seq_kv_rows,
                 const float *sink, const int *idxs, long seq_idx_stride, int n_heads, int d,
-                int topk, float scale, int batch, void *part_buf, cudaStream_t st);
+                int topk, float scale, int batch, void *part_buf, cudaStream_t st,
+                const AttnRope *rope = nullptr);
 
 }  // namespace dsv4b

@@ -264,23 +264,80 @@ static void grp_add(Grp &g, const DevMat &w, const float *x, float *y, cudaStrea
 
 static int grp_run(Grp &g, cudaStream_t st) { return g.rc | gemv_group(g.it, g.n, st); }
 
-static int hc_pre(dsv4b_model *m, const float *h, const float *fn, const float *base, const float *scale,
-                  const float *norm, cudaStream_t st)
+// What the next mHC launch finishes before it mixes: nothing (the embedding),
+// an attention output in m->blk, or an MoE's per-expert outputs (its combine).
+struct Pending {
+    int kind;                 // 0 none, 1 blk, 2 MoE accumulators
+    const MoeLayer *moe;
+};
+
+static bool hc_fused(const DSV4Cfg &c)
+{
+    const int hc = c.hc_mult, n = hc * c.hidden;
+    return (2 + hc) * hc <= kHcPreMixMax && c.hidden % 4 == 0 && c.hidden <= 256 * 4 * kHcPreYPT && n % 256 == 0 &&
+           n / 256 <= kHcPreBlocks;
+}
+
+// The post-mix of the pending sub-layer (hin -> hout, then swapped) and the
+// pre-mix of the next one into y (x1, or the head's xh when head is set).
+static void hc_step(dsv4b_model *m, Pending &p, float *&hin, float *&hout, const float *fn, const float *base,
+                    const float *scale, const float *norm, bool head, float *y, cudaStream_t st)
 {
     const DSV4Cfg &c = m->c;
-    const int hc = c.hc_mult, mix = (2 + hc) * hc, n = hc * c.hidden;
-    if (mix <= kHcPreMixMax && c.hidden % 4 == 0 && c.hidden <= 256 * 4 * kHcPreYPT && n % 256 == 0 &&
-        n / 256 <= kHcPreBlocks) {
-        launch(k_hc_pre, dim3(n / 256), dim3(256), 0, st, m->x1, m->post, m->comb, h, fn, scale, base, norm, m->hc_part,
-                                               m->hc_cnt, hc, c.hidden, c.hc_sinkhorn_iters, c.hc_eps,
-                                               c.rms_eps);
-        return 0;
+    const int hc = c.hc_mult, mix = (2 + hc) * hc, n = hc * c.hidden, wide = n;
+    if (hc_fused(c)) {
+        HcPreArgs a = {};
+        a.y = y;
+        a.post = head ? nullptr : m->post;
+        a.comb = head ? nullptr : m->comb;
+        a.x = hin;
+        if (p.kind) {
+            a.xout = hout;
+            a.post_in = m->post;
+            a.comb_in = m->comb;
+            if (p.kind == 1) {
+                a.blk = m->blk;
+            } else {
+                a.acc = m->ms.acc;
+                a.wts = m->ms.wts;
+                a.topk = p.moe->topk;
+                a.accs = (p.moe->has_shared && p.moe->inter_shared) ? m->ms.acc + (size_t)p.moe->topk * c.hidden
+                                                                       : nullptr;
+            }
+        }
+        a.fn = fn;
+        a.scale = scale;
+        a.base = base;
+        a.norm_w = norm;
+        a.part = m->hc_part;
+        a.count = m->hc_cnt;
+        a.hc = hc;
+        a.hidden = c.hidden;
+        a.iters = c.hc_sinkhorn_iters;
+        a.nmix = head ? hc : mix;
+        a.hc_eps = c.hc_eps;
+        a.rms_eps = c.rms_eps;
+        launch(k_hc_pre, dim3(n / 256), dim3(256), 0, st, a);
+        if (p.kind) std::swap(hin, hout);
+        p.kind = 0;
+        return;
     }
-    launch(k_hc_mix, dim3(mix), dim3(256), 0, st, m->mixes, fn, h, n, c.rms_eps);
-    launch(k_hc_finish, dim3(1), dim3(256), 0, st, m->x1, m->post, m->comb, m->mixes, h, scale, base, hc, c.hidden,
-                                   c.hc_sinkhorn_iters, c.hc_eps);
-    launch(k_rmsnorm, dim3(1), dim3(1024), 0, st, m->x1, m->x1, norm, c.hidden, c.rms_eps);
-    return 0;
+    // unfused: the MoE was combined into m->blk by moe_forward
+    if (p.kind) {
+        launch(k_hc_post, dim3((wide + 255) / 256), dim3(256), 0, st, hout, m->blk, hin, m->post, m->comb, hc,
+               c.hidden);
+        std::swap(hin, hout);
+        p.kind = 0;
+    }
+    if (head) {
+        launch(k_hc_mix, dim3(hc), dim3(256), 0, st, m->mixes, fn, hin, n, c.rms_eps);
+        launch(k_hc_head_finish, dim3(1), dim3(256), 0, st, y, m->mixes, hin, scale, base, hc, c.hidden, c.hc_eps);
+    } else {
+        launch(k_hc_mix, dim3(mix), dim3(256), 0, st, m->mixes, fn, hin, n, c.rms_eps);
+        launch(k_hc_finish, dim3(1), dim3(256), 0, st, y, m->post, m->comb, m->mixes, hin, scale, base, hc, c.hidden,
+               c.hc_sinkhorn_iters, c.hc_eps);
+    }
+    launch(k_rmsnorm, dim3(1), dim3(1024), 0, st, y, y, norm, c.hidden, c.rms_eps);
 }
 
 // One token: enqueue only, no host synchronisation (graph-capturable).
@@ -288,17 +345,20 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
 {
     const DSV4Cfg &c = m->c;
     const int hc = c.hc_mult, d = c.hidden, hd = c.head_dim, rd = c.qk_rope, H = c.n_heads;
-    const int win = c.sliding_window, wide = hc * d;
+    const int win = c.sliding_window;
     int rc = 0;
     PdlChain chain;
     float *hin = m->h, *hout = m->resid;
+    Pending pend = {0, nullptr};
+    const bool fused = hc_fused(c);
     launch(k_embed, dim3(16), dim3(256), 0, st, hin, m->embed, m->emb_wdt, m->st, d, hc);
     for (int Li = 0; Li < c.n_layers; Li++) {
         DevLayer &l = m->L[Li];
         const float *cs = l.ratio ? m->cs_c : m->cs_d, *sn = l.ratio ? m->sn_c : m->sn_d;
-        // ---- attention half (src/model/dsv4_layer.c:495-509); the residual
-        // stream ping-pongs between two buffers, so no copy is needed
-        hc_pre(m, hin, l.hca_fn, l.hca_base, l.hca_scale, l.attn_norm, st);
+        // ---- attention half (src/model/dsv4_layer.c:495-509), after the
+        // previous FFN's post-mix; the residual stream ping-pongs between two
+        // buffers, so no copy is needed
+        hc_step(m, pend, hin, hout, l.hca_fn, l.hca_base, l.hca_scale, l.attn_norm, false, m->x1, st);
         // every projection of x1 in one launch, then both of the normalised q latent
         {
             Grp ga;
@@ -318,27 +378,56 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
             if (l.has_idx) grp_add(gb, l.iwq_b, m->qr, m->idx_q, st);
             rc |= grp_run(gb, st);
         }
-        launch(k_heads_norm_rope, dim3(H), dim3(256), 0, st, m->q, hd, rd, cs, sn, m->st, 0, 0, 1, c.rms_eps);
-        launch(k_kv_finish, dim3(1), dim3(256), 0, st, m->kv, l.kv_norm, hd, rd, cs, sn, m->st, c.rms_eps, l.kv_cache, win);
-        if (l.has_comp) {
-            launch(k_compress, dim3(1), dim3(512), hd * 4, st, l.kv_cache, l.comp_kv, l.comp_score, m->comp_in, m->comp_sc, l.ape,
-                                               l.cnorm, l.ratio, hd, rd, cs, sn, m->st, c.rms_eps, win,
-                                               c.index_topk, l.dyn);
-            if (l.has_idx) {
-                const int ih = c.index_n_heads, id = c.index_head_dim;
-                launch(k_heads_norm_rope, dim3(ih), dim3(128), 0, st, m->idx_q, id, rd, cs, sn, m->st, 0, 0, 0, c.rms_eps);
-                const float scale = (1.0f / sqrtf((float)id)) * (1.0f / sqrtf((float)ih));
-                // the compressed region read as contiguous rows of index_head_dim
-                // floats, as the reference does (dsv4_layer.c:286-289)
-                rc |= indexer_score(m->idx_scores, m->idx_q, l.kv_cache + (size_t)win * hd, DSV4B_DT_F32, id, 0,
-                                    m->idx_w, ih, id, m->ncomp4, scale, 1, st, l.dyn);
-                rc |= topk(m->isel, m->idx_scores, m->ncomp4, c.index_topk, 1, m->ncomp4, c.index_topk, st, l.dyn);
-            }
+        // q heads, the KV row, the compressor, the indexer's q heads (or the
+        // attended row list) in one launch (dsv4_layer.c:224-295)
+        const int ih = c.index_n_heads, id = c.index_head_dim;
+        {
+            PrepArgs pa = {};
+            pa.q = m->q;
+            pa.kv = m->kv;
+            pa.cache = l.kv_cache;
+            pa.comp_kv = l.comp_kv;
+            pa.comp_score = l.comp_score;
+            pa.idx_q = m->idx_q;
+            pa.kv_norm = l.kv_norm;
+            pa.comp_in = m->comp_in;
+            pa.comp_sc = m->comp_sc;
+            pa.ape = l.ape;
+            pa.cnorm = l.cnorm;
+            pa.cs = cs;
+            pa.sn = sn;
+            pa.st = m->st;
+            pa.dyn = l.dyn;
+            pa.idxs = m->idxs;
+            pa.H = H;
+            pa.hd = hd;
+            pa.rd = rd;
+            pa.win = win;
+            pa.has_comp = l.has_comp;
+            pa.has_idx = l.has_comp && l.has_idx;
+            pa.ratio = l.ratio;
+            pa.index_topk = c.index_topk;
+            pa.ih = ih;
+            pa.id = id;
+            pa.nidx = m->nidx;
+            pa.eps = c.rms_eps;
+            const int blocks = H + 1 + (pa.has_comp ? 1 : 0) + (pa.has_idx ? ih : 1);
+            launch(k_attn_prep, dim3(blocks), dim3(256), (size_t)hd * 4, st, pa);
         }
-        launch(k_build_idxs, dim3(1), dim3(256), 0, st, m->idxs, m->nidx, m->st, win, l.has_comp, l.has_idx, l.dyn, m->isel);
+        if (l.has_comp && l.has_idx) {
+            const float scale = (1.0f / sqrtf((float)id)) * (1.0f / sqrtf((float)ih));
+            // the compressed region read as contiguous rows of index_head_dim
+            // floats, as the reference does (dsv4_layer.c:286-289)
+            rc |= indexer_score(m->idx_scores, m->idx_q, l.kv_cache + (size_t)win * hd, DSV4B_DT_F32, id, 0,
+                                m->idx_w, ih, id, m->ncomp4, scale, 1, st, l.dyn);
+            rc |= topk(m->isel, m->idx_scores, m->ncomp4, c.index_topk, 1, m->ncomp4, c.index_topk, st, l.dyn);
+            launch(k_build_idxs, dim3(1), dim3(256), 0, st, m->idxs, m->nidx, m->st, win, l.has_comp, l.has_idx, l.dyn,
+                   m->isel);
+        }
+        // attention, each head de-rotated by the kernel that writes it
+        const AttnRope rope = {cs, sn, &m->st->pos, rd};
         rc |= sparse_attn(m->o, m->q, l.kv_cache, DSV4B_DT_F32, (long)l.kv_rows, l.sink, m->idxs, m->nidx, H, hd,
-                          m->nidx, 1.0f / sqrtf((float)hd), 1, m->attn_part, st);
-        launch(k_heads_norm_rope, dim3(H), dim3(256), 0, st, m->o, hd, rd, cs, sn, m->st, 0, 1, 0, c.rms_eps);
+                          m->nidx, 1.0f / sqrtf((float)hd), 1, m->attn_part, st, &rope);
         // grouped low-rank output (dsv4_layer.c:303-335): the o_groups row
         // slices of wo_a, each on its own slice of o, in one launch
         {
@@ -357,18 +446,14 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
             rc |= grp_run(go, st);
         }
         rc |= G(l.wo_b, m->blk, m->ogrp, st);
-        launch(k_hc_post, dim3((wide + 255) / 256), dim3(256), 0, st, hout, m->blk, hin, m->post, m->comb, hc, d);
-        std::swap(hin, hout);
         // ---- FFN half: the residual is taken after attention (:511-522)
-        hc_pre(m, hin, l.hcf_fn, l.hcf_base, l.hcf_scale, l.ffn_norm, st);
-        rc |= moe_forward(l.moe, m->ms, m->blk, m->x1, &m->st->token, st);
-        launch(k_hc_post, dim3((wide + 255) / 256), dim3(256), 0, st, hout, m->blk, hin, m->post, m->comb, hc, d);
-        std::swap(hin, hout);
+        pend = {1, nullptr};
+        hc_step(m, pend, hin, hout, l.hcf_fn, l.hcf_base, l.hcf_scale, l.ffn_norm, false, m->x1, st);
+        rc |= moe_forward(l.moe, m->ms, m->blk, m->x1, &m->st->token, st, !fused);
+        pend = {fused ? 2 : 1, &l.moe};
     }
     // ---- head (src/cli/dsv4_run.c:467-474)
-    launch(k_hc_mix, dim3(hc), dim3(256), 0, st, m->mixes, m->hch_fn, hin, wide, c.rms_eps);
-    launch(k_hc_head_finish, dim3(1), dim3(256), 0, st, m->xh, m->mixes, hin, m->hch_scale, m->hch_base, hc, d, c.hc_eps);
-    launch(k_rmsnorm, dim3(1), dim3(1024), 0, st, m->xh, m->xh, m->norm, d, c.rms_eps);
+    hc_step(m, pend, hin, hout, m->hch_fn, m->hch_base, m->hch_scale, m->norm, true, m->xh, st);
     rc |= G(m->head, m->logits, m->xh, st);
     launch(k_argmax_part, dim3(148), dim3(256), 0, st, m->am_pv, m->am_pi, m->logits, c.vocab);
     launch(k_argmax_final, dim3(1), dim3(32), 0, st, m->st, m->out_tokens, m->am_pv, m->am_pi, 148, m->prompt, m->n_prompt);

@@ -25,22 +25,39 @@ __global__ void k_hc_finish(float *y, float *post, float *comb, const float *mix
 constexpr int kHcPreMixMax = 24;   // (2 + hc) * hc for hc <= 4
 constexpr int kHcPreBlocks = 64;
 constexpr int kHcPreYPT = 8;       // float4 columns of y per thread: hidden <= 256 * 4 * 8
-__global__ void k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, const float *scale,
-                         const float *base, const float *norm_w, double *part, unsigned *count, int hc, int hidden,
-                         int iters, float hc_eps, float rms_eps);
+// Arguments of one fused mHC launch (k_hc_pre). With blk or acc set it first
+// finishes the previous sub-layer's post-mix into xout and then mixes xout;
+// otherwise it mixes x. Head mode: post and comb null, nmix = hc.
+struct HcPreArgs {
+    float *y, *post, *comb;          // x1 (normalised), the split's post / comb
+    const float *x;                  // the residual (the previous one when stepping)
+    float *xout;                     // stepping: the new residual
+    const float *blk;                // stepping: the sub-layer's output, or
+    const float *acc, *wts, *accs;   //   an MoE's: sum_k wts[k] acc[k] (+ accs)
+    const float *post_in, *comb_in;  // stepping: the previous split
+    const float *fn, *scale, *base, *norm_w;
+    double *part;
+    unsigned *count;
+    int hc, hidden, iters, nmix, topk;
+    float hc_eps, rms_eps;
+};
+__global__ void k_hc_pre(const __grid_constant__ HcPreArgs a);
 __global__ void k_hc_head_finish(float *y, const float *mixes, const float *x, const float *scale,
                                  const float *base, int hc, int hidden, float eps);
 __global__ void k_hc_post(float *y, const float *x, const float *res, const float *post, const float *comb,
                           int hc, int hidden);
 __global__ void k_rmsnorm(float *y, const float *x, const float *w, int n, float eps);
-__global__ void k_heads_norm_rope(float *v, int width, int rd, const float *cs, const float *sn,
-                                  const StepState *st, int pos_off, int inverse, int do_norm, float eps);
-__global__ void k_kv_finish(float *kv, const float *w, int hd, int rd, const float *cs, const float *sn,
-                            const StepState *st, float eps, float *cache, int win);
-__global__ void k_compress(float *cache, float *kv_state, float *score_state, const float *kv_in,
-                           const float *sc_in, const float *ape, const float *norm, int ratio, int hd, int rd,
-                           const float *cs, const float *sn, const StepState *st, float eps, int win,
-                           int index_topk, int *dyn);
+// Arguments of k_attn_prep (the tasks between the q projections and the
+// indexer / attention of one layer).
+struct PrepArgs {
+    float *q, *kv, *cache, *comp_kv, *comp_score, *idx_q;
+    const float *kv_norm, *comp_in, *comp_sc, *ape, *cnorm, *cs, *sn;
+    const StepState *st;
+    int *dyn, *idxs;
+    int H, hd, rd, win, has_comp, has_idx, ratio, index_topk, ih, id, nidx;
+    float eps;
+};
+__global__ void k_attn_prep(const __grid_constant__ PrepArgs a);
 __global__ void k_build_idxs(int *idxs, int nmax, const StepState *st, int win, int has_comp, int has_idx,
                              const int *dyn, const int *sel);
 __global__ void k_argmax_part(float *pv, int *pi, const float *x, int n);

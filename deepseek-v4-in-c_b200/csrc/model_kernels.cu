@@ -124,23 +124,30 @@ __global__ void k_hc_finish(float *y, float *post, float *comb, const float *mix
 
 // The whole mHC pre-mix of one sub-layer in one launch, with the sub-layer's
 // RMSNorm folded in (src/core/dsv4_hc.c:118-140 with dsv4_hc_split_sinkhorn
-// :50-102, then src/core/dsv4_ops.c:25-32 when norm_w is given):
-//   every block: per column the products fn[m][i] * x[i] and x[i]^2 (float),
+// :50-102, then src/core/dsv4_ops.c:25-32 when norm_w is given), optionally
+// preceded by the previous sub-layer's post-mix (k_hc_post, and before it the
+// MoE combine k_combine), each thread finishing the one residual element it
+// then mixes:
+//   every block: [post step: blk[d] (or sum_k wts[k] acc[k][d] + accs[d] in
+//                float, as k_combine), xout[i] = post_in[j] blk[d] +
+//                sum_l comb_in[l][j] x[l][d] in double, as k_hc_post]; per
+//                column the products fn[m][i] * x[i] and x[i]^2 (float),
 //                summed per block in a fixed order (32 columns in float, then
-//                8 such sums in double), written to part[block][0..mix];
+//                8 such sums in double), written to part[block][0..nmix];
 //   last block:  the partials summed in block order (double), mixes, the
-//                Sinkhorn split (lanes of one warp, each lane one comb entry;
-//                every row / column sum gathered by shuffles and added in the
-//                serial order), y = sum_j pre[j] x[j], RMSNorm.
+//                pre weights, [layers: post weights and the Sinkhorn split,
+//                lanes of one warp, each lane one comb entry, every row /
+//                column sum gathered through shared memory and added in the
+//                serial order], y = sum_j pre[j] x[j], RMSNorm.
+// Head mode (post null, nmix = hc) is the head's reduction
+// (src/cli/dsv4_run.c:94-116): the sigmoid pre weights only.
 // The reference sums these in double; here only the short sums across warps
 // and blocks are, which keeps the result within ~1e-7 of it while avoiding
 // long chains of double operations. The last block is the one whose arrival
 // at *count completes the grid; it resets *count, so the kernel is
-// replayable. hc * hc <= 32.
-__global__ void __launch_bounds__(256)
-k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, const float *scale,
-         const float *base, const float *norm_w, double *part, unsigned *count, int hc, int hidden,
-         int iters, float hc_eps, float rms_eps)
+// replayable. post_in / comb_in may be the post / comb outputs: every block
+// has read them before it arrives at *count. hc * hc <= 32.
+__global__ void __launch_bounds__(256) k_hc_pre(const __grid_constant__ HcPreArgs a)
 {
     constexpr int MIXMAX = kHcPreMixMax, NV = MIXMAX + 1;
     __shared__ float prod[NV][256];
@@ -148,10 +155,11 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
     __shared__ double tot[NV];
     __shared__ float mixes[MIXMAX], pre[DSV4B_MAX_HC], sbase[MIXMAX], sscale[3];
     __shared__ bool last;
-    const int n = hc * hidden, mix = (2 + hc) * hc, tid = threadIdx.x;
+    const int hc = a.hc, hidden = a.hidden, n = hc * hidden, mix = a.nmix, tid = threadIdx.x;
+    const bool stepped = a.blk || a.acc;
     pdl_trigger();
-    if (tid < mix) sbase[tid] = __ldg(base + tid);        // weights: before the wait
-    if (tid < 3) sscale[tid] = __ldg(scale + tid);
+    if (tid < mix) sbase[tid] = __ldg(a.base + tid);     // weights: before the wait
+    if (tid < (a.post ? 3 : 1)) sscale[tid] = __ldg(a.scale + tid);
     // one column per thread (the launcher sizes the grid to n / 256); its fn
     // column is a weight, fetched before waiting for x
     const int i = blockIdx.x * blockDim.x + tid;
@@ -160,13 +168,37 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
 #pragma unroll
     for (int u = 0; u < kHcPreYPT; u++) {
         const int d4 = tid + u * (int)blockDim.x;
-        wn[u] = (norm_w && d4 < h4) ? __ldg(reinterpret_cast<const float4 *>(norm_w) + d4) : make_float4(1.f, 1.f, 1.f, 1.f);
+        wn[u] = (a.norm_w && d4 < h4) ? __ldg(reinterpret_cast<const float4 *>(a.norm_w) + d4)
+                                      : make_float4(1.f, 1.f, 1.f, 1.f);
     }
     float fv[MIXMAX];
 #pragma unroll
-    for (int m = 0; m < MIXMAX; m++) fv[m] = (m < mix && i < n) ? __ldg(fn + (size_t)m * n + i) : 0.0f;
+    for (int m = 0; m < MIXMAX; m++) fv[m] = (m < mix && i < n) ? __ldg(a.fn + (size_t)m * n + i) : 0.0f;
     pdl_wait();
-    const float xv = i < n ? __ldcg(x + i) : 0.0f;
+    float xv = 0.0f;
+    if (i < n) {
+        if (stepped) {
+            const int j = i / hidden, d = i - j * hidden;
+            float b;
+            if (a.acc) {
+                float o = 0.0f;
+                for (int k = 0; k < a.topk; k++)
+                    o = __fadd_rn(o, __fmul_rn(ld_act(a.wts + k), ld_act(a.acc + (size_t)k * hidden + d)));
+                if (a.accs) o = __fadd_rn(o, ld_act(a.accs + d));
+                b = o;
+            } else {
+                b = ld_act(a.blk + d);
+            }
+            double s = __dmul_rn((double)ld_act(a.post_in + j), (double)b);
+            for (int l = 0; l < hc; l++)
+                s = __dadd_rn(s, __dmul_rn((double)ld_act(a.comb_in + l * hc + j),
+                                           (double)ld_act(a.x + (size_t)l * hidden + d)));
+            xv = (float)s;
+            a.xout[i] = xv;
+        } else {
+            xv = ld_act(a.x + i);
+        }
+    }
 #pragma unroll
     for (int m = 0; m < MIXMAX; m++) prod[m][tid] = __fmul_rn(fv[m], xv);
     prod[MIXMAX][tid] = __fmul_rn(xv, xv);
@@ -183,14 +215,15 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
         double t = 0.0;
 #pragma unroll
         for (int w = 0; w < 8; w++) t += red8[tid][w];
-        part[(size_t)blockIdx.x * NV + tid] = t;
+        a.part[(size_t)blockIdx.x * NV + tid] = t;
     }
     __threadfence();
     __syncthreads();
-    if (tid == 0) last = atomicAdd(count, 1u) == gridDim.x - 1;
+    if (tid == 0) last = atomicAdd(a.count, 1u) == gridDim.x - 1;
     __syncthreads();
     if (!last) return;
     __threadfence();
+    const float *x = stepped ? a.xout : a.x;
     // every block's partials: 8 threads per value each add gridDim/8 blocks,
     // then the 8 sums in order
     const int nblk = (int)gridDim.x, per = (nblk + 7) >> 3;
@@ -199,7 +232,7 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
         double t = 0.0;
         for (int k = 0; k < per; k++) {
             const int bb = w * per + k;
-            if (bb < nblk) t += __ldcg(part + (size_t)bb * NV + m);
+            if (bb < nblk) t += __ldcg(a.part + (size_t)bb * NV + m);
         }
         red8[m][w] = t;
     }
@@ -211,22 +244,21 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
         tot[tid] = t;
     }
     __syncthreads();
-    if (tid == 0) *count = 0u;
+    if (tid == 0) *a.count = 0u;
     if (tid < 32) {
-        const float rs = __fdiv_rn(1.0f, __fsqrt_rn((float)(tot[MIXMAX] / (double)n) + rms_eps));
+        const float rs = __fdiv_rn(1.0f, __fsqrt_rn((float)(tot[MIXMAX] / (double)n) + a.rms_eps));
         if (tid < mix) mixes[tid] = __fmul_rn((float)tot[tid], rs);
     }
     __syncwarp();
-    if (tid < 32) {
+    if (tid < hc) pre[tid] = __fadd_rn(sigm(__fadd_rn(__fmul_rn(mixes[tid], sscale[0]), sbase[tid])), a.hc_eps);
+    if (a.post && tid < 32) {
         // lane l = one comb entry (row j, column k); a row's or a column's
         // values are gathered through shared memory and added in order
         __shared__ float cm[32];
         const int l = tid, j = l / hc, k = l % hc;
         const bool act = l < hc * hc;
-        if (l < hc) {
-            pre[l] = __fadd_rn(sigm(__fadd_rn(__fmul_rn(mixes[l], sscale[0]), sbase[l])), hc_eps);
-            post[l] = __fmul_rn(2.0f, sigm(__fadd_rn(__fmul_rn(mixes[l + hc], sscale[1]), sbase[l + hc])));
-        }
+        const float hc_eps = a.hc_eps;
+        if (l < hc) a.post[l] = __fmul_rn(2.0f, sigm(__fadd_rn(__fmul_rn(mixes[l + hc], sscale[1]), sbase[l + hc])));
         const int o = 2 * hc + (act ? l : 0);
         float v = __fadd_rn(__fmul_rn(mixes[o], sscale[2]), sbase[o]);
         const int rj = act ? j * hc : 0, ck = act ? k : 0;
@@ -242,7 +274,7 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
         float sum = 0.0f;
         for (int kk = 0; kk < hc; kk++) sum = __fadd_rn(sum, cm[rj + kk]);
         v = __fadd_rn(__fmul_rn(e, __fdiv_rn(1.0f, sum)), hc_eps);
-        const int npass = iters > 1 ? iters : 1;
+        const int npass = a.iters > 1 ? a.iters : 1;
         for (int pass = 0; pass < npass; pass++) {
             if (pass > 0) {
                 __syncwarp();
@@ -259,7 +291,7 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
             for (int jj = 0; jj < hc; jj++) c = __fadd_rn(c, cm[jj * hc + ck]);
             v = __fdiv_rn(v, __fadd_rn(c, hc_eps));
         }
-        if (act) comb[l] = v;
+        if (act) a.comb[l] = v;
     }
     __syncthreads();
     // y = sum_j pre[j] x[j], four columns per float4, in two batches of loads;
@@ -281,39 +313,39 @@ k_hc_pre(float *y, float *post, float *comb, const float *x, const float *fn, co
 #pragma unroll
         for (int uu = 0; uu < YB; uu++) {
             const int u = half * YB + uu, d4 = tid + u * (int)blockDim.x;
-            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             if (d4 < h4) {
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
                     if (j < hc) {
                         const float pj = pre[j];
-                        a.x = __fmaf_rn(pj, xw[uu][j].x, a.x);
-                        a.y = __fmaf_rn(pj, xw[uu][j].y, a.y);
-                        a.z = __fmaf_rn(pj, xw[uu][j].z, a.z);
-                        a.w = __fmaf_rn(pj, xw[uu][j].w, a.w);
+                        acc.x = __fmaf_rn(pj, xw[uu][j].x, acc.x);
+                        acc.y = __fmaf_rn(pj, xw[uu][j].y, acc.y);
+                        acc.z = __fmaf_rn(pj, xw[uu][j].z, acc.z);
+                        acc.w = __fmaf_rn(pj, xw[uu][j].w, acc.w);
                     }
                 }
-                sq = __fmaf_rn(a.x, a.x, sq);
-                sq = __fmaf_rn(a.y, a.y, sq);
-                sq = __fmaf_rn(a.z, a.z, sq);
-                sq = __fmaf_rn(a.w, a.w, sq);
+                sq = __fmaf_rn(acc.x, acc.x, sq);
+                sq = __fmaf_rn(acc.y, acc.y, sq);
+                sq = __fmaf_rn(acc.z, acc.z, sq);
+                sq = __fmaf_rn(acc.w, acc.w, sq);
             }
-            yv[u] = a;
+            yv[u] = acc;
         }
     }
     float inv = 1.0f;
-    if (norm_w) {
+    if (a.norm_w) {
         __shared__ double nred[33];
         const double ssq = block_sum_d((double)sq, nred);
-        inv = __fdiv_rn(1.0f, __fsqrt_rn((float)(ssq / (double)hidden) + rms_eps));
+        inv = __fdiv_rn(1.0f, __fsqrt_rn((float)(ssq / (double)hidden) + a.rms_eps));
     }
-    float4 *y4 = reinterpret_cast<float4 *>(y);
+    float4 *y4 = reinterpret_cast<float4 *>(a.y);
 #pragma unroll
     for (int u = 0; u < kHcPreYPT; u++) {
         const int d4 = tid + u * (int)blockDim.x;
         if (d4 < h4) {
             float4 o = yv[u];
-            if (norm_w) {
+            if (a.norm_w) {
                 const float4 wv = wn[u];
                 o = make_float4(__fmul_rn(wv.x, __fmul_rn(o.x, inv)), __fmul_rn(wv.y, __fmul_rn(o.y, inv)),
                                 __fmul_rn(wv.z, __fmul_rn(o.z, inv)), __fmul_rn(wv.w, __fmul_rn(o.w, inv)));
@@ -373,31 +405,11 @@ __global__ void k_rmsnorm(float *y, const float *x, const float *w, int n, float
     for (int i = threadIdx.x; i < n; i += blockDim.x) y[i] = __fmul_rn(w[i], __fmul_rn(x[i], inv));
 }
 
-// Interleaved-pair RoPE of the last rd dims of a width-wide vector at table
-// row `pos` (src/core/dsv4_rope.c:106-120); inverse negates the sine.
-__device__ __forceinline__ void rope_tail(float *v, int width, int rd, const float *cs, const float *sn,
-                                          int pos, int inverse)
+// One head: optional unweighted RMS (the q path,
+// src/model/dsv4_layer.c:224-231), then RoPE at pos. The whole block.
+__device__ void head_norm_rope(float *h, int width, int rd, const float *cs, const float *sn, int pos, int inverse,
+                               int do_norm, float eps, double *red)
 {
-    float *tail = v + (width - rd);
-    const int half = rd / 2;
-    for (int i = threadIdx.x; i < half; i += blockDim.x) {
-        const float re = tail[2 * i], im = tail[2 * i + 1];
-        const float ci = cs[(size_t)pos * half + i];
-        const float si = inverse ? -sn[(size_t)pos * half + i] : sn[(size_t)pos * half + i];
-        tail[2 * i] = __fsub_rn(__fmul_rn(re, ci), __fmul_rn(im, si));
-        tail[2 * i + 1] = __fadd_rn(__fmul_rn(re, si), __fmul_rn(im, ci));
-    }
-}
-
-// grid = heads. Optional unweighted per-head RMS (the q path,
-// src/model/dsv4_layer.c:224-231), then RoPE at st->pos + pos_off.
-__global__ void k_heads_norm_rope(float *v, int width, int rd, const float *cs, const float *sn,
-                                  const StepState *st, int pos_off, int inverse, int do_norm, float eps)
-{
-    pdl_trigger();
-    pdl_wait();
-    __shared__ double red[33];
-    float *h = v + (size_t)blockIdx.x * width;
     if (do_norm) {
         double s = 0.0;
         for (int i = threadIdx.x; i < width; i += blockDim.x) s = __fma_rn((double)h[i], (double)h[i], s);
@@ -406,44 +418,32 @@ __global__ void k_heads_norm_rope(float *v, int width, int rd, const float *cs, 
         for (int i = threadIdx.x; i < width; i += blockDim.x) h[i] = __fmul_rn(h[i], inv);
         __syncthreads();
     }
-    rope_tail(h, width, rd, cs, sn, st->pos + pos_off, inverse);
+    rope_tail(h, width, rd, cs, sn, pos, inverse);
 }
 
-// kv = RoPE(RMSNorm(kv)), written into the sliding ring at pos % win
-// (src/model/dsv4_layer.c:234-238). One block.
-__global__ void k_kv_finish(float *kv, const float *w, int hd, int rd, const float *cs, const float *sn,
-                            const StepState *st, float eps, float *cache, int win)
+// The new KV row: weighted RMSNorm, RoPE at pos, into its window slot
+// (src/model/dsv4_layer.c:233-238). The whole block.
+__device__ void kv_finish(float *kv, const float *w, int hd, int rd, const float *cs, const float *sn, int pos,
+                          float eps, float *cache, int win, double *red)
 {
-    pdl_trigger();
-    pdl_wait();
-    __shared__ double red[33];
     double s = 0.0;
     for (int i = threadIdx.x; i < hd; i += blockDim.x) s = __fma_rn((double)kv[i], (double)kv[i], s);
     s = block_sum_d(s, red);
     const float inv = (float)(1.0 / sqrt(s / (double)hd + (double)eps));
     for (int i = threadIdx.x; i < hd; i += blockDim.x) kv[i] = __fmul_rn(w[i], __fmul_rn(kv[i], inv));
     __syncthreads();
-    rope_tail(kv, hd, rd, cs, sn, st->pos, 0);
+    rope_tail(kv, hd, rd, cs, sn, pos, 0);
     __syncthreads();
-    float *dst = cache + (size_t)(st->pos % win) * hd;
+    float *dst = cache + (size_t)(pos % win) * hd;
     for (int i = threadIdx.x; i < hd; i += blockDim.x) dst[i] = kv[i];
 }
 
-// One HCA compressor step (src/core/dsv4_compress.c:78-138) and, when a
-// window closes, RMSNorm + RoPE at pos+1-ratio and the cache write
-// (src/model/dsv4_layer.c:250-260). Also publishes this step's compressed-row
-// count and the indexer's take: dyn[0] = avail, dyn[1] = min(avail, topk).
-// One block; kv_state / score_state are [coff*ratio][coff*hd].
-__global__ void k_compress(float *cache, float *kv_state, float *score_state, const float *kv_in,
-                           const float *sc_in, const float *ape, const float *norm, int ratio, int hd, int rd,
-                           const float *cs, const float *sn, const StepState *st, float eps, int win,
-                           int index_topk, int *dyn)
+__device__ void compress_step(float *cache, float *kv_state, float *score_state, const float *kv_in,
+                              const float *sc_in, const float *ape, const float *norm, int ratio, int hd, int rd,
+                              const float *cs, const float *sn, int pos, float eps, int win, int index_topk,
+                              int *dyn, float *cbuf, double *red)
 {
-    pdl_trigger();
-    pdl_wait();
-    extern __shared__ float cbuf[];     // [hd]
-    __shared__ double red[33];
-    const int pos = st->pos, overlap = (ratio == 4), coff = 1 + overlap, width = coff * hd;
+    const int overlap = (ratio == 4), coff = 1 + overlap, width = coff * hd;
     const int phase = pos % ratio, slot = overlap ? ratio + phase : phase;
     const float *apr = ape + (size_t)phase * width;
     for (int c = threadIdx.x; c < width; c += blockDim.x) {
@@ -502,6 +502,62 @@ __global__ void k_compress(float *cache, float *kv_state, float *score_state, co
     float *dst = cache + (size_t)(win + avail - 1) * hd;
     for (int i = threadIdx.x; i < hd; i += blockDim.x) dst[i] = cbuf[i];
 }
+// The attended rows of one token (src/model/dsv4_layer.c:504 and :295): the
+// window newest first, then the compressed rows -- the indexer's selection
+// (sel) on indexer layers, else all (pos + 1) / ratio of them -- in cache
+// coordinates; -1 past the end.
+__device__ void build_idxs(int *idxs, int nmax, int pos, int win, int has_comp, int has_idx, int take,
+                           const int *sel)
+{
+    const int n = (pos + 1 < win) ? pos + 1 : win;
+    if (!has_comp) take = 0;
+    for (int i = threadIdx.x; i < nmax; i += blockDim.x) {
+        int v = -1;
+        if (i < n) v = (pos - i) % win;
+        else if (i < n + take) v = (has_idx ? __ldcg(sel + i - n) : i - n) + win;
+        idxs[i] = v;
+    }
+}
+
+// Everything between the q projections and the indexer / attention of one
+// layer, one block per task (src/model/dsv4_layer.c:224-295): blocks
+// [0, H) normalise and rotate a q head, block H finishes the KV row, then
+// (compressing layers) one block runs the compressor step, then (indexer
+// layers) ih blocks rotate the indexer's q heads, or (other layers) one block
+// writes the attended row list. Every task is the whole-block code of the
+// kernel it replaces, so the results are those of the separate launches.
+__global__ void __launch_bounds__(256) k_attn_prep(const __grid_constant__ PrepArgs a)
+{
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ float cbuf[];     // [hd], the compressor's row
+    __shared__ double red[33];
+    const int pos = a.st->pos;
+    int b = blockIdx.x;
+    if (b < a.H) {
+        head_norm_rope(a.q + (size_t)b * a.hd, a.hd, a.rd, a.cs, a.sn, pos, 0, 1, a.eps, red);
+        return;
+    }
+    b -= a.H;
+    if (b == 0) {
+        kv_finish(a.kv, a.kv_norm, a.hd, a.rd, a.cs, a.sn, pos, a.eps, a.cache, a.win, red);
+        return;
+    }
+    b -= 1;
+    if (a.has_comp) {
+        if (b == 0) {
+            compress_step(a.cache, a.comp_kv, a.comp_score, a.comp_in, a.comp_sc, a.ape, a.cnorm, a.ratio, a.hd,
+                          a.rd, a.cs, a.sn, pos, a.eps, a.win, a.index_topk, a.dyn, cbuf, red);
+            return;
+        }
+        b -= 1;
+    }
+    if (a.has_idx) {
+        if (b < a.ih) head_norm_rope(a.idx_q + (size_t)b * a.id, a.id, a.rd, a.cs, a.sn, pos, 0, 0, a.eps, red);
+        return;
+    }
+    if (b == 0) build_idxs(a.idxs, a.nidx, pos, a.win, a.has_comp, 0, a.has_comp ? (pos + 1) / a.ratio : 0, nullptr);
+}
 
 // The attention index list (src/model/dsv4_layer.c:504-505 and :278-297):
 // the window's ring slots of the last min(pos+1, win) positions, newest
@@ -512,15 +568,7 @@ __global__ void k_build_idxs(int *idxs, int nmax, const StepState *st, int win, 
 {
     pdl_trigger();
     pdl_wait();
-    const int pos = st->pos;
-    const int n = (pos + 1 < win) ? pos + 1 : win;
-    const int take = has_comp ? (has_idx ? dyn[1] : dyn[0]) : 0;
-    for (int i = threadIdx.x; i < nmax; i += blockDim.x) {
-        int v = -1;
-        if (i < n) v = (pos - i) % win;
-        else if (i < n + take) v = (has_idx ? sel[i - n] : i - n) + win;
-        idxs[i] = v;
-    }
+    build_idxs(idxs, nmax, st->pos, win, has_comp, has_idx, has_comp ? __ldcg(dyn + (has_idx ? 1 : 0)) : 0, sel);
 }
 
 // Argmax, first maximum (src/cli/dsv4_run.c:472-473), two stages; the second
@@ -556,11 +604,22 @@ __global__ void k_argmax_final(StepState *st, int *out_tokens, const float *pv, 
 {
     pdl_trigger();
     pdl_wait();
+    if (threadIdx.x >= 32) return;
+    // one warp: each lane the best of its strided share, then the same
+    // comparison (larger value, ties to the lower index) across lanes
+    float bv = -INFINITY;
+    int bi = -1;
+    for (int i = threadIdx.x; i < nparts; i += 32) {
+        const float v = ld_act(pv + i);
+        const int ix = __ldcg(pi + i);
+        if (ix >= 0 && (bi < 0 || v > bv || (v == bv && ix < bi))) { bv = v; bi = ix; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+    }
     if (threadIdx.x != 0) return;
-    float bv = pv[0];
-    int bi = pi[0];
-    for (int i = 1; i < nparts; i++)
-        if (pi[i] >= 0 && (bi < 0 || pv[i] > bv || (pv[i] == bv && pi[i] < bi))) { bv = pv[i]; bi = pi[i]; }
     const int pos = st->pos;
     out_tokens[pos] = bi;
     const int next = pos + 1;

@@ -92,7 +92,7 @@ __global__ void k_combine(float *out, const float *acc, const float *w, int topk
 }
 
 int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float *x,
-                const int *token, cudaStream_t st)
+                const int *token, cudaStream_t st, bool combine)
 {
     const int H = L.hidden, I = L.inter, K = L.topk;
     PdlChain chain;
@@ -144,7 +144,8 @@ int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float 
         n++;
     }
     if (gemv_group(it, n, st)) return -1;
-    launch(k_combine, dim3((H + 255) / 256), dim3(256), 0, st, out, S.acc, S.wts, K, H, Is ? accs : nullptr);
+    if (combine)
+        launch(k_combine, dim3((H + 255) / 256), dim3(256), 0, st, out, S.acc, S.wts, K, H, Is ? accs : nullptr);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 

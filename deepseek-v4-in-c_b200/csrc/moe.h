@@ -39,8 +39,11 @@ struct MoeScratch {
     int *sel;
 };
 
+// out = the MoE of x. With combine false the last step (out = sum_k wts[k]
+// acc[k] + the shared expert's acc) is left to the caller, which reads
+// S.acc / S.wts itself (the decode step folds it into the next mHC launch).
 int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float *x,
-                const int *token, cudaStream_t st);
+                const int *token, cudaStream_t st, bool combine = true);
 size_t moe_scratch_floats(int hidden, int inter, int inter_shared, int n_experts, int topk);
 void moe_scratch_carve(MoeScratch &S, float *base, int hidden, int inter, int inter_shared,
                        int n_experts, int topk);

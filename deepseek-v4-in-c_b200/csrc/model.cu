@@ -317,7 +317,7 @@ static void hc_step(dsv4b_model *m, Pending &p, float *&hin, float *&hout, const
         a.nmix = head ? hc : mix;
         a.hc_eps = c.hc_eps;
         a.rms_eps = c.rms_eps;
-        launch(k_hc_pre, dim3(n / 256), dim3(256), 0, st, a);
+        launch(k_hc_pre, dim3(n / 256), dim3(288), 0, st, a);
         if (p.kind) std::swap(hin, hout);
         p.kind = 0;
         return;

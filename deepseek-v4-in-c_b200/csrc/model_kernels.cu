@@ -28,6 +28,24 @@ __device__ __forceinline__ double block_sum_d(double v, double *red)
     return red[32];
 }
 
+// block_sum_d over the first nw warps only, synchronised by named barrier
+// bar (the other warps of the block are busy elsewhere).
+__device__ __forceinline__ double part_sum_d(double v, double *red, int nw, int bar)
+{
+    v = warp_sum_d(v);
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nw * 32) : "memory");
+    if (lane == 0) red[w] = v;
+    asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nw * 32) : "memory");
+    double t = 0.0;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < nw; i++) t += red[i];
+        red[32] = t;
+    }
+    asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nw * 32) : "memory");
+    return red[32];
+}
+
 // dsv4_embed_row (include/dsv4/dsv4.h:300-314), replicated hc times
 // (src/cli/dsv4_run.c:449-450).
 __global__ void k_embed(float *h, const void *table, int wdt, const StepState *st, int hidden, int hc)
@@ -135,10 +153,11 @@ __global__ void k_hc_finish(float *y, float *post, float *comb, const float *mix
 //                summed per block in a fixed order (32 columns in float, then
 //                8 such sums in double), written to part[block][0..nmix];
 //   last block:  the partials summed in block order (double), mixes, the
-//                pre weights, [layers: post weights and the Sinkhorn split,
-//                lanes of one warp, each lane one comb entry, every row /
-//                column sum gathered through shared memory and added in the
-//                serial order], y = sum_j pre[j] x[j], RMSNorm.
+//                pre weights; then, at the same time, warps 0..7 compute
+//                y = sum_j pre[j] x[j] and its RMSNorm while warp 8 (layers)
+//                computes the post weights and the Sinkhorn split (each lane
+//                one comb entry, every row / column fetched by shuffles and
+//                summed in double in index order, as the reference does).
 // Head mode (post null, nmix = hc) is the head's reduction
 // (src/cli/dsv4_run.c:94-116): the sigmoid pre weights only.
 // The reference sums these in double; here only the short sums across warps
@@ -147,7 +166,7 @@ __global__ void k_hc_finish(float *y, float *post, float *comb, const float *mix
 // at *count completes the grid; it resets *count, so the kernel is
 // replayable. post_in / comb_in may be the post / comb outputs: every block
 // has read them before it arrives at *count. hc * hc <= 32.
-__global__ void __launch_bounds__(256) k_hc_pre(const __grid_constant__ HcPreArgs a)
+__global__ void __launch_bounds__(288) k_hc_pre(const __grid_constant__ HcPreArgs a)
 {
     constexpr int MIXMAX = kHcPreMixMax, NV = MIXMAX + 1;
     __shared__ float prod[NV][256];
@@ -160,23 +179,25 @@ __global__ void __launch_bounds__(256) k_hc_pre(const __grid_constant__ HcPreArg
     pdl_trigger();
     if (tid < mix) sbase[tid] = __ldg(a.base + tid);     // weights: before the wait
     if (tid < (a.post ? 3 : 1)) sscale[tid] = __ldg(a.scale + tid);
-    // one column per thread (the launcher sizes the grid to n / 256); its fn
-    // column is a weight, fetched before waiting for x
-    const int i = blockIdx.x * blockDim.x + tid;
+    // one column per thread of warps 0..7 (the launcher sizes the grid to
+    // n / 256; warp 8 only runs the split); its fn column is a weight,
+    // fetched before waiting for x
+    const bool col = tid < 256;
+    const int i = blockIdx.x * 256 + tid;
     const int h4 = hidden >> 2;
     float4 wn[kHcPreYPT];                                // the norm weights of this thread's columns
 #pragma unroll
     for (int u = 0; u < kHcPreYPT; u++) {
-        const int d4 = tid + u * (int)blockDim.x;
-        wn[u] = (a.norm_w && d4 < h4) ? __ldg(reinterpret_cast<const float4 *>(a.norm_w) + d4)
+        const int d4 = tid + u * 256;
+        wn[u] = (a.norm_w && col && d4 < h4) ? __ldg(reinterpret_cast<const float4 *>(a.norm_w) + d4)
                                       : make_float4(1.f, 1.f, 1.f, 1.f);
     }
     float fv[MIXMAX];
 #pragma unroll
-    for (int m = 0; m < MIXMAX; m++) fv[m] = (m < mix && i < n) ? __ldg(a.fn + (size_t)m * n + i) : 0.0f;
+    for (int m = 0; m < MIXMAX; m++) fv[m] = (m < mix && col && i < n) ? __ldg(a.fn + (size_t)m * n + i) : 0.0f;
     pdl_wait();
     float xv = 0.0f;
-    if (i < n) {
+    if (col && i < n) {
         if (stepped) {
             const int j = i / hidden, d = i - j * hidden;
             float b;
@@ -199,9 +220,11 @@ __global__ void __launch_bounds__(256) k_hc_pre(const __grid_constant__ HcPreArg
             xv = ld_act(a.x + i);
         }
     }
+    if (col) {
 #pragma unroll
-    for (int m = 0; m < MIXMAX; m++) prod[m][tid] = __fmul_rn(fv[m], xv);
-    prod[MIXMAX][tid] = __fmul_rn(xv, xv);
+        for (int m = 0; m < MIXMAX; m++) prod[m][tid] = __fmul_rn(fv[m], xv);
+        prod[MIXMAX][tid] = __fmul_rn(xv, xv);
+    }
     __syncthreads();
     if (tid < NV * 8) {
         const int m = tid >> 3, w = tid & 7;
@@ -248,54 +271,46 @@ __global__ void __launch_bounds__(256) k_hc_pre(const __grid_constant__ HcPreArg
     if (tid < 32) {
         const float rs = __fdiv_rn(1.0f, __fsqrt_rn((float)(tot[MIXMAX] / (double)n) + a.rms_eps));
         if (tid < mix) mixes[tid] = __fmul_rn((float)tot[tid], rs);
+        __syncwarp();
+        if (tid < hc) pre[tid] = __fadd_rn(sigm(__fadd_rn(__fmul_rn(mixes[tid], sscale[0]), sbase[tid])), a.hc_eps);
     }
-    __syncwarp();
-    if (tid < hc) pre[tid] = __fadd_rn(sigm(__fadd_rn(__fmul_rn(mixes[tid], sscale[0]), sbase[tid])), a.hc_eps);
-    if (a.post && tid < 32) {
-        // lane l = one comb entry (row j, column k); a row's or a column's
-        // values are gathered through shared memory and added in order
-        __shared__ float cm[32];
-        const int l = tid, j = l / hc, k = l % hc;
+    __syncthreads();
+    if (tid >= 256) {
+        // the extra warp: post weights and the Sinkhorn split, concurrently
+        // with y below (only the next sub-layer's post-mix reads them)
+        if (!a.post) return;
+        const int l = tid - 256, j = l / hc, k = l % hc;
         const bool act = l < hc * hc;
         const float hc_eps = a.hc_eps;
+        const unsigned full = 0xffffffffu;
         if (l < hc) a.post[l] = __fmul_rn(2.0f, sigm(__fadd_rn(__fmul_rn(mixes[l + hc], sscale[1]), sbase[l + hc])));
         const int o = 2 * hc + (act ? l : 0);
         float v = __fadd_rn(__fmul_rn(mixes[o], sscale[2]), sbase[o]);
         const int rj = act ? j * hc : 0, ck = act ? k : 0;
-        // row softmax: max, exp, sum in k order, scale, + eps
-        cm[l] = v;
-        __syncwarp();
-        float mx = cm[rj];
-        for (int kk = 1; kk < hc; kk++) mx = fmaxf(mx, cm[rj + kk]);
+        // lane l holds comb[j][k]; a row's (column's) entries are fetched by
+        // shuffles and summed in double in index order, as the reference does
+        float mx = __shfl_sync(full, v, rj);
+        for (int kk = 1; kk < hc; kk++) mx = fmaxf(mx, __shfl_sync(full, v, rj + kk));
         const float e = expf(v - mx);
-        __syncwarp();
-        cm[l] = e;
-        __syncwarp();
-        float sum = 0.0f;
-        for (int kk = 0; kk < hc; kk++) sum = __fadd_rn(sum, cm[rj + kk]);
-        v = __fadd_rn(__fmul_rn(e, __fdiv_rn(1.0f, sum)), hc_eps);
+        double sum = 0.0;
+        for (int kk = 0; kk < hc; kk++) sum = __dadd_rn(sum, (double)__shfl_sync(full, e, rj + kk));
+        v = __fadd_rn(__fmul_rn(e, (float)(1.0 / sum)), hc_eps);
         const int npass = a.iters > 1 ? a.iters : 1;
         for (int pass = 0; pass < npass; pass++) {
             if (pass > 0) {
-                __syncwarp();
-                cm[l] = v;
-                __syncwarp();
-                float r = 0.0f;
-                for (int kk = 0; kk < hc; kk++) r = __fadd_rn(r, cm[rj + kk]);
-                v = __fdiv_rn(v, __fadd_rn(r, hc_eps));
+                double r = 0.0;
+                for (int kk = 0; kk < hc; kk++) r = __dadd_rn(r, (double)__shfl_sync(full, v, rj + kk));
+                v = __fdiv_rn(v, __fadd_rn((float)r, hc_eps));
             }
-            __syncwarp();
-            cm[l] = v;
-            __syncwarp();
-            float c = 0.0f;
-            for (int jj = 0; jj < hc; jj++) c = __fadd_rn(c, cm[jj * hc + ck]);
-            v = __fdiv_rn(v, __fadd_rn(c, hc_eps));
+            double cs = 0.0;
+            for (int jj = 0; jj < hc; jj++) cs = __dadd_rn(cs, (double)__shfl_sync(full, v, jj * hc + ck));
+            v = __fdiv_rn(v, __fadd_rn((float)cs, hc_eps));
         }
         if (act) a.comb[l] = v;
+        return;
     }
-    __syncthreads();
-    // y = sum_j pre[j] x[j], four columns per float4, in two batches of loads;
-    // then RMSNorm from the registers
+    // warps 0..7: y = sum_j pre[j] x[j], four columns per float4, in two
+    // batches of loads; then RMSNorm from the registers
     const float4 *x4 = reinterpret_cast<const float4 *>(x);
     float4 yv[kHcPreYPT];
     float sq = 0.0f;
@@ -305,14 +320,14 @@ __global__ void __launch_bounds__(256) k_hc_pre(const __grid_constant__ HcPreArg
         float4 xw[YB][4];
 #pragma unroll
         for (int uu = 0; uu < YB; uu++) {
-            const int d4 = tid + (half * YB + uu) * (int)blockDim.x;
+            const int d4 = tid + (half * YB + uu) * 256;
 #pragma unroll
             for (int j = 0; j < 4; j++)
                 xw[uu][j] = (d4 < h4 && j < hc) ? __ldcg(x4 + (size_t)j * h4 + d4) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int uu = 0; uu < YB; uu++) {
-            const int u = half * YB + uu, d4 = tid + u * (int)blockDim.x;
+            const int u = half * YB + uu, d4 = tid + u * 256;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             if (d4 < h4) {
 #pragma unroll
@@ -336,13 +351,13 @@ __global__ void __launch_bounds__(256) k_hc_pre(const __grid_constant__ HcPreArg
     float inv = 1.0f;
     if (a.norm_w) {
         __shared__ double nred[33];
-        const double ssq = block_sum_d((double)sq, nred);
+        const double ssq = part_sum_d((double)sq, nred, 8, 1);
         inv = __fdiv_rn(1.0f, __fsqrt_rn((float)(ssq / (double)hidden) + a.rms_eps));
     }
     float4 *y4 = reinterpret_cast<float4 *>(a.y);
 #pragma unroll
     for (int u = 0; u < kHcPreYPT; u++) {
-        const int d4 = tid + u * (int)blockDim.x;
+        const int d4 = tid + u * 256;
         if (d4 < h4) {
             float4 o = yv[u];
             if (a.norm_w) {

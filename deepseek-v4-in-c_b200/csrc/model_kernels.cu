@@ -140,6 +140,66 @@ __global__ void k_hc_finish(float *y, float *post, float *comb, const float *mix
     }
 }
 
+// The Sinkhorn split of the comb mixes (src/core/dsv4_hc.c:63-101) on one
+// warp: lane l holds comb[l / hc][l % hc]; a row's (column's) entries are
+// fetched by shuffles and summed in double in index order, rounded to float,
+// plus eps, as the reference does, and every entry divided (float, correctly
+// rounded). HC > 0 fixes hc at compile time, so the shuffles of a sum are
+// issued together; HC = 0 takes hc at run time. hc * hc <= 32.
+template <int HC>
+__device__ __forceinline__ void sinkhorn_warp(float *comb, const float *mixes, float scale2, const float *base,
+                                              int hc_rt, int iters, float eps)
+{
+    const int hc = HC > 0 ? HC : hc_rt;
+    const int l = threadIdx.x & 31, j = l / hc, k = l % hc;
+    const bool act = l < hc * hc;
+    const unsigned full = 0xffffffffu;
+    const int o = 2 * hc + (act ? l : 0);
+    float v = __fadd_rn(__fmul_rn(mixes[o], scale2), base[o]);
+    const int rj = act ? j * hc : 0, ck = act ? k : 0;
+    constexpr int NU = HC > 0 ? HC : 8;           // unroll bound
+    auto row_sum = [&](float x) {
+        float g[NU];
+#pragma unroll
+        for (int kk = 0; kk < NU; kk++) g[kk] = kk < hc ? __shfl_sync(full, x, rj + kk) : 0.0f;
+        double s = 0.0;
+#pragma unroll
+        for (int kk = 0; kk < NU; kk++)
+            if (kk < hc) s = __dadd_rn(s, (double)g[kk]);
+        return s;
+    };
+    auto col_sum = [&](float x) {
+        float g[NU];
+#pragma unroll
+        for (int jj = 0; jj < NU; jj++) g[jj] = jj < hc ? __shfl_sync(full, x, jj * hc + ck) : 0.0f;
+        double s = 0.0;
+#pragma unroll
+        for (int jj = 0; jj < NU; jj++)
+            if (jj < hc) s = __dadd_rn(s, (double)g[jj]);
+        return s;
+    };
+    // first pass: row softmax (max, exp, double sum), + eps, then columns
+    float mx;
+    {
+        float g[NU];
+#pragma unroll
+        for (int kk = 0; kk < NU; kk++) g[kk] = kk < hc ? __shfl_sync(full, v, rj + kk) : -INFINITY;
+        mx = g[0];
+#pragma unroll
+        for (int kk = 1; kk < NU; kk++)
+            if (kk < hc) mx = fmaxf(mx, g[kk]);
+    }
+    const float e = expf(v - mx);
+    v = __fadd_rn(__fmul_rn(e, (float)(1.0 / row_sum(e))), eps);
+    v = __fdiv_rn(v, __fadd_rn((float)col_sum(v), eps));
+    // the remaining iters - 1 passes: rows, then columns
+    for (int pass = 1; pass < iters; pass++) {
+        v = __fdiv_rn(v, __fadd_rn((float)row_sum(v), eps));
+        v = __fdiv_rn(v, __fadd_rn((float)col_sum(v), eps));
+    }
+    if (act) comb[l] = v;
+}
+
 // The whole mHC pre-mix of one sub-layer in one launch, with the sub-layer's
 // RMSNorm folded in (src/core/dsv4_hc.c:118-140 with dsv4_hc_split_sinkhorn
 // :50-102, then src/core/dsv4_ops.c:25-32 when norm_w is given), optionally
@@ -279,34 +339,12 @@ __global__ void __launch_bounds__(288) k_hc_pre(const __grid_constant__ HcPreArg
         // the extra warp: post weights and the Sinkhorn split, concurrently
         // with y below (only the next sub-layer's post-mix reads them)
         if (!a.post) return;
-        const int l = tid - 256, j = l / hc, k = l % hc;
-        const bool act = l < hc * hc;
-        const float hc_eps = a.hc_eps;
-        const unsigned full = 0xffffffffu;
+        const int l = tid - 256;
         if (l < hc) a.post[l] = __fmul_rn(2.0f, sigm(__fadd_rn(__fmul_rn(mixes[l + hc], sscale[1]), sbase[l + hc])));
-        const int o = 2 * hc + (act ? l : 0);
-        float v = __fadd_rn(__fmul_rn(mixes[o], sscale[2]), sbase[o]);
-        const int rj = act ? j * hc : 0, ck = act ? k : 0;
-        // lane l holds comb[j][k]; a row's (column's) entries are fetched by
-        // shuffles and summed in double in index order, as the reference does
-        float mx = __shfl_sync(full, v, rj);
-        for (int kk = 1; kk < hc; kk++) mx = fmaxf(mx, __shfl_sync(full, v, rj + kk));
-        const float e = expf(v - mx);
-        double sum = 0.0;
-        for (int kk = 0; kk < hc; kk++) sum = __dadd_rn(sum, (double)__shfl_sync(full, e, rj + kk));
-        v = __fadd_rn(__fmul_rn(e, (float)(1.0 / sum)), hc_eps);
-        const int npass = a.iters > 1 ? a.iters : 1;
-        for (int pass = 0; pass < npass; pass++) {
-            if (pass > 0) {
-                double r = 0.0;
-                for (int kk = 0; kk < hc; kk++) r = __dadd_rn(r, (double)__shfl_sync(full, v, rj + kk));
-                v = __fdiv_rn(v, __fadd_rn((float)r, hc_eps));
-            }
-            double cs = 0.0;
-            for (int jj = 0; jj < hc; jj++) cs = __dadd_rn(cs, (double)__shfl_sync(full, v, jj * hc + ck));
-            v = __fdiv_rn(v, __fadd_rn((float)cs, hc_eps));
-        }
-        if (act) a.comb[l] = v;
+        if (hc == 4)
+            sinkhorn_warp<4>(a.comb, mixes, sscale[2], sbase, 4, a.iters, a.hc_eps);
+        else
+            sinkhorn_warp<0>(a.comb, mixes, sscale[2], sbase, hc, a.iters, a.hc_eps);
         return;
     }
     // warps 0..7: y = sum_j pre[j] x[j], four columns per float4, in two

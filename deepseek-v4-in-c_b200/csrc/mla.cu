@@ -294,7 +294,8 @@ k_topk(int *idx_out, const float *scores, int n, int k, long seq_in_stride, long
 
 // --------------------------------------------------------------- attention
 constexpr int AT_CH = 32;      // selected positions per chunk
-constexpr int AT_HB = 8;       // heads per block (one warp each in the scores)
+constexpr int AT_HB = 16;      // heads per block
+constexpr int AT_NW = 8;       // warps per block (column slices of the scores)
 
 // Per (sequence, chunk, head) partials: chunk max pm, exp-sum pden (double)
 // and the unnormalised value sum po[d]. A chunk with no valid position has
@@ -305,14 +306,26 @@ struct AttnPart {
     double *pden;
 };
 
-// Rows of the KV tile are padded to d + 4 floats: 16-byte aligned, and the
-// float4 reads of 8 consecutive lanes (one shared-memory phase) of rows p..p+7
-// fall in distinct banks.
-size_t attn_smem_bytes(int d) { return ((size_t)AT_CH * (d + 4) + (size_t)AT_HB * d + AT_CH * AT_HB) * 4; }
+// Shared memory: KV rows and q rows padded to d + 4 floats (16-byte aligned;
+// for d a multiple of 32 every row starts 4 banks after the previous one, so
+// the reads below are conflict-free), the per-slice partial scores [8][32][17]
+// and the weights [32][16].
+size_t attn_smem_bytes(int d)
+{
+    return ((size_t)AT_CH * (d + 4) + (size_t)AT_HB * (d + 4) + (size_t)AT_NW * AT_CH * 17 + AT_CH * AT_HB) * 4;
+}
 
 // grid (nchunk, ceil(n_heads / AT_HB), batch), 256 threads. The index list
 // holds its valid entries first, so the chunks past them only mark
 // themselves empty. d is a multiple of 4.
+//   scores: warp w takes the float4 column groups g = w, w + 8, ...; lane
+//           (pg = lane / 4, hg = lane % 4) accumulates positions pg + 8i and
+//           heads hg + 4j (i, j < 4) by fma over its groups in order; the 8
+//           slice sums of a (position, head) are then added in slice order;
+//   softmax: per head over the chunk's valid positions: max, expf, exp-sum in
+//           double (the sink is added by k_attn_combine);
+//   values:  a thread owns columns c and c + 256 for all 16 heads, fma over
+//           the positions in order (masked rows are zero in shared memory).
 template <int KDT>
 __global__ void __launch_bounds__(256)
 k_attn_chunk(AttnPart part, const float *q, const void *kv, long seq_kv_rows,
@@ -324,16 +337,18 @@ k_attn_chunk(AttnPart part, const float *q, const void *kv, long seq_kv_rows,
     extern __shared__ __align__(16) float ats[];
     const int dp = d + 4, nd4 = d >> 2;
     float *kvs = ats;                                       // [AT_CH][dp]
-    float *qs = kvs + AT_CH * dp;                           // [AT_HB][d]
-    float *scT = qs + AT_HB * d;                            // [AT_CH][AT_HB]: weights, transposed
+    float *qs = kvs + AT_CH * dp;                           // [AT_HB][dp]
+    float *ps = qs + AT_HB * dp;                            // [AT_NW][AT_CH][17]
+    float *scT = ps + AT_NW * AT_CH * 17;                   // [AT_CH][AT_HB]: weights
     __shared__ int pidx[AT_CH];
     const int b = blockIdx.z, nch = gridDim.x, c0 = blockIdx.x * AT_CH, tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
     const int h0 = blockIdx.y * AT_HB, nh = min(AT_HB, n_heads - h0);
     q += (size_t)b * seq_q_stride + (size_t)h0 * d;
     idxs += (size_t)b * seq_idx_stride;
     const char *kvb = reinterpret_cast<const char *>(kv) + (size_t)b * seq_kv_rows * d * dt_bytes<KDT>;
     const int npos = min(AT_CH, topk - c0);
-    const int pi = (tid < npos) ? idxs[c0 + tid] : -1;
+    const int pi = (tid < npos) ? __ldcg(idxs + c0 + tid) : -1;
     if (tid < AT_CH) pidx[tid] = pi;
     const size_t prow = ((size_t)b * nch + blockIdx.x) * n_heads + h0;
     if (!__syncthreads_or(tid < AT_CH && pi >= 0)) {
@@ -343,96 +358,126 @@ k_attn_chunk(AttnPart part, const float *q, const void *kv, long seq_kv_rows,
         }
         return;
     }
-    // KV rows: thread (row tid/8, lane group tid%8) moves float4 groups
-    // g = tid%8 + 8k of its row, 8 loads in flight; masked rows are skipped
-    // (their scores become -inf and their weights 0, so they are never read)
+    // KV rows: thread (row tid / 8, lane group tid % 8) moves float4 groups
+    // tid % 8 + 8k of its row, up to 16 loads in flight; masked rows are
+    // zero-filled
     {
         const int p = tid >> 3, part8 = tid & 7, r = pidx[p];
-        if (r >= 0) {
-            for (int g0 = part8; g0 < nd4; g0 += 64) {
-                float4 v[8];
+        for (int g0 = part8; g0 < nd4; g0 += 128) {
+            float4 v[16];
 #pragma unroll
-                for (int u = 0; u < 8; u++) {
-                    const int g = g0 + 8 * u;
-                    v[u] = g < nd4 ? load4_t<KDT>(kvb, (size_t)r * d + 4 * g) : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
+            for (int u = 0; u < 16; u++) {
+                const int g = g0 + 8 * u;
+                v[u] = (r >= 0 && g < nd4) ? load4_t<KDT>(kvb, (size_t)r * d + 4 * g) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
 #pragma unroll
-                for (int u = 0; u < 8; u++) {
-                    const int g = g0 + 8 * u;
-                    if (g < nd4) *reinterpret_cast<float4 *>(kvs + p * dp + 4 * g) = v[u];
-                }
+            for (int u = 0; u < 16; u++) {
+                const int g = g0 + 8 * u;
+                if (g < nd4) *reinterpret_cast<float4 *>(kvs + p * dp + 4 * g) = v[u];
             }
         }
     }
-    // the block's q tile
+    // the block's q rows (zero past n_heads)
     {
-        const int n4 = nh * nd4;
+        const int n4 = AT_HB * nd4;
         for (int i0 = tid; i0 < n4; i0 += 8 * (int)blockDim.x) {
             float4 v[8];
 #pragma unroll
             for (int u = 0; u < 8; u++) {
-                const int i = i0 + u * (int)blockDim.x;
-                v[u] = i < n4 ? __ldcg(reinterpret_cast<const float4 *>(q) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                const int i = i0 + u * (int)blockDim.x, h = i / nd4;
+                v[u] = (i < n4 && h < nh) ? __ldcg(reinterpret_cast<const float4 *>(q) + i)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
             for (int u = 0; u < 8; u++) {
                 const int i = i0 + u * (int)blockDim.x;
-                if (i < n4) reinterpret_cast<float4 *>(qs)[i] = v[u];
+                if (i < n4) {
+                    const int h = i / nd4, g = i - h * nd4;
+                    *reinterpret_cast<float4 *>(qs + h * dp + 4 * g) = v[u];
+                }
             }
         }
     }
     __syncthreads();
-    // scores: warp = head, lane = position; four partial sums over c mod 4,
-    // then (a0 + a1) + (a2 + a3); the chunk max over valid slots (the sink is
-    // not part of it), exp weights, exp-sum in double
+    // scores, slice sums
     {
-        const int h = tid >> 5, p = tid & 31;
-        if (h < nh) {
-            float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-            const float4 *k4 = reinterpret_cast<const float4 *>(kvs + p * dp);
-            const float4 *q4 = reinterpret_cast<const float4 *>(qs + h * d);
-#pragma unroll 4
-            for (int g = 0; g < nd4; g++) {
-                const float4 qv = q4[g], kv4 = k4[g];
-                a0 = __fmaf_rn(qv.x, kv4.x, a0);
-                a1 = __fmaf_rn(qv.y, kv4.y, a1);
-                a2 = __fmaf_rn(qv.z, kv4.z, a2);
-                a3 = __fmaf_rn(qv.w, kv4.w, a3);
-            }
-            const float acc = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
+        const int pg = lane >> 2, hg = lane & 3;
+        float acc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+        for (int g = warp; g < nd4; g += AT_NW) {
+            float4 kq[4], qq[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) kq[i] = *reinterpret_cast<const float4 *>(kvs + (pg + 8 * i) * dp + 4 * g);
+#pragma unroll
+            for (int j = 0; j < 4; j++) qq[j] = *reinterpret_cast<const float4 *>(qs + (hg + 4 * j) * dp + 4 * g);
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    float t = acc[i][j];
+                    t = __fmaf_rn(qq[j].x, kq[i].x, t);
+                    t = __fmaf_rn(qq[j].y, kq[i].y, t);
+                    t = __fmaf_rn(qq[j].z, kq[i].z, t);
+                    t = __fmaf_rn(qq[j].w, kq[i].w, t);
+                    acc[i][j] = t;
+                }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) ps[(warp * AT_CH + pg + 8 * i) * 17 + hg + 4 * j] = acc[i][j];
+    }
+    __syncthreads();
+    // softmax: warp w takes heads 2w, 2w + 1; lane = position
+    {
+        const int p = lane;
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++) {
+            const int h = 2 * warp + hh;
+            float acc = 0.0f;
+#pragma unroll
+            for (int w = 0; w < AT_NW; w++) acc = __fadd_rn(acc, ps[(w * AT_CH + p) * 17 + h]);
             const float s = (pidx[p] >= 0) ? __fmul_rn(acc, scale) : -INFINITY;
             const float m = warp_max_f(s);
             const float e = (m == -INFINITY || s == -INFINITY) ? 0.0f : expf(s - m);
             const double ds = warp_sum_d((double)e);
             scT[p * AT_HB + h] = e;
-            if (p == 0) {
+            if (p == 0 && h < nh) {
                 part.pm[prow + h] = m;
                 part.pden[prow + h] = ds;
             }
-        } else if (tid - 32 * nh < 32 * (AT_HB - nh) && (tid & 31) < AT_CH) {
-            scT[(tid & 31) * AT_HB + h] = 0.0f;         // heads past n_heads
         }
     }
     __syncthreads();
-    // unnormalised value sums: a thread owns columns c and every head of the
-    // block; positions in order, each product and sum rounded separately
-    for (int c = tid; c < d; c += blockDim.x) {
-        float o[AT_HB];
+    // unnormalised value sums
+    for (int cb = tid; cb < d; cb += 2 * (int)blockDim.x) {
+        const int c1 = cb + (int)blockDim.x;
+        const bool two = c1 < d;
+        float o0[AT_HB], o1[AT_HB];
 #pragma unroll
-        for (int h = 0; h < AT_HB; h++) o[h] = 0.0f;
-#pragma unroll 4
+        for (int h = 0; h < AT_HB; h++) o0[h] = o1[h] = 0.0f;
+#pragma unroll 2
         for (int pp = 0; pp < AT_CH; pp++) {
-            const float4 ea = *reinterpret_cast<const float4 *>(scT + pp * AT_HB);
-            const float4 eb = *reinterpret_cast<const float4 *>(scT + pp * AT_HB + 4);
-            const float e[AT_HB] = {ea.x, ea.y, ea.z, ea.w, eb.x, eb.y, eb.z, eb.w};
-            const float kvv = kvs[pp * dp + c];
+            const float4 *e4 = reinterpret_cast<const float4 *>(scT + pp * AT_HB);
+            const float4 ea = e4[0], eb = e4[1], ec = e4[2], ed = e4[3];
+            const float e[AT_HB] = {ea.x, ea.y, ea.z, ea.w, eb.x, eb.y, eb.z, eb.w,
+                                    ec.x, ec.y, ec.z, ec.w, ed.x, ed.y, ed.z, ed.w};
+            const float v0 = kvs[pp * dp + cb], v1 = two ? kvs[pp * dp + c1] : 0.0f;
 #pragma unroll
-            for (int h = 0; h < AT_HB; h++)
-                o[h] = (e[h] != 0.0f) ? __fadd_rn(o[h], __fmul_rn(e[h], kvv)) : o[h];
+            for (int h = 0; h < AT_HB; h++) {
+                o0[h] = __fmaf_rn(e[h], v0, o0[h]);
+                o1[h] = __fmaf_rn(e[h], v1, o1[h]);
+            }
         }
 #pragma unroll
         for (int h = 0; h < AT_HB; h++)
-            if (h < nh) part.po[(prow + h) * d + c] = o[h];
+            if (h < nh) {
+                part.po[(prow + h) * d + cb] = o0[h];
+                if (two) part.po[(prow + h) * d + c1] = o1[h];
+            }
     }
 }
 

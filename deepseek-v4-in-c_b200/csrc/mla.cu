@@ -481,67 +481,93 @@ k_attn_chunk(AttnPart part, const float *q, const void *kv, long seq_kv_rows,
     }
 }
 
-// grid (n_heads, batch), 128 threads: rescale chunks in chunk order, add the
-// sink to the denominator only, normalise. The chunk factors are computed
-// once into shared memory; empty chunks (pm = -inf) are skipped.
+// grid (n_heads, ceil(d / 128), batch), 128 threads, one output column per
+// thread: rescale chunks in chunk order, add the sink to the denominator
+// only, normalise. Every block works out the chunk factors of its head (a
+// few hundred values at most) and the list of live chunks (pm > -inf) in
+// order; empty chunks are skipped.
 constexpr int AT_MAXCH = 512;
 
-__global__ void k_attn_combine(float *o, AttnPart part, const float *sink, int nch, int n_heads, int d,
-                               long seq_o_stride, AttnRope rope)
+__global__ void __launch_bounds__(128)
+k_attn_combine(float *o, AttnPart part, const float *sink, int nch, int n_heads, int d, long seq_o_stride,
+               AttnRope rope)
 {
     pdl_trigger();
     pdl_wait();
     __shared__ float fac[AT_MAXCH];
-    __shared__ unsigned char live[AT_MAXCH];
+    __shared__ short lst[AT_MAXCH];
     __shared__ double dterm[AT_MAXCH];
     __shared__ float s_inv, s_M;
-    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    __shared__ int s_nl;
+    const int h = blockIdx.x, b = blockIdx.z, tid = threadIdx.x, cb0 = blockIdx.y * 128;
     float *ob = o + (size_t)b * seq_o_stride + (size_t)h * d;
     const size_t r0 = (size_t)b * nch * n_heads + h;
-    // chunk maxima, factors and exp-sum terms, all chunks at once; the terms
-    // are then added in chunk order
-    for (int c = tid; c < nch; c += blockDim.x) fac[c] = ld_act(part.pm + r0 + (size_t)c * n_heads);
-    __syncthreads();
     if (tid < 32) {
         float M = -INFINITY;
-        for (int c = tid; c < nch; c += 32) M = fmaxf(M, fac[c]);
-        M = warp_max_f(M);
-        if (tid == 0) s_M = M;
-        __syncwarp();
         for (int c = tid; c < nch; c += 32) {
-            const float mc = fac[c];
+            const float mc = ld_act(part.pm + r0 + (size_t)c * n_heads);
+            fac[c] = mc;
+            M = fmaxf(M, mc);
+        }
+        M = warp_max_f(M);
+        __syncwarp();
+        int base = 0;
+        for (int c0 = 0; c0 < nch; c0 += 32) {
+            const int c = c0 + tid;
+            const float mc = c < nch ? fac[c] : -INFINITY;
             const bool lv = mc != -INFINITY;
-            live[c] = lv;
-            dterm[c] = lv ? ld_act_d(part.pden + r0 + (size_t)c * n_heads) * (double)expf(mc - M) : 0.0;
-            fac[c] = lv ? ((mc == M) ? 1.0f : expf(mc - M)) : 0.0f;
+            if (c < nch) {
+                dterm[c] = lv ? ld_act_d(part.pden + r0 + (size_t)c * n_heads) * (double)expf(mc - M) : 0.0;
+                fac[c] = lv ? ((mc == M) ? 1.0f : expf(mc - M)) : 0.0f;
+            }
+            const unsigned live = __ballot_sync(0xffffffffu, lv);
+            if (lv) lst[base + __popc(live & ((1u << tid) - 1u))] = (short)c;
+            base += __popc(live);
         }
         __syncwarp();
-        if (tid == 0 && M != -INFINITY) {
-            double den = 0.0;
-            for (int c = 0; c < nch; c++)
-                if (live[c]) den += dterm[c];
-            den += (double)expf(sink[h] - M);
-            s_inv = (float)(1.0 / den);
+        if (tid == 0) {
+            s_M = M;
+            s_nl = base;
+            if (M != -INFINITY) {
+                double den = 0.0;
+                for (int k = 0; k < base; k++) den += dterm[lst[k]];
+                den += (double)expf(sink[h] - M);
+                s_inv = (float)(1.0 / den);
+            }
         }
     }
     __syncthreads();
+    const int cc = cb0 + tid;
     if (s_M == -INFINITY) {       // nothing valid: zero output (dsv4_attn.c:32-37)
-        for (int c = tid; c < d; c += blockDim.x) ob[c] = 0.0f;
+        if (cc < d) ob[cc] = 0.0f;
         return;
     }
-    const float inv = s_inv;
-    for (int cc = tid; cc < d; cc += blockDim.x) {
+    const int nl = s_nl;
+    if (cc < d) {
+        const float *pc = part.po + r0 * d + cc;
+        const size_t cstride = (size_t)n_heads * d;
         float acc = 0.0f;
-#pragma unroll 4
-        for (int c = 0; c < nch; c++) {
-            if (!live[c]) continue;
-            acc = __fadd_rn(acc, __fmul_rn(ld_act(part.po + (r0 + (size_t)c * n_heads) * d + cc), fac[c]));
+        for (int k0 = 0; k0 < nl; k0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) v[u] = k0 + u < nl ? ld_act(pc + (size_t)lst[k0 + u] * cstride) : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                if (k0 + u < nl) acc = __fadd_rn(acc, __fmul_rn(v[u], fac[lst[k0 + u]]));
         }
-        ob[cc] = __fmul_rn(acc, inv);
+        ob[cc] = __fmul_rn(acc, s_inv);
     }
-    if (rope.cs) {          // de-rotate the head (src/model/dsv4_layer.c:303-305)
+    if (rope.cs) {          // de-rotate this block's part of the tail (src/model/dsv4_layer.c:303-305)
         __syncthreads();
-        rope_tail(ob, d, rope.rd, rope.cs, rope.sn, __ldcg(rope.pos), 1);
+        const int half = rope.rd / 2, pos = __ldcg(rope.pos), t0 = d - rope.rd;
+        for (int i = tid; i < half; i += blockDim.x) {
+            const int e0 = t0 + 2 * i;
+            if (e0 < cb0 || e0 >= cb0 + 128) continue;
+            const float re = ob[e0], im = ob[e0 + 1];
+            const float ci = rope.cs[(size_t)pos * half + i], si = -rope.sn[(size_t)pos * half + i];
+            ob[e0] = __fsub_rn(__fmul_rn(re, ci), __fmul_rn(im, si));
+            ob[e0 + 1] = __fadd_rn(__fmul_rn(re, si), __fmul_rn(im, ci));
+        }
     }
 }
 
@@ -639,7 +665,7 @@ int sparse_attn(float *o, const float *q, const void *kv, int kv_dt, long seq_kv
         launch(k_attn_chunk<DSV4B_DT_E4M3>, grid, dim3(256), smem, st, part, q, kv, seq_kv_rows, idxs, seq_idx_stride,
                n_heads, d, topk, scale, sq);
     const AttnRope rp = rope ? *rope : AttnRope{nullptr, nullptr, nullptr, 0};
-    launch(k_attn_combine, dim3(dim3(n_heads, batch)), dim3(128), 0, st, o, part, sink, nch, n_heads, d,
+    launch(k_attn_combine, dim3(n_heads, (d + 127) / 128, batch), dim3(128), 0, st, o, part, sink, nch, n_heads, d,
            (long)n_heads * d, rp);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }

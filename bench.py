@@ -227,10 +227,17 @@ def run_decode(a):
     max_pos = P + W + K + n_e2e + 8
     cfg = M.ConfigOnly(d)
     t0 = time.perf_counter()
-    model = B.Model(cfg, max_pos, synthetic_seed=1234 + rank)
+    if world > 1:
+        # one model sharded over the ranks: experts by inter slice, heads and
+        # o_groups, wo_b columns, the LM head's vocabulary (NCCL exchanges)
+        nid = [B.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(nid, src=0)
+        model = B.Model(cfg, max_pos, synthetic_seed=1234, rank=rank, world=world, nccl_id=nid[0])
+    else:
+        model = B.Model(cfg, max_pos, synthetic_seed=1234)
     t_create = time.perf_counter() - t0
     resident = model.device_bytes()
-    prompt = np.random.default_rng(rank).integers(0, d["vocab"], P).astype(np.int32)
+    prompt = np.random.default_rng(0).integers(0, d["vocab"], P).astype(np.int32)
     model.begin(prompt)
     launches_per_step = L.dsv4_cuda_model_step_kernels(model.h)
     stream = torch.cuda.Stream()
@@ -256,7 +263,7 @@ def run_decode(a):
     if dist:
         dist.barrier()
     ms_step = ms / K
-    value = world * K / (ms * 1e-3)
+    value = K / (ms * 1e-3)            # tokens of the one sequence all ranks decode
 
     # e2e through the host-driven entry (host token/pos in, host token out)
     tok = np.zeros(1, np.int32)
@@ -274,12 +281,13 @@ def run_decode(a):
     e2e_s = max_over_ranks(dist, e2e_s)
 
     peak, src = peaks()
+    peak *= world                      # the ranks' HBM together
     bytes_tok = np.mean([decode_bytes_per_token(d, P + W + i) for i in range(0, K, max(1, K // 16))])
     ach = bytes_tok / (ms_step * 1e-3) / 1e9
     out = {
         "metric": DECODE_METRIC,
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None,
         "dtype": "fp8 e4m3 / fp4 e2m1 / bf16 weights, f32 activations, f64 row sums",
         "data": "synthetic (random-init weights generated on device, random 512-token prompt)",
@@ -290,14 +298,18 @@ def run_decode(a):
                    "resident_gb": round(resident / 1e9, 1), "create_s": round(t_create, 1),
                    "l2": "no flush: each step streams %.1f GB of distinct weights (> 126 MB L2)"
                          % (bytes_tok / 1e9),
-                   "parallelism": ("replica per GPU, one stream each" if world > 1 else "single GPU")},
+                   "parallelism": ("one sequence sharded over %d GPUs: expert inter slices, q heads / "
+                                   "o_groups, wo_b columns, LM-head vocabulary; 2 NCCL all-reduces per "
+                                   "layer + 1 argmax all-gather per token" % world if world > 1
+                                   else "single GPU")},
         "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
-                     "frac": ach / peak, "peak_source": src + " burst hbm_gbs",
+                     "frac": ach / peak,
+                     "peak_source": src + " burst hbm_gbs" + (" x %d GPUs" % world if world > 1 else ""),
                      "scope": "whole decode token (one graph replay, %d kernels)" % launches_per_step,
                      "bytes_per_unit": bytes_tok, "traffic": TRAFFIC_DECODE},
         "gpu_launches": launches_per_step * K,
         "clocks": clk.summary(),
-        "e2e": {"value": world / e2e_s, "unit": "tok/s", "ms_per_step": e2e_s * 1e3,
+        "e2e": {"value": 1.0 / e2e_s, "unit": "tok/s", "ms_per_step": e2e_s * 1e3,
                 "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
                 "api": "dsv4_cuda_model_decode (host token, pos -> host next token), wall clock"},
     }
@@ -415,13 +427,14 @@ def run_gemv(a):
     out = {
         "metric": GEMV_METRIC,
         "value": value, "unit": "GB/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
-        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "e4m3 weights, f32 x, f64 accumulation", "data": "synthetic",
         "config": {"workload": "gemv_fp8 config 1", "rows": C1_ROWS, "cols": C1_COLS, "batch": 1,
                    "l2": "8 rotating resident weight copies (235 MB > 126 MB L2)",
                    "parallelism": "replica per GPU" if world > 1 else "single GPU"},
         "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
-                     "frac": ach / peak, "peak_source": src + " burst hbm_gbs",
+                     "frac": ach / peak,
+                     "peak_source": src + " burst hbm_gbs" + (" x %d GPUs" % world if world > 1 else ""),
                      "scope": "k_gemv_reg, one launch per step", "bytes_per_unit": C1_BYTES,
                      "traffic": TRAFFIC_C1},
         "gpu_launches": a.steps,

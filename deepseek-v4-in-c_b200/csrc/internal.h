@@ -55,6 +55,15 @@ int gemv(int fmt, float *y, long ystride, const float *x, long xstride, const vo
          int rows, int cols, int blk_r, int blk_c, int nt, cudaStream_t st, bool f16s = false);
 int dump_e4m3(float *dev_out, cudaStream_t st);
 
+// Multi-GPU exchange (comm.cu): NCCL opened at run time. comm is an NCCL
+// communicator or null (one GPU: every call is a no-op returning 0).
+size_t comm_id_bytes();
+int comm_unique_id(void *out);
+int comm_open(void **comm, int rank, int world, const void *id);
+void comm_close(void *comm);
+int comm_allreduce_sum(float *buf, size_t n, void *comm, cudaStream_t st);
+int comm_allgather(const void *send, void *recv, size_t bytes_per_rank, void *comm, cudaStream_t st);
+
 // The backend's own stream (NULL stream arguments of the device API).
 cudaStream_t stream_of(void *s);
 

@@ -55,6 +55,11 @@ struct dsv4b_model {
     unsigned *hc_cnt;
     dsv4b::MoeScratch ms;
     dsv4b::StepState *st;
+    // sharding: rank of world GPUs; comm is the NCCL communicator (null on one
+    // GPU); am_pair / am_gather hold the LM-head argmax exchange
+    int rank, world;
+    void *comm;
+    float *am_pair, *am_gather;
     int n_prompt;
     std::vector<void *> allocs;
     cudaStream_t stream;
@@ -191,6 +196,8 @@ static bool alloc_common(dsv4b_model *m)
     m->logits = F(c.vocab);
     m->xh = F(d);
     m->am_pv = F(1024);
+    m->am_pair = F(2);
+    m->am_gather = F(2 * 64);
     m->am_pi = (int *)dcopy(m, nullptr, 1024 * 4, &ok);
     m->idxs = (int *)dcopy(m, nullptr, (size_t)m->nidx * 4, &ok);
     m->isel = (int *)dcopy(m, nullptr, (size_t)(c.index_topk > 0 ? c.index_topk : 1) * 4, &ok);
@@ -344,7 +351,8 @@ static void hc_step(dsv4b_model *m, Pending &p, float *&hin, float *&hout, const
 static int enqueue_step(dsv4b_model *m, cudaStream_t st)
 {
     const DSV4Cfg &c = m->c;
-    const int hc = c.hc_mult, d = c.hidden, hd = c.head_dim, rd = c.qk_rope, H = c.n_heads;
+    // H: the heads of this rank (all of them on one GPU)
+    const int hc = c.hc_mult, d = c.hidden, hd = c.head_dim, rd = c.qk_rope, H = c.n_heads / m->world;
     const int win = c.sliding_window;
     int rc = 0;
     PdlChain chain;
@@ -429,13 +437,14 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
         rc |= sparse_attn(m->o, m->q, l.kv_cache, DSV4B_DT_F32, (long)l.kv_rows, l.sink, m->idxs, m->nidx, H, hd,
                           m->nidx, 1.0f / sqrtf((float)hd), 1, m->attn_part, st, &rope);
         // grouped low-rank output (dsv4_layer.c:303-335): the o_groups row
-        // slices of wo_a, each on its own slice of o, in one launch
+        // slices of wo_a, each on its own slice of o, in one launch (sharded:
+        // this rank's heads are exactly its groups' slices of o)
         {
-            const int gw = H * hd / c.o_groups, gr = c.o_lora;
+            const int gw = c.n_heads * hd / c.o_groups, gr = c.o_lora;
             const DevMat &wa = l.wo_a;
             const size_t rb = row_bytes(wa.wdt, wa.cols);
             Grp go;
-            for (int g = 0; g < c.o_groups; g++) {
+            for (int g = 0; g < c.o_groups / m->world; g++) {
                 DevMat sl = wa;
                 sl.w = wa.w + (size_t)g * gr * rb;
                 sl.s = wa.s ? wa.s + (size_t)(g * gr / wa.blk_r) * ((wa.cols + wa.blk_c - 1) / wa.blk_c) : nullptr;
@@ -446,6 +455,9 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
             rc |= grp_run(go, st);
         }
         rc |= G(l.wo_b, m->blk, m->ogrp, st);
+        // sharded: wo_b holds this rank's groups' columns, so blk is a partial
+        // sum over them
+        rc |= comm_allreduce_sum(m->blk, d, m->comm, st);
         // ---- FFN half: the residual is taken after attention (:511-522)
         pend = {1, nullptr};
         hc_step(m, pend, hin, hout, l.hcf_fn, l.hcf_base, l.hcf_scale, l.ffn_norm, false, m->x1, st);
@@ -455,8 +467,20 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
     // ---- head (src/cli/dsv4_run.c:467-474)
     hc_step(m, pend, hin, hout, m->hch_fn, m->hch_base, m->hch_scale, m->norm, true, m->xh, st);
     rc |= G(m->head, m->logits, m->xh, st);
-    launch(k_argmax_part, dim3(148), dim3(256), 0, st, m->am_pv, m->am_pi, m->logits, c.vocab);
-    launch(k_argmax_final, dim3(1), dim3(32), 0, st, m->st, m->out_tokens, m->am_pv, m->am_pi, 148, m->prompt, m->n_prompt);
+    launch(k_argmax_part, dim3(148), dim3(256), 0, st, m->am_pv, m->am_pi, m->logits, m->head.rows);
+    if (m->world == 1) {
+        launch(k_argmax_final, dim3(1), dim3(32), 0, st, m->st, m->out_tokens, m->am_pv, m->am_pi, 148, 1,
+               m->prompt, m->n_prompt);
+    } else {
+        // sharded head: each rank holds a contiguous vocabulary slice; the
+        // ranks' best (value, index) pairs are gathered and reduced the same
+        // way (larger value, ties to the lower index) on every rank
+        launch(k_argmax_pair, dim3(1), dim3(32), 0, st, m->am_pair, m->am_pv, m->am_pi, 148,
+               m->rank * m->head.rows);
+        rc |= comm_allgather(m->am_pair, m->am_gather, 8, m->comm, st);
+        launch(k_argmax_final, dim3(1), dim3(32), 0, st, m->st, m->out_tokens, m->am_gather,
+               reinterpret_cast<const int *>(m->am_gather) + 1, m->world, 2, m->prompt, m->n_prompt);
+    }
     if (cudaPeekAtLastError() != cudaSuccess) rc = -1;
     return rc ? -1 : 0;
 }
@@ -548,6 +572,7 @@ extern "C" void dsv4_cuda_model_free(dsv4b_model *m)
         cudaGraphExecDestroy(m->exec);
         cudaGraphDestroy(m->graph);
     }
+    comm_close(m->comm);                 // after the graph that holds its collectives
     for (void *p : m->allocs) cudaFree(p);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
@@ -561,6 +586,8 @@ static dsv4b_model *model_new(const DSV4Cfg *c, int max_pos)
         return nullptr;
     dsv4b_model *m = new dsv4b_model();
     m->c = *c;
+    m->rank = 0;
+    m->world = 1;
     for (int L = 0; L < c->n_layers; L++) m->ratios[L] = c->compress_ratios ? c->compress_ratios[L] : 0;
     m->c.compress_ratios = m->ratios;
     m->max_pos = max_pos;
@@ -673,35 +700,49 @@ namespace dsv4b {
 struct Synth {
     dsv4b_model *m;
     uint64_t seed, tensor = 0;
+    int rank = 0, world = 1;
     bool ok = true;
-    void *fill(size_t bytes, size_t n, int kind, float a, float b)
+    uint64_t next_key() { return (seed * 0x9E3779B97F4A7C15ull) ^ (++tensor * 0xD1B54A32D192ED03ull); }
+    void launched()
     {
+        if (cudaPeekAtLastError() != cudaSuccess) ok = false;
+    }
+    // the [nrows][ncols] slice at element base (row stride gstride) of the
+    // next tensor; a whole tensor is the slice at 0 of itself
+    void *slice(size_t bytes, int nrows, int ncols, int kind, float a, float b, size_t base, size_t gstride)
+    {
+        const uint64_t key = next_key();
         if (!ok) return nullptr;
         void *p = dalloc(m, bytes);
         if (!p) { ok = false; return nullptr; }
-        fillat(p, n, kind, a, b);
+        k_synth_slice<<<1184, 256, 0, m->stream>>>(p, nrows, ncols, kind, a, b, key, base, gstride);
+        launched();
         return p;
     }
-    void fillat(void *p, size_t n, int kind, float a, float b)
+    float *f32n(size_t n, float a, float b) { return (float *)slice(n * 4, 1, (int)n, 0, a, b, 0, n); }
+    float *f32u(size_t n, float a, float b) { return (float *)slice(n * 4, 1, (int)n, 1, a, b, 0, n); }
+    float *f32n_part(size_t n, size_t off, size_t cnt, float a, float b)
     {
-        const uint64_t key = (seed * 0x9E3779B97F4A7C15ull) ^ (++tensor * 0xD1B54A32D192ED03ull);
-        k_synth<<<1184, 256, 0, m->stream>>>(p, n, kind, a, b, key);
-        if (cudaPeekAtLastError() != cudaSuccess) ok = false;
+        return (float *)slice(cnt * 4, 1, (int)cnt, 0, a, b, off, n);
     }
-    float *f32n(size_t n, float a, float b) { return (float *)fill(n * 4, n, 0, a, b); }
-    float *f32u(size_t n, float a, float b) { return (float *)fill(n * 4, n, 1, a, b); }
-    DevMat fp8(int rows, int cols)
+    // FP8 128x128, codes of N(0, 0.02) at scale 2^-10: rows [r0, r0 + nr) and
+    // columns [c0, c0 + nc) of a rows x cols matrix (128-aligned slices)
+    DevMat fp8(int rows, int cols, int r0 = 0, int nr = -1, int c0 = 0, int nc = -1)
     {
-        DevMat d = {nullptr, nullptr, DSV4_WFP8, rows, cols, 128, 128};
-        const size_t sb = (size_t)((rows + 127) / 128) * ((cols + 127) / 128);
-        d.w = (const uint8_t *)fill((size_t)rows * cols, (size_t)rows * cols, 3, 0.f, 0.02f / 0.0009765625f);
-        d.s = (const uint8_t *)fill(sb, sb, 5, 117.f, 0.f);           // 2^-10
+        if (nr < 0) nr = rows;
+        if (nc < 0) nc = cols;
+        DevMat d = {nullptr, nullptr, DSV4_WFP8, nr, nc, 128, 128};
+        const size_t sb = (size_t)((nr + 127) / 128) * ((nc + 127) / 128);
+        d.w = (const uint8_t *)slice((size_t)nr * nc, nr, nc, 3, 0.f, 0.02f / 0.0009765625f,
+                                     (size_t)r0 * cols + c0, cols);
+        d.s = (const uint8_t *)slice(sb, 1, (int)sb, 5, 117.f, 0.f, 0, sb);      // 2^-10
         return d;
     }
-    DevMat bf16(int rows, int cols, float sigma)
+    DevMat bf16(int rows, int cols, float sigma, int r0 = 0, int nr = -1)
     {
-        DevMat d = {nullptr, nullptr, DSV4_WBF16, rows, cols, 0, 0};
-        d.w = (const uint8_t *)fill((size_t)rows * cols * 2, (size_t)rows * cols, 2, 0.f, sigma);
+        if (nr < 0) nr = rows;
+        DevMat d = {nullptr, nullptr, DSV4_WBF16, nr, cols, 0, 0};
+        d.w = (const uint8_t *)slice((size_t)nr * cols * 2, nr, cols, 2, 0.f, sigma, (size_t)r0 * cols, cols);
         return d;
     }
 };
@@ -712,18 +753,21 @@ static bool synth_layer(Synth &S, int Li)
     const DSV4Cfg &c = m->c;
     DevLayer &l = m->L[Li];
     const int d = c.hidden, hd = c.head_dim, hc = c.hc_mult, mix = (2 + hc) * hc, H = c.n_heads;
+    // this rank's share: heads (and so o_groups), the wo_b columns of those
+    // groups, every expert's inter slice
+    const int G = S.world, r = S.rank, Hl = H / G, ogl = c.o_groups / G, orl = ogl * c.o_lora;
     l.has_comp = l.ratio != 0;
     l.has_idx = l.ratio == 4;
     l.attn_norm = S.f32n(d, 1.f, 0.1f);
     l.ffn_norm = S.f32n(d, 1.f, 0.1f);
-    l.sink = S.f32n(H, 0.f, 1.f);
+    l.sink = S.f32n_part(H, (size_t)r * Hl, Hl, 0.f, 1.f);
     l.q_norm = S.f32n(c.q_lora, 1.f, 0.1f);
     l.kv_norm = S.f32n(hd, 1.f, 0.1f);
     l.wq_a = S.fp8(c.q_lora, d);
-    l.wq_b = S.fp8(H * hd, c.q_lora);
+    l.wq_b = S.fp8(H * hd, c.q_lora, r * Hl * hd, Hl * hd);
     l.wkv = S.fp8(hd, d);
-    l.wo_a = S.fp8(c.o_groups * c.o_lora, H * hd / c.o_groups);
-    l.wo_b = S.fp8(d, c.o_groups * c.o_lora);
+    l.wo_a = S.fp8(c.o_groups * c.o_lora, H * hd / c.o_groups, r * orl, orl);
+    l.wo_b = S.fp8(d, c.o_groups * c.o_lora, 0, d, r * orl, orl);
     if (l.has_comp) {
         l.ape = S.f32n((size_t)l.ratio * l.coff * hd, 0.f, 0.1f);
         l.cnorm = S.f32n(hd, 1.f, 0.1f);
@@ -753,13 +797,19 @@ static bool synth_layer(Synth &S, int Li)
         mo.tid2eid = nullptr;
         mo.bias = S.f32n(c.n_experts, 0.f, 0.05f);
     }
-    // routed experts: one block per layer, codes of every expert then scales
-    const size_t I = c.moe_inter, E = c.n_experts;
+    // routed experts: one stream of codes per layer (every expert's w1, w3,
+    // w2), then the scales; this rank keeps its inter slice of each expert
+    const size_t I = c.moe_inter / G, E = c.n_experts;
     const size_t cw = I * d / 2, cper = 3 * cw, sw = I * d / 32, sper = 3 * sw;
     uint8_t *codes = (uint8_t *)dalloc(m, E * cper), *scales = (uint8_t *)dalloc(m, E * sper);
     if (!codes || !scales) return false;
-    S.fillat(codes, E * cper, 4, 0.f, 0.02f / 0.015625f);       // e2m1 of N(0,0.02) / 2^-6
-    S.fillat(scales, E * sper, 5, 121.f, 0.f);                  // 2^-6
+    const uint64_t ckey = S.next_key();
+    k_synth_experts<<<1184, 256, 0, m->stream>>>(codes, (int)E, d, c.moe_inter, r, G, 0.02f / 0.015625f,
+                                                   ckey);                    // e2m1 of N(0,0.02) / 2^-6
+    S.launched();
+    S.next_key();
+    k_synth_slice<<<1184, 256, 0, m->stream>>>(scales, 1, (int)(E * sper), 5, 121.f, 0.f, 0, 0, E * sper);
+    S.launched();                                                            // 2^-6
     std::vector<const uint8_t *> tab(6 * E);
     for (size_t e = 0; e < E; e++) {
         for (int j = 0; j < 3; j++) {
@@ -775,16 +825,17 @@ static bool synth_layer(Synth &S, int Li)
     mo.w2tab = t + 4 * E; mo.s2tab = t + 5 * E;
     mo.efmt = DSV4_WFP4; mo.eblk_r = 1; mo.eblk_c = 32;
     mo.ef16s = 1;                                               // every scale is 2^-6
-    const int Is = c.moe_inter * c.n_shared;
-    mo.sh[0] = S.fp8(Is, d);
-    mo.sh[1] = S.fp8(Is, d);
-    mo.sh[2] = S.fp8(d, Is);
+    const int Is = c.moe_inter * c.n_shared, Isl = Is / G;
+    mo.sh[0] = S.fp8(Is, d, r * Isl, Isl);
+    mo.sh[1] = S.fp8(Is, d, r * Isl, Isl);
+    mo.sh[2] = S.fp8(d, Is, 0, d, r * Isl, Isl);
     mo.has_shared = 1;
     mo.n_experts = c.n_experts;
     mo.topk = c.topk;
     mo.hidden = d;
-    mo.inter = c.moe_inter;
-    mo.inter_shared = Is;
+    mo.inter = (int)I;
+    mo.inter_shared = Isl;
+    mo.comm = m->comm;
     mo.score_func = c.scoring_func == DSV4_SCORE_SIGMOID ? 2 : 1;
     mo.route_scale = c.routed_scale;
     mo.swiglu_limit = c.swiglu_limit;
@@ -793,20 +844,58 @@ static bool synth_layer(Synth &S, int Li)
 
 }  // namespace dsv4b
 
-extern "C" dsv4b_model *dsv4_cuda_model_create_synthetic(const DSV4Cfg *c, int max_pos, unsigned long long seed)
+// Whether a model of this configuration splits over `world` GPUs: heads and
+// o_groups by rank (a rank's heads are its groups' slices of o), wo_a / wo_b
+// slices on 128-row / -column FP8 blocks, every expert's inter slice a whole
+// number of 32-column FP4 scale blocks, the shared expert's on 128 blocks,
+// and the vocabulary.
+extern "C" int dsv4b_shard_check(const DSV4Cfg *c, int world)
 {
+    if (!c || world < 1 || world > 64) return -1;
+    if (world == 1) return 0;
+    const int ogl = c->o_groups / world, orl = ogl * c->o_lora, Hl = c->n_heads / world;
+    const int il = c->moe_inter / world, isl = c->moe_inter * c->n_shared / world;
+    const bool ok = c->n_heads % world == 0 && c->o_groups % world == 0 && c->n_heads % c->o_groups == 0 &&
+                    (Hl * c->head_dim) % 128 == 0 && orl % 128 == 0 && c->moe_inter % world == 0 && il % 32 == 0 &&
+                    (c->moe_inter * c->n_shared) % world == 0 && isl % 128 == 0 && c->vocab % world == 0 &&
+                    c->n_shared >= 1;
+    return ok ? 0 : -1;
+}
+
+extern "C" size_t dsv4b_nccl_id_bytes(void) { return comm_id_bytes(); }
+
+extern "C" int dsv4b_nccl_unique_id(void *out) { return comm_unique_id(out); }
+
+// A synthetic model, or this rank's share of one: the tensors of rank r are
+// exactly the corresponding slices of the single-GPU model of the same seed.
+extern "C" dsv4b_model *dsv4_cuda_model_create_synthetic_sharded(const DSV4Cfg *c, int max_pos,
+                                                                unsigned long long seed, int rank, int world,
+                                                                const void *nccl_id)
+{
+    if (!c || dsv4b_shard_check(c, world) != 0 || rank < 0 || rank >= world || (world > 1 && !nccl_id)) {
+        fprintf(stderr, "dsv4_b200: configuration does not split over %d GPUs (or bad rank %d)\n", world, rank);
+        return nullptr;
+    }
     dsv4b_model *m = model_new(c, max_pos);
     if (!m) return nullptr;
+    m->rank = rank;
+    m->world = world;
+    if (comm_open(&m->comm, rank, world, nccl_id) != 0) {
+        dsv4_cuda_model_free(m);
+        return nullptr;
+    }
     dsv4b::Synth S;
     S.m = m;
     S.seed = seed;
+    S.rank = rank;
+    S.world = world;
     bool ok = true;
     for (int L = 0; L < c->n_layers && ok; L++) ok = dsv4b::synth_layer(S, L);
-    const int d = c->hidden, hc = c->hc_mult;
+    const int d = c->hidden, hc = c->hc_mult, vl = c->vocab / world;
     if (ok) {
         m->emb_wdt = DSV4_WBF16;
         m->embed = S.bf16(c->vocab, d, 1.0f).w;
-        m->head = S.bf16(c->vocab, d, 0.02f);
+        m->head = S.bf16(c->vocab, d, 0.02f, rank * vl, vl);
         m->norm = S.f32n(d, 1.f, 0.1f);
         m->hch_fn = S.f32n((size_t)hc * hc * d, 0.f, 0.02f);
         m->hch_base = S.f32n(hc, 0.f, 0.5f);
@@ -820,6 +909,11 @@ extern "C" dsv4b_model *dsv4_cuda_model_create_synthetic(const DSV4Cfg *c, int m
         return nullptr;
     }
     return m;
+}
+
+extern "C" dsv4b_model *dsv4_cuda_model_create_synthetic(const DSV4Cfg *c, int max_pos, unsigned long long seed)
+{
+    return dsv4_cuda_model_create_synthetic_sharded(c, max_pos, seed, 0, 1, nullptr);
 }
 
 extern "C" int dsv4_cuda_model_decode(dsv4b_model *m, int token, int pos, int *next_token)

@@ -62,9 +62,14 @@ __global__ void k_build_idxs(int *idxs, int nmax, const StepState *st, int win, 
                              const int *dyn, const int *sel);
 __global__ void k_argmax_part(float *pv, int *pi, const float *x, int n);
 __global__ void k_argmax_final(StepState *st, int *out_tokens, const float *pv, const int *pi, int nparts,
-                               const int *prompt, int n_prompt);
+                               int stride, const int *prompt, int n_prompt);
+__global__ void k_argmax_pair(float *pair, const float *pv, const int *pi, int nparts, int offset);
 
 __global__ void k_synth(void *dst, size_t n, int kind, float a, float b, uint64_t key);
+__global__ void k_synth_slice(void *dst, int nrows, int ncols, int kind, float a, float b, uint64_t key,
+                              size_t base, size_t gstride);
+__global__ void k_synth_experts(uint8_t *dst, int n_experts, int hidden, int inter, int rank, int world, float b,
+                                uint64_t key);
 __global__ void k_synth_tid2eid(int64_t *t, int vocab, int topk, int n_experts, uint64_t key);
 
 }  // namespace dsv4b

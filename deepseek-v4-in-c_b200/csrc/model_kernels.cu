@@ -652,19 +652,17 @@ __global__ void k_argmax_part(float *pv, int *pi, const float *x, int n)
     }
 }
 
-__global__ void k_argmax_final(StepState *st, int *out_tokens, const float *pv, const int *pi, int nparts,
-                               const int *prompt, int n_prompt)
+// The best (value, index) of pv[i * stride], pi[i * stride], i < nparts, by
+// one warp: each lane the best of its strided share, then the same comparison
+// (larger value, ties to the lower index) across lanes.
+__device__ __forceinline__ void argmax_warp(float &bv, int &bi, const float *pv, const int *pi, int nparts,
+                                            int stride)
 {
-    pdl_trigger();
-    pdl_wait();
-    if (threadIdx.x >= 32) return;
-    // one warp: each lane the best of its strided share, then the same
-    // comparison (larger value, ties to the lower index) across lanes
-    float bv = -INFINITY;
-    int bi = -1;
+    bv = -INFINITY;
+    bi = -1;
     for (int i = threadIdx.x; i < nparts; i += 32) {
-        const float v = ld_act(pv + i);
-        const int ix = __ldcg(pi + i);
+        const float v = ld_act(pv + (size_t)i * stride);
+        const int ix = __ldcg(pi + (size_t)i * stride);
         if (ix >= 0 && (bi < 0 || v > bv || (v == bv && ix < bi))) { bv = v; bi = ix; }
     }
     for (int o = 16; o > 0; o >>= 1) {
@@ -672,12 +670,39 @@ __global__ void k_argmax_final(StepState *st, int *out_tokens, const float *pv, 
         const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
         if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
     }
+}
+
+__global__ void k_argmax_final(StepState *st, int *out_tokens, const float *pv, const int *pi, int nparts,
+                               int stride, const int *prompt, int n_prompt)
+{
+    pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x >= 32) return;
+    float bv;
+    int bi;
+    argmax_warp(bv, bi, pv, pi, nparts, stride);
     if (threadIdx.x != 0) return;
     const int pos = st->pos;
     out_tokens[pos] = bi;
     const int next = pos + 1;
     st->token = (next < n_prompt) ? prompt[next] : bi;
     st->pos = next;
+}
+
+// A rank's best pair of its vocabulary slice, the index made global:
+// pair = {value, index bits}.
+__global__ void k_argmax_pair(float *pair, const float *pv, const int *pi, int nparts, int offset)
+{
+    pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x >= 32) return;
+    float bv;
+    int bi;
+    argmax_warp(bv, bi, pv, pi, nparts, 1);
+    if (threadIdx.x == 0) {
+        pair[0] = bv;
+        pair[1] = __int_as_float(bi >= 0 ? bi + offset : -1);
+    }
 }
 
 }  // namespace dsv4b

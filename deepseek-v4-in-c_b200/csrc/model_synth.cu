@@ -77,6 +77,60 @@ __global__ void k_synth(void *dst, size_t n, int kind, float a, float b, uint64_
     }
 }
 
+// A slice of a synthetic tensor, identical to the same elements of the whole
+// one: element (i, j) of the [nrows][ncols] slice is element
+// base + i * gstride + j of the tensor's stream (kinds 0..3 and 5 of k_synth).
+__global__ void k_synth_slice(void *dst, int nrows, int ncols, int kind, float a, float b, uint64_t key,
+                              size_t base, size_t gstride)
+{
+    const size_t n = (size_t)nrows * ncols;
+    for (size_t li = blockIdx.x * (size_t)blockDim.x + threadIdx.x; li < n; li += (size_t)gridDim.x * blockDim.x) {
+        const size_t i = li / ncols, j = li - i * ncols, gi = base + i * gstride + j;
+        switch (kind) {
+        case 0: reinterpret_cast<float *>(dst)[li] = a + b * nrand(key, gi); break;
+        case 1: reinterpret_cast<float *>(dst)[li] = a + b * urand(key, gi); break;
+        case 2: {
+            const float v = b * nrand(key, gi);
+            reinterpret_cast<uint16_t *>(dst)[li] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+            break;
+        }
+        case 3: {
+            const float v = b * nrand(key, gi);
+            reinterpret_cast<uint8_t *>(dst)[li] = (uint8_t)__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+            break;
+        }
+        default: reinterpret_cast<uint8_t *>(dst)[li] = (uint8_t)a; break;
+        }
+    }
+}
+
+// The routed experts' e2m1 codes of one layer for rank `rank` of `world`:
+// the whole layer is one stream of packed bytes, expert e at e * cper, its
+// w1, w3 ([inter][hidden / 2] bytes) and w2 ([hidden][inter / 2]) one after
+// the other. A rank keeps rows [r I / G, (r + 1) I / G) of w1 and w3 and the
+// same columns of w2, stored as one compact block per expert:
+// [w1 slice][w3 slice][w2 slice].
+__global__ void k_synth_experts(uint8_t *dst, int n_experts, int hidden, int inter, int rank, int world, float b,
+                                uint64_t key)
+{
+    const size_t il = inter / world, cw = (size_t)inter * hidden / 2, cper = 3 * cw;
+    const size_t cwl = il * hidden / 2, cperl = 3 * cwl, n = (size_t)n_experts * cperl;
+    const size_t w2rb = inter / 2, w2rbl = il / 2;
+    for (size_t lb = blockIdx.x * (size_t)blockDim.x + threadIdx.x; lb < n; lb += (size_t)gridDim.x * blockDim.x) {
+        const size_t e = lb / cperl, rem = lb - e * cperl;
+        size_t gb;
+        if (rem < 2 * cwl) {
+            const size_t jm = rem / cwl, off = rem - jm * cwl, row = off / (hidden / 2), cb = off - row * (hidden / 2);
+            gb = e * cper + jm * cw + (rank * il + row) * (hidden / 2) + cb;
+        } else {
+            const size_t off = rem - 2 * cwl, row = off / w2rbl, cb = off - row * w2rbl;
+            gb = e * cper + 2 * cw + row * w2rb + rank * w2rbl + cb;
+        }
+        const float2 v = make_float2(b * nrand(key, 2 * gb), b * nrand(key, 2 * gb + 1));
+        dst[lb] = (uint8_t)__nv_cvt_float2_to_fp4x2(v, __NV_E2M1, cudaRoundNearest);
+    }
+}
+
 __global__ void k_synth_tid2eid(int64_t *t, int vocab, int topk, int n_experts, uint64_t key)
 {
     for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < vocab; v += gridDim.x * blockDim.x) {

@@ -144,6 +144,9 @@ int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float 
         n++;
     }
     if (gemv_group(it, n, st)) return -1;
+    // sharded: every rank holds a slice of each expert's inter dimension, so
+    // its outputs are partial sums over that slice; add them up across ranks
+    if (comm_allreduce_sum(S.acc, (size_t)(K + (Is ? 1 : 0)) * H, L.comm, st)) return -1;
     if (combine)
         launch(k_combine, dim3((H + 255) / 256), dim3(256), 0, st, out, S.acc, S.wts, K, H, Is ? accs : nullptr);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;

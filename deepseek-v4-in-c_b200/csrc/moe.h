@@ -32,6 +32,10 @@ struct MoeLayer {
     int has_shared;
     int n_experts, topk, hidden, inter, inter_shared, score_func;
     float route_scale, swiglu_limit;
+    // sharded over GPUs: every expert's inter slice is local (inter and
+    // inter_shared are the local sizes), and the per-slot outputs are summed
+    // across ranks by an all-reduce on comm before the combine; null on one GPU
+    void *comm;
 };
 
 struct MoeScratch {

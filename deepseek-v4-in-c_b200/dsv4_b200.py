@@ -84,6 +84,10 @@ def _declare(L):
         "dsv4_cuda_model_create_synthetic": ([vp, i, C.c_ulonglong], vp),
         "dsv4_cuda_model_bytes": ([vp], sz),
         "dsv4_cuda_model_step_kernels": ([vp], i),
+        "dsv4b_shard_check": ([vp, i], i),
+        "dsv4b_nccl_id_bytes": ([], sz),
+        "dsv4b_nccl_unique_id": ([vp], i),
+        "dsv4_cuda_model_create_synthetic_sharded": ([vp, i, C.c_ulonglong, i, i, vp], vp),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -316,20 +320,41 @@ def sparse_attn_dev(o, q, kv, kv_dt, seq_kv_rows, sink, idxs, n_heads, d, topk_n
 
 # ------------------------------------------------------------- whole model
 
+def nccl_unique_id():
+    """A new communicator id (bytes) for a sharded model; rank 0 makes it and
+    every rank passes the same bytes to Model(..., nccl_id=...)."""
+    buf = C.create_string_buffer(lib().dsv4b_nccl_id_bytes())
+    check(lib().dsv4b_nccl_unique_id(buf), "dsv4b_nccl_unique_id")
+    return buf.raw
+
+
+def shard_check(cfg, world):
+    """True when a model of ctypes config cfg splits over world GPUs."""
+    return lib().dsv4b_shard_check(C.addressof(cfg), int(world)) == 0
+
+
 class Model:
     """A whole model resident on the device (dsv4_cuda_model_create) from a
-    dsv4_model.SyntheticModel or any holder of cfg/mw/layers/experts structs."""
+    dsv4_model.SyntheticModel or any holder of cfg/mw/layers/experts structs.
+    With world > 1 (synthetic only), this rank's share of a model sharded over
+    world GPUs (one process per GPU, all stepping in lockstep)."""
 
-    def __init__(self, sm, max_pos, synthetic_seed=None):
+    def __init__(self, sm, max_pos, synthetic_seed=None, rank=0, world=1, nccl_id=None):
         """sm: a dsv4_model.SyntheticModel (host weights), or with
         synthetic_seed set, any holder of .cfg/.d for an on-device model."""
         self.sm, self.max_pos = sm, max_pos
         self.vocab = sm.d["vocab"]
         if synthetic_seed is None:
+            if world != 1:
+                raise ValueError("sharded models are synthetic (synthetic_seed)")
             self.h = lib().dsv4_cuda_model_create(C.addressof(sm.cfg), C.addressof(sm.mw),
                                                   C.addressof(sm.layers), C.addressof(sm.experts), max_pos)
-        else:
+        elif world == 1:
             self.h = lib().dsv4_cuda_model_create_synthetic(C.addressof(sm.cfg), max_pos, synthetic_seed)
+        else:
+            idb = C.create_string_buffer(bytes(nccl_id), len(nccl_id))
+            self.h = lib().dsv4_cuda_model_create_synthetic_sharded(C.addressof(sm.cfg), max_pos, synthetic_seed,
+                                                                    int(rank), int(world), idb)
         if not self.h:
             raise RuntimeError("model creation failed")
 

@@ -174,6 +174,34 @@ int dsv4_cuda_model_decode(dsv4b_model *m, int token, int pos, int *next_token);
 dsv4b_model *dsv4_cuda_model_create_synthetic(const DSV4Cfg *c, int max_pos,
                                               unsigned long long seed);
 
+/* ---- multi-GPU decode (one process per GPU). No reference counterpart: the
+ * reference runs on one device (dsv4_cuda.cu:243-249); this is the sharding
+ * its design notes ask for -- routed and shared experts split along their
+ * inter dimension on every rank, q heads (and with them wo_a's o_groups) by
+ * rank, wo_b by the matching columns, the LM head by vocabulary -- with two
+ * NCCL sum all-reduces per layer (the wo_b output, the experts' per-slot
+ * outputs before the k-ordered combine) and one all-gather of the ranks'
+ * argmax pairs per token. Every rank runs the same steps in lockstep. */
+
+/* 0 if configuration c splits over world GPUs (heads, o_groups, wo_a / wo_b
+ * 128-blocks, expert inter slices of whole 32-column FP4 scale blocks, the
+ * shared expert's of 128 blocks, the vocabulary), else -1. No device needed. */
+int dsv4b_shard_check(const DSV4Cfg *c, int world);
+
+/* Size of the communicator id rank 0 creates and every rank passes to
+ * dsv4_cuda_model_create_synthetic_sharded (NCCL's unique id, 128 bytes), and
+ * its creation. NCCL is opened at run time; -1 when it cannot be. */
+size_t dsv4b_nccl_id_bytes(void);
+int dsv4b_nccl_unique_id(void *out);
+
+/* This rank's share of the synthetic model of seed: every tensor is exactly
+ * the corresponding slice of dsv4_cuda_model_create_synthetic's. Binds the
+ * device first (dsv4_cuda_init, DSV4_DEVICE); nccl_id may be NULL for world 1.
+ * NULL if c does not split over world or the model does not fit. */
+dsv4b_model *dsv4_cuda_model_create_synthetic_sharded(const DSV4Cfg *c, int max_pos,
+                                                      unsigned long long seed, int rank,
+                                                      int world, const void *nccl_id);
+
 /* Device memory in use (bytes), for reporting the resident model size. */
 size_t dsv4_cuda_model_bytes(const dsv4b_model *m);
 

@@ -57,3 +57,19 @@ def test_decode_bytes_model():
     head = d["vocab"] * d["hidden"] * 2
     experts = len(bench.layer_ratios(d)) * d["topk"] * 13369344
     assert b > head + experts
+
+
+def test_shard_check_flash():
+    """The Flash geometry splits over 1, 2, 4 and 8 GPUs (heads, o_groups,
+    wo_a / wo_b FP8 blocks, expert inter slices, vocabulary); a head count
+    that does not divide does not."""
+    import dsv4_b200 as B
+    import dsv4_model as M
+    d = M.flash_config()
+    cfg = M.ConfigOnly(d).cfg
+    for g in (1, 2, 4, 8):
+        assert B.shard_check(cfg, g), g
+    assert not B.shard_check(cfg, 3)
+    assert not B.shard_check(cfg, 16)        # o_groups 8 cannot go over 16 ranks
+    d2 = dict(d, n_heads=60)
+    assert not B.shard_check(M.ConfigOnly(d2).cfg, 8)

@@ -318,6 +318,8 @@ def run_decode(a):
         out["cpu_baseline"] = {"value": 1.0 / s_tok, "unit": "tok/s",
                                "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count())),
                                "kind": "reference", "sample": desc}
+    if world > 1 and L.dsv4b_model_comm_status(model.h) != 0:
+        out["comm_error"] = "a peer exchange timed out waiting for a rank: results invalid"
     if rank == 0:
         print(json.dumps(out))
     model.close()

@@ -14,6 +14,9 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <vector>
+
+#include "common.cuh"
 #include "internal.h"
 
 namespace dsv4b {
@@ -106,6 +109,198 @@ int comm_allgather(const void *send, void *recv, size_t bytes_per_rank, void *co
     t_pdl = false;
     return check(N.all_gather(send, recv, bytes_per_rank, ncclUint8, static_cast<ncclComm_t>(comm), st),
                  "ncclAllGather");
+}
+
+}  // namespace dsv4b
+
+// ------------------------------------------------- one-shot peer exchange
+// A sum all-reduce of a small f32 vector over NVLink peer memory, in one
+// kernel and without flags or fences: every rank owns a mailbox in its own
+// HBM ([3 buffers][world][maxn] words), mapped into every other rank by CUDA
+// IPC, whose empty words hold the sentinel -0.0 (0x80000000). An exchange
+// stores this rank's values (a -0.0 sent as +0.0, the same number) into slot
+// `rank` of buffer b of every mailbox; each thread then polls its words of
+// its own mailbox (volatile loads, bounded) until no rank's word is the
+// sentinel, sums them in rank order -- the same order on every rank, so all
+// ranks get the same bits -- and re-arms the words with the sentinel. Aligned
+// 4-byte stores arrive whole, so a word is either empty or final. The buffer
+// of exchange x (x = step * exchanges per step + call, the step count kept on
+// the device) is x mod 3: a rank writes buffer b again only after two more
+// exchanges, which need every rank to have finished (and re-armed) this one.
+namespace dsv4b {
+
+namespace {
+
+constexpr unsigned kSentinel = 0x80000000u;
+constexpr unsigned kSpinLimit = 1u << 26;     // several seconds: a peer that never arrives
+
+struct PeerDev {
+    float *const *pmail;       // [world] every rank's mailbox
+    float *mail;               // mine
+    int *err;
+    int rank, world, maxn;
+};
+
+struct PeerHost {
+    PeerDev d;
+    void *base;                // my mailbox
+    void *misc;                // err, the pointer table
+    std::vector<void *> opened;
+};
+
+__global__ void k_fill_u32(unsigned *p, size_t n, unsigned v)
+{
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) p[i] = v;
+}
+
+__device__ __forceinline__ uint4 ld_volatile_u4(const void *p)
+{
+    uint4 r;
+    asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p) : "memory");
+    return r;
+}
+
+__device__ __forceinline__ unsigned unsent(float v)
+{
+    const unsigned u = __float_as_uint(v);
+    return u == kSentinel ? 0u : u;
+}
+
+__global__ void __launch_bounds__(256) k_peer_allreduce(PeerDev x, float *buf, int n, const unsigned *stepseq,
+                                                        int nx, int call)
+{
+    pdl_trigger();
+    pdl_wait();
+    const int G = x.world, n4 = n >> 2;
+    const unsigned xi = __ldcg(stepseq) * (unsigned)nx + (unsigned)call;
+    const size_t slot = (size_t)x.maxn, bsz = (size_t)G * slot, b = xi % 3u;
+    const int stride = gridDim.x * blockDim.x, i0 = blockIdx.x * blockDim.x + threadIdx.x;
+    const float4 *b4 = reinterpret_cast<const float4 *>(buf);
+    for (int i = i0; i < n4; i += stride) {
+        const float4 v = __ldcg(b4 + i);
+        const uint4 u = make_uint4(unsent(v.x), unsent(v.y), unsent(v.z), unsent(v.w));
+        for (int r = 0; r < G; r++)
+            reinterpret_cast<uint4 *>(x.pmail[r] + b * bsz + (size_t)x.rank * slot)[i] = u;
+    }
+    unsigned spins = 0;
+    bool gave_up = false;
+    for (int i = i0; i < n4; i += stride) {
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < G; r++) {
+            uint4 *w = reinterpret_cast<uint4 *>(x.mail + b * bsz + (size_t)r * slot) + i;
+            uint4 u = ld_volatile_u4(w);
+            while ((u.x == kSentinel || u.y == kSentinel || u.z == kSentinel || u.w == kSentinel) && !gave_up) {
+                if (++spins > kSpinLimit) {
+                    gave_up = true;
+                    atomicExch(x.err, 1);
+                    break;
+                }
+                u = ld_volatile_u4(w);
+            }
+            const float4 v = make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z),
+                                         __uint_as_float(u.w));
+            s = r == 0 ? v
+                       : make_float4(__fadd_rn(s.x, v.x), __fadd_rn(s.y, v.y), __fadd_rn(s.z, v.z), __fadd_rn(s.w, v.w));
+            *w = make_uint4(kSentinel, kSentinel, kSentinel, kSentinel);
+        }
+        reinterpret_cast<float4 *>(buf)[i] = s;
+    }
+}
+
+}  // namespace
+
+int peer_open(void **out, int rank, int world, int maxn, void *comm, cudaStream_t st)
+{
+    *out = nullptr;
+    if (world < 2 || !comm || maxn % 4) return -1;
+    PeerHost *h = new PeerHost();
+    h->d.rank = rank;
+    h->d.world = world;
+    h->d.maxn = maxn;
+    const size_t words = (size_t)3 * world * maxn;
+    bool ok = cudaMalloc(&h->base, words * 4) == cudaSuccess && cudaMalloc(&h->misc, 4096) == cudaSuccess &&
+              cudaMemset(h->misc, 0, 4096) == cudaSuccess;
+    if (ok) {
+        k_fill_u32<<<256, 256, 0, st>>>(static_cast<unsigned *>(h->base), words, kSentinel);
+        ok = cudaStreamSynchronize(st) == cudaSuccess;
+    }
+    cudaIpcMemHandle_t mine;
+    if (ok) ok = cudaIpcGetMemHandle(&mine, h->base) == cudaSuccess;
+    // every rank's handle, gathered through NCCL (which also orders every
+    // rank's sentinel fill before any exchange)
+    std::vector<cudaIpcMemHandle_t> all(world);
+    void *dh = nullptr;
+    if (ok) ok = cudaMalloc(&dh, sizeof(cudaIpcMemHandle_t) * (world + 1)) == cudaSuccess;
+    if (ok) {
+        char *d = static_cast<char *>(dh);
+        ok = cudaMemcpy(d + sizeof(cudaIpcMemHandle_t) * world, &mine, sizeof mine, cudaMemcpyHostToDevice) ==
+                 cudaSuccess &&
+             comm_allgather(d + sizeof(cudaIpcMemHandle_t) * world, d, sizeof mine, comm, st) == 0 &&
+             cudaStreamSynchronize(st) == cudaSuccess &&
+             cudaMemcpy(all.data(), d, sizeof(cudaIpcMemHandle_t) * world, cudaMemcpyDeviceToHost) == cudaSuccess;
+    }
+    if (dh) cudaFree(dh);
+    std::vector<float *> pm(world);
+    for (int r = 0; ok && r < world; r++) {
+        void *p = h->base;
+        if (r != rank) {
+            ok = cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+            if (ok) h->opened.push_back(p);
+        }
+        pm[r] = static_cast<float *>(p);
+    }
+    if (ok) {
+        char *m = static_cast<char *>(h->misc);
+        h->d.err = reinterpret_cast<int *>(m);
+        float **tm = reinterpret_cast<float **>(m + 64);
+        ok = 64 + 8 * world <= 4096 && cudaMemcpy(tm, pm.data(), 8 * world, cudaMemcpyHostToDevice) == cudaSuccess;
+        h->d.pmail = tm;
+        h->d.mail = static_cast<float *>(h->base);
+    }
+    if (!ok) {
+        fprintf(stderr, "dsv4_b200: peer exchange unavailable (%s); using NCCL\n",
+                cudaGetErrorString(cudaGetLastError()));
+        peer_close(h);
+        return -1;
+    }
+    *out = h;
+    return 0;
+}
+
+void peer_close(void *p)
+{
+    PeerHost *h = static_cast<PeerHost *>(p);
+    if (!h) return;
+    for (void *q : h->opened) cudaIpcCloseMemHandle(q);
+    if (h->base) cudaFree(h->base);
+    if (h->misc) cudaFree(h->misc);
+    delete h;
+}
+
+int peer_allreduce_sum(void *p, float *buf, int n, const unsigned *stepseq, int nx, int call, cudaStream_t st)
+{
+    PeerHost *h = static_cast<PeerHost *>(p);
+    if (!h || n > h->d.maxn || (n & 3) || ((uintptr_t)buf & 15) || !stepseq) return -1;
+    const int blocks = 16;
+    return launch(k_peer_allreduce, dim3(blocks), dim3(256), 0, st, h->d, buf, n, stepseq, nx, call) == cudaSuccess
+               ? 0
+               : -1;
+}
+
+int xreduce_sum(const Exch &x, float *buf, size_t n, cudaStream_t st)
+{
+    if (x.peer) return peer_allreduce_sum(x.peer, buf, (int)n, x.stepseq, x.nx, (*x.call)++, st);
+    return comm_allreduce_sum(buf, n, x.comm, st);
+}
+
+int peer_status(void *p)
+{
+    PeerHost *h = static_cast<PeerHost *>(p);
+    if (!h) return 0;
+    int e = 0;
+    if (cudaMemcpy(&e, h->d.err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    return e;
 }
 
 }  // namespace dsv4b

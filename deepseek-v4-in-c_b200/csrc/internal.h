@@ -63,6 +63,24 @@ int comm_open(void **comm, int rank, int world, const void *id);
 void comm_close(void *comm);
 int comm_allreduce_sum(float *buf, size_t n, void *comm, cudaStream_t st);
 int comm_allgather(const void *send, void *recv, size_t bytes_per_rank, void *comm, cudaStream_t st);
+// One-shot sum all-reduce over NVLink peer memory (CUDA IPC mailboxes, one
+// kernel, bounded waits): opened once per model over an NCCL communicator;
+// n <= maxn floats, a multiple of 4; exchange `call` of a step of nx
+// exchanges, the step count at *stepseq. peer_status: 0, or 1 once a wait
+// timed out.
+int peer_open(void **peer, int rank, int world, int maxn, void *comm, cudaStream_t st);
+void peer_close(void *peer);
+int peer_allreduce_sum(void *peer, float *buf, int n, const unsigned *stepseq, int nx, int call, cudaStream_t st);
+int peer_status(void *peer);
+// Where a sharded step's sums go: the peer exchange when open, else NCCL (or
+// nothing on one GPU). *call counts the step's exchanges as they are enqueued.
+struct Exch {
+    void *peer, *comm;
+    const unsigned *stepseq;
+    int nx;
+    int *call;
+};
+int xreduce_sum(const Exch &x, float *buf, size_t n, cudaStream_t st);
 
 // The backend's own stream (NULL stream arguments of the device API).
 cudaStream_t stream_of(void *s);

@@ -58,7 +58,9 @@ struct dsv4b_model {
     // sharding: rank of world GPUs; comm is the NCCL communicator (null on one
     // GPU); am_pair / am_gather hold the LM-head argmax exchange
     int rank, world;
-    void *comm;
+    void *comm, *peer;
+    unsigned *stepseq;         // steps done (device; advanced by the last kernel)
+    int nx, xcall;             // exchanges per step; the next one's index
     float *am_pair, *am_gather;
     int n_prompt;
     std::vector<void *> allocs;
@@ -197,6 +199,9 @@ static bool alloc_common(dsv4b_model *m)
     m->xh = F(d);
     m->am_pv = F(1024);
     m->am_pair = F(2);
+    m->stepseq = (unsigned *)dcopy(m, nullptr, 4, &ok);
+    if (ok && cudaMemset(m->stepseq, 0, 4) != cudaSuccess) ok = false;
+    m->nx = 2 * c.n_layers;
     m->am_gather = F(2 * 64);
     m->am_pi = (int *)dcopy(m, nullptr, 1024 * 4, &ok);
     m->idxs = (int *)dcopy(m, nullptr, (size_t)m->nidx * 4, &ok);
@@ -359,6 +364,8 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
     float *hin = m->h, *hout = m->resid;
     Pending pend = {0, nullptr};
     const bool fused = hc_fused(c);
+    m->xcall = 0;
+    const Exch ex = {m->peer, m->comm, m->stepseq, m->nx, &m->xcall};
     launch(k_embed, dim3(16), dim3(256), 0, st, hin, m->embed, m->emb_wdt, m->st, d, hc);
     for (int Li = 0; Li < c.n_layers; Li++) {
         DevLayer &l = m->L[Li];
@@ -457,11 +464,11 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
         rc |= G(l.wo_b, m->blk, m->ogrp, st);
         // sharded: wo_b holds this rank's groups' columns, so blk is a partial
         // sum over them
-        rc |= comm_allreduce_sum(m->blk, d, m->comm, st);
+        if (m->world > 1) rc |= xreduce_sum(ex, m->blk, d, st);
         // ---- FFN half: the residual is taken after attention (:511-522)
         pend = {1, nullptr};
         hc_step(m, pend, hin, hout, l.hcf_fn, l.hcf_base, l.hcf_scale, l.ffn_norm, false, m->x1, st);
-        rc |= moe_forward(l.moe, m->ms, m->blk, m->x1, &m->st->token, st, !fused);
+        rc |= moe_forward(l.moe, m->ms, m->blk, m->x1, &m->st->token, st, !fused, m->world > 1 ? &ex : nullptr);
         pend = {fused ? 2 : 1, &l.moe};
     }
     // ---- head (src/cli/dsv4_run.c:467-474)
@@ -470,7 +477,7 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
     launch(k_argmax_part, dim3(148), dim3(256), 0, st, m->am_pv, m->am_pi, m->logits, m->head.rows);
     if (m->world == 1) {
         launch(k_argmax_final, dim3(1), dim3(32), 0, st, m->st, m->out_tokens, m->am_pv, m->am_pi, 148, 1,
-               m->prompt, m->n_prompt);
+               m->prompt, m->n_prompt, (unsigned *)nullptr);
     } else {
         // sharded head: each rank holds a contiguous vocabulary slice; the
         // ranks' best (value, index) pairs are gathered and reduced the same
@@ -479,7 +486,7 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
                m->rank * m->head.rows);
         rc |= comm_allgather(m->am_pair, m->am_gather, 8, m->comm, st);
         launch(k_argmax_final, dim3(1), dim3(32), 0, st, m->st, m->out_tokens, m->am_gather,
-               reinterpret_cast<const int *>(m->am_gather) + 1, m->world, 2, m->prompt, m->n_prompt);
+               reinterpret_cast<const int *>(m->am_gather) + 1, m->world, 2, m->prompt, m->n_prompt, m->stepseq);
     }
     if (cudaPeekAtLastError() != cudaSuccess) rc = -1;
     return rc ? -1 : 0;
@@ -572,7 +579,8 @@ extern "C" void dsv4_cuda_model_free(dsv4b_model *m)
         cudaGraphExecDestroy(m->exec);
         cudaGraphDestroy(m->graph);
     }
-    comm_close(m->comm);                 // after the graph that holds its collectives
+    peer_close(m->peer);                 // after the graph that holds its exchanges
+    comm_close(m->comm);
     for (void *p : m->allocs) cudaFree(p);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
@@ -835,7 +843,6 @@ static bool synth_layer(Synth &S, int Li)
     mo.hidden = d;
     mo.inter = (int)I;
     mo.inter_shared = Isl;
-    mo.comm = m->comm;
     mo.score_func = c.scoring_func == DSV4_SCORE_SIGMOID ? 2 : 1;
     mo.route_scale = c.routed_scale;
     mo.swiglu_limit = c.swiglu_limit;
@@ -864,6 +871,10 @@ extern "C" int dsv4b_shard_check(const DSV4Cfg *c, int world)
 
 extern "C" size_t dsv4b_nccl_id_bytes(void) { return comm_id_bytes(); }
 
+// 0 while every exchange of a sharded model has completed in time; 1 once a
+// peer exchange gave up waiting for a rank (its results are then invalid).
+extern "C" int dsv4b_model_comm_status(const dsv4b_model *m) { return m ? peer_status(m->peer) : -1; }
+
 extern "C" int dsv4b_nccl_unique_id(void *out) { return comm_unique_id(out); }
 
 // A synthetic model, or this rank's share of one: the tensors of rank r are
@@ -884,6 +895,10 @@ extern "C" dsv4b_model *dsv4_cuda_model_create_synthetic_sharded(const DSV4Cfg *
         dsv4_cuda_model_free(m);
         return nullptr;
     }
+    // the one-shot peer exchange unless DSV4B_PEER=0 (then NCCL all-reduces)
+    const char *pe = getenv("DSV4B_PEER");
+    if (world > 1 && !(pe && pe[0] == '0'))
+        peer_open(&m->peer, rank, world, (c->topk + 1) * c->hidden, m->comm, m->stream);
     dsv4b::Synth S;
     S.m = m;
     S.seed = seed;

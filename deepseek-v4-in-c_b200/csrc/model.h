@@ -62,7 +62,7 @@ __global__ void k_build_idxs(int *idxs, int nmax, const StepState *st, int win, 
                              const int *dyn, const int *sel);
 __global__ void k_argmax_part(float *pv, int *pi, const float *x, int n);
 __global__ void k_argmax_final(StepState *st, int *out_tokens, const float *pv, const int *pi, int nparts,
-                               int stride, const int *prompt, int n_prompt);
+                               int stride, const int *prompt, int n_prompt, unsigned *stepseq);
 __global__ void k_argmax_pair(float *pair, const float *pv, const int *pi, int nparts, int offset);
 
 __global__ void k_synth(void *dst, size_t n, int kind, float a, float b, uint64_t key);

@@ -673,7 +673,7 @@ __device__ __forceinline__ void argmax_warp(float &bv, int &bi, const float *pv,
 }
 
 __global__ void k_argmax_final(StepState *st, int *out_tokens, const float *pv, const int *pi, int nparts,
-                               int stride, const int *prompt, int n_prompt)
+                               int stride, const int *prompt, int n_prompt, unsigned *stepseq)
 {
     pdl_trigger();
     pdl_wait();
@@ -687,6 +687,7 @@ __global__ void k_argmax_final(StepState *st, int *out_tokens, const float *pv, 
     const int next = pos + 1;
     st->token = (next < n_prompt) ? prompt[next] : bi;
     st->pos = next;
+    if (stepseq) *stepseq += 1u;          // sharded: the exchanges' step count
 }
 
 // A rank's best pair of its vocabulary slice, the index made global:

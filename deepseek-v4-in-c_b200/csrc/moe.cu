@@ -92,7 +92,7 @@ __global__ void k_combine(float *out, const float *acc, const float *w, int topk
 }
 
 int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float *x,
-                const int *token, cudaStream_t st, bool combine)
+                const int *token, cudaStream_t st, bool combine, const Exch *ex)
 {
     const int H = L.hidden, I = L.inter, K = L.topk;
     PdlChain chain;
@@ -146,7 +146,7 @@ int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float 
     if (gemv_group(it, n, st)) return -1;
     // sharded: every rank holds a slice of each expert's inter dimension, so
     // its outputs are partial sums over that slice; add them up across ranks
-    if (comm_allreduce_sum(S.acc, (size_t)(K + (Is ? 1 : 0)) * H, L.comm, st)) return -1;
+    if (ex && xreduce_sum(*ex, S.acc, (size_t)(K + (Is ? 1 : 0)) * H, st)) return -1;
     if (combine)
         launch(k_combine, dim3((H + 255) / 256), dim3(256), 0, st, out, S.acc, S.wts, K, H, Is ? accs : nullptr);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;

@@ -2,6 +2,8 @@
 // the C ABI.
 #pragma once
 
+#include "internal.h"
+
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -32,10 +34,8 @@ struct MoeLayer {
     int has_shared;
     int n_experts, topk, hidden, inter, inter_shared, score_func;
     float route_scale, swiglu_limit;
-    // sharded over GPUs: every expert's inter slice is local (inter and
-    // inter_shared are the local sizes), and the per-slot outputs are summed
-    // across ranks by an all-reduce on comm before the combine; null on one GPU
-    void *comm;
+    // sharded over GPUs, inter and inter_shared are this rank's slices of
+    // every expert (moe_forward then sums the per-slot outputs across ranks)
 };
 
 struct MoeScratch {
@@ -46,8 +46,10 @@ struct MoeScratch {
 // out = the MoE of x. With combine false the last step (out = sum_k wts[k]
 // acc[k] + the shared expert's acc) is left to the caller, which reads
 // S.acc / S.wts itself (the decode step folds it into the next mHC launch).
+// ex (sharded decode): where the per-slot partial outputs are summed across
+// ranks before the combine; null on one GPU.
 int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float *x,
-                const int *token, cudaStream_t st, bool combine = true);
+                const int *token, cudaStream_t st, bool combine = true, const Exch *ex = nullptr);
 size_t moe_scratch_floats(int hidden, int inter, int inter_shared, int n_experts, int topk);
 void moe_scratch_carve(MoeScratch &S, float *base, int hidden, int inter, int inter_shared,
                        int n_experts, int topk);

@@ -85,6 +85,7 @@ def _declare(L):
         "dsv4_cuda_model_bytes": ([vp], sz),
         "dsv4_cuda_model_step_kernels": ([vp], i),
         "dsv4b_shard_check": ([vp, i], i),
+        "dsv4b_model_comm_status": ([vp], i),
         "dsv4b_nccl_id_bytes": ([], sz),
         "dsv4b_nccl_unique_id": ([vp], i),
         "dsv4_cuda_model_create_synthetic_sharded": ([vp, i, C.c_ulonglong, i, i, vp], vp),

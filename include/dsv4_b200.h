@@ -202,6 +202,13 @@ dsv4b_model *dsv4_cuda_model_create_synthetic_sharded(const DSV4Cfg *c, int max_
                                                       unsigned long long seed, int rank,
                                                       int world, const void *nccl_id);
 
+/* The two per-layer sums run as one-shot exchanges over NVLink peer memory
+ * (CUDA IPC mailboxes, one kernel each, every wait bounded) unless
+ * DSV4B_PEER=0 selects NCCL all-reduces. 0 while every exchange has completed
+ * in time; 1 once a wait for a rank gave up (the step's results are invalid);
+ * -1 for a NULL model. Always 0 on one GPU. */
+int dsv4b_model_comm_status(const dsv4b_model *m);
+
 /* Device memory in use (bytes), for reporting the resident model size. */
 size_t dsv4_cuda_model_bytes(const dsv4b_model *m);
 

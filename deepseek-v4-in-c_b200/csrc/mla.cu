@@ -158,6 +158,99 @@ k_indexer_score(float *out, const float *q, const void *keys, long key_stride,
     }
 }
 
+// The same scores with the heads spread over blocks (decode: a few hundred
+// positions would otherwise occupy a handful of SMs with long double FMA
+// chains). grid (ceil(n_pos / 32), n_heads / IX_HS, batch), 256 threads:
+// thread (position t & 31, head (t >> 5) of the block's IX_HS) forms the
+// sequential double dot of its pair and stores term = dot > 0 ? dot * w : 0
+// to terms[b][p][h]; the last block of a position tile to arrive (counter
+// per tile, reset by that block) adds each position's terms in head order
+// -- the reference's loop exactly, skipped heads adding +0 -- and writes out.
+constexpr int IX_HS = 8;
+
+template <int KDT>
+__global__ void __launch_bounds__(256)
+k_indexer_split(float *out, const float *q, const void *keys, long key_stride, long seq_key_stride, const float *w,
+                int n_heads, int head_dim, int n_pos, float scale, long seq_q_stride, long seq_out_stride,
+                const int *dyn_n, double *terms, unsigned *count)
+{
+    pdl_trigger();
+    pdl_wait();
+    const int n_alloc = n_pos;                      // the terms' per-sequence stride
+    if (dyn_n) n_pos = min(n_pos, *dyn_n);
+    if ((int)blockIdx.x * IX_TP >= n_pos) return;
+    extern __shared__ double ixs[];
+    double *qs = ixs;                               // [IX_HS][head_dim]
+    double *kt = qs + IX_HS * head_dim;             // [head_dim][IX_TP]
+    __shared__ bool last;
+    const int b = blockIdx.z, t0 = blockIdx.x * IX_TP, h0 = blockIdx.y * IX_HS, tid = threadIdx.x;
+    const int ntiles = gridDim.x;
+    q += (size_t)b * seq_q_stride + (size_t)h0 * head_dim;
+    w += (size_t)b * n_heads;
+    const char *kb = reinterpret_cast<const char *>(keys) + (size_t)b * seq_key_stride * dt_bytes<KDT>;
+    const int nq4 = (IX_HS * head_dim) >> 2;
+    for (int i = tid; i < nq4; i += blockDim.x) {
+        const float4 v = __ldcg(reinterpret_cast<const float4 *>(q) + i);
+        qs[4 * i] = (double)v.x;
+        qs[4 * i + 1] = (double)v.y;
+        qs[4 * i + 2] = (double)v.z;
+        qs[4 * i + 3] = (double)v.w;
+    }
+    {
+        const int p = tid >> 3, part8 = tid & 7, nd4 = head_dim >> 2;
+        const bool live = t0 + p < n_pos;
+        for (int g0 = part8; g0 < nd4; g0 += 32) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int g = g0 + 8 * u;
+                v[u] = (live && g < nd4) ? load4_t<KDT>(kb, (size_t)(t0 + p) * key_stride + 4 * g)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int g = g0 + 8 * u;
+                if (g < nd4) {
+                    kt[(4 * g) * IX_TP + p] = (double)v[u].x;
+                    kt[(4 * g + 1) * IX_TP + p] = (double)v[u].y;
+                    kt[(4 * g + 2) * IX_TP + p] = (double)v[u].z;
+                    kt[(4 * g + 3) * IX_TP + p] = (double)v[u].w;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    const int p = tid & 31, j = tid >> 5;
+    double *tb = terms + (size_t)b * n_alloc * n_heads;
+    if (t0 + p < n_pos) {
+        double acc = 0.0;
+        for (int c = 0; c < head_dim; c++) acc = __fma_rn(qs[j * head_dim + c], kt[c * IX_TP + p], acc);
+        const double wh = (double)ld_act(w + h0 + j);
+        tb[(size_t)(t0 + p) * n_heads + h0 + j] = acc > 0.0 ? __dmul_rn(acc, wh) : 0.0;
+    }
+    __threadfence();
+    __syncthreads();
+    unsigned *cnt = count + (size_t)b * ntiles + blockIdx.x;
+    if (tid == 0) last = atomicAdd(cnt, 1u) == gridDim.y - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (tid == 0) *cnt = 0u;
+    // the tile's terms into shared memory by every thread (one round of L2
+    // loads, over the q tile, no longer needed), then each position's sum
+    // in head order
+    const int np = min(IX_TP, n_pos - t0), nt = np * n_heads;
+    double *ts = ixs;                               // [np][n_heads]
+    const double *tt = tb + (size_t)t0 * n_heads;
+    for (int i = tid; i < nt; i += blockDim.x) ts[i] = __ldcg(tt + i);
+    __syncthreads();
+    if (tid < np) {
+        double total = 0.0;
+        for (int h = 0; h < n_heads; h++) total = __dadd_rn(total, ts[tid * n_heads + h]);
+        out[(size_t)b * seq_out_stride + t0 + tid] = __fmul_rn((float)total, scale);
+    }
+}
+
 // ------------------------------------------------------------------- top-k
 // Orderable key: larger value -> larger key (IEEE total order on non-NaN).
 __device__ __forceinline__ uint32_t fkey(float v)
@@ -575,9 +668,39 @@ k_attn_combine(float *o, AttnPart part, const float *sink, int nch, int n_heads,
 
 int indexer_score(float *out, const float *q, const void *keys, int key_dt, long key_stride,
                   long seq_key_stride, const float *w, int n_heads, int head_dim, int n_pos, float scale,
-                  int batch, cudaStream_t st, const int *dyn_n)
+                  int batch, cudaStream_t st, const int *dyn_n, double *terms, unsigned *count)
 {
     if (n_pos <= 0 || batch <= 0) return 0;
+    if (terms && count && n_heads % IX_HS == 0 && head_dim % 4 == 0 && (key_stride & 3) == 0 &&
+        (seq_key_stride & 3) == 0 && ((uintptr_t)q & 15) == 0 &&
+        (uintptr_t)keys % (key_dt == DSV4B_DT_F32 ? 16 : key_dt == DSV4B_DT_BF16 ? 8 : 4) == 0) {
+        size_t sm = ((size_t)IX_HS * head_dim + (size_t)head_dim * IX_TP) * 8;
+        if ((size_t)IX_TP * n_heads * 8 > sm) sm = (size_t)IX_TP * n_heads * 8;
+        if (sm <= 200 * 1024) {
+            static bool sattr = false;
+            if (!sattr) {
+                cudaFuncSetAttribute(k_indexer_split<DSV4B_DT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     200 * 1024);
+                cudaFuncSetAttribute(k_indexer_split<DSV4B_DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     200 * 1024);
+                cudaFuncSetAttribute(k_indexer_split<DSV4B_DT_E4M3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     200 * 1024);
+                sattr = true;
+            }
+            const dim3 grid((n_pos + IX_TP - 1) / IX_TP, n_heads / IX_HS, batch);
+            const long sq = (long)n_heads * head_dim;
+            if (key_dt == DSV4B_DT_F32)
+                launch(k_indexer_split<DSV4B_DT_F32>, grid, dim3(256), sm, st, out, q, keys, key_stride,
+                       seq_key_stride, w, n_heads, head_dim, n_pos, scale, sq, (long)n_pos, dyn_n, terms, count);
+            else if (key_dt == DSV4B_DT_BF16)
+                launch(k_indexer_split<DSV4B_DT_BF16>, grid, dim3(256), sm, st, out, q, keys, key_stride,
+                       seq_key_stride, w, n_heads, head_dim, n_pos, scale, sq, (long)n_pos, dyn_n, terms, count);
+            else
+                launch(k_indexer_split<DSV4B_DT_E4M3>, grid, dim3(256), sm, st, out, q, keys, key_stride,
+                       seq_key_stride, w, n_heads, head_dim, n_pos, scale, sq, (long)n_pos, dyn_n, terms, count);
+            return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
+        }
+    }
     // float4 groups of q and of key rows
     const int kal = key_dt == DSV4B_DT_F32 ? 16 : key_dt == DSV4B_DT_BF16 ? 8 : 4;
     if ((head_dim & 3) || (key_stride & 3) || (seq_key_stride & 3) || ((uintptr_t)keys % kal) ||

@@ -18,7 +18,11 @@ constexpr int kTopkMaxK = 4096;
 // t*key_stride elements; q is [batch][n_heads][head_dim], w [batch][n_heads].
 int indexer_score(float *out, const float *q, const void *keys, int key_dt, long key_stride,
                   long seq_key_stride, const float *w, int n_heads, int head_dim, int n_pos,
-                  float scale, int batch, cudaStream_t st, const int *dyn_n = nullptr);
+                  float scale, int batch, cudaStream_t st, const int *dyn_n = nullptr,
+                  double *terms = nullptr, unsigned *count = nullptr);
+// terms / count (optional, both or neither): scratch for the head-split
+// form, [batch][n_pos][n_heads] doubles and [batch][ceil(n_pos / 32)]
+// counters that start (and are left) at zero; same results.
 // idx[b][i], i < min(k, n): descending scores, ties to the lower index.
 // dyn_nk (device, may be null): {n, k} of this step, n <= the launch's n and
 // k <= the launch's k (the launch sizes shared memory for the maxima).

@@ -60,6 +60,8 @@ struct dsv4b_model {
     int rank, world;
     void *comm, *peer;
     unsigned *stepseq;         // steps done (device; advanced by the last kernel)
+    double *ix_terms;          // the head-split indexer's scratch
+    unsigned *ix_count;
     int nx, xcall;             // exchanges per step; the next one's index
     float *am_pair, *am_gather;
     int n_prompt;
@@ -195,6 +197,9 @@ static bool alloc_common(dsv4b_model *m)
     m->idx_q = F((size_t)c.index_n_heads * c.index_head_dim);
     m->idx_w = F(c.index_n_heads);
     m->idx_scores = F(m->ncomp4);
+    m->ix_terms = (double *)dcopy(m, nullptr, (size_t)m->ncomp4 * c.index_n_heads * 8, &ok);
+    m->ix_count = (unsigned *)dcopy(m, nullptr, (size_t)((m->ncomp4 + 31) / 32) * 4, &ok);
+    if (ok && cudaMemset(m->ix_count, 0, (size_t)((m->ncomp4 + 31) / 32) * 4) != cudaSuccess) ok = false;
     m->logits = F(c.vocab);
     m->xh = F(d);
     m->am_pv = F(1024);
@@ -434,7 +439,7 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
             // the compressed region read as contiguous rows of index_head_dim
             // floats, as the reference does (dsv4_layer.c:286-289)
             rc |= indexer_score(m->idx_scores, m->idx_q, l.kv_cache + (size_t)win * hd, DSV4B_DT_F32, id, 0,
-                                m->idx_w, ih, id, m->ncomp4, scale, 1, st, l.dyn);
+                                m->idx_w, ih, id, m->ncomp4, scale, 1, st, l.dyn, m->ix_terms, m->ix_count);
             rc |= topk(m->isel, m->idx_scores, m->ncomp4, c.index_topk, 1, m->ncomp4, c.index_topk, st, l.dyn);
             launch(k_build_idxs, dim3(1), dim3(256), 0, st, m->idxs, m->nidx, m->st, win, l.has_comp, l.has_idx, l.dyn,
                    m->isel);

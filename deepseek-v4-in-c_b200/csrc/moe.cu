@@ -28,7 +28,6 @@ __global__ void k_route(const float *logits, const float *bias, const int *fixed
     pdl_trigger();
     pdl_wait();
     __shared__ float orig[kMoeMaxExperts], sc[kMoeMaxExperts];
-    __shared__ unsigned char taken[kMoeMaxExperts];
     __shared__ int chosen[kMoeMaxTopk];
     const int tid = threadIdx.x, nthr = blockDim.x;
     for (int e = tid; e < n; e += nthr) {
@@ -38,7 +37,6 @@ __global__ void k_route(const float *logits, const float *bias, const int *fixed
         else o = sqrtf((l > 20.0f) ? l : log1pf(expf(l)));
         orig[e] = o;
         sc[e] = bias ? __fadd_rn(o, bias[e]) : o;
-        taken[e] = 0;
     }
     __syncthreads();
     if (fixed || tid2eid) {
@@ -46,21 +44,42 @@ __global__ void k_route(const float *logits, const float *bias, const int *fixed
     } else if (tid < 32) {
         // topk rounds of warp argmax: value descending, ties to the lower
         // index -- the order of the reference's repeated-argmax selection.
+        // Lane l holds experts l + 32 i in registers and its current best;
+        // the round's winner drops its candidate (to -inf: scores are finite)
+        // and rescans its own.
+        constexpr int PER = kMoeMaxExperts / 32;
+        float v[PER];
+#pragma unroll
+        for (int i = 0; i < PER; i++) {
+            const int e = tid + 32 * i;
+            v[i] = e < n ? sc[e] : -INFINITY;
+        }
+        auto local_best = [&](float &bv, int &bi) {
+            bv = -INFINITY;
+            bi = -1;
+#pragma unroll
+            for (int i = 0; i < PER; i++)
+                if (v[i] != -INFINITY && (bi < 0 || v[i] > bv)) { bv = v[i]; bi = tid + 32 * i; }
+        };
+        float lv;
+        int li;
+        local_best(lv, li);
         for (int k = 0; k < topk; k++) {
-            float bv = 0.0f;
-            int bi = -1;
-            for (int e = tid; e < n; e += 32)
-                if (!taken[e] && (bi < 0 || sc[e] > bv || (sc[e] == bv && e < bi))) { bv = sc[e]; bi = e; }
+            float bv = lv;
+            int bi = li;
+#pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
                 const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
                 const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
                 if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
             }
-            if (tid == 0) {
-                chosen[k] = bi;
-                taken[bi] = 1;
+            if (tid == 0) chosen[k] = bi;
+            if (bi >= 0 && (bi & 31) == tid) {
+#pragma unroll
+                for (int i = 0; i < PER; i++)
+                    if (tid + 32 * i == bi) v[i] = -INFINITY;
+                local_best(lv, li);
             }
-            __syncwarp();
         }
     }
     __syncthreads();

@@ -52,7 +52,7 @@ GEMV_METRIC = "FP8 block-scaled GEMV HBM GB/s (config 1, 4096x7168 e4m3, batch 1
 
 # DRAM bytes (read + write) per unit from an ncu capture of the same kernel
 # and workload, or None where none was taken.
-TRAFFIC_C1 = 29456384          # one config-1 GEMV launch
+TRAFFIC_C1 = 29456384          # one config-1 GEMV launch (ncu dram__bytes_read + write)
 TRAFFIC_DECODE = None
 
 
@@ -437,7 +437,7 @@ def run_gemv(a):
         "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
                      "frac": ach / peak,
                      "peak_source": src + " burst hbm_gbs" + (" x %d GPUs" % world if world > 1 else ""),
-                     "scope": "k_gemv_reg, one launch per step", "bytes_per_unit": C1_BYTES,
+                     "scope": "k_gemv_group, one launch per step", "bytes_per_unit": C1_BYTES,
                      "traffic": TRAFFIC_C1},
         "gpu_launches": a.steps,
         "clocks": clk.summary(),

@@ -481,7 +481,7 @@ int gemv_group(GemvItem *items, int n, cudaStream_t st)
         if (it.mma) {
             const int nb = it.cols / mma_unit_cols(it.fmt);
             // a multiple of 16 virtual rows, within the shared memory budget
-            int cap = (int)((kMmaTileSmem - mma_smem(it.fmt, nb, 0)) / ((size_t)(nb + 1) * 4)) & ~15;
+            int cap = (int)((kMmaTileSmem - mma_smem(it.fmt, nb, 0)) / 64) & ~15;
             cap = cap < 512 ? cap : 512;
             if (cap < 16) return -1;
             int tr = ((int)(target / it.rowbytes) + 15) & ~15;

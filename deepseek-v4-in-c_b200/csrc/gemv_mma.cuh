@@ -22,7 +22,10 @@
 // unit order, the eight run sums added in order in double; y = (float)total.
 //
 // Work: a block of 8 warps streams a tile of rows (a multiple of 16); a unit
-// is 16 rows x one 128-column block, taken by the warps in turn. Lane
+// is 16 rows x one 128-column block; the eight contiguous runs of ceil(nb / 8)
+// units of the canonical order are shared out among the warps (a warp, or
+// with fewer than eight runs a set of warps over alternate row groups, per
+// run) and each keeps its run sums itself. Lane
 // (g = lane/4, t = lane%4) loads rows g and g+8 at bytes 64 j + 16 t of the
 // unit row (chunks j = 0..CPL-1) through a ring of cp.async stages it alone
 // reads back; the k index inside a unit is permuted (the dot product does not
@@ -51,11 +54,13 @@ template <> struct MmaFmt<DSV4B_WFP4> { static constexpr int E = 32, CPL = 2, ST
 __host__ __device__ inline int mma_unit_cols(int fmt) { return fmt == DSV4B_WFP4 ? 256 : 128; }
 __host__ __device__ inline int mma_unit_mmas(int fmt) { return fmt == DSV4B_WFP4 ? 16 : 8; }
 
-// Dynamic shared memory of a tile of tr virtual rows over nb units.
+// Dynamic shared memory of a tile of tr virtual rows over nb units: the
+// ring, the FP4 scale ring, the x fragments, the per-unit exponents and the
+// eight run sums (double) of every virtual row.
 __host__ __device__ inline size_t mma_smem(int fmt, int nb, int tr)
 {
     return (size_t)kMmaRing + kMmaSRing + (size_t)nb * mma_unit_mmas(fmt) * kMmaXpPerMma +
-           (((size_t)nb * 4 + 15) & ~(size_t)15) + (size_t)tr * (nb + 1) * 4;
+           (((size_t)nb * 4 + 15) & ~(size_t)15) + (size_t)tr * 8 * 8;
 }
 
 __device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -161,8 +166,8 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
     uint2 *sring = reinterpret_cast<uint2 *>(smem + kMmaRing);
     uint2 *xp = reinterpret_cast<uint2 *>(smem + kMmaRing + kMmaSRing);
     int *kbs = reinterpret_cast<int *>(smem + kMmaRing + kMmaSRing + (size_t)nb * MPU * kMmaXpPerMma);
-    float *qs = reinterpret_cast<float *>(smem + kMmaRing + kMmaSRing + (size_t)nb * MPU * kMmaXpPerMma +
-                                          (((size_t)nb * 4 + 15) & ~(size_t)15));
+    double *runs = reinterpret_cast<double *>(smem + kMmaRing + kMmaSRing + (size_t)nb * MPU * kMmaXpPerMma +
+                                              (((size_t)nb * 4 + 15) & ~(size_t)15));   // [tr][8]
 
     const uint8_t *W = it.W, *S = it.S, *W2 = it.W2, *S2 = it.S2;
     if (it.wtab) {
@@ -175,8 +180,14 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
             S2 = it.s2tab ? it.s2tab[e] : nullptr;
         }
     }
-    const int nunits = (it.tr >> 4) * nb;
-    const int K = warp < nunits ? (nunits - warp + 7) / 8 : 0;   // units of this warp
+    // The canonical order sums eight contiguous runs of ceil(nb / 8) units;
+    // R of them are non-empty. Warp w takes run w % R of row groups
+    // w / R, w / R + SH, ... (SH = 8 / R warps share a run when R < 8), and
+    // keeps that run's sum itself.
+    const int per = (nb + 7) >> 3, R = (nb + per - 1) / per, SH = 8 / R;
+    const int run = warp % R, sub = warp / R;
+    const int cb0 = run * per, cb1 = min(nb, cb0 + per), ngr = it.tr >> 4;
+    const int K = sub < SH ? (cb1 - cb0) * ((ngr - sub + SH - 1) / SH) : 0;   // units of this warp
     const int nsteps = K * STEPS;
 
     // the matrix row of virtual row v, or -1 past the matrix; *second: W2
@@ -185,9 +196,8 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
         const int row = it.pair ? tile * trh + (second ? v - trh : v) : tile * it.tr + v;
         return row < it.rows ? row : -1;
     };
-    // the unit walk: u = warp + 8k, as (row group, block) without divisions
-    int i_rg = 0, i_cb = warp, i_s = 0, i_q = 0;
-    while (i_cb >= nb) { i_cb -= nb; i_rg++; }
+    // the unit walk: the warp's run in each of its row groups in turn
+    int i_rg = sub, i_cb = cb0, i_s = 0, i_q = 0;
     auto issue_next = [&]() {
         if (i_q < nsteps) {
             const int slot = i_q % kMmaStages;
@@ -212,8 +222,7 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
             }
             if (++i_s == STEPS) {
                 i_s = 0;
-                i_cb += 8;
-                while (i_cb >= nb) { i_cb -= nb; i_rg++; }
+                if (++i_cb == cb1) { i_cb = cb0; i_rg += SH; }
             }
         }
         i_q++;
@@ -223,18 +232,19 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
     for (int q = 0; q < kMmaStages - 1; q++) issue_next();
     pdl_wait();
 
-    // x fragments: warp w builds those of units w, w+8, ...; lane = (mma, t),
-    // two passes for the 16 k16-steps of an FP4 unit. All of a warp's x
-    // loads are issued before any is used.
+    // x fragments: every warp builds those of its own run (warps sharing a
+    // run write the same values); lane = (mma, t), two passes for the 16
+    // k16-steps of an FP4 unit. All of a warp's x loads are issued before any
+    // is used.
     constexpr int XU = kMmaMaxBlocks / 8, XH = MPU / 8;
     float4 xv[XU][XH];
 #pragma unroll
     for (int u = 0; u < XU; u++) {
-        const int cb = warp + 8 * u;
+        const int cb = cb0 + u;
 #pragma unroll
         for (int h = 0; h < XH; h++) {
             const int m = h * 8 + (lane >> 2), tt = lane & 3, j = m / MPC, i = m - j * MPC;
-            if (cb >= nb) {
+            if (cb >= cb1) {
                 xv[u][h] = make_float4(0.f, 0.f, 0.f, 0.f);
             } else if constexpr (FMT == DSV4B_WFP4) {
                 // k16 step i pairs elements (8 (i/2) + 2 (i%2) + {0, 4}) and
@@ -249,8 +259,8 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
     }
 #pragma unroll
     for (int u = 0; u < XU; u++) {
-        const int cb = warp + 8 * u;
-        if (cb >= nb) break;
+        const int cb = cb0 + u;
+        if (cb >= cb1) break;
         float mx = 0.0f;
 #pragma unroll
         for (int h = 0; h < XH; h++)
@@ -273,11 +283,11 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
         }
         if (lane == 0) kbs[cb] = k;
     }
-    __syncthreads();
+    __syncwarp();
 
     float c[4] = {0.f, 0.f, 0.f, 0.f};
-    int c_rg = 0, c_cb = warp, c_s = 0;
-    while (c_cb >= nb) { c_cb -= nb; c_rg++; }
+    double run_a = 0.0, run_b = 0.0;                 // rows g, g + 8 of the current row group
+    int c_rg = sub, c_cb = cb0, c_s = 0;
     for (int q = 0; q < nsteps; q++) {
         issue_next();
         cp_wait<kMmaStages - 1>();
@@ -342,46 +352,37 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
                 const float un = pow2f(-kbs[c_cb]);
                 const float qa = __fmul_rn(__fmul_rn(__fadd_rn(__fadd_rn(c[0], c[1]), n2a), un), sa);
                 const float qb = __fmul_rn(__fmul_rn(__fadd_rn(__fadd_rn(c[2], c[3]), n2b), un), sbv);
-                qs[(c_rg * 16 + g) * (nb + 1) + c_cb] = qa;
-                qs[(c_rg * 16 + g + 8) * (nb + 1) + c_cb] = qb;
+                run_a = __dadd_rn(run_a, (double)qa);
+                run_b = __dadd_rn(run_b, (double)qb);
+                if (c_cb == cb1 - 1) {                    // the run ends: its sums are final
+                    runs[(c_rg * 16 + g) * 8 + run] = run_a;
+                    runs[(c_rg * 16 + g + 8) * 8 + run] = run_b;
+                    run_a = run_b = 0.0;
+                }
             }
             c[0] = c[1] = c[2] = c[3] = 0.f;
         }
         if (++c_s == STEPS) {
             c_s = 0;
-            c_cb += 8;
-            while (c_cb >= nb) { c_cb -= nb; c_rg++; }
+            if (++c_cb == cb1) { c_cb = cb0; c_rg += SH; }
         }
     }
     cp_wait<0>();
     __syncthreads();
-    // row totals: 8 lanes per virtual row each add a contiguous eighth of the
-    // blocks in double, then the eight sums in order; the total lands in the
-    // row's spare slot qs[v][nb]
-    {
-        const int per = (nb + 7) >> 3, w8 = tid & 7;
-        for (int v0 = 0; v0 < it.tr; v0 += (int)blockDim.x >> 3) {
-            const int v = v0 + (tid >> 3);
-            double tw = 0.0;
-            if (v < it.tr) {
-                const float *sr = qs + v * (nb + 1) + w8 * per;
-                const int cnt = min(per, nb - w8 * per);
-                for (int k = 0; k < cnt; k++) tw = __dadd_rn(tw, (double)sr[k]);
-            }
-            double tot = 0.0;
+    // row totals: the eight run sums of a virtual row added in run order
+    // (an empty run adds 0)
+    auto total = [&](int v) {
+        double tt = 0.0;
 #pragma unroll
-            for (int w = 0; w < 8; w++) tot = __dadd_rn(tot, __shfl_sync(0xffffffffu, tw, (lane & ~7) | w));
-            __syncwarp();
-            if (w8 == 0 && v < it.tr) qs[v * (nb + 1) + nb] = (float)tot;
-        }
-    }
-    __syncthreads();
+        for (int w = 0; w < 8; w++) tt = __dadd_rn(tt, w < R ? runs[v * 8 + w] : 0.0);
+        return (float)tt;
+    };
     const int nreal = it.pair ? trh : it.tr;
     for (int r = tid; r < nreal; r += blockDim.x) {
         const int row = tile * nreal + r;
         if (row >= it.rows) break;
-        float a = qs[r * (nb + 1) + nb];
-        if (it.pair) a = swiglu_pair(a, qs[(r + trh) * (nb + 1) + nb], it.limit);
+        float a = total(r);
+        if (it.pair) a = swiglu_pair(a, total(r + trh), it.limit);
         it.y[row] = a;
     }
 }

@@ -260,20 +260,37 @@ __global__ void __launch_bounds__(288) k_hc_pre(const __grid_constant__ HcPreArg
     if (col && i < n) {
         if (stepped) {
             const int j = i / hidden, d = i - j * hidden;
+            // every load of the step issued before any is used (fixed-size,
+            // predicated batches), then the sums in their order
             float b;
+            float xl[DSV4B_MAX_HC], cl[DSV4B_MAX_HC];
+#pragma unroll
+            for (int l = 0; l < DSV4B_MAX_HC; l++) {
+                xl[l] = l < hc ? ld_act(a.x + (size_t)l * hidden + d) : 0.0f;
+                cl[l] = l < hc ? ld_act(a.comb_in + l * hc + j) : 0.0f;
+            }
+            const float pj = ld_act(a.post_in + j);
             if (a.acc) {
+                float wv[kMoeMaxTopk], av[kMoeMaxTopk];
+#pragma unroll
+                for (int k = 0; k < kMoeMaxTopk; k++) {
+                    wv[k] = k < a.topk ? ld_act(a.wts + k) : 0.0f;
+                    av[k] = k < a.topk ? ld_act(a.acc + (size_t)k * hidden + d) : 0.0f;
+                }
+                const float sv = a.accs ? ld_act(a.accs + d) : 0.0f;
                 float o = 0.0f;
-                for (int k = 0; k < a.topk; k++)
-                    o = __fadd_rn(o, __fmul_rn(ld_act(a.wts + k), ld_act(a.acc + (size_t)k * hidden + d)));
-                if (a.accs) o = __fadd_rn(o, ld_act(a.accs + d));
+#pragma unroll
+                for (int k = 0; k < kMoeMaxTopk; k++)
+                    if (k < a.topk) o = __fadd_rn(o, __fmul_rn(wv[k], av[k]));
+                if (a.accs) o = __fadd_rn(o, sv);
                 b = o;
             } else {
                 b = ld_act(a.blk + d);
             }
-            double s = __dmul_rn((double)ld_act(a.post_in + j), (double)b);
-            for (int l = 0; l < hc; l++)
-                s = __dadd_rn(s, __dmul_rn((double)ld_act(a.comb_in + l * hc + j),
-                                           (double)ld_act(a.x + (size_t)l * hidden + d)));
+            double s = __dmul_rn((double)pj, (double)b);
+#pragma unroll
+            for (int l = 0; l < DSV4B_MAX_HC; l++)
+                if (l < hc) s = __dadd_rn(s, __dmul_rn((double)cl[l], (double)xl[l]));
             xv = (float)s;
             a.xout[i] = xv;
         } else {
@@ -312,11 +329,17 @@ __global__ void __launch_bounds__(288) k_hc_pre(const __grid_constant__ HcPreArg
     const int nblk = (int)gridDim.x, per = (nblk + 7) >> 3;
     if (tid < NV * 8) {
         const int m = tid >> 3, w = tid & 7;
-        double t = 0.0;
-        for (int k = 0; k < per; k++) {
+        constexpr int PB = kHcPreBlocks / 8;       // per <= PB: all loads first
+        double pv[PB];
+#pragma unroll
+        for (int k = 0; k < PB; k++) {
             const int bb = w * per + k;
-            if (bb < nblk) t += __ldcg(a.part + (size_t)bb * NV + m);
+            pv[k] = (k < per && bb < nblk) ? __ldcg(a.part + (size_t)bb * NV + m) : 0.0;
         }
+        double t = 0.0;
+#pragma unroll
+        for (int k = 0; k < PB; k++)
+            if (k < per && w * per + k < nblk) t += pv[k];
         red8[m][w] = t;
     }
     __syncthreads();

@@ -3,7 +3,7 @@
 // m16n8k16, f32 accumulate.
 //
 // The weights are the A operand: e4m3 codes widen exactly to f16 (one cvt
-// per pair); e2m1 codes are placed in f16 bit fields (e2m1_pair) and
+// per pair); e2m1 codes are placed in f16 bit fields (e2m1_word) and
 // multiplied by their block scale, exact while the scale exponent lies in
 // [-23, 1]; bf16 weights are used as they are. x is the B operand, split
 // into three pieces that add back to x exactly enough for an f32 dot:
@@ -88,18 +88,22 @@ __device__ __forceinline__ uint32_t e4m3x2_h2(uint32_t v)
     return (uint32_t)h.x | ((uint32_t)h.y << 16);
 }
 
-// Nibbles q and q + 4 of a word of eight e2m1 codes (nibble 0 lowest) as the
-// f16x2 pair (value(q), value(q + 4)) * 2^-14, exactly. An e2m1 code s|e1 e0|m
-// placed at f16 bits 12..9 reads as 2^(e-15) (1 + m/2) for e > 0 and as the
-// subnormal m 2^-15 for e = 0, i.e. the code's value times 2^-14 in both
-// cases, once its sign moves from bit 12 to bit 15 (adding 7 * 2^12 does
-// that: bits 13 and 14 are clear). Shifts, masks and one multiply-add per
-// pair, in place of a conversion per byte.
-// q is a constant once the caller's loop is unrolled.
-__device__ __forceinline__ uint32_t e2m1_pair(uint32_t w, int q)
+// The four f16x2 pairs of a word of eight e2m1 codes (nibble 0 lowest):
+// r[q] = (value(q), value(q + 4)) * 2^-14, exactly. An e2m1 code s|e1 e0|m
+// placed at f16 bits 15, 11..9 (sign, exponent low bits, mantissa top bit)
+// reads as 2^(e-15) (1 + m/2) for e > 0 and as the subnormal m 2^-15 for
+// e = 0, i.e. the code's value times 2^-14 in both cases. Only the high byte
+// of each f16 is non-zero: (s << 7) | (e1 e0 m << 1). Two masked shifts give
+// those bytes for the low and for the high nibbles of the four bytes, and one
+// byte permute per pair puts two of them in place.
+__device__ __forceinline__ void e2m1_word(uint32_t w, uint32_t (&r)[4])
 {
-    uint32_t t = (q == 0 ? w << 9 : q == 1 ? w << 5 : q == 2 ? w << 1 : w >> 3) & 0x1E001E00u;
-    return t + 7u * (t & 0x10001000u);
+    const uint32_t lo = ((w << 1) & 0x0E0E0E0Eu) | ((w << 4) & 0x80808080u);   // nibbles 0, 2, 4, 6
+    const uint32_t hi = ((w >> 3) & 0x0E0E0E0Eu) | (w & 0x80808080u);          // nibbles 1, 3, 5, 7
+    r[0] = __byte_perm(lo, 0u, 0x2404);     // nibbles 0, 4
+    r[1] = __byte_perm(hi, 0u, 0x2404);     // 1, 5
+    r[2] = __byte_perm(lo, 0u, 0x3414);     // 2, 6
+    r[3] = __byte_perm(hi, 0u, 0x3414);     // 3, 7
 }
 
 __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b)
@@ -110,7 +114,7 @@ __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b)
 }
 
 // E8M0 byte b (scale 2^e, e = b - 127) -> the f16x2 pair (2^(e+14), 2^(e+14)),
-// the multiplier that turns an e2m1_pair() into value * 2^e. Called only for
+// the multiplier that turns an e2m1_word() pair into value * 2^e. Called only for
 // e in [-23, 1]: the multiplier is a normal f16 and every code times 2^e is an
 // exact f16 (0.5 * 2^-23 = 2^-24 is the smallest subnormal).
 __device__ __forceinline__ uint32_t e8m0_h2x(uint32_t b)
@@ -248,7 +252,7 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
                 xv[u][h] = make_float4(0.f, 0.f, 0.f, 0.f);
             } else if constexpr (FMT == DSV4B_WFP4) {
                 // k16 step i pairs elements (8 (i/2) + 2 (i%2) + {0, 4}) and
-                // (... + {1, 5}) of the lane's 32, as e2m1_pair() decodes them
+                // (... + {1, 5}) of the lane's 32, as e2m1_word() pairs them
                 const float *xb = it.x + cb * F::COLS + 4 * E * j + E * tt + 8 * (i >> 1) + 2 * (i & 1);
                 const float2 lo = ld_f2(xb), hi = ld_f2(xb + 4);
                 xv[u][h] = make_float4(lo.x, hi.x, lo.y, hi.y);
@@ -330,12 +334,15 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
                     const uint32_t va = word_of(wa, i), vb = word_of(wb, i);
                     mma_f16(c, e4m3x2_h2(va), e4m3x2_h2(vb), e4m3x2_h2(va >> 16), e4m3x2_h2(vb >> 16), b.x, b.y);
                 } else if constexpr (FMT == DSV4B_WFP4) {
-                    // word i/2 of each row; step i takes nibble pairs
-                    // (2 (i%2), +4) and (2 (i%2) + 1, +4)
-                    const uint32_t va = word_of(wa, i >> 1), vb = word_of(wb, i >> 1);
+                    // word i/2 of each row (decoded once for both of its
+                    // steps); step i takes nibble pairs (2 (i%2), +4) and
+                    // (2 (i%2) + 1, +4)
+                    uint32_t ra[4], rbv[4];
+                    e2m1_word(word_of(wa, i >> 1), ra);
+                    e2m1_word(word_of(wb, i >> 1), rbv);
                     const int q0 = 2 * (i & 1);
-                    mma_f16(c, hmul2(e2m1_pair(va, q0), ha), hmul2(e2m1_pair(vb, q0), hb),
-                            hmul2(e2m1_pair(va, q0 + 1), ha), hmul2(e2m1_pair(vb, q0 + 1), hb), b.x, b.y);
+                    mma_f16(c, hmul2(ra[q0], ha), hmul2(rbv[q0], hb), hmul2(ra[q0 + 1], ha), hmul2(rbv[q0 + 1], hb),
+                            b.x, b.y);
                 } else {
                     mma_bf16(c, word_of(wa, 2 * i), word_of(wb, 2 * i), word_of(wa, 2 * i + 1),
                              word_of(wb, 2 * i + 1), b.x, b.y);

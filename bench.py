@@ -12,11 +12,13 @@ token by token through the same captured step), then W untimed and K timed
 decode steps. One step = one token = one replay of the captured CUDA graph;
 steps are timed with CUDA events on the model's stream. Every step streams
 ≈11.1 GB of distinct weights, far more than the 126 MB L2, so no flush is
-needed between steps. `value` is tokens/s over all ranks; `e2e` times the
+needed between steps. `value` is tokens/s of the sequence; `e2e` times the
 reference-facing call dsv4_cuda_model_decode (host token and position in,
-host next token out) with the host wall clock. Under torchrun each GPU holds
-its own full replica and decodes its own stream (weak scaling); the slowest
-rank's time is reported.
+host next token out) with the host wall clock. Under torchrun the one
+sequence is decoded by the model sharded over the N GPUs (expert inter
+slices, q heads / o_groups, wo_b columns, LM-head vocabulary; two exchanges
+per layer over NVLink peer memory), every rank stepping in lockstep (strong
+scaling); the slowest rank's time is reported.
 
 Workload `gemv_fp8`: y = W x with W 4096x7168 e4m3 in
 128x128 E8M0 blocks, one GEMV per step over 8 rotating resident copies (235 MB

@@ -2,10 +2,11 @@
 //
 // Weight formats are the reference's (src/core/dsv4_quant.h:74-164): e4m3fn
 // codes with E8M0 128x128 block scales, e2m1 codes two per byte (even element
-// in the LOW nibble) with E8M0 1x32 scales, bf16, f32. Decoding uses the
-// hardware converters (cvt.rn.f16x2.e4m3x2 / .e2m1x2), which are exact: every
-// e4m3 and e2m1 value, subnormals included, is representable in f16, and every
-// f16 in f32.
+// in the LOW nibble) with E8M0 1x32 scales, bf16, f32. The helpers here decode
+// with the hardware converters (cvt.rn.f16x2.e4m3x2 / .e2m1x2), which are
+// exact: every e4m3 and e2m1 value, subnormals included, is representable in
+// f16, and every f16 in f32 (the tensor-core FP4 path places e2m1 codes into
+// f16 bit fields itself, gemv_mma.cuh).
 #pragma once
 
 #include <cuda_runtime.h>

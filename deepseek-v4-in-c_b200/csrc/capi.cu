@@ -9,6 +9,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
+#include <utility>
 #include <vector>
 
 #include "common.cuh"
@@ -37,6 +39,25 @@ struct State {
 State g;
 
 cudaStream_t stream_of(void *s) { return s ? (cudaStream_t)s : g.st; }
+
+int smem_optin(const void *kernel, int bytes)
+{
+    static std::mutex mu;
+    static std::vector<std::pair<int, const void *>> done;   // (device, kernel) pairs already raised
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+    std::lock_guard<std::mutex> lk(mu);
+    for (const auto &d : done)
+        if (d.first == dev && d.second == kernel) return 0;
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) {
+        fprintf(stderr, "dsv4_b200: raising a kernel's shared memory to %d bytes on device %d failed: %s\n", bytes,
+                dev, cudaGetErrorString(e));
+        return -1;
+    }
+    done.emplace_back(dev, kernel);
+    return 0;
+}
 
 thread_local int t_chain = 0;
 thread_local bool t_pdl = false;

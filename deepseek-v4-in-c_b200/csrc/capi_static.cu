@@ -70,6 +70,9 @@ extern "C" int dsv4b_sparse_attn_static(float *o, const float *q, const void *kv
 {
     if (kv_dt < 0 || kv_dt > 2) return -1;
     if (batch <= 0 || topk_n <= 0) return 0;
+    // the shapes sparse_attn accepts, checked before the scratch size is
+    // computed from them (a negative count would wrap it)
+    if (n_heads <= 0 || d <= 0 || d > 1024 || (d & 3)) return -1;
     const size_t need = attn_part_bytes(n_heads, d, topk_n, batch);
     if (need > kStaticScratch) {
         fprintf(stderr,

@@ -528,11 +528,7 @@ int gemv_group(GemvItem *items, int n, cudaStream_t st)
         b.it[i] = it;
     }
     if (!blocks) return 0;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(k_gemv_group, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaTileSmem);
-        attr = true;
-    }
+    if (smem_optin(k_gemv_group, kMmaTileSmem)) return -1;
     return launch(k_gemv_group, dim3(blocks), dim3(kGemvThreads), smem, st, b) ==
                    cudaSuccess
                ? 0

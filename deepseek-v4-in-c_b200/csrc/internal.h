@@ -85,6 +85,17 @@ int xreduce_sum(const Exch &x, float *buf, size_t n, cudaStream_t st);
 // The backend's own stream (NULL stream arguments of the device API).
 cudaStream_t stream_of(void *s);
 
+// Raises kernel's dynamic shared memory limit to `bytes` on the CURRENT
+// device. The attribute belongs to each device's context, so it is set once
+// per (device, kernel) -- under a lock, any host thread -- and its return code
+// is checked; 0 or -1.
+int smem_optin(const void *kernel, int bytes);
+template <typename... A>
+static inline int smem_optin(void (*kernel)(A...), int bytes)
+{
+    return smem_optin(reinterpret_cast<const void *>(kernel), bytes);
+}
+
 // Whether kernels are launched as programmatic dependents of their
 // predecessor ($DSV4B_PDL=0 turns it off).
 bool pdl_enabled();

@@ -677,16 +677,10 @@ int indexer_score(float *out, const float *q, const void *keys, int key_dt, long
         size_t sm = ((size_t)IX_HS * head_dim + (size_t)head_dim * IX_TP) * 8;
         if ((size_t)IX_TP * n_heads * 8 > sm) sm = (size_t)IX_TP * n_heads * 8;
         if (sm <= 200 * 1024) {
-            static bool sattr = false;
-            if (!sattr) {
-                cudaFuncSetAttribute(k_indexer_split<DSV4B_DT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     200 * 1024);
-                cudaFuncSetAttribute(k_indexer_split<DSV4B_DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     200 * 1024);
-                cudaFuncSetAttribute(k_indexer_split<DSV4B_DT_E4M3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     200 * 1024);
-                sattr = true;
-            }
+            if (smem_optin(k_indexer_split<DSV4B_DT_F32>, 200 * 1024) ||
+                smem_optin(k_indexer_split<DSV4B_DT_BF16>, 200 * 1024) ||
+                smem_optin(k_indexer_split<DSV4B_DT_E4M3>, 200 * 1024))
+                return -1;
             const dim3 grid((n_pos + IX_TP - 1) / IX_TP, n_heads / IX_HS, batch);
             const long sq = (long)n_heads * head_dim;
             if (key_dt == DSV4B_DT_F32)
@@ -709,13 +703,9 @@ int indexer_score(float *out, const float *q, const void *keys, int key_dt, long
     const size_t smem = ((size_t)n_heads * head_dim + (size_t)head_dim * IX_TP + (size_t)IX_TP * (n_heads + 1) +
                          (size_t)n_heads) * 8;
     if (smem > 200 * 1024) return -1;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(k_indexer_score<DSV4B_DT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        cudaFuncSetAttribute(k_indexer_score<DSV4B_DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        cudaFuncSetAttribute(k_indexer_score<DSV4B_DT_E4M3>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        attr = true;
-    }
+    if (smem_optin(k_indexer_score<DSV4B_DT_F32>, 200 * 1024) || smem_optin(k_indexer_score<DSV4B_DT_BF16>, 200 * 1024) ||
+        smem_optin(k_indexer_score<DSV4B_DT_E4M3>, 200 * 1024))
+        return -1;
     dim3 grid((n_pos + IX_TP - 1) / IX_TP, batch);
     const long sq = (long)n_heads * head_dim;
     if (key_dt == DSV4B_DT_F32)
@@ -739,11 +729,7 @@ int topk(int *idx, const float *scores, int n, int k, int batch, long seq_in_str
     while (kp < (k < n ? k : n)) kp <<= 1;
     const size_t smem = (size_t)((n + 1) & ~1) * 4 + (size_t)kp * 8;
     if (smem > 220 * 1024) return -1;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(k_topk, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-        attr = true;
-    }
+    if (smem_optin(k_topk, 220 * 1024)) return -1;
     launch(k_topk, dim3(dim3(1, batch)), dim3(1024), smem, st, idx, scores, n, k, seq_in_stride, seq_out_stride, dyn_nk);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
@@ -768,14 +754,10 @@ int sparse_attn(float *o, const float *q, const void *kv, int kv_dt, long seq_kv
     part.pm = reinterpret_cast<float *>(part.pden + n);
     part.po = part.pm + n + (n & 1);
     const size_t smem = attn_smem_bytes(d);
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(k_attn_chunk<DSV4B_DT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-        cudaFuncSetAttribute(k_attn_chunk<DSV4B_DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-        cudaFuncSetAttribute(k_attn_chunk<DSV4B_DT_E4M3>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-        attr = true;
-    }
     if (smem > 220 * 1024) return -1;
+    if (smem_optin(k_attn_chunk<DSV4B_DT_F32>, 220 * 1024) || smem_optin(k_attn_chunk<DSV4B_DT_BF16>, 220 * 1024) ||
+        smem_optin(k_attn_chunk<DSV4B_DT_E4M3>, 220 * 1024))
+        return -1;
     const dim3 grid(nch, (n_heads + AT_HB - 1) / AT_HB, batch);
     const long sq = (long)n_heads * d;
     if (kv_dt == DSV4B_DT_F32)

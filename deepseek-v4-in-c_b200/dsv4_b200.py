@@ -261,6 +261,8 @@ class MoE:
 # ------------------------------------------------------------- sparse MLA
 
 F32, BF16, E4M3 = 0, 1, 2
+# DSV4B_SPARSE_ATTN_STATIC_SCRATCH: the fixed device array of dsv4b_sparse_attn_static
+SPARSE_ATTN_STATIC_SCRATCH = 8 << 20
 
 
 def _f(a):

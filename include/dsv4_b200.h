@@ -179,9 +179,11 @@ dsv4b_model *dsv4_cuda_model_create_synthetic(const DSV4Cfg *c, int max_pos,
  * its design notes ask for -- routed and shared experts split along their
  * inter dimension on every rank, q heads (and with them wo_a's o_groups) by
  * rank, wo_b by the matching columns, the LM head by vocabulary -- with two
- * NCCL sum all-reduces per layer (the wo_b output, the experts' per-slot
+ * sums per layer over all ranks (the wo_b output, the experts' per-slot
  * outputs before the k-ordered combine) and one all-gather of the ranks'
- * argmax pairs per token. Every rank runs the same steps in lockstep. */
+ * argmax pairs per token. The sums run as one-shot exchanges over NVLink
+ * peer memory by default (NCCL all-reduces with DSV4B_PEER=0); the argmax
+ * gather is an NCCL all-gather. Every rank runs the same steps in lockstep. */
 
 /* 0 if configuration c splits over world GPUs (heads, o_groups, wo_a / wo_b
  * 128-blocks, expert inter slices of whole 32-column FP4 scale blocks, the

@@ -6,7 +6,9 @@ import subprocess
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+# the reference checkout: argument, REF_DIR, else `reference` beside the repository
+REF = (sys.argv[1] if len(sys.argv) > 1 else os.environ.get("REF_DIR")
+       or os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(HERE))), "reference"))
 exe = "/tmp/layout_probe_ref"
 subprocess.run(["/usr/bin/gcc", "-DUSE_REF", "-I" + os.path.join(REF, "include", "dsv4"),
                 os.path.join(HERE, "layout_probe.c"), "-o", exe], check=True)

@@ -120,7 +120,9 @@ def test_ragged_shapes(dev, port, fmt, rows, cols):
 
 def test_grouped_wo_a_slices_run_on_device(dev, port):
     """dsv4_layer.c:321-334 hands dsv4_mmq row slices of wo_a; the reference
-    backend finds only group 0 (SURVEY note). Every group must be resident."""
+    backend keys residency on the host pointer alone (src/cuda/dsv4_cuda.cu:
+    232-241, find(m->w) at :389), so it finds only group 0. Every group must be
+    resident here."""
     rng = np.random.default_rng(7)
     G, gr, gw = 8, 1024, 4096
     W, S = Q.random_fp8(rng, G * gr, gw)

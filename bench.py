@@ -68,45 +68,72 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi sampled every 200 ms while the timed region runs."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    """SM clock, power and clock-event reasons of the bench's GPU, read through
+    NVML every 100 ms by a thread while the timed region runs (read-only
+    queries). The device is matched to the CUDA device by its UUID, so the
+    sample is of the GPU the kernels run on whatever CUDA_VISIBLE_DEVICES
+    maps. Falls back to one nvidia-smi query per sample."""
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80))
 
     def __init__(self, dev):
-        self.dev, self.rows, self.p = dev, [], None
+        self.dev, self.rows, self.stop, self.err = dev, [], threading.Event(), None
+
+    def _nvml(self):
+        import pynvml as N
+        import torch
+        N.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(self.dev).uuid)
+        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        h = N.nvmlDeviceGetHandleByUUID(uuid)
+        mx = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+
+        def one():
+            return (N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM), mx,
+                    N.nvmlDeviceGetPowerUsage(h) / 1000.0, N.nvmlDeviceGetCurrentClocksEventReasons(h))
+        return one
+
+    def _smi(self):
+        q = "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active"
+
+        def one():
+            out = subprocess.run(["nvidia-smi", "-i", str(self.dev), "--query-gpu=" + q,
+                                  "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                 timeout=5).stdout.strip().split(",")
+            return float(out[0]), float(out[1]), float(out[2]), int(out[3].strip(), 16)
+        return one
+
+    def _run(self):
+        try:
+            try:
+                one = self._nvml()
+            except Exception as e:          # no NVML binding: the CLI
+                self.err = "nvml: %s" % e
+                one = self._smi()
+            while True:
+                self.rows.append(one())
+                if self.stop.wait(0.1):
+                    break
+        except Exception as e:
+            self.err = str(e)
 
     def __enter__(self):
-        try:
-            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), "--query-gpu=" + self.Q,
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
-                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except Exception:
-            self.p = None
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+        time.sleep(0.15)                      # the first sample precedes the timed work
         return self
 
-    def _read(self):
-        for line in self.p.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
-
     def __exit__(self, *a):
-        if self.p:
-            self.p.terminate()
-            self.p.wait()
-            self.t.join(timeout=2)
+        self.stop.set()
+        self.t.join(timeout=10)
 
     def summary(self):
         if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4)
-                          if len(r) > 4 + i and r[4 + i] == "Active"})
-        return {"sm_mhz": float(np.median(sm)) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled: %s" % self.err]}
+        sm = [r[0] for r in self.rows]
+        reasons = sorted({n for r in self.rows for n, bit in self.REASONS if r[3] & bit})
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(max(r[1] for r in self.rows)),
+                "reasons": reasons, "power_w_max": round(max(r[2] for r in self.rows), 1),
                 "samples": len(self.rows)}
 
 
@@ -198,10 +225,9 @@ def cpu_decode_sample(n_pos, warm=2):
     per-position times, description)."""
     import oracle as O
     import dsv4_model as M
-    d = M.flash_config()
-    full = layer_ratios(d)
+    full = layer_ratios(M.flash_config())
     count = {r: full.count(r) for r in set(full)}
-    d.update(n_layers=3, compress_ratios=[0, 4, 128, 0], num_hash_layers=1, max_pos=4096)
+    d = M.flash_sample_config()
     t0 = time.perf_counter()
     sm = M.SyntheticModel(d, seed=0, fast=True)
     t_build = time.perf_counter() - t0
@@ -301,9 +327,12 @@ def run_decode(a):
                    "l2": "no flush: each step streams %.1f GB of distinct weights (> 126 MB L2)"
                          % (bytes_tok / 1e9),
                    "parallelism": ("one sequence sharded over %d GPUs: expert inter slices, q heads / "
-                                   "o_groups, wo_b columns, LM-head vocabulary; 2 NCCL all-reduces per "
-                                   "layer + 1 argmax all-gather per token" % world if world > 1
-                                   else "single GPU")},
+                                   "o_groups, wo_b columns, LM-head vocabulary; 2 sums per layer as "
+                                   "one-shot exchanges over NVLink peer memory (%s) + 1 NCCL argmax "
+                                   "all-gather per token"
+                                   % (world, "NCCL all-reduce: DSV4B_PEER=0"
+                                      if os.environ.get("DSV4B_PEER") == "0" else "CUDA IPC mailboxes")
+                                   if world > 1 else "single GPU")},
         "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
                      "frac": ach / peak,
                      "peak_source": src + " burst hbm_gbs" + (" x %d GPUs" % world if world > 1 else ""),

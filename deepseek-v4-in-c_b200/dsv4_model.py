@@ -110,6 +110,16 @@ def flash_config():
                 num_nextn_predict=1)
 
 
+def flash_sample_config():
+    """Three layers of the Flash geometry, one of each attention kind
+    (compress ratio 0, 4 with the indexer, 128) plus the MTP tail entry, all
+    256 experts and the full 129280-token head: the sample the benchmark times
+    the reference's CPU decode on and the GPU is checked against."""
+    d = flash_config()
+    d.update(n_layers=3, compress_ratios=[0, 4, 128, 0], num_hash_layers=1, max_pos=4096)
+    return d
+
+
 def make_cfg(d):
     ratios = (_i * len(d["compress_ratios"]))(*d["compress_ratios"])
     c = Cfg()

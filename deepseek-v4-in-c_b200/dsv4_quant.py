@@ -111,6 +111,29 @@ def quant_fp4(w, blk=32):
     return np.ascontiguousarray(packed), e8m0_code(s)
 
 
+def quant_fp4_torch(w, blk=32):
+    """quant_fp4 on a torch tensor, on whatever device it lives (the config-2
+    experts are 6.4 G weights, quantised on the GPU for the tests): the same
+    codes and scales bit for bit. The scale exponent comes from frexp, which
+    equals ceil(log2(absmax / 6)) for every float32 absmax."""
+    import torch
+    rows, cols = w.shape
+    assert cols % blk == 0 and cols % 2 == 0
+    b = w.float().reshape(rows, cols // blk, blk)
+    a = b.abs().amax(dim=2).double() / E2M1_MAX
+    m, e = torch.frexp(a)
+    e = torch.where(a > 0, torch.where(m == 0.5, e - 1, e), torch.zeros_like(e)).to(torch.int32)
+    s = torch.ldexp(torch.ones_like(a), e).float()
+    q = b / s[:, :, None]
+    v = q.abs()
+    code = ((v > 0.25).to(torch.uint8) + (v >= 0.75).to(torch.uint8) + (v > 1.25).to(torch.uint8) +
+            (v >= 1.75).to(torch.uint8) + (v > 2.5).to(torch.uint8) + (v >= 3.5).to(torch.uint8) +
+            (v > 5.0).to(torch.uint8))
+    code = (code | torch.where(q < 0, 8, 0).to(torch.uint8)).reshape(rows, cols)
+    packed = code[:, 0::2] | (code[:, 1::2] << 4)
+    return packed.contiguous(), (e + 127).to(torch.uint8).contiguous()
+
+
 def dequant_fp8(codes, scales, blk=128):
     v = e4m3_decode(codes).astype(np.float64)
     rows, cols = v.shape

@@ -133,7 +133,7 @@ class Checker:
         return y
 
     def route(self, logits, topk, route_scale, bias=None, tid2eid=None,
-              token_id=0, score_func=1):
+              token_id=0, score_func=1, with_scores=False):
         scores = _c(logits, np.float32).copy()
         n = scores.size
         orig = np.empty(n, np.float32)
@@ -151,7 +151,7 @@ class Checker:
             if score_func != 1:
                 raise AttributeError("the reference C implements sqrtsoftplus only")
             self._l.fn("route", at)(*args)
-        return idx, w
+        return (idx, w, orig) if with_scores else (idx, w)
 
     # ---- indexer / attention -------------------------------------------
     def indexer_score(self, q, kv, weights, n_heads, head_dim):

@@ -103,13 +103,11 @@ def test_config3_pipeline(dev, port, batch):
     B.sparse_attn_dev(o, q, kv, B.BF16, N, sink, idx, H, D, K, scale, batch, scratch)
     torch.cuda.synchronize()
     sc_h, idx_h, o_h = scores.cpu().numpy(), idx.cpu().numpy(), o.cpu().numpy()
-    for b in range(min(batch, 2)):       # the oracle's indexer is the slow part
+    for b in range(batch):               # every sequence of the batch against the oracle
         kvf, kf = bf16_to_f32(seqs[b][0]), Q.e4m3_decode(seqs[b][1])
         rs = port.indexer_score(seqs[b][3], kf, seqs[b][4], HI, DI)
         assert sc_h[b].tobytes() == rs.tobytes()
         ri = port.topk(rs, K)
         assert list(idx_h[b]) == list(ri)
         ro = port.sparse_attn(seqs[b][2], kvf, seqs[0][5], ri, scale)   # sinks: per head, shared
-        assert vrel(o_h[b], ro) < TOL
-    for b in range(2, batch):            # the rest: selection from the GPU's own scores
-        assert list(idx_h[b]) == list(port.topk(sc_h[b], K))
+        assert vrel(o_h[b], ro) < TOL, (b, vrel(o_h[b], ro))

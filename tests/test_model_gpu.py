@@ -105,3 +105,22 @@ def test_synthetic_on_device_model_runs():
     assert outs == list(ga)
     a.close()
     b.close()
+
+
+def test_flash_sample_against_reference():
+    """The benchmark's CPU-baseline sample -- three Flash-geometry layers
+    (compress ratios 0 / 4 / 128), all 256 FP4 experts, the 129280-token
+    head -- decoded on the GPU from a 16-token prompt for 16 greedy tokens:
+    the argmax at every position is the reference's own dsv4_layer_forward
+    token loop's (oracle/_ref, the CLI loop of src/cli/dsv4_run.c:444-483)."""
+    import oracle as O
+    assert os.path.exists(O.REF_SO), "oracle/_ref/libdsv4ref.so is built with the package"
+    B.init()
+    sm = M.SyntheticModel(M.flash_sample_config(), seed=0, fast=True)
+    prompt = np.random.default_rng(11).integers(0, sm.d["vocab"], 16).astype(np.int32)
+    m = B.Model(sm, 64)
+    out = m.generate(prompt, 16)
+    m.close()
+    ref, _ = O.model_greedy_ref(sm, prompt, 16, 64)
+    assert len(ref) == 17
+    assert list(out) == list(ref)

@@ -23,11 +23,22 @@ def dev():
 
 
 def build(rng, n_experts, hidden, inter, quantized, gate_fmt=B.WF32):
+    """quantized: True (numpy quant_fp4 of N(0, 0.02)), "gpu" (the same
+    quantiser run by torch on the device, for the 6.4 G weights of the full
+    config-2 expert set; bit-identical to quant_fp4, tests/test_oracle_golden.py)
+    or False (uniform random codes at a constant scale)."""
     experts = []
+    if quantized == "gpu":
+        import torch
+        tg = torch.Generator(device="cuda").manual_seed(int(rng.integers(1 << 31)))
     for e in range(n_experts):
         trio = []
         for rows, cols in ((inter, hidden), (inter, hidden), (hidden, inter)):
-            if quantized:
+            if quantized == "gpu":
+                w = torch.randn((rows, cols), generator=tg, device="cuda") * 0.02
+                Wt, St = Q.quant_fp4_torch(w)
+                W, S = Wt.cpu().numpy(), St.cpu().numpy()
+            elif quantized:
                 W, S = Q.quant_fp4(rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02))
             else:
                 W = np.frombuffer(rng.bytes(rows * cols // 2), np.uint8).reshape(rows, cols // 2)
@@ -54,10 +65,14 @@ def oracle_moe(port, x, gate, experts, shared, bias, topk, rs, sf, lim, fixed=No
                  gate.q.cols, experts[0][0].q.rows, shared[0].q.rows, fixed=fixed)
 
 
-def test_config2_full_size(dev, port):
-    """256 FP4 experts (2048 x 4096), fp32 router, sigmoid top-6, shared FP8."""
+@pytest.mark.parametrize("codes", ["quantised", "uniform"])
+def test_config2_full_size(dev, port, codes):
+    """256 FP4 experts (2048 x 4096), fp32 router, sigmoid top-6, shared FP8.
+    "quantised": every expert N(0, 0.02) in e2m1 with ue8m0 1x32 scales, as
+    config 2 prescribes; "uniform": every code byte drawn uniformly (all 16
+    codes in every position) at the N(0, 0.02) block scale."""
     rng = np.random.default_rng(0)
-    gate, experts, shared = build(rng, 256, 4096, 2048, quantized=False)
+    gate, experts, shared = build(rng, 256, 4096, 2048, quantized="gpu" if codes == "quantised" else False)
     moe = B.MoE(gate, experts, shared, topk=6, route_scale=1.0, score_func=2, swiglu_limit=10.0)
     for trial in range(3):
         x = rng.standard_normal(4096, dtype=np.float32)

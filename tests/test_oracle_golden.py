@@ -57,6 +57,35 @@ def test_route_golden(port, golden):
     beq(idx, golden["rt_hidx"]); beq(w, golden["rt_hw"])
 
 
+def test_route_sigmoid_f32_golden(port):
+    """Config 2's router (fp32 GEMV, sigmoid scores, top-6, selection-only
+    bias, weights renormalised) against the reference's PyTorch restatement
+    (tools/dsv4_ref.py route(score_func="sigmoid"); fixture made by
+    tests/golden/make_route_golden.py). The reference C has sqrt-softplus
+    scoring only, so this pins the oracle's sigmoid path and f32 router."""
+    import os
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+    import make_route_golden as MR
+    g = np.load(MR.OUT)
+    W, xs, bias = MR.inputs()
+    assert MR.digest(W, xs, bias) == str(g["sha256"]), "seeded inputs changed"
+    for t in range(MR.TRIALS):
+        b = bias[t] if t % 2 else None
+        # the f32 router GEMV: the oracle's double tree against torch's fp32 linear
+        lg = port.gemv_f32(xs[t], W, MR.N_EXPERTS, MR.HIDDEN)
+        assert np.max(np.abs(lg - g["logits"][t])) <= 1e-6 * np.max(np.abs(g["logits"][t]))
+        # scoring and selection on the reference's own logits
+        idx, w, orig = port.route(g["logits"][t], MR.TOPK, 1.0, bias=b, score_func=2, with_scores=True)
+        assert list(idx) == list(g["idx"][t])
+        ulp = np.abs(orig.view(np.int32).astype(np.int64) - g["scores"][t].view(np.int32).astype(np.int64))
+        assert ulp.max() <= 4, ulp.max()                    # expf vs torch's vectorised sigmoid: a few ulp
+        assert np.max(np.abs(w - g["wts"][t]) / g["wts"][t]) < 1e-6   # double vs float renormalisation
+        # end to end from x: the same selection
+        idx2, _ = port.route(lg, MR.TOPK, 1.0, bias=b, score_func=2)
+        assert list(idx2) == list(g["idx"][t])
+
+
 def test_indexer_and_topk_golden(port, golden):
     sc = port.indexer_score(golden["ix_q"], Q.e4m3_decode(golden["ix_k"]),
                             golden["ix_w"], 64, 128)
@@ -178,3 +207,19 @@ def test_attention_known_answers(port):
     o = port.sparse_attn(np.zeros((1, 2), np.float32), kv2, np.full(1, 0, np.float32),
                          np.array([-1, -1], np.int32), 1.0)
     assert np.all(o == 0.0)                        # all masked -> zero output
+
+
+def test_fp4_quantiser_torch_matches_numpy():
+    """The torch quantiser the full-size config-2 test runs on the GPU gives
+    quant_fp4's codes and scales bit for bit (on CPU torch here), exact
+    power-of-two block maxima and ties at the e2m1 midpoints included."""
+    import torch
+    rng = np.random.default_rng(4)
+    w = rng.standard_normal((64, 1024), dtype=np.float32) * np.float32(0.02)
+    w[3, :32] = np.float32(0.09375) * np.sign(rng.standard_normal(32)).astype(np.float32)  # absmax/6 = 2^-6
+    w[5, 32:64] = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 6.0] * 4, np.float32) * np.float32(2.0 ** -4)
+    w[7, 64:96] = 0.0
+    W, S = Q.quant_fp4(w)
+    Wt, St = Q.quant_fp4_torch(torch.from_numpy(w))
+    assert Wt.numpy().tobytes() == W.tobytes()
+    assert St.numpy().tobytes() == S.tobytes()

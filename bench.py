@@ -384,6 +384,48 @@ def cpu_reference_gemv(seconds, threads=None):
                       "OMP_NUM_THREADS=%s" % (n, len(copies), os.environ.get("OMP_NUM_THREADS", cores))}
 
 
+def reference_gpu_gemv(W, S, x, ours_y, calls=400):
+    """The reference's own GPU co-processor on config 1: its k_mmq_fp8 through
+    its dsv4_cuda_mmq (src/cuda/dsv4_cuda.cu:93-129, 387-403), compiled
+    unchanged for sm_100a into oracle/_ref/libdsv4ref_cuda.so. The call is
+    host-to-host (pinned staging, two blocking copies, one launch), timed by
+    the wall clock, the way its own bench/gpu_call.c times it; its output is
+    checked against ours (vector-scaled relative error)."""
+    import ctypes as C
+    import oracle as O
+    import dsv4_b200 as B
+    path = os.path.join(os.path.dirname(O.REF_SO), "libdsv4ref_cuda.so")
+    if not os.path.exists(path):
+        return {"unavailable": "oracle/_ref/libdsv4ref_cuda.so not built"}
+    L = C.CDLL(path)
+    L.dsv4_cuda_init.restype = C.c_int
+    L.dsv4_cuda_upload.restype = C.c_int
+    if L.dsv4_cuda_init() != 0:
+        return {"unavailable": "reference dsv4_cuda_init failed"}
+    Wc, Sc = np.ascontiguousarray(W), np.ascontiguousarray(S)
+    q = B.QMat(Wc.ctypes.data, Sc.ctypes.data, B.WFP8, C1_ROWS, C1_COLS, 128, 128)
+    if L.dsv4_cuda_upload(C.byref(q)) != 0:
+        return {"unavailable": "reference dsv4_cuda_upload failed"}
+    y = np.empty(C1_ROWS, np.float32)
+    for _ in range(5):
+        L.dsv4_cuda_mmq(y.ctypes.data, x.ctypes.data, C.byref(q))
+    ts = []
+    for _ in range(calls):
+        t0 = time.perf_counter()
+        L.dsv4_cuda_mmq(y.ctypes.data, x.ctypes.data, C.byref(q))
+        ts.append(time.perf_counter() - t0)
+    L.dsv4_cuda_shutdown()
+    ref = np.asarray(ours_y, np.float64)
+    rms = np.sqrt(np.mean(ref * ref))
+    vrel = float(np.max(np.abs(y - ref) / np.maximum(rms, np.maximum(np.abs(y), np.abs(ref)))))
+    best, med = min(ts), float(np.median(ts))
+    return {"kernel": "k_mmq_fp8 (reference src/cuda/dsv4_cuda.cu, unchanged, sm_100a)",
+            "call_ms_median": med * 1e3, "call_ms_best": best * 1e3,
+            "call_gbs_median": C1_BYTES / med / 1e9, "call_gbs_best": C1_BYTES / best / 1e9,
+            "timing": "wall clock per dsv4_cuda_mmq (host x -> host y), %d calls" % calls,
+            "vrel_vs_ours": vrel}
+
+
 def run_gemv(a):
     import torch
     import dsv4_b200 as B
@@ -476,12 +518,303 @@ def run_gemv(a):
     }
     if rank == 0 and world == 1 and not a.no_cpu:
         out["cpu_baseline"] = cpu_reference_gemv(10.0)
+    if rank == 0 and world == 1:
+        # the same call of ours, host to host, beside the reference GPU kernel's
+        y0 = mats[0].mmq(x)
+        out["reference_gpu"] = reference_gpu_gemv(W, S, x, y0)
+        out["reference_gpu"]["ours_e2e_gbs"] = e2e["value"]
     if rank == 0:
         print(json.dumps(out))
     L.dsv4_cuda_shutdown()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# ------------------------------------------------------------- MoE (C2)
+
+MOE_METRIC = "routed MoE FFN token HBM GB/s (config 2: 256 FP4 experts top-6 + shared FP8, fp32 sigmoid router)"
+C2_H, C2_I, C2_E, C2_K = 4096, 2048, 256, 6
+# one token: 6 routed experts (w1, w3 2048x4096, w2 4096x2048 in e2m1 + 1x32
+# E8M0) + the shared FP8 expert + the fp32 router + x and the output
+C2_BYTES = 6 * 13369344 + 25167360 + 4194304 + 32768
+
+
+def build_moe(seed=0):
+    """Config 2's layer: experts N(0, 0.02) quantised to e2m1 with ue8m0 1x32
+    scales on the GPU (bit-identical to dsv4_quant.quant_fp4), shared expert
+    FP8 128x128, fp32 router N(0, 0.02). Returns host matrices (resident)."""
+    import torch
+    import dsv4_b200 as B
+    import dsv4_quant as Q
+    tg = torch.Generator(device="cuda").manual_seed(seed)
+    experts = []
+    for e in range(C2_E):
+        trio = []
+        for rows, cols in ((C2_I, C2_H), (C2_I, C2_H), (C2_H, C2_I)):
+            Wt, St = Q.quant_fp4_torch(torch.randn((rows, cols), generator=tg, device="cuda") * 0.02)
+            m = B.Matrix(B.WFP4, Wt.cpu().numpy(), St.cpu().numpy())
+            B.check(m.upload(), "upload")
+            trio.append(m)
+        experts.append(trio)
+    rng = np.random.default_rng(seed)
+    shared = []
+    for rows, cols in ((C2_I, C2_H), (C2_I, C2_H), (C2_H, C2_I)):
+        W, S = Q.quant_fp8(rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02), 128)
+        m = B.Matrix(B.WFP8, W, S)
+        B.check(m.upload(), "upload")
+        shared.append(m)
+    gate = B.Matrix(B.WF32, (rng.standard_normal((C2_E, C2_H)) * 0.02).astype(np.float32))
+    B.check(gate.upload(), "upload")
+    torch.cuda.synchronize()
+    return gate, experts, shared
+
+
+def cpu_moe_token(ref, port, x, gate, experts, shared):
+    """One config-2 token on the host: the reference's own kernels for the
+    experts (dsv4_matmul_fp4, dsv4_swiglu, dsv4_matmul_fp8), the restated
+    fp32 router and sigmoid top-6 (the reference C has neither), the k-ordered
+    combine of src/model/dsv4_layer.c:471-483."""
+    logits = port.gemv_f32(x, gate.W, C2_E, C2_H)
+    idx, w = port.route(logits, C2_K, 1.0, score_func=2)
+    out = np.zeros(C2_H, np.float32)
+    for k in range(C2_K):
+        w1, w3, w2 = experts[idx[k]]
+        g = ref.gemv_fp4(x, w1.W, w1.S, C2_I, C2_H)
+        u = ref.gemv_fp4(x, w3.W, w3.S, C2_I, C2_H)
+        h = ref.swiglu(g, u, 10.0)
+        acc = ref.gemv_fp4(h, w2.W, w2.S, C2_H, C2_I)
+        out = out + np.float32(w[k]) * acc
+    g = ref.gemv_fp8(x, shared[0].W, shared[0].S, C2_I, C2_H)
+    u = ref.gemv_fp8(x, shared[1].W, shared[1].S, C2_I, C2_H)
+    return out + ref.gemv_fp8(ref.swiglu(g, u, 10.0), shared[2].W, shared[2].S, C2_H, C2_I)
+
+
+def cpu_moe_sample(gate, experts, shared, seconds):
+    import oracle as O
+    kind = "reference" if os.path.exists(O.REF_SO) else "port"
+    ref, port = O.Checker(kind), O.Checker("port")
+    rng = np.random.default_rng(7)
+    n, t_end, t0 = 0, time.perf_counter() + seconds, time.perf_counter()
+    while time.perf_counter() < t_end or n < 2:
+        cpu_moe_token(ref, port, rng.standard_normal(C2_H, dtype=np.float32), gate, experts, shared)
+        n += 1
+    per = (time.perf_counter() - t0) / n
+    return per, n, kind
+
+
+def run_moe(a):
+    import torch
+    import dsv4_b200 as B
+    rank, world, dist = dist_setup(a.gpus)
+    L = B.init()
+    t0 = time.perf_counter()
+    gate, experts, shared = build_moe()
+    t_build = time.perf_counter() - t0
+    moe = B.MoE(gate, experts, shared, topk=C2_K, route_scale=1.0, score_func=2, swiglu_limit=10.0)
+    st = torch.cuda.Stream()
+    W, K = max(a.warmup, 3), a.steps
+    xs = torch.randn((W + K, C2_H), device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
+    out = torch.empty(C2_H, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")     # > 126 MB L2
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    with torch.cuda.stream(st):
+        for i in range(W):
+            moe.forward_dev(out, xs[i], st)
+    torch.cuda.synchronize()
+    with Clocks(torch.cuda.current_device()) as clk:
+        with torch.cuda.stream(st):
+            for i in range(K):
+                flush.zero_()
+                ev[i][0].record(st)
+                moe.forward_dev(out, xs[W + i], st)
+                ev[i][1].record(st)
+        torch.cuda.synchronize()
+    ms = max_over_ranks(dist, sum(e0.elapsed_time(e1) for e0, e1 in ev))
+    ms_step = ms / K
+    value = C2_BYTES / (ms_step * 1e-3) / 1e9
+    # e2e: the host-buffer call dsv4_cuda_moe (host x in, host output out)
+    xh = np.random.default_rng(3).standard_normal((64, C2_H), dtype=np.float32)
+    for i in range(3):
+        moe(xh[i])
+    t0 = time.perf_counter()
+    for i in range(64):
+        moe(xh[i])
+    e2e_s = (time.perf_counter() - t0) / 64
+    peak, src = peaks()
+    out_line = {
+        "metric": MOE_METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms_step, "tokens_per_s": 1e3 / ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "e2m1 / e4m3 / f32 weights, f32 activations, f64 row sums",
+        "data": "synthetic (config 2 distributions, quantised on the GPU)",
+        "config": {"workload": "moe config 2 (one token)", "hidden": C2_H, "experts": C2_E, "inter": C2_I,
+                   "topk": C2_K, "router": "fp32 sigmoid", "build_s": round(t_build, 1),
+                   "l2": "flushed (256 MB write) before every timed step; a distinct x (routing) per step"},
+        "roofline": {"bound": "hbm", "achieved": value, "peak": peak, "unit": "GB/s", "frac": value / peak,
+                     "peak_source": src + " burst hbm_gbs", "scope": "one token: router + 6 experts + shared "
+                     "(%d launches, CUDA events around each token)" % 4, "bytes_per_unit": C2_BYTES,
+                     "traffic": None},
+        "gpu_launches": 4 * K,
+        "clocks": clk.summary(),
+        "e2e": {"value": C2_BYTES / e2e_s / 1e9, "unit": "GB/s", "ms_per_step": e2e_s * 1e3,
+                "h2d_bytes_per_step": C2_H * 4, "d2h_bytes_per_step": C2_H * 4 + C2_K * 8,
+                "api": "dsv4_cuda_moe (host x -> host output, selection, weights), wall clock"},
+    }
+    if rank == 0 and world == 1 and not a.no_cpu:
+        per, n, kind = cpu_moe_sample(gate, experts, shared, 10.0)
+        out_line["cpu_baseline"] = {"value": C2_BYTES / per / 1e9, "unit": "GB/s",
+                                    "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count())),
+                                    "kind": kind, "sample": "%d config-2 tokens (reference dsv4_matmul_fp4 / "
+                                    "dsv4_swiglu / dsv4_matmul_fp8, restated fp32 sigmoid router), %.1f ms each"
+                                    % (n, per * 1e3)}
+    if rank == 0:
+        print(json.dumps(out_line))
+    moe.close()
+    L.dsv4_cuda_shutdown()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------- sparse MLA (C3)
+
+MLA_METRIC = "sparse-MLA decode step HBM GB/s (config 3: 32768 positions, indexer 64x128 e4m3, top-2048, 64 heads x 576)"
+C3_N, C3_H, C3_D, C3_HI, C3_DI, C3_K = 32768, 64, 576, 64, 128, 2048
+# per sequence: e4m3 keys + the selected bf16 KV rows + q (f32, attention and
+# indexer) + head weights + the score vector written and read + the output
+C3_BYTES = C3_N * C3_DI + C3_K * C3_D * 2 + (C3_H * C3_D + C3_HI * C3_DI + C3_HI) * 4 + 2 * C3_N * 4 + \
+    C3_K * 4 + C3_H * C3_D * 4
+C3_FLOPS = 2 * (C3_N * C3_HI * C3_DI + 2 * C3_K * C3_H * C3_D)
+
+
+def run_mla(a):
+    import torch
+    import dsv4_b200 as B
+    rank, world, dist = dist_setup(a.gpus)
+    B.init()
+    bt = a.batch
+    nset = max(1, -(-4 // bt))                   # >= 4 distinct sequences: > 126 MB L2 every step
+    g = torch.Generator(device="cuda").manual_seed(0)
+    sets = []
+    for _ in range(nset):
+        kv = torch.randn((bt, C3_N, C3_D), generator=g, device="cuda").to(torch.bfloat16)
+        keys = torch.randn((bt, C3_N, C3_DI), generator=g, device="cuda").to(torch.float8_e4m3fn)
+        q = torch.randn((bt, C3_H, C3_D), generator=g, device="cuda")
+        qi = torch.randn((bt, C3_HI, C3_DI), generator=g, device="cuda")
+        w = torch.randn((bt, C3_HI), generator=g, device="cuda")
+        sets.append((kv, keys, q, qi, w))
+    sink = torch.randn(C3_H, generator=g, device="cuda")
+    scores = torch.empty((bt, C3_N), device="cuda")
+    idx = torch.empty((bt, C3_K), dtype=torch.int32, device="cuda")
+    o = torch.empty((bt, C3_H, C3_D), device="cuda")
+    scratch = torch.empty(B.sparse_attn_scratch(C3_H, C3_D, C3_K, bt), dtype=torch.uint8, device="cuda")
+    iscale = float(np.float32(1 / np.sqrt(np.float32(C3_DI))) * np.float32(1 / np.sqrt(np.float32(C3_HI))))
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(C3_D)))
+    st = torch.cuda.Stream()
+
+    def step(i):
+        kv, keys, q, qi, w = sets[i % nset]
+        B.indexer_score_dev(scores, qi, keys.view(torch.uint8), B.E4M3, C3_DI, C3_N * C3_DI, w, C3_HI, C3_DI,
+                            C3_N, iscale, bt, st)
+        B.topk_dev(idx, scores, C3_N, C3_K, bt, st)
+        B.sparse_attn_dev(o, q, kv.view(torch.int16), B.BF16, C3_N, sink, idx, C3_H, C3_D, C3_K, scale, bt,
+                          scratch, st)
+
+    W, K = max(a.warmup, 3), a.steps
+    with torch.cuda.stream(st):
+        for i in range(W):
+            step(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(torch.cuda.current_device()) as clk:
+        with torch.cuda.stream(st):
+            e0.record(st)
+            for i in range(K):
+                step(i)
+            e1.record(st)
+        torch.cuda.synchronize()
+    ms = max_over_ranks(dist, e0.elapsed_time(e1))
+    ms_step = ms / K
+    value = bt * C3_BYTES / (ms_step * 1e-3) / 1e9
+    # e2e: the reference-signature host calls, one sequence at a time (host
+    # keys widened to f32 and host KV as the reference's dsv4_indexer_score /
+    # dsv4_topk / dsv4_sparse_attn take them)
+    kv, keys, q, qi, w = sets[0]
+    kvh = kv[0].float().cpu().numpy()
+    kh = keys[0].float().cpu().numpy()
+    qh, qih, wh, sh = q[0].cpu().numpy(), qi[0].cpu().numpy(), w[0].cpu().numpy(), sink.cpu().numpy()
+    ne = 3
+    t0 = time.perf_counter()
+    for _ in range(ne):
+        sc = B.indexer_score(qih, kh, wh)
+        ii = B.topk(sc, C3_K)
+        B.sparse_attn(qh, kvh, sh, ii, scale)
+    e2e_s = (time.perf_counter() - t0) / ne
+    h2d = C3_HI * C3_DI * 4 + C3_N * C3_DI * 4 + C3_HI * 4 + C3_N * 4 + C3_H * C3_D * 4 + C3_N * C3_D * 4 + \
+        C3_H * 4 + C3_K * 4
+    d2h = C3_N * 4 + C3_K * 4 + C3_H * C3_D * 4
+    peak, src = peaks()
+    tc = 1622.1
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            tc = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        pass
+    flops_s = bt * C3_FLOPS / (ms_step * 1e-3)
+    out_line = {
+        "metric": MLA_METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms_step, "sequences_per_s": bt / (ms_step * 1e-3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "e4m3 keys / bf16 KV, f64 indexer dots, f32 attention",
+        "data": "synthetic (config 3 distributions)",
+        "config": {"workload": "mla config 3", "batch": bt, "positions": C3_N, "heads": C3_H, "d": C3_D,
+                   "index_heads": C3_HI, "index_dim": C3_DI, "topk": C3_K,
+                   "l2": "%d distinct sequence sets rotated (%.0f MB of keys + KV per step set)"
+                         % (nset, bt * (C3_N * C3_D * 2 + C3_N * C3_DI) / 1e6)},
+        "roofline": {"bound": "hbm", "achieved": value, "peak": peak, "unit": "GB/s", "frac": value / peak,
+                     "peak_source": src + " burst hbm_gbs", "bytes_per_unit": C3_BYTES,
+                     "scope": "indexer + top-k + attention per step (4 launches)",
+                     "flops_per_unit": C3_FLOPS, "achieved_tflops": flops_s / 1e12,
+                     "tensor_peak_tflops": tc, "tensor_frac": flops_s / 1e12 / tc,
+                     "note": "the indexer's dots run in exact f64 (bit-identical scores); that, not HBM, bounds it",
+                     "traffic": None},
+        "gpu_launches": 4 * K,
+        "clocks": clk.summary(),
+        "e2e": {"value": C3_BYTES / e2e_s / 1e9, "unit": "GB/s", "ms_per_step": e2e_s * 1e3,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "dsv4_cuda_indexer_score / topk / sparse_attn, one sequence, host buffers"},
+    }
+    if rank == 0 and world == 1 and not a.no_cpu:
+        out_line["cpu_baseline"] = cpu_mla_sample(qih, kh, wh, qh, kvh, sh, scale)
+    if rank == 0:
+        print(json.dumps(out_line))
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_mla_sample(qi, keys, w, q, kv, sink, scale, k_small=256):
+    """One config-3 sequence through the reference's own C (oracle/_ref):
+    dsv4_indexer_score at full size, dsv4_topk at k = 256 (its repeated
+    argmax is O(n k); the time is scaled by 2048 / 256 to the config's k),
+    dsv4_sparse_attn over the 2048 selected rows."""
+    import oracle as O
+    kind = "reference" if os.path.exists(O.REF_SO) else "port"
+    ref = O.Checker(kind)
+    t0 = time.perf_counter()
+    sc = ref.indexer_score(qi, keys, w, C3_HI, C3_DI)
+    t1 = time.perf_counter()
+    ref.topk(sc, k_small)
+    t2 = time.perf_counter()
+    ii = O.Checker("port").topk(sc, C3_K)
+    t3 = time.perf_counter()
+    ref.sparse_attn(q, kv, sink, ii, scale)
+    t4 = time.perf_counter()
+    per = (t1 - t0) + (t2 - t1) * (C3_K / k_small) + (t4 - t3)
+    return {"value": C3_BYTES / per / 1e9, "unit": "GB/s",
+            "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count())), "kind": kind,
+            "sample": "one sequence: indexer %.0f ms, top-%d %.0f ms scaled x%d, attention %.0f ms"
+                      % ((t1 - t0) * 1e3, k_small, (t2 - t1) * 1e3, C3_K // k_small, (t4 - t3) * 1e3)}
 
 
 # ------------------------------------------------------- reference arm
@@ -531,16 +864,21 @@ def main():
                     help="timed steps (default 256 decode tokens / 20000 GEMVs)")
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv_fp8"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv_fp8", "moe", "mla"])
+    ap.add_argument("--batch", type=int, default=1, help="mla: sequences per step (config 3: 1 or 8)")
     ap.add_argument("--context", type=int, default=512, help="decode: prompt tokens before timing")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     a = ap.parse_args()
     if a.steps is None:
-        a.steps = 256 if a.workload == "decode" else 20000
+        a.steps = {"decode": 256, "gemv_fp8": 20000, "moe": 200, "mla": 50}[a.workload]
     if a.impl == "reference":
         run_reference(a)
     elif a.workload == "decode":
         run_decode(a)
+    elif a.workload == "moe":
+        run_moe(a)
+    elif a.workload == "mla":
+        run_mla(a)
     else:
         run_gemv(a)
 

@@ -12,6 +12,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <vector>
@@ -139,7 +140,16 @@ struct PeerDev {
     float *mail;               // mine
     int *err;
     int rank, world, maxn;
+    unsigned spin;             // polls before a wait gives up
 };
+
+// Polls before a wait for a rank gives up: kSpinLimit, or $DSV4B_PEER_SPIN.
+unsigned peer_spin_limit()
+{
+    const char *e = getenv("DSV4B_PEER_SPIN");
+    const long v = e ? atol(e) : 0;
+    return v > 0 ? (unsigned)v : kSpinLimit;
+}
 
 struct PeerHost {
     PeerDev d;
@@ -191,7 +201,7 @@ __global__ void __launch_bounds__(256) k_peer_allreduce(PeerDev x, float *buf, i
             uint4 *w = reinterpret_cast<uint4 *>(x.mail + b * bsz + (size_t)r * slot) + i;
             uint4 u = ld_volatile_u4(w);
             while ((u.x == kSentinel || u.y == kSentinel || u.z == kSentinel || u.w == kSentinel) && !gave_up) {
-                if (++spins > kSpinLimit) {
+                if (++spins > x.spin) {
                     gave_up = true;
                     atomicExch(x.err, 1);
                     break;
@@ -218,6 +228,7 @@ int peer_open(void **out, int rank, int world, int maxn, void *comm, cudaStream_
     h->d.rank = rank;
     h->d.world = world;
     h->d.maxn = maxn;
+    h->d.spin = peer_spin_limit();
     const size_t words = (size_t)3 * world * maxn;
     bool ok = cudaMalloc(&h->base, words * 4) == cudaSuccess && cudaMalloc(&h->misc, 4096) == cudaSuccess &&
               cudaMemset(h->misc, 0, 4096) == cudaSuccess;
@@ -304,3 +315,64 @@ int peer_status(void *p)
 }
 
 }  // namespace dsv4b
+
+// One exchange of the peer kernel on ONE GPU with `world` ranks emulated: all
+// mailboxes are the same local buffer, rank 0 runs the kernel, and ranks
+// 1..world-1 have either stored their vectors beforehand (others_ready) or
+// never do (a rank that is gone), which the kernel must survive by giving up
+// after spin_limit polls. out[n] receives rank 0's result. Returns the status
+// word (0: every rank's values arrived, 1: a wait gave up) or -1.
+extern "C" int dsv4b_peer_selftest(int world, int n, unsigned spin_limit, int others_ready, const float *in,
+                                   float *out)
+{
+    using namespace dsv4b;
+    if (world < 2 || world > 64 || n <= 0 || (n & 3) || !in || !out || !spin_limit) return -1;
+    const size_t words = (size_t)3 * world * n;
+    void *mail = nullptr, *misc = nullptr, *buf = nullptr;
+    int rc = -1, err = 0;
+    PeerDev d = {};
+    if (cudaMalloc(&mail, words * 4) != cudaSuccess || cudaMalloc(&misc, 4096) != cudaSuccess ||
+        cudaMalloc(&buf, (size_t)n * 4) != cudaSuccess)
+        goto done;
+    if (cudaMemset(misc, 0, 4096) != cudaSuccess) goto done;
+    k_fill_u32<<<64, 256>>>(static_cast<unsigned *>(mail), words, kSentinel);
+    if (others_ready) {     // exchange 0 uses buffer 0: ranks 1.. store their slots, -0.0 sent as +0.0
+        std::vector<float> v((size_t)(world - 1) * n);
+        for (size_t i = 0; i < v.size(); i++) {
+            float f = in[(size_t)n + i];
+            unsigned u;
+            memcpy(&u, &f, 4);
+            if (u == kSentinel) f = 0.0f;
+            v[i] = f;
+        }
+        if (cudaMemcpy(static_cast<float *>(mail) + (size_t)n, v.data(), v.size() * 4, cudaMemcpyHostToDevice) !=
+            cudaSuccess)
+            goto done;
+    }
+    if (cudaMemcpy(buf, in, (size_t)n * 4, cudaMemcpyHostToDevice) != cudaSuccess) goto done;
+    {
+        std::vector<float *> pm(world, static_cast<float *>(mail));
+        char *m = static_cast<char *>(misc);
+        if (64 + 8 * world > 4096 || cudaMemcpy(m + 64, pm.data(), 8 * world, cudaMemcpyHostToDevice) != cudaSuccess)
+            goto done;
+        d.pmail = reinterpret_cast<float **>(m + 64);
+        d.mail = static_cast<float *>(mail);
+        d.err = reinterpret_cast<int *>(m);
+        d.rank = 0;
+        d.world = world;
+        d.maxn = n;
+        d.spin = spin_limit;
+        unsigned *seq = reinterpret_cast<unsigned *>(m + 32);     // step 0 (zeroed above)
+        k_peer_allreduce<<<16, 256>>>(d, static_cast<float *>(buf), n, seq, 1, 0);
+        if (cudaDeviceSynchronize() != cudaSuccess) goto done;
+    }
+    if (cudaMemcpy(out, buf, (size_t)n * 4, cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemcpy(&err, d.err, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+        goto done;
+    rc = err;
+done:
+    if (buf) cudaFree(buf);
+    if (misc) cudaFree(misc);
+    if (mail) cudaFree(mail);
+    return rc;
+}

@@ -211,6 +211,21 @@ dsv4b_model *dsv4_cuda_model_create_synthetic_sharded(const DSV4Cfg *c, int max_
  * -1 for a NULL model. Always 0 on one GPU. */
 int dsv4b_model_comm_status(const dsv4b_model *m);
 
+/* After a wait gave up, words a late rank still stores may sit in the
+ * mailboxes: the model must be freed and created again before it exchanges
+ * anything more. $DSV4B_PEER_SPIN sets the polls before a wait gives up
+ * (default 2^26, a few seconds). No reference counterpart. */
+
+/* Diagnostic: one peer exchange on ONE GPU with `world` ranks emulated in a
+ * local mailbox. Ranks 1..world-1 have stored in[r*n .. r*n+n) beforehand
+ * (others_ready) or never store (a rank that is gone, which the kernel must
+ * survive by giving up after spin_limit polls); rank 0 contributes in[0..n)
+ * and receives the rank-ordered sum in out[n]. Returns the status word (0 all
+ * arrived, 1 a wait gave up) or -1. n a multiple of 4. No reference
+ * counterpart. */
+int dsv4b_peer_selftest(int world, int n, unsigned spin_limit, int others_ready,
+                        const float *in, float *out);
+
 /* Device memory in use (bytes), for reporting the resident model size. */
 size_t dsv4_cuda_model_bytes(const dsv4b_model *m);
 

@@ -1,9 +1,9 @@
-"""Sharded decode over two GPUs (one process each): experts split along their
-inter dimension, q heads / o_groups and wo_b columns by rank, the LM head by
-vocabulary, NCCL all-reduces at the two exchange points of a layer. Every
-tensor of a rank is the matching slice of the single-GPU model of the same
-seed, so the greedy token stream must be the single-GPU one. Skipped below
-two devices."""
+"""Sharded decode over 2, 4 and 8 GPUs (one process each): experts split along
+their inter dimension, q heads / o_groups and wo_b columns by rank, the LM
+head by vocabulary, two sums per layer over NVLink peer memory and one argmax
+all-gather per token. Every tensor of a rank is the matching slice of the
+single-GPU model of the same seed, so the greedy token stream must be the
+single-GPU one. Each world size is skipped when the box has fewer GPUs."""
 import os
 import socket
 
@@ -51,15 +51,16 @@ def _rank(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_two_gpu_sharded_decode_matches_single_gpu():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharded_decode_matches_single_gpu(world):
     import torch
     import torch.multiprocessing as mp
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip("needs %d GPUs" % world)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     try:
@@ -71,8 +72,9 @@ def test_two_gpu_sharded_decode_matches_single_gpu():
             if p.is_alive():
                 p.kill()
     res = {}
-    for _ in range(2):
+    for _ in range(world):
         r, got, ref = q.get(timeout=10)
         res[r] = (got, ref)
-    assert res[0][0] == res[1][0], "ranks disagree"
+    for r in range(1, world):
+        assert res[r][0] == res[0][0], "rank %d disagrees" % r
     assert res[0][0] == res[0][1], "sharded %s vs single-GPU %s" % (res[0][0], res[0][1])

@@ -3,19 +3,28 @@
 //
 // Replaces the reference's k_mmq_fp8 / k_mmq_fp8_n (src/cuda/dsv4_cuda.cu:
 // 93-230) and widens it to the four formats dsv4_mmq dispatches on
-// (src/core/dsv4_matmul.c:516-591). Three kernels, one summation order
-// (gemv_core.cuh), so a token's result never depends on the kernel, the grid,
-// the batch or the group it ran in:
+// (src/core/dsv4_matmul.c:516-591). Three kernels:
 //   k_gemv_group  batch 1, up to 16 matrices per launch (mixed formats,
 //                 routed experts picked on the device, optional SwiGLU pair
-//                 epilogue). Each block streams a tile of rows: every
+//                 epilogue), one wave of two blocks per SM, each block a tile
+//                 of rows of one matrix. Every model matrix (FP8 with
+//                 power-of-two blocks of >= 128 columns, FP4 whose scales keep
+//                 the f16 decode exact, BF16; <= 64 units per row) runs on the
+//                 tensor cores (mma_tile, gemv_mma.cuh: mma.sync m16n8k16 with
+//                 x split into three exact pieces, the order written there).
+//                 Other shapes take the CUDA-core tile (group_tile): every
 //                 half-warp owns one or two 256-byte segments of the row, keeps
 //                 their x in registers and walks the tile's rows with eight
 //                 16-byte weight loads in flight per thread; segment sums meet
-//                 in shared memory and are added in double in segment order.
+//                 in shared memory and are added in double in segment order
+//                 (gemv_core.cuh).
 //   k_gemv_nt     nt tokens per weight pass (the batched dsv4_cuda_mmq_n), and
-//                 batch-1 shapes whose scale blocks are narrower than a lane.
+//                 batch-1 shapes whose scale blocks are narrower than a lane;
+//                 the segment order of gemv_core.cuh.
 //   k_gemv_generic any other shape (rows not a multiple of 16 bytes).
+// Each matrix has one order per shape class, independent of the grid, the
+// group it runs in and the launch, so a token's result never depends on how
+// its GEMVs were batched.
 #include <stdlib.h>
 #include <string.h>
 

@@ -768,19 +768,21 @@ static bool synth_layer(Synth &S, int Li)
     const int d = c.hidden, hd = c.head_dim, hc = c.hc_mult, mix = (2 + hc) * hc, H = c.n_heads;
     // this rank's share: heads (and so o_groups), the wo_b columns of those
     // groups, every expert's inter slice
-    const int G = S.world, r = S.rank, Hl = H / G, ogl = c.o_groups / G, orl = ogl * c.o_lora;
+    int sp[2 * DSV4B_SHARD_NDIM];
+    if (dsv4b_shard_plan(&c, S.world, S.rank, sp) < 0) return false;
+    const int *hs = sp + 2 * DSV4B_SHARD_HEADS, *qs = sp + 2 * DSV4B_SHARD_QROWS, *os = sp + 2 * DSV4B_SHARD_OLORA;
     l.has_comp = l.ratio != 0;
     l.has_idx = l.ratio == 4;
     l.attn_norm = S.f32n(d, 1.f, 0.1f);
     l.ffn_norm = S.f32n(d, 1.f, 0.1f);
-    l.sink = S.f32n_part(H, (size_t)r * Hl, Hl, 0.f, 1.f);
+    l.sink = S.f32n_part(H, (size_t)hs[0], hs[1], 0.f, 1.f);
     l.q_norm = S.f32n(c.q_lora, 1.f, 0.1f);
     l.kv_norm = S.f32n(hd, 1.f, 0.1f);
     l.wq_a = S.fp8(c.q_lora, d);
-    l.wq_b = S.fp8(H * hd, c.q_lora, r * Hl * hd, Hl * hd);
+    l.wq_b = S.fp8(H * hd, c.q_lora, qs[0], qs[1]);
     l.wkv = S.fp8(hd, d);
-    l.wo_a = S.fp8(c.o_groups * c.o_lora, H * hd / c.o_groups, r * orl, orl);
-    l.wo_b = S.fp8(d, c.o_groups * c.o_lora, 0, d, r * orl, orl);
+    l.wo_a = S.fp8(c.o_groups * c.o_lora, H * hd / c.o_groups, os[0], os[1]);
+    l.wo_b = S.fp8(d, c.o_groups * c.o_lora, 0, d, os[0], os[1]);
     if (l.has_comp) {
         l.ape = S.f32n((size_t)l.ratio * l.coff * hd, 0.f, 0.1f);
         l.cnorm = S.f32n(hd, 1.f, 0.1f);
@@ -812,12 +814,12 @@ static bool synth_layer(Synth &S, int Li)
     }
     // routed experts: one stream of codes per layer (every expert's w1, w3,
     // w2), then the scales; this rank keeps its inter slice of each expert
-    const size_t I = c.moe_inter / G, E = c.n_experts;
+    const size_t I = sp[2 * DSV4B_SHARD_INTER + 1], E = c.n_experts;
     const size_t cw = I * d / 2, cper = 3 * cw, sw = I * d / 32, sper = 3 * sw;
     uint8_t *codes = (uint8_t *)dalloc(m, E * cper), *scales = (uint8_t *)dalloc(m, E * sper);
     if (!codes || !scales) return false;
     const uint64_t ckey = S.next_key();
-    k_synth_experts<<<1184, 256, 0, m->stream>>>(codes, (int)E, d, c.moe_inter, r, G, 0.02f / 0.015625f,
+    k_synth_experts<<<1184, 256, 0, m->stream>>>(codes, (int)E, d, c.moe_inter, sp[2 * DSV4B_SHARD_INTER], (int)I, 0.02f / 0.015625f,
                                                    ckey);                    // e2m1 of N(0,0.02) / 2^-6
     S.launched();
     S.next_key();
@@ -838,10 +840,10 @@ static bool synth_layer(Synth &S, int Li)
     mo.w2tab = t + 4 * E; mo.s2tab = t + 5 * E;
     mo.efmt = DSV4_WFP4; mo.eblk_r = 1; mo.eblk_c = 32;
     mo.ef16s = 1;                                               // every scale is 2^-6
-    const int Is = c.moe_inter * c.n_shared, Isl = Is / G;
-    mo.sh[0] = S.fp8(Is, d, r * Isl, Isl);
-    mo.sh[1] = S.fp8(Is, d, r * Isl, Isl);
-    mo.sh[2] = S.fp8(d, Is, 0, d, r * Isl, Isl);
+    const int Is = c.moe_inter * c.n_shared, Is0 = sp[2 * DSV4B_SHARD_SHARED_INTER], Isl = sp[2 * DSV4B_SHARD_SHARED_INTER + 1];
+    mo.sh[0] = S.fp8(Is, d, Is0, Isl);
+    mo.sh[1] = S.fp8(Is, d, Is0, Isl);
+    mo.sh[2] = S.fp8(d, Is, 0, d, Is0, Isl);
     mo.has_shared = 1;
     mo.n_experts = c.n_experts;
     mo.topk = c.topk;
@@ -872,6 +874,19 @@ extern "C" int dsv4b_shard_check(const DSV4Cfg *c, int world)
                     (c->moe_inter * c->n_shared) % world == 0 && isl % 128 == 0 && c->vocab % world == 0 &&
                     c->n_shared >= 1;
     return ok ? 0 : -1;
+}
+
+extern "C" int dsv4b_shard_plan(const DSV4Cfg *c, int world, int rank, int *out)
+{
+    if (!out || dsv4b_shard_check(c, world) != 0 || rank < 0 || rank >= world) return -1;
+    const int G = world, r = rank, Hl = c->n_heads / G, ogl = c->o_groups / G, orl = ogl * c->o_lora;
+    const int il = c->moe_inter / G, isl = c->moe_inter * c->n_shared / G, vl = c->vocab / G;
+    const int share[DSV4B_SHARD_NDIM] = { Hl, Hl * c->head_dim, ogl, orl, il, isl, vl };
+    for (int k = 0; k < DSV4B_SHARD_NDIM; k++) {
+        out[2 * k] = r * share[k];
+        out[2 * k + 1] = share[k];
+    }
+    return DSV4B_SHARD_NDIM;
 }
 
 extern "C" size_t dsv4b_nccl_id_bytes(void) { return comm_id_bytes(); }
@@ -911,11 +926,14 @@ extern "C" dsv4b_model *dsv4_cuda_model_create_synthetic_sharded(const DSV4Cfg *
     S.world = world;
     bool ok = true;
     for (int L = 0; L < c->n_layers && ok; L++) ok = dsv4b::synth_layer(S, L);
-    const int d = c->hidden, hc = c->hc_mult, vl = c->vocab / world;
+    const int d = c->hidden, hc = c->hc_mult;
+    int sp[2 * DSV4B_SHARD_NDIM];
+    dsv4b_shard_plan(c, world, rank, sp);
+    const int *vs = sp + 2 * DSV4B_SHARD_VOCAB;
     if (ok) {
         m->emb_wdt = DSV4_WBF16;
         m->embed = S.bf16(c->vocab, d, 1.0f).w;
-        m->head = S.bf16(c->vocab, d, 0.02f, rank * vl, vl);
+        m->head = S.bf16(c->vocab, d, 0.02f, vs[0], vs[1]);
         m->norm = S.f32n(d, 1.f, 0.1f);
         m->hch_fn = S.f32n((size_t)hc * hc * d, 0.f, 0.02f);
         m->hch_base = S.f32n(hc, 0.f, 0.5f);

@@ -68,7 +68,7 @@ __global__ void k_argmax_pair(float *pair, const float *pv, const int *pi, int n
 __global__ void k_synth(void *dst, size_t n, int kind, float a, float b, uint64_t key);
 __global__ void k_synth_slice(void *dst, int nrows, int ncols, int kind, float a, float b, uint64_t key,
                               size_t base, size_t gstride);
-__global__ void k_synth_experts(uint8_t *dst, int n_experts, int hidden, int inter, int rank, int world, float b,
+__global__ void k_synth_experts(uint8_t *dst, int n_experts, int hidden, int inter, int i0, int il, float b,
                                 uint64_t key);
 __global__ void k_synth_tid2eid(int64_t *t, int vocab, int topk, int n_experts, uint64_t key);
 

@@ -104,16 +104,16 @@ __global__ void k_synth_slice(void *dst, int nrows, int ncols, int kind, float a
     }
 }
 
-// The routed experts' e2m1 codes of one layer for rank `rank` of `world`:
-// the whole layer is one stream of packed bytes, expert e at e * cper, its
-// w1, w3 ([inter][hidden / 2] bytes) and w2 ([hidden][inter / 2]) one after
-// the other. A rank keeps rows [r I / G, (r + 1) I / G) of w1 and w3 and the
-// same columns of w2, stored as one compact block per expert:
-// [w1 slice][w3 slice][w2 slice].
-__global__ void k_synth_experts(uint8_t *dst, int n_experts, int hidden, int inter, int rank, int world, float b,
+// The routed experts' e2m1 codes of one layer for one rank's inter slice
+// [i0, i0 + il) (i0 even): the whole layer is one stream of packed bytes,
+// expert e at e * cper, its w1, w3 ([inter][hidden / 2] bytes) and w2
+// ([hidden][inter / 2]) one after the other. A rank keeps rows [i0, i0 + il)
+// of w1 and w3 and the same columns of w2, stored as one compact block per
+// expert: [w1 slice][w3 slice][w2 slice].
+__global__ void k_synth_experts(uint8_t *dst, int n_experts, int hidden, int inter, int i0, int il_, float b,
                                 uint64_t key)
 {
-    const size_t il = inter / world, cw = (size_t)inter * hidden / 2, cper = 3 * cw;
+    const size_t il = il_, cw = (size_t)inter * hidden / 2, cper = 3 * cw;
     const size_t cwl = il * hidden / 2, cperl = 3 * cwl, n = (size_t)n_experts * cperl;
     const size_t w2rb = inter / 2, w2rbl = il / 2;
     for (size_t lb = blockIdx.x * (size_t)blockDim.x + threadIdx.x; lb < n; lb += (size_t)gridDim.x * blockDim.x) {
@@ -121,10 +121,10 @@ __global__ void k_synth_experts(uint8_t *dst, int n_experts, int hidden, int int
         size_t gb;
         if (rem < 2 * cwl) {
             const size_t jm = rem / cwl, off = rem - jm * cwl, row = off / (hidden / 2), cb = off - row * (hidden / 2);
-            gb = e * cper + jm * cw + (rank * il + row) * (hidden / 2) + cb;
+            gb = e * cper + jm * cw + (i0 + row) * (hidden / 2) + cb;
         } else {
             const size_t off = rem - 2 * cwl, row = off / w2rbl, cb = off - row * w2rbl;
-            gb = e * cper + 2 * cw + row * w2rb + rank * w2rbl + cb;
+            gb = e * cper + 2 * cw + row * w2rb + i0 / 2 + cb;
         }
         const float2 v = make_float2(b * nrand(key, 2 * gb), b * nrand(key, 2 * gb + 1));
         dst[lb] = (uint8_t)__nv_cvt_float2_to_fp4x2(v, __NV_E2M1, cudaRoundNearest);

@@ -85,6 +85,7 @@ def _declare(L):
         "dsv4_cuda_model_bytes": ([vp], sz),
         "dsv4_cuda_model_step_kernels": ([vp], i),
         "dsv4b_shard_check": ([vp, i], i),
+        "dsv4b_shard_plan": ([vp, i, i, vp], i),
         "dsv4b_model_comm_status": ([vp], i),
         "dsv4b_nccl_id_bytes": ([], sz),
         "dsv4b_nccl_unique_id": ([vp], i),
@@ -334,6 +335,19 @@ def nccl_unique_id():
 def shard_check(cfg, world):
     """True when a model of ctypes config cfg splits over world GPUs."""
     return lib().dsv4b_shard_check(C.addressof(cfg), int(world)) == 0
+
+
+# the split dimensions of dsv4b_shard_plan, in its order
+SHARD_DIMS = ("heads", "q_rows", "o_groups", "o_lora", "inter", "shared_inter", "vocab")
+
+
+def shard_plan(cfg, world, rank):
+    """{dimension: (first, count)} of rank's share of each split dimension
+    (dsv4b_shard_plan), or None when cfg does not split over world GPUs."""
+    out = (C.c_int * (2 * len(SHARD_DIMS)))()
+    if lib().dsv4b_shard_plan(C.addressof(cfg), int(world), int(rank), out) != len(SHARD_DIMS):
+        return None
+    return {k: (out[2 * j], out[2 * j + 1]) for j, k in enumerate(SHARD_DIMS)}
 
 
 class Model:

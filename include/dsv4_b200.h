@@ -190,6 +190,19 @@ dsv4b_model *dsv4_cuda_model_create_synthetic(const DSV4Cfg *c, int max_pos,
  * shared expert's of 128 blocks, the vocabulary), else -1. No device needed. */
 int dsv4b_shard_check(const DSV4Cfg *c, int world);
 
+/* This rank's share of every split dimension as (first, count) pairs,
+ * out[2 * k], out[2 * k + 1] for k = DSV4B_SHARD_HEADS .. DSV4B_SHARD_VOCAB:
+ * q heads (and the sink), wq_b rows, o_groups, wo_a rows = wo_b columns (the
+ * groups' o_lora slices), each routed expert's inter slice, the shared
+ * expert's inter slice, LM-head rows. Ranks' shares tile each dimension in
+ * rank order. Returns DSV4B_SHARD_NDIM, or -1 when c does not split over
+ * world GPUs or rank is out of range. No device needed. */
+enum {
+    DSV4B_SHARD_HEADS = 0, DSV4B_SHARD_QROWS, DSV4B_SHARD_OGROUPS, DSV4B_SHARD_OLORA,
+    DSV4B_SHARD_INTER, DSV4B_SHARD_SHARED_INTER, DSV4B_SHARD_VOCAB, DSV4B_SHARD_NDIM
+};
+int dsv4b_shard_plan(const DSV4Cfg *c, int world, int rank, int *out);
+
 /* Size of the communicator id rank 0 creates and every rank passes to
  * dsv4_cuda_model_create_synthetic_sharded (NCCL's unique id, 128 bytes), and
  * its creation. NCCL is opened at run time; -1 when it cannot be. */

@@ -218,11 +218,14 @@ def decode_bytes_per_token(d, pos):
     return total
 
 
-def cpu_decode_sample(n_pos, warm=2):
+def cpu_decode_sample(n_pos, warm=2, prompt_len=0):
     """The reference's dsv4_layer_forward on a 3-layer Flash-geometry model
-    (compress ratios 0 / 4 / 128, all 256 experts, vocab 129280) for n_pos
-    positions from a one-token prompt. Returns (seconds per 43-layer token,
-    per-position times, description)."""
+    (compress ratios 0 / 4 / 128, all 256 experts, vocab 129280): without a
+    prompt, n_pos positions after `warm` from a one-token prompt; with
+    prompt_len, the GPU arm's random prompt of that length first (untimed),
+    then `warm` and n_pos timed greedy positions, i.e. positions prompt_len +
+    warm .. prompt_len + warm + n_pos - 1. Returns (seconds per 43-layer
+    token, per-position times, description, first timed position)."""
     import oracle as O
     import dsv4_model as M
     full = layer_ratios(M.flash_config())
@@ -231,16 +234,27 @@ def cpu_decode_sample(n_pos, warm=2):
     t0 = time.perf_counter()
     sm = M.SyntheticModel(d, seed=0, fast=True)
     t_build = time.perf_counter() - t0
-    tl, th, _ = O.model_decode_timed_ref(sm, n_pos + warm)
-    tl, th = tl[warm:], th[warm:]
+    t0 = time.perf_counter()
+    if prompt_len:
+        prompt = np.random.default_rng(0).integers(0, d["vocab"], prompt_len).astype(np.int32)
+        tl, th, _ = O.model_decode_timed_ref(sm, n_pos + warm, prompt=prompt)
+        first = prompt_len + warm
+    else:
+        tl, th, _ = O.model_decode_timed_ref(sm, n_pos + warm)
+        first = warm
+    t_run = time.perf_counter() - t0
+    tl, th = tl[first:first + n_pos], th[first:first + n_pos]
     per = tl[:, 0] * count[0] + tl[:, 1] * count[4] + tl[:, 2] * count[128] + th
     desc = ("reference dsv4_layer_forward + hc_head/norm/LM head/argmax (oracle/_ref) on a 3-layer "
-            "Flash-geometry sample (ratios 0/4/128, 256 experts, vocab 129280), %d positions after %d "
-            "warm-up from position 0, per-layer times scaled to the 43-layer mix (%d/%d/%d); "
-            "OMP_NUM_THREADS=%s; sample build %.0f s"
-            % (n_pos, warm, count[0], count[4], count[128],
-               os.environ.get("OMP_NUM_THREADS", "all %d" % os.cpu_count()), t_build))
-    return float(np.sum(per) / n_pos), per, desc
+            "Flash-geometry sample (ratios 0/4/128, 256 experts, vocab 129280), positions %d..%d%s, "
+            "per-layer times scaled to the 43-layer mix (%d/%d/%d); OMP_NUM_THREADS=%s; sample build "
+            "%.0f s, run %.0f s"
+            % (first, first + n_pos - 1,
+               " after the GPU arm's %d-token prompt (untimed)" % prompt_len if prompt_len
+               else " after %d warm-up from position 0" % warm,
+               count[0], count[4], count[128],
+               os.environ.get("OMP_NUM_THREADS", "all %d" % os.cpu_count()), t_build, t_run))
+    return float(np.sum(per) / n_pos), per, desc, first
 
 
 def run_decode(a):
@@ -320,7 +334,7 @@ def run_decode(a):
         "dtype": "fp8 e4m3 / fp4 e2m1 / bf16 weights, f32 activations, f64 row sums",
         "data": "synthetic (random-init weights generated on device, random 512-token prompt)",
         "config": {"workload": "decode config 5 (Flash-scale synthetic)", "batch": 1,
-                   "context": "%d-token prompt, decode positions %d..%d" % (P, P + W, P + W + K - 1),
+                   "context": "%d-token prompt" % P, "positions": "%d..%d" % (P + W, P + W + K - 1),
                    "layers": d["n_layers"], "hidden": d["hidden"], "experts": d["n_experts"],
                    "topk": d["topk"], "vocab": d["vocab"],
                    "resident_gb": round(resident / 1e9, 1), "create_s": round(t_create, 1),
@@ -345,7 +359,7 @@ def run_decode(a):
                 "api": "dsv4_cuda_model_decode (host token, pos -> host next token), wall clock"},
     }
     if rank == 0 and world == 1 and not a.no_cpu:
-        s_tok, _, desc = cpu_decode_sample(8)
+        s_tok, _, desc, _ = cpu_decode_sample(8)
         out["cpu_baseline"] = {"value": 1.0 / s_tok, "unit": "tok/s",
                                "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count())),
                                "kind": "reference", "sample": desc}
@@ -824,15 +838,22 @@ def run_reference(a):
     if rank != 0:
         return
     if a.workload == "decode":
-        n = max(4, min(a.steps, 32))                 # bounded sample: minutes, not hours
-        s_tok, per, desc = cpu_decode_sample(n, warm=max(1, min(a.warmup, 4)))
+        # the GPU arm's first positions after the same prompt and warm-up (a
+        # bounded sample of them: minutes, not hours)
+        n = max(4, min(a.steps, 32))
+        W = max(a.warmup, 3)
+        s_tok, per, desc, first = cpu_decode_sample(n, warm=W, prompt_len=a.context)
         v = 1.0 / s_tok
         print(json.dumps({
             "metric": DECODE_METRIC, "value": v, "unit": "tok/s", "impl": "reference",
-            "n_gpus": a.gpus, "steps": n, "warmup": a.warmup, "ms_per_step": s_tok * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "n_gpus": a.gpus, "steps": n, "warmup": W, "ms_per_step": s_tok * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "fp8 e4m3 / fp4 e2m1 / bf16 weights, f32 activations, f64 row sums",
-            "data": "synthetic", "config": {"workload": "decode config 5 (Flash-scale synthetic)", "batch": 1},
+            "data": "synthetic (random-init weights, the GPU arm's random %d-token prompt)" % a.context,
+            "config": {"workload": "decode config 5 (Flash-scale synthetic)", "batch": 1,
+                       "context": "%d-token prompt" % a.context,
+                       "positions": "%d..%d" % (first, first + n - 1),
+                       "layers": "43 (3 timed, per-layer times scaled to the 43-layer mix)"},
             "cpu_baseline": {"value": v, "unit": "tok/s",
                              "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count())),
                              "kind": "reference", "sample": desc},

@@ -304,12 +304,30 @@ def model_greedy_ref(sm, tokens, n_gen, max_pos):
     return out[:n], lg[:n]
 
 
-def model_decode_timed_ref(sm, n_pos, first_token=1, max_pos=None):
+def model_decode_timed_ref(sm, n_pos, first_token=1, max_pos=None, prompt=None):
     """Per-layer and head wall times (seconds) of the REFERENCE's decode loop
     (dsv4_layer_forward per layer, then hc_head + norm + LM head + argmax)
-    over positions 0..n_pos-1 of model sm. Returns (t_layer [n_pos][n_layers],
-    t_head [n_pos], tokens)."""
+    over positions 0..n_pos-1 of model sm. With a prompt (int32 tokens), the
+    prompt is fed first and n_pos greedy positions follow; the rows then cover
+    all len(prompt) + n_pos positions (t_head from len(prompt) - 1 on).
+    Returns (t_layer [positions][n_layers], t_head [positions], tokens)."""
     lib = C.CDLL(REF_SO)
+    if prompt is not None:
+        prompt = np.ascontiguousarray(prompt, np.int32)
+        g = lib.dsv4ref_decode_timed_prompt
+        g.argtypes = [_vp, _vp, _vp, _vp, _i, _i32p, _i, _i, _i32p,
+                      np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS"),
+                      np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")]
+        g.restype = _i
+        npos = len(prompt) + n_pos
+        tl = np.zeros((npos, sm.d["n_layers"]), np.float64)
+        th = np.zeros(npos, np.float64)
+        out = np.empty(n_pos + 1, np.int32)
+        n = g(C.addressof(sm.cfg), C.addressof(sm.mw), C.addressof(sm.layers), C.addressof(sm.experts),
+              max_pos or npos + 1, prompt, len(prompt), n_pos, out, tl, th)
+        if n < 0:
+            raise RuntimeError("reference driver failed")
+        return tl, th, out[:n]
     f = lib.dsv4ref_decode_timed
     f.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i, _i32p,
                   np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS"),

@@ -125,3 +125,15 @@ int dsv4ref_decode_timed(const DSV4Cfg *c, const DSV4ModelW *mw, const DSV4Layer
 {
     return run(c, mw, lw, ex, max_pos, &first_token, 1, n_pos - 1, out_tokens, NULL, t_layer, t_head);
 }
+
+/* The same timed loop after a prompt: tokens[0..n_prompt) are fed first (the
+ * reference's prompt path, layer calls only), then n_gen greedy positions.
+ * t_layer / t_head are indexed by position (n_prompt + n_gen rows); t_head is
+ * written from position n_prompt - 1 on. The like-for-like CPU arm of the
+ * decode benchmark, which times the GPU's positions after the same prompt. */
+int dsv4ref_decode_timed_prompt(const DSV4Cfg *c, const DSV4ModelW *mw, const DSV4LayerW *lw,
+                                const DSV4ExpertW *ex, int max_pos, const int *tokens, int n_prompt, int n_gen,
+                                int *out_tokens, double *t_layer, double *t_head)
+{
+    return run(c, mw, lw, ex, max_pos, tokens, n_prompt, n_gen, out_tokens, NULL, t_layer, t_head);
+}

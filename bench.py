@@ -55,7 +55,10 @@ GEMV_METRIC = "FP8 block-scaled GEMV HBM GB/s (config 1, 4096x7168 e4m3, batch 1
 # DRAM bytes (read + write) per unit from an ncu capture of the same kernel
 # and workload, or None where none was taken.
 TRAFFIC_C1 = 29456384          # one config-1 GEMV launch (ncu dram__bytes_read + write)
-TRAFFIC_DECODE = None
+# One decode token's DRAM bytes (read + write, every launch of the token) from
+# an ncu capture at an early prompt position, and the algorithmic bytes of
+# that position; a timed position adds the algorithmic difference (its KV rows).
+TRAFFIC_DECODE = (11.2048e9, 11.1257e9)
 
 
 def peaks():
@@ -351,7 +354,12 @@ def run_decode(a):
                      "frac": ach / peak,
                      "peak_source": src + " burst hbm_gbs" + (" x %d GPUs" % world if world > 1 else ""),
                      "scope": "whole decode token (one graph replay, %d kernels)" % launches_per_step,
-                     "bytes_per_unit": bytes_tok, "traffic": TRAFFIC_DECODE},
+                     "bytes_per_unit": bytes_tok,
+                     "traffic": TRAFFIC_DECODE[0] + (bytes_tok - TRAFFIC_DECODE[1]) if world == 1 else None,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum over one token's "
+                                       "launches (profiles/decode_flash_c5_traffic.md), shifted to these "
+                                       "positions by their algorithmic KV bytes" if world == 1 else
+                                       "not captured for the sharded step"},
         "gpu_launches": launches_per_step * K,
         "clocks": clk.summary(),
         "e2e": {"value": 1.0 / e2e_s, "unit": "tok/s", "ms_per_step": e2e_s * 1e3,

@@ -50,6 +50,29 @@ C1_BYTES = C1_ROWS * C1_COLS + 32 * 56 + C1_COLS * 4 + C1_ROWS * 4
 NCOPY = 8
 
 DECODE_METRIC = "batch-1 decode tok/s (Flash-scale synthetic, config 5)"
+
+
+def decode_metric(batch):
+    return DECODE_METRIC if batch == 1 else "batch-%d decode tok/s (Flash-scale synthetic, config 5)" % batch
+
+
+def expected_experts(d, batch):
+    """Expected distinct routed experts of a layer when `batch` tokens each
+    pick topk of n_experts uniformly: the experts a batched step must read."""
+    E, K = d["n_experts"], d["topk"]
+    return E * (1.0 - (1.0 - K / E) ** batch)
+
+
+def decode_bytes_per_step(d, pos, batch):
+    """Algorithmic HBM bytes of one batched step: the weights once (the routed
+    experts as the expected distinct ones of the batch), every sequence's KV."""
+    one = decode_bytes_per_token(d, pos)
+    if batch == 1:
+        return one
+    per_expert = 3 * fp4_bytes(d["moe_inter"], d["hidden"])
+    nl = len(layer_ratios(d))
+    kv = decode_bytes_per_token(d, pos) - decode_bytes_per_token(d, 0)
+    return one + nl * (expected_experts(d, batch) - d["topk"]) * per_expert + (batch - 1) * kv
 GEMV_METRIC = "FP8 block-scaled GEMV HBM GB/s (config 1, 4096x7168 e4m3, batch 1)"
 
 # DRAM bytes (read + write) per unit from an ncu capture of the same kernel
@@ -268,11 +291,16 @@ def run_decode(a):
     L = B.init()
     d = M.flash_config()
     W, K, P = max(a.warmup, 3), a.steps, a.context
+    NB = a.batch
+    if NB > 1 and world > 1:
+        raise SystemExit("--batch > 1 runs on one GPU")
     n_e2e = max(16, min(K, 128))
     max_pos = P + W + K + n_e2e + 8
     cfg = M.ConfigOnly(d)
     t0 = time.perf_counter()
-    if world > 1:
+    if NB > 1:
+        model = B.Model(cfg, max_pos, synthetic_seed=1234, n_seq=NB)
+    elif world > 1:
         # one model sharded over the ranks: experts by inter slice, heads and
         # o_groups, wo_b columns, the LM head's vocabulary (NCCL exchanges)
         nid = [B.nccl_unique_id() if rank == 0 else None]
@@ -283,7 +311,12 @@ def run_decode(a):
     t_create = time.perf_counter() - t0
     resident = model.device_bytes()
     prompt = np.random.default_rng(0).integers(0, d["vocab"], P).astype(np.int32)
-    model.begin(prompt)
+    if NB > 1:
+        # sequence 0 takes the batch-1 prompt, the others their own
+        rest = np.random.default_rng(1).integers(0, d["vocab"], (NB - 1, P)).astype(np.int32)
+        model.begin_batch(np.concatenate([prompt[None, :], rest]))
+    else:
+        model.begin(prompt)
     launches_per_step = L.dsv4_cuda_model_step_kernels(model.h)
     stream = torch.cuda.Stream()
     sp = stream.cuda_stream
@@ -308,35 +341,49 @@ def run_decode(a):
     if dist:
         dist.barrier()
     ms_step = ms / K
-    value = K / (ms * 1e-3)            # tokens of the one sequence all ranks decode
+    value = NB * K / (ms * 1e-3)       # tokens of the sequences all ranks decode
 
-    # e2e through the host-driven entry (host token/pos in, host token out)
-    tok = np.zeros(1, np.int32)
-    B.check(L.dsv4_cuda_model_step(model.h, tok.ctypes.data, None), "dsv4_cuda_model_step")
-    pos = P + W + K + 1
-    t = int(tok[0])
-    for _ in range(3):
-        t = model.decode(t, pos)
+    # e2e through the host-driven entry (host tokens/pos in, host tokens out)
+    pos = P + W + K
+    if NB > 1:
+        t = np.zeros(NB, np.int32)
+        B.check(L.dsv4b_model_decode_batch(model.h, np.zeros(NB, np.int32).ctypes.data, pos, t.ctypes.data),
+                "dsv4b_model_decode_batch")
         pos += 1
-    t0 = time.perf_counter()
-    for _ in range(n_e2e):
-        t = model.decode(t, pos)
+        for _ in range(3):
+            t = model.decode_batch(t, pos)
+            pos += 1
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            t = model.decode_batch(t, pos)
+            pos += 1
+    else:
+        tok = np.zeros(1, np.int32)
+        B.check(L.dsv4_cuda_model_step(model.h, tok.ctypes.data, None), "dsv4_cuda_model_step")
         pos += 1
+        t = int(tok[0])
+        for _ in range(3):
+            t = model.decode(t, pos)
+            pos += 1
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            t = model.decode(t, pos)
+            pos += 1
     e2e_s = (time.perf_counter() - t0) / n_e2e
     e2e_s = max_over_ranks(dist, e2e_s)
 
     peak, src = peaks()
     peak *= world                      # the ranks' HBM together
-    bytes_tok = np.mean([decode_bytes_per_token(d, P + W + i) for i in range(0, K, max(1, K // 16))])
+    bytes_tok = np.mean([decode_bytes_per_step(d, P + W + i, NB) for i in range(0, K, max(1, K // 16))])
     ach = bytes_tok / (ms_step * 1e-3) / 1e9
     out = {
-        "metric": DECODE_METRIC,
+        "metric": decode_metric(NB),
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None,
         "dtype": "fp8 e4m3 / fp4 e2m1 / bf16 weights, f32 activations, f64 row sums",
         "data": "synthetic (random-init weights generated on device, random 512-token prompt)",
-        "config": {"workload": "decode config 5 (Flash-scale synthetic)", "batch": 1,
+        "config": {"workload": "decode config 5 (Flash-scale synthetic)", "batch": NB,
                    "context": "%d-token prompt" % P, "positions": "%d..%d" % (P + W, P + W + K - 1),
                    "layers": d["n_layers"], "hidden": d["hidden"], "experts": d["n_experts"],
                    "topk": d["topk"], "vocab": d["vocab"],
@@ -349,24 +396,34 @@ def run_decode(a):
                                    "all-gather per token"
                                    % (world, "NCCL all-reduce: DSV4B_PEER=0"
                                       if os.environ.get("DSV4B_PEER") == "0" else "CUDA IPC mailboxes")
-                                   if world > 1 else "single GPU")},
+                                   if world > 1 else
+                                   "single GPU" + (", %d sequences stepped together (one GEMV item per "
+                                                   "sequence, every other launch over all of them)" % NB
+                                                   if NB > 1 else ""))},
         "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
                      "frac": ach / peak,
                      "peak_source": src + " burst hbm_gbs" + (" x %d GPUs" % world if world > 1 else ""),
-                     "scope": "whole decode token (one graph replay, %d kernels)" % launches_per_step,
+                     "scope": ("whole decode token (one graph replay, %d kernels)" % launches_per_step
+                               if NB == 1 else "whole batched step of %d tokens (one graph replay, %d kernels; "
+                               "routed experts counted as the expected %.0f distinct per layer)"
+                               % (NB, launches_per_step, expected_experts(d, NB))),
                      "bytes_per_unit": bytes_tok,
-                     "traffic": TRAFFIC_DECODE[0] + (bytes_tok - TRAFFIC_DECODE[1]) if world == 1 else None,
+                     "traffic": (TRAFFIC_DECODE[0] + (bytes_tok - TRAFFIC_DECODE[1])
+                                 if world == 1 and NB == 1 else None),
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum over one token's "
                                        "launches (profiles/decode_flash_c5_traffic.md), shifted to these "
-                                       "positions by their algorithmic KV bytes" if world == 1 else
-                                       "not captured for the sharded step"},
+                                       "positions by their algorithmic KV bytes" if world == 1 and NB == 1
+                                       else "not captured for this step"},
         "gpu_launches": launches_per_step * K,
         "clocks": clk.summary(),
-        "e2e": {"value": 1.0 / e2e_s, "unit": "tok/s", "ms_per_step": e2e_s * 1e3,
-                "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
-                "api": "dsv4_cuda_model_decode (host token, pos -> host next token), wall clock"},
+        "e2e": {"value": NB / e2e_s, "unit": "tok/s", "ms_per_step": e2e_s * 1e3,
+                "h2d_bytes_per_step": 8 * NB, "d2h_bytes_per_step": 4 * NB,
+                "api": ("dsv4_cuda_model_decode (host token, pos -> host next token), wall clock" if NB == 1 else
+                        "dsv4b_model_decode_batch (host tokens, pos -> host next tokens), wall clock")},
     }
     if rank == 0 and world == 1 and not a.no_cpu:
+        # the reference decodes one sequence at a time: its tok/s is the
+        # batch-1 rate whatever the batch
         s_tok, _, desc, _ = cpu_decode_sample(8)
         out["cpu_baseline"] = {"value": 1.0 / s_tok, "unit": "tok/s",
                                "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count())),
@@ -853,15 +910,19 @@ def run_reference(a):
         s_tok, per, desc, first = cpu_decode_sample(n, warm=W, prompt_len=a.context)
         v = 1.0 / s_tok
         print(json.dumps({
-            "metric": DECODE_METRIC, "value": v, "unit": "tok/s", "impl": "reference",
+            "metric": decode_metric(a.batch), "value": v, "unit": "tok/s", "impl": "reference",
             "n_gpus": a.gpus, "steps": n, "warmup": W, "ms_per_step": s_tok * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "fp8 e4m3 / fp4 e2m1 / bf16 weights, f32 activations, f64 row sums",
             "data": "synthetic (random-init weights, the GPU arm's random %d-token prompt)" % a.context,
-            "config": {"workload": "decode config 5 (Flash-scale synthetic)", "batch": 1,
+            "config": {"workload": "decode config 5 (Flash-scale synthetic)", "batch": a.batch,
                        "context": "%d-token prompt" % a.context,
                        "positions": "%d..%d" % (first, first + n - 1),
-                       "layers": "43 (3 timed, per-layer times scaled to the 43-layer mix)"},
+                       "layers": "43 (3 timed, per-layer times scaled to the 43-layer mix)",
+                       "batching": ("the reference decodes one sequence at a time (its batched layer, "
+                                    "dsv4_layer_forward_n, takes tokens of one sequence): %d sequences take "
+                                    "%d times one, so its tok/s is the batch-1 rate" % (a.batch, a.batch)
+                                    if a.batch > 1 else "one sequence")},
             "cpu_baseline": {"value": v, "unit": "tok/s",
                              "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count())),
                              "kind": "reference", "sample": desc},
@@ -894,7 +955,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "gemv_fp8", "moe", "mla"])
-    ap.add_argument("--batch", type=int, default=1, help="mla: sequences per step (config 3: 1 or 8)")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="decode: sequences stepped together (config 5: 1 or 32); mla: sequences per step "
+                         "(config 3: 1 or 8)")
     ap.add_argument("--context", type=int, default=512, help="decode: prompt tokens before timing")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     a = ap.parse_args()

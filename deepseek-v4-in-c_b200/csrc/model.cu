@@ -65,6 +65,12 @@ struct dsv4b_model {
     int nx, xcall;             // exchanges per step; the next one's index
     float *am_pair, *am_gather;
     int n_prompt;
+    // a batch: nseq sequences decoded in lockstep (the same positions), each
+    // with its own activations, caches, step state and tokens; per-sequence
+    // buffers are packed (sequence b at b times the one-sequence size), the
+    // MoE scratch s_ms floats apart
+    int nseq;
+    long s_ms;
     std::vector<void *> allocs;
     cudaStream_t stream;
     cudaGraph_t graph;
@@ -179,48 +185,50 @@ static bool alloc_common(dsv4b_model *m)
     }
     m->nidx = win + extra;
     const size_t big = (size_t)(d > c.q_lora ? d : c.q_lora);
+    const size_t B = (size_t)m->nseq;
     auto F = [&](size_t n) { return (float *)dcopy(m, nullptr, n * 4, &ok); };
-    m->h = F((size_t)hc * d);
-    m->resid = F((size_t)hc * d);
-    m->x1 = F(d);
-    m->blk = F(d);
-    m->post = F(DSV4B_MAX_HC);
-    m->comb = F(DSV4B_MAX_HC * DSV4B_MAX_HC);
+    m->h = F(B * hc * d);
+    m->resid = F(B * hc * d);
+    m->x1 = F(B * d);
+    m->blk = F(B * d);
+    m->post = F(B * DSV4B_MAX_HC);
+    m->comb = F(B * DSV4B_MAX_HC * DSV4B_MAX_HC);
     m->mixes = F((2 + DSV4B_MAX_HC) * DSV4B_MAX_HC);
-    m->qr = F(big);
-    m->q = F((size_t)c.n_heads * hd);
-    m->kv = F(hd);
-    m->o = F((size_t)c.n_heads * hd);
-    m->ogrp = F((size_t)c.o_groups * c.o_lora);
-    m->comp_in = F(2 * hd);
-    m->comp_sc = F(2 * hd);
-    m->idx_q = F((size_t)c.index_n_heads * c.index_head_dim);
-    m->idx_w = F(c.index_n_heads);
-    m->idx_scores = F(m->ncomp4);
-    m->ix_terms = (double *)dcopy(m, nullptr, (size_t)m->ncomp4 * c.index_n_heads * 8, &ok);
-    m->ix_count = (unsigned *)dcopy(m, nullptr, (size_t)((m->ncomp4 + 31) / 32) * 4, &ok);
-    if (ok && cudaMemset(m->ix_count, 0, (size_t)((m->ncomp4 + 31) / 32) * 4) != cudaSuccess) ok = false;
-    m->logits = F(c.vocab);
-    m->xh = F(d);
-    m->am_pv = F(1024);
+    m->qr = F(B * big);
+    m->q = F(B * c.n_heads * hd);
+    m->kv = F(B * hd);
+    m->o = F(B * c.n_heads * hd);
+    m->ogrp = F(B * c.o_groups * c.o_lora);
+    m->comp_in = F(B * 2 * hd);
+    m->comp_sc = F(B * 2 * hd);
+    m->idx_q = F(B * c.index_n_heads * c.index_head_dim);
+    m->idx_w = F(B * c.index_n_heads);
+    m->idx_scores = F(B * m->ncomp4);
+    m->ix_terms = (double *)dcopy(m, nullptr, B * m->ncomp4 * c.index_n_heads * 8, &ok);
+    m->ix_count = (unsigned *)dcopy(m, nullptr, B * ((m->ncomp4 + 31) / 32) * 4, &ok);
+    if (ok && cudaMemset(m->ix_count, 0, B * ((m->ncomp4 + 31) / 32) * 4) != cudaSuccess) ok = false;
+    m->logits = F(B * c.vocab);
+    m->xh = F(B * d);
+    m->am_pv = F(B * kArgmaxParts);
     m->am_pair = F(2);
     m->stepseq = (unsigned *)dcopy(m, nullptr, 4, &ok);
     if (ok && cudaMemset(m->stepseq, 0, 4) != cudaSuccess) ok = false;
     m->nx = 2 * c.n_layers;
     m->am_gather = F(2 * 64);
-    m->am_pi = (int *)dcopy(m, nullptr, 1024 * 4, &ok);
-    m->idxs = (int *)dcopy(m, nullptr, (size_t)m->nidx * 4, &ok);
-    m->isel = (int *)dcopy(m, nullptr, (size_t)(c.index_topk > 0 ? c.index_topk : 1) * 4, &ok);
-    m->prompt = (int *)dcopy(m, nullptr, (size_t)m->max_pos * 4, &ok);
-    m->out_tokens = (int *)dcopy(m, nullptr, (size_t)m->max_pos * 4, &ok);
-    m->st = (StepState *)dcopy(m, nullptr, sizeof(StepState), &ok);
-    m->attn_part = dcopy(m, nullptr, attn_part_bytes(c.n_heads, hd, m->nidx, 1), &ok);
-    m->hc_part = (double *)dcopy(m, nullptr, (size_t)kHcPreBlocks * (kHcPreMixMax + 1) * 8, &ok);
-    m->hc_cnt = (unsigned *)dcopy(m, nullptr, 4, &ok);
-    if (ok && cudaMemset(m->hc_cnt, 0, 4) != cudaSuccess) ok = false;
+    m->am_pi = (int *)dcopy(m, nullptr, B * kArgmaxParts * 4, &ok);
+    m->idxs = (int *)dcopy(m, nullptr, B * m->nidx * 4, &ok);
+    m->isel = (int *)dcopy(m, nullptr, B * (c.index_topk > 0 ? c.index_topk : 1) * 4, &ok);
+    m->prompt = (int *)dcopy(m, nullptr, B * m->max_pos * 4, &ok);
+    m->out_tokens = (int *)dcopy(m, nullptr, B * m->max_pos * 4, &ok);
+    m->st = (StepState *)dcopy(m, nullptr, B * sizeof(StepState), &ok);
+    m->attn_part = dcopy(m, nullptr, attn_part_bytes(c.n_heads, hd, m->nidx, (int)B), &ok);
+    m->hc_part = (double *)dcopy(m, nullptr, B * kHcPreBlocks * (kHcPreMixMax + 1) * 8, &ok);
+    m->hc_cnt = (unsigned *)dcopy(m, nullptr, B * 4, &ok);
+    if (ok && cudaMemset(m->hc_cnt, 0, B * 4) != cudaSuccess) ok = false;
     const int inter_s = c.moe_inter * c.n_shared;
     const size_t nf = moe_scratch_floats(d, c.moe_inter, inter_s, c.n_experts, c.topk);
-    float *msb = F(nf + kMoeMaxTopk);
+    m->s_ms = (long)((nf + kMoeMaxTopk + 63) & ~(size_t)63);
+    float *msb = F(B * m->s_ms);
     if (ok) moe_scratch_carve(m->ms, msb, d, c.moe_inter, inter_s, c.n_experts, c.topk);
     for (int L = 0; L < c.n_layers && ok; L++) {
         DevLayer &l = m->L[L];
@@ -228,10 +236,10 @@ static bool alloc_common(dsv4b_model *m)
         l.coff = l.ratio == 4 ? 2 : 1;
         const size_t ncomp = l.ratio ? (size_t)(m->max_pos / l.ratio + 1) : 0;
         l.kv_rows = (size_t)win + ncomp;
-        l.kv_cache = F(l.kv_rows * hd);
+        l.kv_cache = F(B * l.kv_rows * hd);
         l.comp_n = l.ratio ? (size_t)l.coff * l.ratio * l.coff * hd : 0;
-        l.comp_kv = l.comp_n ? F(l.comp_n) : nullptr;
-        l.comp_score = l.comp_n ? F(l.comp_n) : nullptr;
+        l.comp_kv = l.comp_n ? F(B * l.comp_n) : nullptr;
+        l.comp_score = l.comp_n ? F(B * l.comp_n) : nullptr;
         l.dyn = (int *)dcopy(m, nullptr, 8, &ok);
     }
     return ok;
@@ -246,11 +254,12 @@ __global__ void k_fill(float *p, size_t n, float v)
 // contribute nothing, src/model/dsv4_layer.c:100-106).
 static int reset_state(dsv4b_model *m)
 {
+    const size_t B = (size_t)m->nseq;
     for (DevLayer &l : m->L) {
-        DSV4B_CUDA_OK(cudaMemsetAsync(l.kv_cache, 0, l.kv_rows * m->c.head_dim * 4, m->stream));
+        DSV4B_CUDA_OK(cudaMemsetAsync(l.kv_cache, 0, B * l.kv_rows * m->c.head_dim * 4, m->stream));
         if (l.comp_n) {
-            DSV4B_CUDA_OK(cudaMemsetAsync(l.comp_kv, 0, l.comp_n * 4, m->stream));
-            k_fill<<<64, 256, 0, m->stream>>>(l.comp_score, l.comp_n, -INFINITY);
+            DSV4B_CUDA_OK(cudaMemsetAsync(l.comp_kv, 0, B * l.comp_n * 4, m->stream));
+            k_fill<<<64, 256, 0, m->stream>>>(l.comp_score, B * l.comp_n, -INFINITY);
         }
         DSV4B_CUDA_OK(cudaMemsetAsync(l.dyn, 0, 8, m->stream));
     }
@@ -270,13 +279,23 @@ struct Grp {
     int n = 0, rc = 0;
 };
 
-static void grp_add(Grp &g, const DevMat &w, const float *x, float *y, cudaStream_t st)
+// nseq items (a batch: token b's x at x + b xs, its y at y + b ys), each the
+// arithmetic of a batch-1 call; a full group is launched and a new one begun.
+static void grp_add(Grp &g, const DevMat &w, const float *x, float *y, cudaStream_t st, int nseq = 1, long xs = 0,
+                    long ys = 0)
 {
-    if (g.n < kGemvMaxItems &&
-        gemv_item(g.it[g.n], w.wdt, w.w, w.s, w.rows, w.cols, w.blk_r, w.blk_c, x, y, w.f16s != 0))
-        g.n++;
-    else
-        g.rc |= G(w, y, x, st);
+    for (int b = 0; b < nseq; b++) {
+        const float *xb = x + (size_t)b * xs;
+        float *yb = y + (size_t)b * ys;
+        if (g.n == kGemvMaxItems) {
+            g.rc |= gemv_group(g.it, g.n, st);
+            g.n = 0;
+        }
+        if (gemv_item(g.it[g.n], w.wdt, w.w, w.s, w.rows, w.cols, w.blk_r, w.blk_c, xb, yb, w.f16s != 0))
+            g.n++;
+        else
+            g.rc |= G(w, yb, xb, st);
+    }
 }
 
 static int grp_run(Grp &g, cudaStream_t st) { return g.rc | gemv_group(g.it, g.n, st); }
@@ -334,7 +353,8 @@ static void hc_step(dsv4b_model *m, Pending &p, float *&hin, float *&hout, const
         a.nmix = head ? hc : mix;
         a.hc_eps = c.hc_eps;
         a.rms_eps = c.rms_eps;
-        launch(k_hc_pre, dim3(n / 256), dim3(288), 0, st, a);
+        a.s_ms = m->s_ms;
+        launch(k_hc_pre, dim3(n / 256, m->nseq), dim3(288), 0, st, a);
         if (p.kind) std::swap(hin, hout);
         p.kind = 0;
         return;
@@ -364,6 +384,9 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
     // H: the heads of this rank (all of them on one GPU)
     const int hc = c.hc_mult, d = c.hidden, hd = c.head_dim, rd = c.qk_rope, H = c.n_heads / m->world;
     const int win = c.sliding_window;
+    // a batch of B sequences: every launch below covers all of them (a grid
+    // dimension, or one GEMV item per sequence)
+    const int B = m->nseq, ql = c.q_lora, ih = c.index_n_heads, id = c.index_head_dim;
     int rc = 0;
     PdlChain chain;
     float *hin = m->h, *hout = m->resid;
@@ -371,7 +394,7 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
     const bool fused = hc_fused(c);
     m->xcall = 0;
     const Exch ex = {m->peer, m->comm, m->stepseq, m->nx, &m->xcall};
-    launch(k_embed, dim3(16), dim3(256), 0, st, hin, m->embed, m->emb_wdt, m->st, d, hc);
+    launch(k_embed, dim3(16, B), dim3(256), 0, st, hin, m->embed, m->emb_wdt, m->st, d, hc);
     for (int Li = 0; Li < c.n_layers; Li++) {
         DevLayer &l = m->L[Li];
         const float *cs = l.ratio ? m->cs_c : m->cs_d, *sn = l.ratio ? m->sn_c : m->sn_d;
@@ -382,25 +405,24 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
         // every projection of x1 in one launch, then both of the normalised q latent
         {
             Grp ga;
-            grp_add(ga, l.wq_a, m->x1, m->qr, st);
-            grp_add(ga, l.wkv, m->x1, m->kv, st);
+            grp_add(ga, l.wq_a, m->x1, m->qr, st, B, d, ql);
+            grp_add(ga, l.wkv, m->x1, m->kv, st, B, d, hd);
             if (l.has_comp) {
-                grp_add(ga, l.cwkv, m->x1, m->comp_in, st);
-                grp_add(ga, l.cwgate, m->x1, m->comp_sc, st);
+                grp_add(ga, l.cwkv, m->x1, m->comp_in, st, B, d, 2 * hd);
+                grp_add(ga, l.cwgate, m->x1, m->comp_sc, st, B, d, 2 * hd);
             }
-            if (l.has_idx) grp_add(ga, l.iwproj, m->x1, m->idx_w, st);
+            if (l.has_idx) grp_add(ga, l.iwproj, m->x1, m->idx_w, st, B, d, ih);
             rc |= grp_run(ga, st);
         }
-        launch(k_rmsnorm, dim3(1), dim3(1024), 0, st, m->qr, m->qr, l.q_norm, c.q_lora, c.rms_eps);
+        launch(k_rmsnorm, dim3(B), dim3(1024), 0, st, m->qr, m->qr, l.q_norm, ql, c.rms_eps);
         {
             Grp gb;
-            grp_add(gb, l.wq_b, m->qr, m->q, st);
-            if (l.has_idx) grp_add(gb, l.iwq_b, m->qr, m->idx_q, st);
+            grp_add(gb, l.wq_b, m->qr, m->q, st, B, ql, (long)H * hd);
+            if (l.has_idx) grp_add(gb, l.iwq_b, m->qr, m->idx_q, st, B, ql, (long)ih * id);
             rc |= grp_run(gb, st);
         }
         // q heads, the KV row, the compressor, the indexer's q heads (or the
         // attended row list) in one launch (dsv4_layer.c:224-295)
-        const int ih = c.index_n_heads, id = c.index_head_dim;
         {
             PrepArgs pa = {};
             pa.q = m->q;
@@ -431,23 +453,26 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
             pa.id = id;
             pa.nidx = m->nidx;
             pa.eps = c.rms_eps;
+            pa.s_cache = (long)(l.kv_rows * hd);
+            pa.s_comp = (long)l.comp_n;
             const int blocks = H + 1 + (pa.has_comp ? 1 : 0) + (pa.has_idx ? ih : 1);
-            launch(k_attn_prep, dim3(blocks), dim3(256), (size_t)hd * 4, st, pa);
+            launch(k_attn_prep, dim3(blocks, B), dim3(256), (size_t)hd * 4, st, pa);
         }
         if (l.has_comp && l.has_idx) {
             const float scale = (1.0f / sqrtf((float)id)) * (1.0f / sqrtf((float)ih));
             // the compressed region read as contiguous rows of index_head_dim
             // floats, as the reference does (dsv4_layer.c:286-289)
-            rc |= indexer_score(m->idx_scores, m->idx_q, l.kv_cache + (size_t)win * hd, DSV4B_DT_F32, id, 0,
-                                m->idx_w, ih, id, m->ncomp4, scale, 1, st, l.dyn, m->ix_terms, m->ix_count);
-            rc |= topk(m->isel, m->idx_scores, m->ncomp4, c.index_topk, 1, m->ncomp4, c.index_topk, st, l.dyn);
-            launch(k_build_idxs, dim3(1), dim3(256), 0, st, m->idxs, m->nidx, m->st, win, l.has_comp, l.has_idx, l.dyn,
-                   m->isel);
+            rc |= indexer_score(m->idx_scores, m->idx_q, l.kv_cache + (size_t)win * hd, DSV4B_DT_F32, id,
+                                (long)(l.kv_rows * hd), m->idx_w, ih, id, m->ncomp4, scale, B, st, l.dyn, m->ix_terms,
+                                m->ix_count);
+            rc |= topk(m->isel, m->idx_scores, m->ncomp4, c.index_topk, B, m->ncomp4, c.index_topk, st, l.dyn);
+            launch(k_build_idxs, dim3(B), dim3(256), 0, st, m->idxs, m->nidx, m->st, win, l.has_comp, l.has_idx, l.dyn,
+                   m->isel, c.index_topk);
         }
         // attention, each head de-rotated by the kernel that writes it
         const AttnRope rope = {cs, sn, &m->st->pos, rd};
         rc |= sparse_attn(m->o, m->q, l.kv_cache, DSV4B_DT_F32, (long)l.kv_rows, l.sink, m->idxs, m->nidx, H, hd,
-                          m->nidx, 1.0f / sqrtf((float)hd), 1, m->attn_part, st, &rope);
+                          m->nidx, 1.0f / sqrtf((float)hd), B, m->attn_part, st, &rope);
         // grouped low-rank output (dsv4_layer.c:303-335): the o_groups row
         // slices of wo_a, each on its own slice of o, in one launch (sharded:
         // this rank's heads are exactly its groups' slices of o)
@@ -462,27 +487,37 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
                 sl.s = wa.s ? wa.s + (size_t)(g * gr / wa.blk_r) * ((wa.cols + wa.blk_c - 1) / wa.blk_c) : nullptr;
                 sl.rows = gr;
                 sl.cols = gw;
-                grp_add(go, sl, m->o + (size_t)g * gw, m->ogrp + (size_t)g * gr, st);
+                grp_add(go, sl, m->o + (size_t)g * gw, m->ogrp + (size_t)g * gr, st, B, (long)H * hd,
+                        (long)c.o_groups * c.o_lora);
             }
             rc |= grp_run(go, st);
         }
-        rc |= G(l.wo_b, m->blk, m->ogrp, st);
+        {
+            Grp gw2;
+            grp_add(gw2, l.wo_b, m->ogrp, m->blk, st, B, (long)c.o_groups * c.o_lora, d);
+            rc |= grp_run(gw2, st);
+        }
         // sharded: wo_b holds this rank's groups' columns, so blk is a partial
         // sum over them
         if (m->world > 1) rc |= xreduce_sum(ex, m->blk, d, st);
         // ---- FFN half: the residual is taken after attention (:511-522)
         pend = {1, nullptr};
         hc_step(m, pend, hin, hout, l.hcf_fn, l.hcf_base, l.hcf_scale, l.ffn_norm, false, m->x1, st);
-        rc |= moe_forward(l.moe, m->ms, m->blk, m->x1, &m->st->token, st, !fused, m->world > 1 ? &ex : nullptr);
+        rc |= moe_forward(l.moe, m->ms, m->blk, m->x1, &m->st->token, st, !fused, m->world > 1 ? &ex : nullptr, B,
+                          m->s_ms, d, (int)(sizeof(StepState) / sizeof(int)));
         pend = {fused ? 2 : 1, &l.moe};
     }
     // ---- head (src/cli/dsv4_run.c:467-474)
     hc_step(m, pend, hin, hout, m->hch_fn, m->hch_base, m->hch_scale, m->norm, true, m->xh, st);
-    rc |= G(m->head, m->logits, m->xh, st);
-    launch(k_argmax_part, dim3(148), dim3(256), 0, st, m->am_pv, m->am_pi, m->logits, m->head.rows);
+    {
+        Grp gh;
+        grp_add(gh, m->head, m->xh, m->logits, st, B, d, m->head.rows);
+        rc |= grp_run(gh, st);
+    }
+    launch(k_argmax_part, dim3(148, B), dim3(256), 0, st, m->am_pv, m->am_pi, m->logits, m->head.rows);
     if (m->world == 1) {
-        launch(k_argmax_final, dim3(1), dim3(32), 0, st, m->st, m->out_tokens, m->am_pv, m->am_pi, 148, 1,
-               m->prompt, m->n_prompt, (unsigned *)nullptr);
+        launch(k_argmax_final, dim3(B), dim3(32), 0, st, m->st, m->out_tokens, m->am_pv, m->am_pi, 148, 1,
+               m->prompt, m->n_prompt, (unsigned *)nullptr, m->max_pos);
     } else {
         // sharded head: each rank holds a contiguous vocabulary slice; the
         // ranks' best (value, index) pairs are gathered and reduced the same
@@ -491,7 +526,8 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
                m->rank * m->head.rows);
         rc |= comm_allgather(m->am_pair, m->am_gather, 8, m->comm, st);
         launch(k_argmax_final, dim3(1), dim3(32), 0, st, m->st, m->out_tokens, m->am_gather,
-               reinterpret_cast<const int *>(m->am_gather) + 1, m->world, 2, m->prompt, m->n_prompt, m->stepseq);
+               reinterpret_cast<const int *>(m->am_gather) + 1, m->world, 2, m->prompt, m->n_prompt, m->stepseq,
+               m->max_pos);
     }
     if (cudaPeekAtLastError() != cudaSuccess) rc = -1;
     return rc ? -1 : 0;
@@ -591,16 +627,17 @@ extern "C" void dsv4_cuda_model_free(dsv4b_model *m)
     delete m;
 }
 
-static dsv4b_model *model_new(const DSV4Cfg *c, int max_pos)
+static dsv4b_model *model_new(const DSV4Cfg *c, int max_pos, int nseq = 1)
 {
     if (dsv4_cuda_init() != 0 || !c || c->n_layers < 1 || c->n_layers > DSV4_MAX_LAYERS || max_pos < 1 ||
         c->hc_mult > DSV4B_MAX_HC || c->topk > kMoeMaxTopk || c->n_experts > kMoeMaxExperts || c->n_heads > 64 ||
-        c->index_topk > kTopkMaxK)
+        c->index_topk > kTopkMaxK || nseq < 1 || nseq > DSV4B_MAX_SEQ || (nseq > 1 && !hc_fused(*c)))
         return nullptr;
     dsv4b_model *m = new dsv4b_model();
     m->c = *c;
     m->rank = 0;
     m->world = 1;
+    m->nseq = nseq;
     for (int L = 0; L < c->n_layers; L++) m->ratios[L] = c->compress_ratios ? c->compress_ratios[L] : 0;
     m->c.compress_ratios = m->ratios;
     m->max_pos = max_pos;
@@ -616,11 +653,12 @@ static dsv4b_model *model_new(const DSV4Cfg *c, int max_pos)
     return m;
 }
 
-extern "C" dsv4b_model *dsv4_cuda_model_create(const DSV4Cfg *c, const DSV4ModelW *mw, const DSV4LayerW *layers,
-                                               const DSV4ExpertW *experts, int max_pos)
+extern "C" dsv4b_model *dsv4_cuda_model_create_batch(const DSV4Cfg *c, const DSV4ModelW *mw,
+                                                     const DSV4LayerW *layers, const DSV4ExpertW *experts,
+                                                     int max_pos, int n_seq)
 {
     if (!mw || !layers || !experts) return nullptr;
-    dsv4b_model *m = model_new(c, max_pos);
+    dsv4b_model *m = model_new(c, max_pos, n_seq);
     if (!m) return nullptr;
     bool ok = true;
     for (int L = 0; L < c->n_layers && ok; L++) ok = build_layer_from_host(m, L, layers[L], experts);
@@ -640,23 +678,38 @@ extern "C" dsv4b_model *dsv4_cuda_model_create(const DSV4Cfg *c, const DSV4Model
     return m;
 }
 
-extern "C" int dsv4_cuda_model_begin(dsv4b_model *m, const int *prompt, int n_prompt)
+extern "C" dsv4b_model *dsv4_cuda_model_create(const DSV4Cfg *c, const DSV4ModelW *mw, const DSV4LayerW *layers,
+                                               const DSV4ExpertW *experts, int max_pos)
 {
-    if (!m || !prompt || n_prompt < 1 || n_prompt > m->max_pos) return -1;
-    for (int i = 0; i < n_prompt; i++)
-        if (prompt[i] < 0 || prompt[i] >= m->c.vocab) return -1;
+    return dsv4_cuda_model_create_batch(c, mw, layers, experts, max_pos, 1);
+}
+
+extern "C" int dsv4b_model_n_seq(const dsv4b_model *m) { return m ? m->nseq : -1; }
+
+extern "C" int dsv4b_model_begin_batch(dsv4b_model *m, const int *prompts, int n_prompt)
+{
+    if (!m || !prompts || n_prompt < 1 || n_prompt > m->max_pos) return -1;
+    const int B = m->nseq;
+    for (int i = 0; i < B * n_prompt; i++)
+        if (prompts[i] < 0 || prompts[i] >= m->c.vocab) return -1;
     m->n_prompt = n_prompt;
-    DSV4B_CUDA_OK(cudaMemcpyAsync(m->prompt, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, m->stream));
-    StepState s0 = { prompt[0], 0 };
+    // sequence b's prompt at row b of the max_pos-wide prompt table
+    for (int b = 0; b < B; b++)
+        DSV4B_CUDA_OK(cudaMemcpyAsync(m->prompt + (size_t)b * m->max_pos, prompts + (size_t)b * n_prompt,
+                                      (size_t)n_prompt * 4, cudaMemcpyHostToDevice, m->stream));
+    std::vector<StepState> s0v(B);
+    for (int b = 0; b < B; b++) s0v[b] = { prompts[(size_t)b * n_prompt], 0 };
+    const StepState *s0 = s0v.data();
+    const size_t s0b = (size_t)B * sizeof(StepState);
     if (reset_state(m)) return -1;
-    DSV4B_CUDA_OK(cudaMemcpyAsync(m->st, &s0, sizeof s0, cudaMemcpyHostToDevice, m->stream));
+    DSV4B_CUDA_OK(cudaMemcpyAsync(m->st, s0, s0b, cudaMemcpyHostToDevice, m->stream));
     if (!m->graphed) {
         // one eager step sets every kernel attribute, then the state is reset
         // and the step is captured once for all positions
         if (enqueue_step(m, m->stream)) return -1;
         DSV4B_CUDA_OK(cudaStreamSynchronize(m->stream));
         if (reset_state(m)) return -1;
-        DSV4B_CUDA_OK(cudaMemcpyAsync(m->st, &s0, sizeof s0, cudaMemcpyHostToDevice, m->stream));
+        DSV4B_CUDA_OK(cudaMemcpyAsync(m->st, s0, s0b, cudaMemcpyHostToDevice, m->stream));
         DSV4B_CUDA_OK(cudaStreamSynchronize(m->stream));
         DSV4B_CUDA_OK(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
         const int rc = enqueue_step(m, m->stream);
@@ -671,6 +724,12 @@ extern "C" int dsv4_cuda_model_begin(dsv4b_model *m, const int *prompt, int n_pr
     return 0;
 }
 
+extern "C" int dsv4_cuda_model_begin(dsv4b_model *m, const int *prompt, int n_prompt)
+{
+    if (!m || m->nseq != 1) return -1;
+    return dsv4b_model_begin_batch(m, prompt, n_prompt);
+}
+
 extern "C" int dsv4b_model_step_async(dsv4b_model *m, void *stream)
 {
     if (!m || !m->graphed) return -1;
@@ -680,7 +739,7 @@ extern "C" int dsv4b_model_step_async(dsv4b_model *m, void *stream)
 
 extern "C" int dsv4_cuda_model_step(dsv4b_model *m, int *token, float *logits)
 {
-    if (!m || !m->graphed) return -1;
+    if (!m || !m->graphed || m->nseq != 1) return -1;
     StepState s;
     DSV4B_CUDA_OK(cudaMemcpyAsync(&s, m->st, sizeof s, cudaMemcpyDeviceToHost, m->stream));
     DSV4B_CUDA_OK(cudaStreamSynchronize(m->stream));
@@ -693,17 +752,25 @@ extern "C" int dsv4_cuda_model_step(dsv4b_model *m, int *token, float *logits)
     return 0;
 }
 
-extern "C" int dsv4_cuda_model_generate(dsv4b_model *m, const int *prompt, int n_prompt, int n_gen, int *out)
+extern "C" int dsv4b_model_generate_batch(dsv4b_model *m, const int *prompts, int n_prompt, int n_gen, int *out)
 {
-    if (dsv4_cuda_model_begin(m, prompt, n_prompt) != 0) return -1;
+    if (dsv4b_model_begin_batch(m, prompts, n_prompt) != 0) return -1;
     const int steps = n_prompt + n_gen;
     if (steps > m->max_pos) return -1;
     for (int i = 0; i < steps; i++) DSV4B_CUDA_OK(cudaGraphLaunch(m->exec, m->stream));
     // position p emits the token after it; the generated ones start at n_prompt-1
-    DSV4B_CUDA_OK(cudaMemcpyAsync(out, m->out_tokens + n_prompt - 1, (size_t)(n_gen + 1) * 4,
-                                  cudaMemcpyDeviceToHost, m->stream));
+    for (int b = 0; b < m->nseq; b++)
+        DSV4B_CUDA_OK(cudaMemcpyAsync(out + (size_t)b * (n_gen + 1),
+                                      m->out_tokens + (size_t)b * m->max_pos + n_prompt - 1, (size_t)(n_gen + 1) * 4,
+                                      cudaMemcpyDeviceToHost, m->stream));
     DSV4B_CUDA_OK(cudaStreamSynchronize(m->stream));
     return n_gen + 1;
+}
+
+extern "C" int dsv4_cuda_model_generate(dsv4b_model *m, const int *prompt, int n_prompt, int n_gen, int *out)
+{
+    if (!m || m->nseq != 1) return -1;
+    return dsv4b_model_generate_batch(m, prompt, n_prompt, n_gen, out);
 }
 
 // ------------------------------------------------------- synthetic models
@@ -899,15 +966,15 @@ extern "C" int dsv4b_nccl_unique_id(void *out) { return comm_unique_id(out); }
 
 // A synthetic model, or this rank's share of one: the tensors of rank r are
 // exactly the corresponding slices of the single-GPU model of the same seed.
-extern "C" dsv4b_model *dsv4_cuda_model_create_synthetic_sharded(const DSV4Cfg *c, int max_pos,
-                                                                unsigned long long seed, int rank, int world,
-                                                                const void *nccl_id)
+static dsv4b_model *synthetic_create(const DSV4Cfg *c, int max_pos, unsigned long long seed, int rank, int world,
+                                     const void *nccl_id, int nseq)
 {
-    if (!c || dsv4b_shard_check(c, world) != 0 || rank < 0 || rank >= world || (world > 1 && !nccl_id)) {
+    if (!c || dsv4b_shard_check(c, world) != 0 || rank < 0 || rank >= world || (world > 1 && !nccl_id) ||
+        (world > 1 && nseq != 1)) {
         fprintf(stderr, "dsv4_b200: configuration does not split over %d GPUs (or bad rank %d)\n", world, rank);
         return nullptr;
     }
-    dsv4b_model *m = model_new(c, max_pos);
+    dsv4b_model *m = model_new(c, max_pos, nseq);
     if (!m) return nullptr;
     m->rank = rank;
     m->world = world;
@@ -949,18 +1016,50 @@ extern "C" dsv4b_model *dsv4_cuda_model_create_synthetic_sharded(const DSV4Cfg *
     return m;
 }
 
+extern "C" dsv4b_model *dsv4_cuda_model_create_synthetic_sharded(const DSV4Cfg *c, int max_pos,
+                                                                unsigned long long seed, int rank, int world,
+                                                                const void *nccl_id)
+{
+    return synthetic_create(c, max_pos, seed, rank, world, nccl_id, 1);
+}
+
 extern "C" dsv4b_model *dsv4_cuda_model_create_synthetic(const DSV4Cfg *c, int max_pos, unsigned long long seed)
 {
-    return dsv4_cuda_model_create_synthetic_sharded(c, max_pos, seed, 0, 1, nullptr);
+    return synthetic_create(c, max_pos, seed, 0, 1, nullptr, 1);
+}
+
+extern "C" dsv4b_model *dsv4_cuda_model_create_synthetic_batch(const DSV4Cfg *c, int max_pos,
+                                                              unsigned long long seed, int n_seq)
+{
+    return synthetic_create(c, max_pos, seed, 0, 1, nullptr, n_seq);
 }
 
 extern "C" int dsv4_cuda_model_decode(dsv4b_model *m, int token, int pos, int *next_token)
 {
-    if (!m || !m->graphed || pos < 0 || pos >= m->max_pos || token < 0 || token >= m->c.vocab) return -1;
+    if (!m || !m->graphed || m->nseq != 1 || pos < 0 || pos >= m->max_pos || token < 0 || token >= m->c.vocab) return -1;
     const dsv4b::StepState s = { token, pos };
     DSV4B_CUDA_OK(cudaMemcpyAsync(m->st, &s, sizeof s, cudaMemcpyHostToDevice, m->stream));
     DSV4B_CUDA_OK(cudaGraphLaunch(m->exec, m->stream));
     DSV4B_CUDA_OK(cudaMemcpyAsync(next_token, m->out_tokens + pos, 4, cudaMemcpyDeviceToHost, m->stream));
+    DSV4B_CUDA_OK(cudaStreamSynchronize(m->stream));
+    return 0;
+}
+
+extern "C" int dsv4b_model_decode_batch(dsv4b_model *m, const int *tokens, int pos, int *next_tokens)
+{
+    if (!m || !m->graphed || !tokens || !next_tokens || pos < 0 || pos >= m->max_pos) return -1;
+    const int B = m->nseq;
+    std::vector<dsv4b::StepState> s(B);
+    for (int b = 0; b < B; b++) {
+        if (tokens[b] < 0 || tokens[b] >= m->c.vocab) return -1;
+        s[b] = { tokens[b], pos };
+    }
+    DSV4B_CUDA_OK(cudaMemcpyAsync(m->st, s.data(), (size_t)B * sizeof(dsv4b::StepState), cudaMemcpyHostToDevice,
+                                  m->stream));
+    DSV4B_CUDA_OK(cudaGraphLaunch(m->exec, m->stream));
+    // token b at out_tokens[b][pos]: one strided copy
+    DSV4B_CUDA_OK(cudaMemcpy2DAsync(next_tokens, 4, m->out_tokens + pos, (size_t)m->max_pos * 4, 4, B,
+                                    cudaMemcpyDeviceToHost, m->stream));
     DSV4B_CUDA_OK(cudaStreamSynchronize(m->stream));
     return 0;
 }

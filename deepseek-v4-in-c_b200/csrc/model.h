@@ -7,6 +7,7 @@
 #include "moe.h"
 
 #define DSV4B_MAX_HC 8
+#define DSV4B_MAX_SEQ 64     // sequences of a batched model
 
 namespace dsv4b {
 
@@ -40,6 +41,11 @@ struct HcPreArgs {
     unsigned *count;
     int hc, hidden, iters, nmix, topk;
     float hc_eps, rms_eps;
+    // a batch: sequence blockIdx.y reads and writes its own rows (residuals
+    // hc hidden apart, y / blk hidden apart, post / comb DSV4B_MAX_HC /
+    // DSV4B_MAX_HC^2 apart, part gridDim.x (nmix + 1) apart, count 1 apart)
+    // and its MoE scratch (acc, wts, accs) s_ms floats apart
+    long s_ms;
 };
 __global__ void k_hc_pre(const __grid_constant__ HcPreArgs a);
 __global__ void k_hc_head_finish(float *y, const float *mixes, const float *x, const float *scale,
@@ -56,13 +62,19 @@ struct PrepArgs {
     int *dyn, *idxs;
     int H, hd, rd, win, has_comp, has_idx, ratio, index_topk, ih, id, nidx;
     float eps;
+    // a batch (blockIdx.y = sequence): the caches and compressor windows of
+    // consecutive sequences are s_cache / s_comp floats apart; q, kv, idx_q,
+    // comp_in / comp_sc (2 hd), idxs (nidx) and st are packed per sequence
+    long s_cache, s_comp;
 };
 __global__ void k_attn_prep(const __grid_constant__ PrepArgs a);
 __global__ void k_build_idxs(int *idxs, int nmax, const StepState *st, int win, int has_comp, int has_idx,
-                             const int *dyn, const int *sel);
+                             const int *dyn, const int *sel, int sel_stride);
+// argmax partials per sequence (k_argmax_part's blocks, <= kArgmaxParts)
+constexpr int kArgmaxParts = 1024;
 __global__ void k_argmax_part(float *pv, int *pi, const float *x, int n);
 __global__ void k_argmax_final(StepState *st, int *out_tokens, const float *pv, const int *pi, int nparts,
-                               int stride, const int *prompt, int n_prompt, unsigned *stepseq);
+                               int stride, const int *prompt, int n_prompt, unsigned *stepseq, int seq_tokens);
 __global__ void k_argmax_pair(float *pair, const float *pv, const int *pi, int nparts, int offset);
 
 __global__ void k_synth(void *dst, size_t n, int kind, float a, float b, uint64_t key);

@@ -47,12 +47,14 @@ __device__ __forceinline__ double part_sum_d(double v, double *red, int nw, int 
 }
 
 // dsv4_embed_row (include/dsv4/dsv4.h:300-314), replicated hc times
-// (src/cli/dsv4_run.c:449-450).
+// (src/cli/dsv4_run.c:449-450). Sequence blockIdx.y of a batch: its step
+// state st[y], its residual at h + y hc hidden.
 __global__ void k_embed(float *h, const void *table, int wdt, const StepState *st, int hidden, int hc)
 {
     pdl_trigger();
     pdl_wait();
-    const long tok = st->token;
+    h += (size_t)blockIdx.y * hc * hidden;
+    const long tok = st[blockIdx.y].token;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < hidden; i += gridDim.x * blockDim.x) {
         float v;
         if (wdt == DSV4B_WBF16)
@@ -229,16 +231,32 @@ __device__ __forceinline__ void sinkhorn_warp(float *comb, const float *mixes, f
 __global__ void __launch_bounds__(288) k_hc_pre(const __grid_constant__ HcPreArgs a)
 {
     constexpr int MIXMAX = kHcPreMixMax, NV = MIXMAX + 1;
+    // sequence blockIdx.y of a batch: its own rows of every activation
+    // (pointers computed here; the argument block itself is never modified)
+    const size_t sq_ = blockIdx.y, wide_ = (size_t)a.hc * a.hidden;
+    float *const yq = a.y + sq_ * a.hidden;
+    float *const postq = a.post ? a.post + sq_ * DSV4B_MAX_HC : nullptr;
+    float *const combq = a.comb ? a.comb + sq_ * DSV4B_MAX_HC * DSV4B_MAX_HC : nullptr;
+    const float *const xq = a.x + sq_ * wide_;
+    float *const xoutq = a.xout ? a.xout + sq_ * wide_ : nullptr;
+    const float *const blkq = a.blk ? a.blk + sq_ * a.hidden : nullptr;
+    const float *const accq = a.acc ? a.acc + sq_ * a.s_ms : nullptr;
+    const float *const wtsq = a.wts ? a.wts + sq_ * a.s_ms : nullptr;
+    const float *const accsq = a.accs ? a.accs + sq_ * a.s_ms : nullptr;
+    const float *const pinq = a.post_in ? a.post_in + sq_ * DSV4B_MAX_HC : nullptr;
+    const float *const cinq = a.comb_in ? a.comb_in + sq_ * DSV4B_MAX_HC * DSV4B_MAX_HC : nullptr;
+    double *const partq = a.part + sq_ * gridDim.x * NV;
+    unsigned *const cntq = a.count + sq_;
     __shared__ float prod[NV][256];
     __shared__ double red8[NV][8];
     __shared__ double tot[NV];
     __shared__ float mixes[MIXMAX], pre[DSV4B_MAX_HC], sbase[MIXMAX], sscale[3];
     __shared__ bool last;
     const int hc = a.hc, hidden = a.hidden, n = hc * hidden, mix = a.nmix, tid = threadIdx.x;
-    const bool stepped = a.blk || a.acc;
+    const bool stepped = blkq || accq;
     pdl_trigger();
     if (tid < mix) sbase[tid] = __ldg(a.base + tid);     // weights: before the wait
-    if (tid < (a.post ? 3 : 1)) sscale[tid] = __ldg(a.scale + tid);
+    if (tid < (postq ? 3 : 1)) sscale[tid] = __ldg(a.scale + tid);
     // one column per thread of warps 0..7 (the launcher sizes the grid to
     // n / 256; warp 8 only runs the split); its fn column is a weight,
     // fetched before waiting for x
@@ -266,35 +284,35 @@ __global__ void __launch_bounds__(288) k_hc_pre(const __grid_constant__ HcPreArg
             float xl[DSV4B_MAX_HC], cl[DSV4B_MAX_HC];
 #pragma unroll
             for (int l = 0; l < DSV4B_MAX_HC; l++) {
-                xl[l] = l < hc ? ld_act(a.x + (size_t)l * hidden + d) : 0.0f;
-                cl[l] = l < hc ? ld_act(a.comb_in + l * hc + j) : 0.0f;
+                xl[l] = l < hc ? ld_act(xq + (size_t)l * hidden + d) : 0.0f;
+                cl[l] = l < hc ? ld_act(cinq + l * hc + j) : 0.0f;
             }
-            const float pj = ld_act(a.post_in + j);
-            if (a.acc) {
+            const float pj = ld_act(pinq + j);
+            if (accq) {
                 float wv[kMoeMaxTopk], av[kMoeMaxTopk];
 #pragma unroll
                 for (int k = 0; k < kMoeMaxTopk; k++) {
-                    wv[k] = k < a.topk ? ld_act(a.wts + k) : 0.0f;
-                    av[k] = k < a.topk ? ld_act(a.acc + (size_t)k * hidden + d) : 0.0f;
+                    wv[k] = k < a.topk ? ld_act(wtsq + k) : 0.0f;
+                    av[k] = k < a.topk ? ld_act(accq + (size_t)k * hidden + d) : 0.0f;
                 }
-                const float sv = a.accs ? ld_act(a.accs + d) : 0.0f;
+                const float sv = accsq ? ld_act(accsq + d) : 0.0f;
                 float o = 0.0f;
 #pragma unroll
                 for (int k = 0; k < kMoeMaxTopk; k++)
                     if (k < a.topk) o = __fadd_rn(o, __fmul_rn(wv[k], av[k]));
-                if (a.accs) o = __fadd_rn(o, sv);
+                if (accsq) o = __fadd_rn(o, sv);
                 b = o;
             } else {
-                b = ld_act(a.blk + d);
+                b = ld_act(blkq + d);
             }
             double s = __dmul_rn((double)pj, (double)b);
 #pragma unroll
             for (int l = 0; l < DSV4B_MAX_HC; l++)
                 if (l < hc) s = __dadd_rn(s, __dmul_rn((double)cl[l], (double)xl[l]));
             xv = (float)s;
-            a.xout[i] = xv;
+            xoutq[i] = xv;
         } else {
-            xv = ld_act(a.x + i);
+            xv = ld_act(xq + i);
         }
     }
     if (col) {
@@ -315,15 +333,15 @@ __global__ void __launch_bounds__(288) k_hc_pre(const __grid_constant__ HcPreArg
         double t = 0.0;
 #pragma unroll
         for (int w = 0; w < 8; w++) t += red8[tid][w];
-        a.part[(size_t)blockIdx.x * NV + tid] = t;
+        partq[(size_t)blockIdx.x * NV + tid] = t;
     }
     __threadfence();
     __syncthreads();
-    if (tid == 0) last = atomicAdd(a.count, 1u) == gridDim.x - 1;
+    if (tid == 0) last = atomicAdd(cntq, 1u) == gridDim.x - 1;
     __syncthreads();
     if (!last) return;
     __threadfence();
-    const float *x = stepped ? a.xout : a.x;
+    const float *x = stepped ? xoutq : xq;
     // every block's partials: 8 threads per value each add gridDim/8 blocks,
     // then the 8 sums in order
     const int nblk = (int)gridDim.x, per = (nblk + 7) >> 3;
@@ -334,7 +352,7 @@ __global__ void __launch_bounds__(288) k_hc_pre(const __grid_constant__ HcPreArg
 #pragma unroll
         for (int k = 0; k < PB; k++) {
             const int bb = w * per + k;
-            pv[k] = (k < per && bb < nblk) ? __ldcg(a.part + (size_t)bb * NV + m) : 0.0;
+            pv[k] = (k < per && bb < nblk) ? __ldcg(partq + (size_t)bb * NV + m) : 0.0;
         }
         double t = 0.0;
 #pragma unroll
@@ -350,7 +368,7 @@ __global__ void __launch_bounds__(288) k_hc_pre(const __grid_constant__ HcPreArg
         tot[tid] = t;
     }
     __syncthreads();
-    if (tid == 0) *a.count = 0u;
+    if (tid == 0) *cntq = 0u;
     if (tid < 32) {
         const float rs = __fdiv_rn(1.0f, __fsqrt_rn((float)(tot[MIXMAX] / (double)n) + a.rms_eps));
         if (tid < mix) mixes[tid] = __fmul_rn((float)tot[tid], rs);
@@ -361,13 +379,13 @@ __global__ void __launch_bounds__(288) k_hc_pre(const __grid_constant__ HcPreArg
     if (tid >= 256) {
         // the extra warp: post weights and the Sinkhorn split, concurrently
         // with y below (only the next sub-layer's post-mix reads them)
-        if (!a.post) return;
+        if (!postq) return;
         const int l = tid - 256;
-        if (l < hc) a.post[l] = __fmul_rn(2.0f, sigm(__fadd_rn(__fmul_rn(mixes[l + hc], sscale[1]), sbase[l + hc])));
+        if (l < hc) postq[l] = __fmul_rn(2.0f, sigm(__fadd_rn(__fmul_rn(mixes[l + hc], sscale[1]), sbase[l + hc])));
         if (hc == 4)
-            sinkhorn_warp<4>(a.comb, mixes, sscale[2], sbase, 4, a.iters, a.hc_eps);
+            sinkhorn_warp<4>(combq, mixes, sscale[2], sbase, 4, a.iters, a.hc_eps);
         else
-            sinkhorn_warp<0>(a.comb, mixes, sscale[2], sbase, hc, a.iters, a.hc_eps);
+            sinkhorn_warp<0>(combq, mixes, sscale[2], sbase, hc, a.iters, a.hc_eps);
         return;
     }
     // warps 0..7: y = sum_j pre[j] x[j], four columns per float4, in two
@@ -415,7 +433,7 @@ __global__ void __launch_bounds__(288) k_hc_pre(const __grid_constant__ HcPreArg
         const double ssq = part_sum_d((double)sq, nred, 8, 1);
         inv = __fdiv_rn(1.0f, __fsqrt_rn((float)(ssq / (double)hidden) + a.rms_eps));
     }
-    float4 *y4 = reinterpret_cast<float4 *>(a.y);
+    float4 *y4 = reinterpret_cast<float4 *>(yq);
 #pragma unroll
     for (int u = 0; u < kHcPreYPT; u++) {
         const int d4 = tid + u * 256;
@@ -468,11 +486,14 @@ __global__ void k_hc_post(float *y, const float *x, const float *res, const floa
 }
 
 // RMSNorm (src/core/dsv4_ops.c:25-32): double sum of squares, eps on the mean,
-// y = w * (x * inv). One block; y may alias x.
+// y = w * (x * inv). One block per vector (block b: the n values at b n);
+// y may alias x.
 __global__ void k_rmsnorm(float *y, const float *x, const float *w, int n, float eps)
 {
     pdl_trigger();
     pdl_wait();
+    y += (size_t)blockIdx.x * n;
+    x += (size_t)blockIdx.x * n;
     __shared__ double red[33];
     double s = 0.0;
     for (int i = threadIdx.x; i < n; i += blockDim.x) s = __fma_rn((double)x[i], (double)x[i], s);
@@ -519,6 +540,9 @@ __device__ void compress_step(float *cache, float *kv_state, float *score_state,
                               const float *cs, const float *sn, int pos, float eps, int win, int index_topk,
                               int *dyn, float *cbuf, double *red)
 {
+    // a batch's sequences stand at the same position: sequence 0 writes the
+    // shared counts
+    if (blockIdx.y != 0) dyn = nullptr;
     const int overlap = (ratio == 4), coff = 1 + overlap, width = coff * hd;
     const int phase = pos % ratio, slot = overlap ? ratio + phase : phase;
     const float *apr = ape + (size_t)phase * width;
@@ -527,7 +551,7 @@ __device__ void compress_step(float *cache, float *kv_state, float *score_state,
         score_state[(size_t)slot * width + c] = __fadd_rn(sc_in[c], apr[c]);
     }
     const int avail = (pos + 1) / ratio;
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == 0 && dyn) {
         dyn[0] = avail;
         dyn[1] = avail < index_topk ? avail : index_topk;
     }
@@ -608,43 +632,56 @@ __global__ void __launch_bounds__(256) k_attn_prep(const __grid_constant__ PrepA
     pdl_wait();
     extern __shared__ float cbuf[];     // [hd], the compressor's row
     __shared__ double red[33];
-    const int pos = a.st->pos;
+    // sequence blockIdx.y of a batch: its activations, cache and compressor
+    // (pointers computed here; the argument block itself is never modified)
+    const size_t y = blockIdx.y;
+    float *const q = a.q + y * a.H * a.hd, *const kv = a.kv + y * a.hd, *const cache = a.cache + y * a.s_cache;
+    float *const comp_kv = a.comp_kv ? a.comp_kv + y * a.s_comp : nullptr;
+    float *const comp_score = a.comp_score ? a.comp_score + y * a.s_comp : nullptr;
+    float *const idx_q = a.idx_q + y * a.ih * a.id;
+    const float *const comp_in = a.comp_in + y * 2 * a.hd, *const comp_sc = a.comp_sc + y * 2 * a.hd;
+    int *const idxs = a.idxs + y * a.nidx;
+    const int pos = a.st[y].pos;
     int b = blockIdx.x;
     if (b < a.H) {
-        head_norm_rope(a.q + (size_t)b * a.hd, a.hd, a.rd, a.cs, a.sn, pos, 0, 1, a.eps, red);
+        head_norm_rope(q + (size_t)b * a.hd, a.hd, a.rd, a.cs, a.sn, pos, 0, 1, a.eps, red);
         return;
     }
     b -= a.H;
     if (b == 0) {
-        kv_finish(a.kv, a.kv_norm, a.hd, a.rd, a.cs, a.sn, pos, a.eps, a.cache, a.win, red);
+        kv_finish(kv, a.kv_norm, a.hd, a.rd, a.cs, a.sn, pos, a.eps, cache, a.win, red);
         return;
     }
     b -= 1;
     if (a.has_comp) {
         if (b == 0) {
-            compress_step(a.cache, a.comp_kv, a.comp_score, a.comp_in, a.comp_sc, a.ape, a.cnorm, a.ratio, a.hd,
+            compress_step(cache, comp_kv, comp_score, comp_in, comp_sc, a.ape, a.cnorm, a.ratio, a.hd,
                           a.rd, a.cs, a.sn, pos, a.eps, a.win, a.index_topk, a.dyn, cbuf, red);
             return;
         }
         b -= 1;
     }
     if (a.has_idx) {
-        if (b < a.ih) head_norm_rope(a.idx_q + (size_t)b * a.id, a.id, a.rd, a.cs, a.sn, pos, 0, 0, a.eps, red);
+        if (b < a.ih) head_norm_rope(idx_q + (size_t)b * a.id, a.id, a.rd, a.cs, a.sn, pos, 0, 0, a.eps, red);
         return;
     }
-    if (b == 0) build_idxs(a.idxs, a.nidx, pos, a.win, a.has_comp, 0, a.has_comp ? (pos + 1) / a.ratio : 0, nullptr);
+    if (b == 0) build_idxs(idxs, a.nidx, pos, a.win, a.has_comp, 0, a.has_comp ? (pos + 1) / a.ratio : 0, nullptr);
 }
 
 // The attention index list (src/model/dsv4_layer.c:504-505 and :278-297):
 // the window's ring slots of the last min(pos+1, win) positions, newest
 // first, then the compressed selections (top-k order, or 0..avail-1 without
 // an indexer) offset by win, then -1 up to nmax.
+// One block per sequence of a batch (block b: idxs + b nmax, st[b], sel + b
+// sel_stride).
 __global__ void k_build_idxs(int *idxs, int nmax, const StepState *st, int win, int has_comp, int has_idx,
-                             const int *dyn, const int *sel)
+                             const int *dyn, const int *sel, int sel_stride)
 {
     pdl_trigger();
     pdl_wait();
-    build_idxs(idxs, nmax, st->pos, win, has_comp, has_idx, has_comp ? __ldcg(dyn + (has_idx ? 1 : 0)) : 0, sel);
+    const int b = blockIdx.x;
+    build_idxs(idxs + (size_t)b * nmax, nmax, st[b].pos, win, has_comp, has_idx,
+               has_comp ? __ldcg(dyn + (has_idx ? 1 : 0)) : 0, sel + (size_t)b * sel_stride);
 }
 
 // Argmax, first maximum (src/cli/dsv4_run.c:472-473), two stages; the second
@@ -654,6 +691,10 @@ __global__ void k_argmax_part(float *pv, int *pi, const float *x, int n)
 {
     pdl_trigger();
     pdl_wait();
+    // sequence blockIdx.y of a batch: its logits and its kArgmaxParts partials
+    pv += (size_t)blockIdx.y * kArgmaxParts;
+    pi += (size_t)blockIdx.y * kArgmaxParts;
+    x += (size_t)blockIdx.y * n;
     __shared__ float sv[32];
     __shared__ int si[32];
     float bv = -INFINITY;
@@ -696,11 +737,20 @@ __device__ __forceinline__ void argmax_warp(float &bv, int &bi, const float *pv,
 }
 
 __global__ void k_argmax_final(StepState *st, int *out_tokens, const float *pv, const int *pi, int nparts,
-                               int stride, const int *prompt, int n_prompt, unsigned *stepseq)
+                               int stride, const int *prompt, int n_prompt, unsigned *stepseq, int seq_tokens)
 {
     pdl_trigger();
     pdl_wait();
     if (threadIdx.x >= 32) return;
+    // sequence blockIdx.x of a batch: its state, its token rows (seq_tokens
+    // apart) and its partials
+    const int sq = blockIdx.x;
+    st += sq;
+    out_tokens += (size_t)sq * seq_tokens;
+    prompt += (size_t)sq * seq_tokens;
+    pv += (size_t)sq * kArgmaxParts;
+    pi += (size_t)sq * kArgmaxParts;
+    if (sq != 0) stepseq = nullptr;
     float bv;
     int bi;
     argmax_warp(bv, bi, pv, pi, nparts, stride);

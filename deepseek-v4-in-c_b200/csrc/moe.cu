@@ -10,6 +10,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "common.cuh"
@@ -21,12 +22,18 @@ namespace dsv4b {
 // Router scoring and selection (dsv4_ops.c:102-141, with sigmoid from
 // tools/dsv4_ref.py:64-93). One block. fixed != nullptr means hash routing:
 // the experts are given (tid2eid row), the weights still come from scores.
+// A batch: block b routes token b (logits, sel_out, w_out s_ms apart; its
+// token id tok_stride ints after token b - 1's).
 __global__ void k_route(const float *logits, const float *bias, const int *fixed,
                         const int64_t *tid2eid, const int *token, int n, int topk,
-                        float route_scale, int score_func, int *sel_out, float *w_out)
+                        float route_scale, int score_func, int *sel_out, float *w_out, long s_ms, int tok_stride)
 {
     pdl_trigger();
     pdl_wait();
+    logits += blockIdx.x * s_ms;
+    sel_out += blockIdx.x * s_ms;
+    w_out += blockIdx.x * s_ms;
+    if (token) token += (size_t)blockIdx.x * tok_stride;
     __shared__ float orig[kMoeMaxExperts], sc[kMoeMaxExperts];
     __shared__ int chosen[kMoeMaxTopk];
     const int tid = threadIdx.x, nthr = blockDim.x;
@@ -111,58 +118,89 @@ __global__ void k_combine(float *out, const float *acc, const float *w, int topk
 }
 
 int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float *x,
-                const int *token, cudaStream_t st, bool combine, const Exch *ex)
+                const int *token, cudaStream_t st, bool combine, const Exch *ex, int nseq, long s_ms, long s_x,
+                int tok_stride)
 {
     const int H = L.hidden, I = L.inter, K = L.topk;
     PdlChain chain;
-    if (K < 1 || K + 1 > kGemvMaxItems || K > kMoeMaxTopk || L.n_experts > kMoeMaxExperts) return -1;
-    // router
-    if (gemv(L.gate.wdt, S.logits, L.n_experts, x, H, L.gate.w, L.gate.s, L.n_experts, H,
-             L.gate.blk_r, L.gate.blk_c, 1, st, L.gate.f16s != 0))
+    if (K < 1 || K > kMoeMaxTopk || L.n_experts > kMoeMaxExperts || nseq < 1) return -1;
+    if (nseq > 1 && (combine || ex)) return -1;          // a batch folds its combine into the next mHC
+    if (nseq == 1) {
+        s_ms = 0;
+        s_x = H;
+    }
+    // router: one item per token, each the batch-1 arithmetic
+    if (gemv(L.gate.wdt, S.logits, nseq > 1 ? s_ms : L.n_experts, x, s_x, L.gate.w, L.gate.s, L.n_experts, H,
+             L.gate.blk_r, L.gate.blk_c, nseq, st, L.gate.f16s != 0))
         return -1;
-    launch(k_route, dim3(1), dim3(256), 0, st, S.logits, L.bias, L.fixed, L.tid2eid, token, L.n_experts, K,
-                               L.route_scale, L.score_func, S.sel, S.wts);
+    launch(k_route, dim3(nseq), dim3(256), 0, st, S.logits, L.bias, L.fixed, L.tid2eid, token, L.n_experts, K,
+           L.route_scale, L.score_func, S.sel, S.wts, s_ms, tok_stride);
     const int Is = L.has_shared ? L.inter_shared : 0;
-    float *hs = S.h + (size_t)K * I, *accs = S.acc + (size_t)K * H;
-    GemvItem it[kGemvMaxItems];
+    // the items of one stage (every token's selected experts, then its shared
+    // expert), launched kGemvMaxItems at a time: a launch's grouping never
+    // changes an item's arithmetic
+    std::vector<GemvItem> items;
+    auto flush = [&]() -> int {
+        for (size_t i0 = 0; i0 < items.size(); i0 += kGemvMaxItems) {
+            const int n = (int)std::min<size_t>(kGemvMaxItems, items.size() - i0);
+            if (gemv_group(items.data() + i0, n, st)) return -1;
+        }
+        items.clear();
+        return 0;
+    };
     // gate / up of every selected expert and the shared one, SwiGLU in the
     // epilogue: h[k] = swiglu(w1 x, w3 x) (dsv4_layer.c:199-206)
-    for (int k = 0; k < K; k++) {
-        if (!gemv_item(it[k], L.efmt, nullptr, nullptr, I, H, L.eblk_r, L.eblk_c, x, S.h + (size_t)k * I,
-                       L.ef16s != 0))
-            return -1;
-        it[k].wtab = L.w1tab; it[k].stab = L.s1tab;
-        it[k].w2tab = L.w3tab; it[k].s2tab = L.s3tab;
-        it[k].sel = S.sel; it[k].slot = k;
-        it[k].pair = 1; it[k].limit = L.swiglu_limit;
+    for (int b = 0; b < nseq; b++) {
+        const float *xb = x + (size_t)b * s_x;
+        float *hb = S.h + (size_t)b * s_ms;
+        const int *selb = S.sel + (size_t)b * s_ms;
+        for (int k = 0; k < K; k++) {
+            GemvItem it;
+            if (!gemv_item(it, L.efmt, nullptr, nullptr, I, H, L.eblk_r, L.eblk_c, xb, hb + (size_t)k * I,
+                           L.ef16s != 0))
+                return -1;
+            it.wtab = L.w1tab; it.stab = L.s1tab;
+            it.w2tab = L.w3tab; it.s2tab = L.s3tab;
+            it.sel = selb; it.slot = k;
+            it.pair = 1; it.limit = L.swiglu_limit;
+            items.push_back(it);
+        }
+        if (Is) {
+            GemvItem it;
+            if (!gemv_item(it, L.sh[0].wdt, L.sh[0].w, L.sh[0].s, Is, H, L.sh[0].blk_r, L.sh[0].blk_c, xb,
+                           hb + (size_t)K * I, L.sh[0].f16s && L.sh[1].f16s) ||
+                L.sh[1].wdt != L.sh[0].wdt)
+                return -1;
+            it.W2 = L.sh[1].w; it.S2 = L.sh[1].s;
+            it.pair = 1; it.limit = L.swiglu_limit;
+            items.push_back(it);
+        }
     }
-    int n = K;
-    if (Is) {
-        if (!gemv_item(it[n], L.sh[0].wdt, L.sh[0].w, L.sh[0].s, Is, H, L.sh[0].blk_r, L.sh[0].blk_c, x, hs,
-                       L.sh[0].f16s && L.sh[1].f16s) ||
-            L.sh[1].wdt != L.sh[0].wdt)
-            return -1;
-        it[n].W2 = L.sh[1].w; it[n].S2 = L.sh[1].s;
-        it[n].pair = 1; it[n].limit = L.swiglu_limit;
-        n++;
-    }
-    if (gemv_group(it, n, st)) return -1;
+    if (flush()) return -1;
     // down projections into the per-k accumulators
-    for (int k = 0; k < K; k++) {
-        if (!gemv_item(it[k], L.efmt, nullptr, nullptr, H, I, L.eblk_r, L.eblk_c, S.h + (size_t)k * I,
-                       S.acc + (size_t)k * H, L.ef16s != 0))
-            return -1;
-        it[k].wtab = L.w2tab; it[k].stab = L.s2tab;
-        it[k].sel = S.sel; it[k].slot = k;
+    for (int b = 0; b < nseq; b++) {
+        const float *hb = S.h + (size_t)b * s_ms;
+        float *accb = S.acc + (size_t)b * s_ms;
+        const int *selb = S.sel + (size_t)b * s_ms;
+        for (int k = 0; k < K; k++) {
+            GemvItem it;
+            if (!gemv_item(it, L.efmt, nullptr, nullptr, H, I, L.eblk_r, L.eblk_c, hb + (size_t)k * I,
+                           accb + (size_t)k * H, L.ef16s != 0))
+                return -1;
+            it.wtab = L.w2tab; it.stab = L.s2tab;
+            it.sel = selb; it.slot = k;
+            items.push_back(it);
+        }
+        if (Is) {
+            GemvItem it;
+            if (!gemv_item(it, L.sh[2].wdt, L.sh[2].w, L.sh[2].s, H, Is, L.sh[2].blk_r, L.sh[2].blk_c,
+                           hb + (size_t)K * I, accb + (size_t)K * H, L.sh[2].f16s != 0))
+                return -1;
+            items.push_back(it);
+        }
     }
-    n = K;
-    if (Is) {
-        if (!gemv_item(it[n], L.sh[2].wdt, L.sh[2].w, L.sh[2].s, H, Is, L.sh[2].blk_r, L.sh[2].blk_c, hs, accs,
-                       L.sh[2].f16s != 0))
-            return -1;
-        n++;
-    }
-    if (gemv_group(it, n, st)) return -1;
+    if (flush()) return -1;
+    float *accs = S.acc + (size_t)K * H;
     // sharded: every rank holds a slice of each expert's inter dimension, so
     // its outputs are partial sums over that slice; add them up across ranks
     if (ex && xreduce_sum(*ex, S.acc, (size_t)(K + (Is ? 1 : 0)) * H, st)) return -1;

@@ -48,8 +48,13 @@ struct MoeScratch {
 // S.acc / S.wts itself (the decode step folds it into the next mHC launch).
 // ex (sharded decode): where the per-slot partial outputs are summed across
 // ranks before the combine; null on one GPU.
+// A batch of nseq tokens (combine false, ex null): token b's x at x + b s_x,
+// its scratch S shifted by b s_ms floats, its token id at token + b
+// tok_stride; every token's experts and arithmetic are those of a batch-1
+// call.
 int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float *x,
-                const int *token, cudaStream_t st, bool combine = true, const Exch *ex = nullptr);
+                const int *token, cudaStream_t st, bool combine = true, const Exch *ex = nullptr, int nseq = 1,
+                long s_ms = 0, long s_x = 0, int tok_stride = 0);
 size_t moe_scratch_floats(int hidden, int inter, int inter_shared, int n_experts, int topk);
 void moe_scratch_carve(MoeScratch &S, float *base, int hidden, int inter, int inter_shared,
                        int n_experts, int topk);

@@ -82,6 +82,12 @@ def _declare(L):
         "dsv4b_model_step_async": ([vp, vp], i),
         "dsv4_cuda_model_decode": ([vp, i, i, vp], i),
         "dsv4_cuda_model_create_synthetic": ([vp, i, C.c_ulonglong], vp),
+        "dsv4_cuda_model_create_synthetic_batch": ([vp, i, C.c_ulonglong, i], vp),
+        "dsv4_cuda_model_create_batch": ([vp, vp, vp, vp, i, i], vp),
+        "dsv4b_model_n_seq": ([vp], i),
+        "dsv4b_model_begin_batch": ([vp, vp, i], i),
+        "dsv4b_model_generate_batch": ([vp, vp, i, i, vp], i),
+        "dsv4b_model_decode_batch": ([vp, vp, i, vp], i),
         "dsv4_cuda_model_bytes": ([vp], sz),
         "dsv4_cuda_model_step_kernels": ([vp], i),
         "dsv4b_shard_check": ([vp, i], i),
@@ -354,20 +360,26 @@ class Model:
     """A whole model resident on the device (dsv4_cuda_model_create) from a
     dsv4_model.SyntheticModel or any holder of cfg/mw/layers/experts structs.
     With world > 1 (synthetic only), this rank's share of a model sharded over
-    world GPUs (one process per GPU, all stepping in lockstep)."""
+    world GPUs (one process per GPU, all stepping in lockstep). With n_seq > 1
+    (one GPU), a batch of n_seq sequences stepped together
+    (generate_batch / begin_batch / decode_batch)."""
 
-    def __init__(self, sm, max_pos, synthetic_seed=None, rank=0, world=1, nccl_id=None):
+    def __init__(self, sm, max_pos, synthetic_seed=None, rank=0, world=1, nccl_id=None, n_seq=1):
         """sm: a dsv4_model.SyntheticModel (host weights), or with
         synthetic_seed set, any holder of .cfg/.d for an on-device model."""
-        self.sm, self.max_pos = sm, max_pos
+        self.sm, self.max_pos, self.n_seq = sm, max_pos, n_seq
         self.vocab = sm.d["vocab"]
+        if n_seq != 1 and world != 1:
+            raise ValueError("a batched model runs on one GPU")
         if synthetic_seed is None:
             if world != 1:
                 raise ValueError("sharded models are synthetic (synthetic_seed)")
-            self.h = lib().dsv4_cuda_model_create(C.addressof(sm.cfg), C.addressof(sm.mw),
-                                                  C.addressof(sm.layers), C.addressof(sm.experts), max_pos)
+            self.h = lib().dsv4_cuda_model_create_batch(C.addressof(sm.cfg), C.addressof(sm.mw),
+                                                        C.addressof(sm.layers), C.addressof(sm.experts), max_pos,
+                                                        int(n_seq))
         elif world == 1:
-            self.h = lib().dsv4_cuda_model_create_synthetic(C.addressof(sm.cfg), max_pos, synthetic_seed)
+            self.h = lib().dsv4_cuda_model_create_synthetic_batch(C.addressof(sm.cfg), max_pos, synthetic_seed,
+                                                                  int(n_seq))
         else:
             idb = C.create_string_buffer(bytes(nccl_id), len(nccl_id))
             self.h = lib().dsv4_cuda_model_create_synthetic_sharded(C.addressof(sm.cfg), max_pos, synthetic_seed,
@@ -402,6 +414,33 @@ class Model:
         if n < 0:
             raise RuntimeError("dsv4_cuda_model_generate failed")
         return out[:n]
+
+    def begin_batch(self, prompts):
+        """prompts: [n_seq][n_prompt] int32, one row per sequence."""
+        p = np.ascontiguousarray(prompts, np.int32)
+        if p.ndim != 2 or p.shape[0] != self.n_seq:
+            raise ValueError("prompts must be [n_seq][n_prompt]")
+        check(lib().dsv4b_model_begin_batch(self.h, p.ctypes.data, p.shape[1]), "dsv4b_model_begin_batch")
+
+    def generate_batch(self, prompts, n_gen):
+        """Greedy tokens [n_seq][n_gen + 1] of every sequence, from its last
+        prompt position on."""
+        p = np.ascontiguousarray(prompts, np.int32)
+        if p.ndim != 2 or p.shape[0] != self.n_seq:
+            raise ValueError("prompts must be [n_seq][n_prompt]")
+        out = np.empty((self.n_seq, n_gen + 1), np.int32)
+        n = lib().dsv4b_model_generate_batch(self.h, p.ctypes.data, p.shape[1], n_gen, out.ctypes.data)
+        if n < 0:
+            raise RuntimeError("dsv4b_model_generate_batch failed")
+        return out[:, :n]
+
+    def decode_batch(self, tokens, pos):
+        """Every sequence's token at pos in (host), the next tokens out."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        nxt = np.zeros(self.n_seq, np.int32)
+        check(lib().dsv4b_model_decode_batch(self.h, t.ctypes.data, int(pos), nxt.ctypes.data),
+              "dsv4b_model_decode_batch")
+        return nxt
 
     def step_async(self, stream=None):
         check(lib().dsv4b_model_step_async(self.h, stream_ptr(stream)), "dsv4b_model_step_async")

@@ -174,6 +174,33 @@ int dsv4_cuda_model_decode(dsv4b_model *m, int token, int pos, int *next_token);
 dsv4b_model *dsv4_cuda_model_create_synthetic(const DSV4Cfg *c, int max_pos,
                                               unsigned long long seed);
 
+/* ---- batched decode: n_seq sequences (<= 64) stepped in lockstep by one
+ * graph. The reference's batched layer (dsv4_layer_forward_n,
+ * src/model/dsv4_layer.c:856-918) runs nt tokens of ONE sequence and keeps
+ * its attention strictly per token; here each of the n_seq sequences has its
+ * own caches, prompt and greedy tokens, and every launch of the step covers
+ * all of them (a grid dimension, or one GEMV item per sequence, so every
+ * sequence's arithmetic is exactly that of a one-sequence model: its tokens
+ * equal the ones dsv4_cuda_model_generate gives for its prompt). Needs the
+ * fused mHC shapes (hc_mult <= 4) and one GPU. */
+dsv4b_model *dsv4_cuda_model_create_batch(const DSV4Cfg *c, const DSV4ModelW *mw,
+                                          const DSV4LayerW *layers,
+                                          const DSV4ExpertW *experts, int max_pos, int n_seq);
+dsv4b_model *dsv4_cuda_model_create_synthetic_batch(const DSV4Cfg *c, int max_pos,
+                                                    unsigned long long seed, int n_seq);
+int dsv4b_model_n_seq(const dsv4b_model *m);
+
+/* dsv4_cuda_model_begin / _generate for a batch: prompts [n_seq][n_prompt]
+ * (every prompt the same length); out [n_seq][n_gen + 1]. The
+ * one-sequence calls (begin, step, generate, decode) return -1 on a batched
+ * model; dsv4b_model_step_async steps every sequence. */
+int dsv4b_model_begin_batch(dsv4b_model *m, const int *prompts, int n_prompt);
+int dsv4b_model_generate_batch(dsv4b_model *m, const int *prompts, int n_prompt, int n_gen,
+                               int *out);
+/* dsv4_cuda_model_decode for a batch: tokens[n_seq] at position pos in,
+ * next_tokens[n_seq] out. 0 or -1. */
+int dsv4b_model_decode_batch(dsv4b_model *m, const int *tokens, int pos, int *next_tokens);
+
 /* ---- multi-GPU decode (one process per GPU). No reference counterpart: the
  * reference runs on one device (dsv4_cuda.cu:243-249); this is the sharding
  * its design notes ask for -- routed and shared experts split along their

@@ -249,6 +249,9 @@ __device__ __forceinline__ void group_tile(const GemvItem &it, int tile, unsigne
     }
 }
 
+// NP: token pairs a tensor-core item may carry (0: one token, the batch-1
+// launches, with the pair logic compiled out; 1: up to two; 2: up to four).
+template <int NP>
 __global__ void __launch_bounds__(kGemvThreads, 2)
 k_gemv_group(const __grid_constant__ GemvBatch b)
 {
@@ -259,9 +262,9 @@ k_gemv_group(const __grid_constant__ GemvBatch b)
     const GemvItem &it = b.it[i];
     const int tile = (int)blockIdx.x - it.tile0;
     if (it.mma) {
-        if (it.fmt == DSV4B_WFP8) mma_tile<DSV4B_WFP8>(it, tile, gsm);
-        else if (it.fmt == DSV4B_WFP4) mma_tile<DSV4B_WFP4>(it, tile, gsm);
-        else mma_tile<DSV4B_WBF16>(it, tile, gsm);
+        if (it.fmt == DSV4B_WFP8) mma_tile<DSV4B_WFP8, NP>(it, tile, gsm);
+        else if (it.fmt == DSV4B_WFP4) mma_tile<DSV4B_WFP4, NP>(it, tile, gsm);
+        else mma_tile<DSV4B_WBF16, NP>(it, tile, gsm);
         return;
     }
     switch (it.fmt) {
@@ -450,6 +453,20 @@ bool gemv_mma_shape(int fmt, int cols, int blk_r, int blk_c, bool f16s)
     return true;
 }
 
+int gemv_item_tokens(GemvItem &it, int want, long xts, long yts)
+{
+    if (!it.mma || want <= 1) return 1;
+    const int nb = it.cols / mma_unit_cols(it.fmt), minrows = it.pair ? 32 : 16;
+    int k = want < 4 ? want : 4;
+    while (k > 1 && mma_smem(it.fmt, nb, minrows, k) > (size_t)kMmaTileSmem) k--;
+    if (k > 1) {
+        it.nt = k;
+        it.xts = (int)xts;
+        it.yts = (int)yts;
+    }
+    return k;
+}
+
 bool fp4_scales_f16(const uint8_t *s, size_t n)
 {
     for (size_t i = 0; i < n; i++)
@@ -488,9 +505,9 @@ int gemv_group(GemvItem *items, int n, cudaStream_t st)
             continue;
         }
         if (it.mma) {
-            const int nb = it.cols / mma_unit_cols(it.fmt);
+            const int nb = it.cols / mma_unit_cols(it.fmt), ntk = it.nt > 1 ? it.nt : 1;
             // a multiple of 16 virtual rows, within the shared memory budget
-            int cap = (int)((kMmaTileSmem - mma_smem(it.fmt, nb, 0)) / 64) & ~15;
+            int cap = (int)((kMmaTileSmem - mma_smem(it.fmt, nb, 0, ntk)) / (64 * ntk)) & ~15;
             cap = cap < 512 ? cap : 512;
             if (cap < 16) return -1;
             int tr = ((int)(target / it.rowbytes) + 15) & ~15;
@@ -506,7 +523,7 @@ int gemv_group(GemvItem *items, int n, cudaStream_t st)
             it.tr = tr;
             const int per = it.pair ? tr / 2 : tr;
             blocks += (it.rows + per - 1) / per;
-            const size_t sm = mma_smem(it.fmt, nb, tr);
+            const size_t sm = mma_smem(it.fmt, nb, tr, ntk);
             if (sm > smem) smem = sm;
             b.it[i] = it;
             continue;
@@ -537,8 +554,11 @@ int gemv_group(GemvItem *items, int n, cudaStream_t st)
         b.it[i] = it;
     }
     if (!blocks) return 0;
-    if (smem_optin(k_gemv_group, kMmaTileSmem)) return -1;
-    return launch(k_gemv_group, dim3(blocks), dim3(kGemvThreads), smem, st, b) ==
+    int maxnt = 1;
+    for (int i = 0; i < n; i++) maxnt = items[i].nt > maxnt ? items[i].nt : maxnt;
+    auto kern = maxnt > 2 ? k_gemv_group<2> : maxnt > 1 ? k_gemv_group<1> : k_gemv_group<0>;
+    if (smem_optin(kern, kMmaTileSmem)) return -1;
+    return launch(kern, dim3(blocks), dim3(kGemvThreads), smem, st, b) ==
                    cudaSuccess
                ? 0
                : -1;

@@ -57,10 +57,10 @@ __host__ __device__ inline int mma_unit_mmas(int fmt) { return fmt == DSV4B_WFP4
 // Dynamic shared memory of a tile of tr virtual rows over nb units: the
 // ring, the FP4 scale ring, the x fragments, the per-unit exponents and the
 // eight run sums (double) of every virtual row.
-__host__ __device__ inline size_t mma_smem(int fmt, int nb, int tr)
+__host__ __device__ inline size_t mma_smem(int fmt, int nb, int tr, int nt = 1)
 {
-    return (size_t)kMmaRing + kMmaSRing + (size_t)nb * mma_unit_mmas(fmt) * kMmaXpPerMma +
-           (((size_t)nb * 4 + 15) & ~(size_t)15) + (size_t)tr * 8 * 8;
+    return (size_t)kMmaRing + kMmaSRing + (size_t)nt * nb * mma_unit_mmas(fmt) * kMmaXpPerMma +
+           (((size_t)nt * nb * 4 + 15) & ~(size_t)15) + (size_t)nt * tr * 8 * 8;
 }
 
 __device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -158,7 +158,13 @@ __device__ __forceinline__ void x_pieces(const float4 &x, float sc, uint2 (&out)
         out[q] = make_uint2((uint32_t)p[q][0] | ((uint32_t)p[q][1] << 16), (uint32_t)p[q][2] | ((uint32_t)p[q][3] << 16));
 }
 
-template <int FMT>
+// NP token pairs per item (it.nt <= 2 NP tokens, x / y it.xts / it.yts
+// floats apart): the two tokens of a pair share every mma, token 2p in B
+// columns 0-2 and token 2p+1 in columns 3-5. The tensor core forms each
+// column from that column's operands alone, so a token's result is the one
+// it gets on its own; the weights are streamed and decoded once per item.
+// NP = 0: exactly one token (batch-1 launches), the pair logic compiled out.
+template <int FMT, int NP>
 __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned char *smem)
 {
     using F = MmaFmt<FMT>;
@@ -166,17 +172,29 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
     constexpr bool BF = FMT == DSV4B_WBF16;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
     const int nb = it.cols / F::COLS, rb = it.rowbytes, trh = it.tr >> 1;
+    constexpr int NPP = NP > 0 ? NP : 1;                 // accumulator sets
+    const int nt = NP > 0 && it.nt > 1 ? it.nt : 1;
+    const size_t xtab = (size_t)nb * MPU * 12;            // one token's x fragments (uint2)
     uint4 *ring = reinterpret_cast<uint4 *>(smem);
     uint2 *sring = reinterpret_cast<uint2 *>(smem + kMmaRing);
-    uint2 *xp = reinterpret_cast<uint2 *>(smem + kMmaRing + kMmaSRing);
-    int *kbs = reinterpret_cast<int *>(smem + kMmaRing + kMmaSRing + (size_t)nb * MPU * kMmaXpPerMma);
-    double *runs = reinterpret_cast<double *>(smem + kMmaRing + kMmaSRing + (size_t)nb * MPU * kMmaXpPerMma +
-                                              (((size_t)nb * 4 + 15) & ~(size_t)15));   // [tr][8]
+    uint2 *xp = reinterpret_cast<uint2 *>(smem + kMmaRing + kMmaSRing);                         // [nt][...]
+    int *kbs = reinterpret_cast<int *>(smem + kMmaRing + kMmaSRing + (size_t)nt * nb * MPU * kMmaXpPerMma);  // [nt][nb]
+    double *runs = reinterpret_cast<double *>(smem + kMmaRing + kMmaSRing + (size_t)nt * nb * MPU * kMmaXpPerMma +
+                                              (((size_t)nt * nb * 4 + 15) & ~(size_t)15));   // [nt][tr][8]
 
     const uint8_t *W = it.W, *S = it.S, *W2 = it.W2, *S2 = it.S2;
+    const float *X = it.x;
+    float *Y = it.y;
     if (it.wtab) {
         pdl_wait();                  // the selection comes from the previous kernel
-        const int e = __ldcg(it.sel + it.slot);
+        int si = it.slot;
+        if (it.perm) {               // a batch's routed item: its token and slot
+            const int pe = __ldcg(it.perm + it.slot), tk = pe >> 8, kk = pe & 255;
+            X += (size_t)tk * it.xs + (size_t)kk * it.xk;
+            Y += (size_t)tk * it.ys + (size_t)kk * it.yk;
+            si = tk * it.ss + kk;
+        }
+        const int e = __ldcg(it.sel + si);
         W = it.wtab[e];
         S = it.stab ? it.stab[e] : nullptr;
         if (it.pair) {
@@ -236,61 +254,79 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
     for (int q = 0; q < kMmaStages - 1; q++) issue_next();
     pdl_wait();
 
-    // x fragments: every warp builds those of its own run (warps sharing a
-    // run write the same values); lane = (mma, t), two passes for the 16
-    // k16-steps of an FP4 unit. All of a warp's x loads are issued before any
-    // is used.
+    // x fragments: every warp builds those of its own run for every token
+    // (warps sharing a run write the same values); lane = (mma, t), two
+    // passes for the 16 k16-steps of an FP4 unit. All of a token's x loads
+    // are issued before any is used.
     constexpr int XU = kMmaMaxBlocks / 8, XH = MPU / 8;
-    float4 xv[XU][XH];
+    for (int tk = 0; tk < nt; tk++) {
+        const float *xt = X + (size_t)tk * it.xts;
+        uint2 *xpt = xp + tk * xtab;
+        float4 xv[XU][XH];
 #pragma unroll
-    for (int u = 0; u < XU; u++) {
-        const int cb = cb0 + u;
+        for (int u = 0; u < XU; u++) {
+            const int cb = cb0 + u;
 #pragma unroll
-        for (int h = 0; h < XH; h++) {
-            const int m = h * 8 + (lane >> 2), tt = lane & 3, j = m / MPC, i = m - j * MPC;
-            if (cb >= cb1) {
-                xv[u][h] = make_float4(0.f, 0.f, 0.f, 0.f);
-            } else if constexpr (FMT == DSV4B_WFP4) {
-                // k16 step i pairs elements (8 (i/2) + 2 (i%2) + {0, 4}) and
-                // (... + {1, 5}) of the lane's 32, as e2m1_word() pairs them
-                const float *xb = it.x + cb * F::COLS + 4 * E * j + E * tt + 8 * (i >> 1) + 2 * (i & 1);
-                const float2 lo = ld_f2(xb), hi = ld_f2(xb + 4);
-                xv[u][h] = make_float4(lo.x, hi.x, lo.y, hi.y);
-            } else {
-                xv[u][h] = ld_f4(it.x + cb * F::COLS + 4 * E * j + E * tt + 4 * i);
+            for (int h = 0; h < XH; h++) {
+                const int m = h * 8 + (lane >> 2), tt = lane & 3, j = m / MPC, i = m - j * MPC;
+                if (cb >= cb1) {
+                    xv[u][h] = make_float4(0.f, 0.f, 0.f, 0.f);
+                } else if constexpr (FMT == DSV4B_WFP4) {
+                    // k16 step i pairs elements (8 (i/2) + 2 (i%2) + {0, 4}) and
+                    // (... + {1, 5}) of the lane's 32, as e2m1_word() pairs them
+                    const float *xb = xt + cb * F::COLS + 4 * E * j + E * tt + 8 * (i >> 1) + 2 * (i & 1);
+                    const float2 lo = ld_f2(xb), hi = ld_f2(xb + 4);
+                    xv[u][h] = make_float4(lo.x, hi.x, lo.y, hi.y);
+                } else {
+                    xv[u][h] = ld_f4(xt + cb * F::COLS + 4 * E * j + E * tt + 4 * i);
+                }
             }
         }
-    }
 #pragma unroll
-    for (int u = 0; u < XU; u++) {
-        const int cb = cb0 + u;
-        if (cb >= cb1) break;
-        float mx = 0.0f;
+        for (int u = 0; u < XU; u++) {
+            const int cb = cb0 + u;
+            if (cb >= cb1) break;
+            float mx = 0.0f;
 #pragma unroll
-        for (int h = 0; h < XH; h++)
-            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(xv[u][h].x), fabsf(xv[u][h].y)),
-                                 fmaxf(fabsf(xv[u][h].z), fabsf(xv[u][h].w))));
-        mx = warp_max_f(mx);
-        int k = 0;
-        if (!BF && mx > 0.0f && mx == mx) {
-            const int ex = (int)((__float_as_uint(mx) >> 23) & 0xFFu) - 127;   // floor(log2 mx), normal mx
-            k = 14 - (ex < -126 ? -126 : ex);
-            k = k > 126 ? 126 : (k < -126 ? -126 : k);
+            for (int h = 0; h < XH; h++)
+                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(xv[u][h].x), fabsf(xv[u][h].y)),
+                                     fmaxf(fabsf(xv[u][h].z), fabsf(xv[u][h].w))));
+            mx = warp_max_f(mx);
+            int k = 0;
+            if (!BF && mx > 0.0f && mx == mx) {
+                const int ex = (int)((__float_as_uint(mx) >> 23) & 0xFFu) - 127;   // floor(log2 mx), normal mx
+                k = 14 - (ex < -126 ? -126 : ex);
+                k = k > 126 ? 126 : (k < -126 ? -126 : k);
+            }
+#pragma unroll
+            for (int h = 0; h < XH; h++) {
+                const int m = h * 8 + (lane >> 2), tt = lane & 3;
+                uint2 pc[3];
+                x_pieces<BF>(xv[u][h], BF ? 1.0f : pow2f(k), pc);
+#pragma unroll
+                for (int p = 0; p < 3; p++) xpt[(cb * MPU + m) * 12 + tt * 3 + p] = pc[p];
+            }
+            if (lane == 0) kbs[tk * nb + cb] = k;
         }
-#pragma unroll
-        for (int h = 0; h < XH; h++) {
-            const int m = h * 8 + (lane >> 2), tt = lane & 3;
-            uint2 pc[3];
-            x_pieces<BF>(xv[u][h], BF ? 1.0f : pow2f(k), pc);
-#pragma unroll
-            for (int p = 0; p < 3; p++) xp[(cb * MPU + m) * 12 + tt * 3 + p] = pc[p];
-        }
-        if (lane == 0) kbs[cb] = k;
     }
     __syncwarp();
 
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
-    double run_a = 0.0, run_b = 0.0;                 // rows g, g + 8 of the current row group
+    // this lane's B source: token 2 p + (g >= 3) of pair p, piece g % 3
+    // (columns 6 and 7 stay zero), resolved once
+    const uint2 *bsrc[NPP];
+#pragma unroll
+    for (int pp = 0; pp < NPP; pp++) {
+        const int tk = 2 * pp + (g < 3 ? 0 : 1);
+        bsrc[pp] = (g < (NP > 0 ? 6 : 3) && tk < nt) ? xp + tk * xtab + t * 3 + (g < 3 ? g : g - 3) : nullptr;
+    }
+    const bool two = NP > 0 && nt > 1;               // a second token in pair 0 (lanes t = 2 flush it)
+    float c[NPP][4];
+    double run_a[NPP], run_b[NPP];                   // lanes t = 0 / 2: rows g, g + 8 of the current row group
+#pragma unroll
+    for (int pp = 0; pp < NPP; pp++) {
+        c[pp][0] = c[pp][1] = c[pp][2] = c[pp][3] = 0.f;
+        run_a[pp] = run_b[pp] = 0.0;
+    }
     int c_rg = sub, c_cb = cb0, c_s = 0;
     for (int q = 0; q < nsteps; q++) {
         issue_next();
@@ -301,7 +337,7 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
         float sa = 1.0f, sbv = 1.0f;
         bool s2a = false, s2b = false;
         const int ra = row_of(c_rg * 16 + g, s2a), rbw = row_of(c_rg * 16 + g + 8, s2b);
-        if (FMT == DSV4B_WFP8 && t == 0 && c_s == STEPS - 1) {
+        if (FMT == DSV4B_WFP8 && (t == 0 || (t == 2 && two)) && c_s == STEPS - 1) {
             const int col = (c_cb * F::COLS) >> it.lbc;
             sa = ra >= 0 ? e8m0(__ldg((s2a ? S2 : S) + (size_t)(ra >> it.lbr) * it.sc + col)) : 0.0f;
             sbv = rbw >= 0 ? e8m0(__ldg((s2b ? S2 : S) + (size_t)(rbw >> it.lbr) * it.sc + col)) : 0.0f;
@@ -328,46 +364,76 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
 #pragma unroll
             for (int i = 0; i < MPC; i++) {
                 const int m = j * MPC + i;
-                uint2 b = make_uint2(0u, 0u);
-                if (g < 3) b = xp[(c_cb * MPU + m) * 12 + t * 3 + g];
+                // the weights' A fragments, formed once for every token pair
+                uint32_t a0, a1, a2, a3;
                 if constexpr (FMT == DSV4B_WFP8) {
                     const uint32_t va = word_of(wa, i), vb = word_of(wb, i);
-                    mma_f16(c, e4m3x2_h2(va), e4m3x2_h2(vb), e4m3x2_h2(va >> 16), e4m3x2_h2(vb >> 16), b.x, b.y);
+                    a0 = e4m3x2_h2(va);
+                    a1 = e4m3x2_h2(vb);
+                    a2 = e4m3x2_h2(va >> 16);
+                    a3 = e4m3x2_h2(vb >> 16);
                 } else if constexpr (FMT == DSV4B_WFP4) {
                     // word i/2 of each row (decoded once for both of its
                     // steps); step i takes nibble pairs (2 (i%2), +4) and
                     // (2 (i%2) + 1, +4)
-                    uint32_t ra[4], rbv[4];
-                    e2m1_word(word_of(wa, i >> 1), ra);
-                    e2m1_word(word_of(wb, i >> 1), rbv);
+                    uint32_t ra4[4], rb4[4];
+                    e2m1_word(word_of(wa, i >> 1), ra4);
+                    e2m1_word(word_of(wb, i >> 1), rb4);
                     const int q0 = 2 * (i & 1);
-                    mma_f16(c, hmul2(ra[q0], ha), hmul2(rbv[q0], hb), hmul2(ra[q0 + 1], ha), hmul2(rbv[q0 + 1], hb),
-                            b.x, b.y);
+                    a0 = hmul2(ra4[q0], ha);
+                    a1 = hmul2(rb4[q0], hb);
+                    a2 = hmul2(ra4[q0 + 1], ha);
+                    a3 = hmul2(rb4[q0 + 1], hb);
                 } else {
-                    mma_bf16(c, word_of(wa, 2 * i), word_of(wb, 2 * i), word_of(wa, 2 * i + 1),
-                             word_of(wb, 2 * i + 1), b.x, b.y);
+                    a0 = word_of(wa, 2 * i);
+                    a1 = word_of(wb, 2 * i);
+                    a2 = word_of(wa, 2 * i + 1);
+                    a3 = word_of(wb, 2 * i + 1);
+                }
+                const int xo = (c_cb * MPU + m) * 12;
+#pragma unroll
+                for (int pp = 0; pp < NPP; pp++) {
+                    uint2 b = make_uint2(0u, 0u);
+                    if (bsrc[pp]) b = bsrc[pp][xo];
+                    if constexpr (BF) mma_bf16(c[pp], a0, a1, a2, a3, b.x, b.y);
+                    else mma_f16(c[pp], a0, a1, a2, a3, b.x, b.y);
                 }
             }
         }
         if (FMT == DSV4B_WFP4) __syncwarp();
         if (c_s == STEPS - 1) {
-            // flush the unit: rows g and g + 8 sit on lane t = 0 (n = 0, 1)
-            // and lane t = 1 (n = 2)
-            const float n2a = __shfl_sync(0xffffffffu, c[0], lane | 1);
-            const float n2b = __shfl_sync(0xffffffffu, c[2], lane | 1);
-            if (t == 0) {
-                const float un = pow2f(-kbs[c_cb]);
-                const float qa = __fmul_rn(__fmul_rn(__fadd_rn(__fadd_rn(c[0], c[1]), n2a), un), sa);
-                const float qb = __fmul_rn(__fmul_rn(__fadd_rn(__fadd_rn(c[2], c[3]), n2b), un), sbv);
-                run_a = __dadd_rn(run_a, (double)qa);
-                run_b = __dadd_rn(run_b, (double)qb);
-                if (c_cb == cb1 - 1) {                    // the run ends: its sums are final
-                    runs[(c_rg * 16 + g) * 8 + run] = run_a;
-                    runs[(c_rg * 16 + g + 8) * 8 + run] = run_b;
-                    run_a = run_b = 0.0;
+            // flush the unit: token A's pieces (n = 0, 1, 2) sit on lanes t = 0
+            // (n = 0, 1) and t = 1 (n = 2); token B's (n = 3, 4, 5) on t = 1
+            // (n = 3) and t = 2 (n = 4, 5); rows g (c0, c1) and g + 8 (c2, c3)
+#pragma unroll
+            for (int pp = 0; pp < NPP; pp++) {
+                const float n2a = __shfl_sync(0xffffffffu, c[pp][0], lane | 1);
+                const float n2b = __shfl_sync(0xffffffffu, c[pp][2], lane | 1);
+                float n3a = 0.f, n3b = 0.f;
+                if (two) {                                // warp-uniform
+                    n3a = __shfl_sync(0xffffffffu, c[pp][1], (lane & ~3) | 1);
+                    n3b = __shfl_sync(0xffffffffu, c[pp][3], (lane & ~3) | 1);
                 }
+                const int tk = 2 * pp + (t == 2 ? 1 : 0);
+                if ((t == 0 || (NP > 0 && t == 2)) && tk < nt) {
+                    const float un = pow2f(-kbs[tk * nb + c_cb]);
+                    const float pa = t == 0 ? __fadd_rn(__fadd_rn(c[pp][0], c[pp][1]), n2a)
+                                            : __fadd_rn(__fadd_rn(n3a, c[pp][0]), c[pp][1]);
+                    const float pb = t == 0 ? __fadd_rn(__fadd_rn(c[pp][2], c[pp][3]), n2b)
+                                            : __fadd_rn(__fadd_rn(n3b, c[pp][2]), c[pp][3]);
+                    const float qa = __fmul_rn(__fmul_rn(pa, un), sa);
+                    const float qb = __fmul_rn(__fmul_rn(pb, un), sbv);
+                    run_a[pp] = __dadd_rn(run_a[pp], (double)qa);
+                    run_b[pp] = __dadd_rn(run_b[pp], (double)qb);
+                    if (c_cb == cb1 - 1) {                // the run ends: its sums are final
+                        double *rt = runs + (size_t)tk * it.tr * 8;
+                        rt[(c_rg * 16 + g) * 8 + run] = run_a[pp];
+                        rt[(c_rg * 16 + g + 8) * 8 + run] = run_b[pp];
+                        run_a[pp] = run_b[pp] = 0.0;
+                    }
+                }
+                c[pp][0] = c[pp][1] = c[pp][2] = c[pp][3] = 0.f;
             }
-            c[0] = c[1] = c[2] = c[3] = 0.f;
         }
         if (++c_s == STEPS) {
             c_s = 0;
@@ -377,20 +443,24 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
     cp_wait<0>();
     __syncthreads();
     // row totals: the eight run sums of a virtual row added in run order
-    // (an empty run adds 0)
-    auto total = [&](int v) {
+    // (an empty run adds 0), per token
+    auto total = [&](int tk, int v) {
+        const double *rt = runs + (size_t)tk * it.tr * 8;
         double tt = 0.0;
 #pragma unroll
-        for (int w = 0; w < 8; w++) tt = __dadd_rn(tt, w < R ? runs[v * 8 + w] : 0.0);
+        for (int w = 0; w < 8; w++) tt = __dadd_rn(tt, w < R ? rt[v * 8 + w] : 0.0);
         return (float)tt;
     };
     const int nreal = it.pair ? trh : it.tr;
-    for (int r = tid; r < nreal; r += blockDim.x) {
-        const int row = tile * nreal + r;
-        if (row >= it.rows) break;
-        float a = total(r);
-        if (it.pair) a = swiglu_pair(a, total(r + trh), it.limit);
-        it.y[row] = a;
+    for (int tk = 0; tk < nt; tk++) {
+        float *yt = Y + (size_t)tk * it.yts;
+        for (int r = tid; r < nreal; r += blockDim.x) {
+            const int row = tile * nreal + r;
+            if (row >= it.rows) break;
+            float a = total(tk, r);
+            if (it.pair) a = swiglu_pair(a, total(tk, r + trh), it.limit);
+            yt[row] = a;
+        }
     }
 }
 

@@ -22,6 +22,17 @@ struct GemvItem {
     float *y;
     int fmt, rows, cols, sc, lbr, lbc, rowbytes, slot, pair;
     int mma;                // on the tensor cores (gemv_mma.cuh)
+    // Routed items of a batch (tensor-core items only): with perm set, entry
+    // perm[slot] = (token << 8) | k names the token and its selection slot k;
+    // the item reads x + token xs + k xk, writes y + token ys + k yk, and its
+    // expert is sel[token ss + k]. A launch's items then follow an order
+    // chosen on the device (tokens sorted by expert) without changing any
+    // item's arithmetic.
+    const int *perm;
+    int xs, xk, ys, yk, ss;
+    // Tokens of one item (tensor-core items): nt > 1 applies the matrix to nt
+    // vectors x + i xts with results at y + i yts, streaming it once.
+    int nt, xts, yts;
     float limit;
     int tile0, tr;          // first block of this item; virtual rows per block
 };
@@ -49,6 +60,10 @@ bool gemv_item(GemvItem &it, int fmt, const void *W, const uint8_t *S, int rows,
                int blk_c, const float *x, float *y, bool f16s = false);
 // One launch over n <= kGemvMaxItems items (blocks planned here).
 int gemv_group(GemvItem *items, int n, cudaStream_t st);
+// Give a tensor-core item up to `want` tokens (x / y xts / yts floats apart),
+// as many as its shared memory allows; returns the tokens it now covers (1
+// for other items, which stay single-token).
+int gemv_item_tokens(GemvItem &it, int want, long xts, long yts);
 bool gemv_vectorizable(int fmt, const void *W, int cols, int blk_r, int blk_c, const float *x, long xstride);
 // y[t*ystride + o] = sum_c W[o][c] * x[t*xstride + c], t < nt, o < rows.
 int gemv(int fmt, float *y, long ystride, const float *x, long xstride, const void *W, const uint8_t *S,

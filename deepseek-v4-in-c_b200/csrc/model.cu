@@ -71,6 +71,7 @@ struct dsv4b_model {
     // MoE scratch s_ms floats apart
     int nseq;
     long s_ms;
+    int *moe_perm;             // a batch's (token, slot) pairs in expert order
     std::vector<void *> allocs;
     cudaStream_t stream;
     cudaGraph_t graph;
@@ -228,6 +229,7 @@ static bool alloc_common(dsv4b_model *m)
     const int inter_s = c.moe_inter * c.n_shared;
     const size_t nf = moe_scratch_floats(d, c.moe_inter, inter_s, c.n_experts, c.topk);
     m->s_ms = (long)((nf + kMoeMaxTopk + 63) & ~(size_t)63);
+    m->moe_perm = (int *)dcopy(m, nullptr, B * kMoeMaxTopk * 4, &ok);
     float *msb = F(B * m->s_ms);
     if (ok) moe_scratch_carve(m->ms, msb, d, c.moe_inter, inter_s, c.n_experts, c.topk);
     for (int L = 0; L < c.n_layers && ok; L++) {
@@ -279,22 +281,28 @@ struct Grp {
     int n = 0, rc = 0;
 };
 
-// nseq items (a batch: token b's x at x + b xs, its y at y + b ys), each the
-// arithmetic of a batch-1 call; a full group is launched and a new one begun.
+// nseq tokens (a batch: token b's x at x + b xs, its y at y + b ys), as
+// items of up to four tokens where the matrix runs on the tensor cores (one
+// weight stream per item), every token's arithmetic that of a batch-1 call;
+// a full group is launched and a new one begun.
 static void grp_add(Grp &g, const DevMat &w, const float *x, float *y, cudaStream_t st, int nseq = 1, long xs = 0,
                     long ys = 0)
 {
-    for (int b = 0; b < nseq; b++) {
+    for (int b = 0; b < nseq;) {
         const float *xb = x + (size_t)b * xs;
         float *yb = y + (size_t)b * ys;
         if (g.n == kGemvMaxItems) {
             g.rc |= gemv_group(g.it, g.n, st);
             g.n = 0;
         }
-        if (gemv_item(g.it[g.n], w.wdt, w.w, w.s, w.rows, w.cols, w.blk_r, w.blk_c, xb, yb, w.f16s != 0))
+        if (gemv_item(g.it[g.n], w.wdt, w.w, w.s, w.rows, w.cols, w.blk_r, w.blk_c, xb, yb, w.f16s != 0)) {
+            // a batch: several tokens per item where the matrix takes them
+            b += gemv_item_tokens(g.it[g.n], nseq - b, xs, ys);
             g.n++;
-        else
+        } else {
             g.rc |= G(w, yb, xb, st);
+            b++;
+        }
     }
 }
 
@@ -354,7 +362,8 @@ static void hc_step(dsv4b_model *m, Pending &p, float *&hin, float *&hout, const
         a.hc_eps = c.hc_eps;
         a.rms_eps = c.rms_eps;
         a.s_ms = m->s_ms;
-        launch(k_hc_pre, dim3(n / 256, m->nseq), dim3(288), 0, st, a);
+        if (m->nseq > 1) launch(k_hc_pre_batch, dim3(n / 256, m->nseq), dim3(288), 0, st, a);
+        else launch(k_hc_pre, dim3(n / 256), dim3(288), 0, st, a);
         if (p.kind) std::swap(hin, hout);
         p.kind = 0;
         return;
@@ -504,7 +513,7 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
         pend = {1, nullptr};
         hc_step(m, pend, hin, hout, l.hcf_fn, l.hcf_base, l.hcf_scale, l.ffn_norm, false, m->x1, st);
         rc |= moe_forward(l.moe, m->ms, m->blk, m->x1, &m->st->token, st, !fused, m->world > 1 ? &ex : nullptr, B,
-                          m->s_ms, d, (int)(sizeof(StepState) / sizeof(int)));
+                          m->s_ms, d, (int)(sizeof(StepState) / sizeof(int)), m->moe_perm);
         pend = {fused ? 2 : 1, &l.moe};
     }
     // ---- head (src/cli/dsv4_run.c:467-474)

@@ -47,7 +47,9 @@ struct HcPreArgs {
     // and its MoE scratch (acc, wts, accs) s_ms floats apart
     long s_ms;
 };
+// k_hc_pre: one sequence; k_hc_pre_batch: sequence blockIdx.y of a batch
 __global__ void k_hc_pre(const __grid_constant__ HcPreArgs a);
+__global__ void k_hc_pre_batch(const __grid_constant__ HcPreArgs a);
 __global__ void k_hc_head_finish(float *y, const float *mixes, const float *x, const float *scale,
                                  const float *base, int hc, int hidden, float eps);
 __global__ void k_hc_post(float *y, const float *x, const float *res, const float *post, const float *comb,

@@ -228,12 +228,14 @@ __device__ __forceinline__ void sinkhorn_warp(float *comb, const float *mixes, f
 // at *count completes the grid; it resets *count, so the kernel is
 // replayable. post_in / comb_in may be the post / comb outputs: every block
 // has read them before it arrives at *count. hc * hc <= 32.
-__global__ void __launch_bounds__(288) k_hc_pre(const __grid_constant__ HcPreArgs a)
+template <bool BATCH>
+__device__ __forceinline__ void hc_pre_body(const HcPreArgs &a)
 {
     constexpr int MIXMAX = kHcPreMixMax, NV = MIXMAX + 1;
     // sequence blockIdx.y of a batch: its own rows of every activation
-    // (pointers computed here; the argument block itself is never modified)
-    const size_t sq_ = blockIdx.y, wide_ = (size_t)a.hc * a.hidden;
+    // (pointers computed here; the argument block itself is never modified;
+    // one sequence: every offset is the constant 0)
+    const size_t sq_ = BATCH ? blockIdx.y : 0, wide_ = (size_t)a.hc * a.hidden;
     float *const yq = a.y + sq_ * a.hidden;
     float *const postq = a.post ? a.post + sq_ * DSV4B_MAX_HC : nullptr;
     float *const combq = a.comb ? a.comb + sq_ * DSV4B_MAX_HC * DSV4B_MAX_HC : nullptr;
@@ -448,6 +450,9 @@ __global__ void __launch_bounds__(288) k_hc_pre(const __grid_constant__ HcPreArg
         }
     }
 }
+
+__global__ void __launch_bounds__(288) k_hc_pre(const __grid_constant__ HcPreArgs a) { hc_pre_body<false>(a); }
+__global__ void __launch_bounds__(288) k_hc_pre_batch(const __grid_constant__ HcPreArgs a) { hc_pre_body<true>(a); }
 
 // The head's reduction: a sigmoid gate per copy, one scalar scale, no
 // Sinkhorn (src/cli/dsv4_run.c:94-116). One block.

@@ -102,6 +102,31 @@ __global__ void k_route(const float *logits, const float *bias, const int *fixed
     }
 }
 
+// A batch's (token, slot) pairs in expert order: perm[r] = (t << 8) | k for
+// the pair of rank r under (expert, token, slot), so the grouped expert
+// launches that follow meet the tokens sharing an expert side by side and
+// read its weights from HBM once (the other tokens' blocks find them in L2).
+// One block; n = nseq topk <= 1024.
+__global__ void k_moe_sort(const int *sel, long s_ms, int nseq, int topk, int *perm)
+{
+    pdl_trigger();
+    pdl_wait();
+    __shared__ int es[1024];
+    const int n = nseq * topk;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int t = i / topk, k = i - t * topk;
+        es[i] = __ldcg(sel + (size_t)t * s_ms + k);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int e = es[i];
+        int r = 0;
+        for (int j = 0; j < n; j++) r += (es[j] < e) || (es[j] == e && j < i);
+        const int t = i / topk;
+        perm[r] = (t << 8) | (i - t * topk);
+    }
+}
+
 // out[i] = sum_k w[k] * acc[k][i] in k order, each product and sum rounded
 // separately (dsv4_layer.c:471-475), then + shared[i] (:479-483).
 __global__ void k_combine(float *out, const float *acc, const float *w, int topk, int hidden,
@@ -119,7 +144,7 @@ __global__ void k_combine(float *out, const float *acc, const float *w, int topk
 
 int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float *x,
                 const int *token, cudaStream_t st, bool combine, const Exch *ex, int nseq, long s_ms, long s_x,
-                int tok_stride)
+                int tok_stride, int *perm)
 {
     const int H = L.hidden, I = L.inter, K = L.topk;
     PdlChain chain;
@@ -136,6 +161,12 @@ int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float 
     launch(k_route, dim3(nseq), dim3(256), 0, st, S.logits, L.bias, L.fixed, L.tid2eid, token, L.n_experts, K,
            L.route_scale, L.score_func, S.sel, S.wts, s_ms, tok_stride);
     const int Is = L.has_shared ? L.inter_shared : 0;
+    // a batch on the tensor-core path: the routed items in expert order (the
+    // order is picked on the device; every item's arithmetic is unchanged)
+    const bool sorted = nseq > 1 && perm && nseq * K <= 1024 &&
+                        gemv_mma_shape(L.efmt, H, L.eblk_r, L.eblk_c, L.ef16s != 0) &&
+                        gemv_mma_shape(L.efmt, I, L.eblk_r, L.eblk_c, L.ef16s != 0);
+    if (sorted) launch(k_moe_sort, dim3(1), dim3(256), 0, st, S.sel, s_ms, nseq, K, perm);
     // the items of one stage (every token's selected experts, then its shared
     // expert), launched kGemvMaxItems at a time: a launch's grouping never
     // changes an item's arithmetic
@@ -150,11 +181,24 @@ int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float 
     };
     // gate / up of every selected expert and the shared one, SwiGLU in the
     // epilogue: h[k] = swiglu(w1 x, w3 x) (dsv4_layer.c:199-206)
+    if (sorted) {
+        for (int j = 0; j < nseq * K; j++) {
+            GemvItem it;
+            if (!gemv_item(it, L.efmt, nullptr, nullptr, I, H, L.eblk_r, L.eblk_c, x, S.h, L.ef16s != 0) || !it.mma)
+                return -1;
+            it.wtab = L.w1tab; it.stab = L.s1tab;
+            it.w2tab = L.w3tab; it.s2tab = L.s3tab;
+            it.sel = S.sel; it.slot = j;
+            it.perm = perm; it.xs = (int)s_x; it.xk = 0; it.ys = (int)s_ms; it.yk = I; it.ss = (int)s_ms;
+            it.pair = 1; it.limit = L.swiglu_limit;
+            items.push_back(it);
+        }
+    }
     for (int b = 0; b < nseq; b++) {
         const float *xb = x + (size_t)b * s_x;
         float *hb = S.h + (size_t)b * s_ms;
         const int *selb = S.sel + (size_t)b * s_ms;
-        for (int k = 0; k < K; k++) {
+        for (int k = 0; k < K && !sorted; k++) {
             GemvItem it;
             if (!gemv_item(it, L.efmt, nullptr, nullptr, I, H, L.eblk_r, L.eblk_c, xb, hb + (size_t)k * I,
                            L.ef16s != 0))
@@ -165,24 +209,38 @@ int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float 
             it.pair = 1; it.limit = L.swiglu_limit;
             items.push_back(it);
         }
-        if (Is) {
-            GemvItem it;
-            if (!gemv_item(it, L.sh[0].wdt, L.sh[0].w, L.sh[0].s, Is, H, L.sh[0].blk_r, L.sh[0].blk_c, xb,
-                           hb + (size_t)K * I, L.sh[0].f16s && L.sh[1].f16s) ||
-                L.sh[1].wdt != L.sh[0].wdt)
-                return -1;
-            it.W2 = L.sh[1].w; it.S2 = L.sh[1].s;
-            it.pair = 1; it.limit = L.swiglu_limit;
-            items.push_back(it);
-        }
+    }
+    // the shared expert: a batch's tokens several to an item
+    for (int b = 0; Is && b < nseq;) {
+        GemvItem it;
+        if (!gemv_item(it, L.sh[0].wdt, L.sh[0].w, L.sh[0].s, Is, H, L.sh[0].blk_r, L.sh[0].blk_c,
+                       x + (size_t)b * s_x, S.h + (size_t)b * s_ms + (size_t)K * I, L.sh[0].f16s && L.sh[1].f16s) ||
+            L.sh[1].wdt != L.sh[0].wdt)
+            return -1;
+        it.W2 = L.sh[1].w; it.S2 = L.sh[1].s;
+        it.pair = 1; it.limit = L.swiglu_limit;
+        b += gemv_item_tokens(it, nseq - b, s_x, s_ms);
+        items.push_back(it);
     }
     if (flush()) return -1;
     // down projections into the per-k accumulators
+    if (sorted) {
+        for (int j = 0; j < nseq * K; j++) {
+            GemvItem it;
+            if (!gemv_item(it, L.efmt, nullptr, nullptr, H, I, L.eblk_r, L.eblk_c, S.h, S.acc, L.ef16s != 0) ||
+                !it.mma)
+                return -1;
+            it.wtab = L.w2tab; it.stab = L.s2tab;
+            it.sel = S.sel; it.slot = j;
+            it.perm = perm; it.xs = (int)s_ms; it.xk = I; it.ys = (int)s_ms; it.yk = H; it.ss = (int)s_ms;
+            items.push_back(it);
+        }
+    }
     for (int b = 0; b < nseq; b++) {
         const float *hb = S.h + (size_t)b * s_ms;
         float *accb = S.acc + (size_t)b * s_ms;
         const int *selb = S.sel + (size_t)b * s_ms;
-        for (int k = 0; k < K; k++) {
+        for (int k = 0; k < K && !sorted; k++) {
             GemvItem it;
             if (!gemv_item(it, L.efmt, nullptr, nullptr, H, I, L.eblk_r, L.eblk_c, hb + (size_t)k * I,
                            accb + (size_t)k * H, L.ef16s != 0))
@@ -191,13 +249,15 @@ int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float 
             it.sel = selb; it.slot = k;
             items.push_back(it);
         }
-        if (Is) {
-            GemvItem it;
-            if (!gemv_item(it, L.sh[2].wdt, L.sh[2].w, L.sh[2].s, H, Is, L.sh[2].blk_r, L.sh[2].blk_c,
-                           hb + (size_t)K * I, accb + (size_t)K * H, L.sh[2].f16s != 0))
-                return -1;
-            items.push_back(it);
-        }
+    }
+    for (int b = 0; Is && b < nseq;) {
+        GemvItem it;
+        if (!gemv_item(it, L.sh[2].wdt, L.sh[2].w, L.sh[2].s, H, Is, L.sh[2].blk_r, L.sh[2].blk_c,
+                       S.h + (size_t)b * s_ms + (size_t)K * I, S.acc + (size_t)b * s_ms + (size_t)K * H,
+                       L.sh[2].f16s != 0))
+            return -1;
+        b += gemv_item_tokens(it, nseq - b, s_ms, s_ms);
+        items.push_back(it);
     }
     if (flush()) return -1;
     float *accs = S.acc + (size_t)K * H;

@@ -36,6 +36,7 @@ namespace dsv4b {
 constexpr int kGemvThreads = 256;           // 16 half-warps per block
 constexpr int kGemvSmem = 32 * 1024;        // a block's segment sums
 constexpr int kMmaTileSmem = 112 * 1024;    // a tensor-core tile's whole shared memory (two blocks per SM)
+constexpr int kMmaTileSmemMT = 220 * 1024;  // a multi-token tile's (one block per SM: fewer passes over the weights)
 constexpr int kGemvMaxTr = 512;
 
 // SwiGLU with the reference's asymmetric clamp (src/core/dsv4_ops.c:60-78):
@@ -458,7 +459,7 @@ int gemv_item_tokens(GemvItem &it, int want, long xts, long yts)
     if (!it.mma || want <= 1) return 1;
     const int nb = it.cols / mma_unit_cols(it.fmt), minrows = it.pair ? 32 : 16;
     int k = want < 4 ? want : 4;
-    while (k > 1 && mma_smem(it.fmt, nb, minrows, k) > (size_t)kMmaTileSmem) k--;
+    while (k > 1 && mma_smem(it.fmt, nb, minrows, k) > (size_t)kMmaTileSmemMT) k--;
     if (k > 1) {
         it.nt = k;
         it.xts = (int)xts;
@@ -506,8 +507,9 @@ int gemv_group(GemvItem *items, int n, cudaStream_t st)
         }
         if (it.mma) {
             const int nb = it.cols / mma_unit_cols(it.fmt), ntk = it.nt > 1 ? it.nt : 1;
+            const int budget = ntk > 1 ? kMmaTileSmemMT : kMmaTileSmem;
             // a multiple of 16 virtual rows, within the shared memory budget
-            int cap = (int)((kMmaTileSmem - mma_smem(it.fmt, nb, 0, ntk)) / (64 * ntk)) & ~15;
+            int cap = (int)((budget - mma_smem(it.fmt, nb, 0, ntk)) / (64 * ntk)) & ~15;
             cap = cap < 512 ? cap : 512;
             if (cap < 16) return -1;
             int tr = ((int)(target / it.rowbytes) + 15) & ~15;
@@ -557,7 +559,7 @@ int gemv_group(GemvItem *items, int n, cudaStream_t st)
     int maxnt = 1;
     for (int i = 0; i < n; i++) maxnt = items[i].nt > maxnt ? items[i].nt : maxnt;
     auto kern = maxnt > 2 ? k_gemv_group<2> : maxnt > 1 ? k_gemv_group<1> : k_gemv_group<0>;
-    if (smem_optin(kern, kMmaTileSmem)) return -1;
+    if (smem_optin(kern, maxnt > 1 ? kMmaTileSmemMT : kMmaTileSmem)) return -1;
     return launch(kern, dim3(blocks), dim3(kGemvThreads), smem, st, b) ==
                    cudaSuccess
                ? 0

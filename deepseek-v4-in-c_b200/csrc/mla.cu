@@ -60,101 +60,150 @@ __device__ __forceinline__ float4 load4_t(const void *base, size_t e)
 
 
 // ---------------------------------------------------------------- indexer
-// grid (ceil(n_pos / 32), batch), 256 threads. Thread t: position t & 31 of
-// the tile, heads (t >> 5) * 8 .. +8. q and the key tile live in shared
-// memory as double (keys transposed so a warp reads 32 consecutive doubles).
-constexpr int IX_TP = 32;
+constexpr int IX_TP = 32;        // positions per tile of the head-split form
 
-template <int KDT>
+// Persistent blocks (256 threads) over the batch's tiles of 32 PPL
+// positions, every head; tile t of the grid-stride walk is sequence
+// t / tiles, positions (t % tiles) 32 PPL .. Lane l holds positions PPL l ..
+// PPL l + PPL - 1 of a tile, warp w heads 8 w .. 8 w + 7 of each group of
+// 64: a register tile of PPL x 8 dots, each the sequential double FMA chain
+// of the reference (src/core/dsv4_indexer.c:64-85). q sits transposed in
+// shared memory ([head_dim][n_heads], loaded once per sequence; a warp reads
+// its 8 heads as four 16-byte broadcasts) and the key tile as
+// [head_dim][32 PPL + 2] doubles (a lane reads its PPL positions in one
+// load); the next tile's keys are loaded into registers while the current
+// one is computed. The per-position sum over heads in head order follows.
+template <int KDT, int PPL>
 __global__ void __launch_bounds__(256)
 k_indexer_score(float *out, const float *q, const void *keys, long key_stride,
                 long seq_key_stride, const float *w, int n_heads, int head_dim, int n_pos,
-                float scale, long seq_q_stride, long seq_out_stride, const int *dyn_n)
+                float scale, long seq_q_stride, long seq_out_stride, const int *dyn_n, int batch)
 {
+    constexpr int TP = 32 * PPL, KS = TP + 2;       // tile positions, key-row stride (doubles)
+    constexpr int KR = 4 * PPL;                     // key float4 groups per thread per tile (head_dim <= 128)
     pdl_trigger();
     pdl_wait();
     if (dyn_n) n_pos = min(n_pos, *dyn_n);       // rows that exist this step
-    if ((int)blockIdx.x * IX_TP >= n_pos) return;
     extern __shared__ double ixs[];
-    double *qs = ixs;                               // [n_heads][head_dim]
-    double *kt = qs + n_heads * head_dim;           // [head_dim][IX_TP]
-    double *dots = kt + head_dim * IX_TP;           // [IX_TP][n_heads + 1]
-    double *ws = dots + IX_TP * (n_heads + 1);      // [n_heads]
-    const int b = blockIdx.y, t0 = blockIdx.x * IX_TP;
-    q += (size_t)b * seq_q_stride;
-    w += (size_t)b * n_heads;
-    const char *kb = reinterpret_cast<const char *>(keys);
-    kb += (size_t)b * seq_key_stride * dt_bytes<KDT>;
-    for (int h = threadIdx.x; h < n_heads; h += blockDim.x) ws[h] = (double)ld_act(w + h);
-    // q as float4 groups, 8 loads in flight per thread
-    const int nq4 = (n_heads * head_dim) >> 2;
-    for (int i0 = threadIdx.x; i0 < nq4; i0 += 8 * (int)blockDim.x) {
-        float4 v[8];
+    double *qt = ixs;                               // [head_dim][n_heads]
+    double *kt = qt + (size_t)head_dim * n_heads;   // [head_dim][KS]
+    double *dots = kt + (size_t)head_dim * KS;      // [TP][n_heads + 1]
+    double *ws = dots + TP * (n_heads + 1);         // [n_heads]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nd4 = head_dim >> 2;
+    const int tiles = (n_pos + TP - 1) / TP, total = tiles * batch;
+    // this thread's key groups of a tile: position p = (tid >> 3) + 32 r,
+    // group g = (tid & 7) + 8 u (r < PPL, u < 4)
+    auto load_keys = [&](int t, float4 (&v)[KR]) {
+        const int b = t / tiles, t0 = (t - b * tiles) * TP;
+        const char *kb = reinterpret_cast<const char *>(keys) + (size_t)b * seq_key_stride * dt_bytes<KDT>;
 #pragma unroll
-        for (int u = 0; u < 8; u++) {
-            const int i = i0 + u * (int)blockDim.x;
-            v[u] = i < nq4 ? __ldcg(reinterpret_cast<const float4 *>(q) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-            const int i = i0 + u * (int)blockDim.x;
-            if (i < nq4) {
-                qs[4 * i] = (double)v[u].x;
-                qs[4 * i + 1] = (double)v[u].y;
-                qs[4 * i + 2] = (double)v[u].z;
-                qs[4 * i + 3] = (double)v[u].w;
-            }
-        }
-    }
-    // the key tile: thread (position tid/8, lane group tid%8) moves float4
-    // groups g = tid%8 + 8k of its row into kt[c][p]
-    {
-        const int p = threadIdx.x >> 3, part8 = threadIdx.x & 7, nd4 = head_dim >> 2;
-        const bool live = p < IX_TP && t0 + p < n_pos;
-        for (int g0 = part8; g0 < nd4; g0 += 32) {
-            float4 v[4];
+        for (int r = 0; r < PPL; r++)
 #pragma unroll
             for (int u = 0; u < 4; u++) {
-                const int g = g0 + 8 * u;
-                v[u] = (live && g < nd4) ? load4_t<KDT>(kb, (size_t)(t0 + p) * key_stride + 4 * g)
-                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+                const int p = (tid >> 3) + 32 * r, g = (tid & 7) + 8 * u;
+                v[r * 4 + u] = (t0 + p < n_pos && g < nd4) ? load4_t<KDT>(kb, (size_t)(t0 + p) * key_stride + 4 * g)
+                                                            : make_float4(0.f, 0.f, 0.f, 0.f);
             }
+    };
+    float4 kv4[KR];
+    int t = blockIdx.x, qb = -1;
+    if (t < total) load_keys(t, kv4);
+    for (; t < total; t += gridDim.x) {
+        const int b = t / tiles, t0 = (t - b * tiles) * TP;
+        if (b != qb) {                              // q and w of this sequence
+            qb = b;
+            const float *qs = q + (size_t)b * seq_q_stride;
+            for (int h = tid; h < n_heads; h += blockDim.x) ws[h] = (double)ld_act(w + (size_t)b * n_heads + h);
+            const int nq4 = n_heads * nd4;
+            for (int i0 = tid; i0 < nq4; i0 += 4 * (int)blockDim.x) {
+                float4 v[4];
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int g = g0 + 8 * u;
-                if (p < IX_TP && g < nd4) {
-                    kt[(4 * g) * IX_TP + p] = (double)v[u].x;
-                    kt[(4 * g + 1) * IX_TP + p] = (double)v[u].y;
-                    kt[(4 * g + 2) * IX_TP + p] = (double)v[u].z;
-                    kt[(4 * g + 3) * IX_TP + p] = (double)v[u].w;
+                for (int u = 0; u < 4; u++) {
+                    const int i = i0 + u * (int)blockDim.x, h = i % n_heads, g = i / n_heads;
+                    v[u] = i < nq4 ? __ldcg(reinterpret_cast<const float4 *>(qs + (size_t)h * head_dim) + g)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int i = i0 + u * (int)blockDim.x, h = i % n_heads, g = i / n_heads;
+                    if (i < nq4) {
+                        qt[(size_t)(4 * g) * n_heads + h] = (double)v[u].x;
+                        qt[(size_t)(4 * g + 1) * n_heads + h] = (double)v[u].y;
+                        qt[(size_t)(4 * g + 2) * n_heads + h] = (double)v[u].z;
+                        qt[(size_t)(4 * g + 3) * n_heads + h] = (double)v[u].w;
+                    }
                 }
             }
         }
-    }
-    __syncthreads();
-    const int p = threadIdx.x & 31, hg = threadIdx.x >> 5;
-    for (int h0 = hg * 8; h0 < n_heads; h0 += 64) {
-        double acc[8];
+        // this tile's keys (loaded during the previous tile) into shared memory
 #pragma unroll
-        for (int j = 0; j < 8; j++) acc[j] = 0.0;
-        for (int c = 0; c < head_dim; c++) {
-            const double kv = kt[c * IX_TP + p];
+        for (int r = 0; r < PPL; r++)
 #pragma unroll
-            for (int j = 0; j < 8; j++)
-                if (h0 + j < n_heads) acc[j] = __fma_rn(qs[(h0 + j) * head_dim + c], kv, acc[j]);
+            for (int u = 0; u < 4; u++) {
+                const int p = (tid >> 3) + 32 * r, g = (tid & 7) + 8 * u;
+                if (g < nd4) {
+                    const float4 v = kv4[r * 4 + u];
+                    kt[(4 * g) * KS + p] = (double)v.x;
+                    kt[(4 * g + 1) * KS + p] = (double)v.y;
+                    kt[(4 * g + 2) * KS + p] = (double)v.z;
+                    kt[(4 * g + 3) * KS + p] = (double)v.w;
+                }
+            }
+        __syncthreads();
+        if (t + (int)gridDim.x < total) load_keys(t + gridDim.x, kv4);   // in flight during the dots
+        const bool vec = (n_heads & 7) == 0;        // 8 heads per warp as aligned pairs
+        for (int hb = 0; hb < n_heads; hb += 64) {
+            const int h0 = hb + 8 * warp;
+            if (h0 >= n_heads) continue;            // warp-uniform
+            double acc[PPL][8];
+#pragma unroll
+            for (int r = 0; r < PPL; r++)
+#pragma unroll
+                for (int j = 0; j < 8; j++) acc[r][j] = 0.0;
+            for (int c = 0; c < head_dim; c++) {
+                double kv[PPL];
+                if constexpr (PPL == 2) {
+                    const double2 k2 = *reinterpret_cast<const double2 *>(kt + c * KS + 2 * lane);
+                    kv[0] = k2.x;
+                    kv[1] = k2.y;
+                } else {
+                    kv[0] = kt[c * KS + lane];
+                }
+                const double *qr = qt + (size_t)c * n_heads + h0;
+                double qv[8];
+                if (vec) {
+#pragma unroll
+                    for (int j = 0; j < 8; j += 2) {
+                        const double2 q2 = *reinterpret_cast<const double2 *>(qr + j);
+                        qv[j] = q2.x;
+                        qv[j + 1] = q2.y;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; j++) qv[j] = h0 + j < n_heads ? qr[j] : 0.0;
+                }
+#pragma unroll
+                for (int r = 0; r < PPL; r++)
+#pragma unroll
+                    for (int j = 0; j < 8; j++) acc[r][j] = __fma_rn(qv[j], kv[r], acc[r][j]);
+            }
+#pragma unroll
+            for (int r = 0; r < PPL; r++)
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    if (h0 + j < n_heads) dots[(PPL * lane + r) * (n_heads + 1) + h0 + j] = acc[r][j];
         }
-#pragma unroll
-        for (int j = 0; j < 8; j++)
-            if (h0 + j < n_heads) dots[p * (n_heads + 1) + h0 + j] = acc[j];
-    }
-    __syncthreads();
-    if (threadIdx.x < IX_TP && t0 + threadIdx.x < n_pos) {
-        double total = 0.0;
-        for (int h = 0; h < n_heads; h++) {
-            const double d = dots[threadIdx.x * (n_heads + 1) + h];
-            if (d > 0.0) total = __dadd_rn(total, __dmul_rn(d, ws[h]));
+        __syncthreads();
+        for (int p = tid; p < TP; p += blockDim.x) {
+            if (t0 + p >= n_pos) break;
+            double total_s = 0.0;
+            for (int h = 0; h < n_heads; h++) {
+                const double d = dots[p * (n_heads + 1) + h];
+                if (d > 0.0) total_s = __dadd_rn(total_s, __dmul_rn(d, ws[h]));
+            }
+            out[(size_t)b * seq_out_stride + t0 + p] = __fmul_rn((float)total_s, scale);
         }
-        out[(size_t)b * seq_out_stride + t0 + threadIdx.x] = __fmul_rn((float)total, scale);
+        __syncthreads();                            // dots, kt and (for a new sequence) qt are reused
     }
 }
 
@@ -270,7 +319,8 @@ k_topk(int *idx_out, const float *scores, int n, int k, long seq_in_stride, long
     if (dyn_nk) { n = min(n, dyn_nk[0]); k = dyn_nk[1]; }
     extern __shared__ uint32_t tks[];
     uint32_t *key = tks;                                   // [n]
-    unsigned long long *sel = reinterpret_cast<unsigned long long *>(key + ((n + 1) & ~1)); // [kpow2]
+    int *eqi = reinterpret_cast<int *>(key + ((n + 1) & ~1));   // [kTopkEqCap] indices == the k-th key
+    unsigned long long *sel = reinterpret_cast<unsigned long long *>(eqi + kTopkEqCap);   // [kpow2]
     __shared__ uint32_t hist[256];
     __shared__ uint32_t s_prefix, s_want, s_gt, s_eqtaken;
     const int b = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
@@ -288,8 +338,14 @@ k_topk(int *idx_out, const float *scores, int n, int k, long seq_in_stride, long
         for (int i = tid; i < 256; i += nt) hist[i] = 0;
         __syncthreads();
         const uint32_t pre = s_prefix;
+        // lanes with the same bin add once (float exponents cluster, and
+        // unaggregated atomics on a few bins serialise)
         for (int i = tid; i < n; i += nt)
-            if ((key[i] & mask) == pre) atomicAdd(&hist[(key[i] >> shift) & 255u], 1u);
+            if ((key[i] & mask) == pre) {
+                const uint32_t bin = (key[i] >> shift) & 255u;
+                const unsigned same = __match_any_sync(__activemask(), bin);
+                if ((tid & 31) == __ffs(same) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(same));
+            }
         __syncthreads();
         // the bin holding the want-th largest: lane l owns bins 255-8l .. 248-8l,
         // an exclusive scan over lanes finds the lane, the lane walks its bins
@@ -331,14 +387,35 @@ k_topk(int *idx_out, const float *scores, int n, int k, long seq_in_stride, long
     while (kp < k) kp <<= 1;
     for (int i = tid; i < kp; i += nt) sel[i] = 0ull;   // padding sorts last
     __syncthreads();
-    for (int i = tid; i < n; i += nt)
+    __shared__ uint32_t s_eq;
+    if (tid == 0) s_eq = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += nt) {
         if (key[i] > kth) {
             const uint32_t slot = atomicAdd(&s_gt, 1u);
             sel[slot] = ((unsigned long long)key[i] << 32) | (uint32_t)(~(uint32_t)i);
+        } else if (key[i] == kth) {                   // ties at the threshold, in any order
+            const uint32_t slot = atomicAdd(&s_eq, 1u);
+            if (slot < (uint32_t)kTopkEqCap) eqi[slot] = i;
         }
+    }
     __syncthreads();
-    // ties at the threshold: lowest indices first -- a block-wide ordered scan
-    const uint32_t base = s_gt;
+    const uint32_t base = s_gt, neq = s_eq;
+    if (neq <= (uint32_t)kTopkEqCap) {
+        // the lowest need_eq indices of the ties: all of them when every tie
+        // is taken (the final sort orders them), else those of rank < need_eq
+        // (rank = how many ties have a lower index)
+        for (uint32_t e = tid; e < neq; e += nt) {
+            const int i = eqi[e];
+            uint32_t rank = 0;
+            if (neq > need_eq)
+                for (uint32_t f = 0; f < neq; f++) rank += eqi[f] < i;
+            if (rank < need_eq) sel[base + rank] = ((unsigned long long)kth << 32) | (uint32_t)(~(uint32_t)i);
+        }
+        if (tid == 0) s_eqtaken = need_eq;
+        __syncthreads();
+    }
+    // many ties: lowest indices first -- a block-wide ordered scan
     for (int c0 = 0; c0 < n && s_eqtaken < need_eq; c0 += nt) {
         const int i = c0 + tid;
         const int is_eq = (i < n && key[i] == kth) ? 1 : 0;
@@ -369,9 +446,42 @@ k_topk(int *idx_out, const float *scores, int n, int k, long seq_in_stride, long
         __syncthreads();
     }
     // bitonic sort, descending by (key, ~index): larger value first, and for
-    // equal values the larger ~index, i.e. the lower index, first
-    for (int size = 2; size <= kp; size <<= 1)
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+    // equal values the larger ~index, i.e. the lower index, first. Thread
+    // pair q holds elements 2q, 2q + 1 in registers for every stage of
+    // stride <= 32 (partners within the thread or the warp: shuffles); the
+    // wider strides go through shared memory.
+    const int npair = kp < 64 ? 32 : kp >> 1;           // warp-aligned element pairs
+    auto reg_stages = [&](unsigned long long &v0, unsigned long long &v1, int q, int size, int smax) {
+        for (int stride = smax; stride >= 1; stride >>= 1) {
+            const bool desc = ((2 * q) & size) == 0;
+            if (stride == 1) {
+                const unsigned long long hi = v0 > v1 ? v0 : v1, lo = v0 > v1 ? v1 : v0;
+                v0 = desc ? hi : lo;
+                v1 = desc ? lo : hi;
+            } else {
+                const unsigned long long p0 = __shfl_xor_sync(0xffffffffu, v0, stride >> 1);
+                const unsigned long long p1 = __shfl_xor_sync(0xffffffffu, v1, stride >> 1);
+                const bool keep_hi = ((2 * q) < ((2 * q) ^ stride)) == desc;
+                v0 = keep_hi ? (v0 > p0 ? v0 : p0) : (v0 < p0 ? v0 : p0);
+                v1 = keep_hi ? (v1 > p1 ? v1 : p1) : (v1 < p1 ? v1 : p1);
+            }
+        }
+    };
+    auto reg_phase = [&](int size_lo, int size_hi, int smax) {
+        for (int q0 = 0; q0 < npair; q0 += nt) {
+            const int q = q0 + tid;
+            if (q0 + (tid & ~31) >= npair) continue;    // whole warps only
+            unsigned long long v0 = 2 * q < kp ? sel[2 * q] : 0ull, v1 = 2 * q + 1 < kp ? sel[2 * q + 1] : 0ull;
+            for (int size = size_lo; size <= size_hi; size <<= 1)
+                reg_stages(v0, v1, q, size, smax < (size >> 1) ? smax : (size >> 1));
+            if (2 * q < kp) sel[2 * q] = v0;
+            if (2 * q + 1 < kp) sel[2 * q + 1] = v1;
+        }
+        __syncthreads();
+    };
+    reg_phase(2, 64, 32);                               // every size up to 64
+    for (int size = 128; size <= kp; size <<= 1) {
+        for (int stride = size >> 1; stride >= 64; stride >>= 1) {
             for (int i = tid; i < kp; i += nt) {
                 const int j = i ^ stride;
                 if (j > i) {
@@ -382,6 +492,8 @@ k_topk(int *idx_out, const float *scores, int n, int k, long seq_in_stride, long
             }
             __syncthreads();
         }
+        reg_phase(size, size, 32);                      // strides 32 .. 1 of this size
+    }
     for (int i = tid; i < k; i += nt) idx_out[i] = (int)(~(uint32_t)(sel[i] & 0xffffffffull));
 }
 
@@ -700,23 +812,36 @@ int indexer_score(float *out, const float *q, const void *keys, int key_dt, long
     if ((head_dim & 3) || (key_stride & 3) || (seq_key_stride & 3) || ((uintptr_t)keys % kal) ||
         ((uintptr_t)q & 15))
         return -1;
-    const size_t smem = ((size_t)n_heads * head_dim + (size_t)head_dim * IX_TP + (size_t)IX_TP * (n_heads + 1) +
-                         (size_t)n_heads) * 8;
+    // 64 positions per tile where q, the key tile and the dots fit, else 32;
+    // one persistent block per SM (two where they fit) over every tile
+    if (head_dim > 128) return -1;
+    auto smem_of = [&](int ppl) {
+        const size_t tp = 32 * (size_t)ppl;
+        return ((size_t)n_heads * head_dim + (size_t)head_dim * (tp + 2) + tp * (n_heads + 1) + (size_t)n_heads) * 8;
+    };
+    const int ppl = smem_of(2) <= 200 * 1024 ? 2 : 1;
+    const size_t smem = smem_of(ppl);
     if (smem > 200 * 1024) return -1;
-    if (smem_optin(k_indexer_score<DSV4B_DT_F32>, 200 * 1024) || smem_optin(k_indexer_score<DSV4B_DT_BF16>, 200 * 1024) ||
-        smem_optin(k_indexer_score<DSV4B_DT_E4M3>, 200 * 1024))
-        return -1;
-    dim3 grid((n_pos + IX_TP - 1) / IX_TP, batch);
     const long sq = (long)n_heads * head_dim;
-    if (key_dt == DSV4B_DT_F32)
-        launch(k_indexer_score<DSV4B_DT_F32>, grid, dim3(256), smem, st, out, q, keys, key_stride, seq_key_stride, w,
-               n_heads, head_dim, n_pos, scale, sq, n_pos, dyn_n);
-    else if (key_dt == DSV4B_DT_BF16)
-        launch(k_indexer_score<DSV4B_DT_BF16>, grid, dim3(256), smem, st, out, q, keys, key_stride, seq_key_stride, w,
-               n_heads, head_dim, n_pos, scale, sq, n_pos, dyn_n);
-    else
-        launch(k_indexer_score<DSV4B_DT_E4M3>, grid, dim3(256), smem, st, out, q, keys, key_stride, seq_key_stride, w,
-               n_heads, head_dim, n_pos, scale, sq, n_pos, dyn_n);
+    int dev = 0, nsm = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const long tiles = ((long)n_pos + 32 * ppl - 1) / (32 * ppl) * batch;
+    const long cap = (long)nsm * (smem <= 110 * 1024 ? 2 : 1);
+    const dim3 grid((unsigned)(tiles < cap ? tiles : cap));
+#define DSV4B_IX_LAUNCH(KDT, PPL)                                                                                 \
+    do {                                                                                                         \
+        if (smem_optin(k_indexer_score<KDT, PPL>, 200 * 1024)) return -1;                                        \
+        launch(k_indexer_score<KDT, PPL>, grid, dim3(256), smem, st, out, q, keys, key_stride, seq_key_stride, w, \
+               n_heads, head_dim, n_pos, scale, sq, n_pos, dyn_n, batch);                                        \
+    } while (0)
+    if (key_dt == DSV4B_DT_F32) {
+        if (ppl == 2) DSV4B_IX_LAUNCH(DSV4B_DT_F32, 2); else DSV4B_IX_LAUNCH(DSV4B_DT_F32, 1);
+    } else if (key_dt == DSV4B_DT_BF16) {
+        if (ppl == 2) DSV4B_IX_LAUNCH(DSV4B_DT_BF16, 2); else DSV4B_IX_LAUNCH(DSV4B_DT_BF16, 1);
+    } else {
+        if (ppl == 2) DSV4B_IX_LAUNCH(DSV4B_DT_E4M3, 2); else DSV4B_IX_LAUNCH(DSV4B_DT_E4M3, 1);
+    }
+#undef DSV4B_IX_LAUNCH
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -727,7 +852,7 @@ int topk(int *idx, const float *scores, int n, int k, int batch, long seq_in_str
     if (n > kTopkMaxN || k > kTopkMaxK) return -1;
     int kp = 1;
     while (kp < (k < n ? k : n)) kp <<= 1;
-    const size_t smem = (size_t)((n + 1) & ~1) * 4 + (size_t)kp * 8;
+    const size_t smem = (size_t)((n + 1) & ~1) * 4 + (size_t)kTopkEqCap * 4 + (size_t)kp * 8;
     if (smem > 220 * 1024) return -1;
     if (smem_optin(k_topk, 220 * 1024)) return -1;
     launch(k_topk, dim3(dim3(1, batch)), dim3(1024), smem, st, idx, scores, n, k, seq_in_stride, seq_out_stride, dyn_nk);

@@ -12,6 +12,7 @@ namespace dsv4b {
 
 constexpr int kTopkMaxN = 49152;    // scores held in shared memory
 constexpr int kTopkMaxK = 4096;
+constexpr int kTopkEqCap = 1024;    // ties at the k-th score ranked directly (more: an ordered scan)
 
 // out[b][t] for t < n_pos: the reference's indexer score of key row t.
 // keys of sequence b start at keys + b*seq_key_stride elements; row t at

@@ -362,8 +362,12 @@ static void hc_step(dsv4b_model *m, Pending &p, float *&hin, float *&hout, const
         a.hc_eps = c.hc_eps;
         a.rms_eps = c.rms_eps;
         a.s_ms = m->s_ms;
-        if (m->nseq > 1) launch(k_hc_pre_batch, dim3(n / 256, m->nseq), dim3(288), 0, st, a);
-        else launch(k_hc_pre, dim3(n / 256), dim3(288), 0, st, a);
+        if (m->nseq > 1) {
+            launch(k_hc_part_batch, dim3(n / 256, m->nseq), dim3(288), 0, st, a);
+            launch(k_hc_tail_batch, dim3(m->nseq), dim3(288), 0, st, a);
+        } else {
+            launch(k_hc_pre, dim3(n / 256), dim3(288), 0, st, a);
+        }
         if (p.kind) std::swap(hin, hout);
         p.kind = 0;
         return;

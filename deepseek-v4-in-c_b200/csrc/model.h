@@ -50,6 +50,10 @@ struct HcPreArgs {
 // k_hc_pre: one sequence; k_hc_pre_batch: sequence blockIdx.y of a batch
 __global__ void k_hc_pre(const __grid_constant__ HcPreArgs a);
 __global__ void k_hc_pre_batch(const __grid_constant__ HcPreArgs a);
+// a batch in two launches: the partials of every (256 columns, sequence), then
+// one block per sequence for the rest (same arithmetic)
+__global__ void k_hc_part_batch(const __grid_constant__ HcPreArgs a);
+__global__ void k_hc_tail_batch(const __grid_constant__ HcPreArgs a);
 __global__ void k_hc_head_finish(float *y, const float *mixes, const float *x, const float *scale,
                                  const float *base, int hc, int hidden, float eps);
 __global__ void k_hc_post(float *y, const float *x, const float *res, const float *post, const float *comb,

@@ -228,14 +228,19 @@ __device__ __forceinline__ void sinkhorn_warp(float *comb, const float *mixes, f
 // at *count completes the grid; it resets *count, so the kernel is
 // replayable. post_in / comb_in may be the post / comb outputs: every block
 // has read them before it arrives at *count. hc * hc <= 32.
-template <bool BATCH>
+// MODE 0: the whole step in one launch (the last block to finish its
+// partials runs the tail); MODE 1: the partials only (a batch's first
+// launch, no counter, blocks exit); MODE 2: the tail only, block = sequence
+// (a batch's second launch). The arithmetic is the same in every mode.
+template <bool BATCH, int MODE>
 __device__ __forceinline__ void hc_pre_body(const HcPreArgs &a)
 {
     constexpr int MIXMAX = kHcPreMixMax, NV = MIXMAX + 1;
-    // sequence blockIdx.y of a batch: its own rows of every activation
-    // (pointers computed here; the argument block itself is never modified;
-    // one sequence: every offset is the constant 0)
-    const size_t sq_ = BATCH ? blockIdx.y : 0, wide_ = (size_t)a.hc * a.hidden;
+    // sequence blockIdx.y (tail: blockIdx.x) of a batch: its own rows of
+    // every activation (pointers computed here; the argument block itself is
+    // never modified; one sequence: every offset is the constant 0)
+    const size_t sq_ = MODE == 2 ? blockIdx.x : (BATCH ? blockIdx.y : 0), wide_ = (size_t)a.hc * a.hidden;
+    const int nparts = (int)(wide_ >> 8);           // blocks of the partials (256 columns each)
     float *const yq = a.y + sq_ * a.hidden;
     float *const postq = a.post ? a.post + sq_ * DSV4B_MAX_HC : nullptr;
     float *const combq = a.comb ? a.comb + sq_ * DSV4B_MAX_HC * DSV4B_MAX_HC : nullptr;
@@ -247,7 +252,7 @@ __device__ __forceinline__ void hc_pre_body(const HcPreArgs &a)
     const float *const accsq = a.accs ? a.accs + sq_ * a.s_ms : nullptr;
     const float *const pinq = a.post_in ? a.post_in + sq_ * DSV4B_MAX_HC : nullptr;
     const float *const cinq = a.comb_in ? a.comb_in + sq_ * DSV4B_MAX_HC * DSV4B_MAX_HC : nullptr;
-    double *const partq = a.part + sq_ * gridDim.x * NV;
+    double *const partq = a.part + sq_ * nparts * NV;
     unsigned *const cntq = a.count + sq_;
     __shared__ float prod[NV][256];
     __shared__ double red8[NV][8];
@@ -272,6 +277,7 @@ __device__ __forceinline__ void hc_pre_body(const HcPreArgs &a)
         wn[u] = (a.norm_w && col && d4 < h4) ? __ldg(reinterpret_cast<const float4 *>(a.norm_w) + d4)
                                       : make_float4(1.f, 1.f, 1.f, 1.f);
     }
+    if constexpr (MODE != 2) {
     float fv[MIXMAX];
 #pragma unroll
     for (int m = 0; m < MIXMAX; m++) fv[m] = (m < mix && col && i < n) ? __ldg(a.fn + (size_t)m * n + i) : 0.0f;
@@ -337,16 +343,20 @@ __device__ __forceinline__ void hc_pre_body(const HcPreArgs &a)
         for (int w = 0; w < 8; w++) t += red8[tid][w];
         partq[(size_t)blockIdx.x * NV + tid] = t;
     }
+    if constexpr (MODE == 1) return;
     __threadfence();
     __syncthreads();
     if (tid == 0) last = atomicAdd(cntq, 1u) == gridDim.x - 1;
     __syncthreads();
     if (!last) return;
     __threadfence();
+    } else {
+        pdl_wait();                                 // the partials of the previous launch
+    }
     const float *x = stepped ? xoutq : xq;
     // every block's partials: 8 threads per value each add gridDim/8 blocks,
     // then the 8 sums in order
-    const int nblk = (int)gridDim.x, per = (nblk + 7) >> 3;
+    const int nblk = nparts, per = (nblk + 7) >> 3;
     if (tid < NV * 8) {
         const int m = tid >> 3, w = tid & 7;
         constexpr int PB = kHcPreBlocks / 8;       // per <= PB: all loads first
@@ -370,7 +380,7 @@ __device__ __forceinline__ void hc_pre_body(const HcPreArgs &a)
         tot[tid] = t;
     }
     __syncthreads();
-    if (tid == 0) *cntq = 0u;
+    if (MODE == 0 && tid == 0) *cntq = 0u;
     if (tid < 32) {
         const float rs = __fdiv_rn(1.0f, __fsqrt_rn((float)(tot[MIXMAX] / (double)n) + a.rms_eps));
         if (tid < mix) mixes[tid] = __fmul_rn((float)tot[tid], rs);
@@ -451,8 +461,10 @@ __device__ __forceinline__ void hc_pre_body(const HcPreArgs &a)
     }
 }
 
-__global__ void __launch_bounds__(288) k_hc_pre(const __grid_constant__ HcPreArgs a) { hc_pre_body<false>(a); }
-__global__ void __launch_bounds__(288) k_hc_pre_batch(const __grid_constant__ HcPreArgs a) { hc_pre_body<true>(a); }
+__global__ void __launch_bounds__(288) k_hc_pre(const __grid_constant__ HcPreArgs a) { hc_pre_body<false, 0>(a); }
+__global__ void __launch_bounds__(288) k_hc_pre_batch(const __grid_constant__ HcPreArgs a) { hc_pre_body<true, 0>(a); }
+__global__ void __launch_bounds__(288) k_hc_part_batch(const __grid_constant__ HcPreArgs a) { hc_pre_body<true, 1>(a); }
+__global__ void __launch_bounds__(288) k_hc_tail_batch(const __grid_constant__ HcPreArgs a) { hc_pre_body<true, 2>(a); }
 
 // The head's reduction: a sigmoid gate per copy, one scalar scale, no
 // Sinkhorn (src/cli/dsv4_run.c:94-116). One block.

@@ -173,26 +173,40 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
     const int nb = it.cols / F::COLS, rb = it.rowbytes, trh = it.tr >> 1;
     constexpr int NPP = NP > 0 ? NP : 1;                 // accumulator sets
-    const int nt = NP > 0 && it.nt > 1 ? it.nt : 1;
+    constexpr int MAXT = NP > 0 ? 2 * NP : 1;           // tokens an item can carry
+    int nt = NP > 0 && it.nt > 1 ? it.nt : 1;
     const size_t xtab = (size_t)nb * MPU * 12;            // one token's x fragments (uint2)
     uint4 *ring = reinterpret_cast<uint4 *>(smem);
     uint2 *sring = reinterpret_cast<uint2 *>(smem + kMmaRing);
     uint2 *xp = reinterpret_cast<uint2 *>(smem + kMmaRing + kMmaSRing);                         // [nt][...]
-    int *kbs = reinterpret_cast<int *>(smem + kMmaRing + kMmaSRing + (size_t)nt * nb * MPU * kMmaXpPerMma);  // [nt][nb]
-    double *runs = reinterpret_cast<double *>(smem + kMmaRing + kMmaSRing + (size_t)nt * nb * MPU * kMmaXpPerMma +
-                                              (((size_t)nt * nb * 4 + 15) & ~(size_t)15));   // [nt][tr][8]
 
     const uint8_t *W = it.W, *S = it.S, *W2 = it.W2, *S2 = it.S2;
     const float *X = it.x;
     float *Y = it.y;
+    // token i's x / y: X + xo[i], Y + yo[i]
+    size_t xo[MAXT], yo[MAXT];
+#pragma unroll
+    for (int i = 0; i < MAXT; i++) {
+        xo[i] = (size_t)i * it.xts;
+        yo[i] = (size_t)i * it.yts;
+    }
     if (it.wtab) {
         pdl_wait();                  // the selection comes from the previous kernel
         int si = it.slot;
-        if (it.perm) {               // a batch's routed item: its token and slot
-            const int pe = __ldcg(it.perm + it.slot), tk = pe >> 8, kk = pe & 255;
-            X += (size_t)tk * it.xs + (size_t)kk * it.xk;
-            Y += (size_t)tk * it.ys + (size_t)kk * it.yk;
-            si = tk * it.ss + kk;
+        if (it.perm) {
+            // a batch's routed group: perm[5 slot] tokens (0 = an unused slot)
+            // of one expert, entries (token << 8) | k
+            const int *gd = it.perm + (size_t)it.slot * 5;
+            const int ng = __ldcg(gd);
+            if (ng <= 0) return;
+            nt = NP > 0 ? min(ng, MAXT) : 1;
+#pragma unroll
+            for (int i = 0; i < MAXT; i++) {
+                const int pe = i < nt ? __ldcg(gd + 1 + i) : 0, tk = pe >> 8, kk = pe & 255;
+                xo[i] = (size_t)tk * it.xs + (size_t)kk * it.xk;
+                yo[i] = (size_t)tk * it.ys + (size_t)kk * it.yk;
+                if (i == 0) si = tk * it.ss + kk;
+            }
         }
         const int e = __ldcg(it.sel + si);
         W = it.wtab[e];
@@ -202,6 +216,9 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
             S2 = it.s2tab ? it.s2tab[e] : nullptr;
         }
     }
+    int *kbs = reinterpret_cast<int *>(smem + kMmaRing + kMmaSRing + (size_t)nt * nb * MPU * kMmaXpPerMma);  // [nt][nb]
+    double *runs = reinterpret_cast<double *>(smem + kMmaRing + kMmaSRing + (size_t)nt * nb * MPU * kMmaXpPerMma +
+                                              (((size_t)nt * nb * 4 + 15) & ~(size_t)15));   // [nt][tr][8]
     // The canonical order sums eight contiguous runs of ceil(nb / 8) units;
     // R of them are non-empty. Warp w takes run w % R of row groups
     // w / R, w / R + SH, ... (SH = 8 / R warps share a run when R < 8), and
@@ -259,8 +276,10 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
     // passes for the 16 k16-steps of an FP4 unit. All of a token's x loads
     // are issued before any is used.
     constexpr int XU = kMmaMaxBlocks / 8, XH = MPU / 8;
-    for (int tk = 0; tk < nt; tk++) {
-        const float *xt = X + (size_t)tk * it.xts;
+#pragma unroll
+    for (int tk = 0; tk < MAXT; tk++) {
+        if (tk >= nt) break;
+        const float *xt = X + xo[tk];
         uint2 *xpt = xp + tk * xtab;
         float4 xv[XU][XH];
 #pragma unroll
@@ -452,8 +471,10 @@ __device__ __forceinline__ void mma_tile(const GemvItem &it, int tile, unsigned 
         return (float)tt;
     };
     const int nreal = it.pair ? trh : it.tr;
-    for (int tk = 0; tk < nt; tk++) {
-        float *yt = Y + (size_t)tk * it.yts;
+#pragma unroll
+    for (int tk = 0; tk < MAXT; tk++) {
+        if (tk >= nt) break;
+        float *yt = Y + yo[tk];
         for (int r = tid; r < nreal; r += blockDim.x) {
             const int row = tile * nreal + r;
             if (row >= it.rows) break;

@@ -22,12 +22,12 @@ struct GemvItem {
     float *y;
     int fmt, rows, cols, sc, lbr, lbc, rowbytes, slot, pair;
     int mma;                // on the tensor cores (gemv_mma.cuh)
-    // Routed items of a batch (tensor-core items only): with perm set, entry
-    // perm[slot] = (token << 8) | k names the token and its selection slot k;
-    // the item reads x + token xs + k xk, writes y + token ys + k yk, and its
-    // expert is sel[token ss + k]. A launch's items then follow an order
-    // chosen on the device (tokens sorted by expert) without changing any
-    // item's arithmetic.
+    // Routed items of a batch (tensor-core items only): with perm set, the
+    // item is group `slot` of a device-side list (perm[5 slot] tokens, 0 for
+    // an unused slot, entries (token << 8) | k at perm[5 slot + 1 ..]): for
+    // each entry it reads x + token xs + k xk and writes y + token ys + k yk;
+    // the group's expert is sel[token ss + k] of its first entry. Every
+    // token's arithmetic is that of a single-token item.
     const int *perm;
     int xs, xk, ys, yk, ss;
     // Tokens of one item (tensor-core items): nt > 1 applies the matrix to nt

@@ -71,7 +71,7 @@ struct dsv4b_model {
     // MoE scratch s_ms floats apart
     int nseq;
     long s_ms;
-    int *moe_perm;             // a batch's (token, slot) pairs in expert order
+    int *moe_perm;             // a batch's expert groups (5 ints per slot, k_moe_group)
     std::vector<void *> allocs;
     cudaStream_t stream;
     cudaGraph_t graph;
@@ -229,7 +229,7 @@ static bool alloc_common(dsv4b_model *m)
     const int inter_s = c.moe_inter * c.n_shared;
     const size_t nf = moe_scratch_floats(d, c.moe_inter, inter_s, c.n_experts, c.topk);
     m->s_ms = (long)((nf + kMoeMaxTopk + 63) & ~(size_t)63);
-    m->moe_perm = (int *)dcopy(m, nullptr, B * kMoeMaxTopk * 4, &ok);
+    m->moe_perm = (int *)dcopy(m, nullptr, B * kMoeMaxTopk * 5 * 4, &ok);
     float *msb = F(B * m->s_ms);
     if (ok) moe_scratch_carve(m->ms, msb, d, c.moe_inter, inter_s, c.n_experts, c.topk);
     for (int L = 0; L < c.n_layers && ok; L++) {

@@ -102,16 +102,18 @@ __global__ void k_route(const float *logits, const float *bias, const int *fixed
     }
 }
 
-// A batch's (token, slot) pairs in expert order: perm[r] = (t << 8) | k for
-// the pair of rank r under (expert, token, slot), so the grouped expert
-// launches that follow meet the tokens sharing an expert side by side and
-// read its weights from HBM once (the other tokens' blocks find them in L2).
-// One block; n = nseq topk <= 1024.
-__global__ void k_moe_sort(const int *sel, long s_ms, int nseq, int topk, int *perm)
+// The union of a batch's experts, in groups: the (token, slot) pairs are
+// ordered by (expert, token, slot), each expert's run is cut into groups of
+// at most `chunk` pairs, and group g is written as groups[5 g] = its size,
+// groups[5 g + 1 ..] = (t << 8) | k; the slots after the last group get size
+// 0. A routed item per slot then streams and decodes its expert once for
+// every token of its group. One block; n = nseq topk <= 1024.
+__global__ void k_moe_group(const int *sel, long s_ms, int nseq, int topk, int chunk, int *groups)
 {
     pdl_trigger();
     pdl_wait();
-    __shared__ int es[1024];
+    __shared__ int es[1024], ord[1024];
+    __shared__ int s_ng;
     const int n = nseq * topk;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int t = i / topk, k = i - t * topk;
@@ -122,9 +124,26 @@ __global__ void k_moe_sort(const int *sel, long s_ms, int nseq, int topk, int *p
         const int e = es[i];
         int r = 0;
         for (int j = 0; j < n; j++) r += (es[j] < e) || (es[j] == e && j < i);
-        const int t = i / topk;
-        perm[r] = (t << 8) | (i - t * topk);
+        ord[r] = i;
     }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int ng = 0, run = 0, prev = -1;
+        for (int r = 0; r < n; r++) {
+            const int i = ord[r], e = es[i];
+            if (e != prev || run == chunk) {      // a new group
+                ng++;
+                run = 0;
+                prev = e;
+            }
+            const int t = i / topk;
+            groups[(size_t)(ng - 1) * 5 + 1 + run] = (t << 8) | (i - t * topk);
+            groups[(size_t)(ng - 1) * 5] = ++run;
+        }
+        s_ng = ng;
+    }
+    __syncthreads();
+    for (int g = s_ng + threadIdx.x; g < n; g += blockDim.x) groups[(size_t)g * 5] = 0;
 }
 
 // out[i] = sum_k w[k] * acc[k][i] in k order, each product and sum rounded
@@ -166,7 +185,19 @@ int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float 
     const bool sorted = nseq > 1 && perm && nseq * K <= 1024 &&
                         gemv_mma_shape(L.efmt, H, L.eblk_r, L.eblk_c, L.ef16s != 0) &&
                         gemv_mma_shape(L.efmt, I, L.eblk_r, L.eblk_c, L.ef16s != 0);
-    if (sorted) launch(k_moe_sort, dim3(1), dim3(256), 0, st, S.sel, s_ms, nseq, K, perm);
+    // tokens per group: what both the gate / up and the down items can carry
+    int chunk = 1;
+    if (sorted) {
+        GemvItem u, dn;
+        if (!gemv_item(u, L.efmt, nullptr, nullptr, I, H, L.eblk_r, L.eblk_c, x, S.h, L.ef16s != 0) ||
+            !gemv_item(dn, L.efmt, nullptr, nullptr, H, I, L.eblk_r, L.eblk_c, S.h, S.acc, L.ef16s != 0))
+            return -1;
+        u.pair = 1;
+        // two tokens keep two blocks per SM (four need the one-block budget)
+        const int cu = gemv_item_tokens(u, 2, 0, 0), cd = gemv_item_tokens(dn, 2, 0, 0);
+        chunk = cu < cd ? cu : cd;
+        launch(k_moe_group, dim3(1), dim3(256), 0, st, S.sel, s_ms, nseq, K, chunk, perm);
+    }
     // the items of one stage (every token's selected experts, then its shared
     // expert), launched kGemvMaxItems at a time: a launch's grouping never
     // changes an item's arithmetic
@@ -190,6 +221,7 @@ int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float 
             it.w2tab = L.w3tab; it.s2tab = L.s3tab;
             it.sel = S.sel; it.slot = j;
             it.perm = perm; it.xs = (int)s_x; it.xk = 0; it.ys = (int)s_ms; it.yk = I; it.ss = (int)s_ms;
+            it.nt = chunk;
             it.pair = 1; it.limit = L.swiglu_limit;
             items.push_back(it);
         }
@@ -233,6 +265,7 @@ int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float 
             it.wtab = L.w2tab; it.stab = L.s2tab;
             it.sel = S.sel; it.slot = j;
             it.perm = perm; it.xs = (int)s_ms; it.xk = I; it.ys = (int)s_ms; it.yk = H; it.ss = (int)s_ms;
+            it.nt = chunk;
             items.push_back(it);
         }
     }

@@ -51,8 +51,8 @@ struct MoeScratch {
 // A batch of nseq tokens (combine false, ex null): token b's x at x + b s_x,
 // its scratch S shifted by b s_ms floats, its token id at token + b
 // tok_stride; every token's experts and arithmetic are those of a batch-1
-// call. perm (device, nseq topk ints), when given, lets the routed items run
-// in expert order (tokens sharing an expert in one launch).
+// call. perm (device, 5 nseq topk ints), when given, holds the batch's
+// expert groups: every distinct expert's tokens, up to four to a routed item.
 int moe_forward(const MoeLayer &L, const MoeScratch &S, float *out, const float *x,
                 const int *token, cudaStream_t st, bool combine = true, const Exch *ex = nullptr, int nseq = 1,
                 long s_ms = 0, long s_x = 0, int tok_stride = 0, int *perm = nullptr);

@@ -304,6 +304,41 @@ def model_greedy_ref(sm, tokens, n_gen, max_pos):
     return out[:n], lg[:n]
 
 
+class BoundCheckpoint:
+    """A checkpoint directory bound by the REFERENCE's own reader and binder
+    (oracle/_ref: dsv4_st_open, dsv4_bind_model, dsv4_bind_layer, experts by
+    their cache's names) into the structs the model constructor takes: .cfg,
+    .mw, .layers, .experts, .d (so it stands in for a SyntheticModel)."""
+
+    def __init__(self, directory, sm):
+        import dsv4_model as M
+        self.d, self.cfg = sm.d, sm.cfg
+        nl, ne = sm.d["n_layers"], sm.d["n_experts"]
+        self.mw = M.ModelW()
+        self.layers = (M.LayerW * nl)()
+        self.experts = (M.ExpertW * (nl * ne))()
+        self._lib = C.CDLL(REF_SO)
+        f = self._lib.dsv4ref_bind_dir
+        f.argtypes = [C.c_char_p, _vp, _vp, _vp, _vp]
+        f.restype = _vp
+        self._lib.dsv4ref_bind_free.argtypes = [_vp]
+        self.h = f(os.fsencode(directory), C.addressof(self.cfg), C.addressof(self.mw),
+                   C.addressof(self.layers), C.addressof(self.experts))
+        if not self.h:
+            raise RuntimeError("the reference's binder rejected " + str(directory))
+
+    def close(self):
+        if self.h:
+            self._lib.dsv4ref_bind_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def model_decode_timed_ref(sm, n_pos, first_token=1, max_pos=None, prompt=None):
     """Per-layer and head wall times (seconds) of the REFERENCE's decode loop
     (dsv4_layer_forward per layer, then hc_head + norm + LM head + argmax)

@@ -75,6 +75,28 @@ def decode_bytes_per_step(d, pos, batch):
     return one + nl * (expected_experts(d, batch) - d["topk"]) * per_expert + (batch - 1) * kv
 GEMV_METRIC = "FP8 block-scaled GEMV HBM GB/s (config 1, 4096x7168 e4m3, batch 1)"
 
+
+def prefill_metric(n_prompt, chunk):
+    return ("prefill tok/s (Flash-scale synthetic, config 5, %d-token prompt in passes of %d)"
+            % (n_prompt, chunk))
+
+
+def prefill_bytes(d, n_prompt, chunk):
+    """Algorithmic HBM bytes of a whole prefill: per pass every weight once
+    (the routed experts as the expected distinct ones of the pass's tokens)
+    and every token's attended KV rows; the LM head once (the prompt's last
+    token only)."""
+    head = d["vocab"] * d["hidden"] * 2
+    per_expert = 3 * fp4_bytes(d["moe_inter"], d["hidden"])
+    nl = len(layer_ratios(d))
+    b0 = decode_bytes_per_token(d, 0)
+    total = head
+    for p0 in range(0, n_prompt, chunk):
+        nt = min(chunk, n_prompt - p0)
+        total += decode_bytes_per_token(d, p0) - head + nl * (expected_experts(d, nt) - d["topk"]) * per_expert
+        total += sum(decode_bytes_per_token(d, p0 + t) - b0 for t in range(1, nt))
+    return total
+
 # DRAM bytes (read + write) per unit from an ncu capture of the same kernel
 # and workload, or None where none was taken.
 TRAFFIC_C1 = 29456384          # one config-1 GEMV launch (ncu dram__bytes_read + write)
@@ -437,6 +459,121 @@ def run_decode(a):
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# ------------------------------------------------------------- prefill
+
+def cpu_prefill_sample(chunk, n_pass=2):
+    """The reference's batched prompt path (dsv4_layer_forward_n in passes of
+    chunk tokens, oracle/_ref) on the 3-layer Flash-geometry sample: a random
+    prompt of n_pass passes, per-layer pass times scaled to the 43-layer mix.
+    Returns (seconds per prompt token, description)."""
+    import oracle as O
+    import dsv4_model as M
+    full = layer_ratios(M.flash_config())
+    count = {r: full.count(r) for r in set(full)}
+    d = M.flash_sample_config()
+    t0 = time.perf_counter()
+    sm = M.SyntheticModel(d, seed=0, fast=True)
+    t_build = time.perf_counter() - t0
+    n = chunk * n_pass
+    prompt = np.random.default_rng(0).integers(0, d["vocab"], n).astype(np.int32)
+    t0 = time.perf_counter()
+    _, tp = O.model_prefill_ref(sm, prompt, 0, n + 1, chunk)
+    t_run = time.perf_counter() - t0
+    per_pass = tp[:, 0] * count[0] + tp[:, 1] * count[4] + tp[:, 2] * count[128]
+    desc = ("reference dsv4_layer_forward_n in passes of %d (oracle/_ref, the --batch prompt path of "
+            "src/cli/dsv4_run.c:391-442) on a 3-layer Flash-geometry sample (ratios 0/4/128, 256 experts), "
+            "positions 0..%d, per-layer pass times scaled to the 43-layer mix (%d/%d/%d), the one LM head "
+            "of the prompt left out; OMP_NUM_THREADS=%s; sample build %.0f s, run %.0f s"
+            % (chunk, n - 1, count[0], count[4], count[128],
+               os.environ.get("OMP_NUM_THREADS", "all %d" % os.cpu_count()), t_build, t_run))
+    return float(np.sum(per_pass) / n), desc
+
+
+def run_prefill(a):
+    import torch
+    import dsv4_b200 as B
+    import dsv4_model as M
+    if a.gpus != 1:
+        raise SystemExit("prefill runs on one GPU (a one-sequence model)")
+    L = B.init()
+    d = M.flash_config()
+    W, K, P, CH = max(a.warmup, 3), a.steps, a.context, a.chunk
+    t0 = time.perf_counter()
+    model = B.Model(M.ConfigOnly(d), P + 8, synthetic_seed=1234)
+    t_create = time.perf_counter() - t0
+    prompt = np.random.default_rng(0).integers(0, d["vocab"], P).astype(np.int32)
+    stream = torch.cuda.ExternalStream(L.dsv4b_model_stream(model.h))
+    # the prompt through per-token decode steps (the graph generate() runs),
+    # for comparison
+    model.begin(prompt)
+    torch.cuda.synchronize()
+    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record(stream)
+    for _ in range(P):
+        B.check(L.dsv4b_model_step_async(model.h, None), "dsv4b_model_step_async")
+    eb.record(stream)
+    torch.cuda.synchronize()
+    per_token_s = ea.elapsed_time(eb) * 1e-3
+    # warm-up: each pass shape runs eagerly, then is captured, then replayed
+    for _ in range(W):
+        first = model.prefill(prompt, CH)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(torch.cuda.current_device()) as clk:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(K):
+            if model.prefill(prompt, CH) != first:
+                raise SystemExit("prefill is not deterministic")
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    kernels = L.dsv4b_model_prefill_kernels(model.h)
+    ms_step = ms / K
+    value = P * K / (ms * 1e-3)
+    # e2e: the C-ABI call on wall clock (host prompt in, first token out)
+    t0 = time.perf_counter()
+    for _ in range(K):
+        model.prefill(prompt, CH)
+    e2e_s = (time.perf_counter() - t0) / K
+    peak, src = peaks()
+    byts = prefill_bytes(d, P, CH)
+    ach = byts / (ms_step * 1e-3) / 1e9
+    n_pass = -(-P // CH)
+    out = {
+        "metric": prefill_metric(P, CH),
+        "value": value, "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp8 e4m3 / fp4 e2m1 / bf16 weights, f32 activations, f64 row sums",
+        "data": "synthetic (random-init weights generated on device, random %d-token prompt)" % P,
+        "config": {"workload": "prefill config 5 (Flash-scale synthetic)", "prompt": P, "chunk": CH,
+                   "passes": n_pass, "layers": d["n_layers"], "experts": d["n_experts"], "topk": d["topk"],
+                   "vocab": d["vocab"], "create_s": round(t_create, 1),
+                   "step": "one whole prefill (dsv4b_model_prefill: reset, %d passes, the head on the last "
+                           "token), each pass a replayed graph" % n_pass,
+                   "per_token_prompt_tok_s": P / per_token_s,
+                   "l2": "no flush: each pass streams > 10 GB of distinct weights (> 126 MB L2)"},
+        "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                     "peak_source": src + " burst hbm_gbs",
+                     "scope": "whole prefill (every pass's launches)",
+                     "bytes_per_unit": byts, "traffic": None,
+                     "traffic_source": "not captured for this workload"},
+        "gpu_launches": kernels * K if kernels > 0 else None,
+        "clocks": clk.summary(),
+        "e2e": {"value": P / e2e_s, "unit": "tok/s", "ms_per_step": e2e_s * 1e3,
+                "h2d_bytes_per_step": 4 * P + 8 * P + 8, "d2h_bytes_per_step": 4,
+                "api": "dsv4b_model_prefill (host prompt -> host first token), wall clock"},
+    }
+    if not a.no_cpu:
+        s_tok, desc = cpu_prefill_sample(CH)
+        out["cpu_baseline"] = {"value": 1.0 / s_tok, "unit": "tok/s",
+                               "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count())),
+                               "kind": "reference", "sample": desc}
+    print(json.dumps(out))
+    model.close()
+    L.dsv4_cuda_shutdown()
 
 
 # -------------------------------------------------------------- GEMV (C1)
@@ -902,6 +1039,23 @@ def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    if a.workload == "prefill":
+        s_tok, desc = cpu_prefill_sample(a.chunk)
+        v = 1.0 / s_tok
+        print(json.dumps({
+            "metric": prefill_metric(a.context, a.chunk), "value": v, "unit": "tok/s", "impl": "reference",
+            "n_gpus": a.gpus, "steps": 1, "warmup": 0, "ms_per_step": s_tok * a.context * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp8 e4m3 / fp4 e2m1 / bf16 weights, f32 activations, f64 row sums",
+            "data": "synthetic (random-init weights, random prompt)",
+            "config": {"workload": "prefill config 5 (Flash-scale synthetic)", "prompt": a.context,
+                       "chunk": a.chunk, "layers": "43 (3 timed, per-layer times scaled to the 43-layer mix)",
+                       "sample": "the first 2 passes of the prompt"},
+            "cpu_baseline": {"value": v, "unit": "tok/s",
+                             "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count())),
+                             "kind": "reference", "sample": desc},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
     if a.workload == "decode":
         # the GPU arm's first positions after the same prompt and warm-up (a
         # bounded sample of them: minutes, not hours)
@@ -954,19 +1108,23 @@ def main():
                     help="timed steps (default 256 decode tokens / 20000 GEMVs)")
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv_fp8", "moe", "mla"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "gemv_fp8", "moe", "mla"])
     ap.add_argument("--batch", type=int, default=1,
                     help="decode: sequences stepped together (config 5: 1 or 32); mla: sequences per step "
                          "(config 3: 1 or 8)")
-    ap.add_argument("--context", type=int, default=512, help="decode: prompt tokens before timing")
+    ap.add_argument("--context", type=int, default=512,
+                    help="decode: prompt tokens before timing; prefill: the prompt's tokens")
+    ap.add_argument("--chunk", type=int, default=32, help="prefill: tokens per pass (1..64)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     a = ap.parse_args()
     if a.steps is None:
-        a.steps = {"decode": 256, "gemv_fp8": 20000, "moe": 200, "mla": 50}[a.workload]
+        a.steps = {"decode": 256, "prefill": 3, "gemv_fp8": 20000, "moe": 200, "mla": 50}[a.workload]
     if a.impl == "reference":
         run_reference(a)
     elif a.workload == "decode":
         run_decode(a)
+    elif a.workload == "prefill":
+        run_prefill(a)
     elif a.workload == "moe":
         run_moe(a)
     elif a.workload == "mla":

@@ -11,6 +11,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <utility>
 #include <vector>
 
@@ -72,6 +73,22 @@ struct dsv4b_model {
     int nseq;
     long s_ms;
     int *moe_perm;             // a batch's expert groups (5 ints per slot, k_moe_group)
+    // activation rows: nseq, or on a one-sequence model the tokens of a
+    // prefill pass (pst holds their step states)
+    int cap;
+    dsv4b::StepState *pst;
+    // prefill passes as graphs, one per (tokens, last) shape: a shape runs
+    // eagerly the first time (which also sets every kernel attribute), is
+    // captured the second, replayed after; pf_kernels counts the kernels the
+    // last prefill launched (-1 when a pass ran eagerly)
+    struct PassGraph {
+        int key, kernels;
+        cudaGraph_t graph;
+        cudaGraphExec_t exec;
+    };
+    std::vector<PassGraph> pgraphs;
+    std::vector<int> pseen;
+    int pf_kernels;
     std::vector<void *> allocs;
     cudaStream_t stream;
     cudaGraph_t graph;
@@ -186,30 +203,31 @@ static bool alloc_common(dsv4b_model *m)
     }
     m->nidx = win + extra;
     const size_t big = (size_t)(d > c.q_lora ? d : c.q_lora);
-    const size_t B = (size_t)m->nseq;
+    // B: sequences (caches, step states, tokens); R: activation rows
+    const size_t B = (size_t)m->nseq, R = (size_t)m->cap;
     auto F = [&](size_t n) { return (float *)dcopy(m, nullptr, n * 4, &ok); };
-    m->h = F(B * hc * d);
-    m->resid = F(B * hc * d);
-    m->x1 = F(B * d);
-    m->blk = F(B * d);
-    m->post = F(B * DSV4B_MAX_HC);
-    m->comb = F(B * DSV4B_MAX_HC * DSV4B_MAX_HC);
+    m->h = F(R * hc * d);
+    m->resid = F(R * hc * d);
+    m->x1 = F(R * d);
+    m->blk = F(R * d);
+    m->post = F(R * DSV4B_MAX_HC);
+    m->comb = F(R * DSV4B_MAX_HC * DSV4B_MAX_HC);
     m->mixes = F((2 + DSV4B_MAX_HC) * DSV4B_MAX_HC);
-    m->qr = F(B * big);
-    m->q = F(B * c.n_heads * hd);
-    m->kv = F(B * hd);
-    m->o = F(B * c.n_heads * hd);
-    m->ogrp = F(B * c.o_groups * c.o_lora);
-    m->comp_in = F(B * 2 * hd);
-    m->comp_sc = F(B * 2 * hd);
-    m->idx_q = F(B * c.index_n_heads * c.index_head_dim);
-    m->idx_w = F(B * c.index_n_heads);
+    m->qr = F(R * big);
+    m->q = F(R * c.n_heads * hd);
+    m->kv = F(R * hd);
+    m->o = F(R * c.n_heads * hd);
+    m->ogrp = F(R * c.o_groups * c.o_lora);
+    m->comp_in = F(R * 2 * hd);
+    m->comp_sc = F(R * 2 * hd);
+    m->idx_q = F(R * c.index_n_heads * c.index_head_dim);
+    m->idx_w = F(R * c.index_n_heads);
     m->idx_scores = F(B * m->ncomp4);
     m->ix_terms = (double *)dcopy(m, nullptr, B * m->ncomp4 * c.index_n_heads * 8, &ok);
     m->ix_count = (unsigned *)dcopy(m, nullptr, B * ((m->ncomp4 + 31) / 32) * 4, &ok);
     if (ok && cudaMemset(m->ix_count, 0, B * ((m->ncomp4 + 31) / 32) * 4) != cudaSuccess) ok = false;
     m->logits = F(B * c.vocab);
-    m->xh = F(B * d);
+    m->xh = F(R * d);
     m->am_pv = F(B * kArgmaxParts);
     m->am_pair = F(2);
     m->stepseq = (unsigned *)dcopy(m, nullptr, 4, &ok);
@@ -217,20 +235,21 @@ static bool alloc_common(dsv4b_model *m)
     m->nx = 2 * c.n_layers;
     m->am_gather = F(2 * 64);
     m->am_pi = (int *)dcopy(m, nullptr, B * kArgmaxParts * 4, &ok);
-    m->idxs = (int *)dcopy(m, nullptr, B * m->nidx * 4, &ok);
+    m->idxs = (int *)dcopy(m, nullptr, R * m->nidx * 4, &ok);
     m->isel = (int *)dcopy(m, nullptr, B * (c.index_topk > 0 ? c.index_topk : 1) * 4, &ok);
     m->prompt = (int *)dcopy(m, nullptr, B * m->max_pos * 4, &ok);
     m->out_tokens = (int *)dcopy(m, nullptr, B * m->max_pos * 4, &ok);
     m->st = (StepState *)dcopy(m, nullptr, B * sizeof(StepState), &ok);
+    m->pst = (StepState *)dcopy(m, nullptr, R * sizeof(StepState), &ok);
     m->attn_part = dcopy(m, nullptr, attn_part_bytes(c.n_heads, hd, m->nidx, (int)B), &ok);
-    m->hc_part = (double *)dcopy(m, nullptr, B * kHcPreBlocks * (kHcPreMixMax + 1) * 8, &ok);
-    m->hc_cnt = (unsigned *)dcopy(m, nullptr, B * 4, &ok);
-    if (ok && cudaMemset(m->hc_cnt, 0, B * 4) != cudaSuccess) ok = false;
+    m->hc_part = (double *)dcopy(m, nullptr, R * kHcPreBlocks * (kHcPreMixMax + 1) * 8, &ok);
+    m->hc_cnt = (unsigned *)dcopy(m, nullptr, R * 4, &ok);
+    if (ok && cudaMemset(m->hc_cnt, 0, R * 4) != cudaSuccess) ok = false;
     const int inter_s = c.moe_inter * c.n_shared;
     const size_t nf = moe_scratch_floats(d, c.moe_inter, inter_s, c.n_experts, c.topk);
     m->s_ms = (long)((nf + kMoeMaxTopk + 63) & ~(size_t)63);
-    m->moe_perm = (int *)dcopy(m, nullptr, B * kMoeMaxTopk * 5 * 4, &ok);
-    float *msb = F(B * m->s_ms);
+    m->moe_perm = (int *)dcopy(m, nullptr, R * kMoeMaxTopk * 5 * 4, &ok);
+    float *msb = F(R * m->s_ms);
     if (ok) moe_scratch_carve(m->ms, msb, d, c.moe_inter, inter_s, c.n_experts, c.topk);
     for (int L = 0; L < c.n_layers && ok; L++) {
         DevLayer &l = m->L[L];
@@ -323,9 +342,10 @@ static bool hc_fused(const DSV4Cfg &c)
 }
 
 // The post-mix of the pending sub-layer (hin -> hout, then swapped) and the
-// pre-mix of the next one into y (x1, or the head's xh when head is set).
+// pre-mix of the next one into y (x1, or the head's xh when head is set), for
+// the rows activation rows (a batch's sequences or a prefill pass's tokens).
 static void hc_step(dsv4b_model *m, Pending &p, float *&hin, float *&hout, const float *fn, const float *base,
-                    const float *scale, const float *norm, bool head, float *y, cudaStream_t st)
+                    const float *scale, const float *norm, bool head, float *y, cudaStream_t st, int rows)
 {
     const DSV4Cfg &c = m->c;
     const int hc = c.hc_mult, mix = (2 + hc) * hc, n = hc * c.hidden, wide = n;
@@ -362,9 +382,9 @@ static void hc_step(dsv4b_model *m, Pending &p, float *&hin, float *&hout, const
         a.hc_eps = c.hc_eps;
         a.rms_eps = c.rms_eps;
         a.s_ms = m->s_ms;
-        if (m->nseq > 1) {
-            launch(k_hc_part_batch, dim3(n / 256, m->nseq), dim3(288), 0, st, a);
-            launch(k_hc_tail_batch, dim3(m->nseq), dim3(288), 0, st, a);
+        if (rows > 1) {
+            launch(k_hc_part_batch, dim3(n / 256, rows), dim3(288), 0, st, a);
+            launch(k_hc_tail_batch, dim3(rows), dim3(288), 0, st, a);
         } else {
             launch(k_hc_pre, dim3(n / 256), dim3(288), 0, st, a);
         }
@@ -390,16 +410,91 @@ static void hc_step(dsv4b_model *m, Pending &p, float *&hin, float *&hout, const
     launch(k_rmsnorm, dim3(1), dim3(1024), 0, st, y, y, norm, c.hidden, c.rms_eps);
 }
 
-// One token: enqueue only, no host synchronisation (graph-capturable).
-static int enqueue_step(dsv4b_model *m, cudaStream_t st)
+// The cache-bound work of one layer's attention (src/model/dsv4_layer.c:224-301):
+// the q heads, the KV row and the compressor step, the indexer's scores and
+// top-k (or the full row list), then attention over the attended rows. It
+// covers n activation rows from row r0: in a decode step the batch's
+// sequences (r0 = 0, row y is sequence y, with its own cache); in a prefill
+// pass one token (n = 1) of sequence 0, whose step state is sts.
+static int attn_core(dsv4b_model *m, DevLayer &l, int r0, int n, const StepState *sts, cudaStream_t st)
+{
+    const DSV4Cfg &c = m->c;
+    const int hd = c.head_dim, rd = c.qk_rope, H = c.n_heads / m->world, win = c.sliding_window;
+    const int ih = c.index_n_heads, id = c.index_head_dim;
+    const float *cs = l.ratio ? m->cs_c : m->cs_d, *sn = l.ratio ? m->sn_c : m->sn_d;
+    int rc = 0;
+    // q heads, the KV row, the compressor, the indexer's q heads (or the
+    // attended row list) in one launch (dsv4_layer.c:224-295)
+    PrepArgs pa = {};
+    pa.q = m->q + (size_t)r0 * H * hd;
+    pa.kv = m->kv + (size_t)r0 * hd;
+    pa.cache = l.kv_cache;
+    pa.comp_kv = l.comp_kv;
+    pa.comp_score = l.comp_score;
+    pa.idx_q = m->idx_q + (size_t)r0 * ih * id;
+    pa.kv_norm = l.kv_norm;
+    pa.comp_in = m->comp_in + (size_t)r0 * 2 * hd;
+    pa.comp_sc = m->comp_sc + (size_t)r0 * 2 * hd;
+    pa.ape = l.ape;
+    pa.cnorm = l.cnorm;
+    pa.cs = cs;
+    pa.sn = sn;
+    pa.st = sts;
+    pa.dyn = l.dyn;
+    pa.idxs = m->idxs + (size_t)r0 * m->nidx;
+    pa.H = H;
+    pa.hd = hd;
+    pa.rd = rd;
+    pa.win = win;
+    pa.has_comp = l.has_comp;
+    pa.has_idx = l.has_comp && l.has_idx;
+    pa.ratio = l.ratio;
+    pa.index_topk = c.index_topk;
+    pa.ih = ih;
+    pa.id = id;
+    pa.nidx = m->nidx;
+    pa.eps = c.rms_eps;
+    pa.s_cache = (long)(l.kv_rows * hd);
+    pa.s_comp = (long)l.comp_n;
+    const int blocks = H + 1 + (pa.has_comp ? 1 : 0) + (pa.has_idx ? ih : 1);
+    launch(k_attn_prep, dim3(blocks, n), dim3(256), (size_t)hd * 4, st, pa);
+    if (l.has_comp && l.has_idx) {
+        const float scale = (1.0f / sqrtf((float)id)) * (1.0f / sqrtf((float)ih));
+        // the compressed region read as contiguous rows of index_head_dim
+        // floats, as the reference does (dsv4_layer.c:286-289)
+        rc |= indexer_score(m->idx_scores, pa.idx_q, l.kv_cache + (size_t)win * hd, DSV4B_DT_F32, id,
+                            (long)(l.kv_rows * hd), m->idx_w + (size_t)r0 * ih, ih, id, m->ncomp4, scale, n, st,
+                            l.dyn, m->ix_terms, m->ix_count);
+        rc |= topk(m->isel, m->idx_scores, m->ncomp4, c.index_topk, n, m->ncomp4, c.index_topk, st, l.dyn);
+        launch(k_build_idxs, dim3(n), dim3(256), 0, st, pa.idxs, m->nidx, sts, win, l.has_comp, l.has_idx, l.dyn,
+               m->isel, c.index_topk);
+    }
+    // attention, each head de-rotated by the kernel that writes it
+    const AttnRope rope = {cs, sn, &sts->pos, rd};
+    rc |= sparse_attn(m->o + (size_t)r0 * H * hd, pa.q, l.kv_cache, DSV4B_DT_F32, (long)l.kv_rows, l.sink, pa.idxs,
+                      m->nidx, H, hd, m->nidx, 1.0f / sqrtf((float)hd), n, m->attn_part, st, &rope);
+    return rc;
+}
+
+// One pass: enqueue only, no host synchronisation (graph-capturable).
+// A decode step (rows = 0): one token of each of the nseq sequences, their
+// step states at m->st. A prefill pass (rows >= 1, dsv4_layer_forward_n,
+// src/model/dsv4_layer.c:856-918): rows consecutive prompt tokens of
+// sequence 0, their step states at m->pst; every token-local step (mHC,
+// projections, output projections, MoE) runs over all rows at once, the
+// cache-bound core token by token in position order, and the head runs only
+// when head is set, on the last row, advancing m->st (which then holds that
+// row's position).
+static int enqueue_pass(dsv4b_model *m, cudaStream_t st, int rows, bool head)
 {
     const DSV4Cfg &c = m->c;
     // H: the heads of this rank (all of them on one GPU)
-    const int hc = c.hc_mult, d = c.hidden, hd = c.head_dim, rd = c.qk_rope, H = c.n_heads / m->world;
-    const int win = c.sliding_window;
-    // a batch of B sequences: every launch below covers all of them (a grid
-    // dimension, or one GEMV item per sequence)
-    const int B = m->nseq, ql = c.q_lora, ih = c.index_n_heads, id = c.index_head_dim;
+    const int hc = c.hc_mult, d = c.hidden, hd = c.head_dim, H = c.n_heads / m->world;
+    const bool prefill = rows > 0;
+    // B activation rows: a batch's sequences (every launch below covers all
+    // of them: a grid dimension, or one GEMV item per row) or a pass's tokens
+    const int B = prefill ? rows : m->nseq, ql = c.q_lora, ih = c.index_n_heads, id = c.index_head_dim;
+    const StepState *sts = prefill ? m->pst : m->st;
     int rc = 0;
     PdlChain chain;
     float *hin = m->h, *hout = m->resid;
@@ -407,14 +502,13 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
     const bool fused = hc_fused(c);
     m->xcall = 0;
     const Exch ex = {m->peer, m->comm, m->stepseq, m->nx, &m->xcall};
-    launch(k_embed, dim3(16, B), dim3(256), 0, st, hin, m->embed, m->emb_wdt, m->st, d, hc);
+    launch(k_embed, dim3(16, B), dim3(256), 0, st, hin, m->embed, m->emb_wdt, sts, d, hc);
     for (int Li = 0; Li < c.n_layers; Li++) {
         DevLayer &l = m->L[Li];
-        const float *cs = l.ratio ? m->cs_c : m->cs_d, *sn = l.ratio ? m->sn_c : m->sn_d;
         // ---- attention half (src/model/dsv4_layer.c:495-509), after the
         // previous FFN's post-mix; the residual stream ping-pongs between two
         // buffers, so no copy is needed
-        hc_step(m, pend, hin, hout, l.hca_fn, l.hca_base, l.hca_scale, l.attn_norm, false, m->x1, st);
+        hc_step(m, pend, hin, hout, l.hca_fn, l.hca_base, l.hca_scale, l.attn_norm, false, m->x1, st, B);
         // every projection of x1 in one launch, then both of the normalised q latent
         {
             Grp ga;
@@ -434,58 +528,13 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
             if (l.has_idx) grp_add(gb, l.iwq_b, m->qr, m->idx_q, st, B, ql, (long)ih * id);
             rc |= grp_run(gb, st);
         }
-        // q heads, the KV row, the compressor, the indexer's q heads (or the
-        // attended row list) in one launch (dsv4_layer.c:224-295)
-        {
-            PrepArgs pa = {};
-            pa.q = m->q;
-            pa.kv = m->kv;
-            pa.cache = l.kv_cache;
-            pa.comp_kv = l.comp_kv;
-            pa.comp_score = l.comp_score;
-            pa.idx_q = m->idx_q;
-            pa.kv_norm = l.kv_norm;
-            pa.comp_in = m->comp_in;
-            pa.comp_sc = m->comp_sc;
-            pa.ape = l.ape;
-            pa.cnorm = l.cnorm;
-            pa.cs = cs;
-            pa.sn = sn;
-            pa.st = m->st;
-            pa.dyn = l.dyn;
-            pa.idxs = m->idxs;
-            pa.H = H;
-            pa.hd = hd;
-            pa.rd = rd;
-            pa.win = win;
-            pa.has_comp = l.has_comp;
-            pa.has_idx = l.has_comp && l.has_idx;
-            pa.ratio = l.ratio;
-            pa.index_topk = c.index_topk;
-            pa.ih = ih;
-            pa.id = id;
-            pa.nidx = m->nidx;
-            pa.eps = c.rms_eps;
-            pa.s_cache = (long)(l.kv_rows * hd);
-            pa.s_comp = (long)l.comp_n;
-            const int blocks = H + 1 + (pa.has_comp ? 1 : 0) + (pa.has_idx ? ih : 1);
-            launch(k_attn_prep, dim3(blocks, B), dim3(256), (size_t)hd * 4, st, pa);
-        }
-        if (l.has_comp && l.has_idx) {
-            const float scale = (1.0f / sqrtf((float)id)) * (1.0f / sqrtf((float)ih));
-            // the compressed region read as contiguous rows of index_head_dim
-            // floats, as the reference does (dsv4_layer.c:286-289)
-            rc |= indexer_score(m->idx_scores, m->idx_q, l.kv_cache + (size_t)win * hd, DSV4B_DT_F32, id,
-                                (long)(l.kv_rows * hd), m->idx_w, ih, id, m->ncomp4, scale, B, st, l.dyn, m->ix_terms,
-                                m->ix_count);
-            rc |= topk(m->isel, m->idx_scores, m->ncomp4, c.index_topk, B, m->ncomp4, c.index_topk, st, l.dyn);
-            launch(k_build_idxs, dim3(B), dim3(256), 0, st, m->idxs, m->nidx, m->st, win, l.has_comp, l.has_idx, l.dyn,
-                   m->isel, c.index_topk);
-        }
-        // attention, each head de-rotated by the kernel that writes it
-        const AttnRope rope = {cs, sn, &m->st->pos, rd};
-        rc |= sparse_attn(m->o, m->q, l.kv_cache, DSV4B_DT_F32, (long)l.kv_rows, l.sink, m->idxs, m->nidx, H, hd,
-                          m->nidx, 1.0f / sqrtf((float)hd), B, m->attn_part, st, &rope);
+        // the cache-bound core: all sequences at once, or a pass's tokens
+        // strictly in position order (token t must find the window ring and
+        // the compressor as they stood at its own position)
+        if (!prefill)
+            rc |= attn_core(m, l, 0, B, sts, st);
+        else
+            for (int t = 0; t < B; t++) rc |= attn_core(m, l, t, 1, sts + t, st);
         // grouped low-rank output (dsv4_layer.c:303-335): the o_groups row
         // slices of wo_a, each on its own slice of o, in one launch (sharded:
         // this rank's heads are exactly its groups' slices of o)
@@ -515,21 +564,25 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
         if (m->world > 1) rc |= xreduce_sum(ex, m->blk, d, st);
         // ---- FFN half: the residual is taken after attention (:511-522)
         pend = {1, nullptr};
-        hc_step(m, pend, hin, hout, l.hcf_fn, l.hcf_base, l.hcf_scale, l.ffn_norm, false, m->x1, st);
-        rc |= moe_forward(l.moe, m->ms, m->blk, m->x1, &m->st->token, st, !fused, m->world > 1 ? &ex : nullptr, B,
+        hc_step(m, pend, hin, hout, l.hcf_fn, l.hcf_base, l.hcf_scale, l.ffn_norm, false, m->x1, st, B);
+        rc |= moe_forward(l.moe, m->ms, m->blk, m->x1, &sts->token, st, !fused, m->world > 1 ? &ex : nullptr, B,
                           m->s_ms, d, (int)(sizeof(StepState) / sizeof(int)), m->moe_perm);
         pend = {fused ? 2 : 1, &l.moe};
     }
-    // ---- head (src/cli/dsv4_run.c:467-474)
-    hc_step(m, pend, hin, hout, m->hch_fn, m->hch_base, m->hch_scale, m->norm, true, m->xh, st);
+    // a prefill pass that is not the prompt's last: only its caches matter
+    if (prefill && !head) return (rc || cudaPeekAtLastError() != cudaSuccess) ? -1 : 0;
+    // ---- head (src/cli/dsv4_run.c:467-474); a prefill pass reads only its
+    // last token's logits (the one that picks the first generated token)
+    hc_step(m, pend, hin, hout, m->hch_fn, m->hch_base, m->hch_scale, m->norm, true, m->xh, st, B);
+    const int hrows = prefill ? 1 : B;
     {
         Grp gh;
-        grp_add(gh, m->head, m->xh, m->logits, st, B, d, m->head.rows);
+        grp_add(gh, m->head, m->xh + (prefill ? (size_t)(B - 1) * d : 0), m->logits, st, hrows, d, m->head.rows);
         rc |= grp_run(gh, st);
     }
-    launch(k_argmax_part, dim3(148, B), dim3(256), 0, st, m->am_pv, m->am_pi, m->logits, m->head.rows);
+    launch(k_argmax_part, dim3(148, hrows), dim3(256), 0, st, m->am_pv, m->am_pi, m->logits, m->head.rows);
     if (m->world == 1) {
-        launch(k_argmax_final, dim3(B), dim3(32), 0, st, m->st, m->out_tokens, m->am_pv, m->am_pi, 148, 1,
+        launch(k_argmax_final, dim3(hrows), dim3(32), 0, st, m->st, m->out_tokens, m->am_pv, m->am_pi, 148, 1,
                m->prompt, m->n_prompt, (unsigned *)nullptr, m->max_pos);
     } else {
         // sharded head: each rank holds a contiguous vocabulary slice; the
@@ -545,6 +598,8 @@ static int enqueue_step(dsv4b_model *m, cudaStream_t st)
     if (cudaPeekAtLastError() != cudaSuccess) rc = -1;
     return rc ? -1 : 0;
 }
+
+static int enqueue_step(dsv4b_model *m, cudaStream_t st) { return enqueue_pass(m, st, 0, true); }
 
 static bool build_layer_from_host(dsv4b_model *m, int Li, const DSV4LayerW &w, const DSV4ExpertW *ex)
 {
@@ -633,6 +688,10 @@ extern "C" void dsv4_cuda_model_free(dsv4b_model *m)
         cudaGraphExecDestroy(m->exec);
         cudaGraphDestroy(m->graph);
     }
+    for (auto &p : m->pgraphs) {
+        cudaGraphExecDestroy(p.exec);
+        cudaGraphDestroy(p.graph);
+    }
     peer_close(m->peer);                 // after the graph that holds its exchanges
     comm_close(m->comm);
     for (void *p : m->allocs) cudaFree(p);
@@ -651,6 +710,9 @@ static dsv4b_model *model_new(const DSV4Cfg *c, int max_pos, int nseq = 1)
     m->rank = 0;
     m->world = 1;
     m->nseq = nseq;
+    // a one-sequence model keeps rows for a prefill pass (batched mHC needs
+    // the fused form)
+    m->cap = nseq > 1 ? nseq : (hc_fused(*c) ? DSV4B_MAX_PREFILL : 1);
     for (int L = 0; L < c->n_layers; L++) m->ratios[L] = c->compress_ratios ? c->compress_ratios[L] : 0;
     m->c.compress_ratios = m->ratios;
     m->max_pos = max_pos;
@@ -664,6 +726,48 @@ static dsv4b_model *model_new(const DSV4Cfg *c, int max_pos, int nseq = 1)
         return nullptr;
     }
     return m;
+}
+
+// The kernel nodes of a captured graph, or -1.
+static int graph_kernels(cudaGraph_t g)
+{
+    size_t n = 0;
+    if (cudaGraphGetNodes(g, nullptr, &n) != cudaSuccess) return -1;
+    std::vector<cudaGraphNode_t> nodes(n);
+    if (n && cudaGraphGetNodes(g, nodes.data(), &n) != cudaSuccess) return -1;
+    int k = 0;
+    for (size_t i = 0; i < n; i++) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(nodes[i], &t) != cudaSuccess) return -1;
+        k += t == cudaGraphNodeTypeKernel;
+    }
+    return k;
+}
+
+// One prefill pass of nt tokens (their step states already at m->pst), on
+// m->stream: eagerly the first time its shape is seen, captured the second
+// time, its graph replayed after that. Returns the kernels it launched (-1
+// if unknown: an eager pass), or -2 on failure.
+static int run_pass(dsv4b_model *m, int nt, bool last)
+{
+    const int key = nt * 2 + (last ? 1 : 0);
+    for (auto &p : m->pgraphs)
+        if (p.key == key) return cudaGraphLaunch(p.exec, m->stream) == cudaSuccess ? p.kernels : -2;
+    if (std::find(m->pseen.begin(), m->pseen.end(), key) == m->pseen.end()) {
+        m->pseen.push_back(key);
+        return enqueue_pass(m, m->stream, nt, last) ? -2 : -1;
+    }
+    dsv4b_model::PassGraph p = {key, 0, nullptr, nullptr};
+    if (cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return -2;
+    const int rc = enqueue_pass(m, m->stream, nt, last);
+    const cudaError_t e = cudaStreamEndCapture(m->stream, &p.graph);
+    if (rc || e != cudaSuccess || cudaGraphInstantiate(&p.exec, p.graph, 0) != cudaSuccess) {
+        if (p.graph) cudaGraphDestroy(p.graph);
+        return -2;
+    }
+    p.kernels = graph_kernels(p.graph);
+    m->pgraphs.push_back(p);
+    return cudaGraphLaunch(p.exec, m->stream) == cudaSuccess ? p.kernels : -2;
 }
 
 extern "C" dsv4b_model *dsv4_cuda_model_create_batch(const DSV4Cfg *c, const DSV4ModelW *mw,
@@ -784,6 +888,47 @@ extern "C" int dsv4_cuda_model_generate(dsv4b_model *m, const int *prompt, int n
 {
     if (!m || m->nseq != 1) return -1;
     return dsv4b_model_generate_batch(m, prompt, n_prompt, n_gen, out);
+}
+
+extern "C" int dsv4b_model_prefill(dsv4b_model *m, const int *prompt, int n_prompt, int chunk)
+{
+    if (!m || m->nseq != 1 || m->world != 1 || chunk < 1 || chunk > m->cap || !dsv4b::hc_fused(m->c)) return -1;
+    if (dsv4b_model_begin_batch(m, prompt, n_prompt) != 0) return -1;
+    // every prompt token's step state; pass p0 copies its slice
+    std::vector<dsv4b::StepState> s(n_prompt);
+    for (int i = 0; i < n_prompt; i++) s[i] = { prompt[i], i };
+    int kernels = 0;
+    for (int p0 = 0; p0 < n_prompt; p0 += chunk) {
+        const int nt = std::min(chunk, n_prompt - p0);
+        const bool last = p0 + nt >= n_prompt;
+        DSV4B_CUDA_OK(cudaMemcpyAsync(m->pst, s.data() + p0, (size_t)nt * sizeof(dsv4b::StepState),
+                                      cudaMemcpyHostToDevice, m->stream));
+        // the head of the last pass advances the decode state from the last
+        // prompt position, as a per-token run's last prompt step does
+        if (last)
+            DSV4B_CUDA_OK(cudaMemcpyAsync(m->st, s.data() + n_prompt - 1, sizeof(dsv4b::StepState),
+                                          cudaMemcpyHostToDevice, m->stream));
+        const int k = run_pass(m, nt, last);
+        if (k == -2) return -1;
+        kernels = (kernels < 0 || k < 0) ? -1 : kernels + k;
+    }
+    m->pf_kernels = kernels;
+    int tok = -1;
+    DSV4B_CUDA_OK(cudaMemcpyAsync(&tok, m->out_tokens + n_prompt - 1, 4, cudaMemcpyDeviceToHost, m->stream));
+    DSV4B_CUDA_OK(cudaStreamSynchronize(m->stream));
+    return tok;
+}
+
+extern "C" int dsv4b_model_generate_prefill(dsv4b_model *m, const int *prompt, int n_prompt, int n_gen, int chunk,
+                                            int *out)
+{
+    if (!m || !prompt || !out || n_prompt < 1 || n_gen < 0 || n_prompt + n_gen > m->max_pos) return -1;
+    if (dsv4b_model_prefill(m, prompt, n_prompt, chunk) < 0) return -1;
+    for (int i = 0; i < n_gen; i++) DSV4B_CUDA_OK(cudaGraphLaunch(m->exec, m->stream));
+    DSV4B_CUDA_OK(cudaMemcpyAsync(out, m->out_tokens + n_prompt - 1, (size_t)(n_gen + 1) * 4, cudaMemcpyDeviceToHost,
+                                  m->stream));
+    DSV4B_CUDA_OK(cudaStreamSynchronize(m->stream));
+    return n_gen + 1;
 }
 
 // ------------------------------------------------------- synthetic models
@@ -1080,18 +1225,12 @@ extern "C" int dsv4b_model_decode_batch(dsv4b_model *m, const int *tokens, int p
 extern "C" int dsv4_cuda_model_step_kernels(const dsv4b_model *m)
 {
     if (!m || !m->graphed) return -1;
-    size_t n = 0;
-    if (cudaGraphGetNodes(m->graph, nullptr, &n) != cudaSuccess) return -1;
-    std::vector<cudaGraphNode_t> nodes(n);
-    if (n && cudaGraphGetNodes(m->graph, nodes.data(), &n) != cudaSuccess) return -1;
-    int k = 0;
-    for (size_t i = 0; i < n; i++) {
-        cudaGraphNodeType t;
-        if (cudaGraphNodeGetType(nodes[i], &t) != cudaSuccess) return -1;
-        k += t == cudaGraphNodeTypeKernel;
-    }
-    return k;
+    return graph_kernels(m->graph);
 }
+
+extern "C" int dsv4b_model_prefill_kernels(const dsv4b_model *m) { return m ? m->pf_kernels : -1; }
+
+extern "C" void *dsv4b_model_stream(const dsv4b_model *m) { return m ? (void *)m->stream : nullptr; }
 
 extern "C" size_t dsv4_cuda_model_bytes(const dsv4b_model *m)
 {

@@ -8,6 +8,7 @@
 
 #define DSV4B_MAX_HC 8
 #define DSV4B_MAX_SEQ 64     // sequences of a batched model
+#define DSV4B_MAX_PREFILL 64 // tokens of one prefill pass (a one-sequence model)
 
 namespace dsv4b {
 

@@ -88,6 +88,10 @@ def _declare(L):
         "dsv4b_model_begin_batch": ([vp, vp, i], i),
         "dsv4b_model_generate_batch": ([vp, vp, i, i, vp], i),
         "dsv4b_model_decode_batch": ([vp, vp, i, vp], i),
+        "dsv4b_model_prefill": ([vp, vp, i, i], i),
+        "dsv4b_model_generate_prefill": ([vp, vp, i, i, i, vp], i),
+        "dsv4b_model_prefill_kernels": ([vp], i),
+        "dsv4b_model_stream": ([vp], vp),
         "dsv4_cuda_model_bytes": ([vp], sz),
         "dsv4_cuda_model_step_kernels": ([vp], i),
         "dsv4b_shard_check": ([vp, i], i),
@@ -413,6 +417,24 @@ class Model:
         n = lib().dsv4_cuda_model_generate(self.h, p.ctypes.data, p.size, n_gen, out.ctypes.data)
         if n < 0:
             raise RuntimeError("dsv4_cuda_model_generate failed")
+        return out[:n]
+
+    def prefill(self, prompt, chunk=32):
+        """The prompt in passes of chunk tokens; returns the first generated
+        token. Steps continue from position len(prompt)."""
+        p = np.ascontiguousarray(prompt, np.int32)
+        tok = lib().dsv4b_model_prefill(self.h, p.ctypes.data, p.size, int(chunk))
+        if tok < 0:
+            raise RuntimeError("dsv4b_model_prefill failed")
+        return tok
+
+    def generate_prefill(self, prompt, n_gen, chunk=32):
+        """generate() with the prompt prefilled in passes of chunk tokens."""
+        p = np.ascontiguousarray(prompt, np.int32)
+        out = np.empty(n_gen + 1, np.int32)
+        n = lib().dsv4b_model_generate_prefill(self.h, p.ctypes.data, p.size, n_gen, int(chunk), out.ctypes.data)
+        if n < 0:
+            raise RuntimeError("dsv4b_model_generate_prefill failed")
         return out[:n]
 
     def begin_batch(self, prompts):

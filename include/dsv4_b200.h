@@ -174,6 +174,35 @@ int dsv4_cuda_model_decode(dsv4b_model *m, int token, int pos, int *next_token);
 dsv4b_model *dsv4_cuda_model_create_synthetic(const DSV4Cfg *c, int max_pos,
                                               unsigned long long seed);
 
+/* ---- batched prefill (src/cli/dsv4_run.c:391-442, the --batch prompt
+ * path; dsv4_layer_forward_n, src/model/dsv4_layer.c:856-918): the prompt
+ * of a one-sequence model in passes of up to chunk tokens (1..64; the
+ * reference's default is 32). Within a pass every token-local step (mHC,
+ * every projection, the output projections, the MoE over the union of the
+ * pass's experts) runs over all chunk tokens at once, and the cache-bound
+ * core (q / KV finish, compressor, indexer, top-k, attention) runs token by
+ * token in position order; the head runs once, on the prompt's last token.
+ * Every token's arithmetic is that of a decode step, so the model is left
+ * where dsv4_cuda_model_begin + n_prompt steps leave it: caches filled,
+ * position n_prompt, the first generated token emitted. */
+
+/* begin + the prompt in passes; returns the first generated token (the
+ * argmax at position n_prompt - 1), or -1 (a batched or sharded model, or
+ * chunk out of range). Steps and dsv4b_model_step_async continue from
+ * position n_prompt. */
+int dsv4b_model_prefill(dsv4b_model *m, const int *prompt, int n_prompt, int chunk);
+/* dsv4_cuda_model_generate with the prompt prefilled in passes of chunk:
+ * out receives the same n_gen + 1 tokens. Returns that count, or -1. */
+int dsv4b_model_generate_prefill(dsv4b_model *m, const int *prompt, int n_prompt, int n_gen,
+                                 int chunk, int *out);
+/* The kernels the last prefill launched (each pass shape runs eagerly the
+ * first time it is seen and as a captured graph after that), or -1 when a
+ * pass of it ran eagerly. */
+int dsv4b_model_prefill_kernels(const dsv4b_model *m);
+/* The stream every call of the model enqueues on (a cudaStream_t): for
+ * timing a synchronous call with events, or ordering other work after it. */
+void *dsv4b_model_stream(const dsv4b_model *m);
+
 /* ---- batched decode: n_seq sequences (<= 64) stepped in lockstep by one
  * graph. The reference's batched layer (dsv4_layer_forward_n,
  * src/model/dsv4_layer.c:856-918) runs nt tokens of ONE sequence and keeps

@@ -304,6 +304,26 @@ def model_greedy_ref(sm, tokens, n_gen, max_pos):
     return out[:n], lg[:n]
 
 
+def model_prefill_ref(sm, tokens, n_gen, max_pos, chunk):
+    """The REFERENCE's batched prompt path (oracle/_ref: dsv4_layer_forward_n
+    in passes of chunk tokens, dsv4_run.c:391-442), then its per-token loop:
+    (the n_gen + 1 greedy tokens from the last prompt position on, the
+    seconds of each pass's layer calls, [pass][layer])."""
+    lib = C.CDLL(REF_SO)
+    f = lib.dsv4ref_prefill_greedy
+    f.argtypes = [_vp, _vp, _vp, _vp, _i, _i32p, _i, _i, _i, _i32p,
+                  np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")]
+    f.restype = _i
+    toks = np.ascontiguousarray(tokens, np.int32)
+    out = np.empty(n_gen + 1, np.int32)
+    tp = np.zeros((-(-toks.size // chunk), sm.d["n_layers"]), np.float64)
+    n = f(C.addressof(sm.cfg), C.addressof(sm.mw), C.addressof(sm.layers), C.addressof(sm.experts),
+          max_pos, toks, toks.size, n_gen, int(chunk), out, tp)
+    if n < 0:
+        raise RuntimeError("reference driver failed")
+    return out[:n], tp
+
+
 class BoundCheckpoint:
     """A checkpoint directory bound by the REFERENCE's own reader and binder
     (oracle/_ref: dsv4_st_open, dsv4_bind_model, dsv4_bind_layer, experts by

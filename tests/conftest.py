@@ -26,6 +26,15 @@ def golden():
 
 
 @pytest.fixture(scope="session")
+def flash_sample():
+    """The benchmark's CPU-baseline sample (three Flash layers, all 256
+    experts, the 129280-token head) as host weights, built once per session
+    (minutes of host work)."""
+    import dsv4_model as M
+    return M.SyntheticModel(M.flash_sample_config(), seed=0, fast=True)
+
+
+@pytest.fixture(scope="session")
 def port():
     import oracle
     return oracle.Checker("port")

@@ -75,7 +75,7 @@ def test_flash_slice_batch8_matches_single():
     m1.close()
 
 
-def test_flash_sample_batch_against_reference():
+def test_flash_sample_batch_against_reference(flash_sample):
     """The benchmark's CPU-baseline sample (three Flash layers, all 256
     experts, the 129280-token head), three sequences: sequence 0 is the
     reference's token loop's (oracle/_ref) for its prompt, the others the
@@ -83,7 +83,7 @@ def test_flash_sample_batch_against_reference():
     import oracle as O
     assert os.path.exists(O.REF_SO), "oracle/_ref/libdsv4ref.so is built with the package"
     B.init()
-    sm = M.SyntheticModel(M.flash_sample_config(), seed=0, fast=True)
+    sm = flash_sample
     first = np.random.default_rng(11).integers(0, sm.d["vocab"], 16).astype(np.int32)
     prompts = _prompts(first, 3, sm.d["vocab"], 12)
     mb = B.Model(sm, 64, n_seq=3)

@@ -107,7 +107,7 @@ def test_synthetic_on_device_model_runs():
     b.close()
 
 
-def test_flash_sample_against_reference():
+def test_flash_sample_against_reference(flash_sample):
     """The benchmark's CPU-baseline sample -- three Flash-geometry layers
     (compress ratios 0 / 4 / 128), all 256 FP4 experts, the 129280-token
     head -- decoded on the GPU from a 16-token prompt for 16 greedy tokens:
@@ -116,7 +116,7 @@ def test_flash_sample_against_reference():
     import oracle as O
     assert os.path.exists(O.REF_SO), "oracle/_ref/libdsv4ref.so is built with the package"
     B.init()
-    sm = M.SyntheticModel(M.flash_sample_config(), seed=0, fast=True)
+    sm = flash_sample
     prompt = np.random.default_rng(11).integers(0, sm.d["vocab"], 16).astype(np.int32)
     m = B.Model(sm, 64)
     out = m.generate(prompt, 16)

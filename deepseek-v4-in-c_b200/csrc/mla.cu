@@ -77,13 +77,17 @@ template <int KDT, int PPL>
 __global__ void __launch_bounds__(256)
 k_indexer_score(float *out, const float *q, const void *keys, long key_stride,
                 long seq_key_stride, const float *w, int n_heads, int head_dim, int n_pos,
-                float scale, long seq_q_stride, long seq_out_stride, const int *dyn_n, int batch)
+                float scale, long seq_q_stride, long seq_out_stride, const int *dyn_n, int batch, int dyn_stride)
 {
     constexpr int TP = 32 * PPL, KS = TP + 2;       // tile positions, key-row stride (doubles)
     constexpr int KR = 4 * PPL;                     // key float4 groups per thread per tile (head_dim <= 128)
     pdl_trigger();
     pdl_wait();
-    if (dyn_n) n_pos = min(n_pos, *dyn_n);       // rows that exist this step
+    // rows that exist this step: one count for every sequence, or (a
+    // dyn_stride) sequence b's at dyn_n[b * dyn_stride], tiles cut for the most
+    const int n_launch = n_pos;
+    if (dyn_n && !dyn_stride) n_pos = min(n_pos, *dyn_n);
+    auto n_of = [&](int b) { return (dyn_n && dyn_stride) ? min(n_launch, dyn_n[(size_t)b * dyn_stride]) : n_pos; };
     extern __shared__ double ixs[];
     double *qt = ixs;                               // [head_dim][n_heads]
     double *kt = qt + (size_t)head_dim * n_heads;   // [head_dim][KS]
@@ -94,15 +98,15 @@ k_indexer_score(float *out, const float *q, const void *keys, long key_stride,
     // this thread's key groups of a tile: position p = (tid >> 3) + 32 r,
     // group g = (tid & 7) + 8 u (r < PPL, u < 4)
     auto load_keys = [&](int t, float4 (&v)[KR]) {
-        const int b = t / tiles, t0 = (t - b * tiles) * TP;
+        const int b = t / tiles, t0 = (t - b * tiles) * TP, nb = n_of(b);
         const char *kb = reinterpret_cast<const char *>(keys) + (size_t)b * seq_key_stride * dt_bytes<KDT>;
 #pragma unroll
         for (int r = 0; r < PPL; r++)
 #pragma unroll
             for (int u = 0; u < 4; u++) {
                 const int p = (tid >> 3) + 32 * r, g = (tid & 7) + 8 * u;
-                v[r * 4 + u] = (t0 + p < n_pos && g < nd4) ? load4_t<KDT>(kb, (size_t)(t0 + p) * key_stride + 4 * g)
-                                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+                v[r * 4 + u] = (t0 + p < nb && g < nd4) ? load4_t<KDT>(kb, (size_t)(t0 + p) * key_stride + 4 * g)
+                                                         : make_float4(0.f, 0.f, 0.f, 0.f);
             }
     };
     float4 kv4[KR];
@@ -194,8 +198,9 @@ k_indexer_score(float *out, const float *q, const void *keys, long key_stride,
                     if (h0 + j < n_heads) dots[(PPL * lane + r) * (n_heads + 1) + h0 + j] = acc[r][j];
         }
         __syncthreads();
+        const int nb = n_of(b);
         for (int p = tid; p < TP; p += blockDim.x) {
-            if (t0 + p >= n_pos) break;
+            if (t0 + p >= nb) break;
             double total_s = 0.0;
             for (int h = 0; h < n_heads; h++) {
                 const double d = dots[p * (n_heads + 1) + h];
@@ -221,12 +226,13 @@ template <int KDT>
 __global__ void __launch_bounds__(256)
 k_indexer_split(float *out, const float *q, const void *keys, long key_stride, long seq_key_stride, const float *w,
                 int n_heads, int head_dim, int n_pos, float scale, long seq_q_stride, long seq_out_stride,
-                const int *dyn_n, double *terms, unsigned *count)
+                const int *dyn_n, double *terms, unsigned *count, int dyn_stride)
 {
     pdl_trigger();
     pdl_wait();
     const int n_alloc = n_pos;                      // the terms' per-sequence stride
-    if (dyn_n) n_pos = min(n_pos, *dyn_n);
+    // rows that exist this step (sequence blockIdx.z's with a dyn_stride)
+    if (dyn_n) n_pos = min(n_pos, dyn_n[(size_t)blockIdx.z * dyn_stride]);
     if ((int)blockIdx.x * IX_TP >= n_pos) return;
     extern __shared__ double ixs[];
     double *qs = ixs;                               // [IX_HS][head_dim]
@@ -312,11 +318,15 @@ __device__ __forceinline__ uint32_t fkey(float v)
 // descending order, ties to the lower index. n <= kTopkMaxN, k <= kTopkMaxK.
 __global__ void __launch_bounds__(1024)
 k_topk(int *idx_out, const float *scores, int n, int k, long seq_in_stride, long seq_out_stride,
-       const int *dyn_nk)
+       const int *dyn_nk, int dyn_stride)
 {
     pdl_trigger();
     pdl_wait();
-    if (dyn_nk) { n = min(n, dyn_nk[0]); k = dyn_nk[1]; }
+    if (dyn_nk) {                                   // sequence blockIdx.y's {n, k} with a dyn_stride
+        const int *dk = dyn_nk + (size_t)blockIdx.y * dyn_stride;
+        n = min(n, dk[0]);
+        k = dk[1];
+    }
     extern __shared__ uint32_t tks[];
     uint32_t *key = tks;                                   // [n]
     int *eqi = reinterpret_cast<int *>(key + ((n + 1) & ~1));   // [kTopkEqCap] indices == the k-th key
@@ -764,7 +774,7 @@ k_attn_combine(float *o, AttnPart part, const float *sink, int nch, int n_heads,
     }
     if (rope.cs) {          // de-rotate this block's part of the tail (src/model/dsv4_layer.c:303-305)
         __syncthreads();
-        const int half = rope.rd / 2, pos = __ldcg(rope.pos), t0 = d - rope.rd;
+        const int half = rope.rd / 2, pos = __ldcg(rope.pos + (size_t)b * rope.pos_stride), t0 = d - rope.rd;
         for (int i = tid; i < half; i += blockDim.x) {
             const int e0 = t0 + 2 * i;
             if (e0 < cb0 || e0 >= cb0 + 128) continue;
@@ -780,7 +790,7 @@ k_attn_combine(float *o, AttnPart part, const float *sink, int nch, int n_heads,
 
 int indexer_score(float *out, const float *q, const void *keys, int key_dt, long key_stride,
                   long seq_key_stride, const float *w, int n_heads, int head_dim, int n_pos, float scale,
-                  int batch, cudaStream_t st, const int *dyn_n, double *terms, unsigned *count)
+                  int batch, cudaStream_t st, const int *dyn_n, double *terms, unsigned *count, int dyn_stride)
 {
     if (n_pos <= 0 || batch <= 0) return 0;
     if (terms && count && n_heads % IX_HS == 0 && head_dim % 4 == 0 && (key_stride & 3) == 0 &&
@@ -797,13 +807,16 @@ int indexer_score(float *out, const float *q, const void *keys, int key_dt, long
             const long sq = (long)n_heads * head_dim;
             if (key_dt == DSV4B_DT_F32)
                 launch(k_indexer_split<DSV4B_DT_F32>, grid, dim3(256), sm, st, out, q, keys, key_stride,
-                       seq_key_stride, w, n_heads, head_dim, n_pos, scale, sq, (long)n_pos, dyn_n, terms, count);
+                       seq_key_stride, w, n_heads, head_dim, n_pos, scale, sq, (long)n_pos, dyn_n, terms, count,
+                       dyn_stride);
             else if (key_dt == DSV4B_DT_BF16)
                 launch(k_indexer_split<DSV4B_DT_BF16>, grid, dim3(256), sm, st, out, q, keys, key_stride,
-                       seq_key_stride, w, n_heads, head_dim, n_pos, scale, sq, (long)n_pos, dyn_n, terms, count);
+                       seq_key_stride, w, n_heads, head_dim, n_pos, scale, sq, (long)n_pos, dyn_n, terms, count,
+                       dyn_stride);
             else
                 launch(k_indexer_split<DSV4B_DT_E4M3>, grid, dim3(256), sm, st, out, q, keys, key_stride,
-                       seq_key_stride, w, n_heads, head_dim, n_pos, scale, sq, (long)n_pos, dyn_n, terms, count);
+                       seq_key_stride, w, n_heads, head_dim, n_pos, scale, sq, (long)n_pos, dyn_n, terms, count,
+                       dyn_stride);
             return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
         }
     }
@@ -832,7 +845,7 @@ int indexer_score(float *out, const float *q, const void *keys, int key_dt, long
     do {                                                                                                         \
         if (smem_optin(k_indexer_score<KDT, PPL>, 200 * 1024)) return -1;                                        \
         launch(k_indexer_score<KDT, PPL>, grid, dim3(256), smem, st, out, q, keys, key_stride, seq_key_stride, w, \
-               n_heads, head_dim, n_pos, scale, sq, n_pos, dyn_n, batch);                                        \
+               n_heads, head_dim, n_pos, scale, sq, n_pos, dyn_n, batch, dyn_stride);                            \
     } while (0)
     if (key_dt == DSV4B_DT_F32) {
         if (ppl == 2) DSV4B_IX_LAUNCH(DSV4B_DT_F32, 2); else DSV4B_IX_LAUNCH(DSV4B_DT_F32, 1);
@@ -846,7 +859,7 @@ int indexer_score(float *out, const float *q, const void *keys, int key_dt, long
 }
 
 int topk(int *idx, const float *scores, int n, int k, int batch, long seq_in_stride, long seq_out_stride,
-         cudaStream_t st, const int *dyn_nk)
+         cudaStream_t st, const int *dyn_nk, int dyn_stride)
 {
     if (batch <= 0 || n <= 0 || k <= 0) return 0;
     if (n > kTopkMaxN || k > kTopkMaxK) return -1;
@@ -855,7 +868,8 @@ int topk(int *idx, const float *scores, int n, int k, int batch, long seq_in_str
     const size_t smem = (size_t)((n + 1) & ~1) * 4 + (size_t)kTopkEqCap * 4 + (size_t)kp * 8;
     if (smem > 220 * 1024) return -1;
     if (smem_optin(k_topk, 220 * 1024)) return -1;
-    launch(k_topk, dim3(dim3(1, batch)), dim3(1024), smem, st, idx, scores, n, k, seq_in_stride, seq_out_stride, dyn_nk);
+    launch(k_topk, dim3(dim3(1, batch)), dim3(1024), smem, st, idx, scores, n, k, seq_in_stride, seq_out_stride, dyn_nk,
+           dyn_stride);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -33,7 +33,10 @@ struct DevLayer {
     MoeLayer moe;
     float *kv_cache, *comp_kv, *comp_score;
     int *dyn;
+    // cache rows: the window ring, the compressed rows, then (a one-sequence
+    // model) a prefill pass's staging rows from stage_row
     size_t kv_rows, comp_n;
+    int stage_row;
 };
 
 }  // namespace dsv4b
@@ -77,6 +80,8 @@ struct dsv4b_model {
     // prefill pass (pst holds their step states)
     int cap;
     dsv4b::StepState *pst;
+    int *pdyn;                 // a prefill pass's per-token compressed-row counts (2 ints each)
+    int ix_rows;               // rows of the indexer's head-split scratch (ix_terms / ix_count)
     // prefill passes as graphs, one per (tokens, last) shape: a shape runs
     // eagerly the first time (which also sets every kernel attribute), is
     // captured the second, replayed after; pf_kernels counts the kernels the
@@ -222,10 +227,17 @@ static bool alloc_common(dsv4b_model *m)
     m->comp_sc = F(R * 2 * hd);
     m->idx_q = F(R * c.index_n_heads * c.index_head_dim);
     m->idx_w = F(R * c.index_n_heads);
-    m->idx_scores = F(B * m->ncomp4);
-    m->ix_terms = (double *)dcopy(m, nullptr, B * m->ncomp4 * c.index_n_heads * 8, &ok);
-    m->ix_count = (unsigned *)dcopy(m, nullptr, B * ((m->ncomp4 + 31) / 32) * 4, &ok);
-    if (ok && cudaMemset(m->ix_count, 0, B * ((m->ncomp4 + 31) / 32) * 4) != cudaSuccess) ok = false;
+    m->idx_scores = F(R * m->ncomp4);
+    // the head-split indexer's terms for up to R rows, within 256 MB (a
+    // prefill pass scores its tokens in groups of ix_rows)
+    const size_t ix_row = (size_t)m->ncomp4 * c.index_n_heads * 8;
+    size_t ixr = (256u << 20) / (ix_row ? ix_row : 1);
+    ixr = ixr < B ? B : (ixr > R ? R : ixr);
+    m->ix_rows = (int)ixr;
+    m->ix_terms = (double *)dcopy(m, nullptr, ixr * ix_row, &ok);
+    m->ix_count = (unsigned *)dcopy(m, nullptr, ixr * ((m->ncomp4 + 31) / 32) * 4, &ok);
+    if (ok && cudaMemset(m->ix_count, 0, ixr * ((m->ncomp4 + 31) / 32) * 4) != cudaSuccess) ok = false;
+    m->pdyn = (int *)dcopy(m, nullptr, R * 2 * 4, &ok);
     m->logits = F(B * c.vocab);
     m->xh = F(R * d);
     m->am_pv = F(B * kArgmaxParts);
@@ -236,12 +248,12 @@ static bool alloc_common(dsv4b_model *m)
     m->am_gather = F(2 * 64);
     m->am_pi = (int *)dcopy(m, nullptr, B * kArgmaxParts * 4, &ok);
     m->idxs = (int *)dcopy(m, nullptr, R * m->nidx * 4, &ok);
-    m->isel = (int *)dcopy(m, nullptr, B * (c.index_topk > 0 ? c.index_topk : 1) * 4, &ok);
+    m->isel = (int *)dcopy(m, nullptr, R * (c.index_topk > 0 ? c.index_topk : 1) * 4, &ok);
     m->prompt = (int *)dcopy(m, nullptr, B * m->max_pos * 4, &ok);
     m->out_tokens = (int *)dcopy(m, nullptr, B * m->max_pos * 4, &ok);
     m->st = (StepState *)dcopy(m, nullptr, B * sizeof(StepState), &ok);
     m->pst = (StepState *)dcopy(m, nullptr, R * sizeof(StepState), &ok);
-    m->attn_part = dcopy(m, nullptr, attn_part_bytes(c.n_heads, hd, m->nidx, (int)B), &ok);
+    m->attn_part = dcopy(m, nullptr, attn_part_bytes(c.n_heads, hd, m->nidx, (int)R), &ok);
     m->hc_part = (double *)dcopy(m, nullptr, R * kHcPreBlocks * (kHcPreMixMax + 1) * 8, &ok);
     m->hc_cnt = (unsigned *)dcopy(m, nullptr, R * 4, &ok);
     if (ok && cudaMemset(m->hc_cnt, 0, R * 4) != cudaSuccess) ok = false;
@@ -251,12 +263,16 @@ static bool alloc_common(dsv4b_model *m)
     m->moe_perm = (int *)dcopy(m, nullptr, R * kMoeMaxTopk * 5 * 4, &ok);
     float *msb = F(R * m->s_ms);
     if (ok) moe_scratch_carve(m->ms, msb, d, c.moe_inter, inter_s, c.n_experts, c.topk);
+    // a one-sequence model's prefill pass writes its KV rows to staging rows
+    // at the end of each cache (the ring is read by the pass's own tokens)
+    const size_t stage = (m->nseq == 1 && R > 1) ? R : 0;
     for (int L = 0; L < c.n_layers && ok; L++) {
         DevLayer &l = m->L[L];
         l.ratio = m->ratios[L];
         l.coff = l.ratio == 4 ? 2 : 1;
         const size_t ncomp = l.ratio ? (size_t)(m->max_pos / l.ratio + 1) : 0;
-        l.kv_rows = (size_t)win + ncomp;
+        l.stage_row = (int)(win + ncomp);
+        l.kv_rows = (size_t)win + ncomp + stage;
         l.kv_cache = F(B * l.kv_rows * hd);
         l.comp_n = l.ratio ? (size_t)l.coff * l.ratio * l.coff * hd : 0;
         l.comp_kv = l.comp_n ? F(B * l.comp_n) : nullptr;
@@ -412,36 +428,45 @@ static void hc_step(dsv4b_model *m, Pending &p, float *&hin, float *&hout, const
 
 // The cache-bound work of one layer's attention (src/model/dsv4_layer.c:224-301):
 // the q heads, the KV row and the compressor step, the indexer's scores and
-// top-k (or the full row list), then attention over the attended rows. It
-// covers n activation rows from row r0: in a decode step the batch's
-// sequences (r0 = 0, row y is sequence y, with its own cache); in a prefill
-// pass one token (n = 1) of sequence 0, whose step state is sts.
-static int attn_core(dsv4b_model *m, DevLayer &l, int r0, int n, const StepState *sts, cudaStream_t st)
+// top-k (or the full row list), then attention over the attended rows, for n
+// activation rows whose step states are sts. A decode step: row y is
+// sequence y, with its own cache. A prefill pass (pass set): row t is token t
+// of sequence 0, all on one cache; each token must see the window as it
+// stood at its own position, so the pass's KV rows go to staging rows (the
+// ring keeps the positions before the pass), the compressor steps through the
+// tokens in order inside one block, every token's row list points at the
+// staging rows for positions in the pass, and the ring takes the staging rows
+// at the end. Every token's arithmetic is that of its decode step.
+static int attn_core(dsv4b_model *m, DevLayer &l, int n, const StepState *sts, bool pass, cudaStream_t st)
 {
     const DSV4Cfg &c = m->c;
     const int hd = c.head_dim, rd = c.qk_rope, H = c.n_heads / m->world, win = c.sliding_window;
     const int ih = c.index_n_heads, id = c.index_head_dim;
     const float *cs = l.ratio ? m->cs_c : m->cs_d, *sn = l.ratio ? m->sn_c : m->sn_d;
     int rc = 0;
+    // token t's compressed-row counts {avail, take}: the layer's pair (every
+    // sequence of a decode step stands at the same position) or the pass's
+    int *dyn = pass ? m->pdyn : l.dyn;
+    const int dstride = pass ? 2 : 0, stage = pass ? l.stage_row : -1;
     // q heads, the KV row, the compressor, the indexer's q heads (or the
     // attended row list) in one launch (dsv4_layer.c:224-295)
     PrepArgs pa = {};
-    pa.q = m->q + (size_t)r0 * H * hd;
-    pa.kv = m->kv + (size_t)r0 * hd;
+    pa.q = m->q;
+    pa.kv = m->kv;
     pa.cache = l.kv_cache;
     pa.comp_kv = l.comp_kv;
     pa.comp_score = l.comp_score;
-    pa.idx_q = m->idx_q + (size_t)r0 * ih * id;
+    pa.idx_q = m->idx_q;
     pa.kv_norm = l.kv_norm;
-    pa.comp_in = m->comp_in + (size_t)r0 * 2 * hd;
-    pa.comp_sc = m->comp_sc + (size_t)r0 * 2 * hd;
+    pa.comp_in = m->comp_in;
+    pa.comp_sc = m->comp_sc;
     pa.ape = l.ape;
     pa.cnorm = l.cnorm;
     pa.cs = cs;
     pa.sn = sn;
     pa.st = sts;
-    pa.dyn = l.dyn;
-    pa.idxs = m->idxs + (size_t)r0 * m->nidx;
+    pa.dyn = dyn;
+    pa.idxs = m->idxs;
     pa.H = H;
     pa.hd = hd;
     pa.rd = rd;
@@ -454,25 +479,33 @@ static int attn_core(dsv4b_model *m, DevLayer &l, int r0, int n, const StepState
     pa.id = id;
     pa.nidx = m->nidx;
     pa.eps = c.rms_eps;
-    pa.s_cache = (long)(l.kv_rows * hd);
-    pa.s_comp = (long)l.comp_n;
+    pa.s_cache = pass ? 0 : (long)(l.kv_rows * hd);
+    pa.s_comp = pass ? 0 : (long)l.comp_n;
+    pa.stage = stage;
+    pa.pass_nt = pass ? n : 0;
     const int blocks = H + 1 + (pa.has_comp ? 1 : 0) + (pa.has_idx ? ih : 1);
     launch(k_attn_prep, dim3(blocks, n), dim3(256), (size_t)hd * 4, st, pa);
     if (l.has_comp && l.has_idx) {
         const float scale = (1.0f / sqrtf((float)id)) * (1.0f / sqrtf((float)ih));
         // the compressed region read as contiguous rows of index_head_dim
-        // floats, as the reference does (dsv4_layer.c:286-289)
-        rc |= indexer_score(m->idx_scores, pa.idx_q, l.kv_cache + (size_t)win * hd, DSV4B_DT_F32, id,
-                            (long)(l.kv_rows * hd), m->idx_w + (size_t)r0 * ih, ih, id, m->ncomp4, scale, n, st,
-                            l.dyn, m->ix_terms, m->ix_count);
-        rc |= topk(m->isel, m->idx_scores, m->ncomp4, c.index_topk, n, m->ncomp4, c.index_topk, st, l.dyn);
-        launch(k_build_idxs, dim3(n), dim3(256), 0, st, pa.idxs, m->nidx, sts, win, l.has_comp, l.has_idx, l.dyn,
-               m->isel, c.index_topk);
+        // floats, as the reference does (dsv4_layer.c:286-289); a pass's
+        // tokens share it, in groups the head-split scratch holds
+        for (int b0 = 0; b0 < n; b0 += m->ix_rows) {
+            const int nb = n - b0 < m->ix_rows ? n - b0 : m->ix_rows;
+            rc |= indexer_score(m->idx_scores + (size_t)b0 * m->ncomp4, m->idx_q + (size_t)b0 * ih * id,
+                                l.kv_cache + (size_t)win * hd, DSV4B_DT_F32, id, pass ? 0 : (long)(l.kv_rows * hd),
+                                m->idx_w + (size_t)b0 * ih, ih, id, m->ncomp4, scale, nb, st, dyn + b0 * dstride,
+                                m->ix_terms, m->ix_count, dstride);
+        }
+        rc |= topk(m->isel, m->idx_scores, m->ncomp4, c.index_topk, n, m->ncomp4, c.index_topk, st, dyn, dstride);
+        launch(k_build_idxs, dim3(n), dim3(256), 0, st, m->idxs, m->nidx, sts, win, l.has_comp, l.has_idx,
+               (const int *)dyn, (const int *)m->isel, c.index_topk, dstride, stage);
     }
     // attention, each head de-rotated by the kernel that writes it
-    const AttnRope rope = {cs, sn, &sts->pos, rd};
-    rc |= sparse_attn(m->o + (size_t)r0 * H * hd, pa.q, l.kv_cache, DSV4B_DT_F32, (long)l.kv_rows, l.sink, pa.idxs,
-                      m->nidx, H, hd, m->nidx, 1.0f / sqrtf((float)hd), n, m->attn_part, st, &rope);
+    const AttnRope rope = {cs, sn, &sts->pos, rd, pass ? (int)(sizeof(StepState) / sizeof(int)) : 0};
+    rc |= sparse_attn(m->o, m->q, l.kv_cache, DSV4B_DT_F32, pass ? 0 : (long)l.kv_rows, l.sink, m->idxs, m->nidx, H,
+                      hd, m->nidx, 1.0f / sqrtf((float)hd), n, m->attn_part, st, &rope);
+    if (pass) launch(k_stage_commit, dim3(n), dim3(128), 0, st, l.kv_cache, stage, win, hd, sts, n);
     return rc;
 }
 
@@ -480,9 +513,8 @@ static int attn_core(dsv4b_model *m, DevLayer &l, int r0, int n, const StepState
 // A decode step (rows = 0): one token of each of the nseq sequences, their
 // step states at m->st. A prefill pass (rows >= 1, dsv4_layer_forward_n,
 // src/model/dsv4_layer.c:856-918): rows consecutive prompt tokens of
-// sequence 0, their step states at m->pst; every token-local step (mHC,
-// projections, output projections, MoE) runs over all rows at once, the
-// cache-bound core token by token in position order, and the head runs only
+// sequence 0, their step states at m->pst; every step runs over all rows at
+// once (the cache-bound core as attn_core describes), and the head runs only
 // when head is set, on the last row, advancing m->st (which then holds that
 // row's position).
 static int enqueue_pass(dsv4b_model *m, cudaStream_t st, int rows, bool head)
@@ -528,13 +560,8 @@ static int enqueue_pass(dsv4b_model *m, cudaStream_t st, int rows, bool head)
             if (l.has_idx) grp_add(gb, l.iwq_b, m->qr, m->idx_q, st, B, ql, (long)ih * id);
             rc |= grp_run(gb, st);
         }
-        // the cache-bound core: all sequences at once, or a pass's tokens
-        // strictly in position order (token t must find the window ring and
-        // the compressor as they stood at its own position)
-        if (!prefill)
-            rc |= attn_core(m, l, 0, B, sts, st);
-        else
-            for (int t = 0; t < B; t++) rc |= attn_core(m, l, t, 1, sts + t, st);
+        // the cache-bound core, over all sequences or all of the pass's tokens
+        rc |= attn_core(m, l, B, sts, prefill, st);
         // grouped low-rank output (dsv4_layer.c:303-335): the o_groups row
         // slices of wo_a, each on its own slice of o, in one launch (sharded:
         // this rank's heads are exactly its groups' slices of o)

@@ -7,6 +7,8 @@
 // position. Each kernel restates its reference function (cited) with the same
 // operation order; reductions over a vector are block-wide in double where the
 // reference sums in double.
+#include <limits.h>
+
 #include "common.cuh"
 #include "model.h"
 
@@ -537,8 +539,10 @@ __device__ void head_norm_rope(float *h, int width, int rd, const float *cs, con
 
 // The new KV row: weighted RMSNorm, RoPE at pos, into its window slot
 // (src/model/dsv4_layer.c:233-238). The whole block.
+// dst: the cache row the finished KV row goes to (its window ring slot, or
+// a prefill pass's staging row).
 __device__ void kv_finish(float *kv, const float *w, int hd, int rd, const float *cs, const float *sn, int pos,
-                          float eps, float *cache, int win, double *red)
+                          float eps, float *dst, double *red)
 {
     double s = 0.0;
     for (int i = threadIdx.x; i < hd; i += blockDim.x) s = __fma_rn((double)kv[i], (double)kv[i], s);
@@ -548,7 +552,6 @@ __device__ void kv_finish(float *kv, const float *w, int hd, int rd, const float
     __syncthreads();
     rope_tail(kv, hd, rd, cs, sn, pos, 0);
     __syncthreads();
-    float *dst = cache + (size_t)(pos % win) * hd;
     for (int i = threadIdx.x; i < hd; i += blockDim.x) dst[i] = kv[i];
 }
 
@@ -622,15 +625,17 @@ __device__ void compress_step(float *cache, float *kv_state, float *score_state,
 // The attended rows of one token (src/model/dsv4_layer.c:504 and :295): the
 // window newest first, then the compressed rows -- the indexer's selection
 // (sel) on indexer layers, else all (pos + 1) / ratio of them -- in cache
-// coordinates; -1 past the end.
+// coordinates; -1 past the end. In a prefill pass whose first position is p0
+// the window positions from p0 on are in staging rows (position q at row
+// stage + q - p0), the older ones in the ring (p0 = INT_MAX: ring only).
 __device__ void build_idxs(int *idxs, int nmax, int pos, int win, int has_comp, int has_idx, int take,
-                           const int *sel)
+                           const int *sel, int p0, int stage)
 {
     const int n = (pos + 1 < win) ? pos + 1 : win;
     if (!has_comp) take = 0;
     for (int i = threadIdx.x; i < nmax; i += blockDim.x) {
         int v = -1;
-        if (i < n) v = (pos - i) % win;
+        if (i < n) v = (pos - i >= p0) ? stage + (pos - i - p0) : (pos - i) % win;
         else if (i < n + take) v = (has_idx ? __ldcg(sel + i - n) : i - n) + win;
         idxs[i] = v;
     }
@@ -659,6 +664,8 @@ __global__ void __launch_bounds__(256) k_attn_prep(const __grid_constant__ PrepA
     const float *const comp_in = a.comp_in + y * 2 * a.hd, *const comp_sc = a.comp_sc + y * 2 * a.hd;
     int *const idxs = a.idxs + y * a.nidx;
     const int pos = a.st[y].pos;
+    // a prefill pass: the first token's position (its staging rows start there)
+    const int p0 = a.pass_nt ? a.st[0].pos : INT_MAX;
     int b = blockIdx.x;
     if (b < a.H) {
         head_norm_rope(q + (size_t)b * a.hd, a.hd, a.rd, a.cs, a.sn, pos, 0, 1, a.eps, red);
@@ -666,14 +673,27 @@ __global__ void __launch_bounds__(256) k_attn_prep(const __grid_constant__ PrepA
     }
     b -= a.H;
     if (b == 0) {
-        kv_finish(kv, a.kv_norm, a.hd, a.rd, a.cs, a.sn, pos, a.eps, cache, a.win, red);
+        const int row = a.pass_nt ? a.stage + (int)y : pos % a.win;
+        kv_finish(kv, a.kv_norm, a.hd, a.rd, a.cs, a.sn, pos, a.eps, cache + (size_t)row * a.hd, red);
         return;
     }
     b -= 1;
     if (a.has_comp) {
         if (b == 0) {
-            compress_step(cache, comp_kv, comp_score, comp_in, comp_sc, a.ape, a.cnorm, a.ratio, a.hd,
-                          a.rd, a.cs, a.sn, pos, a.eps, a.win, a.index_topk, a.dyn, cbuf, red);
+            if (!a.pass_nt) {
+                compress_step(cache, comp_kv, comp_score, comp_in, comp_sc, a.ape, a.cnorm, a.ratio, a.hd,
+                              a.rd, a.cs, a.sn, pos, a.eps, a.win, a.index_topk, a.dyn, cbuf, red);
+            } else if (y == 0) {
+                // a prefill pass: the compressor is a state machine over
+                // positions, so one block steps it through the pass's tokens in
+                // order; token t's counts go to dyn + 2 t
+                for (int t = 0; t < a.pass_nt; t++) {
+                    compress_step(cache, comp_kv, comp_score, a.comp_in + (size_t)t * 2 * a.hd,
+                                  a.comp_sc + (size_t)t * 2 * a.hd, a.ape, a.cnorm, a.ratio, a.hd, a.rd, a.cs,
+                                  a.sn, a.st[t].pos, a.eps, a.win, a.index_topk, a.dyn + 2 * t, cbuf, red);
+                    __syncthreads();
+                }
+            }
             return;
         }
         b -= 1;
@@ -682,7 +702,9 @@ __global__ void __launch_bounds__(256) k_attn_prep(const __grid_constant__ PrepA
         if (b < a.ih) head_norm_rope(idx_q + (size_t)b * a.id, a.id, a.rd, a.cs, a.sn, pos, 0, 0, a.eps, red);
         return;
     }
-    if (b == 0) build_idxs(idxs, a.nidx, pos, a.win, a.has_comp, 0, a.has_comp ? (pos + 1) / a.ratio : 0, nullptr);
+    if (b == 0)
+        build_idxs(idxs, a.nidx, pos, a.win, a.has_comp, 0, a.has_comp ? (pos + 1) / a.ratio : 0, nullptr, p0,
+                   a.stage);
 }
 
 // The attention index list (src/model/dsv4_layer.c:504-505 and :278-297):
@@ -690,15 +712,32 @@ __global__ void __launch_bounds__(256) k_attn_prep(const __grid_constant__ PrepA
 // first, then the compressed selections (top-k order, or 0..avail-1 without
 // an indexer) offset by win, then -1 up to nmax.
 // One block per sequence of a batch (block b: idxs + b nmax, st[b], sel + b
-// sel_stride).
+// sel_stride, its counts at dyn + b dyn_stride), or per token of a prefill
+// pass (stage >= 0: the pass's window rows in staging rows from stage).
 __global__ void k_build_idxs(int *idxs, int nmax, const StepState *st, int win, int has_comp, int has_idx,
-                             const int *dyn, const int *sel, int sel_stride)
+                             const int *dyn, const int *sel, int sel_stride, int dyn_stride, int stage)
 {
     pdl_trigger();
     pdl_wait();
     const int b = blockIdx.x;
     build_idxs(idxs + (size_t)b * nmax, nmax, st[b].pos, win, has_comp, has_idx,
-               has_comp ? __ldcg(dyn + (has_idx ? 1 : 0)) : 0, sel + (size_t)b * sel_stride);
+               has_comp ? __ldcg(dyn + (size_t)b * dyn_stride + (has_idx ? 1 : 0)) : 0, sel + (size_t)b * sel_stride,
+               stage >= 0 ? st[0].pos : INT_MAX, stage);
+}
+
+// The end of a prefill pass: its KV rows move from the staging rows into the
+// window ring (token t at slot pos_t % win). Only the last min(nt, win)
+// tokens are copied (earlier ones would be overwritten), so no slot is
+// written twice. One block per token.
+__global__ void k_stage_commit(float *cache, int stage, int win, int hd, const StepState *st, int nt)
+{
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.x;
+    if (t < nt - win) return;
+    const float *src = cache + (size_t)(stage + t) * hd;
+    float *dst = cache + (size_t)(st[t].pos % win) * hd;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) dst[i] = src[i];
 }
 
 // Argmax, first maximum (src/cli/dsv4_run.c:472-473), two stages; the second

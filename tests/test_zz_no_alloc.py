@@ -35,6 +35,23 @@ def _case(torch, seed, batch, H, D, N, K):
     return kv, q, sink, idx.cuda()
 
 
+def _settled_free(torch):
+    """The device's free memory once it has stopped changing. The free figure
+    is device-wide: a process that ended just before (the reference's gate
+    runs as a subprocess) can still be returning its memory, which would read
+    as this process's calls changing it. Polled every 0.2 s until two
+    readings agree, for at most 10 s."""
+    import time
+    last = torch.cuda.mem_get_info()[0]
+    for _ in range(50):
+        time.sleep(0.2)
+        now = torch.cuda.mem_get_info()[0]
+        if now == last:
+            break
+        last = now
+    return last
+
+
 @pytest.mark.parametrize("batch,H,D,N,K", [(1, 64, 576, 4096, 640), (2, 64, 512, 2048, 512)])
 def test_static_scratch_matches_caller_scratch(batch, H, D, N, K):
     import torch
@@ -47,7 +64,7 @@ def test_static_scratch_matches_caller_scratch(batch, H, D, N, K):
     cases = [_case(torch, 100 * call + batch, batch, H, D, N, K) for call in range(2)]
     outs = [torch.full((batch, H, D), float("nan"), device="cuda") for _ in range(2)]
     torch.cuda.synchronize()
-    free = [torch.cuda.mem_get_info()[0]]
+    free = [_settled_free(torch)]
     for call in range(2):                                  # two calls in a row, fresh inputs each
         kv, q, sink, idx = cases[call]
         rc = fn(outs[call].data_ptr(), q.data_ptr(), kv.data_ptr(), B.BF16, N, sink.data_ptr(), idx.data_ptr(),

@@ -433,10 +433,12 @@ static void hc_step(dsv4b_model *m, Pending &p, float *&hin, float *&hout, const
 // sequence y, with its own cache. A prefill pass (pass set): row t is token t
 // of sequence 0, all on one cache; each token must see the window as it
 // stood at its own position, so the pass's KV rows go to staging rows (the
-// ring keeps the positions before the pass), the compressor steps through the
-// tokens in order inside one block, every token's row list points at the
-// staging rows for positions in the pass, and the ring takes the staging rows
-// at the end. Every token's arithmetic is that of its decode step.
+// ring keeps the positions before the pass), every token's row list points
+// at the staging rows for positions in the pass, each token that closes a
+// compressor window pools that window from the pass's projection rows and
+// the compressor state as it stood before the pass, and at the end the ring
+// takes the staging rows and the compressor state moves past the pass.
+// Every token's arithmetic is that of its decode step.
 static int attn_core(dsv4b_model *m, DevLayer &l, int n, const StepState *sts, bool pass, cudaStream_t st)
 {
     const DSV4Cfg &c = m->c;
@@ -505,7 +507,7 @@ static int attn_core(dsv4b_model *m, DevLayer &l, int n, const StepState *sts, b
     const AttnRope rope = {cs, sn, &sts->pos, rd, pass ? (int)(sizeof(StepState) / sizeof(int)) : 0};
     rc |= sparse_attn(m->o, m->q, l.kv_cache, DSV4B_DT_F32, pass ? 0 : (long)l.kv_rows, l.sink, m->idxs, m->nidx, H,
                       hd, m->nidx, 1.0f / sqrtf((float)hd), n, m->attn_part, st, &rope);
-    if (pass) launch(k_stage_commit, dim3(n), dim3(128), 0, st, l.kv_cache, stage, win, hd, sts, n);
+    if (pass) launch(k_stage_commit, dim3(n + 1), dim3(256), 0, st, pa);
     return rc;
 }
 

@@ -74,14 +74,15 @@ struct PrepArgs {
     // comp_in / comp_sc (2 hd), idxs (nidx) and st are packed per sequence
     long s_cache, s_comp;
     // a prefill pass (pass_nt > 0, blockIdx.y = token, one cache): token y's
-    // KV row goes to staging row stage + y, the compressor steps through the
-    // pass's tokens in one block (token t's counts at dyn + 2 t)
+    // KV row goes to staging row stage + y, its compressed-row counts to
+    // dyn + 2 y, the compressed row it closes (if any) to the cache; the
+    // compressor state moves past the pass in k_stage_commit
     int stage, pass_nt;
 };
 __global__ void k_attn_prep(const __grid_constant__ PrepArgs a);
 __global__ void k_build_idxs(int *idxs, int nmax, const StepState *st, int win, int has_comp, int has_idx,
                              const int *dyn, const int *sel, int sel_stride, int dyn_stride, int stage);
-__global__ void k_stage_commit(float *cache, int stage, int win, int hd, const StepState *st, int nt);
+__global__ void k_stage_commit(const __grid_constant__ PrepArgs a);
 // argmax partials per sequence (k_argmax_part's blocks, <= kArgmaxParts)
 constexpr int kArgmaxParts = 1024;
 __global__ void k_argmax_part(float *pv, int *pi, const float *x, int n);

@@ -555,6 +555,52 @@ __device__ void kv_finish(float *kv, const float *w, int hd, int rd, const float
     for (int i = threadIdx.x; i < hd; i += blockDim.x) dst[i] = kv[i];
 }
 
+// cbuf[c], c < hd: column c of an emitted compressed row, the softmax over
+// its ns slots in slot order (src/core/dsv4_compress.c), slot s's (value,
+// score) from get(s, c); a -inf score is an empty slot, and an all-empty
+// column is 0.
+template <class Get>
+__device__ __forceinline__ void comp_pool(float *cbuf, int hd, int ns, Get get)
+{
+    for (int c = threadIdx.x; c < hd; c += blockDim.x) {
+        float mx = -INFINITY;
+        for (int s = 0; s < ns; s++) {
+            const float v = get(s, c).y;
+            if (v > mx) mx = v;
+        }
+        float out = 0.0f;
+        if (mx != -INFINITY) {
+            double den = 0.0, acc = 0.0;
+            for (int s = 0; s < ns; s++) {
+                const float2 g = get(s, c);
+                if (g.y == -INFINITY) continue;
+                const double e = (double)expf(g.y - mx);
+                den = __dadd_rn(den, e);
+                acc = __dadd_rn(acc, __dmul_rn(e, (double)g.x));
+            }
+            out = (float)(acc / den);
+        }
+        cbuf[c] = out;
+    }
+}
+
+// The pooled row's RMSNorm (weights norm) and RoPE at the window's first
+// position pos0, written to cache row `row`.
+__device__ void comp_finish(float *cache, float *cbuf, const float *norm, int hd, int rd, const float *cs,
+                            const float *sn, int pos0, float eps, int row, double *red)
+{
+    double s = 0.0;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) s = __fma_rn((double)cbuf[i], (double)cbuf[i], s);
+    s = block_sum_d(s, red);
+    const float inv = (float)(1.0 / sqrt(s / (double)hd + (double)eps));
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) cbuf[i] = __fmul_rn(norm[i], __fmul_rn(cbuf[i], inv));
+    __syncthreads();
+    rope_tail(cbuf, hd, rd, cs, sn, pos0, 0);
+    __syncthreads();
+    float *dst = cache + (size_t)row * hd;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) dst[i] = cbuf[i];
+}
+
 __device__ void compress_step(float *cache, float *kv_state, float *score_state, const float *kv_in,
                               const float *sc_in, const float *ape, const float *norm, int ratio, int hd, int rd,
                               const float *cs, const float *sn, int pos, float eps, int win, int index_topk,
@@ -577,33 +623,13 @@ __device__ void compress_step(float *cache, float *kv_state, float *score_state,
     }
     __syncthreads();
     if ((pos + 1) % ratio != 0) return;
-    const int ns = overlap ? 2 * ratio : ratio;
-    for (int c = threadIdx.x; c < hd; c += blockDim.x) {
-        // slot s of the pool: overlap mode takes the previous window's first
-        // half-width and the current window's second half-width
-        float mx = -INFINITY;
-        for (int s = 0; s < ns; s++) {
-            const size_t off = overlap ? ((s < ratio) ? (size_t)s * width + c : (size_t)s * width + hd + c)
-                                       : (size_t)s * width + c;
-            const float v = score_state[off];
-            if (v > mx) mx = v;
-        }
-        float out = 0.0f;
-        if (mx != -INFINITY) {
-            double den = 0.0, acc = 0.0;
-            for (int s = 0; s < ns; s++) {
-                const size_t off = overlap ? ((s < ratio) ? (size_t)s * width + c : (size_t)s * width + hd + c)
-                                           : (size_t)s * width + c;
-                const float v = score_state[off];
-                if (v == -INFINITY) continue;
-                const double e = (double)expf(v - mx);
-                den = __dadd_rn(den, e);
-                acc = __dadd_rn(acc, __dmul_rn(e, (double)kv_state[off]));
-            }
-            out = (float)(acc / den);
-        }
-        cbuf[c] = out;
-    }
+    // slot s of the pool: overlap mode takes the previous window's first
+    // half-width and the current window's second half-width
+    comp_pool(cbuf, hd, overlap ? 2 * ratio : ratio, [&](int s, int c) {
+        const size_t off = overlap ? ((s < ratio) ? (size_t)s * width + c : (size_t)s * width + hd + c)
+                                   : (size_t)s * width + c;
+        return make_float2(kv_state[off], score_state[off]);
+    });
     __syncthreads();
     if (overlap) {       // slide: the current window becomes the previous one
         for (int i = threadIdx.x; i < ratio * width; i += blockDim.x) {
@@ -611,16 +637,87 @@ __device__ void compress_step(float *cache, float *kv_state, float *score_state,
             score_state[i] = score_state[(size_t)ratio * width + i];
         }
     }
-    double s = 0.0;
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) s = __fma_rn((double)cbuf[i], (double)cbuf[i], s);
-    s = block_sum_d(s, red);
-    const float inv = (float)(1.0 / sqrt(s / (double)hd + (double)eps));
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) cbuf[i] = __fmul_rn(norm[i], __fmul_rn(cbuf[i], inv));
+    comp_finish(cache, cbuf, norm, hd, rd, cs, sn, pos + 1 - ratio, eps, win + avail - 1, red);
+}
+
+// A prefill pass's compressor, token y of the pass (position pos, the pass
+// from position p0): its counts {avail, take} at dyn, and, when its position
+// closes a window, the compressed row of that window. The row's slots are
+// read where the per-token steps would have put them: positions inside the
+// pass from the pass's projection rows (the score plus its ape row, as a step
+// adds it), earlier ones from the compressor state as it stood before the
+// pass (the current window's slots, and with overlap the previous window's),
+// which nothing writes until the pass's last kernel (comp_state_after).
+__device__ void compress_pass(const PrepArgs &a, float *cache, const float *kv_state, const float *score_state,
+                              int y, int pos, int p0, float *cbuf, double *red)
+{
+    const int ratio = a.ratio, hd = a.hd, overlap = (ratio == 4), width = (1 + overlap) * hd;
+    const int avail = (pos + 1) / ratio;
+    if (threadIdx.x == 0) {
+        a.dyn[2 * y] = avail;
+        a.dyn[2 * y + 1] = avail < a.index_topk ? avail : a.index_topk;
+    }
+    if ((pos + 1) % ratio != 0) return;
+    const int e = avail - 1, cw = p0 / ratio;
+    comp_pool(cbuf, hd, overlap ? 2 * ratio : ratio, [&](int s, int c) {
+        // slot s: position q, column col of its projection row (overlap:
+        // the previous window's first half-width, then the current window's
+        // second half-width)
+        int q = e * ratio + s, col = c;
+        if (overlap) {
+            q = s < ratio ? (e - 1) * ratio + s : e * ratio + (s - ratio);
+            col = s < ratio ? c : hd + c;
+        }
+        if (q < 0) return make_float2(0.0f, -INFINITY);    // before position 0: never written
+        if (q >= p0) {
+            const size_t r = (size_t)(q - p0) * 2 * hd + col;
+            return make_float2(a.comp_in[r], __fadd_rn(a.comp_sc[r], a.ape[(size_t)(q % ratio) * width + col]));
+        }
+        // before the pass: the current window's slots, or the previous window's
+        const int slot = (q >= cw * ratio && overlap ? ratio : 0) + q % ratio;
+        return make_float2(kv_state[(size_t)slot * width + col], score_state[(size_t)slot * width + col]);
+    });
     __syncthreads();
-    rope_tail(cbuf, hd, rd, cs, sn, pos + 1 - ratio, 0);
+    comp_finish(cache, cbuf, a.cnorm, hd, a.rd, a.cs, a.sn, pos + 1 - ratio, a.eps, a.win + e, red);
+}
+
+// The compressor state after a prefill pass of nt tokens (p0 .. pe - 1): what
+// the per-token steps leave, for every slot a later step reads before it is
+// overwritten -- with overlap the previous window's slots (window pe / ratio
+// - 1, when the pass closed one), then the current window's slots of the
+// positions it already holds (the ones inside the pass; earlier ones are in
+// place). One block.
+__device__ void comp_state_after(const PrepArgs &a, float *kv_state, float *score_state, int p0, int pe)
+{
+    const int ratio = a.ratio, hd = a.hd, overlap = (ratio == 4), width = (1 + overlap) * hd;
+    const int cw = p0 / ratio, cwn = pe / ratio;
+    if (overlap && cwn > cw) {
+        // window cwn - 1's positions: inside the pass, or (when it is the
+        // window current before the pass) in the current slots
+        for (int i = threadIdx.x; i < ratio * width; i += blockDim.x) {
+            const int s = i / width, col = i - s * width, q = (cwn - 1) * ratio + s;
+            float kv, sc;
+            if (q >= p0) {
+                const size_t r = (size_t)(q - p0) * 2 * hd + col;
+                kv = a.comp_in[r];
+                sc = __fadd_rn(a.comp_sc[r], a.ape[(size_t)s * width + col]);
+            } else {
+                kv = kv_state[(size_t)(ratio + s) * width + col];
+                sc = score_state[(size_t)(ratio + s) * width + col];
+            }
+            kv_state[i] = kv;
+            score_state[i] = sc;
+        }
+    }
     __syncthreads();
-    float *dst = cache + (size_t)(win + avail - 1) * hd;
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) dst[i] = cbuf[i];
+    const int held = pe - cwn * ratio;           // positions of window cwn already processed
+    for (int i = threadIdx.x; i < held * width; i += blockDim.x) {
+        const int ph = i / width, col = i - ph * width, q = cwn * ratio + ph;
+        if (q < p0) continue;
+        const size_t r = (size_t)(q - p0) * 2 * hd + col, dst = (size_t)((overlap ? ratio : 0) + ph) * width + col;
+        kv_state[dst] = a.comp_in[r];
+        score_state[dst] = __fadd_rn(a.comp_sc[r], a.ape[(size_t)ph * width + col]);
+    }
 }
 // The attended rows of one token (src/model/dsv4_layer.c:504 and :295): the
 // window newest first, then the compressed rows -- the indexer's selection
@@ -683,16 +780,10 @@ __global__ void __launch_bounds__(256) k_attn_prep(const __grid_constant__ PrepA
             if (!a.pass_nt) {
                 compress_step(cache, comp_kv, comp_score, comp_in, comp_sc, a.ape, a.cnorm, a.ratio, a.hd,
                               a.rd, a.cs, a.sn, pos, a.eps, a.win, a.index_topk, a.dyn, cbuf, red);
-            } else if (y == 0) {
-                // a prefill pass: the compressor is a state machine over
-                // positions, so one block steps it through the pass's tokens in
-                // order; token t's counts go to dyn + 2 t
-                for (int t = 0; t < a.pass_nt; t++) {
-                    compress_step(cache, comp_kv, comp_score, a.comp_in + (size_t)t * 2 * a.hd,
-                                  a.comp_sc + (size_t)t * 2 * a.hd, a.ape, a.cnorm, a.ratio, a.hd, a.rd, a.cs,
-                                  a.sn, a.st[t].pos, a.eps, a.win, a.index_topk, a.dyn + 2 * t, cbuf, red);
-                    __syncthreads();
-                }
+            } else {
+                // a prefill pass: token y's counts and (closing a window) its
+                // compressed row; the state moves on after the pass
+                compress_pass(a, cache, comp_kv, comp_score, (int)y, pos, p0, cbuf, red);
             }
             return;
         }
@@ -725,19 +816,24 @@ __global__ void k_build_idxs(int *idxs, int nmax, const StepState *st, int win, 
                stage >= 0 ? st[0].pos : INT_MAX, stage);
 }
 
-// The end of a prefill pass: its KV rows move from the staging rows into the
-// window ring (token t at slot pos_t % win). Only the last min(nt, win)
-// tokens are copied (earlier ones would be overwritten), so no slot is
-// written twice. One block per token.
-__global__ void k_stage_commit(float *cache, int stage, int win, int hd, const StepState *st, int nt)
+// The end of a prefill pass (a.pass_nt tokens): its KV rows move from the
+// staging rows into the window ring (token t at slot pos_t % win; only the
+// last min(nt, win) tokens are copied, earlier ones would be overwritten, so
+// no slot is written twice), one block per token, and one more block moves
+// the compressor state past the pass.
+__global__ void k_stage_commit(const __grid_constant__ PrepArgs a)
 {
     pdl_trigger();
     pdl_wait();
-    const int t = blockIdx.x;
-    if (t < nt - win) return;
-    const float *src = cache + (size_t)(stage + t) * hd;
-    float *dst = cache + (size_t)(st[t].pos % win) * hd;
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) dst[i] = src[i];
+    const int t = blockIdx.x, nt = a.pass_nt;
+    if (t == nt) {
+        if (a.has_comp) comp_state_after(a, a.comp_kv, a.comp_score, a.st[0].pos, a.st[nt - 1].pos + 1);
+        return;
+    }
+    if (t < nt - a.win) return;
+    const float *src = a.cache + (size_t)(a.stage + t) * a.hd;
+    float *dst = a.cache + (size_t)(a.st[t].pos % a.win) * a.hd;
+    for (int i = threadIdx.x; i < a.hd; i += blockDim.x) dst[i] = src[i];
 }
 
 // Argmax, first maximum (src/cli/dsv4_run.c:472-473), two stages; the second

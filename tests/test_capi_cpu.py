@@ -41,3 +41,18 @@ def test_without_device_nothing_is_resident():
     assert m.upload() == -1
     assert m.has() == 0
     assert L.dsv4_cuda_free_vram() == 0
+
+
+def test_model_calls_refuse_a_null_model():
+    """The whole-model entry points check their handle before any device
+    work: a null model is refused (-1, or a null stream) on any machine."""
+    L = B.lib()
+    prompt = np.arange(4, dtype=np.int32)
+    out = np.zeros(8, np.int32)
+    assert L.dsv4b_model_prefill(None, prompt.ctypes.data, 4, 32) == -1
+    assert L.dsv4b_model_generate_prefill(None, prompt.ctypes.data, 4, 2, 32, out.ctypes.data) == -1
+    assert L.dsv4b_model_prefill_kernels(None) == -1
+    assert not L.dsv4b_model_stream(None)
+    assert L.dsv4b_model_begin_batch(None, prompt.ctypes.data, 4) == -1
+    assert L.dsv4b_model_decode_batch(None, prompt.ctypes.data, 0, out.ctypes.data) == -1
+    assert L.dsv4b_model_n_seq(None) == -1

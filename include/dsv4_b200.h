@@ -177,11 +177,14 @@ dsv4b_model *dsv4_cuda_model_create_synthetic(const DSV4Cfg *c, int max_pos,
 /* ---- batched prefill (src/cli/dsv4_run.c:391-442, the --batch prompt
  * path; dsv4_layer_forward_n, src/model/dsv4_layer.c:856-918): the prompt
  * of a one-sequence model in passes of up to chunk tokens (1..64; the
- * reference's default is 32). Within a pass every token-local step (mHC,
- * every projection, the output projections, the MoE over the union of the
- * pass's experts) runs over all chunk tokens at once, and the cache-bound
- * core (q / KV finish, compressor, indexer, top-k, attention) runs token by
- * token in position order; the head runs once, on the prompt's last token.
+ * reference's default is 32). Every launch of a pass covers all of its
+ * tokens: mHC, every projection, the output projections, the MoE over the
+ * union of the pass's experts, and the cache-bound core (q / KV finish,
+ * compressor, indexer, top-k, attention). Each token still sees the window
+ * and the compressor as they stood at its own position: the pass's KV rows
+ * are staged beside the ring until the pass ends, and each compressor
+ * window is pooled by the token that closes it. The head runs once, on the
+ * prompt's last token.
  * Every token's arithmetic is that of a decode step, so the model is left
  * where dsv4_cuda_model_begin + n_prompt steps leave it: caches filled,
  * position n_prompt, the first generated token emitted. */

@@ -6,7 +6,10 @@
 // the sparse-MLA kernels of mla.cu and the support ops of model_kernels.cu.
 // Nothing in the sequence depends on the host: the position and token live in
 // a device StepState that the last kernel advances, so the sequence is
-// captured once into a CUDA graph and replayed for every position.
+// captured once into a CUDA graph and replayed for every position. The same
+// sequence serves a batch of sequences (one row each) and a prefill pass of
+// one sequence's prompt tokens (dsv4_run.c:391-442, one row per token; see
+// attn_core for how the pass keeps each token's view of the caches).
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
